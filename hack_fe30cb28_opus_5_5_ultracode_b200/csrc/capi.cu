@@ -1,0 +1,103 @@
+// extern "C" entry points of libqlora_sm100a.so (declared in include/qlora_sm100.h): argument
+// checks, the per-thread error message, the device status word, and dispatch to the kernels.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace {
+__device__ int g_status_word = 0;  // QL_STATUS_TIMEOUT etc., recorded by kernels
+thread_local std::string g_last_error;
+
+int fail(int code, const char* where) {
+  const cudaError_t e = cudaGetLastError();
+  char buf[512];
+  std::snprintf(buf, sizeof(buf), "%s: %s%s%s", where,
+                code == QL_STATUS_BAD_ARG     ? "invalid argument"
+                : code == QL_STATUS_UNSUPPORTED ? "unsupported request"
+                : code == QL_STATUS_TIMEOUT   ? "timeout"
+                                              : "CUDA error",
+                e != cudaSuccess ? " / " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
+  g_last_error = buf;
+  return code;
+}
+
+int done(int code, const char* where) {
+  if (code == QL_STATUS_OK) return QL_STATUS_OK;
+  return fail(code, where);
+}
+}  // namespace
+
+namespace ql {
+int* status_word() {
+  // one address per device; cudaGetSymbolAddress is cheap after the first call per device
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+}  // namespace ql
+
+extern "C" {
+
+const char* ql_version(void) { return "qlora_sm100a 0.1 (sm_100a, tcgen05)"; }
+
+const char* ql_last_error(void) { return g_last_error.c_str(); }
+
+int* ql_device_status_ptr(void) { return ql::status_word(); }
+
+int ql_device_status(int* status_out, int clear) {
+  int* p = ql::status_word();
+  if (p == nullptr || status_out == nullptr) return fail(QL_STATUS_CUDA, "ql_device_status");
+  if (cudaMemcpy(status_out, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(QL_STATUS_CUDA, "ql_device_status");
+  if (clear && cudaMemset(p, 0, sizeof(int)) != cudaSuccess)
+    return fail(QL_STATUS_CUDA, "ql_device_status");
+  return QL_STATUS_OK;
+}
+
+int ql_nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
+                   const float* absmax2, const float* offsets, const float* code, void* out,
+                   int64_t rows, int64_t cols, int nested, int bs2, int64_t seg1, int64_t seg2,
+                   int out_dtype, int transpose, cudaStream_t stream) {
+  return done(ql::nf4_dequant(packed, absmax, code2, absmax2, offsets, code, out, rows, cols,
+                              nested, bs2, seg1, seg2, out_dtype, transpose, stream),
+              "ql_nf4_dequant");
+}
+
+int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+               const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+               cudaStream_t stream) {
+  return done(ql::gemm_tn(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
+                          ql::status_word(), stream),
+              "ql_gemm_tn");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int ql_rms_fwd(const ql_rms_fwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_rms_fwd");
+  return done(ql::rms_fwd(*args, stream), "ql_rms_fwd");
+}
+
+int ql_rms_bwd(const ql_rms_bwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_rms_bwd");
+  return done(ql::rms_bwd(*args, stream), "ql_rms_bwd");
+}
+
+int ql_dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t threads,
+                    float p_keep, int vec, cudaStream_t stream) {
+  return done(ql::dropout_keep(out, nelem, seed, ctr, threads, p_keep, vec, stream),
+              "ql_dropout_keep");
+}
+
+}  // extern "C"

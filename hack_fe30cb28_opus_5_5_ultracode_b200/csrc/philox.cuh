@@ -1,0 +1,57 @@
+// PyTorch's CUDA dropout keep mask, bit for bit, as a pure function of the element index.
+//
+// Follows the reference's restatement (solution/kernels.py:108-126): element e of the contiguous
+// [B, T, H] LoRA input is drawn by thread t = (e / VEC) % G of the dropout kernel's G threads, at
+// Philox counter ctr + (e / VEC / G) * (VEC / 4) + (e % VEC) / 4, component e % 4, and is kept iff
+// u * 2^-32 + 2^-33 < 1 - p (fp32). Philox4x32-10 (key = seed, counter = (c_lo, c_hi, t, 0)) is
+// written from Salmon et al., "Parallel random numbers: as easy as 1, 2, 3" (SC'11).
+#pragma once
+#include <stdint.h>
+
+namespace ql {
+
+struct DropoutArgs {
+  const int64_t* tok;  // [n] each packed token's index in the padded [B, T] batch
+  int64_t seed;        // the generator's seed, its 64 bits as an int64
+  int64_t ctr_q, ctr_v;  // Philox counters (offset / 4) of the q and v masks
+  int64_t threads;     // G = dropout grid * 256
+  float p_keep, keep_scale;
+  int vec;             // 16 / sizeof(LoRA input element): 4 for fp32
+  int drop_q, drop_v;  // which masks exist
+};
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    if (r < 9) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ bool keep_from_u(uint32_t u, float p_keep) {
+  // the product is exact (a power-of-two scale), so a contracted multiply-add rounds the same
+  const float f = __fadd_rn(__fmul_rn(__uint2float_rn(u), 2.3283064365386963e-10f),
+                            1.1641532182693481e-10f);
+  return f < p_keep;
+}
+
+// Keep bits of the 4 consecutive elements e0 .. e0+3 (e0 % 4 == 0) of one dropout call: they
+// share thread and counter when VEC is 4; for VEC 8 as well (the 4-group lies inside one VEC).
+// Bit j of the result is element e0 + j.
+__device__ __forceinline__ uint32_t keep4(int64_t e0, int64_t ctr, const DropoutArgs& d) {
+  const int64_t g = e0 / d.vec;
+  const uint32_t thread = (uint32_t)(g % d.threads);
+  const uint64_t c = (uint64_t)(ctr + (g / d.threads) * (d.vec / 4) + (e0 % d.vec) / 4);
+  const uint4 r = philox4x32_10(make_uint4((uint32_t)c, (uint32_t)(c >> 32), thread, 0u),
+                                (uint32_t)(uint64_t)d.seed, (uint32_t)((uint64_t)d.seed >> 32));
+  return (keep_from_u(r.x, d.p_keep) ? 1u : 0u) | (keep_from_u(r.y, d.p_keep) ? 2u : 0u) |
+         (keep_from_u(r.z, d.p_keep) ? 4u : 0u) | (keep_from_u(r.w, d.p_keep) ? 8u : 0u);
+}
+
+}  // namespace ql

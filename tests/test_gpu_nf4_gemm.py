@@ -1,0 +1,144 @@
+"""NF4 dequantisation (bit-exact vs the reference kernel's golden output and the oracle) and the
+tcgen05 GEMM (vs a torch fp32 matmul), through the C ABI on the GPU."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.nf4 import bf16_bits_to_f32, dequant_nf4, quantize_nf4
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+class _W:
+    """What ops.nf4_dequant reads from a weight."""
+
+    def __init__(self, st, seg1=2147483647, seg2=2147483647, offsets=None):
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+        self.shape = st.shape
+        self.packed = t(st.packed)
+        self.absmax = t(st.absmax)
+        self.code = t(st.code)
+        self.nested = st.nested
+        self.bs2 = st.bs2 if st.nested else 1
+        self.seg1, self.seg2 = seg1, seg2
+        if st.nested:
+            self.code2 = t(st.code2)
+            self.absmax2 = t(st.absmax2)
+            self.offsets = t(offsets if offsets is not None else st.offset)
+        else:
+            self.code2 = self.absmax2 = self.offsets = None
+
+
+def test_nf4_dequant_matches_reference_golden(golden):
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = golden("nf4.npz")
+    rows, cols = int(g["rows"]), int(g["cols"])
+
+    class St:
+        pass
+
+    st = St()
+    st.shape, st.packed, st.absmax, st.nested = (rows, cols), g["packed"], g["absmax"], False
+    st.bs2 = 1
+    from oracle.nf4 import NF4_LEVELS
+
+    st.code = NF4_LEVELS
+    out = ops.nf4_dequant(_W(st))
+    assert torch.equal(out.cpu(), torch.from_numpy(g["out"]))
+
+
+@pytest.mark.parametrize("nested", [False, True])
+@pytest.mark.parametrize("shape", [(256, 1536), (1536, 512), (17920, 1536), (128, 64)])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_nf4_dequant_matches_oracle(nested, shape, dtype):
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    rng = np.random.default_rng(shape[0] + 7 * nested)
+    w = (rng.standard_normal(shape) * 0.05).astype(np.float32)
+    st = quantize_nf4(w, nested=nested)
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    out = ops.nf4_dequant(_W(st), dtype=tdt)
+    ref = dequant_nf4(st, dtype)
+    if dtype == "f16":
+        assert torch.equal(out.cpu(), torch.from_numpy(ref))
+    else:
+        assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+    if shape[0] % 64 == 0 and shape[1] % 64 == 0:
+        out_t = ops.nf4_dequant(_W(st), transpose=True, dtype=tdt)
+        assert torch.equal(out_t.cpu(), out.cpu().t().contiguous())
+
+
+def test_nf4_dequant_nested_segments():
+    """Three weights back to back (q, k, v): only the double-quantisation offset differs per
+    segment (solution/engine.py:112-157)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    rng = np.random.default_rng(5)
+    parts = [quantize_nf4((rng.standard_normal((r, 256)) * 0.03).astype(np.float32), nested=True)
+             for r in (256, 128, 128)]
+
+    class St:
+        pass
+
+    st = St()
+    st.shape = (512, 256)
+    st.packed = np.concatenate([p.packed for p in parts])
+    st.absmax = np.concatenate([p.absmax for p in parts])
+    st.absmax2 = np.concatenate([p.absmax2 for p in parts])
+    st.code2 = parts[0].code2
+    st.code = parts[0].code
+    st.nested, st.bs2 = True, 256
+    st.offset = parts[0].offset
+    offsets = np.concatenate([p.offset for p in parts])
+    seg1 = 256 * 256 // 64
+    seg2 = seg1 + 128 * 256 // 64
+    out = ops.nf4_dequant(_W(st, seg1, seg2, offsets))
+    ref = np.concatenate([dequant_nf4(p) for p in parts])
+    assert torch.equal(out.cpu(), torch.from_numpy(ref))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (37, 256, 1536), (300, 2048, 1536),
+                                   (1400, 17920, 1536), (1400, 1536, 8960), (129, 200, 136),
+                                   (1000, 151936 // 8, 1536)])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_matches_torch(M, N, K, dt):
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(M * 31 + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(dt)
+    b = (torch.randn(N, K, device=DEV, generator=g) * 0.05).to(dt)
+    bias = torch.randn(N, device=DEV, generator=g).to(dt)
+    ref = a.float() @ b.float().t()
+    out = ops.gemm(a, b)
+    tol = 2e-2 if dt == torch.bfloat16 else 4e-3
+    scale = ref.abs().max().item() + 1e-6
+    assert (out.float() - ref).abs().max().item() / scale < tol
+    out32 = ops.gemm(a, b, out_dtype=torch.float32, bias=bias)
+    assert (out32 - (ref + bias.float())).abs().max().item() / scale < 1e-3
+    ops.gemm(a, b, out=out32, accumulate=True)
+    assert (out32 - (2 * ref + bias.float())).abs().max().item() / scale < 2e-3
+    assert ops.device_status() == 0
+
+
+def test_gemm_strided_output():
+    """C written into columns of a wider buffer (the [gate | up] halves, the LoRA slices)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    a = torch.randn(200, 512, device=DEV).half()
+    b = torch.randn(256, 512, device=DEV).half() * 0.05
+    buf = torch.zeros(200, 1024, device=DEV, dtype=torch.half)
+    ops.gemm(a, b, out=buf[:, 512:768])
+    ref = a.float() @ b.float().t()
+    assert (buf[:, 512:768].float() - ref).abs().max() < 2e-2 * ref.abs().max()
+    assert buf[:, :512].abs().max() == 0 and buf[:, 768:].abs().max() == 0
+
+
+def test_bf16_helpers():
+    x = np.array([1.0, 1.00390625, -3.5, 1e-3], np.float32)
+    from oracle.nf4 import f32_to_bf16_bits
+
+    back = bf16_bits_to_f32(f32_to_bf16_bits(x))
+    assert np.allclose(back, torch.tensor(x).bfloat16().float().numpy())
