@@ -1,33 +1,76 @@
-"""Loads libqlora_sm100a.so (built in-tree by build.py) and declares its C ABI for ctypes.
+"""Loads libqlora_sm100a.so (built in-tree by build.py) and binds its C ABI for ctypes.
 
-There is no fallback: if the library is missing or does not load, every op raises. The
-signatures below mirror include/qlora_sm100.h one for one.
+The argument structs and prototypes are read from include/qlora_sm100.h itself, so the Python
+binding cannot drift from the header (tests/test_abi.py also checks the layouts against gcc).
+There is no fallback: if the library is missing or does not load, every op raises.
 """
 
 import ctypes
 import os
+import re
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libqlora_sm100a.so")
+HEADER = os.path.join(os.path.dirname(_HERE), "include", "qlora_sm100.h")
 
-P = ctypes.c_void_p
-I32 = ctypes.c_int
-I64 = ctypes.c_int64
-F32 = ctypes.c_float
-U64 = ctypes.c_uint64
+_SCALARS = {"int": ctypes.c_int, "int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64,
+            "long long": ctypes.c_longlong,
+            "float": ctypes.c_float, "double": ctypes.c_double, "void": None}
 
-# name -> argument types (every function returns int status unless listed in _RESTYPES)
-SIGNATURES = {
-    "ql_version": [],
-    "ql_last_error": [],
-    "ql_device_status": [P, I32],
-    "ql_device_status_ptr": [],
-    "ql_nf4_dequant": [P, P, P, P, P, P, P, I64, I64, I32, I32, I64, I64, I32, I32, P],
-    "ql_gemm_tn": [P, I64, P, I64, P, I64, P, I32, I32, I32, I32, I32, I32, P],
-}
-_RESTYPES = {"ql_version": ctypes.c_char_p, "ql_last_error": ctypes.c_char_p,
-             "ql_device_status_ptr": P}
 
+def _strip_comments(text):
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    return re.sub(r"//[^\n]*", " ", text)
+
+
+def _ctype(decl_type):
+    t = decl_type.replace("const", " ").strip()
+    if "*" in t:
+        if re.sub(r"\s+", "", t) == "char*":
+            return ctypes.c_char_p
+        return ctypes.c_void_p
+    t = re.sub(r"\s+", " ", t).strip()
+    if t == "cudaStream_t":
+        return ctypes.c_void_p
+    if t not in _SCALARS:
+        raise ValueError(f"unknown C type {decl_type!r}")
+    return _SCALARS[t]
+
+
+def parse_header(path=HEADER):
+    """(structs: name -> ctypes.Structure subclass, functions: name -> (restype, argtypes))."""
+    with open(path, encoding="utf-8") as fh:
+        text = _strip_comments(fh.read())
+    structs = {}
+    for body, name in re.findall(r"typedef\s+struct\s*\{(.*?)\}\s*(\w+)\s*;", text, flags=re.S):
+        fields = []
+        for decl in body.split(";"):
+            decl = " ".join(decl.split())
+            if not decl:
+                continue
+            m = re.match(r"^((?:const\s+)?[A-Za-z_]\w*(?:\s*\*)?)\s*(.*)$", decl)
+            base, names = m.group(1), m.group(2)
+            for nm in names.split(","):
+                nm = nm.strip()
+                stars = nm.count("*")
+                nm = nm.replace("*", "").strip()
+                fields.append((nm, _ctype(base + "*" * stars)))
+        structs[name] = type(name, (ctypes.Structure,), {"_fields_": fields})
+    functions = {}
+    for ret, name, args in re.findall(r"\b((?:const\s+)?(?:long\s+long|[A-Za-z_]\w*)\s*\**)\s*(ql_\w+)\s*\(([^)]*)\)\s*;",
+                                      text):
+        argtypes = []
+        args = args.strip()
+        if args and args != "void":
+            for a in args.split(","):
+                a = " ".join(a.split())
+                m = re.match(r"^(.*?)(\w+)$", a)
+                argtypes.append(_ctype(m.group(1)))
+        functions[name] = (_ctype(ret), argtypes)
+    return structs, functions
+
+
+STRUCTS, FUNCTIONS = parse_header()
 _lib = None
 
 
@@ -47,16 +90,16 @@ def lib():
             raise ImportError(f"{LIB_PATH} is missing: build it with "
                               "`python -m hack_fe30cb28_opus_5_5_ultracode_b200.build`")
         handle = ctypes.CDLL(LIB_PATH)
-        for name, args in SIGNATURES.items():
+        for name, (restype, argtypes) in FUNCTIONS.items():
             fn = getattr(handle, name)
-            fn.argtypes = args
-            fn.restype = _RESTYPES.get(name, I32)
+            fn.argtypes = argtypes
+            fn.restype = restype
         _lib = handle
     return _lib
 
 
 def call(name, *args):
-    """Calls an entry point and raises QLError on a non-zero status."""
+    """Calls an entry point returning a status and raises QLError unless it is 0."""
     status = getattr(lib(), name)(*args)
     if status != 0:
         msg = lib().ql_last_error().decode(errors="replace")
@@ -64,5 +107,13 @@ def call(name, *args):
     return status
 
 
+def struct(name, **fields):
+    """An argument struct of the header, zero-initialised, with the given fields set."""
+    s = STRUCTS[name]()
+    for k, v in fields.items():
+        setattr(s, k, v)
+    return s
+
+
 def exported_symbols():
-    return list(SIGNATURES)
+    return list(FUNCTIONS)

@@ -1,0 +1,534 @@
+// Varlen causal attention with grouped-query heads over the packed tokens of one step.
+//
+// Replaces PyTorch's memory-efficient attention in its cu_seqlens form (_attn_fwd / _attn_bwd,
+// solution/engine.py:857-869): q [n, HQ, D], k and v [n, HKV, D] (one copy per KV head, shared by
+// the HQ / HKV query heads of its group), sequences given by cu_seqlens [B + 1], causal within a
+// sequence, scale D^-1/2. Forward writes out [n, HQ, D] and the natural-log logsumexp [HQ, n];
+// backward recomputes the probabilities from it (FlashAttention-2 scheme, Dao 2023) and writes
+// dq [n, HQ, D], dk and dv [n, HKV, D] in fp32 (accumulated over the GQA group and query blocks).
+//
+// This first version runs on the warp-level tensor-core path (mma.sync m16n8k16, fp32
+// accumulation); the tiles are 64 queries x 64 keys, head dim D = 128 (Qwen2.5) or 64, staged by
+// cp.async into XOR-swizzled shared memory read with ldmatrix.
+#include "common.cuh"
+#include "ops.h"
+
+namespace ql {
+
+constexpr int AT_BM = 64;   // queries per forward CTA
+constexpr int AT_BN = 64;   // keys per step / per backward CTA
+constexpr int AT_BQ = 32;   // queries per backward step
+
+// element offset of (row, col) in a [rows][D] 16-bit tile (D = 64 or 128) with its 16-byte
+// chunks XOR-swizzled by the row (conflict-free ldmatrix)
+template <int D>
+__device__ __forceinline__ int sw(int row, int col) {
+  return row * D + ((((col >> 3) ^ (row & 7))) << 3) + (col & 7);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
+  T l = from_f<T>(lo), h = from_f<T>(hi);
+  return (uint32_t)(*reinterpret_cast<uint16_t*>(&l)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&h)) << 16);
+}
+
+// Loads rows [r0, r0 + ROWS) of a [len, heads, D] sequence slice (row stride ld elements) into a
+// swizzled [ROWS][D] tile; rows at or past len are zero-filled.
+template <typename T, int D, int ROWS, int NT>
+__device__ __forceinline__ void load_tile(T* tile, const T* base, int64_t ld, int r0, int len) {
+  constexpr int CPR = D / 8;  // 16-byte chunks per row
+  constexpr int CHUNKS = ROWS * CPR;
+  for (int i = threadIdx.x; i < CHUNKS; i += NT) {
+    const int r = i / CPR, ch = i % CPR;
+    const bool ok = r0 + r < len;
+    const T* src = ok ? base + (int64_t)(r0 + r) * ld + ch * 8 : base;
+    cp_async16(tile + sw<D>(r, ch * 8), src, ok);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------
+template <typename T, int AT_D>
+__global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
+  extern __shared__ __align__(16) uint8_t at_smem[];
+  T* sQ = reinterpret_cast<T*>(at_smem);
+  T* sK = sQ + AT_BM * AT_D;          // [2][64][D]
+  T* sV = sK + 2 * AT_BN * AT_D;      // [2][64][D]
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
+  if (qb * AT_BM >= len) return;
+  const int group = a.HQ / a.HKV, kvh = h / group;
+  const int64_t ldq = (int64_t)a.HQ * AT_D, ldk = (int64_t)a.HKV * AT_D;
+  const T* Q = reinterpret_cast<const T*>(a.q) + (int64_t)start * ldq + h * AT_D;
+  const T* K = reinterpret_cast<const T*>(a.k) + (int64_t)start * ldk + kvh * AT_D;
+  const T* V = reinterpret_cast<const T*>(a.v) + (int64_t)start * ldk + kvh * AT_D;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const float sl2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
+
+  load_tile<T, AT_D, AT_BM, 128>(sQ, Q, ldq, qb * AT_BM, len);
+  const int nkb = qb + 1;  // causal: key blocks 0 .. qb
+  load_tile<T, AT_D, AT_BN, 128>(sK, K, ldk, 0, len);
+  load_tile<T, AT_D, AT_BN, 128>(sV, V, ldk, 0, len);
+  cp_async_commit();
+
+  constexpr int NT = AT_D / 8;   // 8-wide d tiles
+  constexpr int KS = AT_D / 16;  // 16-wide k steps over d
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  uint32_t qf[KS][4];
+  const int qrow0 = qb * AT_BM + warp * 16;  // first query row of this warp (in the sequence)
+
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 < nkb) {
+      load_tile<T, AT_D, AT_BN, 128>(sK + (buf ^ 1) * AT_BN * AT_D, K, ldk, (kb + 1) * AT_BN, len);
+      load_tile<T, AT_D, AT_BN, 128>(sV + (buf ^ 1) * AT_BN * AT_D, V, ldk, (kb + 1) * AT_BN, len);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(sQ + sw<AT_D>(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+    }
+    const T* tK = sK + buf * AT_BN * AT_D;
+    const T* tV = sV + buf * AT_BN * AT_D;
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {  // pairs of 8-key n-tiles
+        uint32_t b0, b1, b2, b3;
+        const int r = jp * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(tK + sw<AT_D>(r, c), b0, b1, b2, b3);
+        mma16816<T>(s[2 * jp], qf[kk], b0, b1);
+        mma16816<T>(s[2 * jp + 1], qf[kk], b2, b3);
+      }
+    }
+    // scale, causal / length mask, online softmax (rows g and g + 8 of this warp)
+    const bool diag = kb == qb;
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int qi = qrow0 + g + hr * 8;
+      float mx = mrow[hr];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kj = kb * AT_BN + j * 8 + 2 * t4 + e;
+          float v = s[j][hr * 2 + e] * sl2;
+          if (diag && (kj > qi || kj >= len)) v = -INFINITY;
+          s[j][hr * 2 + e] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float corr = mrow[hr] == -INFINITY ? 0.f : exp2f(mrow[hr] - mx);
+      mrow[hr] = mx;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float p = mx == -INFINITY ? 0.f : exp2f(s[j][hr * 2 + e] - mx);
+          s[j][hr * 2 + e] = p;
+          sum += p;
+        }
+      }
+      lrow[hr] = lrow[hr] * corr + sum;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        o[i][hr * 2] *= corr;
+        o[i][hr * 2 + 1] *= corr;
+      }
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 16 keys per k-step
+      uint32_t pa[4];
+      pa[0] = pack_t2<T>(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_t2<T>(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_t2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_t2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {  // pairs of 8-wide d tiles
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(tV + sw<AT_D>(r, c), b0, b1, b2, b3);
+        mma16816<T>(o[2 * np], pa, b0, b1);
+        mma16816<T>(o[2 * np + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // the buffer is reloaded two steps later
+  }
+  // finalize
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float l = lrow[hr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int qi = qrow0 + g + hr * 8;
+    if (qi < len) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* out = reinterpret_cast<T*>(a.out) + ((int64_t)(start + qi) * a.HQ + h) * AT_D;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        *reinterpret_cast<uint32_t*>(out + i * 8 + 2 * t4) = pack_t2<T>(o[i][hr * 2] * inv, o[i][hr * 2 + 1] * inv);
+      }
+      if (t4 == 0) a.lse[(int64_t)h * a.n + start + qi] = (mrow[hr] + log2f(l)) * 0.6931471805599453f;
+    }
+  }
+}
+
+template <typename T, int D>
+static void launch_attn_fwd(const AttnFwdC& a, cudaStream_t s) {
+  const int smem = (AT_BM + 4 * AT_BN) * D * 2;
+  static bool cfg = false;
+  if (!cfg) {
+    cudaFuncSetAttribute(attn_fwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cfg = true;
+  }
+  dim3 grid((unsigned)cdiv(a.max_len, AT_BM), (unsigned)a.HQ, (unsigned)a.B);
+  attn_fwd_kernel<T, D><<<grid, 128, smem, s>>>(a);
+}
+
+int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
+  if (a.D != 128 && a.D != 64) return QL_STATUS_UNSUPPORTED;
+  if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
+  if (a.n == 0 || a.B == 0 || a.max_len == 0) return QL_STATUS_OK;
+  if (a.dtype == QL_F16) {
+    if (a.D == 128) launch_attn_fwd<__half, 128>(a, s); else launch_attn_fwd<__half, 64>(a, s);
+  } else if (a.dtype == QL_BF16) {
+    if (a.D == 128) launch_attn_fwd<__nv_bfloat16, 128>(a, s); else launch_attn_fwd<__nv_bfloat16, 64>(a, s);
+  } else {
+    return QL_STATUS_BAD_ARG;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+}  // namespace ql
+
+namespace ql {
+
+// ---------------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------------
+// Dvec[h][t] = sum_d dO[t, h, d] * O[t, h, d] (the softmax-gradient row term).
+template <typename T, int AT_D>
+__global__ void attn_bwd_pre_kernel(const T* __restrict__ dout, const T* __restrict__ out,
+                                    float* __restrict__ dvec, int64_t n, int HQ) {
+  const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + (threadIdx.x >> 5);  // (t, h)
+  const int lane = threadIdx.x & 31;
+  if (row >= n * HQ) return;
+  const T* a = dout + row * AT_D;
+  const T* b = out + row * AT_D;
+  float s = 0.f;
+  constexpr int PER = AT_D / 32;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) s += to_f<T>(a[lane * PER + j]) * to_f<T>(b[lane * PER + j]);
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int64_t t = row / HQ;
+    const int h = (int)(row % HQ);
+    dvec[(int64_t)h * n + t] = s;
+  }
+}
+
+// One CTA per (64-key block, query head, sequence); 4 warps, warp w owns keys 16w .. 16w + 15.
+// Steps over the query rows from the key block's start in blocks of 32: recomputes P^T, then
+// dV += P^T dO, dP^T = V dO^T, dS^T = P^T (dP^T - Dvec), dK += dS^T Q, and dQ += dS K through a
+// shared-memory copy of dS^T (atomically added to the fp32 dq). dK, dV are added atomically
+// into the KV head's fp32 rows at the end (the group's query heads all contribute).
+template <typename T, int AT_D>
+__global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
+  extern __shared__ __align__(16) uint8_t at_smem[];
+  T* sK = reinterpret_cast<T*>(at_smem);   // [64][D]
+  T* sV = sK + AT_BN * AT_D;                // [64][D]
+  T* sQ = sV + AT_BN * AT_D;                // [2][32][D]
+  T* sO = sQ + 2 * AT_BQ * AT_D;            // [2][32][D] (dO)
+  T* sS = sO + 2 * AT_BQ * AT_D;            // [64][40] dS^T (padded rows)
+  float* sL = reinterpret_cast<float*>(sS + AT_BN * 40);  // [2][32] lse
+  float* sD = sL + 2 * AT_BQ;                              // [2][32] Dvec
+  constexpr int SROW = 40;
+
+  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
+  if (kb * AT_BN >= len) return;
+  const int group = a.HQ / a.HKV, kvh = h / group;
+  const int64_t ldq = (int64_t)a.HQ * AT_D, ldk = (int64_t)a.HKV * AT_D;
+  const T* Q = reinterpret_cast<const T*>(a.q) + (int64_t)start * ldq + h * AT_D;
+  const T* dO = reinterpret_cast<const T*>(a.dout) + (int64_t)start * ldq + h * AT_D;
+  const T* K = reinterpret_cast<const T*>(a.k) + (int64_t)start * ldk + kvh * AT_D;
+  const T* V = reinterpret_cast<const T*>(a.v) + (int64_t)start * ldk + kvh * AT_D;
+  const float* lse = a.lse + (int64_t)h * a.n + start;
+  const float* dvec = a.dvec + (int64_t)h * a.n + start;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const float sl2 = a.scale * 1.4426950408889634f;
+
+  load_tile<T, AT_D, AT_BN, 128>(sK, K, ldk, kb * AT_BN, len);
+  load_tile<T, AT_D, AT_BN, 128>(sV, V, ldk, kb * AT_BN, len);
+  const int q_first = kb * AT_BN;
+  const int nsteps = (int)cdiv(len - q_first, AT_BQ);
+  auto load_q = [&](int step, int buf) {
+    const int r0 = q_first + step * AT_BQ;
+    load_tile<T, AT_D, AT_BQ, 128>(sQ + buf * AT_BQ * AT_D, Q, ldq, r0, len);
+    load_tile<T, AT_D, AT_BQ, 128>(sO + buf * AT_BQ * AT_D, dO, ldq, r0, len);
+    if (threadIdx.x < AT_BQ) {
+      const int qi = r0 + threadIdx.x;
+      sL[buf * AT_BQ + threadIdx.x] = qi < len ? lse[qi] : INFINITY;  // masked: p = 0
+      sD[buf * AT_BQ + threadIdx.x] = qi < len ? dvec[qi] : 0.f;
+    }
+  };
+  load_q(0, 0);
+  cp_async_commit();
+
+  constexpr int NT = AT_D / 8, KS = AT_D / 16;
+  float dk[NT][4], dv[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.f;
+    dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
+  }
+  const int key0 = kb * AT_BN + warp * 16;  // this warp's first key (in the sequence)
+
+  for (int st = 0; st < nsteps; ++st) {
+    const int buf = st & 1;
+    if (st + 1 < nsteps) {
+      load_q(st + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const T* tQ = sQ + buf * AT_BQ * AT_D;
+    const T* tO = sO + buf * AT_BQ * AT_D;
+    const float* tL = sL + buf * AT_BQ;
+    const float* tD = sD + buf * AT_BQ;
+    const int qbase = q_first + st * AT_BQ;
+
+    // S^T = K_w Q^T and dP^T = V_w dO^T: 16 keys x 32 queries each
+    float s[4][4], dp[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+      dp[j][0] = dp[j][1] = dp[j][2] = dp[j][3] = 0.f;
+    }
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t ka[4], va[4];
+      const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = kk * 16 + (lane >> 4) * 8;
+      ldsm_x4(sK + sw<AT_D>(r, c), ka[0], ka[1], ka[2], ka[3]);
+      ldsm_x4(sV + sw<AT_D>(r, c), va[0], va[1], va[2], va[3]);
+#pragma unroll
+      for (int jp = 0; jp < 2; ++jp) {
+        uint32_t b0, b1, b2, b3;
+        const int qr = jp * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int qc = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(tQ + sw<AT_D>(qr, qc), b0, b1, b2, b3);
+        mma16816<T>(s[2 * jp], ka, b0, b1);
+        mma16816<T>(s[2 * jp + 1], ka, b2, b3);
+        ldsm_x4(tO + sw<AT_D>(qr, qc), b0, b1, b2, b3);
+        mma16816<T>(dp[2 * jp], va, b0, b1);
+        mma16816<T>(dp[2 * jp + 1], va, b2, b3);
+      }
+    }
+    // P^T and dS^T (rows: keys g, g + 8 of the warp; columns: queries)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + g + (e >> 1) * 8;
+        const int ql = j * 8 + 2 * t4 + (e & 1);  // query within the step
+        const int qi = qbase + ql;
+        float p = exp2f(s[j][e] * sl2 - tL[ql] * 1.4426950408889634f);
+        if (key > qi || qi >= len || key >= len) p = 0.f;
+        s[j][e] = p;
+        dp[j][e] = p * (dp[j][e] - tD[ql]);
+      }
+    }
+    // dV += P^T dO ; dK += dS^T Q   (k = 32 queries: 2 k-steps)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4], sa[4];
+      pa[0] = pack_t2<T>(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_t2<T>(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_t2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_t2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      sa[0] = pack_t2<T>(dp[2 * kk][0], dp[2 * kk][1]);
+      sa[1] = pack_t2<T>(dp[2 * kk][2], dp[2 * kk][3]);
+      sa[2] = pack_t2<T>(dp[2 * kk + 1][0], dp[2 * kk + 1][1]);
+      sa[3] = pack_t2<T>(dp[2 * kk + 1][2], dp[2 * kk + 1][3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(tO + sw<AT_D>(r, c), b0, b1, b2, b3);
+        mma16816<T>(dv[2 * np], pa, b0, b1);
+        mma16816<T>(dv[2 * np + 1], pa, b2, b3);
+        ldsm_x4_t(tQ + sw<AT_D>(r, c), b0, b1, b2, b3);
+        mma16816<T>(dk[2 * np], sa, b0, b1);
+        mma16816<T>(dk[2 * np + 1], sa, b2, b3);
+      }
+    }
+    // dS^T to shared memory: sS[key][query]
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int kr = warp * 16 + g + hr * 8;
+        *reinterpret_cast<uint32_t*>(sS + kr * SROW + j * 8 + 2 * t4) =
+            pack_t2<T>(dp[j][hr * 2], dp[j][hr * 2 + 1]);
+      }
+    }
+    __syncthreads();
+    // dQ (32 queries x D) = dS (32 x 64 keys) K (64 x D): warp -> 16 queries x D/2
+    {
+      constexpr int HT = AT_D / 16;  // 8-wide d tiles per warp
+      const int qm = (warp & 1) * 16, dn = (warp >> 1) * (AT_D / 2);
+      float dq[HT][4];
+#pragma unroll
+      for (int i = 0; i < HT; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t aq[4];
+        // A[m = query][k = key] from sS[key][query] (transposed load)
+        const int mi = lane >> 3;
+        const int kr = kk * 16 + (lane & 7) + (mi >> 1) * 8;
+        const int qc = qm + (mi & 1) * 8;
+        ldsm_x4_t(sS + kr * SROW + qc, aq[0], aq[1], aq[2], aq[3]);
+#pragma unroll
+        for (int np = 0; np < HT / 2; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = dn + np * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(sK + sw<AT_D>(r, c), b0, b1, b2, b3);
+          mma16816<T>(dq[2 * np], aq, b0, b1);
+          mma16816<T>(dq[2 * np + 1], aq, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int qi = qbase + qm + g + hr * 8;
+        if (qi < len) {
+          float* dst = a.dq + ((int64_t)(start + qi) * a.HQ + h) * AT_D + dn;
+#pragma unroll
+          for (int i = 0; i < HT; ++i) {
+            atomicAdd(dst + i * 8 + 2 * t4, dq[i][hr * 2] * a.scale);
+            atomicAdd(dst + i * 8 + 2 * t4 + 1, dq[i][hr * 2 + 1] * a.scale);
+          }
+        }
+      }
+    }
+    __syncthreads();  // sS, and the Q / dO buffer reloaded next step
+  }
+  // dK (scaled), dV into the KV head's fp32 rows
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int key = key0 + g + hr * 8;
+    if (key < len) {
+      float* dkp = a.dk + ((int64_t)(start + key) * a.HKV + kvh) * AT_D;
+      float* dvp = a.dv + ((int64_t)(start + key) * a.HKV + kvh) * AT_D;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        atomicAdd(dkp + i * 8 + 2 * t4, dk[i][hr * 2] * a.scale);
+        atomicAdd(dkp + i * 8 + 2 * t4 + 1, dk[i][hr * 2 + 1] * a.scale);
+        atomicAdd(dvp + i * 8 + 2 * t4, dv[i][hr * 2]);
+        atomicAdd(dvp + i * 8 + 2 * t4 + 1, dv[i][hr * 2 + 1]);
+      }
+    }
+  }
+}
+
+template <typename T, int D>
+static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
+  const int64_t rows = (int64_t)a.n * a.HQ;
+  attn_bwd_pre_kernel<T, D><<<(unsigned)cdiv(rows, 8), 256, 0, s>>>(
+      (const T*)a.dout, (const T*)a.out, a.dvec, a.n, a.HQ);
+  const int smem = (2 * AT_BN + 4 * AT_BQ) * D * 2 + AT_BN * 40 * 2 + 4 * AT_BQ * 4;
+  static bool cfg = false;
+  if (!cfg) {
+    cudaFuncSetAttribute(attn_bwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cfg = true;
+  }
+  dim3 grid((unsigned)cdiv(a.max_len, AT_BN), (unsigned)a.HQ, (unsigned)a.B);
+  attn_bwd_kernel<T, D><<<grid, 128, smem, s>>>(a);
+}
+
+int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
+  if (a.D != 128 && a.D != 64) return QL_STATUS_UNSUPPORTED;
+  if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
+  if (a.n == 0 || a.B == 0) return QL_STATUS_OK;
+  if (a.dvec == nullptr) return QL_STATUS_BAD_ARG;
+  // gradients accumulate atomically: start from zero
+  if (cudaMemsetAsync(a.dq, 0, sizeof(float) * a.n * a.HQ * a.D, s) != cudaSuccess ||
+      cudaMemsetAsync(a.dk, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess ||
+      cudaMemsetAsync(a.dv, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess)
+    return QL_STATUS_CUDA;
+  if (a.max_len == 0) return QL_STATUS_OK;
+  if (a.dtype == QL_F16) {
+    if (a.D == 128) launch_attn_bwd<__half, 128>(a, s); else launch_attn_bwd<__half, 64>(a, s);
+  } else if (a.dtype == QL_BF16) {
+    if (a.D == 128) launch_attn_bwd<__nv_bfloat16, 128>(a, s); else launch_attn_bwd<__nv_bfloat16, 64>(a, s);
+  } else {
+    return QL_STATUS_BAD_ARG;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+}  // namespace ql

@@ -1,5 +1,6 @@
 // extern "C" entry points of libqlora_sm100a.so (declared in include/qlora_sm100.h): argument
 // checks, the per-thread error message, the device status word, and dispatch to the kernels.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -10,6 +11,7 @@
 namespace {
 __device__ int g_status_word = 0;  // QL_STATUS_TIMEOUT etc., recorded by kernels
 thread_local std::string g_last_error;
+std::atomic<long long> g_launches{0};  // kernels launched through this ABI (all host threads)
 
 int fail(int code, const char* where) {
   const cudaError_t e = cudaGetLastError();
@@ -24,8 +26,11 @@ int fail(int code, const char* where) {
   return code;
 }
 
-int done(int code, const char* where) {
-  if (code == QL_STATUS_OK) return QL_STATUS_OK;
+int done(int code, const char* where, int launches = 1) {
+  if (code == QL_STATUS_OK) {
+    g_launches.fetch_add(launches, std::memory_order_relaxed);
+    return QL_STATUS_OK;
+  }
   return fail(code, where);
 }
 }  // namespace
@@ -51,6 +56,8 @@ const char* ql_version(void) { return "qlora_sm100a 0.1 (sm_100a, tcgen05)"; }
 
 const char* ql_last_error(void) { return g_last_error.c_str(); }
 
+long long ql_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 int* ql_device_status_ptr(void) { return ql::status_word(); }
 
 int ql_device_status(int* status_out, int clear) {
@@ -74,9 +81,9 @@ int ql_nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2
 
 int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-               cudaStream_t stream) {
+               const float* residual, cudaStream_t stream) {
   return done(ql::gemm_tn(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
-                          ql::status_word(), stream),
+                          residual, ql::status_word(), stream),
               "ql_gemm_tn");
 }
 
@@ -98,6 +105,89 @@ int ql_dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64
                     float p_keep, int vec, cudaStream_t stream) {
   return done(ql::dropout_keep(out, nelem, seed, ctr, threads, p_keep, vec, stream),
               "ql_dropout_keep");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int ql_rope_fwd(const ql_rope_fwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_rope_fwd");
+  return done(ql::rope_fwd(*args, stream), "ql_rope_fwd");
+}
+
+int ql_rope_bwd(const ql_rope_bwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_rope_bwd");
+  return done(ql::rope_bwd(*args, stream), "ql_rope_bwd");
+}
+
+int ql_glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t stream) {
+  return done(ql::glu_fwd(gu, m, n, I, dtype, stream), "ql_glu_fwd");
+}
+
+int ql_glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t stream) {
+  return done(ql::glu_bwd(dm, gu, n, I, dtype, stream), "ql_glu_bwd");
+}
+
+int64_t ql_lora_colsum_workspace(int64_t n, int ncols, int rank) {
+  return (int64_t)ql::lora_colsum_splits(n) * ncols * rank;
+}
+
+int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
+                   int ncols, int rank, float scale, int transpose, float* out, float* workspace,
+                   int64_t workspace_floats, cudaStream_t stream) {
+  return done(ql::lora_colsum(X, ldx, x_dtype, Y, y_dtype, n, ncols, rank, scale, transpose, out,
+                              workspace, workspace_floats, stream),
+              "ql_lora_colsum", 2);
+}
+
+int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
+             int dtype, cudaStream_t stream) {
+  return done(ql::embed(ids, W, h, n, H, vocab, dtype, ql::status_word(), stream), "ql_embed");
+}
+
+int ql_ce_rows(const ql_ce_rows_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_ce_rows");
+  return done(ql::ce_rows(*args, stream), "ql_ce_rows");
+}
+
+int ql_ce_piece(const ql_ce_piece_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_ce_piece");
+  return done(ql::ce_piece(*args, stream), "ql_ce_piece");
+}
+
+int ql_ce_finish(const ql_ce_finish_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_ce_finish");
+  return done(ql::ce_finish(*args, stream), "ql_ce_finish");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_attn_fwd");
+  return done(ql::attn_fwd(*args, stream), "ql_attn_fwd");
+}
+
+int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream) {
+  if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_attn_bwd");
+  return done(ql::attn_bwd(*args, stream), "ql_attn_bwd", 2);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int ql_gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, int H,
+                   cudaStream_t stream) {
+  return done(ql::gather_rows(src, idx, dst, n, H, stream), "ql_gather_rows");
+}
+
+int ql_scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst,
+                    void* dst16, int64_t n, int H, int dtype, cudaStream_t stream) {
+  return done(ql::scatter_rows(src, idx, scale, dst, dst16, n, H, dtype, stream),
+              "ql_scatter_rows");
 }
 
 }  // extern "C"

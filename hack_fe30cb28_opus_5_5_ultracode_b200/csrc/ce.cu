@@ -1,0 +1,211 @@
+// Cross-entropy, entropy and argmax over a 151,936-word vocabulary without fp32 logits.
+//
+// ce_rows (reference lm_head_ce_kernel, solution/kernels.py:344-388): one CTA per row of 16-bit
+// logits. One online pass keeps (max, sum exp, sum exp * x, best, argmax) per thread — merged
+// across the CTA, first maximum wins — giving lse, entropy = lse - sum(p x), the loss lse - x_t
+// and accuracy; a second pass writes softmax - onehot over the row in place (unscaled), or zeros
+// for a row without a target when asked. The target logit is read before any thread writes.
+//
+// ce_piece / ce_finish (reference lm_head_piece_kernel / lm_head_finish_kernel,
+// solution/kernels.py:401-479): the same statistics carried across vocabulary pieces in a
+// [rows, 4] state (max, sum exp, sum exp * x, best) plus the argmax; rows with a target get
+// exp(x - running max) written over their logits for the gradient GEMM and the rescale factor
+// alpha = exp(old max - new max); the target's weight row is copied out when it falls in the
+// piece; finish forms loss, entropy, accuracy and dh = acc / s - W_target.
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace ql {
+
+constexpr int CE_THREADS = 512;
+
+struct OnlineStat {
+  float m, s, t, best;
+  int64_t arg;
+};
+
+__device__ __forceinline__ void stat_merge(OnlineStat& a, const OnlineStat& b) {
+  const float m = fmaxf(a.m, b.m);
+  const float fa = a.m == -CUDART_INF_F ? 0.f : __expf(a.m - m);
+  const float fb = b.m == -CUDART_INF_F ? 0.f : __expf(b.m - m);
+  a.s = a.s * fa + b.s * fb;
+  a.t = a.t * fa + b.t * fb;
+  a.m = m;
+  if (b.best > a.best || (b.best == a.best && b.arg < a.arg)) {
+    a.best = b.best;
+    a.arg = b.arg;
+  }
+}
+
+__device__ __forceinline__ void stat_add(OnlineStat& st, float x, int64_t col) {
+  if (x > st.best) {  // columns arrive in increasing order per thread: first max wins
+    st.best = x;
+    st.arg = col;
+  }
+  if (x > st.m) {
+    const float f = st.m == -CUDART_INF_F ? 0.f : __expf(st.m - x);
+    st.s *= f;
+    st.t *= f;
+    st.m = x;
+  }
+  const float e = __expf(x - st.m);
+  st.s += e;
+  st.t += e * x;
+}
+
+__device__ OnlineStat block_merge(OnlineStat st, OnlineStat* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    OnlineStat b;
+    b.m = __shfl_xor_sync(0xffffffffu, st.m, o);
+    b.s = __shfl_xor_sync(0xffffffffu, st.s, o);
+    b.t = __shfl_xor_sync(0xffffffffu, st.t, o);
+    b.best = __shfl_xor_sync(0xffffffffu, st.best, o);
+    b.arg = __shfl_xor_sync(0xffffffffu, st.arg, o);
+    stat_merge(st, b);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sh[warp] = st;
+  __syncthreads();
+  OnlineStat r = sh[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) stat_merge(r, sh[w]);
+  return r;
+}
+
+// Online statistics of row [0, width) of src, columns offset by v0 for the argmax.
+template <typename T>
+__device__ __forceinline__ OnlineStat row_stats(const T* src, int64_t width, int64_t v0) {
+  OnlineStat st{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0};
+  const bool vec = (reinterpret_cast<uintptr_t>(src) % 16 == 0);
+  if (vec) {
+    const int64_t nvec = width / 8;
+    for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + i * 8);
+      const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) stat_add(st, to_f<T>(h[j]), v0 + i * 8 + j);
+    }
+    for (int64_t c = nvec * 8 + threadIdx.x; c < width; c += blockDim.x) stat_add(st, to_f<T>(src[c]), v0 + c);
+  } else {
+    for (int64_t c = threadIdx.x; c < width; c += blockDim.x) stat_add(st, to_f<T>(src[c]), v0 + c);
+  }
+  return st;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(CE_THREADS) ce_rows_kernel(CeRowsC a) {
+  __shared__ OnlineStat sh[CE_THREADS / 32];
+  __shared__ float xt_sh;
+  const int64_t row = blockIdx.x;
+  T* src = reinterpret_cast<T*>(a.logits) + row * a.ld;
+  const int64_t target = a.target[row];
+  const bool valid = target >= 0 && target < a.V;
+  if (threadIdx.x == 0) xt_sh = valid ? to_f<T>(src[target]) : 0.f;
+  OnlineStat st = row_stats<T>(src, a.V, 0);
+  st = block_merge(st, sh);  // (its __syncthreads also publish xt_sh)
+  const float lse = st.m + logf(st.s);
+  if (threadIdx.x == 0) {
+    a.entropy[row] = lse - st.t / st.s;
+    a.loss[row] = valid ? lse - xt_sh : 0.f;
+    a.correct[row] = (valid && st.arg == target) ? 1 : 0;
+  }
+  if (valid && a.write_grad) {
+    for (int64_t c = threadIdx.x; c < a.V; c += blockDim.x) {
+      const float x = to_f<T>(src[c]);
+      src[c] = from_f<T>(__expf(x - lse) - (c == target ? 1.f : 0.f));
+    }
+  } else if (!valid && a.zero_unsupervised) {
+    for (int64_t c = threadIdx.x; c < a.V; c += blockDim.x) src[c] = from_f<T>(0.f);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
+  __shared__ OnlineStat sh[CE_THREADS / 32];
+  __shared__ float xt_sh;
+  const int64_t row = blockIdx.x;
+  T* src = reinterpret_cast<T*>(a.logits) + row * a.ld;
+  const int64_t target = a.target[row];
+  const int64_t local = target - a.v0;
+  const bool here = target >= 0 && local >= 0 && local < a.width;
+  if (threadIdx.x == 0) xt_sh = here ? to_f<T>(src[local]) : 0.f;
+  OnlineStat prev{a.state[row * 4], a.state[row * 4 + 1], a.state[row * 4 + 2],
+                  a.state[row * 4 + 3], a.best_idx[row]};
+  OnlineStat st = row_stats<T>(src, a.width, a.v0);
+  st = block_merge(st, sh);
+  const float m_old = prev.m;
+  // earlier pieces hold smaller columns, so on a tie the earlier maximum stays (stat_merge)
+  stat_merge(prev, st);
+  st = prev;
+  if (threadIdx.x == 0) {
+    a.state[row * 4] = st.m;
+    a.state[row * 4 + 1] = st.s;
+    a.state[row * 4 + 2] = st.t;
+    a.state[row * 4 + 3] = st.best;
+    a.best_idx[row] = st.arg;
+    if (here) a.xt[row] = xt_sh;
+    if (row < a.n_sup) a.alpha[row] = m_old == -CUDART_INF_F ? 0.f : __expf(m_old - st.m);
+  }
+  if (here && a.wt != nullptr) {
+    const T* w = reinterpret_cast<const T*>(a.w) + local * a.H;
+    T* dst = reinterpret_cast<T*>(a.wt) + row * a.H;
+    for (int c = threadIdx.x; c < a.H; c += blockDim.x) dst[c] = w[c];
+  }
+  if (row < a.n_sup) {
+    const float m = st.m;
+    for (int64_t c = threadIdx.x; c < a.width; c += blockDim.x)
+      src[c] = from_f<T>(__expf(to_f<T>(src[c]) - m));
+  }
+}
+
+template <typename T>
+__global__ void ce_finish_kernel(CeFinishC a) {
+  const int64_t row = blockIdx.x;
+  const float m = a.state[row * 4], s = a.state[row * 4 + 1], t = a.state[row * 4 + 2];
+  const float lse = m + logf(s);
+  const int64_t target = a.target[row];
+  const bool valid = target >= 0;
+  if (threadIdx.x == 0) {
+    a.entropy[row] = lse - t / s;
+    a.loss[row] = valid ? lse - a.xt[row] : 0.f;
+    a.correct[row] = (valid && a.best_idx[row] == target) ? 1 : 0;
+  }
+  if (row < a.n_sup) {
+    const float* acc = a.acc + row * a.H;
+    const T* wt = reinterpret_cast<const T*>(a.wt) + row * a.H;
+    T* dh = reinterpret_cast<T*>(a.dh) + row * a.H;
+    for (int c = threadIdx.x; c < a.H; c += blockDim.x) dh[c] = from_f<T>(acc[c] / s - to_f<T>(wt[c]));
+  }
+}
+
+int ce_rows(const CeRowsC& a, cudaStream_t s) {
+  if (a.rows < 0 || a.V <= 0 || a.ld < a.V) return QL_STATUS_BAD_ARG;
+  if (a.rows == 0) return QL_STATUS_OK;
+  if (a.dtype == QL_F16) ce_rows_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
+  else if (a.dtype == QL_BF16) ce_rows_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
+  else return QL_STATUS_BAD_ARG;
+  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+int ce_piece(const CePieceC& a, cudaStream_t s) {
+  if (a.rows < 0 || a.width <= 0 || a.ld < a.width || a.H <= 0) return QL_STATUS_BAD_ARG;
+  if (a.rows == 0) return QL_STATUS_OK;
+  if (a.dtype == QL_F16) ce_piece_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
+  else if (a.dtype == QL_BF16) ce_piece_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
+  else return QL_STATUS_BAD_ARG;
+  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+int ce_finish(const CeFinishC& a, cudaStream_t s) {
+  if (a.rows < 0 || a.H <= 0) return QL_STATUS_BAD_ARG;
+  if (a.rows == 0) return QL_STATUS_OK;
+  if (a.dtype == QL_F16) ce_finish_kernel<__half><<<a.rows, 256, 0, s>>>(a);
+  else if (a.dtype == QL_BF16) ce_finish_kernel<__nv_bfloat16><<<a.rows, 256, 0, s>>>(a);
+  else return QL_STATUS_BAD_ARG;
+  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+}  // namespace ql

@@ -26,6 +26,7 @@ struct GemmArgs {
   const void* bias;  // [N] of the input type, or null
   int out_dtype;     // QL_F16 / QL_BF16 / QL_F32
   int accumulate;    // C += result (fp32 output only)
+  const float* residual;  // fp32 [M, ldc] or null: C = residual + (result rounded to the input type)
   int* err;
 };
 
@@ -176,7 +177,10 @@ __global__ void __launch_bounds__(192, 1)
           }
           OutT* dst = C + (int64_t)row * p.ldc + col0;
           if constexpr (sizeof(OutT) == 4) {
-            if (p.accumulate) {
+            if (p.residual != nullptr) {
+              const float* res = p.residual + (int64_t)row * p.ldc + col0;
+              for (int i = 0; i < 32 && i < ncols; ++i) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
+            } else if (p.accumulate) {
               for (int i = 0; i < 32 && i < ncols; ++i) v[i] += to_f<OutT>(dst[i]);
             }
           }
@@ -274,11 +278,11 @@ static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const Gemm
 
 int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
             const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-            int* err, cudaStream_t stream) {
+            const float* residual, int* err, cudaStream_t stream) {
   if (M < 0 || N < 0 || K < 0) return QL_STATUS_BAD_ARG;
   if (M == 0 || N == 0) return QL_STATUS_OK;
   if (in_dtype != QL_F16 && in_dtype != QL_BF16) return QL_STATUS_BAD_ARG;
-  if (accumulate && out_dtype != QL_F32) return QL_STATUS_BAD_ARG;
+  if ((accumulate || residual != nullptr) && out_dtype != QL_F32) return QL_STATUS_BAD_ARG;
   // TMA: 16-byte aligned base and row strides
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) % 16 != 0)
     return QL_STATUS_BAD_ARG;
@@ -291,7 +295,7 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   CUtensorMap ma, mb;
   if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
   if (make_kmajor_map(&mb, B, N, K, ldb, BN, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, err};
+  GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err};
   if (BN == 256)
     return bf16 ? dispatch_out<256, true>(ma, mb, a, stream) : dispatch_out<256, false>(ma, mb, a, stream);
   return bf16 ? dispatch_out<128, true>(ma, mb, a, stream) : dispatch_out<128, false>(ma, mb, a, stream);

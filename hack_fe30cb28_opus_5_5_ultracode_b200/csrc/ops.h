@@ -16,7 +16,7 @@ int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
 
 int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
             const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-            int* err, cudaStream_t stream);
+            const float* residual, int* err, cudaStream_t stream);
 
 typedef ql_rms_fwd_args RmsFwdC;
 typedef ql_rms_bwd_args RmsBwdC;
@@ -25,4 +25,38 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s);
 int dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t threads,
                  float p_keep, int vec, cudaStream_t s);
 
+}  // namespace ql
+
+namespace ql {
+typedef ql_rope_fwd_args RopeFwdC;
+typedef ql_rope_bwd_args RopeBwdC;
+typedef ql_ce_rows_args CeRowsC;
+typedef ql_ce_piece_args CePieceC;
+typedef ql_ce_finish_args CeFinishC;
+int rope_fwd(const RopeFwdC& a, cudaStream_t s);
+int rope_bwd(const RopeBwdC& a, cudaStream_t s);
+int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s);
+int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t s);
+int lora_colsum_splits(int64_t n);
+int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
+                int ncols, int rank, float scale, int transpose, float* out, float* workspace,
+                int64_t workspace_floats, cudaStream_t s);
+int embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
+          int dtype, int* err, cudaStream_t s);
+int ce_rows(const CeRowsC& a, cudaStream_t s);
+int ce_piece(const CePieceC& a, cudaStream_t s);
+int ce_finish(const CeFinishC& a, cudaStream_t s);
+}  // namespace ql
+
+namespace ql {
+typedef ql_attn_fwd_args AttnFwdC;
+typedef ql_attn_bwd_args AttnBwdC;
+int attn_fwd(const AttnFwdC& a, cudaStream_t s);
+int attn_bwd(const AttnBwdC& a, cudaStream_t s);
+}  // namespace ql
+
+namespace ql {
+int gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, int H, cudaStream_t s);
+int scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst, void* dst16,
+                 int64_t n, int H, int dtype, cudaStream_t s);
 }  // namespace ql

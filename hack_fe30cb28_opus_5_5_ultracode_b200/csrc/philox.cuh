@@ -45,6 +45,7 @@ __device__ __forceinline__ bool keep_from_u(uint32_t u, float p_keep) {
 // share thread and counter when VEC is 4; for VEC 8 as well (the 4-group lies inside one VEC).
 // Bit j of the result is element e0 + j.
 __device__ __forceinline__ uint32_t keep4(int64_t e0, int64_t ctr, const DropoutArgs& d) {
+  if (d.p_keep >= 1.0f) return 0xFu;  // no dropout: the LoRA input is used as is
   const int64_t g = e0 / d.vec;
   const uint32_t thread = (uint32_t)(g % d.threads);
   const uint64_t c = (uint64_t)(ctr + (g / d.threads) * (d.vec / 4) + (e0 % d.vec) / 4);

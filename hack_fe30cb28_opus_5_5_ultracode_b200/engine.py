@@ -1,0 +1,576 @@
+"""The fused Qwen2 + NF4 + LoRA training step on B200, driving the sm_100a kernels of
+libqlora_sm100a.so. Mirrors the reference's FusedQwen2 (solution/engine.py:1568-1922): same
+inputs, same outputs (loss, packed batch, per-token statistics), same LoRA gradients through
+autograd, same use of the CUDA generator for the LoRA dropout masks.
+
+B200-first differences from the reference (which was built for a 16 GB T4):
+  * HBM is plentiful (180 GB), so the default plan keeps every intermediate a layer's backward
+    reads instead of recomputing it; NF4 weights stay resident (0.74 GB for 1.5B).
+  * every matrix product runs on the tcgen05 GEMM of this library (fp32 accumulation in TMEM),
+    the NF4 weights dequantised by this library's kernel once per pass (forward: W, backward: W^T
+    for the data-gradient GEMMs);
+  * LoRA-A products ride in the RMSNorm kernel, LoRA-B products and the LoRA input gradients in
+    the RoPE kernels, the residual adds in the GEMM epilogues;
+  * attention is this library's varlen causal GQA kernel: k / v are never expanded;
+  * the whole model is one autograd Function: forward runs the layers and the head (whose
+    gradient is formed in the forward, as the reference's head does), backward runs the layers
+    in reverse and hands autograd the LoRA gradients from one flat fp32 buffer, which a
+    data-parallel run all-reduces with NCCL.
+"""
+
+import math
+
+import torch
+
+from . import ops
+
+HEAD_CHUNK = 4096  # rows of logits alive at a time: 4096 x 151936 x 2 B = 1.2 GB of HBM
+
+
+# ---------------------------------------------------------------------------------------------
+# NF4 weights (solution/engine.py:74-157)
+# ---------------------------------------------------------------------------------------------
+class NF4Group:
+    """One or more bitsandbytes NF4 weights with the same column count stored back to back in
+    device memory (q, k, v; gate, up; or a single weight): one dequantisation launch for all of
+    them. Only the double-quantisation offset differs between members (per segment); their
+    absmax2 are concatenated, which needs every member but the last to end on a whole absmax2
+    block (else each member is dequantised on its own)."""
+
+    def __init__(self, params, device):
+        states = [p.quant_state for p in params]
+        s0 = states[0]
+        self.cols = int(s0.shape[1])
+        self.rows_each = [int(s.shape[0]) for s in states]
+        self.rows = sum(self.rows_each)
+        self.nested = bool(s0.nested)
+        self.code = s0.code.float().contiguous().to(device)
+        if int(s0.blocksize) != 64:
+            raise ValueError("NF4 blocksize must be 64")
+        for s in states:
+            if int(s.shape[1]) != self.cols or bool(s.nested) != self.nested \
+                    or int(s.blocksize) != 64 or not torch.equal(s.code.float().to(device), self.code):
+                raise ValueError("weights of a group differ in layout")
+        blocks = [r * self.cols // 64 for r in self.rows_each]
+        # packed bytes and absmax of every member, contiguous
+        self.packed = torch.cat([p.data.reshape(-1).view(torch.uint8).to(device) for p in params])
+        if self.nested:
+            self.bs2 = int(s0.state2.blocksize)
+            self.code2 = s0.state2.code.float().contiguous().to(device)
+            self.absmax = torch.cat([s.absmax.reshape(-1).to(device) for s in states])
+            self.absmax2 = torch.cat([s.state2.absmax.float().reshape(-1).to(device) for s in states])
+            self.offsets = torch.stack([torch.as_tensor(s.offset, dtype=torch.float32).reshape(())
+                                        .to(device) for s in states])
+            self.split = any(b % self.bs2 for b in blocks[:-1])
+        else:
+            self.bs2 = 1
+            self.code2 = self.absmax2 = self.offsets = None
+            self.absmax = torch.cat([s.absmax.float().reshape(-1).to(device) for s in states])
+            self.split = False
+        bounds = []
+        for b in blocks[:-1]:
+            bounds.append((bounds[-1] if bounds else 0) + b)
+        self.seg1, self.seg2 = (bounds + [ops.INT_MAX, ops.INT_MAX])[:2]
+        self.blocks = blocks
+        self.shape = (self.rows, self.cols)
+        # the bitsandbytes parameters now point at the group's bytes (no second copy)
+        off_p = off_a = 0
+        for p, s, b in zip(params, states, blocks):
+            p.data = self.packed[off_p:off_p + b * 32].view(-1, 1)
+            s.absmax = self.absmax[off_a:off_a + b]
+            off_p += b * 32
+            off_a += b
+
+    def _member(self, i):
+        """A view of member i as a single-weight group (for the split nested case)."""
+        m = NF4Group.__new__(NF4Group)
+        b0 = sum(self.blocks[:i])
+        b = self.blocks[i]
+        m.cols, m.rows = self.cols, self.rows_each[i]
+        m.shape = (m.rows, m.cols)
+        m.nested, m.code, m.bs2, m.code2 = self.nested, self.code, self.bs2, self.code2
+        m.packed = self.packed[b0 * 32:(b0 + b) * 32]
+        m.absmax = self.absmax[b0:b0 + b]
+        start2 = sum(-(-x // self.bs2) for x in self.blocks[:i])
+        m.absmax2 = self.absmax2[start2:start2 + -(-b // self.bs2)]
+        m.offsets = self.offsets[i:i + 1]
+        m.seg1 = m.seg2 = ops.INT_MAX
+        m.split = False
+        return m
+
+    def dequant(self, out, transpose=False):
+        """out [rows, cols] (or [cols, rows] with transpose) in out's 16-bit dtype."""
+        if not self.split:
+            return ops.nf4_dequant(self, out=out, transpose=transpose, dtype=out.dtype)
+        r0 = 0
+        for i, r in enumerate(self.rows_each):
+            part = out[:, r0:r0 + r] if transpose else out[r0:r0 + r]
+            if transpose and not part.is_contiguous():
+                tmp = torch.empty((self.cols, r), device=out.device, dtype=out.dtype)
+                self._member(i).dequant(tmp, transpose=True)
+                part.copy_(tmp)
+            else:
+                self._member(i).dequant(part, transpose=transpose)
+            r0 += r
+        return out
+
+
+# ---------------------------------------------------------------------------------------------
+# LoRA dropout masks: PyTorch's own (solution/engine.py:767-828)
+# ---------------------------------------------------------------------------------------------
+class TorchDropout:
+    """The LoRA dropout masks PEFT's nn.Dropout draws, bit for bit: each call takes the CUDA
+    generator's (seed, offset) and advances the offset as aten's dropout kernel does
+    (block 256, UNROLL 4, grid min(SMs * maxThreadsPerSM / 256, ceil(nelem / 256))); the
+    kernels of this library compute the mask from (seed, offset / 4, grid * 256) and the element
+    index, in backward again instead of storing it."""
+
+    BLOCK, UNROLL = 256, 4
+    CHECK_SEED = 20261031
+    CHECK_TOKENS = 64
+
+    def __init__(self, device, dtype):
+        self.device, self.dtype = device, dtype
+        self.ok = None
+        props = torch.cuda.get_device_properties(device)
+        self.max_blocks = props.multi_processor_count * (
+            props.max_threads_per_multi_processor // self.BLOCK)
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.gen = torch.cuda.default_generators[idx]
+        self.vec = 16 // torch.empty((), dtype=dtype).element_size()
+        assert self.vec in (4, 8), dtype
+
+    def draw(self, nelem):
+        """(seed, counter, threads) of a dropout call on nelem elements; advances the generator."""
+        assert nelem % self.vec == 0, nelem
+        blocks = min(self.max_blocks, (nelem + self.BLOCK - 1) // self.BLOCK)
+        increment = ((nelem - 1) // (self.BLOCK * blocks * self.UNROLL) + 1) * self.UNROLL
+        seed, offset = self.gen.initial_seed(), self.gen.get_offset()
+        self.gen.set_offset(offset + increment)
+        if seed >= 2**63:
+            seed -= 2**64
+        return seed, offset // 4, blocks * self.BLOCK
+
+    def check(self, B, T, H, p):
+        """Whether this library's mask is PyTorch's on this GPU: the RMSNorm kernel's dropout of
+        ones over [B, T, H] against torch._fused_dropout on a private generator (the default
+        generator is not touched)."""
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(self.CHECK_SEED)
+        ones = torch.ones((B, T, H), device=self.device, dtype=self.dtype)
+        _, ref = torch._fused_dropout(ones, 1.0 - p, gen)
+        nelem = B * T * H
+        blocks = min(self.max_blocks, (nelem + self.BLOCK - 1) // self.BLOCK)
+        tok = torch.arange(B * T, device=self.device)
+        drop = ops.Drop(tok, self.CHECK_SEED, 0, 0, blocks * self.BLOCK, p, self.vec,
+                        drop_q=True, drop_v=False)
+        x = torch.ones((B * T, H), device=self.device)
+        _, _, yq, _, _, _, _ = ops.rms_fwd(x, torch.ones(H, device=self.device), 1e-6,
+                                           write_y=False, drop=drop, want_yq=True)
+        return bool(torch.equal((yq != 0).view(B, T, H), ref.bool()))
+
+
+class UnsupportedBatch(ValueError):
+    """The fused step does not take this batch; raised before the step changes anything, so the
+    caller can run the original code instead (solution/engine.py:700-702)."""
+
+
+# ---------------------------------------------------------------------------------------------
+# per-step packing (solution/engine.py:705-764)
+# ---------------------------------------------------------------------------------------------
+class Packed:
+    """One micro-batch without its padding: the real tokens of every row back to back."""
+
+    def __init__(self, input_ids, attention_mask, labels):
+        if input_ids.dim() != 2 or attention_mask.shape != input_ids.shape \
+                or labels.shape != input_ids.shape:
+            raise UnsupportedBatch("inputs are not [rows, tokens]")
+        B, T = input_ids.shape
+        dev = input_ids.device
+        lengths = attention_mask.sum(dim=1)
+        lengths_cpu = lengths.tolist()
+        expected = torch.arange(T, device=dev)[None, :] < lengths[:, None]
+        if not bool(torch.equal(attention_mask.bool(), expected)):
+            raise UnsupportedBatch("attention_mask is not right-padded")
+        flat = expected.reshape(-1).nonzero().squeeze(1)
+        self.n = int(flat.numel())
+        self.tok = flat
+        self.T, self.rows = T, B
+        self.lengths = [int(x) for x in lengths_cpu]
+        self.max_len = max(self.lengths) if self.lengths else 0
+        self.ids = input_ids.reshape(-1)[flat].contiguous()
+        self.pos = (flat % T).to(torch.int32)
+        shifted = torch.full_like(labels, -100)
+        shifted[:, :-1] = labels[:, 1:]
+        self.targets = shifted.reshape(-1)[flat].contiguous()
+        supervised = self.targets >= 0
+        self.head_order = torch.argsort((~supervised).to(torch.int8), stable=True)
+        self.n_supervised = int(supervised.sum())
+        cu = [0]
+        for length in self.lengths:
+            cu.append(cu[-1] + length)
+        self.cu_seqlens = torch.tensor(cu, device=dev, dtype=torch.int32)
+        self.row_of_token = torch.repeat_interleave(torch.arange(B, device=dev), lengths)
+
+
+class RopeTable:
+    """cos / sin of the model's rotary embedding, first half of head_dim (Qwen2 repeats it)."""
+
+    def __init__(self, rotary, head_dim, device):
+        self.rotary, self.half, self.device = rotary, head_dim // 2, device
+        self.cos = self.sin = None
+
+    def table(self, length):
+        if self.cos is None or self.cos.shape[0] < length:
+            size = max(1024, 1 << max(0, (length - 1).bit_length()))
+            dummy = torch.zeros(1, device=self.device, dtype=torch.float32)
+            pos = torch.arange(size, device=self.device)[None, :]
+            with torch.no_grad():
+                cos, sin = self.rotary(dummy, pos)
+            cos, sin = cos[0].float(), sin[0].float()
+            if not (torch.equal(cos[:, :self.half], cos[:, self.half:])
+                    and torch.equal(sin[:, :self.half], sin[:, self.half:])):
+                raise ValueError("rotary table is not rotate_half style")
+            self.cos = cos[:, :self.half].contiguous()
+            self.sin = sin[:, :self.half].contiguous()
+        return self.cos, self.sin
+
+
+class HeadStats:
+    """What the head hands back for the logged metrics: row order, per-token loss, entropy,
+    correct (solution/engine.py:1343-1349)."""
+
+
+# ---------------------------------------------------------------------------------------------
+# one decoder layer's weights (solution/engine.py:872-915)
+# ---------------------------------------------------------------------------------------------
+def _base(module):
+    return getattr(module, "base_layer", module)
+
+
+def _lora_targets(layer):
+    found = {}
+    for short, module in (("q", layer.self_attn.q_proj), ("k", layer.self_attn.k_proj),
+                          ("v", layer.self_attn.v_proj)):
+        names = getattr(module, "active_adapters", None)
+        if names:
+            found[short] = names[0]
+    return found
+
+
+def _lora_dropout(layer, lora_names):
+    ps = set()
+    for short, name in lora_names.items():
+        drop = getattr(layer.self_attn, f"{short}_proj").lora_dropout[name]
+        ps.add(float(getattr(drop, "p", 0.0)))
+    assert len(ps) <= 1
+    return ps.pop() if ps else 0.0
+
+
+def _lora_input_dtype(layer, lora_names):
+    """dtype of the tensor PEFT's LoRA dropout runs on (solution/engine.py:1935-1946): the fp32
+    norm output under prepare_model_for_kbit_training, promoted with lora_A's dtype."""
+    dtypes = {layer.input_layernorm.weight.dtype}
+    for short, name in lora_names.items():
+        dtypes.add(getattr(layer.self_attn, f"{short}_proj").lora_A[name].weight.dtype)
+    out = dtypes.pop()
+    for d in dtypes:
+        out = torch.promote_types(out, d)
+    return out
+
+
+class LayerSpec:
+    def __init__(self, layer, config, lora_names, index, device, dtype):
+        attn, mlp = layer.self_attn, layer.mlp
+        self.index = index
+        self.H = config.hidden_size
+        self.D = getattr(config, "head_dim", None) or self.H // config.num_attention_heads
+        self.HQ = config.num_attention_heads
+        self.HKV = config.num_key_value_heads
+        self.I = config.intermediate_size
+        self.C = (self.HQ + 2 * self.HKV) * self.D
+        self.eps = float(layer.input_layernorm.variance_epsilon)
+        self.ln1 = layer.input_layernorm.weight.detach().float().contiguous()
+        self.ln2 = layer.post_attention_layernorm.weight.detach().float().contiguous()
+        self.scale = float(attn.scaling)
+        w = lambda m: _base(m).weight  # noqa: E731
+        self.qkv = NF4Group([w(attn.q_proj), w(attn.k_proj), w(attn.v_proj)], device)
+        self.o = NF4Group([w(attn.o_proj)], device)
+        self.gu = NF4Group([w(mlp.gate_proj), w(mlp.up_proj)], device)
+        self.down = NF4Group([w(mlp.down_proj)], device)
+        biases = [_base(getattr(attn, f"{s}_proj")).bias for s in ("q", "k", "v")]
+        if any(b is None for b in biases):
+            biases = [b if b is not None else torch.zeros(_base(getattr(attn, f"{s}_proj"))
+                                                          .weight.quant_state.shape[0],
+                                                          device=device)
+                      for b, s in zip(biases, ("q", "k", "v"))]
+        self.bias_qkv = torch.cat([b.detach().to(dtype) for b in biases]).contiguous()
+        self.lora = {}
+        for short in ("q", "v"):
+            module = getattr(attn, f"{short}_proj")
+            if short in lora_names:
+                name = lora_names[short]
+                self.lora[short] = (module.lora_A[name].weight, module.lora_B[name].weight,
+                                    float(module.scaling[name]))
+        if set(self.lora) != {"q", "v"}:
+            raise ValueError("the fused step needs LoRA on q_proj and v_proj of every layer")
+        self.lora_scale = self.lora["q"][2]
+        assert self.lora["v"][2] == self.lora_scale
+
+    def lora_params(self):
+        return [self.lora["q"][0], self.lora["q"][1], self.lora["v"][0], self.lora["v"][1]]
+
+
+# ---------------------------------------------------------------------------------------------
+# the model
+# ---------------------------------------------------------------------------------------------
+class FusedQwen2:
+    """Holds what the step needs from a PEFT-wrapped, 4-bit Qwen2ForCausalLM."""
+
+    def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK):
+        causal = peft_model.get_base_model()
+        inner = causal.model
+        config = causal.config
+        self.dtype = dtype
+        self.device = inner.norm.weight.device
+        lora_names = _lora_targets(inner.layers[0])
+        if "k" in lora_names:
+            raise NotImplementedError("LoRA on k_proj")
+        self.layers = [LayerSpec(layer, config, lora_names, i, self.device, dtype)
+                       for i, layer in enumerate(inner.layers)]
+        spec = self.layers[0]
+        self.dropout_p = _lora_dropout(inner.layers[0], lora_names)
+        self.dropout = TorchDropout(self.device, _lora_input_dtype(inner.layers[0], lora_names)) \
+            if self.dropout_p > 0 else None
+        self.drop_vec = self.dropout.vec if self.dropout is not None else 4
+        self.norm_w = inner.norm.weight.detach().float().contiguous()
+        self.eps = float(inner.norm.variance_epsilon)
+        self.embed = inner.embed_tokens.weight.detach().to(dtype).contiguous()
+        lm = causal.lm_head.weight.detach()
+        self.lm_w = self.embed if lm.data_ptr() == inner.embed_tokens.weight.data_ptr() \
+            and lm.dtype == dtype else lm.to(dtype).contiguous()
+        # the head's data-gradient GEMM reads the lm_head weight K-major along the vocabulary
+        self.lm_wT = self.lm_w.t().contiguous()
+        self.V = self.lm_w.shape[0]
+        self.rope = RopeTable(inner.rotary_emb, spec.D, self.device)
+        self.head_chunk = head_chunk
+        self._logits = None
+        # fp32 LoRA weights (PEFT owns them) and one 16-bit shadow buffer refreshed per step
+        self.lora_fp32 = [t for s in self.layers for t in s.lora_params()]
+        sizes = [t.numel() for t in self.lora_fp32]
+        self.lora_total = sum(sizes)
+        self.lora_buf = torch.empty(self.lora_total, device=self.device, dtype=dtype)
+        self.lora_views, start = [], 0
+        for t, n in zip(self.lora_fp32, sizes):
+            self.lora_views.append(self.lora_buf[start:start + n].view(t.shape))
+            start += n
+        self.offsets = [0]
+        for n in sizes:
+            self.offsets.append(self.offsets[-1] + n)
+        self.process_group = None
+        self.data_parallel = False  # LoRA gradients averaged over the ranks (dist.GradReducer)
+
+    def set_data_parallel(self, group=None):
+        """Average the LoRA gradients over `group` (None: the default process group) inside the
+        backward, one bucket per layer as it finishes, overlapped with the layers below it."""
+        self.process_group = group
+        self.data_parallel = True
+
+    def logits_buffer(self, rows):
+        if self._logits is None or self._logits.shape[0] < rows:
+            self._logits = torch.empty((rows, self.V), device=self.device, dtype=self.dtype)
+        return self._logits[:rows]
+
+    def step(self, input_ids, attention_mask, labels, denom):
+        """One training step's forward: (loss, packed, stats); autograd runs the backward."""
+        packed = Packed(input_ids, attention_mask, labels)
+        spec = self.layers[0]
+        if self.dropout is not None and self.dropout.ok is None:
+            self.dropout.ok = self.dropout.check(
+                packed.rows, min(packed.T, TorchDropout.CHECK_TOKENS), spec.H, self.dropout_p)
+        if self.dropout is not None and not self.dropout.ok:
+            raise UnsupportedBatch("LoRA dropout masks differ from PyTorch's (TorchDropout.check)")
+        with torch.no_grad():
+            torch._foreach_copy_(self.lora_views, self.lora_fp32)
+        stats = HeadStats()
+        loss = _FusedStep.apply(self, packed, float(denom), stats, *self.lora_fp32)
+        return loss, packed, stats
+
+    # -----------------------------------------------------------------------------------------
+    # forward
+    # -----------------------------------------------------------------------------------------
+    def _drop(self, packed, H):
+        if self.dropout is None:
+            return ops.Drop(packed.tok, 0, 0, 0, 1, 0.0, 4)
+        nelem = packed.rows * packed.T * H
+        seed, ctr_q, threads = self.dropout.draw(nelem)
+        seed_v, ctr_v, threads_v = self.dropout.draw(nelem)
+        assert seed_v == seed and threads_v == threads
+        return ops.Drop(packed.tok, seed, ctr_q, ctr_v, threads, self.dropout_p, self.drop_vec)
+
+    def _forward(self, packed, denom, stats):
+        n = packed.n
+        cos, sin = self.rope.table(max(packed.max_len, 1))
+        h = ops.embed(packed.ids, self.embed)
+        saved = []
+        for spec in self.layers:
+            drop = self._drop(packed, spec.H)
+            h, sv = self._layer_fwd(spec, h, packed, drop, cos, sin)
+            saved.append(sv)
+        dhp, loss = self._head(h, packed, denom, stats) if n else (None, None)
+        if loss is None:
+            loss = torch.zeros((), device=self.device)
+        return loss, saved, dhp
+
+    def _layer_fwd(self, spec, h, packed, drop, cos, sin):
+        n, H, D, HQ, HKV, I = packed.n, spec.H, spec.D, spec.HQ, spec.HKV, spec.I
+        dt, dev = self.dtype, self.device
+        Aq, Bq, Av, Bv = self.lora_views[4 * spec.index:4 * spec.index + 4]
+        # input RMSNorm + dropped LoRA inputs + LoRA-A products
+        _, a, yq, yv, rstd1, xq, xv = ops.rms_fwd(h, spec.ln1, spec.eps, dtype=dt, drop=drop,
+                                                  Aq=Aq, Av=Av, want_yq=True)
+        w = spec.qkv.dequant(torch.empty((spec.C, H), device=dev, dtype=dt))
+        qkv = ops.gemm(a, w, bias=spec.bias_qkv)
+        del a, w
+        q, k, v = ops.rope_fwd(qkv, cos, sin, packed.pos, HQ, HKV, D, spec.lora_scale, xq=xq,
+                               xv=xv, Bq=Bq, Bv=Bv)
+        del qkv
+        out, lse = ops.attn_fwd(q, k, v, packed.cu_seqlens, packed.max_len, spec.scale)
+        w = spec.o.dequant(torch.empty((H, HQ * D), device=dev, dtype=dt))
+        h2 = ops.gemm(out.view(n, HQ * D), w, out_dtype=torch.float32, residual=h)
+        del w
+        _, b, _, _, rstd2, _, _ = ops.rms_fwd(h2, spec.ln2, spec.eps, dtype=dt)
+        w = spec.gu.dequant(torch.empty((2 * I, H), device=dev, dtype=dt))
+        gu = ops.gemm(b, w)
+        del b, w
+        m = ops.glu_fwd(gu, I)
+        w = spec.down.dequant(torch.empty((H, I), device=dev, dtype=dt))
+        h3 = ops.gemm(m, w, out_dtype=torch.float32, residual=h2)
+        del m, w
+        return h3, (h, rstd1, yq, yv, xq, xv, q, k, v, out, lse, h2, rstd2, gu, drop)
+
+    def _head(self, h, packed, denom, stats):
+        """Final norm, lm_head, cross-entropy and the logged metrics over chunks of rows taken
+        supervised-first, with the gradient w.r.t. the final hidden state formed here
+        (solution/engine.py:1352-1400). Returns (dh in head order, loss)."""
+        n, H = h.shape
+        dev, dt = self.device, self.dtype
+        order = packed.head_order
+        n_sup = packed.n_supervised
+        hp = ops.gather_rows(h, order)
+        targets = packed.targets.index_select(0, order)
+        _, hn, _, _, rstd, _, _ = ops.rms_fwd(hp, self.norm_w, self.eps, dtype=dt)
+        tok_loss = torch.empty((n,), device=dev, dtype=torch.float32)
+        entropy = torch.empty((n,), device=dev, dtype=torch.float32)
+        correct = torch.empty((n,), device=dev, dtype=torch.int32)
+        dhp = torch.empty_like(hp)
+        if n_sup < n:
+            dhp[n_sup:].zero_()
+        inv = 1.0 / denom if denom else float("nan")  # 0 / 0, as in the base
+        for c0 in range(0, n, self.head_chunk):
+            c1 = min(n, c0 + self.head_chunk)
+            logits = ops.gemm(hn[c0:c1], self.lm_w, out=self.logits_buffer(c1 - c0))
+            sup = max(0, min(c1, n_sup) - c0)
+            ops.ce_rows(logits, targets[c0:c1], write_grad=sup > 0, loss=tok_loss[c0:c1],
+                        entropy=entropy[c0:c1], correct=correct[c0:c1])
+            if sup:
+                dhn = ops.gemm(logits[:sup], self.lm_wT)
+                ops.rms_bwd(dhn, hp[c0:c0 + sup], rstd[c0:c0 + sup], self.norm_w, dtype=dt,
+                            grad_scale=inv, out=dhp[c0:c0 + sup])
+        stats.order, stats.tok_loss, stats.entropy, stats.correct = order, tok_loss, entropy, correct
+        return dhp, tok_loss.sum() * inv
+
+    # -----------------------------------------------------------------------------------------
+    # backward
+    # -----------------------------------------------------------------------------------------
+    def _backward(self, packed, saved, dhp, grad):
+        n = packed.n
+        H = self.layers[0].H
+        grads = torch.zeros(self.lora_total, device=self.device, dtype=torch.float32)
+        views = [grads[self.offsets[i]:self.offsets[i + 1]].view(t.shape)
+                 for i, t in enumerate(self.lora_fp32)]
+        reducer = None
+        if self.data_parallel:
+            from .dist import GradReducer
+
+            reducer = GradReducer(self.process_group)
+        if n:
+            cos, sin = self.rope.table(max(packed.max_len, 1))
+            dh = torch.empty((n, H), device=self.device, dtype=torch.float32)
+            dh16 = torch.empty((n, H), device=self.device, dtype=self.dtype)
+            g = grad.detach().float().reshape(1).contiguous()
+            ops.scatter_rows(dhp, packed.head_order, dh, scale=g, out16=dh16)
+            for spec in reversed(self.layers):
+                sv = saved[spec.index]
+                saved[spec.index] = None
+                dh, dh16 = self._layer_bwd(spec, sv, dh, dh16, views[4 * spec.index:4 * spec.index + 4],
+                                           packed, cos, sin, need_dh=spec.index > 0)
+                if reducer is not None:
+                    lo, hi = self.offsets[4 * spec.index], self.offsets[4 * spec.index + 4]
+                    reducer.launch(grads[lo:hi])
+        elif reducer is not None:
+            reducer.launch(grads)
+        if reducer is not None:
+            reducer.finish(grads)
+        return views
+
+    def _layer_bwd(self, spec, sv, dh3, dh3_16, grads, packed, cos, sin, need_dh):
+        h, rstd1, yq, yv, xq, xv, q, k, v, out, lse, h2, rstd2, gu, drop = sv
+        n, H, D, HQ, HKV, I = packed.n, spec.H, spec.D, spec.HQ, spec.HKV, spec.I
+        dt, dev = self.dtype, self.device
+        Aq, Bq, Av, Bv = self.lora_views[4 * spec.index:4 * spec.index + 4]
+        gAq, gBq, gAv, gBv = grads
+        s = spec.lora_scale
+        # MLP
+        wt = spec.down.dequant(torch.empty((I, H), device=dev, dtype=dt), transpose=True)
+        dm = ops.gemm(dh3_16, wt)
+        del wt
+        ops.glu_bwd(dm, gu, I)
+        del dm
+        wt = spec.gu.dequant(torch.empty((H, 2 * I), device=dev, dtype=dt), transpose=True)
+        db = ops.gemm(gu, wt)
+        del wt, gu
+        dh2_16 = torch.empty((n, H), device=dev, dtype=dt)
+        dh2 = ops.rms_bwd(db, h2, rstd2, spec.ln2, dtype=dt, dres=dh3, out16=dh2_16)
+        del db
+        # attention
+        wt = spec.o.dequant(torch.empty((HQ * D, H), device=dev, dtype=dt), transpose=True)
+        dout = ops.gemm(dh2_16, wt).view(n, HQ, D)
+        del wt
+        dq, dk, dv = ops.attn_bwd(dout, q, k, v, out, lse, packed.cu_seqlens, packed.max_len,
+                                  spec.scale)
+        del dout
+        dqkv, dxq, dxv = ops.rope_bwd(dq, dk, dv, cos, sin, packed.pos, HQ, HKV, D, dtype=dt,
+                                      Bq=Bq, Bv=Bv, lora_scale=s)
+        del dq, dk, dv
+        # LoRA weight gradients: dB = s g^T x_lo, dA = dx_lo^T drop(a)
+        ops.lora_colsum(dqkv[:, :HQ * D], xq, scale=s, out=gBq)
+        ops.lora_colsum(dqkv[:, (HQ + HKV) * D:], xv, scale=s, out=gBv)
+        ops.lora_colsum(yq, dxq, transpose=True, out=gAq)
+        ops.lora_colsum(yv, dxv, transpose=True, out=gAv)
+        if not need_dh:  # the first layer's input is the frozen embedding
+            return None, None
+        wt = spec.qkv.dequant(torch.empty((H, spec.C), device=dev, dtype=dt), transpose=True)
+        da = ops.gemm(dqkv, wt)
+        del wt, dqkv
+        dh16 = torch.empty((n, H), device=dev, dtype=dt)
+        dh = ops.rms_bwd(da, h, rstd1, spec.ln1, dtype=dt, dres=dh2, dxlo_q=dxq, dxlo_v=dxv,
+                         Aq=Aq, Av=Av, drop=drop, out16=dh16)
+        return dh, dh16
+
+
+class _FusedStep(torch.autograd.Function):
+    """The whole model as one autograd node: its inputs are the fp32 LoRA weights, its output the
+    loss; backward returns their gradients (the frozen base gets none)."""
+
+    @staticmethod
+    def forward(ctx, engine, packed, denom, stats, *lora):
+        loss, saved, dhp = engine._forward(packed, denom, stats)
+        ctx.engine, ctx.packed, ctx.saved, ctx.dhp = engine, packed, saved, dhp
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad):
+        grads = ctx.engine._backward(ctx.packed, ctx.saved, ctx.dhp, grad)
+        ctx.saved = ctx.dhp = None
+        return (None, None, None, None, *grads)

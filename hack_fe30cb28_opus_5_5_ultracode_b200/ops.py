@@ -55,7 +55,19 @@ def nf4_dequant(w, out=None, transpose=False, dtype=torch.float16):
 # ---------------------------------------------------------------------------------------------
 # GEMM
 # ---------------------------------------------------------------------------------------------
-def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None):
+_GEMM_EVENTS = None  # while measuring: [(start event, end event, flops)] of every GEMM launch
+
+
+def record_gemms(on=True):
+    """Start (or stop, returning the records) timing every GEMM launch with CUDA events on the
+    launching stream; bench.py uses it for the dominant kernel's live roofline."""
+    global _GEMM_EVENTS
+    out = _GEMM_EVENTS
+    _GEMM_EVENTS = [] if on else None
+    return out
+
+
+def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=None):
     """out[M, N] (+)= a[M, K] @ b[N, K]^T (+ bias) on tcgen05. a and b: fp16 or bf16 with unit
     column stride; out: fp16 / bf16 / fp32 with unit column stride."""
     M, K = a.shape
@@ -71,10 +83,25 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None):
         raise ValueError("gemm needs unit column strides")
     if bias is not None and bias.dtype != a.dtype:
         raise ValueError("bias must have the input dtype")
+    if residual is not None and (residual.stride(0) != out.stride(0) or residual.stride(1) != 1):
+        raise ValueError("residual must share the output's row stride")
+    ev = _GEMM_EVENTS
+    if ev is not None:
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
     call("ql_gemm_tn", _ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out), out.stride(0),
          _ptr(bias), M, N, K, dtype_code(a.dtype), dtype_code(out.dtype), int(accumulate),
-         stream_ptr())
+         _ptr(residual), stream_ptr())
+    if ev is not None:
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        ev.append((start, end, 2.0 * M * N * K))
     return out
+
+
+def launch_count():
+    """Kernels launched through the library so far (its own counter)."""
+    return int(_lib.lib().ql_launch_count())
 
 
 def device_status(clear=True):
@@ -84,3 +111,248 @@ def device_status(clear=True):
     v = ctypes.c_int(0)
     call("ql_device_status", ctypes.addressof(v), int(clear))
     return v.value
+
+
+# ---------------------------------------------------------------------------------------------
+# dropout / RMSNorm
+# ---------------------------------------------------------------------------------------------
+class Drop:
+    """The LoRA dropout state of one layer's two masks (TorchDropout.draw, engine.py:787-797):
+    tok = packed tokens' indices in the padded batch, seed, Philox counters of the q and v
+    calls, the dropout kernel's threads, p, VEC."""
+
+    def __init__(self, tok, seed, ctr_q, ctr_v, threads, p, vec=4, drop_q=True, drop_v=True):
+        self.tok, self.seed, self.ctr_q, self.ctr_v = tok, int(seed), int(ctr_q), int(ctr_v)
+        self.threads, self.p, self.vec = int(threads), float(p), int(vec)
+        self.drop_q, self.drop_v = bool(drop_q), bool(drop_v)
+
+    def fields(self):
+        return dict(tok=_ptr(self.tok), seed=self.seed, ctr_q=self.ctr_q, ctr_v=self.ctr_v,
+                    threads=self.threads, p_keep=1.0 - self.p, keep_scale=1.0 / (1.0 - self.p),
+                    vec=self.vec, drop_q=int(self.drop_q), drop_v=int(self.drop_v))
+
+
+def dropout_keep(nelem, seed, ctr, threads, p, vec=4, device="cuda"):
+    out = torch.empty(nelem, device=device, dtype=torch.int8)
+    call("ql_dropout_keep", _ptr(out), nelem, int(seed), int(ctr), int(threads), 1.0 - p,
+         int(vec), stream_ptr())
+    return out
+
+
+def rms_fwd(x, w, eps, dtype=torch.float16, delta=None, write_y=True, drop=None, Aq=None,
+            Av=None, want_yq=False, out_y=None, out_xsum=None):
+    """(xsum, y, yq, yv, rstd, xq, xv) of reference _rms_fwd (engine.py:947-966), with the
+    LoRA-A products xq / xv when Aq / Av are given."""
+    n, H = x.shape
+    dev = x.device
+    xsum = (out_xsum if out_xsum is not None else torch.empty_like(x)) if delta is not None else x
+    y = (out_y if out_y is not None else torch.empty((n, H), device=dev, dtype=dtype)) \
+        if write_y else None
+    dq = drop is not None and drop.drop_q
+    dv = drop is not None and drop.drop_v
+    yq = torch.empty((n, H), device=dev, dtype=dtype) if dq and want_yq else None
+    yv = torch.empty((n, H), device=dev, dtype=dtype) if dv and want_yq else None
+    xq = torch.empty((n, 16), device=dev, dtype=dtype) if dq and Aq is not None else None
+    xv = torch.empty((n, 16), device=dev, dtype=dtype) if dv and Av is not None else None
+    rstd = torch.empty((n,), device=dev, dtype=torch.float32)
+    fields = dict(x=_ptr(x), delta=_ptr(delta), w=_ptr(w), xsum=_ptr(xsum) if delta is not None
+                  else None, y=_ptr(y), yq=_ptr(yq), yv=_ptr(yv), rstd=_ptr(rstd),
+                  Aq=_ptr(Aq) if dq else None, Av=_ptr(Av) if dv else None, xq=_ptr(xq),
+                  xv=_ptr(xv), n=n, H=H, rank=16, dtype=dtype_code(dtype), eps=float(eps),
+                  vec=4)
+    if drop is not None:
+        fields.update(drop.fields())
+    args = _lib.struct("ql_rms_fwd_args", **fields)
+    call("ql_rms_fwd", ctypes_ref(args), stream_ptr())
+    return xsum, y, yq, yv, rstd, xq, xv
+
+
+def rms_bwd(dy, x, rstd, w, dtype=torch.float16, dres=None, tq=None, tv=None, dxlo_q=None,
+            dxlo_v=None, Aq=None, Av=None, drop=None, grad_scale=1.0, out=None, out16=None):
+    """Reference _rms_bwd (engine.py:969-981); dx fp32 (and its 16-bit copy into out16)."""
+    n, H = x.shape
+    dx = out if out is not None else torch.empty_like(x)
+    fields = dict(dy=_ptr(dy), ld_dy=dy.stride(0), x=_ptr(x), rstd=_ptr(rstd), w=_ptr(w),
+                  dres=_ptr(dres), dx=_ptr(dx), dx16=_ptr(out16), tq=_ptr(tq), tv=_ptr(tv),
+                  dxlo_q=_ptr(dxlo_q), dxlo_v=_ptr(dxlo_v), Aq=_ptr(Aq), Av=_ptr(Av), n=n, H=H,
+                  rank=16, dtype=dtype_code(dtype), grad_scale=float(grad_scale), vec=4)
+    if drop is not None:
+        fields.update(drop.fields())
+    args = _lib.struct("ql_rms_bwd_args", **fields)
+    call("ql_rms_bwd", ctypes_ref(args), stream_ptr())
+    return dx
+
+
+def ctypes_ref(s):
+    import ctypes
+
+    return ctypes.addressof(s)
+
+
+# ---------------------------------------------------------------------------------------------
+# qkv + RoPE
+# ---------------------------------------------------------------------------------------------
+def rope_fwd(qkv, cos, sin, pos, HQ, HKV, D, lora_scale, lq=None, lv=None, xq=None, xv=None,
+             Bq=None, Bv=None, out=None):
+    n = qkv.shape[0]
+    dev, dt = qkv.device, qkv.dtype
+    if out is None:
+        q = torch.empty((n, HQ, D), device=dev, dtype=dt)
+        k = torch.empty((n, HKV, D), device=dev, dtype=dt)
+        v = torch.empty((n, HKV, D), device=dev, dtype=dt)
+    else:
+        q, k, v = out
+    args = _lib.struct("ql_rope_fwd_args", qkv=_ptr(qkv), lq=_ptr(lq), lv=_ptr(lv), xq=_ptr(xq),
+                       xv=_ptr(xv), Bq=_ptr(Bq), Bv=_ptr(Bv), cos=_ptr(cos), sin=_ptr(sin),
+                       pos=_ptr(pos), q=_ptr(q), k=_ptr(k), v=_ptr(v),
+                       lora_scale=float(lora_scale), n=n, HQ=HQ, HKV=HKV, D=D, rank=16,
+                       dtype=dtype_code(dt))
+    call("ql_rope_fwd", ctypes_ref(args), stream_ptr())
+    return q, k, v
+
+
+def rope_bwd(dq, dk, dv, cos, sin, pos, HQ, HKV, D, dtype=torch.float16, Bq=None, Bv=None,
+             lora_scale=1.0, out=None):
+    """(dqkv, dxlo_q, dxlo_v): the pre-rotary qkv gradient and, with Bq / Bv, the LoRA-A
+    output gradients s * (g . B) (fp32)."""
+    n = dq.shape[0]
+    dev = dq.device
+    C = (HQ + 2 * HKV) * D
+    dqkv = out if out is not None else torch.empty((n, C), device=dev, dtype=dtype)
+    dxlo_q = torch.empty((n, 16), device=dev, dtype=torch.float32) if Bq is not None else None
+    dxlo_v = torch.empty((n, 16), device=dev, dtype=torch.float32) if Bv is not None else None
+    args = _lib.struct("ql_rope_bwd_args", dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv), cos=_ptr(cos),
+                       sin=_ptr(sin), pos=_ptr(pos), dqkv=_ptr(dqkv), Bq=_ptr(Bq), Bv=_ptr(Bv),
+                       dxlo_q=_ptr(dxlo_q), dxlo_v=_ptr(dxlo_v), lora_scale=float(lora_scale),
+                       n=n, HQ=HQ, HKV=HKV, D=D, kv_heads_in=dk.shape[1], rank=16,
+                       dtype=dtype_code(dtype), grad_dtype=dtype_code(dq.dtype))
+    call("ql_rope_bwd", ctypes_ref(args), stream_ptr())
+    return dqkv, dxlo_q, dxlo_v
+
+
+# ---------------------------------------------------------------------------------------------
+# SwiGLU, LoRA weight gradients, embedding
+# ---------------------------------------------------------------------------------------------
+def glu_fwd(gu, I, out=None):
+    n = gu.shape[0]
+    m = out if out is not None else torch.empty((n, I), device=gu.device, dtype=gu.dtype)
+    call("ql_glu_fwd", _ptr(gu), _ptr(m), n, I, dtype_code(gu.dtype), stream_ptr())
+    return m
+
+
+def glu_bwd(dm, gu, I):
+    call("ql_glu_bwd", _ptr(dm), _ptr(gu), gu.shape[0], I, dtype_code(gu.dtype), stream_ptr())
+    return gu
+
+
+def lora_colsum(X, Y, scale=1.0, transpose=False, out=None, workspace=None):
+    """scale * X^T Y as [ncols, R] (or [R, ncols] with transpose), fp32; X [n, ncols] may be a
+    column slice (unit column stride)."""
+    n, ncols = X.shape
+    R = Y.shape[1]
+    if out is None:
+        out = torch.empty((R, ncols) if transpose else (ncols, R), device=X.device,
+                          dtype=torch.float32)
+    need = int(_lib.lib().ql_lora_colsum_workspace(n, ncols, R))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=X.device, dtype=torch.float32)
+    call("ql_lora_colsum", _ptr(X), X.stride(0), dtype_code(X.dtype), _ptr(Y),
+         dtype_code(Y.dtype), n, ncols, R, float(scale), int(transpose), _ptr(out),
+         _ptr(workspace), workspace.numel(), stream_ptr())
+    return out
+
+
+def embed(ids, W, out=None):
+    n = ids.numel()
+    h = out if out is not None else torch.empty((n, W.shape[1]), device=W.device,
+                                                dtype=torch.float32)
+    call("ql_embed", _ptr(ids), _ptr(W), _ptr(h), n, W.shape[1], W.shape[0],
+         dtype_code(W.dtype), stream_ptr())
+    return h
+
+
+# ---------------------------------------------------------------------------------------------
+# cross-entropy head
+# ---------------------------------------------------------------------------------------------
+def ce_rows(logits, target, write_grad=True, zero_unsupervised=False, loss=None, entropy=None,
+            correct=None):
+    rows, V = logits.shape
+    dev = logits.device
+    loss = loss if loss is not None else torch.empty(rows, device=dev, dtype=torch.float32)
+    entropy = entropy if entropy is not None else torch.empty(rows, device=dev,
+                                                              dtype=torch.float32)
+    correct = correct if correct is not None else torch.empty(rows, device=dev,
+                                                              dtype=torch.int32)
+    args = _lib.struct("ql_ce_rows_args", logits=_ptr(logits), target=_ptr(target),
+                       loss=_ptr(loss), entropy=_ptr(entropy), correct=_ptr(correct), rows=rows,
+                       V=V, ld=logits.stride(0), write_grad=int(write_grad),
+                       zero_unsupervised=int(zero_unsupervised), dtype=dtype_code(logits.dtype))
+    call("ql_ce_rows", ctypes_ref(args), stream_ptr())
+    return loss, entropy, correct
+
+
+def ce_piece(logits, w, target, state, best_idx, xt, alpha, wt, v0, n_sup):
+    rows, width = logits.shape
+    args = _lib.struct("ql_ce_piece_args", logits=_ptr(logits), w=_ptr(w), target=_ptr(target),
+                       state=_ptr(state), best_idx=_ptr(best_idx), xt=_ptr(xt),
+                       alpha=_ptr(alpha), wt=_ptr(wt), rows=rows, v0=int(v0), width=width,
+                       ld=logits.stride(0), n_sup=int(n_sup), H=w.shape[1],
+                       dtype=dtype_code(logits.dtype))
+    call("ql_ce_piece", ctypes_ref(args), stream_ptr())
+
+
+def ce_finish(state, best_idx, xt, target, loss, entropy, correct, acc, wt, dh, n_sup):
+    args = _lib.struct("ql_ce_finish_args", state=_ptr(state), best_idx=_ptr(best_idx),
+                       xt=_ptr(xt), target=_ptr(target), loss=_ptr(loss),
+                       entropy=_ptr(entropy), correct=_ptr(correct), acc=_ptr(acc),
+                       wt=_ptr(wt), dh=_ptr(dh), rows=state.shape[0], n_sup=int(n_sup),
+                       H=acc.shape[1], dtype=dtype_code(dh.dtype))
+    call("ql_ce_finish", ctypes_ref(args), stream_ptr())
+
+
+# ---------------------------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------------------------
+def attn_fwd(q, k, v, cu_seqlens, max_len, scale, out=None, lse=None):
+    n, HQ, D = q.shape
+    HKV = k.shape[1]
+    out = out if out is not None else torch.empty_like(q)
+    lse = lse if lse is not None else torch.empty((HQ, n), device=q.device, dtype=torch.float32)
+    args = _lib.struct("ql_attn_fwd_args", q=_ptr(q), k=_ptr(k), v=_ptr(v),
+                       cu_seqlens=_ptr(cu_seqlens), out=_ptr(out), lse=_ptr(lse),
+                       scale=float(scale), n=n, B=cu_seqlens.numel() - 1, max_len=int(max_len),
+                       HQ=HQ, HKV=HKV, D=D, dtype=dtype_code(q.dtype))
+    call("ql_attn_fwd", ctypes_ref(args), stream_ptr())
+    return out, lse
+
+
+def attn_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len, scale, dq=None, dk=None, dv=None,
+             dvec=None):
+    n, HQ, D = q.shape
+    HKV = k.shape[1]
+    dev = q.device
+    dq = dq if dq is not None else torch.empty((n, HQ, D), device=dev, dtype=torch.float32)
+    dk = dk if dk is not None else torch.empty((n, HKV, D), device=dev, dtype=torch.float32)
+    dv = dv if dv is not None else torch.empty((n, HKV, D), device=dev, dtype=torch.float32)
+    dvec = dvec if dvec is not None else torch.empty((HQ, n), device=dev, dtype=torch.float32)
+    args = _lib.struct("ql_attn_bwd_args", q=_ptr(q), k=_ptr(k), v=_ptr(v), out=_ptr(out),
+                       dout=_ptr(dout), lse=_ptr(lse), cu_seqlens=_ptr(cu_seqlens),
+                       dvec=_ptr(dvec), dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv),
+                       scale=float(scale), n=n, B=cu_seqlens.numel() - 1, max_len=int(max_len),
+                       HQ=HQ, HKV=HKV, D=D, dtype=dtype_code(q.dtype))
+    call("ql_attn_bwd", ctypes_ref(args), stream_ptr())
+    return dq, dk, dv
+
+
+def gather_rows(src, idx, out=None):
+    n, H = idx.numel(), src.shape[1]
+    out = out if out is not None else torch.empty((n, H), device=src.device, dtype=torch.float32)
+    call("ql_gather_rows", _ptr(src), _ptr(idx), _ptr(out), n, H, stream_ptr())
+    return out
+
+
+def scatter_rows(src, idx, out, scale=None, out16=None):
+    n, H = src.shape
+    call("ql_scatter_rows", _ptr(src), _ptr(idx), _ptr(scale), _ptr(out), _ptr(out16), n, H,
+         dtype_code(out16.dtype) if out16 is not None else 0, stream_ptr())
+    return out

@@ -39,6 +39,8 @@ const char* ql_last_error(void);
 int ql_device_status(int* status_out, int clear);
 /* Device address of the status word, which kernels are given to record a timeout in. */
 int* ql_device_status_ptr(void);
+/* Kernels launched through this library since it was loaded (all host threads). */
+long long ql_launch_count(void);
 
 /* ---- NF4 dequantisation ------------------------------------------------------------------
  * Replaces NF4Weight.dequant_into / NF4Group.dequant_into (solution/engine.py:103-109,
@@ -61,10 +63,13 @@ int ql_nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2
  * 1111-1112, 1132-1139, 1163-1165, 1178-1179, 1238-1301, 1386-1390).
  * C[M, N] (+)= A[M, K] . B[N, K]^T (+ bias[N]); A, B of in_dtype (QL_F16 / QL_BF16), row-major
  * with leading dimensions lda, ldb (elements, multiples of 8, 16-byte aligned bases), K % 8 == 0;
- * C of out_dtype with leading dimension ldc; accumulate (fp32 C only) adds to C. */
+ * C of out_dtype with leading dimension ldc; accumulate (fp32 C only) adds to C; residual
+ * (fp32 C only, [M, ldc] or NULL) writes C = residual + (the result rounded to in_dtype), the
+ * reference's fp16 projection output added to the fp32 residual stream (solution/engine.py:
+ * 1048-1051, 966 delta add). */
 int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-               cudaStream_t stream);
+               const float* residual, cudaStream_t stream);
 
 /* ---- RMSNorm with the LoRA dropout inputs --------------------------------------------------
  * Dropout fields (shared by both structs): the mask is PyTorch's CUDA dropout mask of the padded
@@ -127,6 +132,167 @@ int ql_rms_bwd(const ql_rms_bwd_args* args, cudaStream_t stream);
  * torch_dropout_keep_kernel (solution/kernels.py:129-135). */
 int ql_dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t threads,
                     float p_keep, int vec, cudaStream_t stream);
+
+/* ---- qkv + LoRA + RoPE ---------------------------------------------------------------------
+ * cos / sin: fp32 [positions, D/2] (the first half of the model's rotary table); pos: int32 [n].
+ * All void* tensors are of dtype (16-bit). */
+typedef struct {
+  const void* qkv;      /* [n, (HQ + 2 HKV) D] biased qkv GEMM output */
+  const void* lq;       /* [n, HQ D] or NULL: explicit LoRA-B output of q */
+  const void* lv;       /* [n, HKV D] or NULL */
+  const void* xq;       /* [n, rank] or NULL: lq = xq . Bq^T formed in-kernel */
+  const void* xv;
+  const void* Bq;       /* [HQ D, rank] */
+  const void* Bv;       /* [HKV D, rank] */
+  const float* cos;
+  const float* sin;
+  const int32_t* pos;
+  void* q;              /* [n, HQ, D] */
+  void* k;              /* [n, HKV, D] */
+  void* v;              /* [n, HKV, D] */
+  float lora_scale;
+  int32_t n, HQ, HKV, D, rank, dtype;
+} ql_rope_fwd_args;
+
+typedef struct {
+  const void* dq;       /* [n, HQ, D] of grad_dtype */
+  const void* dk;       /* [n, kv_heads_in, D]: HKV, or HQ (summed over each GQA group) */
+  const void* dv;
+  const float* cos;
+  const float* sin;
+  const int32_t* pos;
+  void* dqkv;           /* [n, (HQ + 2 HKV) D] of dtype: the pre-rotary gradient */
+  const void* Bq;       /* [HQ D, rank] or NULL */
+  const void* Bv;
+  float* dxlo_q;        /* [n, rank] or NULL: s * (dqkv_q . Bq), the LoRA-A output gradient */
+  float* dxlo_v;
+  float lora_scale;
+  int32_t n, HQ, HKV, D, kv_heads_in, rank, dtype, grad_dtype;
+} ql_rope_bwd_args;
+
+/* Replaces _rope_fwd + qkv_rope_fwd_kernel (solution/engine.py:984-997,
+ * solution/kernels.py:212-264) and the LoRA-B GEMMs lq = xq @ B^T (solution/engine.py:1088-1093). */
+int ql_rope_fwd(const ql_rope_fwd_args* args, cudaStream_t stream);
+/* Replaces _rope_bwd + qkv_rope_bwd_kernel (solution/engine.py:1000-1009,
+ * solution/kernels.py:267-306) and dx_lo = s * (g @ B) (solution/engine.py:1322-1326). */
+int ql_rope_bwd(const ql_rope_bwd_args* args, cudaStream_t stream);
+
+/* ---- SwiGLU ------------------------------------------------------------------------------ */
+/* Replaces _glu_fwd + glu_fwd_kernel (solution/engine.py:1012-1017, solution/kernels.py:312-321):
+ * m[n, I] = silu(gu[:, :I]) * gu[:, I:]. I % 8 == 0. */
+int ql_glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t stream);
+/* Replaces _glu_bwd + glu_bwd_kernel (solution/engine.py:1020-1023, solution/kernels.py:324-336):
+ * overwrites gu with [dL/dg | dL/du] given dm = dL/dm. */
+int ql_glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t stream);
+
+/* ---- LoRA weight gradients ---------------------------------------------------------------
+ * Replaces db_w = (g^T @ x_lo) * s and da_w = dx_lo^T @ a_in (solution/engine.py:1322-1328):
+ * out[i, r] (transpose = 0) or out[r, i] (transpose = 1) = scale * sum_t X[t, i] * Y[t, r],
+ * X [n, ldx] (x_dtype 16-bit), Y [n, rank] (y_dtype 16-bit or QL_F32), out fp32. Deterministic:
+ * per-split partials go to workspace (ql_lora_colsum_workspace floats), summed in fixed order. */
+int64_t ql_lora_colsum_workspace(int64_t n, int ncols, int rank);
+int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
+                   int ncols, int rank, float scale, int transpose, float* out, float* workspace,
+                   int64_t workspace_floats, cudaStream_t stream);
+
+/* ---- embedding ---------------------------------------------------------------------------
+ * Replaces the embedding lookup of FusedQwen2.step (solution/engine.py:1904-1907):
+ * h[t, :] = float(W[ids[t], :]). An id outside [0, vocab) records QL_STATUS_BAD_ARG in the
+ * device status word and yields a zero row. */
+int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
+             int dtype, cudaStream_t stream);
+
+/* ---- cross-entropy head ------------------------------------------------------------------ */
+typedef struct {
+  void* logits;         /* [rows, ld] 16-bit, overwritten by the gradient */
+  const int64_t* target;/* [rows], < 0: no target */
+  float* loss;          /* [rows] */
+  float* entropy;       /* [rows] */
+  int32_t* correct;     /* [rows] */
+  int64_t rows, V, ld;
+  int32_t write_grad, zero_unsupervised, dtype;
+} ql_ce_rows_args;
+
+typedef struct {
+  void* logits;         /* [rows, ld] logits of vocabulary [v0, v0 + width) */
+  const void* w;        /* [width, H] the piece of the lm_head weight */
+  const int64_t* target;
+  float* state;         /* [rows, 4] (max, sum exp, sum exp * x, best); start -inf, 0, 0, -inf */
+  int64_t* best_idx;    /* [rows] */
+  float* xt;            /* [rows] target logit */
+  float* alpha;         /* [n_sup] rescale of earlier pieces' accumulation */
+  void* wt;             /* [n_sup, H] or NULL: the target's weight row */
+  int64_t rows, v0, width, ld, n_sup;
+  int32_t H, dtype;
+} ql_ce_piece_args;
+
+typedef struct {
+  const float* state;
+  const int64_t* best_idx;
+  const float* xt;
+  const int64_t* target;
+  float* loss;
+  float* entropy;
+  int32_t* correct;
+  const float* acc;     /* [n_sup, H] sum_v exp(x_v - max) W_v */
+  const void* wt;       /* [n_sup, H] */
+  void* dh;             /* [n_sup, H] acc / s - W_target */
+  int64_t rows, n_sup;
+  int32_t H, dtype;
+} ql_ce_finish_args;
+
+/* Replaces _ce + lm_head_ce_kernel (solution/engine.py:1026-1030, solution/kernels.py:344-388). */
+int ql_ce_rows(const ql_ce_rows_args* args, cudaStream_t stream);
+/* Replaces _ce_piece + lm_head_piece_kernel (solution/engine.py:1033-1038,
+ * solution/kernels.py:401-450). */
+int ql_ce_piece(const ql_ce_piece_args* args, cudaStream_t stream);
+/* Replaces _ce_finish + lm_head_finish_kernel (solution/engine.py:1041-1045,
+ * solution/kernels.py:458-479). */
+int ql_ce_finish(const ql_ce_finish_args* args, cudaStream_t stream);
+
+/* ---- varlen causal GQA attention ----------------------------------------------------------
+ * Replaces _attn_fwd / _attn_bwd, PyTorch's memory-efficient attention over cu_seqlens
+ * (solution/engine.py:857-869). q [n, HQ, D], k / v [n, HKV, D] (not expanded: each KV head
+ * serves HQ / HKV query heads), cu_seqlens int32 [B + 1], causal, D = 128. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* cu_seqlens;
+  void* out;            /* [n, HQ, D] */
+  float* lse;           /* [HQ, n] natural-log logsumexp of the scaled scores */
+  float scale;
+  int32_t n, B, max_len, HQ, HKV, D, dtype;
+} ql_attn_fwd_args;
+
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* out;
+  const void* dout;     /* [n, HQ, D] */
+  const float* lse;
+  const int32_t* cu_seqlens;
+  float* dvec;          /* [HQ, n] workspace: rowsum(dout * out) */
+  float* dq;            /* [n, HQ, D] fp32 (zeroed by the call) */
+  float* dk;            /* [n, HKV, D] fp32, summed over each GQA group */
+  float* dv;
+  float scale;
+  int32_t n, B, max_len, HQ, HKV, D, dtype;
+} ql_attn_bwd_args;
+
+int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream);
+int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream);
+
+/* ---- head row order ----------------------------------------------------------------------
+ * The head takes rows with a target first (solution/engine.py:731, 1364-1398):
+ * gather: dst[i, :] = src[idx[i], :]; scatter: dst[idx[i], :] = src[i, :] * (*scale) (scale is a
+ * device pointer, e.g. the loss's upstream gradient, or NULL for 1), also into the 16-bit dst16
+ * when given. fp32 rows of H values (gather needs H % 4 == 0). */
+int ql_gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, int H,
+                   cudaStream_t stream);
+int ql_scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst,
+                    void* dst16, int64_t n, int H, int dtype, cudaStream_t stream);
 
 #ifdef __cplusplus
 }
