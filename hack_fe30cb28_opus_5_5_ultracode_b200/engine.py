@@ -118,6 +118,14 @@ class NF4Group:
 # ---------------------------------------------------------------------------------------------
 # LoRA dropout masks: PyTorch's own (solution/engine.py:767-828)
 # ---------------------------------------------------------------------------------------------
+def dropout_call(nelem, max_blocks, block=256, unroll=4):
+    """(threads, generator offset increment) of aten's CUDA dropout on nelem elements with at
+    most max_blocks resident blocks (solution/engine.py:787-797)."""
+    blocks = min(max_blocks, (nelem + block - 1) // block)
+    increment = ((nelem - 1) // (block * blocks * unroll) + 1) * unroll
+    return blocks * block, increment
+
+
 class TorchDropout:
     """The LoRA dropout masks PEFT's nn.Dropout draws, bit for bit: each call takes the CUDA
     generator's (seed, offset) and advances the offset as aten's dropout kernel does
@@ -143,13 +151,12 @@ class TorchDropout:
     def draw(self, nelem):
         """(seed, counter, threads) of a dropout call on nelem elements; advances the generator."""
         assert nelem % self.vec == 0, nelem
-        blocks = min(self.max_blocks, (nelem + self.BLOCK - 1) // self.BLOCK)
-        increment = ((nelem - 1) // (self.BLOCK * blocks * self.UNROLL) + 1) * self.UNROLL
+        threads, increment = dropout_call(nelem, self.max_blocks, self.BLOCK, self.UNROLL)
         seed, offset = self.gen.initial_seed(), self.gen.get_offset()
         self.gen.set_offset(offset + increment)
         if seed >= 2**63:
             seed -= 2**64
-        return seed, offset // 4, blocks * self.BLOCK
+        return seed, offset // 4, threads
 
     def check(self, B, T, H, p):
         """Whether this library's mask is PyTorch's on this GPU: the RMSNorm kernel's dropout of

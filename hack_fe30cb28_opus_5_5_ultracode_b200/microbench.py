@@ -1,0 +1,160 @@
+"""Per-kernel timing of the fused step's kernels at the Qwen2.5-1.5B shapes, with CUDA events
+on the launching stream (warm-up, then `--iters` launches, each input set larger than L2):
+
+    python -m hack_fe30cb28_opus_5_5_ultracode_b200.microbench [--tokens 1090] [--iters 20]
+        [--only gemm|dequant|attn|rms|glu|rope|ce]
+
+Prints one JSON line per kernel and shape: average launch time, algorithmic FLOPs or bytes per
+launch, achieved TFLOP/s or GB/s and the fraction of the measured peak (MEASURED_PEAKS.json).
+Also the small, self-contained case the ncu captures run on.
+"""
+
+import argparse
+import json
+import os
+
+import torch
+
+from . import ops
+from .model import QWEN25_1P5B, quantize_nf4
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return p["hbm_gbs"], p["bf16_tflops"]
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0
+
+
+def _time(fn, iters):
+    for _ in range(3):
+        fn(0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters / 1e3
+
+
+def _report(name, shape, sec, flops=None, nbytes=None):
+    hbm, tf = _peaks()
+    line = {"kernel": name, "shape": shape, "us": sec * 1e6}
+    if flops:
+        line.update(tflops=flops / sec / 1e12, frac_of_measured_bf16=flops / sec / 1e12 / tf)
+    if nbytes:
+        line.update(gbs=nbytes / sec / 1e9, frac_of_measured_hbm=nbytes / sec / 1e9 / hbm)
+    print(json.dumps(line), flush=True)
+
+
+class _W:
+    def __init__(self, p):
+        qs = p.quant_state
+        self.shape = tuple(qs.shape)
+        self.packed = p.data.reshape(-1)
+        self.absmax = qs.absmax
+        self.code = qs.code
+        self.nested, self.bs2 = False, 1
+        self.code2 = self.absmax2 = self.offsets = None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=1090)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", default=None)
+    args = ap.parse_args()
+    dev = torch.device("cuda")
+    cfg = QWEN25_1P5B
+    n, H, I, V = args.tokens, cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+    HQ, HKV, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    dt = torch.float16
+    g = torch.Generator(device=dev).manual_seed(0)
+    want = (lambda k: args.only is None or args.only == k)
+    copies = 4  # rotate inputs so consecutive launches do not hit L2
+
+    if want("gemm") or want("dequant"):
+        shapes = {"qkv": ((HQ + 2 * HKV) * D, H), "o": (H, HQ * D), "gate_up": (2 * I, H),
+                  "down": (H, I)}
+        for name, (N, K) in shapes.items():
+            ws = [_W(quantize_nf4(torch.randn(N, K, device=dev, generator=g) * 0.02))
+                  for _ in range(2)]
+            if want("dequant"):
+                outs = [torch.empty(N, K, device=dev, dtype=dt) for _ in range(2)]
+                nbytes = N * K * (0.5 + 4 / 64 + 2)
+                sec = _time(lambda i: ops.nf4_dequant(ws[i % 2], out=outs[i % 2]), args.iters)
+                _report("nf4_dequant", [N, K], sec, nbytes=nbytes)
+                sec = _time(lambda i: ops.nf4_dequant(ws[i % 2], out=outs[i % 2].view(K, N),
+                                                      transpose=True), args.iters)
+                _report("nf4_dequant_t", [K, N], sec, nbytes=nbytes)
+            if want("gemm"):
+                a = [torch.randn(n, K, device=dev, generator=g).to(dt) for _ in range(copies)]
+                b = [torch.randn(N, K, device=dev, generator=g).to(dt) * 0.02 for _ in range(2)]
+                c = [torch.empty(n, N, device=dev, dtype=dt) for _ in range(copies)]
+                sec = _time(lambda i: ops.gemm(a[i % copies], b[i % 2], out=c[i % copies]),
+                            args.iters)
+                _report("gemm_tn " + name, [n, N, K], sec, flops=2.0 * n * N * K)
+                # the data-gradient GEMM of the same projection: [n, N] x [K, N]^T
+                at = [torch.randn(n, N, device=dev, generator=g).to(dt) for _ in range(copies)]
+                bt = [torch.randn(K, N, device=dev, generator=g).to(dt) * 0.02 for _ in range(2)]
+                ct = [torch.empty(n, K, device=dev, dtype=dt) for _ in range(copies)]
+                sec = _time(lambda i: ops.gemm(at[i % copies], bt[i % 2], out=ct[i % copies]),
+                            args.iters)
+                _report("gemm_tn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
+    if want("gemm"):
+        hn = torch.randn(n, H, device=dev, generator=g).to(dt)
+        W = torch.randn(V, H, device=dev, generator=g).to(dt) * 0.02
+        logits = torch.empty(n, V, device=dev, dtype=dt)
+        sec = _time(lambda i: ops.gemm(hn, W, out=logits), args.iters)
+        _report("gemm_tn lm_head", [n, V, H], sec, flops=2.0 * n * V * H)
+        WT = W.t().contiguous()
+        sec = _time(lambda i: ops.gemm(logits, WT), args.iters)
+        _report("gemm_tn lm_head dgrad", [n, H, V], sec, flops=2.0 * n * V * H)
+    if want("attn"):
+        lengths = [300, 257, 400, 133]
+        m = sum(lengths)
+        cu = torch.tensor([0] + torch.tensor(lengths).cumsum(0).tolist(), device=dev,
+                          dtype=torch.int32)
+        q = torch.randn(m, HQ, D, device=dev, generator=g).to(dt)
+        k = torch.randn(m, HKV, D, device=dev, generator=g).to(dt)
+        v = torch.randn(m, HKV, D, device=dev, generator=g).to(dt)
+        flops = sum(4.0 * L * (L + 1) / 2 * HQ * D for L in lengths)
+        out, lse = ops.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5)
+        sec = _time(lambda i: ops.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5, out=out, lse=lse),
+                    args.iters)
+        _report("attn_fwd", lengths, sec, flops=flops)
+        dout = torch.randn_like(q)
+        sec = _time(lambda i: ops.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths), D ** -0.5),
+                    args.iters)
+        _report("attn_bwd", lengths, sec, flops=2.5 * flops)
+    if want("glu"):
+        gu = [torch.randn(n, 2 * I, device=dev, generator=g).to(dt) for _ in range(copies)]
+        m_ = [torch.empty(n, I, device=dev, dtype=dt) for _ in range(copies)]
+        sec = _time(lambda i: ops.glu_fwd(gu[i % copies], I, out=m_[i % copies]), args.iters)
+        _report("glu_fwd", [n, I], sec, nbytes=n * I * 6)
+        sec = _time(lambda i: ops.glu_bwd(m_[i % copies], gu[i % copies], I), args.iters)
+        _report("glu_bwd", [n, I], sec, nbytes=n * I * 10)
+    if want("rms"):
+        xs = [torch.randn(n, H, device=dev, generator=g) for _ in range(copies)]
+        w = torch.ones(H, device=dev)
+        A = torch.randn(16, H, device=dev, generator=g).to(dt) * 0.02
+        tok = torch.arange(n, device=dev)
+        drop = ops.Drop(tok, 1, 0, 10, 1184 * 256, 0.05)
+        sec = _time(lambda i: ops.rms_fwd(xs[i % copies], w, 1e-6, drop=drop, Aq=A, Av=A,
+                                          want_yq=True), args.iters)
+        _report("rms_fwd (+dropout, LoRA-A)", [n, H], sec, nbytes=n * H * (4 + 3 * 2))
+    if want("ce"):
+        logits = [torch.randn(n, V, device=dev, generator=g).to(dt) for _ in range(2)]
+        tgt = torch.randint(0, V, (n,), device=dev, generator=g)
+        sec = _time(lambda i: ops.ce_rows(logits[i % 2], tgt), args.iters)
+        _report("ce_rows", [n, V], sec, nbytes=n * V * 2 * 3)
+
+
+if __name__ == "__main__":
+    main()

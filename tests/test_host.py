@@ -1,0 +1,214 @@
+"""CPU: host-side logic of the fused step — batch packing, the dropout-call arithmetic, the
+model stand-in, and the drop-in boundary's bookkeeping and fallbacks (solution/test_fallback.py
+is the reference's model for the latter: a SimpleNamespace trainer, the original compute_loss
+called for anything the fused step does not take)."""
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from hack_fe30cb28_opus_5_5_ultracode_b200 import patch
+from hack_fe30cb28_opus_5_5_ultracode_b200.engine import (HeadStats, Packed, RopeTable,
+                                                          UnsupportedBatch, dropout_call)
+from hack_fe30cb28_opus_5_5_ultracode_b200.model import TINY, build_qwen2_qlora
+from oracle.philox import draw
+
+
+def _batch(lengths, left=False, vocab=3000, prompt=2):
+    torch.manual_seed(3)
+    B, T = len(lengths), max(lengths)
+    ids = torch.randint(0, vocab, (B, T))
+    ar = torch.arange(T)[None]
+    L = torch.tensor(lengths)[:, None]
+    mask = ((ar >= T - L) if left else (ar < L)).long()
+    labels = torch.where(mask.bool(), ids, -100)
+    labels[:, :prompt] = -100
+    return {"input_ids": ids, "attention_mask": mask, "labels": labels}
+
+
+def test_packed_unpads_and_shifts():
+    b = _batch([5, 3, 7])
+    p = Packed(b["input_ids"], b["attention_mask"], b["labels"])
+    assert p.n == 15 and p.rows == 3 and p.T == 7 and p.max_len == 7
+    assert p.cu_seqlens.tolist() == [0, 5, 8, 15]
+    assert p.tok.tolist() == [0, 1, 2, 3, 4, 7, 8, 9, 14, 15, 16, 17, 18, 19, 20]
+    assert p.pos.tolist() == [0, 1, 2, 3, 4, 0, 1, 2, 0, 1, 2, 3, 4, 5, 6]
+    assert torch.equal(p.ids, b["input_ids"].reshape(-1)[p.tok])
+    # targets: the next token's label (HF labels are unshifted), -100 at each row's end
+    lab = b["labels"]
+    exp = []
+    for r, ln in enumerate([5, 3, 7]):
+        exp += [int(lab[r, t + 1]) for t in range(ln - 1)] + [-100]
+    assert p.targets.tolist() == exp
+    sup = [t >= 0 for t in exp]
+    assert p.n_supervised == sum(sup)
+    order = p.head_order.tolist()
+    assert all(sup[i] for i in order[:p.n_supervised]) and not any(sup[i] for i in order[p.n_supervised:])
+    assert order[:p.n_supervised] == sorted(order[:p.n_supervised])  # stable
+    assert p.row_of_token.tolist() == [0] * 5 + [1] * 3 + [2] * 7
+
+
+def test_packed_rejects_left_padding_and_bad_shapes():
+    b = _batch([5, 3], left=True)
+    with pytest.raises(UnsupportedBatch):
+        Packed(b["input_ids"], b["attention_mask"], b["labels"])
+    with pytest.raises(UnsupportedBatch):
+        Packed(b["input_ids"][0], b["attention_mask"][0], b["labels"][0])
+
+
+@pytest.mark.parametrize("nelem,max_blocks", [(4 * 512 * 1536, 1184), (960, 1184), (8, 1184),
+                                              (4 * 37 * 1536, 160), (10**9, 1184)])
+def test_dropout_call_matches_oracle(nelem, max_blocks):
+    threads, inc = dropout_call(nelem, max_blocks)
+    _, ctr, thr, off = draw(nelem, 40, 5, max_blocks)
+    assert (threads, 40 + inc, ctr) == (thr, off, 10)
+
+
+def test_rope_table_is_rotate_half():
+    model = build_qwen2_qlora(TINY, device="cpu", seed=0)
+    table = RopeTable(model.get_base_model().model.rotary_emb, TINY.head_dim, "cpu")
+    cos, sin = table.table(300)
+    assert cos.shape == (1024, TINY.head_dim // 2)
+    inv = 1.0 / (TINY.rope_theta ** (torch.arange(0, TINY.head_dim, 2).float() / TINY.head_dim))
+    torch.testing.assert_close(cos[7], torch.cos(7 * inv))
+    assert table.table(2000)[0].shape[0] == 2048
+
+
+def test_model_stand_in_has_the_peft_bnb_layout():
+    model = build_qwen2_qlora(TINY, device="cpu", seed=0, nested=True)
+    causal = model.get_base_model()
+    layer = causal.model.layers[0]
+    q = layer.self_attn.q_proj
+    assert q.base_layer.weight.quant_state.quant_type == "nf4"
+    assert q.base_layer.weight.data.dtype == torch.uint8
+    assert q.base_layer.weight.data.numel() * 2 == TINY.num_attention_heads * TINY.head_dim * TINY.hidden_size
+    assert q.lora_A["default"].weight.requires_grad and q.scaling["default"] == 2.0
+    assert not hasattr(layer.self_attn.k_proj, "lora_A")
+    assert causal.lm_head.weight is causal.model.embed_tokens.weight
+    params = [p for p in model.parameters() if p.requires_grad]
+    assert len(params) == 4 * TINY.num_hidden_layers
+    assert patch.is_supported(model) is False  # no GPU here: the fused step is never offered
+
+
+# ---------------------------------------------------------------------------------------------
+# the boundary (solution/patch.py:268-389), with a stand-in engine
+# ---------------------------------------------------------------------------------------------
+class _FakeEngine:
+    """Runs Packed on the batch and returns a loss with the fused step's statistics."""
+
+    def __init__(self, fail=False):
+        self.calls, self.fail = [], fail
+
+    def step(self, input_ids, attention_mask, labels, denom):
+        self.calls.append(denom)
+        packed = Packed(input_ids, attention_mask, labels)  # raises UnsupportedBatch itself
+        if self.fail:
+            raise UnsupportedBatch("dropout masks differ")
+        n = packed.n
+        stats = HeadStats()
+        stats.order = packed.head_order
+        stats.tok_loss = torch.where(packed.targets[stats.order] >= 0, torch.ones(n) * 2.0,
+                                     torch.zeros(n))
+        stats.entropy = torch.full((n,), 3.0)
+        stats.correct = (torch.arange(n) % 2 == 0).int() * (packed.targets[stats.order] >= 0).int()
+        loss = stats.tok_loss.sum() / denom
+        return loss, packed, stats
+
+
+class _Rewind:
+    def __init__(self):
+        self.rows, self.failed = [], False
+
+    def on_micro_batch(self, step, row_loss, row_tokens):
+        self.rows.append((step, row_loss, row_tokens))
+
+    def fail(self, exc):
+        self.failed = True
+
+
+def _trainer(engine, **kw):
+    calls = []
+
+    def original(model, inputs, return_outputs=False, num_items_in_batch=None):
+        calls.append(sorted(inputs))
+        return torch.tensor(123.0)
+
+    t = types.SimpleNamespace(compute_loss_func=None, label_smoother=None,
+                              model_accepts_loss_kwargs=True,
+                              args=types.SimpleNamespace(average_tokens_across_devices=False,
+                                                         n_gpu=1),
+                              state=types.SimpleNamespace(global_step=4),
+                              _metrics={"train": {"entropy": [], "mean_token_accuracy": [],
+                                                  "num_tokens": []}},
+                              _total_train_tokens=0, _soup_rewind_state=_Rewind())
+    t._soup_original_compute_loss = original
+    t._soup_kernels_engine = engine
+    for k, v in kw.items():
+        setattr(t, k, v)
+    return t, calls
+
+
+class _Model(torch.nn.Module):
+    pass
+
+
+def test_fused_compute_loss_bookkeeping():
+    engine = _FakeEngine()
+    t, calls = _trainer(engine)
+    model = _Model().train()
+    b = _batch([5, 3, 7])
+    n_items = int((b["labels"][:, 1:] != -100).sum())
+    loss = patch.fused_compute_loss(t, model, dict(b), num_items_in_batch=torch.tensor(n_items))
+    assert not calls and engine.calls == [float(n_items)]
+    assert loss.item() == pytest.approx(2.0)  # every supervised token costs 2
+    assert t._total_train_tokens == 15 and t._metrics["train"]["num_tokens"] == [15]
+    patch._flush_metrics(t)
+    assert t._metrics["train"]["entropy"] == [pytest.approx(3.0)]
+    sup = n_items
+    assert t._metrics["train"]["mean_token_accuracy"][0] == pytest.approx(
+        sum(1 for i in range(15) if i % 2 == 0 and i < sup) / sup)
+    (step, row_loss, row_tokens), = t._soup_rewind_state.rows
+    assert step == 5 and row_tokens == [3, 1, 5] and row_loss == [2.0, 2.0, 2.0]
+    # without loss kwargs the denominator is the supervised count
+    t2, _ = _trainer(_FakeEngine(), model_accepts_loss_kwargs=False)
+    patch.fused_compute_loss(t2, model, dict(b), num_items_in_batch=99)
+    assert t2._soup_kernels_engine.calls == [float(n_items)]
+
+
+def test_fused_compute_loss_scales_under_average_tokens_across_devices():
+    t, _ = _trainer(_FakeEngine())
+    t.args.average_tokens_across_devices = True
+    t.accelerator = types.SimpleNamespace(num_processes=4, parallelism_config=None)
+    model = _Model().train()
+    b = _batch([5, 3, 7])
+    n_items = int((b["labels"][:, 1:] != -100).sum())
+    loss = patch.fused_compute_loss(t, model, dict(b), num_items_in_batch=n_items)
+    assert loss.item() == pytest.approx(8.0)
+
+
+@pytest.mark.parametrize("case", ["eval", "extra_key", "label_smoother", "left_padding",
+                                  "unsupported_batch"])
+def test_fused_compute_loss_falls_back(case):
+    engine = _FakeEngine(fail=case == "unsupported_batch")
+    t, calls = _trainer(engine)
+    model = _Model().train()
+    b = _batch([5, 3], left=case == "left_padding")
+    b["_prediction_loss_only"] = False
+    if case == "eval":
+        model.eval()
+    if case == "extra_key":
+        b["position_ids"] = torch.zeros_like(b["input_ids"])
+    if case == "label_smoother":
+        t.label_smoother = object()
+    loss = patch.fused_compute_loss(t, model, b, num_items_in_batch=3)
+    assert loss.item() == 123.0 and len(calls) == 1
+    assert "_prediction_loss_only" in calls[0]  # the inputs reach the original unchanged
+    assert t._total_train_tokens == 0
+
+
+def test_install_refuses_unsupported_models():
+    t = types.SimpleNamespace(model=_Model(), compute_loss=lambda *a, **k: None)
+    assert patch.install(t) is False
+    assert not hasattr(t, patch._INSTALLED_ATTR) or getattr(t, patch._INSTALLED_ATTR) is None
