@@ -248,22 +248,24 @@ def run_ours(args, rank, world, local):
     clocks.start()
     time.sleep(0.3)
     launches0 = ops.launch_count()
-    ops.record_gemms(True)
+    ops.profile_start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.warmup, args.warmup + args.steps):
         train_step(i)
     e1.record()
     barrier_sync()
-    gemms = ops.record_gemms(False)
+    ops.profile_stop()
+    prof = ops.profile_read()
     launches = ops.launch_count() - launches0
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
     tokens = sum_over_ranks(sum(b[3] for b in host[args.warmup:]))
     value = tokens / (ms / 1000.0)
     peak_mib = torch.cuda.max_memory_allocated(dev) / 2**20
-    gemm_ms = sum(s.elapsed_time(e) for s, e, _ in gemms)
-    gemm_flops = sum(f for _, _, f in gemms)
+    gemm_ms = prof.get("gemm", {}).get("ms", 0.0)
+    gemm_flops = prof.get("gemm", {}).get("flops", 0.0)
+    kernel_ms = {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()}
 
     # e2e: the drop-in boundary from pinned host batches
     import types
@@ -331,7 +333,9 @@ def run_ours(args, rank, world, local):
                      "unit": "TFLOP/s", "frac": (achieved / tf_sust) if achieved else None,
                      "peak_source": f"{src} bf16 dense, sustained (kernel inside a long step)",
                      "traffic": traffic, "gemm_share_of_step": gemm_ms / ms if ms else None,
-                     "launches": len(gemms)},
+                     "launches": int(prof.get("gemm", {}).get("count", 0))},
+        "op_ms_per_step": kernel_ms,
+        "op_busy_share": sum(v["ms"] for v in prof.values()) / ms if ms else None,
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:

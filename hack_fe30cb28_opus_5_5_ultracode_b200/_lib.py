@@ -23,8 +23,10 @@ def _strip_comments(text):
     return re.sub(r"//[^\n]*", " ", text)
 
 
-def _ctype(decl_type):
+def _ctype(decl_type, structs=None):
     t = decl_type.replace("const", " ").strip()
+    if structs and "*" not in t and t in structs:
+        return structs[t]
     if "*" in t:
         if re.sub(r"\s+", "", t) == "char*":
             return ctypes.c_char_p
@@ -54,7 +56,7 @@ def parse_header(path=HEADER):
                 nm = nm.strip()
                 stars = nm.count("*")
                 nm = nm.replace("*", "").strip()
-                fields.append((nm, _ctype(base + "*" * stars)))
+                fields.append((nm, _ctype(base + "*" * stars, structs)))
         structs[name] = type(name, (ctypes.Structure,), {"_fields_": fields})
     functions = {}
     for ret, name, args in re.findall(r"\b((?:const\s+)?(?:long\s+long|[A-Za-z_]\w*)\s*\**)\s*(ql_\w+)\s*\(([^)]*)\)\s*;",

@@ -11,6 +11,7 @@
 // accumulation); the tiles are 64 queries x 64 keys, head dim D = 128 (Qwen2.5) or 64, staged by
 // cp.async into XOR-swizzled shared memory read with ldmatrix.
 #include "common.cuh"
+#include "profile.h"
 #include "ops.h"
 
 namespace ql {
@@ -248,6 +249,7 @@ int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
   if (a.D != 128 && a.D != 64) return QL_STATUS_UNSUPPORTED;
   if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
   if (a.n == 0 || a.B == 0 || a.max_len == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_ATTN_FWD, 0, 0, s);
   if (a.dtype == QL_F16) {
     if (a.D == 128) launch_attn_fwd<__half, 128>(a, s); else launch_attn_fwd<__half, 64>(a, s);
   } else if (a.dtype == QL_BF16) {
@@ -255,7 +257,7 @@ int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
   } else {
     return QL_STATUS_BAD_ARG;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 }  // namespace ql
@@ -515,6 +517,7 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
   if (a.n == 0 || a.B == 0) return QL_STATUS_OK;
   if (a.dvec == nullptr) return QL_STATUS_BAD_ARG;
+  ProfScope prof(PK_ATTN_BWD, 0, 0, s);
   // gradients accumulate atomically: start from zero
   if (cudaMemsetAsync(a.dq, 0, sizeof(float) * a.n * a.HQ * a.D, s) != cudaSuccess ||
       cudaMemsetAsync(a.dk, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess ||
@@ -528,7 +531,7 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   } else {
     return QL_STATUS_BAD_ARG;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(2);
 }
 
 }  // namespace ql

@@ -11,7 +11,7 @@
 namespace {
 __device__ int g_status_word = 0;  // QL_STATUS_TIMEOUT etc., recorded by kernels
 thread_local std::string g_last_error;
-std::atomic<long long> g_launches{0};  // kernels launched through this ABI (all host threads)
+std::atomic<long long> g_launches{0};  // kernels launched by this library (all host threads)
 
 int fail(int code, const char* where) {
   const cudaError_t e = cudaGetLastError();
@@ -26,16 +26,19 @@ int fail(int code, const char* where) {
   return code;
 }
 
-int done(int code, const char* where, int launches = 1) {
-  if (code == QL_STATUS_OK) {
-    g_launches.fetch_add(launches, std::memory_order_relaxed);
-    return QL_STATUS_OK;
-  }
+int done(int code, const char* where) {
+  if (code == QL_STATUS_OK) return QL_STATUS_OK;
   return fail(code, where);
 }
 }  // namespace
 
 namespace ql {
+int launched(int kernels) {
+  if (cudaPeekAtLastError() != cudaSuccess) return QL_STATUS_CUDA;
+  g_launches.fetch_add(kernels, std::memory_order_relaxed);
+  return QL_STATUS_OK;
+}
+
 int* status_word() {
   // one address per device; cudaGetSymbolAddress is cheap after the first call per device
   static int* cache[64] = {nullptr};
@@ -130,7 +133,7 @@ int ql_glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream
 }
 
 int64_t ql_lora_colsum_workspace(int64_t n, int ncols, int rank) {
-  return (int64_t)ql::lora_colsum_splits(n) * ncols * rank;
+  return (int64_t)ql::lora_colsum_splits(n, ncols) * ncols * rank;
 }
 
 int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
@@ -138,7 +141,7 @@ int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y
                    int64_t workspace_floats, cudaStream_t stream) {
   return done(ql::lora_colsum(X, ldx, x_dtype, Y, y_dtype, n, ncols, rank, scale, transpose, out,
                               workspace, workspace_floats, stream),
-              "ql_lora_colsum", 2);
+              "ql_lora_colsum");
 }
 
 int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
@@ -172,7 +175,7 @@ int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream) {
 
 int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream) {
   if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_attn_bwd");
-  return done(ql::attn_bwd(*args, stream), "ql_attn_bwd", 2);
+  return done(ql::attn_bwd(*args, stream), "ql_attn_bwd");
 }
 
 }  // extern "C"
@@ -188,6 +191,41 @@ int ql_scatter_rows(const float* src, const int64_t* idx, const float* scale, fl
                     void* dst16, int64_t n, int H, int dtype, cudaStream_t stream) {
   return done(ql::scatter_rows(src, idx, scale, dst, dst16, n, H, dtype, stream),
               "ql_scatter_rows");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int64_t ql_layer_workspace_bytes(const ql_layer_desc* layer, int backward) {
+  return layer == nullptr ? -1 : ql::layer_workspace_bytes(*layer, backward);
+}
+
+int ql_layer_forward(const ql_layer_desc* layer, const ql_layer_saved* saved, float* h_out,
+                     void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  if (layer == nullptr || saved == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_layer_forward");
+  return done(ql::layer_forward(*layer, *saved, h_out, workspace, workspace_bytes,
+                                ql::status_word(), stream),
+              "ql_layer_forward");
+}
+
+int ql_layer_backward(const ql_layer_desc* layer, const ql_layer_saved* saved, const float* dh3,
+                      const void* dh3_16, float* grads, float* dh_out, void* dh16_out,
+                      void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  if (layer == nullptr || saved == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_layer_backward");
+  return done(ql::layer_backward(*layer, *saved, dh3, dh3_16, grads, dh_out, dh16_out, workspace,
+                                 workspace_bytes, ql::status_word(), stream),
+              "ql_layer_backward");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int ql_profile_start(int capacity) { return done(ql::profile_start(capacity), "ql_profile_start"); }
+int ql_profile_stop(void) { return done(ql::profile_stop(), "ql_profile_stop"); }
+int ql_profile_read(double* count, double* ms, double* flops, double* bytes) {
+  return done(ql::profile_read(count, ms, flops, bytes), "ql_profile_read");
 }
 
 }  // extern "C"

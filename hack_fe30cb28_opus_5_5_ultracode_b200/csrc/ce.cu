@@ -15,6 +15,7 @@
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "profile.h"
 #include "ops.h"
 
 namespace ql {
@@ -184,10 +185,11 @@ __global__ void ce_finish_kernel(CeFinishC a) {
 int ce_rows(const CeRowsC& a, cudaStream_t s) {
   if (a.rows < 0 || a.V <= 0 || a.ld < a.V) return QL_STATUS_BAD_ARG;
   if (a.rows == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_CE, 0, (double)a.rows * a.V * 2 * (a.write_grad ? 3 : 1), s);
   if (a.dtype == QL_F16) ce_rows_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
   else if (a.dtype == QL_BF16) ce_rows_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 int ce_piece(const CePieceC& a, cudaStream_t s) {
@@ -196,7 +198,7 @@ int ce_piece(const CePieceC& a, cudaStream_t s) {
   if (a.dtype == QL_F16) ce_piece_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
   else if (a.dtype == QL_BF16) ce_piece_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 int ce_finish(const CeFinishC& a, cudaStream_t s) {
@@ -205,7 +207,7 @@ int ce_finish(const CeFinishC& a, cudaStream_t s) {
   if (a.dtype == QL_F16) ce_finish_kernel<__half><<<a.rows, 256, 0, s>>>(a);
   else if (a.dtype == QL_BF16) ce_finish_kernel<__nv_bfloat16><<<a.rows, 256, 0, s>>>(a);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 }  // namespace ql

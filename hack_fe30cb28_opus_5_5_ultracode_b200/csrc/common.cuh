@@ -20,6 +20,9 @@ constexpr unsigned long long QL_WAIT_NS = 2000000000ull;  // 2 s per wait
 
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Host: the status of the launch(es) just issued; counts them in the library's launch counter.
+int launched(int kernels);
+
 // ---------------------------------------------------------------------------------------------
 // element conversion
 // ---------------------------------------------------------------------------------------------

@@ -16,6 +16,7 @@
 //   warps 2-5   epilogue: tcgen05.ld of their 32 TMEM lanes, bias add, conversion, stores.
 // The accumulator of tile t+1 is written while the epilogue drains tile t.
 #include "common.cuh"
+#include "profile.h"
 
 namespace ql {
 
@@ -61,7 +62,9 @@ __device__ __forceinline__ void store_row32(OutT* dst, const float* v, int ncols
       for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
   } else {
-    for (int i = 0; i < 32 && i < ncols; ++i) dst[i] = from_f<OutT>(v[i]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = from_f<OutT>(v[i]);
   }
 }
 
@@ -173,15 +176,21 @@ __global__ void __launch_bounds__(192, 1)
         if (row < p.M && col0 < p.N) {
           const int ncols = min(32, p.N - col0);
           if (bias != nullptr) {
-            for (int i = 0; i < 32 && i < ncols; ++i) v[i] += to_f<InT>(bias[col0 + i]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncols) v[i] += to_f<InT>(bias[col0 + i]);
           }
           OutT* dst = C + (int64_t)row * p.ldc + col0;
           if constexpr (sizeof(OutT) == 4) {
             if (p.residual != nullptr) {
               const float* res = p.residual + (int64_t)row * p.ldc + col0;
-              for (int i = 0; i < 32 && i < ncols; ++i) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < ncols) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
             } else if (p.accumulate) {
-              for (int i = 0; i < 32 && i < ncols; ++i) v[i] += to_f<OutT>(dst[i]);
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < ncols) v[i] += to_f<OutT>(dst[i]);
             }
           }
           store_row32<OutT>(dst, v, ncols);
@@ -262,7 +271,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   const int tiles = (int)(cdiv(a.M, 128) * cdiv(a.N, BN));
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, a);
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 template <int BN, bool IS_BF16>
@@ -289,6 +298,9 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   if ((lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 || K % 8 != 0) return QL_STATUS_BAD_ARG;
   if (K == 0) return QL_STATUS_UNSUPPORTED;
   const bool bf16 = in_dtype == QL_BF16;
+  ProfScope prof(PK_GEMM, 2.0 * M * N * K,
+                 2.0 * ((double)M * K + (double)N * K) + (double)M * N * (out_dtype == QL_F32 ? 4 : 2),
+                 stream);
   // Wide N tiles when there are enough of them to fill the machine, else 128.
   const int64_t tiles256 = cdiv(M, 128) * cdiv(N, 256);
   const int BN = (tiles256 >= num_sms()) ? 256 : 128;

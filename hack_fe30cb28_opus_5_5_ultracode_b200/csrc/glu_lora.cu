@@ -12,6 +12,7 @@
 // deterministic two-stage column reduction over the tokens (per-split partials in a caller
 // workspace, then a fixed-order sum).
 #include "common.cuh"
+#include "profile.h"
 #include "ops.h"
 
 namespace ql {
@@ -64,6 +65,7 @@ __global__ void glu_bwd_kernel(const T* __restrict__ dm, T* __restrict__ gu, int
 int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s) {
   if (n < 0 || I <= 0 || I % 8 != 0) return QL_STATUS_BAD_ARG;
   if (n == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_GLU_FWD, 0, (double)n * I * 6, s);
   const int64_t work = n * (I / 8);
   const unsigned grid = (unsigned)cdiv(work, 256);
   if (dtype == QL_F16)
@@ -71,12 +73,13 @@ int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s
   else if (dtype == QL_BF16)
     glu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)gu, (__nv_bfloat16*)m, n, I);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t s) {
   if (n < 0 || I <= 0 || I % 8 != 0) return QL_STATUS_BAD_ARG;
   if (n == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_GLU_BWD, 0, (double)n * I * 10, s);
   const int64_t work = n * (I / 8);
   const unsigned grid = (unsigned)cdiv(work, 256);
   if (dtype == QL_F16)
@@ -84,47 +87,75 @@ int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t 
   else if (dtype == QL_BF16)
     glu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dm, (__nv_bfloat16*)gu, n, I);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 // ---------------------------------------------------------------------------------------------
 // LoRA weight gradients
 // ---------------------------------------------------------------------------------------------
-constexpr int CS_COLS = 128, CS_TOK = 64, CS_R = 16;
+constexpr int CS_COLS = 64, CS_TOK = 32, CS_R = 16, CS_THREADS = 256;
 
-// Stage 1: split `sp` of the tokens, columns [blockIdx.x * 128, +128): partial[sp][i][r].
+__device__ __forceinline__ void cs_cp16(void* smem, const void* gmem, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+
+// Stage 1: split blockIdx.y of the tokens, columns [blockIdx.x * 64, +64): partial[sp][i][r].
+// Tiles of 32 tokens x 64 columns of X and 32 x 16 of Y are staged by cp.async (double buffered,
+// every load of a tile in flight at once); thread t accumulates column t % 64 for 4 of the 16 r.
 template <typename TX, typename TY>
-__global__ void __launch_bounds__(CS_COLS) colsum_kernel(const TX* __restrict__ X, int64_t ldx,
-                                                          const TY* __restrict__ Y, int64_t n,
-                                                          int ncols, int64_t tok_per_split,
-                                                          float* __restrict__ partial) {
-  __shared__ float ys[CS_TOK][CS_R];
-  const int i = blockIdx.x * CS_COLS + threadIdx.x;
+__global__ void __launch_bounds__(CS_THREADS) colsum_kernel(const TX* __restrict__ X, int64_t ldx,
+                                                             const TY* __restrict__ Y, int64_t n,
+                                                             int ncols, int64_t tok_per_split,
+                                                             float* __restrict__ partial) {
+  __shared__ __align__(16) TX xs[2][CS_TOK][CS_COLS];
+  __shared__ __align__(16) TY ys[2][CS_TOK][CS_R];
+  const int c0 = blockIdx.x * CS_COLS;
   const int64_t t0 = blockIdx.y * tok_per_split;
   const int64_t t1 = min(n, t0 + tok_per_split);
-  float acc[CS_R];
-#pragma unroll
-  for (int r = 0; r < CS_R; ++r) acc[r] = 0.f;
+  const int c = threadIdx.x % CS_COLS, rg = threadIdx.x / CS_COLS;  // rg: r = 4 rg .. 4 rg + 3
+  constexpr int XCH = CS_TOK * CS_COLS * sizeof(TX) / 16;  // 16-byte chunks of an X tile
+  constexpr int YCH = CS_TOK * CS_R * sizeof(TY) / 16;
+  constexpr int XPR = CS_COLS * sizeof(TX) / 16;           // chunks per X row
+  constexpr int YPR = CS_R * sizeof(TY) / 16;
+  auto load = [&](int buf, int64_t tb) {
+    for (int i = threadIdx.x; i < XCH; i += CS_THREADS) {
+      const int tt = i / XPR, ch = i % XPR;
+      const int col = c0 + ch * (16 / (int)sizeof(TX));
+      const bool ok = tb + tt < t1 && col < ncols;
+      cs_cp16(&xs[buf][tt][ch * (16 / sizeof(TX))], ok ? X + (tb + tt) * ldx + col : X, ok);
+    }
+    for (int i = threadIdx.x; i < YCH; i += CS_THREADS) {
+      const int tt = i / YPR, ch = i % YPR;
+      const bool ok = tb + tt < t1;
+      cs_cp16(&ys[buf][tt][ch * (16 / sizeof(TY))], ok ? Y + (tb + tt) * CS_R + ch * (16 / sizeof(TY)) : Y, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int buf = 0;
+  if (t0 < t1) load(0, t0);
   for (int64_t tb = t0; tb < t1; tb += CS_TOK) {
-    const int cnt = (int)min((int64_t)CS_TOK, t1 - tb);
-    __syncthreads();
-    for (int j = threadIdx.x; j < CS_TOK * CS_R; j += CS_COLS) {
-      const int tt = j / CS_R, r = j % CS_R;
-      ys[tt][r] = tt < cnt ? to_f<TY>(Y[(tb + tt) * CS_R + r]) : 0.f;
+    if (tb + CS_TOK < t1) {
+      load(buf ^ 1, tb + CS_TOK);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    if (i < ncols) {
-      for (int tt = 0; tt < cnt; ++tt) {
-        const float x = to_f<TX>(X[(tb + tt) * ldx + i]);
+#pragma unroll 8
+    for (int tt = 0; tt < CS_TOK; ++tt) {
+      const float x = to_f<TX>(xs[buf][tt][c]);
 #pragma unroll
-        for (int r = 0; r < CS_R; ++r) acc[r] += x * ys[tt][r];
-      }
+      for (int j = 0; j < 4; ++j) acc[j] += x * to_f<TY>(ys[buf][tt][4 * rg + j]);
     }
+    __syncthreads();  // the buffer is refilled next iteration
+    buf ^= 1;
   }
-  if (i < ncols) {
-    float* p = partial + ((int64_t)blockIdx.y * ncols + i) * CS_R;
-#pragma unroll
-    for (int r = 0; r < CS_R; ++r) p[r] = acc[r];
+  if (c0 + c < ncols) {
+    float* p = partial + ((int64_t)blockIdx.y * ncols + c0 + c) * CS_R + 4 * rg;
+    *reinterpret_cast<float4*>(p) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
 }
 
@@ -140,9 +171,14 @@ __global__ void colsum_reduce_kernel(const float* __restrict__ partial, int spli
   else out[idx] = s * scale;
 }
 
-int lora_colsum_splits(int64_t n) {
-  const int64_t s = cdiv(n, 128);
-  return (int)(s < 1 ? 1 : (s > 64 ? 64 : s));
+int lora_colsum_splits(int64_t n, int ncols) {
+  // about 4 CTAs per SM of 148, at least 32 tokens per split, at most 64 splits
+  const int64_t colblocks = cdiv(ncols, CS_COLS);
+  int64_t s = cdiv(592, colblocks);
+  const int64_t by_tokens = cdiv(n, CS_TOK);
+  if (s > by_tokens) s = by_tokens;
+  if (s > 64) s = 64;
+  return (int)(s < 1 ? 1 : s);
 }
 
 int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
@@ -150,12 +186,17 @@ int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dt
                 int64_t workspace_floats, cudaStream_t s) {
   if (rank != CS_R) return QL_STATUS_UNSUPPORTED;
   if (n < 0 || ncols <= 0) return QL_STATUS_BAD_ARG;
-  const int splits = lora_colsum_splits(n);
+  // 16-byte staging: aligned bases and row strides, whole 8-column groups
+  if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(Y) % 16 != 0 ||
+      ldx % 8 != 0 || ncols % 8 != 0)
+    return QL_STATUS_BAD_ARG;
+  const int splits = lora_colsum_splits(n, ncols);
   if (workspace_floats < (int64_t)splits * ncols * CS_R) return QL_STATUS_BAD_ARG;
-  const int64_t per = cdiv(n > 0 ? n : 1, splits);
+  ProfScope prof(PK_COLSUM, 2.0 * n * ncols * CS_R, (double)n * ncols * 2, s);
+  const int64_t per = cdiv(cdiv(n > 0 ? n : 1, splits), CS_TOK) * CS_TOK;
   dim3 grid((unsigned)cdiv(ncols, CS_COLS), (unsigned)splits);
 #define QL_COLSUM(TX, TY) \
-  colsum_kernel<TX, TY><<<grid, CS_COLS, 0, s>>>((const TX*)X, ldx, (const TY*)Y, n, ncols, per, workspace)
+  colsum_kernel<TX, TY><<<grid, CS_THREADS, 0, s>>>((const TX*)X, ldx, (const TY*)Y, n, ncols, per, workspace)
   if (x_dtype == QL_F16 && y_dtype == QL_F16) QL_COLSUM(__half, __half);
   else if (x_dtype == QL_F16 && y_dtype == QL_F32) QL_COLSUM(__half, float);
   else if (x_dtype == QL_BF16 && y_dtype == QL_BF16) QL_COLSUM(__nv_bfloat16, __nv_bfloat16);
@@ -165,7 +206,7 @@ int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dt
   const int64_t total = (int64_t)ncols * CS_R;
   colsum_reduce_kernel<<<(unsigned)cdiv(total, 256), 256, 0, s>>>(workspace, splits, ncols, scale,
                                                                   transpose, out);
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(2);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -192,7 +233,7 @@ int embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t
   else if (dtype == QL_BF16)
     embed_kernel<__nv_bfloat16><<<n, 256, 0, s>>>(ids, (const __nv_bfloat16*)W, h, n, H, vocab, err);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 }  // namespace ql
@@ -228,7 +269,7 @@ int gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, int
   if (n < 0 || H <= 0 || H % 4 != 0) return QL_STATUS_BAD_ARG;
   if (n == 0) return QL_STATUS_OK;
   gather_rows_kernel<<<n, 128, 0, s>>>(src, idx, dst, H);
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 int scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst, void* dst16,
@@ -239,7 +280,7 @@ int scatter_rows(const float* src, const int64_t* idx, const float* scale, float
   else if (dtype == QL_BF16)
     scatter_rows_kernel<__nv_bfloat16><<<n, 128, 0, s>>>(src, idx, scale, dst, (__nv_bfloat16*)dst16, H);
   else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 }  // namespace ql

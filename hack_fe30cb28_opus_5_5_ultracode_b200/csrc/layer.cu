@@ -1,0 +1,252 @@
+// Host-side orchestration of one decoder layer (forward and backward) in C++: the launch sequence
+// of the reference's _layer_forward / _Layer.backward (solution/engine.py:1054-1340) over this
+// library's kernels, on one stream, temporaries carved out of a caller-owned workspace. One call
+// per layer pass replaces ~20 Python-level launches.
+#include "common.cuh"
+#include "ops.h"
+
+namespace ql {
+namespace {
+
+struct Bump {
+  uint8_t* base;
+  int64_t cap, off;
+  void* take(int64_t bytes) {
+    off = (off + 255) & ~int64_t(255);
+    void* p = base != nullptr ? base + off : nullptr;
+    off += bytes;
+    return p;
+  }
+  bool ok() const { return base == nullptr || off <= cap; }
+};
+
+int64_t esz(int dtype) { return dtype == QL_F32 ? 4 : 2; }
+
+int64_t max_weight_elems(const ql_layer_desc& L) {
+  const int64_t C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
+  int64_t m = C * L.H;
+  m = m > (int64_t)L.H * L.HQ * L.D ? m : (int64_t)L.H * L.HQ * L.D;
+  m = m > 2LL * L.I * L.H ? m : 2LL * L.I * L.H;
+  return m;
+}
+
+int dequant(const ql_nf4_weight& w, void* out, int dtype, int transpose, cudaStream_t s) {
+  return nf4_dequant(w.packed, w.absmax, w.code2, w.absmax2, w.offsets, w.code, out, w.rows,
+                     w.cols, w.nested, w.bs2, w.seg1, w.seg2, dtype, transpose, s);
+}
+
+#define QL_TRY(x)                  \
+  do {                             \
+    const int _rc = (x);           \
+    if (_rc != QL_STATUS_OK) return _rc; \
+  } while (0)
+
+struct FwdWs {
+  void* w;    // dequantised weight (largest of the four)
+  void* a;    // [n, H] norm output (a, then b)
+  void* qkv;  // [n, C]
+  void* m;    // [n, I]
+};
+
+FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
+  const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D, e = esz(L.dtype);
+  FwdWs w;
+  w.w = b.take(max_weight_elems(L) * e);
+  w.a = b.take(n * L.H * e);
+  w.qkv = b.take(n * C * e);
+  w.m = b.take(n * L.I * e);
+  return w;
+}
+
+struct BwdWs {
+  void* w;
+  void* dm;      // [n, I]
+  void* db;      // [n, H]
+  float* dh2;    // [n, H]
+  void* dh2_16;  // [n, H]
+  void* dout;    // [n, HQ D]
+  float* dq;     // [n, HQ D]
+  float* dk;     // [n, HKV D]
+  float* dv;
+  float* dvec;   // [HQ, n]
+  void* dqkv;    // [n, C]
+  float* dxq;    // [n, rank]
+  float* dxv;
+  float* cs;     // colsum partials
+  int64_t cs_floats;
+  void* da;      // [n, H]
+};
+
+BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
+  const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D, e = esz(L.dtype);
+  BwdWs w;
+  w.w = b.take(max_weight_elems(L) * e);
+  w.dm = b.take(n * L.I * e);
+  w.db = b.take(n * L.H * e);
+  w.dh2 = (float*)b.take(n * L.H * 4);
+  w.dh2_16 = b.take(n * L.H * e);
+  w.dout = b.take(n * L.HQ * L.D * e);
+  w.dq = (float*)b.take(n * L.HQ * L.D * 4);
+  w.dk = (float*)b.take(n * L.HKV * L.D * 4);
+  w.dv = (float*)b.take(n * L.HKV * L.D * 4);
+  w.dvec = (float*)b.take((int64_t)L.HQ * n * 4);
+  w.dqkv = b.take(n * C * e);
+  w.dxq = (float*)b.take(n * L.rank * 4);
+  w.dxv = (float*)b.take(n * L.rank * 4);
+  int64_t csf = 0;
+  for (int64_t cols : {(int64_t)L.H, (int64_t)L.HQ * L.D, (int64_t)L.HKV * L.D}) {
+    const int64_t f = (int64_t)lora_colsum_splits(n, (int)cols) * cols * L.rank;
+    csf = f > csf ? f : csf;
+  }
+  w.cs_floats = csf;
+  w.cs = (float*)b.take(w.cs_floats * 4);
+  w.da = b.take(n * L.H * e);
+  return w;
+}
+
+void fill_drop(const ql_layer_desc& L, int64_t& seed, int64_t& cq, int64_t& cv, int64_t& thr,
+               float& pk, float& ks, int32_t& vec, int32_t& dq, int32_t& dv) {
+  seed = L.seed; cq = L.ctr_q; cv = L.ctr_v; thr = L.threads;
+  pk = L.p_keep; ks = L.keep_scale; vec = L.vec; dq = L.drop_q; dv = L.drop_v;
+}
+
+int check(const ql_layer_desc& L) {
+  if (L.n < 0 || L.H <= 0 || L.HQ <= 0 || L.HKV <= 0 || L.D <= 0 || L.I <= 0) return QL_STATUS_BAD_ARG;
+  if (L.rank != 16) return QL_STATUS_UNSUPPORTED;
+  if (L.dtype != QL_F16 && L.dtype != QL_BF16) return QL_STATUS_BAD_ARG;
+  return QL_STATUS_OK;
+}
+
+}  // namespace
+
+int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward) {
+  Bump b{nullptr, 0, 0};
+  if (backward) carve_bwd(L, b); else carve_fwd(L, b);
+  return b.off + 256;
+}
+
+int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,
+                  int64_t ws_bytes, int* err, cudaStream_t s) {
+  QL_TRY(check(L));
+  if (L.n == 0) return QL_STATUS_OK;
+  Bump bump{(uint8_t*)ws, ws_bytes, 0};
+  const FwdWs w = carve_fwd(L, bump);
+  if (!bump.ok()) return QL_STATUS_BAD_ARG;
+  const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
+  const int dt = L.dtype;
+
+  // input RMSNorm + the dropped LoRA inputs + LoRA-A products
+  RmsFwdC r1{};
+  r1.x = S.h; r1.w = L.ln1; r1.y = w.a; r1.yq = S.yq; r1.yv = S.yv; r1.rstd = S.rstd1;
+  r1.Aq = L.Aq; r1.Av = L.Av; r1.xq = S.xq; r1.xv = S.xv;
+  r1.n = L.n; r1.H = L.H; r1.rank = L.rank; r1.dtype = dt; r1.eps = L.eps; r1.tok = L.tok;
+  fill_drop(L, r1.seed, r1.ctr_q, r1.ctr_v, r1.threads, r1.p_keep, r1.keep_scale, r1.vec,
+            r1.drop_q, r1.drop_v);
+  QL_TRY(rms_fwd(r1, s));
+  // q, k, v in one GEMM (bias in the epilogue), then LoRA-B + RoPE
+  QL_TRY(dequant(L.qkv, w.w, dt, 0, s));
+  QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, w.qkv, C, L.bias_qkv, L.n, (int)C, L.H, dt, dt, 0, nullptr,
+                 err, s));
+  RopeFwdC rf{};
+  rf.qkv = w.qkv; rf.xq = S.xq; rf.xv = S.xv; rf.Bq = L.Bq; rf.Bv = L.Bv; rf.cos = L.cos;
+  rf.sin = L.sin; rf.pos = L.pos; rf.q = S.q; rf.k = S.k; rf.v = S.v;
+  rf.lora_scale = L.lora_scale; rf.n = L.n; rf.HQ = L.HQ; rf.HKV = L.HKV; rf.D = L.D;
+  rf.rank = L.rank; rf.dtype = dt;
+  QL_TRY(rope_fwd(rf, s));
+  AttnFwdC af{};
+  af.q = S.q; af.k = S.k; af.v = S.v; af.cu_seqlens = L.cu_seqlens; af.out = S.out; af.lse = S.lse;
+  af.scale = L.scale; af.n = L.n; af.B = L.B; af.max_len = L.max_len; af.HQ = L.HQ;
+  af.HKV = L.HKV; af.D = L.D; af.dtype = dt;
+  QL_TRY(attn_fwd(af, s));
+  // o projection, residual add in the epilogue: h2 = h + o
+  QL_TRY(dequant(L.o, w.w, dt, 0, s));
+  QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, w.w, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
+                 L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s));
+  // post-attention RMSNorm
+  RmsFwdC r2{};
+  r2.x = S.h2; r2.w = L.ln2; r2.y = w.a; r2.rstd = S.rstd2; r2.n = L.n; r2.H = L.H;
+  r2.rank = L.rank; r2.dtype = dt; r2.eps = L.eps; r2.vec = 4; r2.threads = 1; r2.p_keep = 1.f;
+  r2.keep_scale = 1.f;
+  QL_TRY(rms_fwd(r2, s));
+  // [gate | up], SwiGLU, down with the residual add: h3 = h2 + d
+  QL_TRY(dequant(L.gu, w.w, dt, 0, s));
+  QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
+                 nullptr, err, s));
+  QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
+  QL_TRY(dequant(L.down, w.w, dt, 0, s));
+  QL_TRY(gemm_tn(w.m, L.I, w.w, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
+                 err, s));
+  return QL_STATUS_OK;
+}
+
+int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float* dh3,
+                   const void* dh3_16, float* grads, float* dh_out, void* dh16_out, void* ws,
+                   int64_t ws_bytes, int* err, cudaStream_t s) {
+  QL_TRY(check(L));
+  if (L.n == 0) return QL_STATUS_OK;
+  Bump bump{(uint8_t*)ws, ws_bytes, 0};
+  const BwdWs w = carve_bwd(L, bump);
+  if (!bump.ok()) return QL_STATUS_BAD_ARG;
+  const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
+  const int dt = L.dtype;
+  float* gAq = grads;
+  float* gBq = gAq + (int64_t)L.rank * L.H;
+  float* gAv = gBq + (int64_t)L.HQ * L.D * L.rank;
+  float* gBv = gAv + (int64_t)L.rank * L.H;
+
+  // MLP: dm = dh3 . Wd ; [dg | du] in place ; db = [dg | du] . Wgu
+  QL_TRY(dequant(L.down, w.w, dt, 1, s));
+  QL_TRY(gemm_tn(dh3_16, L.H, w.w, L.H, w.dm, L.I, nullptr, L.n, L.I, L.H, dt, dt, 0, nullptr,
+                 err, s));
+  QL_TRY(glu_bwd(w.dm, S.gu, n, L.I, dt, s));
+  QL_TRY(dequant(L.gu, w.w, dt, 1, s));
+  QL_TRY(gemm_tn(S.gu, 2LL * L.I, w.w, 2LL * L.I, w.db, L.H, nullptr, L.n, L.H, 2 * L.I, dt, dt,
+                 0, nullptr, err, s));
+  RmsBwdC r2{};
+  r2.dy = w.db; r2.ld_dy = L.H; r2.x = S.h2; r2.rstd = S.rstd2; r2.w = L.ln2; r2.dres = dh3;
+  r2.dx = w.dh2; r2.dx16 = w.dh2_16; r2.n = L.n; r2.H = L.H; r2.rank = L.rank; r2.dtype = dt;
+  r2.grad_scale = 1.f; r2.vec = 4; r2.threads = 1; r2.p_keep = 1.f; r2.keep_scale = 1.f;
+  QL_TRY(rms_bwd(r2, s));
+  // attention
+  QL_TRY(dequant(L.o, w.w, dt, 1, s));
+  QL_TRY(gemm_tn(w.dh2_16, L.H, w.w, L.H, w.dout, (int64_t)L.HQ * L.D, nullptr, L.n, L.HQ * L.D,
+                 L.H, dt, dt, 0, nullptr, err, s));
+  AttnBwdC ab{};
+  ab.q = S.q; ab.k = S.k; ab.v = S.v; ab.out = S.out; ab.dout = w.dout; ab.lse = S.lse;
+  ab.cu_seqlens = L.cu_seqlens; ab.dvec = w.dvec; ab.dq = w.dq; ab.dk = w.dk; ab.dv = w.dv;
+  ab.scale = L.scale; ab.n = L.n; ab.B = L.B; ab.max_len = L.max_len; ab.HQ = L.HQ;
+  ab.HKV = L.HKV; ab.D = L.D; ab.dtype = dt;
+  QL_TRY(attn_bwd(ab, s));
+  RopeBwdC rb{};
+  rb.dq = w.dq; rb.dk = w.dk; rb.dv = w.dv; rb.cos = L.cos; rb.sin = L.sin; rb.pos = L.pos;
+  rb.dqkv = w.dqkv; rb.Bq = L.Bq; rb.Bv = L.Bv; rb.dxlo_q = w.dxq; rb.dxlo_v = w.dxv;
+  rb.lora_scale = L.lora_scale; rb.n = L.n; rb.HQ = L.HQ; rb.HKV = L.HKV; rb.D = L.D;
+  rb.kv_heads_in = L.HKV; rb.rank = L.rank; rb.dtype = dt; rb.grad_dtype = QL_F32;
+  QL_TRY(rope_bwd(rb, s));
+  // LoRA weight gradients: dB = s g^T x_lo, dA = dx_lo^T drop(a)
+  const int64_t qcols = (int64_t)L.HQ * L.D, vcols = (int64_t)L.HKV * L.D;
+  const uint8_t* dqkv = (const uint8_t*)w.dqkv;
+  QL_TRY(lora_colsum(dqkv, C, dt, S.xq, dt, n, (int)qcols, L.rank, L.lora_scale, 0, gBq, w.cs,
+                     w.cs_floats, s));
+  QL_TRY(lora_colsum(dqkv + (qcols + vcols) * esz(dt), C, dt, S.xv, dt, n, (int)vcols, L.rank,
+                     L.lora_scale, 0, gBv, w.cs, w.cs_floats, s));
+  QL_TRY(lora_colsum(S.yq, L.H, dt, w.dxq, QL_F32, n, L.H, L.rank, 1.f, 1, gAq, w.cs,
+                     w.cs_floats, s));
+  QL_TRY(lora_colsum(S.yv, L.H, dt, w.dxv, QL_F32, n, L.H, L.rank, 1.f, 1, gAv, w.cs,
+                     w.cs_floats, s));
+  if (dh_out == nullptr) return QL_STATUS_OK;  // the first layer's input is the frozen embedding
+  QL_TRY(dequant(L.qkv, w.w, dt, 1, s));
+  QL_TRY(gemm_tn(w.dqkv, C, w.w, C, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,
+                 err, s));
+  RmsBwdC r1{};
+  r1.dy = w.da; r1.ld_dy = L.H; r1.x = S.h; r1.rstd = S.rstd1; r1.w = L.ln1; r1.dres = w.dh2;
+  r1.dx = dh_out; r1.dx16 = dh16_out; r1.dxlo_q = w.dxq; r1.dxlo_v = w.dxv; r1.Aq = L.Aq;
+  r1.Av = L.Av; r1.n = L.n; r1.H = L.H; r1.rank = L.rank; r1.dtype = dt; r1.grad_scale = 1.f;
+  r1.tok = L.tok;
+  fill_drop(L, r1.seed, r1.ctr_q, r1.ctr_v, r1.threads, r1.p_keep, r1.keep_scale, r1.vec,
+            r1.drop_q, r1.drop_v);
+  QL_TRY(rms_bwd(r1, s));
+  return QL_STATUS_OK;
+}
+
+}  // namespace ql

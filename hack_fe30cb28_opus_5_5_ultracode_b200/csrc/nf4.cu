@@ -9,6 +9,7 @@
 // block), and its transpose ([cols, rows], through a 64 x 64 shared-memory tile) for the
 // data-gradient GEMMs, whose B operand is the weight's transpose in K-major order.
 #include "common.cuh"
+#include "profile.h"
 
 namespace ql {
 
@@ -127,7 +128,7 @@ static int launch_nf4(const Nf4Args& a, void* out, int64_t rows, int64_t cols, b
     if (nested) nf4_dequant_kernel<OutT, true><<<grid, 256, 0, s>>>(a, o);
     else nf4_dequant_kernel<OutT, false><<<grid, 256, 0, s>>>(a, o);
   }
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
@@ -145,6 +146,7 @@ int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
     return QL_STATUS_BAD_ARG;
   Nf4Args a{packed, absmax, code2, absmax2, offsets, code, numel / 64, bs2 > 0 ? bs2 : 1,
             seg1, seg2};
+  ProfScope prof(PK_DEQUANT, 0, numel * (0.5 + (nested ? 1.0 : 4.0) / 64 + 2.0), stream);
   if (out_dtype == QL_F16) return launch_nf4<__half>(a, out, rows, cols, nested, transpose, stream);
   if (out_dtype == QL_BF16)
     return launch_nf4<__nv_bfloat16>(a, out, rows, cols, nested, transpose, stream);

@@ -13,16 +13,19 @@
 // LoRA factors, tq = dx_lo . A (solution/engine.py:1326-1330), rounded like the reference's fp16
 // GEMM output. Optionally also writes dx in the 16-bit type (the next data-gradient GEMM's A).
 //
-// One CTA of 128 threads per row, each thread holding groups of 4 consecutive columns in
-// registers (H <= 4096): one HBM read of the row, one write per output.
+// One warp per row, each lane holding groups of 4 consecutive columns in registers (H <= 4096):
+// one HBM read of the row, one write per output; the LoRA factors A (2 x 16 x H 16-bit) are
+// staged in shared memory once per CTA, and the 32 LoRA-A sums of a row leave the warp by one
+// reduce-scatter.
 #include "common.cuh"
+#include "profile.h"
 #include "ops.h"
 #include "philox.cuh"
 
 namespace ql {
 
-constexpr int RMS_THREADS = 128;
-constexpr int RMS_MAXG = 8;  // groups of 4 per thread: H <= 4 * 128 * 8 = 4096
+constexpr int RMS_THREADS = 128;  // (used for the H bound below)
+constexpr int RMS_MAXG = 8;       // H <= 4 * 128 * 8 = 4096
 constexpr int LORA_R = 16;
 
 struct RmsFwdArgs {
@@ -95,186 +98,213 @@ __device__ __forceinline__ float4 masked4(float4 v, uint32_t keep, float s) {
                      (keep & 4u) ? v.z * s : 0.f, (keep & 8u) ? v.w * s : 0.f);
 }
 
-// Sums NV values held by every thread of the CTA; the result is valid in all threads.
-template <int NV>
-__device__ __forceinline__ void block_sum(float* v, float* scratch /* [4][NV] */) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Sum over the warp of 32 per-lane values v[0..31]; afterwards lane l holds the total of value l
+// (reduce-scatter: 31 shuffles instead of 32 x 5).
+__device__ __forceinline__ float reduce_scatter32(float* v) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) v[i] = warp_sum(v[i]);
-  __syncthreads();
-  if (lane == 0) {
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) scratch[warp * NV + i] = v[i];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < NV; ++i) v[i] = scratch[i] + scratch[NV + i] + scratch[2 * NV + i] + scratch[3 * NV + i];
-}
-
-template <typename T>
-__global__ void __launch_bounds__(RMS_THREADS) rms_fwd_kernel(RmsFwdArgs a) {
-  __shared__ float scratch[4 * 2 * LORA_R];
-  const int row = blockIdx.x;
-  const int H = a.H, ngroups = H / 4;
-  const int64_t base = (int64_t)row * H;
-  float4 xv[RMS_MAXG];
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < RMS_MAXG; ++k) {
-    const int gi = threadIdx.x + k * RMS_THREADS;
-    if (gi < ngroups) {
-      float4 x = *reinterpret_cast<const float4*>(a.x + base + 4 * gi);
-      if (a.delta != nullptr) {
-        const float4 d = load4<T>(reinterpret_cast<const T*>(a.delta) + base + 4 * gi);
-        x = make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
-        *reinterpret_cast<float4*>(a.xsum + base + 4 * gi) = x;
-      }
-      xv[k] = x;
-      ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
     }
   }
-  float tot[1] = {ss};
-  block_sum<1>(tot, scratch);
-  const float rstd = 1.0f / sqrtf(tot[0] / (float)H + a.eps);
-  if (threadIdx.x == 0) a.rstd[row] = rstd;
+  return v[0];
+}
 
+// One warp per row (8 rows in flight per CTA, rows strided over the grid); the row's groups of
+// 4 columns g = lane + 32 k stay in registers between the two passes (G = groups per lane).
+// The LoRA-A factors are staged once per CTA in shared memory.
+template <typename T, int G>
+__global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
+  extern __shared__ __align__(16) uint8_t rms_smem[];
+  T* sAq = reinterpret_cast<T*>(rms_smem);
+  T* sAv = sAq + LORA_R * a.H;
+  const int H = a.H, ngroups = H / 4;
   const bool lora_q = a.drop.drop_q && a.Aq != nullptr, lora_v = a.drop.drop_v && a.Av != nullptr;
-  float accq[LORA_R], accv[LORA_R];
-#pragma unroll
-  for (int r = 0; r < LORA_R; ++r) accq[r] = accv[r] = 0.f;
-  const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
-#pragma unroll
-  for (int k = 0; k < RMS_MAXG; ++k) {
-    const int gi = threadIdx.x + k * RMS_THREADS;
-    if (gi < ngroups) {
-      const int c = 4 * gi;
-      const float4 w = *reinterpret_cast<const float4*>(a.w + c);
-      const float4 x = xv[k];
-      const float4 y = make_float4(w.x * (x.x * rstd), w.y * (x.y * rstd), w.z * (x.z * rstd),
-                                   w.w * (x.w * rstd));
-      if (a.y != nullptr) store4<T>(reinterpret_cast<T*>(a.y) + base + c, y);
-      if (a.drop.drop_q) {
-        const float4 yq = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_q, a.drop), a.drop.keep_scale));
-        if (a.yq != nullptr) store4<T>(reinterpret_cast<T*>(a.yq) + base + c, yq);
-        if (lora_q) {
-          const T* A = reinterpret_cast<const T*>(a.Aq);
-#pragma unroll
-          for (int r = 0; r < LORA_R; ++r) {
-            const float4 av = load4<T>(A + (int64_t)r * H + c);
-            accq[r] += yq.x * av.x + yq.y * av.y + yq.z * av.z + yq.w * av.w;
-          }
-        }
-      }
-      if (a.drop.drop_v) {
-        const float4 yv = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_v, a.drop), a.drop.keep_scale));
-        if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
-        if (lora_v) {
-          const T* A = reinterpret_cast<const T*>(a.Av);
-#pragma unroll
-          for (int r = 0; r < LORA_R; ++r) {
-            const float4 av = load4<T>(A + (int64_t)r * H + c);
-            accv[r] += yv.x * av.x + yv.y * av.y + yv.z * av.z + yv.w * av.w;
-          }
-        }
-      }
-    }
-  }
   if (lora_q || lora_v) {
-    float v[2 * LORA_R];
-#pragma unroll
-    for (int r = 0; r < LORA_R; ++r) {
-      v[r] = accq[r];
-      v[LORA_R + r] = accv[r];
+    const int chunks = LORA_R * H / 8;  // 16-byte chunks per factor
+    for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+      if (lora_q) reinterpret_cast<uint4*>(sAq)[i] = reinterpret_cast<const uint4*>(a.Aq)[i];
+      if (lora_v) reinterpret_cast<uint4*>(sAv)[i] = reinterpret_cast<const uint4*>(a.Av)[i];
     }
-    block_sum<2 * LORA_R>(v, scratch);
-    if (threadIdx.x < LORA_R) {
-      const int r = threadIdx.x;
-      float q = 0.f, vv = 0.f;
+    __syncthreads();
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {
+    const int64_t base = (int64_t)row * H;
+    float4 xv[G];
+    float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < LORA_R; ++i) {
-        if (i == r) { q = v[i]; vv = v[LORA_R + i]; }
+    for (int k = 0; k < G; ++k) {
+      const int gi = lane + 32 * k;
+      if (gi < ngroups) {
+        float4 x = *reinterpret_cast<const float4*>(a.x + base + 4 * gi);
+        if (a.delta != nullptr) {
+          const float4 d = load4<T>(reinterpret_cast<const T*>(a.delta) + base + 4 * gi);
+          x = make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
+          *reinterpret_cast<float4*>(a.xsum + base + 4 * gi) = x;
+        }
+        xv[k] = x;
+        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
       }
-      if (lora_q) reinterpret_cast<T*>(a.xq)[(int64_t)row * LORA_R + r] = from_f<T>(q);
-      if (lora_v) reinterpret_cast<T*>(a.xv)[(int64_t)row * LORA_R + r] = from_f<T>(vv);
+    }
+    ss = warp_sum(ss);
+    const float rstd = 1.0f / sqrtf(ss / (float)H + a.eps);
+    if (lane == 0) a.rstd[row] = rstd;
+    float acc[2 * LORA_R];
+#pragma unroll
+    for (int r = 0; r < 2 * LORA_R; ++r) acc[r] = 0.f;
+    const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
+#pragma unroll
+    for (int k = 0; k < G; ++k) {
+      const int gi = lane + 32 * k;
+      if (gi < ngroups) {
+        const int c = 4 * gi;
+        const float4 w = *reinterpret_cast<const float4*>(a.w + c);
+        const float4 x = xv[k];
+        const float4 y = make_float4(w.x * (x.x * rstd), w.y * (x.y * rstd), w.z * (x.z * rstd),
+                                     w.w * (x.w * rstd));
+        if (a.y != nullptr) store4<T>(reinterpret_cast<T*>(a.y) + base + c, y);
+        if (a.drop.drop_q) {
+          const float4 yq = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_q, a.drop), a.drop.keep_scale));
+          if (a.yq != nullptr) store4<T>(reinterpret_cast<T*>(a.yq) + base + c, yq);
+          if (lora_q) {
+#pragma unroll
+            for (int r = 0; r < LORA_R; ++r) {
+              const float4 av = load4<T>(sAq + r * H + c);
+              acc[r] += yq.x * av.x + yq.y * av.y + yq.z * av.z + yq.w * av.w;
+            }
+          }
+        }
+        if (a.drop.drop_v) {
+          const float4 yv = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_v, a.drop), a.drop.keep_scale));
+          if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
+          if (lora_v) {
+#pragma unroll
+            for (int r = 0; r < LORA_R; ++r) {
+              const float4 av = load4<T>(sAv + r * H + c);
+              acc[LORA_R + r] += yv.x * av.x + yv.y * av.y + yv.z * av.z + yv.w * av.w;
+            }
+          }
+        }
+      }
+    }
+    if (lora_q || lora_v) {
+      const float tot = reduce_scatter32(acc);  // lane l: value l (q: 0..15, v: 16..31)
+      if (lane < LORA_R) {
+        if (lora_q) reinterpret_cast<T*>(a.xq)[(int64_t)row * LORA_R + lane] = from_f<T>(tot);
+      } else if (lora_v) {
+        reinterpret_cast<T*>(a.xv)[(int64_t)row * LORA_R + lane - LORA_R] = from_f<T>(tot);
+      }
     }
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(RMS_THREADS) rms_bwd_kernel(RmsBwdArgs a) {
-  __shared__ float scratch[4];
-  __shared__ float lq[LORA_R], lv[LORA_R];
-  const int row = blockIdx.x;
+template <typename T, int G>
+__global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
+  extern __shared__ __align__(16) uint8_t rms_smem[];
+  T* sAq = reinterpret_cast<T*>(rms_smem);
+  T* sAv = sAq + LORA_R * a.H;
   const int H = a.H, ngroups = H / 4;
-  const int64_t base = (int64_t)row * H;
-  if (threadIdx.x < LORA_R) {
-    lq[threadIdx.x] = a.dxlo_q != nullptr ? a.dxlo_q[(int64_t)row * LORA_R + threadIdx.x] : 0.f;
-    lv[threadIdx.x] = a.dxlo_v != nullptr ? a.dxlo_v[(int64_t)row * LORA_R + threadIdx.x] : 0.f;
+  const bool fq = a.drop.drop_q && a.tq == nullptr, fv = a.drop.drop_v && a.tv == nullptr;
+  if (fq || fv) {
+    const int chunks = LORA_R * H / 8;
+    for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+      if (fq) reinterpret_cast<uint4*>(sAq)[i] = reinterpret_cast<const uint4*>(a.Aq)[i];
+      if (fv) reinterpret_cast<uint4*>(sAv)[i] = reinterpret_cast<const uint4*>(a.Av)[i];
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  const float rstd = a.rstd[row];
-  const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
-  float4 gv[RMS_MAXG], xh[RMS_MAXG];
-  float dot = 0.f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {
+    const int64_t base = (int64_t)row * H;
+    const float rstd = a.rstd[row];
+    // this row's LoRA input gradients dx_lo (q: lanes 0..15, v: lanes 16..31), broadcast below
+    float lo_mine = 0.f;
+    if (lane < LORA_R) { if (a.dxlo_q != nullptr) lo_mine = a.dxlo_q[(int64_t)row * LORA_R + lane]; }
+    else if (a.dxlo_v != nullptr) lo_mine = a.dxlo_v[(int64_t)row * LORA_R + lane - LORA_R];
+    float lo[2 * LORA_R];
 #pragma unroll
-  for (int k = 0; k < RMS_MAXG; ++k) {
-    const int gi = threadIdx.x + k * RMS_THREADS;
-    if (gi < ngroups) {
-      const int c = 4 * gi;
-      float4 dy = load4<T>(reinterpret_cast<const T*>(a.dy) + (int64_t)row * a.ld_dy + c);
-      for (int which = 0; which < 2; ++which) {
-        const bool on = which == 0 ? a.drop.drop_q : a.drop.drop_v;
-        if (!on) continue;
-        const void* tex = which == 0 ? a.tq : a.tv;
-        const float* lo = which == 0 ? lq : lv;
-        const void* A = which == 0 ? a.Aq : a.Av;
-        float4 t;
-        if (tex != nullptr) {
-          t = load4<T>(reinterpret_cast<const T*>(tex) + base + c);
-        } else {
-          const T* At = reinterpret_cast<const T*>(A);
-          t = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < 2 * LORA_R; ++r) lo[r] = __shfl_sync(0xffffffffu, lo_mine, r);
+    const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
+    float4 gv[G], xh[G];
+    float dot = 0.f;
 #pragma unroll
-          for (int r = 0; r < LORA_R; ++r) {
-            const float4 av = load4<T>(At + (int64_t)r * H + c);
-            t.x += lo[r] * av.x; t.y += lo[r] * av.y; t.z += lo[r] * av.z; t.w += lo[r] * av.w;
+    for (int k = 0; k < G; ++k) {
+      const int gi = lane + 32 * k;
+      if (gi < ngroups) {
+        const int c = 4 * gi;
+        float4 dy = load4<T>(reinterpret_cast<const T*>(a.dy) + (int64_t)row * a.ld_dy + c);
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const bool on = which == 0 ? a.drop.drop_q : a.drop.drop_v;
+          if (!on) continue;
+          const void* tex = which == 0 ? a.tq : a.tv;
+          float4 t;
+          if (tex != nullptr) {
+            t = load4<T>(reinterpret_cast<const T*>(tex) + base + c);
+          } else {
+            const T* At = which == 0 ? sAq : sAv;
+            t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < LORA_R; ++r) {
+              const float l = lo[which * LORA_R + r];
+              const float4 av = load4<T>(At + r * H + c);
+              t.x += l * av.x; t.y += l * av.y; t.z += l * av.z; t.w += l * av.w;
+            }
+            t = round4<T>(t);
           }
-          t = round4<T>(t);
+          const uint32_t keep = keep4(e_row + c, which == 0 ? a.drop.ctr_q : a.drop.ctr_v, a.drop);
+          const float4 m = masked4(t, keep, a.drop.keep_scale);
+          dy = make_float4(dy.x + m.x, dy.y + m.y, dy.z + m.z, dy.w + m.w);
         }
-        const uint32_t keep = keep4(e_row + c, which == 0 ? a.drop.ctr_q : a.drop.ctr_v, a.drop);
-        const float4 m = masked4(t, keep, a.drop.keep_scale);
-        dy = make_float4(dy.x + m.x, dy.y + m.y, dy.z + m.z, dy.w + m.w);
+        const float4 w = *reinterpret_cast<const float4*>(a.w + c);
+        const float4 x = *reinterpret_cast<const float4*>(a.x + base + c);
+        const float4 g = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
+        const float4 h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
+        gv[k] = g;
+        xh[k] = h;
+        dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
       }
-      const float4 w = *reinterpret_cast<const float4*>(a.w + c);
-      const float4 x = *reinterpret_cast<const float4*>(a.x + base + c);
-      const float4 g = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
-      const float4 h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
-      gv[k] = g;
-      xh[k] = h;
-      dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
     }
-  }
-  float tot[1] = {dot};
-  block_sum<1>(tot, scratch);
-  const float mean = tot[0] / (float)H;
+    const float mean = warp_sum(dot) / (float)H;
 #pragma unroll
-  for (int k = 0; k < RMS_MAXG; ++k) {
-    const int gi = threadIdx.x + k * RMS_THREADS;
-    if (gi < ngroups) {
-      const int c = 4 * gi;
-      const float4 g = gv[k], h = xh[k];
-      float4 d = make_float4(rstd * (g.x - h.x * mean) * a.grad_scale,
-                             rstd * (g.y - h.y * mean) * a.grad_scale,
-                             rstd * (g.z - h.z * mean) * a.grad_scale,
-                             rstd * (g.w - h.w * mean) * a.grad_scale);
-      if (a.dres != nullptr) {
-        const float4 r = *reinterpret_cast<const float4*>(a.dres + base + c);
-        d = make_float4(d.x + r.x, d.y + r.y, d.z + r.z, d.w + r.w);
+    for (int k = 0; k < G; ++k) {
+      const int gi = lane + 32 * k;
+      if (gi < ngroups) {
+        const int c = 4 * gi;
+        const float4 g = gv[k], h = xh[k];
+        float4 d = make_float4(rstd * (g.x - h.x * mean) * a.grad_scale,
+                               rstd * (g.y - h.y * mean) * a.grad_scale,
+                               rstd * (g.z - h.z * mean) * a.grad_scale,
+                               rstd * (g.w - h.w * mean) * a.grad_scale);
+        if (a.dres != nullptr) {
+          const float4 r = *reinterpret_cast<const float4*>(a.dres + base + c);
+          d = make_float4(d.x + r.x, d.y + r.y, d.z + r.z, d.w + r.w);
+        }
+        *reinterpret_cast<float4*>(a.dx + base + c) = d;
+        if (a.dx16 != nullptr) store4<T>(reinterpret_cast<T*>(a.dx16) + base + c, d);
       }
-      *reinterpret_cast<float4*>(a.dx + base + c) = d;
-      if (a.dx16 != nullptr) store4<T>(reinterpret_cast<T*>(a.dx16) + base + c, d);
     }
   }
+}
+
+static int rms_grid(int64_t n) {
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = cdiv(n, 8);
+  const int64_t cap = (int64_t)sms * 4;
+  return (int)(want < cap ? want : cap);
+}
+
+template <typename K>
+static void set_smem(K kern, int bytes) {
+  if (bytes > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
@@ -284,15 +314,32 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   if ((c.drop_q || c.drop_v) && c.tok == nullptr) return QL_STATUS_BAD_ARG;
   if ((c.Aq != nullptr && c.xq == nullptr) || (c.Av != nullptr && c.xv == nullptr)) return QL_STATUS_BAD_ARG;
   if ((c.Aq != nullptr || c.Av != nullptr) && c.rank != LORA_R) return QL_STATUS_UNSUPPORTED;
+  ProfScope prof(PK_RMS_FWD, 0, (double)c.n * c.H * (4 + (c.delta ? 6 : 0) + (c.y ? 2 : 0) +
+                                                     (c.yq ? 2 : 0) + (c.yv ? 2 : 0)), s);
   RmsFwdArgs a{c.x, c.delta, c.w, c.xsum, c.y, c.yq, c.yv, c.rstd, c.Aq, c.Av, c.xq, c.xv, c.n,
                c.H, c.eps,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
                            c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v}};
   if (c.vec != 4 && c.vec != 8) return QL_STATUS_BAD_ARG;
-  if (c.dtype == QL_F16) rms_fwd_kernel<__half><<<c.n, RMS_THREADS, 0, s>>>(a);
-  else if (c.dtype == QL_BF16) rms_fwd_kernel<__nv_bfloat16><<<c.n, RMS_THREADS, 0, s>>>(a);
-  else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  const bool lora = (c.drop_q && c.Aq != nullptr) || (c.drop_v && c.Av != nullptr);
+  const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
+  const int grid = rms_grid(c.n);
+#define QL_RMSF(TT, GG)                                              \
+  do {                                                               \
+    set_smem(rms_fwd_kernel<TT, GG>, smem);                          \
+    rms_fwd_kernel<TT, GG><<<grid, 256, smem, s>>>(a);               \
+  } while (0)
+  const int G = (int)cdiv(c.H / 4, 32);
+  if (c.dtype == QL_F16) {
+    if (G <= 4) QL_RMSF(__half, 4); else if (G <= 12) QL_RMSF(__half, 12); else QL_RMSF(__half, 32);
+  } else if (c.dtype == QL_BF16) {
+    if (G <= 4) QL_RMSF(__nv_bfloat16, 4); else if (G <= 12) QL_RMSF(__nv_bfloat16, 12);
+    else QL_RMSF(__nv_bfloat16, 32);
+  } else {
+    return QL_STATUS_BAD_ARG;
+  }
+#undef QL_RMSF
+  return launched(1);
 }
 
 int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
@@ -304,14 +351,31 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   if ((c.dxlo_q != nullptr || c.dxlo_v != nullptr) && c.rank != LORA_R) return QL_STATUS_UNSUPPORTED;
   if (c.ld_dy % 4 != 0) return QL_STATUS_BAD_ARG;
   if (c.vec != 4 && c.vec != 8) return QL_STATUS_BAD_ARG;
+  ProfScope prof(PK_RMS_BWD, 0, (double)c.n * c.H * (2 + 4 + 4 + (c.dres ? 4 : 0) +
+                                                     (c.dx16 ? 2 : 0)), s);
   RmsBwdArgs a{c.dy, c.ld_dy, c.x, c.rstd, c.w, c.dres, c.dx, c.dx16, c.tq, c.tv, c.dxlo_q,
                c.dxlo_v, c.Aq, c.Av, c.n, c.H, c.grad_scale,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
                            c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v}};
-  if (c.dtype == QL_F16) rms_bwd_kernel<__half><<<c.n, RMS_THREADS, 0, s>>>(a);
-  else if (c.dtype == QL_BF16) rms_bwd_kernel<__nv_bfloat16><<<c.n, RMS_THREADS, 0, s>>>(a);
-  else return QL_STATUS_BAD_ARG;
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  const bool lora = (c.drop_q && c.tq == nullptr) || (c.drop_v && c.tv == nullptr);
+  const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
+  const int grid = rms_grid(c.n);
+#define QL_RMSB(TT, GG)                                              \
+  do {                                                               \
+    set_smem(rms_bwd_kernel<TT, GG>, smem);                          \
+    rms_bwd_kernel<TT, GG><<<grid, 256, smem, s>>>(a);               \
+  } while (0)
+  const int G = (int)cdiv(c.H / 4, 32);
+  if (c.dtype == QL_F16) {
+    if (G <= 4) QL_RMSB(__half, 4); else if (G <= 12) QL_RMSB(__half, 12); else QL_RMSB(__half, 32);
+  } else if (c.dtype == QL_BF16) {
+    if (G <= 4) QL_RMSB(__nv_bfloat16, 4); else if (G <= 12) QL_RMSB(__nv_bfloat16, 12);
+    else QL_RMSB(__nv_bfloat16, 32);
+  } else {
+    return QL_STATUS_BAD_ARG;
+  }
+#undef QL_RMSB
+  return launched(1);
 }
 
 }  // namespace ql
@@ -332,7 +396,7 @@ int dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t 
   DropoutArgs d{nullptr, seed, ctr, 0, threads, p_keep, 1.f, vec, 1, 0};
   const int64_t groups = cdiv(nelem, 4);
   dropout_keep_kernel<<<(unsigned)cdiv(groups, 256), 256, 0, s>>>(out, nelem, d);
-  return cudaPeekAtLastError() == cudaSuccess ? QL_STATUS_OK : QL_STATUS_CUDA;
+  return launched(1);
 }
 
 }  // namespace ql

@@ -37,7 +37,7 @@ int rope_fwd(const RopeFwdC& a, cudaStream_t s);
 int rope_bwd(const RopeBwdC& a, cudaStream_t s);
 int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s);
 int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t s);
-int lora_colsum_splits(int64_t n);
+int lora_colsum_splits(int64_t n, int ncols);
 int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
                 int ncols, int rank, float scale, int transpose, float* out, float* workspace,
                 int64_t workspace_floats, cudaStream_t s);
@@ -59,4 +59,19 @@ namespace ql {
 int gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, int H, cudaStream_t s);
 int scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst, void* dst16,
                  int64_t n, int H, int dtype, cudaStream_t s);
+}  // namespace ql
+
+namespace ql {
+int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward);
+int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,
+                  int64_t ws_bytes, int* err, cudaStream_t s);
+int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float* dh3,
+                   const void* dh3_16, float* grads, float* dh_out, void* dh16_out, void* ws,
+                   int64_t ws_bytes, int* err, cudaStream_t s);
+}  // namespace ql
+
+namespace ql {
+int profile_start(int capacity);
+int profile_stop();
+int profile_read(double* count, double* ms, double* flops, double* bytes);
 }  // namespace ql

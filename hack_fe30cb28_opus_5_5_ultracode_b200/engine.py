@@ -18,11 +18,11 @@ B200-first differences from the reference (which was built for a 16 GB T4):
     data-parallel run all-reduces with NCCL.
 """
 
-import math
+import ctypes
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 HEAD_CHUNK = 4096  # rows of logits alive at a time: 4096 x 151936 x 2 B = 1.2 GB of HBM
 
@@ -376,6 +376,39 @@ class FusedQwen2:
             self.offsets.append(self.offsets[-1] + n)
         self.process_group = None
         self.data_parallel = False  # LoRA gradients averaged over the ranks (dist.GradReducer)
+        for spec in self.layers:
+            for g in (spec.qkv, spec.o, spec.gu, spec.down):
+                if g.split:
+                    raise ValueError("double-quantised weights whose absmax2 blocks straddle "
+                                     "two members of a group are not supported")
+        self.descs = [self._layer_desc(spec) for spec in self.layers]
+        self._workspace = None
+
+    def _layer_desc(self, spec):
+        """The step-independent part of a layer's ql_layer_desc (weights, norms, LoRA, dims)."""
+        def w(g):
+            return _lib.struct("ql_nf4_weight", packed=g.packed.data_ptr(),
+                               absmax=g.absmax.data_ptr(), code=g.code.data_ptr(),
+                               code2=ops._ptr(g.code2), absmax2=ops._ptr(g.absmax2),
+                               offsets=ops._ptr(g.offsets), rows=g.rows, cols=g.cols,
+                               seg1=g.seg1, seg2=g.seg2, nested=int(g.nested), bs2=int(g.bs2))
+
+        Aq, Bq, Av, Bv = self.lora_views[4 * spec.index:4 * spec.index + 4]
+        return _lib.struct("ql_layer_desc", qkv=w(spec.qkv), o=w(spec.o), gu=w(spec.gu),
+                           down=w(spec.down), bias_qkv=spec.bias_qkv.data_ptr(),
+                           ln1=spec.ln1.data_ptr(), ln2=spec.ln2.data_ptr(), Aq=Aq.data_ptr(),
+                           Bq=Bq.data_ptr(), Av=Av.data_ptr(), Bv=Bv.data_ptr(), eps=spec.eps,
+                           scale=spec.scale, lora_scale=spec.lora_scale, H=spec.H, HQ=spec.HQ,
+                           HKV=spec.HKV, D=spec.D, I=spec.I, rank=16,
+                           dtype=ops.dtype_code(self.dtype))
+
+    def _workspace_for(self, desc):
+        need = max(int(_lib.lib().ql_layer_workspace_bytes(ctypes.addressof(desc), 0)),
+                   int(_lib.lib().ql_layer_workspace_bytes(ctypes.addressof(desc), 1)))
+        if self._workspace is None or self._workspace.numel() < need:
+            self._workspace = None
+            self._workspace = torch.empty(need, device=self.device, dtype=torch.uint8)
+        return self._workspace
 
     def set_data_parallel(self, group=None):
         """Average the LoRA gradients over `group` (None: the default process group) inside the
@@ -417,44 +450,40 @@ class FusedQwen2:
 
     def _forward(self, packed, denom, stats):
         n = packed.n
+        spec0 = self.layers[0]
         cos, sin = self.rope.table(max(packed.max_len, 1))
-        h = ops.embed(packed.ids, self.embed)
+        arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device)
+        h = arena.h(0)
+        if n:
+            ops.embed(packed.ids, self.embed, out=h)
         saved = []
-        for spec in self.layers:
+        for spec, desc in zip(self.layers, self.descs):
             drop = self._drop(packed, spec.H)
-            h, sv = self._layer_fwd(spec, h, packed, drop, cos, sin)
-            saved.append(sv)
+            self._set_step(desc, packed, drop, cos, sin)
+            sv = arena.saved(spec.index)
+            if n:
+                ws = self._workspace_for(desc)
+                _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
+                          arena.h(spec.index + 1).data_ptr(), ws.data_ptr(), ws.numel(),
+                          ops.stream_ptr())
+            saved.append((sv, drop))
+        h = arena.h(len(self.layers))
         dhp, loss = self._head(h, packed, denom, stats) if n else (None, None)
         if loss is None:
             loss = torch.zeros((), device=self.device)
-        return loss, saved, dhp
+        return loss, (arena, saved), dhp
 
-    def _layer_fwd(self, spec, h, packed, drop, cos, sin):
-        n, H, D, HQ, HKV, I = packed.n, spec.H, spec.D, spec.HQ, spec.HKV, spec.I
-        dt, dev = self.dtype, self.device
-        Aq, Bq, Av, Bv = self.lora_views[4 * spec.index:4 * spec.index + 4]
-        # input RMSNorm + dropped LoRA inputs + LoRA-A products
-        _, a, yq, yv, rstd1, xq, xv = ops.rms_fwd(h, spec.ln1, spec.eps, dtype=dt, drop=drop,
-                                                  Aq=Aq, Av=Av, want_yq=True)
-        w = spec.qkv.dequant(torch.empty((spec.C, H), device=dev, dtype=dt))
-        qkv = ops.gemm(a, w, bias=spec.bias_qkv)
-        del a, w
-        q, k, v = ops.rope_fwd(qkv, cos, sin, packed.pos, HQ, HKV, D, spec.lora_scale, xq=xq,
-                               xv=xv, Bq=Bq, Bv=Bv)
-        del qkv
-        out, lse = ops.attn_fwd(q, k, v, packed.cu_seqlens, packed.max_len, spec.scale)
-        w = spec.o.dequant(torch.empty((H, HQ * D), device=dev, dtype=dt))
-        h2 = ops.gemm(out.view(n, HQ * D), w, out_dtype=torch.float32, residual=h)
-        del w
-        _, b, _, _, rstd2, _, _ = ops.rms_fwd(h2, spec.ln2, spec.eps, dtype=dt)
-        w = spec.gu.dequant(torch.empty((2 * I, H), device=dev, dtype=dt))
-        gu = ops.gemm(b, w)
-        del b, w
-        m = ops.glu_fwd(gu, I)
-        w = spec.down.dequant(torch.empty((H, I), device=dev, dtype=dt))
-        h3 = ops.gemm(m, w, out_dtype=torch.float32, residual=h2)
-        del m, w
-        return h3, (h, rstd1, yq, yv, xq, xv, q, k, v, out, lse, h2, rstd2, gu, drop)
+    def _set_step(self, desc, packed, drop, cos, sin):
+        """The step-dependent fields of a layer's descriptor."""
+        desc.cos, desc.sin = cos.data_ptr(), sin.data_ptr()
+        desc.pos, desc.cu_seqlens = packed.pos.data_ptr(), packed.cu_seqlens.data_ptr()
+        desc.tok = packed.tok.data_ptr()
+        desc.n, desc.B, desc.max_len = packed.n, packed.rows, packed.max_len
+        f = drop.fields()
+        desc.seed, desc.ctr_q, desc.ctr_v, desc.threads = (f["seed"], f["ctr_q"], f["ctr_v"],
+                                                           f["threads"])
+        desc.p_keep, desc.keep_scale, desc.vec = f["p_keep"], f["keep_scale"], f["vec"]
+        desc.drop_q, desc.drop_v = f["drop_q"], f["drop_v"]
 
     def _head(self, h, packed, denom, stats):
         """Final norm, lm_head, cross-entropy and the logged metrics over chunks of rows taken
@@ -493,6 +522,7 @@ class FusedQwen2:
     def _backward(self, packed, saved, dhp, grad):
         n = packed.n
         H = self.layers[0].H
+        arena, per_layer = saved
         grads = torch.zeros(self.lora_total, device=self.device, dtype=torch.float32)
         views = [grads[self.offsets[i]:self.offsets[i + 1]].view(t.shape)
                  for i, t in enumerate(self.lora_fp32)]
@@ -503,67 +533,67 @@ class FusedQwen2:
             reducer = GradReducer(self.process_group)
         if n:
             cos, sin = self.rope.table(max(packed.max_len, 1))
-            dh = torch.empty((n, H), device=self.device, dtype=torch.float32)
-            dh16 = torch.empty((n, H), device=self.device, dtype=self.dtype)
+            dh = [torch.empty((n, H), device=self.device, dtype=torch.float32) for _ in range(2)]
+            dh16 = [torch.empty((n, H), device=self.device, dtype=self.dtype) for _ in range(2)]
             g = grad.detach().float().reshape(1).contiguous()
-            ops.scatter_rows(dhp, packed.head_order, dh, scale=g, out16=dh16)
+            ops.scatter_rows(dhp, packed.head_order, dh[0], scale=g, out16=dh16[0])
+            cur = 0
             for spec in reversed(self.layers):
-                sv = saved[spec.index]
-                saved[spec.index] = None
-                dh, dh16 = self._layer_bwd(spec, sv, dh, dh16, views[4 * spec.index:4 * spec.index + 4],
-                                           packed, cos, sin, need_dh=spec.index > 0)
+                i = spec.index
+                desc = self.descs[i]
+                sv, drop = per_layer[i]
+                self._set_step(desc, packed, drop, cos, sin)
+                ws = self._workspace_for(desc)
+                lo = self.offsets[4 * i]
+                nxt = 1 - cur
+                need = i > 0  # the first layer's input is the frozen embedding
+                _lib.call("ql_layer_backward", ctypes.addressof(desc), ctypes.addressof(sv),
+                          dh[cur].data_ptr(), dh16[cur].data_ptr(), grads[lo:].data_ptr(),
+                          dh[nxt].data_ptr() if need else None,
+                          dh16[nxt].data_ptr() if need else None, ws.data_ptr(), ws.numel(),
+                          ops.stream_ptr())
                 if reducer is not None:
-                    lo, hi = self.offsets[4 * spec.index], self.offsets[4 * spec.index + 4]
-                    reducer.launch(grads[lo:hi])
+                    reducer.launch(grads[lo:self.offsets[4 * i + 4]])
+                cur = nxt
         elif reducer is not None:
             reducer.launch(grads)
         if reducer is not None:
             reducer.finish(grads)
         return views
 
-    def _layer_bwd(self, spec, sv, dh3, dh3_16, grads, packed, cos, sin, need_dh):
-        h, rstd1, yq, yv, xq, xv, q, k, v, out, lse, h2, rstd2, gu, drop = sv
-        n, H, D, HQ, HKV, I = packed.n, spec.H, spec.D, spec.HQ, spec.HKV, spec.I
-        dt, dev = self.dtype, self.device
-        Aq, Bq, Av, Bv = self.lora_views[4 * spec.index:4 * spec.index + 4]
-        gAq, gBq, gAv, gBv = grads
-        s = spec.lora_scale
-        # MLP
-        wt = spec.down.dequant(torch.empty((I, H), device=dev, dtype=dt), transpose=True)
-        dm = ops.gemm(dh3_16, wt)
-        del wt
-        ops.glu_bwd(dm, gu, I)
-        del dm
-        wt = spec.gu.dequant(torch.empty((H, 2 * I), device=dev, dtype=dt), transpose=True)
-        db = ops.gemm(gu, wt)
-        del wt, gu
-        dh2_16 = torch.empty((n, H), device=dev, dtype=dt)
-        dh2 = ops.rms_bwd(db, h2, rstd2, spec.ln2, dtype=dt, dres=dh3, out16=dh2_16)
-        del db
-        # attention
-        wt = spec.o.dequant(torch.empty((HQ * D, H), device=dev, dtype=dt), transpose=True)
-        dout = ops.gemm(dh2_16, wt).view(n, HQ, D)
-        del wt
-        dq, dk, dv = ops.attn_bwd(dout, q, k, v, out, lse, packed.cu_seqlens, packed.max_len,
-                                  spec.scale)
-        del dout
-        dqkv, dxq, dxv = ops.rope_bwd(dq, dk, dv, cos, sin, packed.pos, HQ, HKV, D, dtype=dt,
-                                      Bq=Bq, Bv=Bv, lora_scale=s)
-        del dq, dk, dv
-        # LoRA weight gradients: dB = s g^T x_lo, dA = dx_lo^T drop(a)
-        ops.lora_colsum(dqkv[:, :HQ * D], xq, scale=s, out=gBq)
-        ops.lora_colsum(dqkv[:, (HQ + HKV) * D:], xv, scale=s, out=gBv)
-        ops.lora_colsum(yq, dxq, transpose=True, out=gAq)
-        ops.lora_colsum(yv, dxv, transpose=True, out=gAv)
-        if not need_dh:  # the first layer's input is the frozen embedding
-            return None, None
-        wt = spec.qkv.dequant(torch.empty((H, spec.C), device=dev, dtype=dt), transpose=True)
-        da = ops.gemm(dqkv, wt)
-        del wt, dqkv
-        dh16 = torch.empty((n, H), device=dev, dtype=dt)
-        dh = ops.rms_bwd(da, h, rstd1, spec.ln1, dtype=dt, dres=dh2, dxlo_q=dxq, dxlo_v=dxv,
-                         Aq=Aq, Av=Av, drop=drop, out16=dh16)
-        return dh, dh16
+
+class _SavedArena:
+    """One device allocation per step for every layer's saved activations (ql_layer_saved) and
+    the residual stream between layers (L + 1 fp32 [n, H] slots)."""
+
+    def __init__(self, n, spec, layers, dtype, device):
+        e = torch.empty((), dtype=dtype).element_size()
+        H, HQ, HKV, D, I = spec.H, spec.HQ, spec.HKV, spec.D, spec.I
+        sizes = [("rstd1", n * 4), ("yq", n * H * e), ("yv", n * H * e), ("xq", n * 16 * e),
+                 ("xv", n * 16 * e), ("q", n * HQ * D * e), ("k", n * HKV * D * e),
+                 ("v", n * HKV * D * e), ("out", n * HQ * D * e), ("lse", HQ * n * 4),
+                 ("h2", n * H * 4), ("rstd2", n * 4), ("gu", n * 2 * I * e)]
+        self.fields, off = {}, 0
+        for name, b in sizes:
+            self.fields[name] = off
+            off = (off + b + 255) // 256 * 256
+        self.layer_bytes = off
+        self.h_bytes = (n * H * 4 + 255) // 256 * 256
+        self.layers, self.n, self.H = layers, n, H
+        total = layers * self.layer_bytes + (layers + 1) * self.h_bytes
+        self.buf = torch.empty(max(total, 256), device=device, dtype=torch.uint8)
+        self.base = self.buf.data_ptr()
+
+    def h(self, i):
+        """Residual stream slot i: the input of layer i (slot L: the head's input)."""
+        start = self.layers * self.layer_bytes + i * self.h_bytes
+        return self.buf[start:start + self.n * self.H * 4].view(torch.float32).view(self.n, self.H)
+
+    def saved(self, i):
+        b = self.base + i * self.layer_bytes
+        fields = {k: b + off for k, off in self.fields.items()}
+        fields["h"] = self.h(i).data_ptr()
+        return _lib.struct("ql_layer_saved", **fields)
 
 
 class _FusedStep(torch.autograd.Function):

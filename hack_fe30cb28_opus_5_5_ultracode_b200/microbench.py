@@ -68,7 +68,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=1090)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", default=None)
+    ap.add_argument("--only", default=None,
+                    help="gemm | gemm:<qkv|o|gate_up|down|lm_head> | dequant | attn | glu | rms | ce")
     args = ap.parse_args()
     dev = torch.device("cuda")
     cfg = QWEN25_1P5B
@@ -76,13 +77,18 @@ def main():
     HQ, HKV, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     dt = torch.float16
     g = torch.Generator(device=dev).manual_seed(0)
-    want = (lambda k: args.only is None or args.only == k)
+    only = args.only.split(":")[0] if args.only else None
+    shape_only = args.only.split(":")[1] if args.only and ":" in args.only else None
+    want = (lambda k: only is None or only == k)
+    want_shape = (lambda name: shape_only is None or shape_only == name)
     copies = 4  # rotate inputs so consecutive launches do not hit L2
 
     if want("gemm") or want("dequant"):
         shapes = {"qkv": ((HQ + 2 * HKV) * D, H), "o": (H, HQ * D), "gate_up": (2 * I, H),
                   "down": (H, I)}
         for name, (N, K) in shapes.items():
+            if not want_shape(name):
+                continue
             ws = [_W(quantize_nf4(torch.randn(N, K, device=dev, generator=g) * 0.02))
                   for _ in range(2)]
             if want("dequant"):
@@ -107,7 +113,7 @@ def main():
                 sec = _time(lambda i: ops.gemm(at[i % copies], bt[i % 2], out=ct[i % copies]),
                             args.iters)
                 _report("gemm_tn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
-    if want("gemm"):
+    if want("gemm") and want_shape("lm_head"):
         hn = torch.randn(n, H, device=dev, generator=g).to(dt)
         W = torch.randn(V, H, device=dev, generator=g).to(dt) * 0.02
         logits = torch.empty(n, V, device=dev, dtype=dt)

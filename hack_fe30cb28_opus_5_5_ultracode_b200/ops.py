@@ -55,18 +55,6 @@ def nf4_dequant(w, out=None, transpose=False, dtype=torch.float16):
 # ---------------------------------------------------------------------------------------------
 # GEMM
 # ---------------------------------------------------------------------------------------------
-_GEMM_EVENTS = None  # while measuring: [(start event, end event, flops)] of every GEMM launch
-
-
-def record_gemms(on=True):
-    """Start (or stop, returning the records) timing every GEMM launch with CUDA events on the
-    launching stream; bench.py uses it for the dominant kernel's live roofline."""
-    global _GEMM_EVENTS
-    out = _GEMM_EVENTS
-    _GEMM_EVENTS = [] if on else None
-    return out
-
-
 def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=None):
     """out[M, N] (+)= a[M, K] @ b[N, K]^T (+ bias) on tcgen05. a and b: fp16 or bf16 with unit
     column stride; out: fp16 / bf16 / fp32 with unit column stride."""
@@ -85,18 +73,34 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
         raise ValueError("bias must have the input dtype")
     if residual is not None and (residual.stride(0) != out.stride(0) or residual.stride(1) != 1):
         raise ValueError("residual must share the output's row stride")
-    ev = _GEMM_EVENTS
-    if ev is not None:
-        start = torch.cuda.Event(enable_timing=True)
-        start.record()
     call("ql_gemm_tn", _ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out), out.stride(0),
          _ptr(bias), M, N, K, dtype_code(a.dtype), dtype_code(out.dtype), int(accumulate),
          _ptr(residual), stream_ptr())
-    if ev is not None:
-        end = torch.cuda.Event(enable_timing=True)
-        end.record()
-        ev.append((start, end, 2.0 * M * N * K))
     return out
+
+
+PROFILE_KINDS = ("gemm", "dequant", "rms_fwd", "rms_bwd", "rope_fwd", "rope_bwd", "attn_fwd",
+                 "attn_bwd", "glu_fwd", "glu_bwd", "lora_colsum", "ce", "other")
+
+
+def profile_start(capacity=200000):
+    """Time every library operation with CUDA events (see ql_profile_start)."""
+    call("ql_profile_start", int(capacity))
+
+
+def profile_stop():
+    call("ql_profile_stop")
+
+
+def profile_read():
+    """{kind: {"count", "ms", "flops", "bytes"}} of the operations recorded since profile_start."""
+    import ctypes
+
+    n = len(PROFILE_KINDS)
+    arrs = [(ctypes.c_double * n)() for _ in range(4)]
+    call("ql_profile_read", *[ctypes.addressof(a) for a in arrs])
+    return {k: {"count": arrs[0][i], "ms": arrs[1][i], "flops": arrs[2][i], "bytes": arrs[3][i]}
+            for i, k in enumerate(PROFILE_KINDS) if arrs[0][i]}
 
 
 def launch_count():

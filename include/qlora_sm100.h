@@ -41,6 +41,14 @@ int ql_device_status(int* status_out, int clear);
 int* ql_device_status_ptr(void);
 /* Kernels launched through this library since it was loaded (all host threads). */
 long long ql_launch_count(void);
+/* Optional operation profiler: while started, every operation records a CUDA event before and
+ * after its launches (a pool of 2 x capacity events); ql_profile_read synchronises on them and
+ * returns per kind (gemm, dequant, rms_fwd, rms_bwd, rope_fwd, rope_bwd, attn_fwd, attn_bwd,
+ * glu_fwd, glu_bwd, lora_colsum, ce, other: 13 entries per array) the operation count,
+ * milliseconds, algorithmic FLOPs and bytes. */
+int ql_profile_start(int capacity);
+int ql_profile_stop(void);
+int ql_profile_read(double* count, double* ms, double* flops, double* bytes);
 
 /* ---- NF4 dequantisation ------------------------------------------------------------------
  * Replaces NF4Weight.dequant_into / NF4Group.dequant_into (solution/engine.py:103-109,
@@ -293,6 +301,72 @@ int ql_gather_rows(const float* src, const int64_t* idx, float* dst, int64_t n, 
                    cudaStream_t stream);
 int ql_scatter_rows(const float* src, const int64_t* idx, const float* scale, float* dst,
                     void* dst16, int64_t n, int H, int dtype, cudaStream_t stream);
+
+/* ---- one decoder layer, forward and backward ----------------------------------------------
+ * Replaces _Layer.forward / _Layer.backward (solution/engine.py:1184-1340) with keep-everything
+ * semantics: the forward writes every intermediate the backward reads into caller-owned
+ * buffers (ql_layer_saved), the backward reads them and recomputes nothing. Both launch the
+ * kernels above in the reference's order on one stream; temporaries live in a caller-owned
+ * workspace of ql_layer_workspace_bytes() bytes. */
+typedef struct {
+  const uint8_t* packed;   /* NF4 bytes of the group's weights back to back */
+  const void* absmax;      /* fp32 [blocks] or (nested) uint8 [blocks] */
+  const float* code;       /* [16] */
+  const float* code2;      /* nested: [256] */
+  const float* absmax2;    /* nested: [ceil(blocks / bs2)] over the whole group */
+  const float* offsets;    /* nested: [members] */
+  int64_t rows, cols, seg1, seg2;
+  int32_t nested, bs2;
+} ql_nf4_weight;
+
+typedef struct {
+  ql_nf4_weight qkv, o, gu, down;   /* [C, H], [H, HQ D], [2 I, H] (gate rows, then up), [H, I] */
+  const void* bias_qkv;             /* [C] */
+  const float* ln1;                 /* [H] */
+  const float* ln2;
+  const void* Aq;                   /* LoRA in the 16-bit type: A [rank, H], B [out, rank] */
+  const void* Bq;
+  const void* Av;
+  const void* Bv;
+  const float* cos;                 /* [positions, D/2] */
+  const float* sin;
+  const int32_t* pos;               /* [n] */
+  const int32_t* cu_seqlens;        /* [B + 1] */
+  const int64_t* tok;               /* [n] padded-batch index of each token (dropout) */
+  int64_t seed, ctr_q, ctr_v, threads;
+  float p_keep, keep_scale, eps, scale, lora_scale;
+  int32_t vec, drop_q, drop_v;
+  int32_t n, B, max_len, H, HQ, HKV, D, I, rank, dtype;
+} ql_layer_desc;
+
+typedef struct {              /* what the forward keeps for the backward (all [n, ...]) */
+  const float* h;             /* [n, H] fp32 layer input */
+  float* rstd1;               /* [n] */
+  void* yq;                   /* [n, H] dropped LoRA inputs */
+  void* yv;
+  void* xq;                   /* [n, rank] LoRA-A outputs */
+  void* xv;
+  void* q;                    /* [n, HQ, D] */
+  void* k;                    /* [n, HKV, D] */
+  void* v;
+  void* out;                  /* [n, HQ, D] attention output */
+  float* lse;                 /* [HQ, n] */
+  float* h2;                  /* [n, H] residual after attention */
+  float* rstd2;               /* [n] */
+  void* gu;                   /* [n, 2 I] [gate | up] (overwritten by its gradient in backward) */
+} ql_layer_saved;
+
+/* Workspace bytes of the forward (backward = 0) or backward (backward = 1) of a layer. */
+int64_t ql_layer_workspace_bytes(const ql_layer_desc* layer, int backward);
+/* h_out [n, H] fp32: the layer's output (the next layer's input). */
+int ql_layer_forward(const ql_layer_desc* layer, const ql_layer_saved* saved, float* h_out,
+                     void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+/* dh3 / dh3_16: gradient of the layer's output (fp32 and 16-bit). Writes the LoRA gradients
+ * into grads = [dAq (rank x H) | dBq (HQ D x rank) | dAv (rank x H) | dBv (HKV D x rank)] fp32,
+ * and, when dh_out is not NULL, the gradient of the layer's input (dh_out fp32, dh16_out 16-bit). */
+int ql_layer_backward(const ql_layer_desc* layer, const ql_layer_saved* saved, const float* dh3,
+                      const void* dh3_16, float* grads, float* dh_out, void* dh16_out,
+                      void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 }
