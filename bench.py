@@ -213,9 +213,13 @@ def run_ours(args, rank, world, local):
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
 
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import HostBatch
+
+    hosts = [HostBatch.of(torch.from_numpy(b[1]), torch.from_numpy(b[2])) for b in host]
+
     def train_step(i):
         ids, mask, labels, _ = dev_batches[i]
-        loss, _, _ = engine.step(ids, mask, labels, denoms[i])
+        loss, _, _ = engine.step(ids, mask, labels, denoms[i], hosts[i])
         loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
@@ -248,17 +252,24 @@ def run_ours(args, rank, world, local):
     clocks.start()
     time.sleep(0.3)
     launches0 = ops.launch_count()
-    ops.profile_start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("bench_timed")  # (lets ncu --nvtx-include capture these steps)
     e0.record()
     for i in range(args.warmup, args.warmup + args.steps):
         train_step(i)
     e1.record()
+    torch.cuda.nvtx.range_pop()
+    barrier_sync()
+    launches = ops.launch_count() - launches0
+    clk = clocks.stop()
+    # Per-operation breakdown and the GEMM roofline: the same K steps again with the library's
+    # CUDA-event profiler on (kept out of the timed region: its event pairs cost host time).
+    ops.profile_start()
+    for i in range(args.warmup, args.warmup + args.steps):
+        train_step(i)
     barrier_sync()
     ops.profile_stop()
     prof = ops.profile_read()
-    launches = ops.launch_count() - launches0
-    clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
     tokens = sum_over_ranks(sum(b[3] for b in host[args.warmup:]))
     value = tokens / (ms / 1000.0)
@@ -279,11 +290,11 @@ def run_ours(args, rank, world, local):
     trainer._soup_original_compute_loss = trainer.compute_loss
     setattr(trainer, patch._INSTALLED_ATTR, engine)
     pinned = [tuple(torch.from_numpy(a).pin_memory() for a in b[:3]) for b in host]
-    h2d = sum(a.numel() * a.element_size() for a in pinned[0])
 
     def e2e_step(i):
-        ids, mask, labels = (a.to(dev, non_blocking=True) for a in pinned[i])
-        inputs = {"input_ids": ids, "attention_mask": mask, "labels": labels}
+        ids, mask, labels = pinned[i]
+        inputs = patch.prepare_inputs(trainer, {"input_ids": ids, "attention_mask": mask,
+                                                "labels": labels}, dev)
         loss = patch.fused_compute_loss(trainer, model, inputs,
                                         num_items_in_batch=denoms[i])
         loss.backward()
@@ -332,10 +343,9 @@ def run_ours(args, rank, world, local):
                      "bound": "tensor", "achieved": achieved, "peak": tf_sust,
                      "unit": "TFLOP/s", "frac": (achieved / tf_sust) if achieved else None,
                      "peak_source": f"{src} bf16 dense, sustained (kernel inside a long step)",
-                     "traffic": traffic, "gemm_share_of_step": gemm_ms / ms if ms else None,
+                     "traffic": traffic, "gemm_ms_per_step": gemm_ms / args.steps,
                      "launches": int(prof.get("gemm", {}).get("count", 0))},
         "op_ms_per_step": kernel_ms,
-        "op_busy_share": sum(v["ms"] for v in prof.values()) / ms if ms else None,
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:

@@ -302,9 +302,14 @@ static int rms_grid(int64_t n) {
   return (int)(want < cap ? want : cap);
 }
 
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel.
 template <typename K>
 static void set_smem(K kern, int bytes) {
-  if (bytes > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  static int done = 0;  // one flag per kernel instantiation
+  if (bytes > 48 * 1024 && bytes > done) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done = bytes;
+  }
 }
 
 int rms_fwd(const RmsFwdC& c, cudaStream_t s) {

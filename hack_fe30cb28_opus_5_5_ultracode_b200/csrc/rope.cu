@@ -200,9 +200,14 @@ static int rope_grid(int64_t n) {
   return (int)(want < cap ? want : cap);
 }
 
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel.
 template <typename K>
 static void rope_smem_attr(K kern, int bytes) {
-  if (bytes > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  static int done = 0;  // one flag per kernel instantiation
+  if (bytes > 48 * 1024 && bytes > done) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done = bytes;
+  }
 }
 
 int rope_fwd(const RopeFwdC& a, cudaStream_t s) {

@@ -185,39 +185,79 @@ class UnsupportedBatch(ValueError):
 # ---------------------------------------------------------------------------------------------
 # per-step packing (solution/engine.py:705-764)
 # ---------------------------------------------------------------------------------------------
-class Packed:
-    """One micro-batch without its padding: the real tokens of every row back to back."""
+class HostBatch:
+    """What the step needs to know about a batch on the host: each row's length and the number
+    of tokens with a target. Computed from the batch while it is still in host memory
+    (patch.prepare_inputs), it spares the step the device reads that would otherwise stall the
+    host until the previous step's GPU work is done (the reference reads both back,
+    solution/engine.py:714, 732)."""
 
-    def __init__(self, input_ids, attention_mask, labels):
+    def __init__(self, lengths, n_supervised):
+        self.lengths = [int(x) for x in lengths]
+        self.n_supervised = int(n_supervised)
+
+    @classmethod
+    def of(cls, attention_mask, labels):
+        """From host (CPU) tensors of a right-padded batch; None if it is not right-padded."""
+        mask = attention_mask.to("cpu").bool()
+        T = mask.shape[1]
+        lengths = mask.sum(dim=1)
+        if not torch.equal(mask, torch.arange(T)[None, :] < lengths[:, None]):
+            return None
+        lab = labels.to("cpu")
+        cols = torch.arange(T - 1)[None, :]
+        sup = (lab[:, 1:] != -100) & (cols < (lengths[:, None] - 1))
+        return cls(lengths.tolist(), int(sup.sum()))
+
+
+class Packed:
+    """One micro-batch without its padding: the real tokens of every row back to back
+    (solution/engine.py:705-764)."""
+
+    def __init__(self, input_ids, attention_mask, labels, host=None):
+        """host: a HostBatch of this batch (then nothing is read back from the device); without
+        it the lengths and the supervised count are read back from the device - a host sync, as
+        in solution/engine.py:714 - and the right padding is checked there."""
         if input_ids.dim() != 2 or attention_mask.shape != input_ids.shape \
                 or labels.shape != input_ids.shape:
             raise UnsupportedBatch("inputs are not [rows, tokens]")
         B, T = input_ids.shape
         dev = input_ids.device
-        lengths = attention_mask.sum(dim=1)
-        lengths_cpu = lengths.tolist()
-        expected = torch.arange(T, device=dev)[None, :] < lengths[:, None]
-        if not bool(torch.equal(attention_mask.bool(), expected)):
-            raise UnsupportedBatch("attention_mask is not right-padded")
-        flat = expected.reshape(-1).nonzero().squeeze(1)
-        self.n = int(flat.numel())
-        self.tok = flat
+        if host is None:
+            lengths = attention_mask.sum(dim=1)
+            expected = torch.arange(T, device=dev)[None, :] < lengths[:, None]
+            if not bool(torch.equal(attention_mask.bool(), expected)):
+                raise UnsupportedBatch("attention_mask is not right-padded")
+            lengths_cpu = [int(x) for x in lengths.tolist()]
+        else:
+            lengths_cpu = list(host.lengths)
+            if len(lengths_cpu) != B or any(not 0 <= x <= T for x in lengths_cpu):
+                raise UnsupportedBatch("host lengths do not match the batch")
         self.T, self.rows = T, B
-        self.lengths = [int(x) for x in lengths_cpu]
-        self.max_len = max(self.lengths) if self.lengths else 0
-        self.ids = input_ids.reshape(-1)[flat].contiguous()
-        self.pos = (flat % T).to(torch.int32)
+        self.lengths = lengths_cpu
+        self.n = sum(lengths_cpu)
+        self.max_len = max(lengths_cpu) if lengths_cpu else 0
+        # index tensors built on the host from the lengths, copied once
+        flat = torch.cat([torch.arange(r * T, r * T + ln) for r, ln in enumerate(lengths_cpu)]) \
+            if B else torch.zeros(0, dtype=torch.int64)
+        cu = torch.zeros(B + 1, dtype=torch.int32)
+        cu[1:] = torch.tensor(lengths_cpu, dtype=torch.int32).cumsum(0) if B else cu[1:]
+        rows = torch.repeat_interleave(torch.arange(B), torch.tensor(lengths_cpu, dtype=torch.int64))
+        staged = torch.cat([flat, (flat % T), rows, cu.to(torch.int64)])
+        if dev.type == "cuda":
+            staged = staged.pin_memory().to(dev, non_blocking=True)
+        n = self.n
+        self.tok = staged[:n]                       # padded-batch index of each token (int64)
+        self.pos = staged[n:2 * n].to(torch.int32)
+        self.row_of_token = staged[2 * n:3 * n]
+        self.cu_seqlens = staged[3 * n:].to(torch.int32)
+        self.ids = input_ids.reshape(-1).index_select(0, self.tok)
         shifted = torch.full_like(labels, -100)
         shifted[:, :-1] = labels[:, 1:]
-        self.targets = shifted.reshape(-1)[flat].contiguous()
+        self.targets = shifted.reshape(-1).index_select(0, self.tok)
         supervised = self.targets >= 0
         self.head_order = torch.argsort((~supervised).to(torch.int8), stable=True)
-        self.n_supervised = int(supervised.sum())
-        cu = [0]
-        for length in self.lengths:
-            cu.append(cu[-1] + length)
-        self.cu_seqlens = torch.tensor(cu, device=dev, dtype=torch.int32)
-        self.row_of_token = torch.repeat_interleave(torch.arange(B, device=dev), lengths)
+        self.n_supervised = host.n_supervised if host is not None else int(supervised.sum())
 
 
 class RopeTable:
@@ -383,6 +423,8 @@ class FusedQwen2:
                                      "two members of a group are not supported")
         self.descs = [self._layer_desc(spec) for spec in self.layers]
         self._workspace = None
+        self._arena_buf = None     # grow-only device memory of the saved activations
+        self._arena_busy = False   # a forward's activations await their backward
 
     def _layer_desc(self, spec):
         """The step-independent part of a layer's ql_layer_desc (weights, norms, LoRA, dims)."""
@@ -421,9 +463,10 @@ class FusedQwen2:
             self._logits = torch.empty((rows, self.V), device=self.device, dtype=self.dtype)
         return self._logits[:rows]
 
-    def step(self, input_ids, attention_mask, labels, denom):
-        """One training step's forward: (loss, packed, stats); autograd runs the backward."""
-        packed = Packed(input_ids, attention_mask, labels)
+    def step(self, input_ids, attention_mask, labels, denom, host=None):
+        """One training step's forward: (loss, packed, stats); autograd runs the backward.
+        host: an optional HostBatch of this batch (see HostBatch)."""
+        packed = Packed(input_ids, attention_mask, labels, host)
         spec = self.layers[0]
         if self.dropout is not None and self.dropout.ok is None:
             self.dropout.ok = self.dropout.check(
@@ -452,7 +495,12 @@ class FusedQwen2:
         n = packed.n
         spec0 = self.layers[0]
         cos, sin = self.rope.table(max(packed.max_len, 1))
-        arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device)
+        arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device,
+                            None if self._arena_busy else self._arena_buf)
+        if not self._arena_busy:
+            self._arena_buf = arena.buf
+            self._arena_busy = True
+            arena.owned = True
         h = arena.h(0)
         if n:
             ops.embed(packed.ids, self.embed, out=h)
@@ -523,6 +571,8 @@ class FusedQwen2:
         n = packed.n
         H = self.layers[0].H
         arena, per_layer = saved
+        if arena.owned:  # the next forward may reuse the arena (queued after this backward)
+            self._arena_busy = False
         grads = torch.zeros(self.lora_total, device=self.device, dtype=torch.float32)
         views = [grads[self.offsets[i]:self.offsets[i + 1]].view(t.shape)
                  for i, t in enumerate(self.lora_fp32)]
@@ -566,7 +616,8 @@ class _SavedArena:
     """One device allocation per step for every layer's saved activations (ql_layer_saved) and
     the residual stream between layers (L + 1 fp32 [n, H] slots)."""
 
-    def __init__(self, n, spec, layers, dtype, device):
+    def __init__(self, n, spec, layers, dtype, device, reuse=None):
+        self.owned = False
         e = torch.empty((), dtype=dtype).element_size()
         H, HQ, HKV, D, I = spec.H, spec.HQ, spec.HKV, spec.D, spec.I
         sizes = [("rstd1", n * 4), ("yq", n * H * e), ("yv", n * H * e), ("xq", n * 16 * e),
@@ -580,8 +631,12 @@ class _SavedArena:
         self.layer_bytes = off
         self.h_bytes = (n * H * 4 + 255) // 256 * 256
         self.layers, self.n, self.H = layers, n, H
-        total = layers * self.layer_bytes + (layers + 1) * self.h_bytes
-        self.buf = torch.empty(max(total, 256), device=device, dtype=torch.uint8)
+        total = max(layers * self.layer_bytes + (layers + 1) * self.h_bytes, 256)
+        if reuse is not None and reuse.numel() >= total:
+            self.buf = reuse
+        else:  # grow by a quarter beyond the need, so slightly longer steps still fit
+            self.buf = torch.empty(total + total // 4 if reuse is not None else total,
+                                   device=device, dtype=torch.uint8)
         self.base = self.buf.data_ptr()
 
     def h(self, i):

@@ -101,8 +101,13 @@ def fused_compute_loss(self, model, inputs, return_outputs=False, num_items_in_b
     denom = float(denom.item() if torch.is_tensor(denom) else denom)
     from .engine import UnsupportedBatch
 
+    host = getattr(self, "_qlora_host_batch", None)
+    self._qlora_host_batch = None
+    if host is not None and (host[0] is not input_ids):
+        host = None  # stale: prepared for other inputs
     try:
-        loss, packed, stats = engine.step(input_ids, attention_mask, labels, denom)
+        loss, packed, stats = engine.step(input_ids, attention_mask, labels, denom,
+                                          host[1] if host is not None else None)
     except UnsupportedBatch:  # raised before the step changed anything
         inputs.update(popped)
         return original(model, inputs, return_outputs=return_outputs,
@@ -133,6 +138,32 @@ def fused_compute_loss(self, model, inputs, return_outputs=False, num_items_in_b
         except ImportError:
             return loss, types.SimpleNamespace(loss=loss, logits=None)
     return loss
+
+
+def prepare_inputs(trainer, inputs, device):
+    """Move a host batch to the GPU as HF Trainer._prepare_inputs does (pinned, non-blocking)
+    and keep its HostBatch (lengths, supervised count) for the next fused_compute_loss, which
+    then reads nothing back from the device. install() routes the trainer's own
+    _prepare_inputs through this."""
+    from .engine import HostBatch
+
+    host = None
+    if isinstance(inputs, dict) and "attention_mask" in inputs and "labels" in inputs \
+            and not inputs["attention_mask"].is_cuda and not inputs["labels"].is_cuda:
+        host = HostBatch.of(inputs["attention_mask"], inputs["labels"])
+    device = torch.device(device)
+
+    def move(v):
+        if not torch.is_tensor(v) or v.device == device:
+            return v
+        if device.type == "cuda":
+            return v.pin_memory().to(device, non_blocking=True)
+        return v.to(device)
+
+    moved = {k: move(v) for k, v in inputs.items()}
+    if host is not None and "input_ids" in moved:
+        trainer._qlora_host_batch = (moved["input_ids"], host)
+    return moved
 
 
 def _flush_metrics(trainer):
@@ -204,6 +235,23 @@ def install(trainer, dtype=None):
     trainer._soup_original_compute_loss = trainer.compute_loss
     setattr(trainer, _INSTALLED_ATTR, engine)
     trainer.compute_loss = types.MethodType(fused_compute_loss, trainer)
+    original_prepare = getattr(trainer, "_prepare_inputs", None)
+    if original_prepare is not None:
+        def _prepare_inputs(inputs):
+            # keep the batch's host-side facts before HF moves it (no device read-backs later)
+            from .engine import HostBatch
+
+            host = None
+            if isinstance(inputs, dict) and "attention_mask" in inputs and "labels" in inputs \
+                    and torch.is_tensor(inputs["attention_mask"]) \
+                    and not inputs["attention_mask"].is_cuda and not inputs["labels"].is_cuda:
+                host = HostBatch.of(inputs["attention_mask"], inputs["labels"])
+            moved = original_prepare(inputs)
+            if host is not None and isinstance(moved, dict) and "input_ids" in moved:
+                trainer._qlora_host_batch = (moved["input_ids"], host)
+            return moved
+
+        trainer._prepare_inputs = _prepare_inputs
     if hasattr(trainer, "add_callback"):
         trainer.add_callback(_FlushMetrics(trainer))
     _log(f"fused Qwen2 step installed ({len(engine.layers)} layers, {dtype}, LoRA dropout "

@@ -101,9 +101,9 @@ class _FakeEngine:
     def __init__(self, fail=False):
         self.calls, self.fail = [], fail
 
-    def step(self, input_ids, attention_mask, labels, denom):
+    def step(self, input_ids, attention_mask, labels, denom, host=None):
         self.calls.append(denom)
-        packed = Packed(input_ids, attention_mask, labels)  # raises UnsupportedBatch itself
+        packed = Packed(input_ids, attention_mask, labels, host)  # raises UnsupportedBatch itself
         if self.fail:
             raise UnsupportedBatch("dropout masks differ")
         n = packed.n
@@ -212,3 +212,24 @@ def test_install_refuses_unsupported_models():
     t = types.SimpleNamespace(model=_Model(), compute_loss=lambda *a, **k: None)
     assert patch.install(t) is False
     assert not hasattr(t, patch._INSTALLED_ATTR) or getattr(t, patch._INSTALLED_ATTR) is None
+
+
+def test_host_batch_matches_the_device_reads():
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import HostBatch
+
+    b = _batch([5, 3, 7])
+    host = HostBatch.of(b["attention_mask"], b["labels"])
+    a = Packed(b["input_ids"], b["attention_mask"], b["labels"])
+    p = Packed(b["input_ids"], b["attention_mask"], b["labels"], host)
+    assert host.lengths == [5, 3, 7] and host.n_supervised == a.n_supervised == p.n_supervised
+    for name in ("tok", "pos", "cu_seqlens", "ids", "targets", "head_order", "row_of_token"):
+        assert torch.equal(getattr(a, name), getattr(p, name)), name
+    assert HostBatch.of(_batch([5, 3], left=True)["attention_mask"], b["labels"][:2, :5]) is None
+
+
+def test_prepare_inputs_keeps_the_host_facts():
+    t, _ = _trainer(_FakeEngine())
+    b = _batch([5, 3, 7])
+    moved = patch.prepare_inputs(t, dict(b), torch.device("cpu"))
+    assert t._qlora_host_batch[0] is moved["input_ids"]
+    assert t._qlora_host_batch[1].lengths == [5, 3, 7]
