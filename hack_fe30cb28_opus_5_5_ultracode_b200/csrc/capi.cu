@@ -2,6 +2,8 @@
 // checks, the per-thread error message, the device status word, and dispatch to the kernels.
 #include <atomic>
 #include <cstdio>
+#include <mutex>
+#include <unordered_map>
 #include <cstring>
 #include <string>
 
@@ -37,6 +39,17 @@ int launched(int kernels) {
   if (cudaPeekAtLastError() != cudaSuccess) return QL_STATUS_CUDA;
   g_launches.fetch_add(kernels, std::memory_order_relaxed);
   return QL_STATUS_OK;
+}
+
+void smem_optin(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done;  // per kernel: the limit already set
+  std::lock_guard<std::mutex> lk(mu);
+  int& have = done[kernel];
+  if (have >= bytes) return;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+      cudaSuccess)
+    have = bytes;
 }
 
 int* status_word() {

@@ -22,6 +22,8 @@ __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 
 
 // Host: the status of the launch(es) just issued; counts them in the library's launch counter.
 int launched(int kernels);
+// Host: raises a kernel's dynamic shared-memory limit to `bytes` the first time it is needed.
+void smem_optin(const void* kernel, int bytes);
 
 // ---------------------------------------------------------------------------------------------
 // element conversion

@@ -302,14 +302,10 @@ static int rms_grid(int64_t n) {
   return (int)(want < cap ? want : cap);
 }
 
-// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel.
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
 template <typename K>
 static void set_smem(K kern, int bytes) {
-  static int done = 0;  // one flag per kernel instantiation
-  if (bytes > 48 * 1024 && bytes > done) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    done = bytes;
-  }
+  if (bytes > 48 * 1024) smem_optin(reinterpret_cast<const void*>(kern), bytes);
 }
 
 int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
@@ -324,8 +320,9 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   RmsFwdArgs a{c.x, c.delta, c.w, c.xsum, c.y, c.yq, c.yv, c.rstd, c.Aq, c.Av, c.xq, c.xv, c.n,
                c.H, c.eps,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
-                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v}};
+                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}}};
   if (c.vec != 4 && c.vec != 8) return QL_STATUS_BAD_ARG;
+  if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.Aq != nullptr) || (c.drop_v && c.Av != nullptr);
   const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
   const int grid = rms_grid(c.n);
@@ -361,7 +358,8 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   RmsBwdArgs a{c.dy, c.ld_dy, c.x, c.rstd, c.w, c.dres, c.dx, c.dx16, c.tq, c.tv, c.dxlo_q,
                c.dxlo_v, c.Aq, c.Av, c.n, c.H, c.grad_scale,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
-                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v}};
+                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}}};
+  if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.tq == nullptr) || (c.drop_v && c.tv == nullptr);
   const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
   const int grid = rms_grid(c.n);
@@ -398,7 +396,8 @@ int dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t 
                  float p_keep, int vec, cudaStream_t s) {
   if (nelem < 0 || threads <= 0 || (vec != 4 && vec != 8)) return QL_STATUS_BAD_ARG;
   if (nelem == 0) return QL_STATUS_OK;
-  DropoutArgs d{nullptr, seed, ctr, 0, threads, p_keep, 1.f, vec, 1, 0};
+  DropoutArgs d{nullptr, seed, ctr, 0, threads, p_keep, 1.f, vec, 1, 0, FastDiv{}};
+  if (!prepare_dropout(d)) return QL_STATUS_BAD_ARG;
   const int64_t groups = cdiv(nelem, 4);
   dropout_keep_kernel<<<(unsigned)cdiv(groups, 256), 256, 0, s>>>(out, nelem, d);
   return launched(1);

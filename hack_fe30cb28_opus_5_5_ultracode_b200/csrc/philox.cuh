@@ -10,6 +10,27 @@
 
 namespace ql {
 
+// Division of 32-bit unsigned integers by a divisor fixed at launch, by a multiply-high and a
+// shift (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994):
+// for d >= 1, l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (t + ((n - t) >> 1)) >> (l - 1) with t = mulhi(m, n)   (l >= 1; d = 1 is n itself).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{d, 0u, 0u};
+  while (f.l < 32 && (1ull << f.l) < d) ++f.l;
+  f.m = (uint32_t)(((1ull << 32) * ((1ull << f.l) - d)) / d + 1);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  if (f.l == 0) return n;  // d == 1
+  const uint32_t t = __umulhi(f.m, n);
+  return (t + ((n - t) >> 1)) >> (f.l - 1);
+}
+
 struct DropoutArgs {
   const int64_t* tok;  // [n] each packed token's index in the padded [B, T] batch
   int64_t seed;        // the generator's seed, its 64 bits as an int64
@@ -18,7 +39,16 @@ struct DropoutArgs {
   float p_keep, keep_scale;
   int vec;             // 16 / sizeof(LoRA input element): 4 for fp32
   int drop_q, drop_v;  // which masks exist
+  FastDiv div_threads; // division by `threads`, set by the launcher (prepare_dropout)
 };
+
+// Host: completes a DropoutArgs before launch. The element indices of a mask stay below 2^32
+// (B T H < 4.3e9), so the per-element index math runs in 32 bits.
+inline bool prepare_dropout(DropoutArgs& d) {
+  if (d.threads <= 0 || d.threads > 0xFFFFFFFFll) return false;
+  d.div_threads = make_fastdiv((uint32_t)d.threads);
+  return true;
+}
 
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
@@ -46,9 +76,12 @@ __device__ __forceinline__ bool keep_from_u(uint32_t u, float p_keep) {
 // Bit j of the result is element e0 + j.
 __device__ __forceinline__ uint32_t keep4(int64_t e0, int64_t ctr, const DropoutArgs& d) {
   if (d.p_keep >= 1.0f) return 0xFu;  // no dropout: the LoRA input is used as is
-  const int64_t g = e0 / d.vec;
-  const uint32_t thread = (uint32_t)(g % d.threads);
-  const uint64_t c = (uint64_t)(ctr + (g / d.threads) * (d.vec / 4) + (e0 % d.vec) / 4);
+  const uint32_t e = (uint32_t)e0;
+  const uint32_t g = d.vec == 4 ? (e >> 2) : (e >> 3);       // e / VEC
+  const uint32_t it = fdiv(g, d.div_threads);                 // g / threads
+  const uint32_t thread = g - it * (uint32_t)d.threads;       // g % threads
+  const uint64_t c = (uint64_t)ctr + (uint64_t)it * (uint32_t)(d.vec >> 2) +
+                     (((e & (uint32_t)(d.vec - 1))) >> 2);    // + (e % VEC) / 4
   const uint4 r = philox4x32_10(make_uint4((uint32_t)c, (uint32_t)(c >> 32), thread, 0u),
                                 (uint32_t)(uint64_t)d.seed, (uint32_t)((uint64_t)d.seed >> 32));
   return (keep_from_u(r.x, d.p_keep) ? 1u : 0u) | (keep_from_u(r.y, d.p_keep) ? 2u : 0u) |

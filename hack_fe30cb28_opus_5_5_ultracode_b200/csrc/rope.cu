@@ -21,8 +21,49 @@ namespace ql {
 
 constexpr int RANK = 16;
 
-// One warp per token (8 per CTA, tokens strided over the grid); the LoRA-B factors (rows of 16)
-// are staged in shared memory once per CTA.
+// 8 consecutive values of a 16-bit or fp32 row as floats, and back.
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float* v) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = to_f<T>(h[j]);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float* v) {
+  T h[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[j] = from_f<T>(v[j]);
+  *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(h);
+}
+
+// lo[j] = sum_r x[r] B[idx + j][r] for 8 consecutive rows of a [rows, 16] factor in smem,
+// rounded to the 16-bit type (the reference's fp16 GEMM output).
+template <typename T>
+__device__ __forceinline__ void lora_rows8(const T* B, int idx, const float* x, float* lo) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)(idx + j) * RANK);
+    const uint4 u0 = b4[0], u1 = b4[1];
+    const T* b0 = reinterpret_cast<const T*>(&u0);
+    const T* b1 = reinterpret_cast<const T*>(&u1);
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc += x[r] * to_f<T>(b0[r]);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc += x[8 + r] * to_f<T>(b1[r]);
+    lo[j] = to_f<T>(from_f<T>(acc));
+  }
+}
+
+// One warp per token (8 per CTA, tokens strided over the grid). A lane takes chunks of 8
+// consecutive positions d .. d+7 of the first half of a head together with their partners
+// d + D/2 (16-byte loads and stores); the LoRA-B factors sit in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(256) rope_fwd_kernel(RopeFwdC a) {
   extern __shared__ __align__(16) uint8_t rope_smem[];
@@ -40,9 +81,11 @@ __global__ void __launch_bounds__(256) rope_fwd_kernel(RopeFwdC a) {
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float s = a.lora_scale;
+  const int cph = HALF / 8;                 // chunks per head
+  const int rot_chunks = (HQ + HKV) * cph;  // q and k heads
+  const int v_chunks = HKV * D / 8;
   for (int64_t tok = blockIdx.x * 8 + warp; tok < a.n; tok += (int64_t)gridDim.x * 8) {
     const T* row = reinterpret_cast<const T*>(a.qkv) + tok * C;
-    // this token's LoRA-A outputs, broadcast from lanes 0..15 (q) and 16..31 (v)
     float mine = 0.f;
     if (lane < RANK) { if (fq) mine = to_f<T>(reinterpret_cast<const T*>(a.xq)[tok * RANK + lane]); }
     else if (fv) mine = to_f<T>(reinterpret_cast<const T*>(a.xv)[tok * RANK + lane - RANK]);
@@ -52,44 +95,52 @@ __global__ void __launch_bounds__(256) rope_fwd_kernel(RopeFwdC a) {
     const int pos = a.pos[tok];
     const float* cs = a.cos + (int64_t)pos * HALF;
     const float* sn = a.sin + (int64_t)pos * HALF;
-    auto lora_b = [&](const T* B, const float* x, int idx) -> float {  // rounded like a GEMM output
-      const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)idx * RANK);
-      const uint4 u0 = b4[0], u1 = b4[1];
-      const T* b0 = reinterpret_cast<const T*>(&u0);
-      const T* b1 = reinterpret_cast<const T*>(&u1);
-      float acc = 0.f;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) acc += x[r] * to_f<T>(b0[r]);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) acc += x[8 + r] * to_f<T>(b1[r]);
-      return to_f<T>(from_f<T>(acc));
-    };
-    for (int idx = lane; idx < (HQ + HKV) * HALF; idx += 32) {
-      const int hh = idx / HALF, d = idx % HALF;
+#pragma unroll 2
+    for (int ch = lane; ch < rot_chunks; ch += 32) {
+      const int hh = ch / cph, d = (ch % cph) * 8;
       const bool is_q = hh < HQ;
       const int src = hh * D + d;
-      float x1 = to_f<T>(row[src]), x2 = to_f<T>(row[src + HALF]);
-      if (is_q) {
+      float x1[8], x2[8], c[8], sv[8];
+      ld8<T>(row + src, x1);
+      ld8<T>(row + src + HALF, x2);
+      ld8<float>(cs + d, c);
+      ld8<float>(sn + d, sv);
+      if (is_q && (a.lq != nullptr || fq)) {
+        float l1[8], l2[8];
         if (a.lq != nullptr) {
           const T* lq = reinterpret_cast<const T*>(a.lq) + tok * HQ * D;
-          x1 += to_f<T>(lq[src]) * s;
-          x2 += to_f<T>(lq[src + HALF]) * s;
-        } else if (fq) {
-          x1 += lora_b(sBq, xl, src) * s;
-          x2 += lora_b(sBq, xl, src + HALF) * s;
+          ld8<T>(lq + src, l1);
+          ld8<T>(lq + src + HALF, l2);
+        } else {
+          lora_rows8<T>(sBq, src, xl, l1);
+          lora_rows8<T>(sBq, src + HALF, xl, l2);
         }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { x1[j] += l1[j] * s; x2[j] += l2[j] * s; }
       }
-      const float c = cs[d], sv = sn[d];
+      float o1[8], o2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o1[j] = x1[j] * c[j] - x2[j] * sv[j];
+        o2[j] = x2[j] * c[j] + x1[j] * sv[j];
+      }
       T* out = is_q ? reinterpret_cast<T*>(a.q) + tok * HQ * D + hh * D
                     : reinterpret_cast<T*>(a.k) + tok * HKV * D + (hh - HQ) * D;
-      out[d] = from_f<T>(x1 * c - x2 * sv);
-      out[d + HALF] = from_f<T>(x2 * c + x1 * sv);
+      st8<T>(out + d, o1);
+      st8<T>(out + d + HALF, o2);
     }
-    for (int idx = lane; idx < HKV * D; idx += 32) {
-      float v = to_f<T>(row[(HQ + HKV) * D + idx]);
-      if (a.lv != nullptr) v += to_f<T>(reinterpret_cast<const T*>(a.lv)[tok * HKV * D + idx]) * s;
-      else if (fv) v += lora_b(sBv, xl + RANK, idx) * s;
-      reinterpret_cast<T*>(a.v)[tok * HKV * D + idx] = from_f<T>(v);
+    for (int ch = lane; ch < v_chunks; ch += 32) {
+      const int idx = ch * 8;
+      float v[8];
+      ld8<T>(row + (HQ + HKV) * D + idx, v);
+      if (a.lv != nullptr || fv) {
+        float l[8];
+        if (a.lv != nullptr) ld8<T>(reinterpret_cast<const T*>(a.lv) + tok * HKV * D + idx, l);
+        else lora_rows8<T>(sBv, idx, xl + RANK, l);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += l[j] * s;
+      }
+      st8<T>(reinterpret_cast<T*>(a.v) + tok * HKV * D + idx, v);
     }
   }
 }
@@ -110,6 +161,22 @@ __device__ __forceinline__ float rs32(float* v) {
   return v[0];
 }
 
+// acc[off + r] += sum_j g[j] B[idx + j][r] (8 consecutive rows of a [rows, 16] factor in smem)
+template <typename T>
+__device__ __forceinline__ void lora_acc8(const T* B, int idx, const float* g, float* acc, int off) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)(idx + j) * RANK);
+    const uint4 u0 = b4[0], u1 = b4[1];
+    const T* b0 = reinterpret_cast<const T*>(&u0);
+    const T* b1 = reinterpret_cast<const T*>(&u1);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[off + r] += g[j] * to_f<T>(b0[r]);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[off + 8 + r] += g[j] * to_f<T>(b1[r]);
+  }
+}
+
 template <typename T, typename TIn>
 __global__ void __launch_bounds__(256) rope_bwd_kernel(RopeBwdC a) {
   extern __shared__ __align__(16) uint8_t rope_smem[];
@@ -128,6 +195,9 @@ __global__ void __launch_bounds__(256) rope_bwd_kernel(RopeBwdC a) {
     __syncthreads();
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cph = HALF / 8;
+  const int rot_chunks = (HQ + HKV) * cph;
+  const int v_chunks = HKV * D / 8;
   for (int64_t tok = blockIdx.x * 8 + warp; tok < a.n; tok += (int64_t)gridDim.x * 8) {
     const int pos = a.pos[tok];
     const float* cs = a.cos + (int64_t)pos * HALF;
@@ -139,46 +209,56 @@ __global__ void __launch_bounds__(256) rope_bwd_kernel(RopeBwdC a) {
     float acc[2 * RANK];
 #pragma unroll
     for (int r = 0; r < 2 * RANK; ++r) acc[r] = 0.f;
-    auto accum = [&](const T* B, int idx, float g, int off) {
-      const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)idx * RANK);
-      const uint4 u0 = b4[0], u1 = b4[1];
-      const T* b0 = reinterpret_cast<const T*>(&u0);
-      const T* b1 = reinterpret_cast<const T*>(&u1);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) acc[off + r] += g * to_f<T>(b0[r]);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) acc[off + 8 + r] += g * to_f<T>(b1[r]);
-    };
-    for (int idx = lane; idx < (HQ + HKV) * HALF; idx += 32) {
-      const int hh = idx / HALF, d = idx % HALF;
-      float g1 = 0.f, g2 = 0.f;
+#pragma unroll 2
+    for (int ch = lane; ch < rot_chunks; ch += 32) {
+      const int hh = ch / cph, d = (ch % cph) * 8;
+      float g1[8], g2[8], c[8], sv[8];
       if (hh < HQ) {
-        g1 = to_f<TIn>(dq[hh * D + d]);
-        g2 = to_f<TIn>(dq[hh * D + d + HALF]);
+        ld8<TIn>(dq + hh * D + d, g1);
+        ld8<TIn>(dq + hh * D + d + HALF, g2);
       } else {
         const int j = hh - HQ;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) g1[t] = g2[t] = 0.f;
         for (int r = 0; r < group; ++r) {
-          g1 += to_f<TIn>(dk[(j * group + r) * D + d]);
-          g2 += to_f<TIn>(dk[(j * group + r) * D + d + HALF]);
+          float t1[8], t2[8];
+          ld8<TIn>(dk + (j * group + r) * D + d, t1);
+          ld8<TIn>(dk + (j * group + r) * D + d + HALF, t2);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) { g1[t] += t1[t]; g2[t] += t2[t]; }
         }
       }
-      const float c = cs[d], sv = sn[d];
-      const T o1 = from_f<T>(g1 * c + g2 * sv), o2 = from_f<T>(g2 * c - g1 * sv);
+      ld8<float>(cs + d, c);
+      ld8<float>(sn + d, sv);
+      float o1[8], o2[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        o1[t] = to_f<T>(from_f<T>(g1[t] * c[t] + g2[t] * sv[t]));
+        o2[t] = to_f<T>(from_f<T>(g2[t] * c[t] - g1[t] * sv[t]));
+      }
       const int col = hh * D + d;
-      out[col] = o1;
-      out[col + HALF] = o2;
+      st8<T>(out + col, o1);
+      st8<T>(out + col + HALF, o2);
       if (hh < HQ && lq) {
-        accum(sBq, col, to_f<T>(o1), 0);
-        accum(sBq, col + HALF, to_f<T>(o2), 0);
+        lora_acc8<T>(sBq, col, o1, acc, 0);
+        lora_acc8<T>(sBq, col + HALF, o2, acc, 0);
       }
     }
-    for (int idx = lane; idx < HKV * D; idx += 32) {
-      const int j = idx / D, d = idx % D;
-      float g = 0.f;
-      for (int r = 0; r < group; ++r) g += to_f<TIn>(dv[(j * group + r) * D + d]);
-      const T o = from_f<T>(g);
-      out[(HQ + HKV) * D + idx] = o;
-      if (lv) accum(sBv, idx, to_f<T>(o), RANK);
+    for (int ch = lane; ch < v_chunks; ch += 32) {
+      const int idx = ch * 8, j = idx / D, d = idx % D;
+      float g[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) g[t] = 0.f;
+      for (int r = 0; r < group; ++r) {
+        float t1[8];
+        ld8<TIn>(dv + (j * group + r) * D + d, t1);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) g[t] += t1[t];
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) g[t] = to_f<T>(from_f<T>(g[t]));
+      st8<T>(out + (HQ + HKV) * D + idx, g);
+      if (lv) lora_acc8<T>(sBv, idx, g, acc, RANK);
     }
     if (lq || lv) {
       const float sum = rs32(acc);  // lane l: value l (q: 0..15, v: 16..31)
@@ -200,18 +280,14 @@ static int rope_grid(int64_t n) {
   return (int)(want < cap ? want : cap);
 }
 
-// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel.
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
 template <typename K>
 static void rope_smem_attr(K kern, int bytes) {
-  static int done = 0;  // one flag per kernel instantiation
-  if (bytes > 48 * 1024 && bytes > done) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    done = bytes;
-  }
+  if (bytes > 48 * 1024) smem_optin(reinterpret_cast<const void*>(kern), bytes);
 }
 
 int rope_fwd(const RopeFwdC& a, cudaStream_t s) {
-  if (a.n < 0 || a.D % 2 != 0 || a.HKV <= 0 || a.HQ % a.HKV != 0) return QL_STATUS_BAD_ARG;
+  if (a.n < 0 || a.D % 16 != 0 || a.HKV <= 0 || a.HQ % a.HKV != 0) return QL_STATUS_BAD_ARG;
   if (a.n == 0) return QL_STATUS_OK;
   if ((a.xq != nullptr && a.Bq == nullptr) || (a.xv != nullptr && a.Bv == nullptr)) return QL_STATUS_BAD_ARG;
   if ((a.xq != nullptr || a.xv != nullptr) && a.rank != RANK) return QL_STATUS_UNSUPPORTED;
@@ -232,7 +308,7 @@ int rope_fwd(const RopeFwdC& a, cudaStream_t s) {
 }
 
 int rope_bwd(const RopeBwdC& a, cudaStream_t s) {
-  if (a.n < 0 || a.D % 2 != 0 || a.HKV <= 0 || a.HQ % a.HKV != 0) return QL_STATUS_BAD_ARG;
+  if (a.n < 0 || a.D % 16 != 0 || a.HKV <= 0 || a.HQ % a.HKV != 0) return QL_STATUS_BAD_ARG;
   if (a.kv_heads_in != a.HKV && a.kv_heads_in != a.HQ) return QL_STATUS_BAD_ARG;
   if (a.n == 0) return QL_STATUS_OK;
   if ((a.dxlo_q != nullptr && a.Bq == nullptr) || (a.dxlo_v != nullptr && a.Bv == nullptr)) return QL_STATUS_BAD_ARG;

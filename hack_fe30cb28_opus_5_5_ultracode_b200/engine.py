@@ -657,12 +657,20 @@ class _FusedStep(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, engine, packed, denom, stats, *lora):
-        loss, saved, dhp = engine._forward(packed, denom, stats)
+        torch.cuda.nvtx.range_push("qlora_fwd")
+        try:
+            loss, saved, dhp = engine._forward(packed, denom, stats)
+        finally:
+            torch.cuda.nvtx.range_pop()
         ctx.engine, ctx.packed, ctx.saved, ctx.dhp = engine, packed, saved, dhp
         return loss
 
     @staticmethod
     def backward(ctx, grad):
-        grads = ctx.engine._backward(ctx.packed, ctx.saved, ctx.dhp, grad)
+        torch.cuda.nvtx.range_push("qlora_bwd")
+        try:
+            grads = ctx.engine._backward(ctx.packed, ctx.saved, ctx.dhp, grad)
+        finally:
+            torch.cuda.nvtx.range_pop()
         ctx.saved = ctx.dhp = None
         return (None, None, None, None, *grads)

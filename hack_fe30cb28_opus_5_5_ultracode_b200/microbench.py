@@ -31,13 +31,24 @@ def _peaks():
 
 
 def _time(fn, iters):
+    """Seconds per launch of fn, the launches replayed from a CUDA graph (no host overhead
+    between them)."""
     for _ in range(3):
         fn(0)
     torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn(0)  # (warm-up on the capture stream)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(iters):
+                fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for i in range(iters):
-        fn(i)
+    graph.replay()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters / 1e3
@@ -152,9 +163,48 @@ def main():
         A = torch.randn(16, H, device=dev, generator=g).to(dt) * 0.02
         tok = torch.arange(n, device=dev)
         drop = ops.Drop(tok, 1, 0, 10, 1184 * 256, 0.05)
+        ys = [torch.empty(n, H, device=dev, dtype=dt) for _ in range(copies)]
         sec = _time(lambda i: ops.rms_fwd(xs[i % copies], w, 1e-6, drop=drop, Aq=A, Av=A,
-                                          want_yq=True), args.iters)
+                                          want_yq=True, out_y=ys[i % copies]), args.iters)
         _report("rms_fwd (+dropout, LoRA-A)", [n, H], sec, nbytes=n * H * (4 + 3 * 2))
+        sec = _time(lambda i: ops.rms_fwd(xs[i % copies], w, 1e-6, out_y=ys[i % copies]),
+                    args.iters)
+        _report("rms_fwd (plain)", [n, H], sec, nbytes=n * H * (4 + 2))
+        rstd = torch.ones(n, device=dev)
+        dy = [torch.randn(n, H, device=dev, generator=g).to(dt) for _ in range(copies)]
+        lo = torch.randn(n, 16, device=dev, generator=g)
+        dx = [torch.empty(n, H, device=dev) for _ in range(copies)]
+        sec = _time(lambda i: ops.rms_bwd(dy[i % copies], xs[i % copies], rstd, w, dres=xs[0],
+                                          dxlo_q=lo, dxlo_v=lo, Aq=A, Av=A, drop=drop,
+                                          out=dx[i % copies]), args.iters)
+        _report("rms_bwd (+dropout, LoRA dx)", [n, H], sec, nbytes=n * H * (2 + 4 + 4 + 4))
+    if want("rope"):
+        C = (HQ + 2 * HKV) * D
+        qkv = [torch.randn(n, C, device=dev, generator=g).to(dt) for _ in range(copies)]
+        xq = torch.randn(n, 16, device=dev, generator=g).to(dt)
+        Bq = torch.randn(HQ * D, 16, device=dev, generator=g).to(dt) * 0.02
+        Bv = torch.randn(HKV * D, 16, device=dev, generator=g).to(dt) * 0.02
+        pos = torch.arange(n, device=dev, dtype=torch.int32) % 512
+        cos = torch.rand(1024, D // 2, device=dev)
+        sin = torch.rand(1024, D // 2, device=dev)
+        outs = [(torch.empty(n, HQ, D, device=dev, dtype=dt), torch.empty(n, HKV, D, device=dev, dtype=dt),
+                 torch.empty(n, HKV, D, device=dev, dtype=dt)) for _ in range(copies)]
+        sec = _time(lambda i: ops.rope_fwd(qkv[i % copies], cos, sin, pos, HQ, HKV, D, 2.0, xq=xq,
+                                           xv=xq, Bq=Bq, Bv=Bv, out=outs[i % copies]), args.iters)
+        _report("rope_fwd (+LoRA-B)", [n, C], sec, nbytes=n * C * 4)
+        dq = torch.randn(n, HQ, D, device=dev, generator=g)
+        dk = torch.randn(n, HKV, D, device=dev, generator=g)
+        sec = _time(lambda i: ops.rope_bwd(dq, dk, dk, cos, sin, pos, HQ, HKV, D, Bq=Bq, Bv=Bv,
+                                           lora_scale=2.0, out=qkv[i % copies]), args.iters)
+        _report("rope_bwd (+LoRA dx)", [n, C], sec, nbytes=n * C * 6)
+    if want("colsum"):
+        X = torch.randn(n, H, device=dev, generator=g).to(dt)
+        Y = torch.randn(n, 16, device=dev, generator=g)
+        out = torch.empty(16, H, device=dev)
+        ws = torch.empty(64 * H * 16, device=dev)
+        sec = _time(lambda i: ops.lora_colsum(X, Y, transpose=True, out=out, workspace=ws),
+                    args.iters)
+        _report("lora_colsum", [n, H], sec, nbytes=n * H * 2)
     if want("ce"):
         logits = [torch.randn(n, V, device=dev, generator=g).to(dt) for _ in range(2)]
         tgt = torch.randint(0, V, (n,), device=dev, generator=g)
