@@ -208,6 +208,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// bulk staging of a small read-only array into shared memory: every 16-byte copy in flight at
+// once (cp.async), then a CTA barrier. (A plain copy loop through generic pointers would run
+// its loads one after another: the compiler cannot prove they do not alias the shared stores.)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void stage_to_smem(void* smem, const void* gmem, int bytes) {
+  const char* g = static_cast<const char*>(gmem);
+  char* d = static_cast<char*>(smem);
+  for (int off = threadIdx.x * 16; off < bytes; off += blockDim.x * 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(d + off)), "l"(g + off)
+                 : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void stage_wait() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------------------------
 // warp reductions
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {

@@ -126,12 +126,9 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
   const int H = a.H, ngroups = H / 4;
   const bool lora_q = a.drop.drop_q && a.Aq != nullptr, lora_v = a.drop.drop_v && a.Av != nullptr;
   if (lora_q || lora_v) {
-    const int chunks = LORA_R * H / 8;  // 16-byte chunks per factor
-    for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
-      if (lora_q) reinterpret_cast<uint4*>(sAq)[i] = reinterpret_cast<const uint4*>(a.Aq)[i];
-      if (lora_v) reinterpret_cast<uint4*>(sAv)[i] = reinterpret_cast<const uint4*>(a.Av)[i];
-    }
-    __syncthreads();
+    if (lora_q) stage_to_smem(sAq, a.Aq, LORA_R * H * (int)sizeof(T));
+    if (lora_v) stage_to_smem(sAv, a.Av, LORA_R * H * (int)sizeof(T));
+    stage_wait();
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {
@@ -212,12 +209,9 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
   const int H = a.H, ngroups = H / 4;
   const bool fq = a.drop.drop_q && a.tq == nullptr, fv = a.drop.drop_v && a.tv == nullptr;
   if (fq || fv) {
-    const int chunks = LORA_R * H / 8;
-    for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
-      if (fq) reinterpret_cast<uint4*>(sAq)[i] = reinterpret_cast<const uint4*>(a.Aq)[i];
-      if (fv) reinterpret_cast<uint4*>(sAv)[i] = reinterpret_cast<const uint4*>(a.Av)[i];
-    }
-    __syncthreads();
+    if (fq) stage_to_smem(sAq, a.Aq, LORA_R * H * (int)sizeof(T));
+    if (fv) stage_to_smem(sAv, a.Av, LORA_R * H * (int)sizeof(T));
+    stage_wait();
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {

@@ -73,11 +73,9 @@ __global__ void __launch_bounds__(256) rope_fwd_kernel(RopeFwdC a) {
   T* sBv = sBq + (int64_t)HQ * D * RANK;
   const bool fq = a.lq == nullptr && a.xq != nullptr, fv = a.lv == nullptr && a.xv != nullptr;
   if (fq || fv) {
-    for (int i = threadIdx.x; i < HQ * D * RANK / 8; i += blockDim.x)
-      if (fq) reinterpret_cast<uint4*>(sBq)[i] = reinterpret_cast<const uint4*>(a.Bq)[i];
-    for (int i = threadIdx.x; i < HKV * D * RANK / 8; i += blockDim.x)
-      if (fv) reinterpret_cast<uint4*>(sBv)[i] = reinterpret_cast<const uint4*>(a.Bv)[i];
-    __syncthreads();
+    if (fq) stage_to_smem(sBq, a.Bq, HQ * D * RANK * (int)sizeof(T));
+    if (fv) stage_to_smem(sBv, a.Bv, HKV * D * RANK * (int)sizeof(T));
+    stage_wait();
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float s = a.lora_scale;
@@ -188,11 +186,9 @@ __global__ void __launch_bounds__(256) rope_bwd_kernel(RopeBwdC a) {
   T* sBv = sBq + (int64_t)HQ * D * RANK;
   const bool lq = a.dxlo_q != nullptr, lv = a.dxlo_v != nullptr;
   if (lq || lv) {
-    for (int i = threadIdx.x; i < HQ * D * RANK / 8; i += blockDim.x)
-      if (lq) reinterpret_cast<uint4*>(sBq)[i] = reinterpret_cast<const uint4*>(a.Bq)[i];
-    for (int i = threadIdx.x; i < HKV * D * RANK / 8; i += blockDim.x)
-      if (lv) reinterpret_cast<uint4*>(sBv)[i] = reinterpret_cast<const uint4*>(a.Bv)[i];
-    __syncthreads();
+    if (lq) stage_to_smem(sBq, a.Bq, HQ * D * RANK * (int)sizeof(T));
+    if (lv) stage_to_smem(sBv, a.Bv, HKV * D * RANK * (int)sizeof(T));
+    stage_wait();
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cph = HALF / 8;
