@@ -97,11 +97,14 @@ int ql_nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2
 
 int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-               const float* residual, cudaStream_t stream) {
+               const float* residual, void* workspace, int64_t workspace_bytes,
+               cudaStream_t stream) {
   return done(ql::gemm_tn(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
-                          residual, ql::status_word(), stream),
+                          residual, ql::status_word(), stream, workspace, workspace_bytes),
               "ql_gemm_tn");
 }
+
+int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
 }  // extern "C"
 

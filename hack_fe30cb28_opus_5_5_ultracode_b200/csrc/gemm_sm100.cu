@@ -8,7 +8,8 @@
 // 1111-1112, 1132-1139, 1163-1165, 1178-1179, 1238-1316, 1386-1390).
 //
 // Structure: a persistent, warp-specialised kernel with one CTA per SM.
-//   warp 0      TMA producer: 128 x 64 tiles of A and BN x 64 tiles of B into a ring of STAGES
+//   warp 0      TMA producer: 128 x 64 tiles of A and BN x 64 tiles of B (BN = 96 .. 256, picked
+//               per shape so that the output tiles fill whole waves of SMs) into a ring of STAGES
 //               shared-memory slots (128-byte swizzle), completion counted on an mbarrier;
 //   warp 1      allocates 2 x BN TMEM columns (two accumulators) and issues tcgen05.mma from one
 //               thread, 4 x (K = 16) per 64-wide K step; tcgen05.commit frees each slot and, at
@@ -29,6 +30,12 @@ struct GemmArgs {
   int accumulate;    // C += result (fp32 output only)
   const float* residual;  // fp32 [M, ldc] or null: C = residual + (result rounded to the input type)
   int* err;
+  // split-K: each output tile's K range is cut into `splits` parts computed by different work
+  // units; every unit writes its fp32 partial to ws, the last one of a tile (counters) adds them
+  // in split order and runs the epilogue. counters: one int per tile, zero between launches.
+  int splits, kb_per_split;
+  float* ws;
+  int* counters;
 };
 
 template <int BN>
@@ -37,9 +44,14 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
-  static constexpr int TMEM_COLS = 2 * BN;  // 256 or 512: a power of two >= 32
+  // as many ring slots as fit in 225 KB (at most 8)
+  static constexpr int STAGES_FIT = (225 * 1024 - 1280) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  // two accumulators of BN fp32 columns; the allocation is a power of two >= 32 columns
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (M = 128) and 32-column epilogue");
+  static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
 };
 
 template <typename OutT>
@@ -86,6 +98,8 @@ __global__ void __launch_bounds__(192, 1)
   const int m_tiles = (int)cdiv(p.M, Cfg::BM), n_tiles = (int)cdiv(p.N, BN);
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (int)cdiv(p.K, Cfg::BK);
+  const int S = p.splits;
+  const int num_units = num_tiles * S;  // unit u: tile u / S, split u % S
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -111,9 +125,11 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u / S, sp = u % S;
         const int mb = tile % m_tiles, nb = tile / m_tiles;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb0 = sp * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
@@ -131,13 +147,15 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+        const int sp = u % S;
+        const int kb0 = sp * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
@@ -145,7 +163,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
             umma_f16(tmem_d, umma_desc_k_sw128(sa + k * 32), umma_desc_k_sw128(sb + k * 32), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+                     (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
@@ -160,7 +178,9 @@ __global__ void __launch_bounds__(192, 1)
     int local = 0;
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const InT* bias = reinterpret_cast<const InT*>(p.bias);
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    __shared__ int last_flag;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      const int tile = u / S, sp = u % S;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
@@ -168,32 +188,80 @@ __global__ void __launch_bounds__(192, 1)
       const int mb = tile % m_tiles, nb = tile / m_tiles;
       const int row = mb * Cfg::BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      bool finish = true;  // this unit writes the output tile
+      float* part = nullptr;
+      if (S > 1) {
+        // this split's fp32 partial, stored column-major within the tile ([BN][128 rows]) so
+        // that the 32 lanes of a warp (32 consecutive rows) write and read whole 128-byte lines
+        part = p.ws + ((int64_t)tile * S) * Cfg::BM * BN;
+        float* mine = part + (int64_t)sp * Cfg::BM * BN + row_in_tile;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld32(taddr + c, v);
-        const int col0 = nb * BN + c;
-        if (row < p.M && col0 < p.N) {
-          const int ncols = min(32, p.N - col0);
-          if (bias != nullptr) {
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < ncols) v[i] += to_f<InT>(bias[col0 + i]);
-          }
-          OutT* dst = C + (int64_t)row * p.ldc + col0;
-          if constexpr (sizeof(OutT) == 4) {
-            if (p.residual != nullptr) {
-              const float* res = p.residual + (int64_t)row * p.ldc + col0;
+          for (int i = 0; i < 32; ++i) __stcg(mine + (c + i) * Cfg::BM, v[i]);
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(p.counters + tile, 1);
+          last_flag = (old == S - 1);
+          if (old == S - 1) p.counters[tile] = 0;  // ready for the next launch
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        finish = last_flag != 0;
+        if (finish) __threadfence();
+      }
+      if (finish) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          if (S > 1) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < ncols) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
-            } else if (p.accumulate) {
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            const float* src = part + row_in_tile + (int64_t)c * Cfg::BM;
+            for (int j = 0; j < S; j += 2) {  // fixed order p0 + p1 + ...: reproducible sums
+              float x0[32], x1[32];
+              const float* s0 = src + (int64_t)j * Cfg::BM * BN;
+              const bool two = j + 1 < S;
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < ncols) v[i] += to_f<OutT>(dst[i]);
+              for (int i = 0; i < 32; ++i) x0[i] = __ldcg(s0 + i * Cfg::BM);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) x1[i] = two ? __ldcg(s0 + Cfg::BM * BN + i * Cfg::BM) : 0.f;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += x0[i];
+              if (two) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += x1[i];
+              }
             }
+          } else {
+            tmem_ld32(taddr + c, v);
           }
-          store_row32<OutT>(dst, v, ncols);
+          const int col0 = nb * BN + c;
+          if (row < p.M && col0 < p.N) {
+            const int ncols = min(32, p.N - col0);
+            if (bias != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < ncols) v[i] += to_f<InT>(bias[col0 + i]);
+            }
+            OutT* dst = C + (int64_t)row * p.ldc + col0;
+            if constexpr (sizeof(OutT) == 4) {
+              if (p.residual != nullptr) {
+                const float* res = p.residual + (int64_t)row * p.ldc + col0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < ncols) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
+              } else if (p.accumulate) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < ncols) v[i] += to_f<OutT>(dst[i]);
+              }
+            }
+            store_row32<OutT>(dst, v, ncols);
+          }
         }
       }
       tc_fence_before();
@@ -268,8 +336,8 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
       return QL_STATUS_CUDA;
     configured = true;
   }
-  const int tiles = (int)(cdiv(a.M, 128) * cdiv(a.N, BN));
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int units = (int)(cdiv(a.M, 128) * cdiv(a.N, BN)) * a.splits;
+  const int grid = units < num_sms() ? units : num_sms();
   kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, a);
   return launched(1);
 }
@@ -285,9 +353,71 @@ static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const Gemm
   return QL_STATUS_BAD_ARG;
 }
 
+template <int BN>
+static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, bool bf16,
+                       cudaStream_t s) {
+  return bf16 ? dispatch_out<BN, true>(ma, mb, a, s) : dispatch_out<BN, false>(ma, mb, a, s);
+}
+
+// Split-K workspace: tile counters first (a fixed region, left all-zero by every launch, so
+// GEMMs of any shape can share one workspace), then the fp32 partial tiles.
+constexpr int64_t kCounterBytes = 2048;  // 512 tiles: split-K only runs below 2 x SMs tiles
+
+struct GemmPlan {
+  int bn;
+  int64_t tiles;
+  int splits, kb_per_split;
+};
+
+// Tile width and K splits of a shape. BN: the fewest waves of output tiles over the SMs, each
+// wave costed as BN + 64 (a tile streams 128 + BN rows of A and B per K step and does BN columns
+// of MMA), ties to the wider tile. Split-K only when the tiles leave most SMs idle and every
+// split keeps at least 32 K-blocks (shorter splits cost more in partial traffic than they gain):
+// the best last-wave efficiency over 2..8 splits, the fewest splits within 2% of it, used only if
+// it beats the unsplit launch by 5 points.
+static GemmPlan plan_gemm(int M, int N, int K, int sms) {
+  static const int widths[] = {256, 224, 192, 128, 96};
+  GemmPlan g{256, 0, 1, 0};
+  int64_t best = -1;
+  for (int bn : widths) {
+    const int64_t tiles = cdiv(M, 128) * cdiv(N, bn);
+    const int64_t cost = cdiv(tiles, sms) * (bn + 64);
+    if (best < 0 || cost < best) {
+      best = cost;
+      g.bn = bn;
+      g.tiles = tiles;
+    }
+  }
+  const int k_blocks = (int)cdiv(K, 64);
+  g.kb_per_split = k_blocks;
+  if (g.tiles >= 2 * (int64_t)sms || g.tiles * 4 > kCounterBytes) return g;
+  auto eff = [&](int s) {
+    const int64_t u = g.tiles * s;
+    return (double)u / (double)(cdiv(u, sms) * sms);
+  };
+  double top = 0.0;
+  for (int s = 2; s <= 8 && k_blocks / s >= 32; ++s) top = eff(s) > top ? eff(s) : top;
+  if (top < eff(1) + 0.05) return g;
+  for (int s = 2; s <= 8; ++s)
+    if (eff(s) >= top - 0.02) {
+      g.kb_per_split = (int)cdiv(k_blocks, s);
+      g.splits = (int)cdiv(k_blocks, g.kb_per_split);  // no empty split
+      break;
+    }
+  return g;
+}
+
+int64_t gemm_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const GemmPlan g = plan_gemm(M, N, K, num_sms());
+  if (g.splits == 1) return 0;
+  return kCounterBytes + g.tiles * g.splits * 128 * g.bn * 4;
+}
+
 int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
             const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-            const float* residual, int* err, cudaStream_t stream) {
+            const float* residual, int* err, cudaStream_t stream, void* workspace,
+            int64_t workspace_bytes) {
   if (M < 0 || N < 0 || K < 0) return QL_STATUS_BAD_ARG;
   if (M == 0 || N == 0) return QL_STATUS_OK;
   if (in_dtype != QL_F16 && in_dtype != QL_BF16) return QL_STATUS_BAD_ARG;
@@ -301,16 +431,31 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   ProfScope prof(PK_GEMM, 2.0 * M * N * K,
                  2.0 * ((double)M * K + (double)N * K) + (double)M * N * (out_dtype == QL_F32 ? 4 : 2),
                  stream);
-  // Wide N tiles when there are enough of them to fill the machine, else 128.
-  const int64_t tiles256 = cdiv(M, 128) * cdiv(N, 256);
-  const int BN = (tiles256 >= num_sms()) ? 256 : 128;
+  GemmPlan g = plan_gemm(M, N, K, num_sms());
+  const int64_t need = kCounterBytes + g.tiles * g.splits * 128 * g.bn * 4;
+  if (g.splits > 1 && (workspace == nullptr || workspace_bytes < need ||
+                       reinterpret_cast<uintptr_t>(workspace) % 256 != 0 ||
+                       accumulate /* C is read by the epilogue: keep one writer per tile */)) {
+    g.splits = 1;
+    g.kb_per_split = (int)cdiv(K, 64);
+  }
   CUtensorMap ma, mb;
   if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  if (make_kmajor_map(&mb, B, N, K, ldb, BN, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err};
-  if (BN == 256)
-    return bf16 ? dispatch_out<256, true>(ma, mb, a, stream) : dispatch_out<256, false>(ma, mb, a, stream);
-  return bf16 ? dispatch_out<128, true>(ma, mb, a, stream) : dispatch_out<128, false>(ma, mb, a, stream);
+  if (make_kmajor_map(&mb, B, N, K, ldb, g.bn, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+  GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
+             g.kb_per_split, nullptr, nullptr};
+  if (g.splits > 1) {
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    a.counters = reinterpret_cast<int*>(w);
+    a.ws = reinterpret_cast<float*>(w + kCounterBytes);
+  }
+  switch (g.bn) {
+    case 96: return dispatch_in<96>(ma, mb, a, bf16, stream);
+    case 128: return dispatch_in<128>(ma, mb, a, bf16, stream);
+    case 192: return dispatch_in<192>(ma, mb, a, bf16, stream);
+    case 224: return dispatch_in<224>(ma, mb, a, bf16, stream);
+    default: return dispatch_in<256>(ma, mb, a, bf16, stream);
+  }
 }
 
 }  // namespace ql

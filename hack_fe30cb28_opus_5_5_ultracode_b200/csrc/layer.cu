@@ -41,7 +41,24 @@ int dequant(const ql_nf4_weight& w, void* out, int dtype, int transpose, cudaStr
     if (_rc != QL_STATUS_OK) return _rc; \
   } while (0)
 
+// The split-K GEMM workspace sits at the start of the layer workspace (its first bytes are
+// tile counters, zero between launches): the largest any GEMM of the layer asks for.
+int64_t layer_gemm_ws(const ql_layer_desc& L) {
+  const int64_t C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
+  const int n = L.n, H = L.H, I = L.I, QD = L.HQ * L.D;
+  const int64_t shapes[8][3] = {{n, C, H}, {n, H, QD}, {n, 2 * I, H}, {n, H, I},
+                                {n, I, H}, {n, H, 2 * I}, {n, QD, H}, {n, H, C}};
+  int64_t m = 0;
+  for (const auto& sh : shapes) {
+    const int64_t b = gemm_workspace_bytes((int)sh[0], (int)sh[1], (int)sh[2]);
+    m = b > m ? b : m;
+  }
+  return m;
+}
+
 struct FwdWs {
+  void* gws;  // split-K GEMM workspace
+  int64_t gws_bytes;
   void* w;    // dequantised weight (largest of the four)
   void* a;    // [n, H] norm output (a, then b)
   void* qkv;  // [n, C]
@@ -51,6 +68,8 @@ struct FwdWs {
 FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
   const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D, e = esz(L.dtype);
   FwdWs w;
+  w.gws_bytes = layer_gemm_ws(L);
+  w.gws = b.take(w.gws_bytes);
   w.w = b.take(max_weight_elems(L) * e);
   w.a = b.take(n * L.H * e);
   w.qkv = b.take(n * C * e);
@@ -59,6 +78,8 @@ FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
 }
 
 struct BwdWs {
+  void* gws;
+  int64_t gws_bytes;
   void* w;
   void* dm;      // [n, I]
   void* db;      // [n, H]
@@ -80,6 +101,8 @@ struct BwdWs {
 BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
   const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D, e = esz(L.dtype);
   BwdWs w;
+  w.gws_bytes = layer_gemm_ws(L);
+  w.gws = b.take(w.gws_bytes);
   w.w = b.take(max_weight_elems(L) * e);
   w.dm = b.take(n * L.I * e);
   w.db = b.take(n * L.H * e);
@@ -146,7 +169,7 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   // q, k, v in one GEMM (bias in the epilogue), then LoRA-B + RoPE
   QL_TRY(dequant(L.qkv, w.w, dt, 0, s));
   QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, w.qkv, C, L.bias_qkv, L.n, (int)C, L.H, dt, dt, 0, nullptr,
-                 err, s));
+                 err, s, w.gws, w.gws_bytes));
   RopeFwdC rf{};
   rf.qkv = w.qkv; rf.xq = S.xq; rf.xv = S.xv; rf.Bq = L.Bq; rf.Bv = L.Bv; rf.cos = L.cos;
   rf.sin = L.sin; rf.pos = L.pos; rf.q = S.q; rf.k = S.k; rf.v = S.v;
@@ -161,7 +184,7 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   // o projection, residual add in the epilogue: h2 = h + o
   QL_TRY(dequant(L.o, w.w, dt, 0, s));
   QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, w.w, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
-                 L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s));
+                 L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s, w.gws, w.gws_bytes));
   // post-attention RMSNorm
   RmsFwdC r2{};
   r2.x = S.h2; r2.w = L.ln2; r2.y = w.a; r2.rstd = S.rstd2; r2.n = L.n; r2.H = L.H;
@@ -171,11 +194,11 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   // [gate | up], SwiGLU, down with the residual add: h3 = h2 + d
   QL_TRY(dequant(L.gu, w.w, dt, 0, s));
   QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
-                 nullptr, err, s));
+                 nullptr, err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
   QL_TRY(dequant(L.down, w.w, dt, 0, s));
   QL_TRY(gemm_tn(w.m, L.I, w.w, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
-                 err, s));
+                 err, s, w.gws, w.gws_bytes));
   return QL_STATUS_OK;
 }
 
@@ -197,11 +220,11 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   // MLP: dm = dh3 . Wd ; [dg | du] in place ; db = [dg | du] . Wgu
   QL_TRY(dequant(L.down, w.w, dt, 1, s));
   QL_TRY(gemm_tn(dh3_16, L.H, w.w, L.H, w.dm, L.I, nullptr, L.n, L.I, L.H, dt, dt, 0, nullptr,
-                 err, s));
+                 err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_bwd(w.dm, S.gu, n, L.I, dt, s));
   QL_TRY(dequant(L.gu, w.w, dt, 1, s));
   QL_TRY(gemm_tn(S.gu, 2LL * L.I, w.w, 2LL * L.I, w.db, L.H, nullptr, L.n, L.H, 2 * L.I, dt, dt,
-                 0, nullptr, err, s));
+                 0, nullptr, err, s, w.gws, w.gws_bytes));
   RmsBwdC r2{};
   r2.dy = w.db; r2.ld_dy = L.H; r2.x = S.h2; r2.rstd = S.rstd2; r2.w = L.ln2; r2.dres = dh3;
   r2.dx = w.dh2; r2.dx16 = w.dh2_16; r2.n = L.n; r2.H = L.H; r2.rank = L.rank; r2.dtype = dt;
@@ -210,7 +233,7 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   // attention
   QL_TRY(dequant(L.o, w.w, dt, 1, s));
   QL_TRY(gemm_tn(w.dh2_16, L.H, w.w, L.H, w.dout, (int64_t)L.HQ * L.D, nullptr, L.n, L.HQ * L.D,
-                 L.H, dt, dt, 0, nullptr, err, s));
+                 L.H, dt, dt, 0, nullptr, err, s, w.gws, w.gws_bytes));
   AttnBwdC ab{};
   ab.q = S.q; ab.k = S.k; ab.v = S.v; ab.out = S.out; ab.dout = w.dout; ab.lse = S.lse;
   ab.cu_seqlens = L.cu_seqlens; ab.dvec = w.dvec; ab.dq = w.dq; ab.dk = w.dk; ab.dv = w.dv;
@@ -237,7 +260,7 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   if (dh_out == nullptr) return QL_STATUS_OK;  // the first layer's input is the frozen embedding
   QL_TRY(dequant(L.qkv, w.w, dt, 1, s));
   QL_TRY(gemm_tn(w.dqkv, C, w.w, C, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,
-                 err, s));
+                 err, s, w.gws, w.gws_bytes));
   RmsBwdC r1{};
   r1.dy = w.da; r1.ld_dy = L.H; r1.x = S.h; r1.rstd = S.rstd1; r1.w = L.ln1; r1.dres = w.dh2;
   r1.dx = dh_out; r1.dx16 = dh16_out; r1.dxlo_q = w.dxq; r1.dxlo_v = w.dxv; r1.Aq = L.Aq;

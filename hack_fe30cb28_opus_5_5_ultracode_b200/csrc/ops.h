@@ -16,7 +16,9 @@ int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
 
 int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
             const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-            const float* residual, int* err, cudaStream_t stream);
+            const float* residual, int* err, cudaStream_t stream, void* workspace = nullptr,
+            int64_t workspace_bytes = 0);
+int64_t gemm_workspace_bytes(int M, int N, int K);
 
 typedef ql_rms_fwd_args RmsFwdC;
 typedef ql_rms_bwd_args RmsBwdC;

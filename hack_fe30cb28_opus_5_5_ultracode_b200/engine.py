@@ -448,8 +448,8 @@ class FusedQwen2:
         need = max(int(_lib.lib().ql_layer_workspace_bytes(ctypes.addressof(desc), 0)),
                    int(_lib.lib().ql_layer_workspace_bytes(ctypes.addressof(desc), 1)))
         if self._workspace is None or self._workspace.numel() < need:
-            self._workspace = None
-            self._workspace = torch.empty(need, device=self.device, dtype=torch.uint8)
+            self._workspace = None  # zeroed: its leading GEMM tile counters must start at zero
+            self._workspace = torch.zeros(need + need // 4, device=self.device, dtype=torch.uint8)
         return self._workspace
 
     def set_data_parallel(self, group=None):

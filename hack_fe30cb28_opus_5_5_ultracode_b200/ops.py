@@ -73,10 +73,26 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
         raise ValueError("bias must have the input dtype")
     if residual is not None and (residual.stride(0) != out.stride(0) or residual.stride(1) != 1):
         raise ValueError("residual must share the output's row stride")
+    ws = gemm_workspace(a.device, int(_lib.lib().ql_gemm_workspace_bytes(M, N, K)))
     call("ql_gemm_tn", _ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out), out.stride(0),
          _ptr(bias), M, N, K, dtype_code(a.dtype), dtype_code(out.dtype), int(accumulate),
-         _ptr(residual), stream_ptr())
+         _ptr(residual), _ptr(ws), 0 if ws is None else ws.numel(), stream_ptr())
     return out
+
+
+_GEMM_WS = {}
+
+
+def gemm_workspace(device, nbytes):
+    """A zero-initialised, grow-only split-K workspace per device (its counter region is left
+    zero by every GEMM, so it is reused as is)."""
+    if nbytes <= 0:
+        return None
+    ws = _GEMM_WS.get(device)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, device=device, dtype=torch.uint8)
+        _GEMM_WS[device] = ws
+    return ws
 
 
 PROFILE_KINDS = ("gemm", "dequant", "rms_fwd", "rms_bwd", "rope_fwd", "rope_bwd", "attn_fwd",

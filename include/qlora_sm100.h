@@ -74,10 +74,17 @@ int ql_nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2
  * C of out_dtype with leading dimension ldc; accumulate (fp32 C only) adds to C; residual
  * (fp32 C only, [M, ldc] or NULL) writes C = residual + (the result rounded to in_dtype), the
  * reference's fp16 projection output added to the fp32 residual stream (solution/engine.py:
- * 1048-1051, 966 delta add). */
+ * 1048-1051, 966 delta add).
+ * workspace (256-byte aligned, or NULL): lets a GEMM with too few output tiles to fill the
+ * GPU split K across SMs; partial sums are added in a fixed order (results do not depend on
+ * scheduling). Its first 2048 bytes must be zero before the first call; calls leave them zero,
+ * so one workspace serves every later call. ql_gemm_workspace_bytes(M, N, K) is the size a
+ * shape can use (0: it never splits). */
 int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-               const float* residual, cudaStream_t stream);
+               const float* residual, void* workspace, int64_t workspace_bytes,
+               cudaStream_t stream);
+int64_t ql_gemm_workspace_bytes(int M, int N, int K);
 
 /* ---- RMSNorm with the LoRA dropout inputs --------------------------------------------------
  * Dropout fields (shared by both structs): the mask is PyTorch's CUDA dropout mask of the padded
@@ -356,7 +363,8 @@ typedef struct {              /* what the forward keeps for the backward (all [n
   void* gu;                   /* [n, 2 I] [gate | up] (overwritten by its gradient in backward) */
 } ql_layer_saved;
 
-/* Workspace bytes of the forward (backward = 0) or backward (backward = 1) of a layer. */
+/* Workspace bytes of the forward (backward = 0) or backward (backward = 1) of a layer. Its first
+ * 2048 bytes must be zero before the first call (GEMM tile counters); calls leave them zero. */
 int64_t ql_layer_workspace_bytes(const ql_layer_desc* layer, int backward);
 /* h_out [n, H] fp32: the layer's output (the next layer's input). */
 int ql_layer_forward(const ql_layer_desc* layer, const ql_layer_saved* saved, float* h_out,

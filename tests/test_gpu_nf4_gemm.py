@@ -102,7 +102,9 @@ def test_nf4_dequant_nested_segments():
 
 @pytest.mark.parametrize("M,N,K", [(1, 128, 64), (37, 256, 1536), (300, 2048, 1536),
                                    (1400, 17920, 1536), (1400, 1536, 8960), (129, 200, 136),
-                                   (1000, 151936 // 8, 1536)])
+                                   (1000, 151936 // 8, 1536), (1090, 1536, 1536),
+                                   (1090, 8960, 1536), (1090, 17920, 1536), (200, 96, 512),
+                                   (1090, 1536, 17920)])
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
 def test_gemm_matches_torch(M, N, K, dt):
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
@@ -142,3 +144,38 @@ def test_bf16_helpers():
 
     back = bf16_bits_to_f32(f32_to_bf16_bits(x))
     assert np.allclose(back, torch.tensor(x).bfloat16().float().numpy())
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 256, 17920), (130, 1536, 8960), (1090, 512, 8960),
+                                   (64, 1536, 17920)])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_split_k(M, N, K, dt):
+    """Shapes with too few output tiles to fill the GPU split K; the partial sums are added in a
+    fixed order, so two calls agree bit for bit, and the result matches the unsplit GEMM (no
+    workspace) to rounding."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
+
+    assert _lib.lib().ql_gemm_workspace_bytes(M, N, K) > 0
+    g = torch.Generator(device=DEV).manual_seed(M + 7 * N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(dt)
+    b = (torch.randn(N, K, device=DEV, generator=g) * 0.05).to(dt)
+    res = torch.randn(M, N, device=DEV, generator=g)
+    ref = a.float() @ b.float().t()
+    scale = ref.abs().max().item()
+    out1 = ops.gemm(a, b)
+    out2 = ops.gemm(a, b)
+    assert torch.equal(out1, out2)
+    tol = 2e-2 if dt == torch.bfloat16 else 4e-3
+    assert (out1.float() - ref).abs().max().item() / scale < tol
+    # residual epilogue: C = residual + round16(A B^T)
+    out32 = ops.gemm(a, b, out_dtype=torch.float32, residual=res)
+    assert (out32 - (res + out1.float())).abs().max().item() / scale < 2e-3
+    # the same GEMM with no workspace runs unsplit
+    plain = torch.empty(M, N, device=DEV, dtype=dt)
+    _lib.call("ql_gemm_tn", a.data_ptr(), K, b.data_ptr(), K, plain.data_ptr(), N, None, M, N, K,
+              ops.dtype_code(dt), ops.dtype_code(dt), 0, None, None, 0,
+              torch.cuda.current_stream().cuda_stream)
+    assert (plain.float() - out1.float()).abs().max().item() / scale < tol
+    ws = ops.gemm_workspace(a.device, 2048)
+    assert int(ws[:2048].count_nonzero()) == 0  # the tile counters are left at zero
+    assert ops.device_status() == 0
