@@ -160,6 +160,61 @@ int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y
               "ql_lora_colsum");
 }
 
+// LoRA column sums whose per-split partials live in a scratch array compiled into the library,
+// for callers that cannot hand in a workspace: a plain C or ctypes host with no device allocator
+// of its own (a cudaMalloc there would synchronise the whole device in the middle of a step), or
+// a runtime whose device memory is planned once at start-up and must not grow while a step runs.
+// The scratch is one per device: calls that overlap on a device race on it. Nothing in it has to
+// start at zero (every call writes each partial it later reads).
+namespace {
+__device__ __align__(256) float g_colsum_scratch[QL_COLSUM_STATIC_FLOATS];
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// The scratch's address on the current device, looked up once per device (the lookup can load
+// the module on that device, so it is done by the first call, never per launch).
+int colsum_scratch(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(QL_STATUS_CUDA, "ql_lora_colsum_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    g_last_error = "ql_lora_colsum_noalloc: device ordinal " + std::to_string(dev) +
+                   " is beyond the " + std::to_string(kMaxDevices) + " devices it keeps scratch for";
+    return QL_STATUS_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_colsum_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(QL_STATUS_CUDA, "ql_lora_colsum_noalloc: cudaGetSymbolAddress of the scratch");
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return QL_STATUS_OK;
+}
+}  // namespace
+
+int ql_lora_colsum_noalloc(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype,
+                           int64_t n, int ncols, int rank, float scale, int transpose, float* out,
+                           cudaStream_t stream) {
+  if (n < 0 || ncols <= 0) return done(QL_STATUS_BAD_ARG, "ql_lora_colsum_noalloc");
+  const int64_t need = (int64_t)ql::lora_colsum_splits(n, ncols) * ncols * rank;
+  if (need > QL_COLSUM_STATIC_FLOATS) {
+    g_last_error = "ql_lora_colsum_noalloc: this shape needs " + std::to_string(need) +
+                   " floats of scratch, the static scratch holds " +
+                   std::to_string((long long)QL_COLSUM_STATIC_FLOATS) +
+                   " (4 MiB); use ql_lora_colsum with a workspace";
+    return QL_STATUS_BAD_ARG;
+  }
+  float* scratch = nullptr;
+  const int rc = colsum_scratch(&scratch);
+  if (rc != QL_STATUS_OK) return rc;
+  return done(ql::lora_colsum(X, ldx, x_dtype, Y, y_dtype, n, ncols, rank, scale, transpose, out,
+                              scratch, QL_COLSUM_STATIC_FLOATS, stream),
+              "ql_lora_colsum_noalloc");
+}
+
 int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
              int dtype, cudaStream_t stream) {
   return done(ql::embed(ids, W, h, n, H, vocab, dtype, ql::status_word(), stream), "ql_embed");

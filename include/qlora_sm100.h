@@ -210,6 +210,24 @@ int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y
                    int ncols, int rank, float scale, int transpose, float* out, float* workspace,
                    int64_t workspace_floats, cudaStream_t stream);
 
+/* ---- LoRA column sums with the scratch built in (no counterpart in the reference) ---------
+ * The same operation and results as ql_lora_colsum, but the per-split partial sums go to a
+ * scratch array compiled into this library (static device memory, QL_COLSUM_STATIC_FLOATS floats
+ * = 4 MiB per device) instead of a caller workspace. For callers that cannot allocate device
+ * memory: a plain C or ctypes host with no device allocator of its own (cudaMalloc would stall the
+ * whole device mid-step), or a runtime that plans all device memory at start-up.
+ * Limit: shapes whose ql_lora_colsum_workspace(n, ncols, rank) exceeds QL_COLSUM_STATIC_FLOATS
+ * (ncols above about 65,000 columns) return QL_STATUS_BAD_ARG, the sizes in ql_last_error().
+ * Nothing in the scratch has to start at zero: each call writes every partial before reading it.
+ * The first call on a device looks up the scratch's address there (cudaGetSymbolAddress, the
+ * caller's current device) and keeps it; make that first call before any stream capture.
+ * One scratch per device: calls that overlap on a device (other streams or host threads) race
+ * on it and can return wrong sums; serialise them. */
+enum { QL_COLSUM_STATIC_FLOATS = 1048576 };
+int ql_lora_colsum_noalloc(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype,
+                           int64_t n, int ncols, int rank, float scale, int transpose, float* out,
+                           cudaStream_t stream);
+
 /* ---- embedding ---------------------------------------------------------------------------
  * Replaces the embedding lookup of FusedQwen2.step (solution/engine.py:1904-1907):
  * h[t, :] = float(W[ids[t], :]). An id outside [0, vocab) records QL_STATUS_BAD_ARG in the
