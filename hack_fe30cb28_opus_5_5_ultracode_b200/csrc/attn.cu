@@ -47,29 +47,6 @@ __device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t&
                : "r"(smem_u32(p)));
 }
 
-template <typename T>
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  if constexpr (std::is_same<T, __half>::value) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-        "{%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-        "{%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
-  T l = from_f<T>(lo), h = from_f<T>(hi);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&l)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&h)) << 16);
-}
-
 // Loads rows [r0, r0 + ROWS) of a [len, heads, D] sequence slice (row stride ld elements) into a
 // swizzled [ROWS][D] tile; rows at or past len are zero-filled.
 template <typename T, int D, int ROWS, int NT>

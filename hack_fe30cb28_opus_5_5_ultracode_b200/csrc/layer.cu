@@ -161,7 +161,8 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   // input RMSNorm + the dropped LoRA inputs + LoRA-A products
   RmsFwdC r1{};
   r1.x = S.h; r1.w = L.ln1; r1.y = w.a; r1.yq = S.yq; r1.yv = S.yv; r1.rstd = S.rstd1;
-  r1.Aq = L.Aq; r1.Av = L.Av; r1.xq = S.xq; r1.xv = S.xv;
+  r1.Aq = L.Aq; r1.Av = L.Av; r1.xq = S.xq; r1.xv = S.xv; r1.keep_q = S.keep_q;
+  r1.keep_v = S.keep_v;
   r1.n = L.n; r1.H = L.H; r1.rank = L.rank; r1.dtype = dt; r1.eps = L.eps; r1.tok = L.tok;
   fill_drop(L, r1.seed, r1.ctr_q, r1.ctr_v, r1.threads, r1.p_keep, r1.keep_scale, r1.vec,
             r1.drop_q, r1.drop_v);
@@ -265,7 +266,7 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   r1.dy = w.da; r1.ld_dy = L.H; r1.x = S.h; r1.rstd = S.rstd1; r1.w = L.ln1; r1.dres = w.dh2;
   r1.dx = dh_out; r1.dx16 = dh16_out; r1.dxlo_q = w.dxq; r1.dxlo_v = w.dxv; r1.Aq = L.Aq;
   r1.Av = L.Av; r1.n = L.n; r1.H = L.H; r1.rank = L.rank; r1.dtype = dt; r1.grad_scale = 1.f;
-  r1.tok = L.tok;
+  r1.tok = L.tok; r1.keep_q = S.keep_q; r1.keep_v = S.keep_v;
   fill_drop(L, r1.seed, r1.ctr_q, r1.ctr_v, r1.threads, r1.p_keep, r1.keep_scale, r1.vec,
             r1.drop_q, r1.drop_v);
   QL_TRY(rms_bwd(r1, s));

@@ -13,10 +13,13 @@
 // LoRA factors, tq = dx_lo . A (solution/engine.py:1326-1330), rounded like the reference's fp16
 // GEMM output. Optionally also writes dx in the 16-bit type (the next data-gradient GEMM's A).
 //
-// One warp per row, each lane holding groups of 4 consecutive columns in registers (H <= 4096):
-// one HBM read of the row, one write per output; the LoRA factors A (2 x 16 x H 16-bit) are
-// staged in shared memory once per CTA, and the 32 LoRA-A sums of a row leave the warp by one
-// reduce-scatter.
+// CTA tiles of 8 rows, one warp per row, each lane holding groups of 4 consecutive columns in
+// registers (H <= 4096): one HBM read of the row, one write per output. The rank-16 LoRA products
+// run on the tensor cores (mma.sync m16n8k16, fp32 accumulation) over the tile: forward, the
+// dropped rows go to shared memory and 8 warps (2 adapters x 4 quarters of K) multiply them by
+// A^T; backward, tq = dx_lo . A is formed per tile into shared memory before the row pass reads
+// it. The dropout masks can be kept as bits by the forward and read by the backward instead of
+// drawing the Philox numbers again.
 #include "common.cuh"
 #include "profile.h"
 #include "ops.h"
@@ -44,6 +47,8 @@ struct RmsFwdArgs {
   int n, H;
   float eps;
   DropoutArgs drop;
+  uint32_t* keep_q;   // [n, H / 32] or null: masks out as bits
+  uint32_t* keep_v;
 };
 
 struct RmsBwdArgs {
@@ -64,6 +69,8 @@ struct RmsBwdArgs {
   int n, H;
   float grad_scale;
   DropoutArgs drop;
+  const uint32_t* keep_q;  // [n, H / 32] or null: masks in as bits
+  const uint32_t* keep_v;
 };
 
 template <typename T>
@@ -98,105 +105,129 @@ __device__ __forceinline__ float4 masked4(float4 v, uint32_t keep, float s) {
                      (keep & 4u) ? v.z * s : 0.f, (keep & 8u) ? v.w * s : 0.f);
 }
 
-// Sum over the warp of 32 per-lane values v[0..31]; afterwards lane l holds the total of value l
-// (reduce-scatter: 31 shuffles instead of 32 x 5).
-__device__ __forceinline__ float reduce_scatter32(float* v) {
+constexpr int RMS_ROWS = 8;  // rows per CTA tile (one per warp)
+constexpr int RMS_PAD = 8;   // 16-bit elements of padding per shared row: conflict-free fragments
+
+// OR of 4-bit masks over the 8 lanes that share a 32-column word; lane 8j returns word j.
+__device__ __forceinline__ uint32_t gather_bits(uint32_t nib) {
   const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = upper ? v[i] : v[i + off];
-      const float keep = upper ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
+  uint32_t w = nib << (4 * (lane & 7));
+  w |= __shfl_xor_sync(0xffffffffu, w, 1);
+  w |= __shfl_xor_sync(0xffffffffu, w, 2);
+  w |= __shfl_xor_sync(0xffffffffu, w, 4);
+  return w;
 }
 
-// One warp per row (8 rows in flight per CTA, rows strided over the grid); the row's groups of
-// 4 columns g = lane + 32 k stay in registers between the two passes (G = groups per lane).
-// The LoRA-A factors are staged once per CTA in shared memory.
+// Tiles of 8 rows (one warp per row, tiles strided over the grid); the row's groups of 4
+// columns g = lane + 32 k stay in registers between the two passes (G = groups per lane).
 template <typename T, int G>
 __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
   extern __shared__ __align__(16) uint8_t rms_smem[];
-  T* sAq = reinterpret_cast<T*>(rms_smem);
-  T* sAv = sAq + LORA_R * a.H;
-  const int H = a.H, ngroups = H / 4;
+  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
+  T* sY = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] dropped rows (q, v) of the tile
+  float* sRed = reinterpret_cast<float*>(sY + 2 * RMS_ROWS * ld);  // [8 warps][8 rows][16]
   const bool lora_q = a.drop.drop_q && a.Aq != nullptr, lora_v = a.drop.drop_v && a.Av != nullptr;
-  if (lora_q || lora_v) {
-    if (lora_q) stage_to_smem(sAq, a.Aq, LORA_R * H * (int)sizeof(T));
-    if (lora_v) stage_to_smem(sAv, a.Av, LORA_R * H * (int)sizeof(T));
-    stage_wait();
-  }
+  const bool lora = lora_q || lora_v;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {
-    const int64_t base = (int64_t)row * H;
-    float4 xv[G];
-    float ss = 0.f;
+  const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int row = tile * RMS_ROWS + warp;
+    if (row < a.n) {
+      const int64_t base = (int64_t)row * H;
+      float4 xv[G];
+      float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const int gi = lane + 32 * k;
-      if (gi < ngroups) {
-        float4 x = *reinterpret_cast<const float4*>(a.x + base + 4 * gi);
-        if (a.delta != nullptr) {
-          const float4 d = load4<T>(reinterpret_cast<const T*>(a.delta) + base + 4 * gi);
-          x = make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
-          *reinterpret_cast<float4*>(a.xsum + base + 4 * gi) = x;
+      for (int k = 0; k < G; ++k) {
+        const int gi = lane + 32 * k;
+        if (gi < ngroups) {
+          float4 x = *reinterpret_cast<const float4*>(a.x + base + 4 * gi);
+          if (a.delta != nullptr) {
+            const float4 d = load4<T>(reinterpret_cast<const T*>(a.delta) + base + 4 * gi);
+            x = make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
+            *reinterpret_cast<float4*>(a.xsum + base + 4 * gi) = x;
+          }
+          xv[k] = x;
+          ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
         }
-        xv[k] = x;
-        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
       }
-    }
-    ss = warp_sum(ss);
-    const float rstd = 1.0f / sqrtf(ss / (float)H + a.eps);
-    if (lane == 0) a.rstd[row] = rstd;
-    float acc[2 * LORA_R];
+      ss = warp_sum(ss);
+      const float rstd = 1.0f / sqrtf(ss / (float)H + a.eps);
+      if (lane == 0) a.rstd[row] = rstd;
+      const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
+      const int64_t wrow = (int64_t)row * (H / 32);
 #pragma unroll
-    for (int r = 0; r < 2 * LORA_R; ++r) acc[r] = 0.f;
-    const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
-#pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const int gi = lane + 32 * k;
-      if (gi < ngroups) {
-        const int c = 4 * gi;
-        const float4 w = *reinterpret_cast<const float4*>(a.w + c);
-        const float4 x = xv[k];
-        const float4 y = make_float4(w.x * (x.x * rstd), w.y * (x.y * rstd), w.z * (x.z * rstd),
-                                     w.w * (x.w * rstd));
-        if (a.y != nullptr) store4<T>(reinterpret_cast<T*>(a.y) + base + c, y);
-        if (a.drop.drop_q) {
-          const float4 yq = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_q, a.drop), a.drop.keep_scale));
-          if (a.yq != nullptr) store4<T>(reinterpret_cast<T*>(a.yq) + base + c, yq);
-          if (lora_q) {
-#pragma unroll
-            for (int r = 0; r < LORA_R; ++r) {
-              const float4 av = load4<T>(sAq + r * H + c);
-              acc[r] += yq.x * av.x + yq.y * av.y + yq.z * av.z + yq.w * av.w;
-            }
+      for (int k = 0; k < G; ++k) {
+        const int gi = lane + 32 * k;
+        uint32_t nq = 0, nv = 0;
+        if (gi < ngroups) {
+          const int c = 4 * gi;
+          const float4 w = *reinterpret_cast<const float4*>(a.w + c);
+          const float4 x = xv[k];
+          const float4 y = make_float4(w.x * (x.x * rstd), w.y * (x.y * rstd),
+                                       w.z * (x.z * rstd), w.w * (x.w * rstd));
+          if (a.y != nullptr) store4<T>(reinterpret_cast<T*>(a.y) + base + c, y);
+          if (a.drop.drop_q) {
+            nq = keep4(e_row + c, a.drop.ctr_q, a.drop);
+            const float4 yq = masked4(y, nq, a.drop.keep_scale);
+            if (a.yq != nullptr) store4<T>(reinterpret_cast<T*>(a.yq) + base + c, yq);
+            if (lora_q) store4<T>(sY + warp * ld + c, yq);
+          }
+          if (a.drop.drop_v) {
+            nv = keep4(e_row + c, a.drop.ctr_v, a.drop);
+            const float4 yv = masked4(y, nv, a.drop.keep_scale);
+            if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
+            if (lora_v) store4<T>(sY + (RMS_ROWS + warp) * ld + c, yv);
           }
         }
-        if (a.drop.drop_v) {
-          const float4 yv = round4<T>(masked4(y, keep4(e_row + c, a.drop.ctr_v, a.drop), a.drop.keep_scale));
-          if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
-          if (lora_v) {
-#pragma unroll
-            for (int r = 0; r < LORA_R; ++r) {
-              const float4 av = load4<T>(sAv + r * H + c);
-              acc[LORA_R + r] += yv.x * av.x + yv.y * av.y + yv.z * av.z + yv.w * av.w;
-            }
-          }
+        if (a.keep_q != nullptr) {
+          const uint32_t wq = gather_bits(nq);
+          if ((lane & 7) == 0 && gi < ngroups) a.keep_q[wrow + gi / 8] = wq;
+        }
+        if (a.keep_v != nullptr) {
+          const uint32_t wv = gather_bits(nv);
+          if ((lane & 7) == 0 && gi < ngroups) a.keep_v[wrow + gi / 8] = wv;
         }
       }
     }
-    if (lora_q || lora_v) {
-      const float tot = reduce_scatter32(acc);  // lane l: value l (q: 0..15, v: 16..31)
-      if (lane < LORA_R) {
-        if (lora_q) reinterpret_cast<T*>(a.xq)[(int64_t)row * LORA_R + lane] = from_f<T>(tot);
-      } else if (lora_v) {
-        reinterpret_cast<T*>(a.xv)[(int64_t)row * LORA_R + lane - LORA_R] = from_f<T>(tot);
+    if (lora) {
+      // x_lo[8 rows][16] = drop(y)[8][H] . A^T on the tensor cores: warp = (adapter, K quarter);
+      // the tile's 8 rows are rows 0-7 of the 16-row A fragment (rows 8-15 zero).
+      __syncthreads();
+      const int ad = warp >> 2, kq = warp & 3, g = lane >> 2, t = lane & 3;
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if (ad == 0 ? lora_q : lora_v) {
+        const T* A = reinterpret_cast<const T*>(ad == 0 ? a.Aq : a.Av);
+        const T* Y = sY + (ad * RMS_ROWS + g) * ld + 2 * t;
+        const int kper = H / 4;
+#pragma unroll 4
+        for (int k0 = kq * kper; k0 < (kq + 1) * kper; k0 += 16) {
+          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(Y + k0), 0u,
+                                  *reinterpret_cast<const uint32_t*>(Y + k0 + 8), 0u};
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const unsigned int* Ab =
+                reinterpret_cast<const unsigned int*>(A + (int64_t)(nt * 8 + g) * H + k0 + 2 * t);
+            mma16816<T>(acc[nt], af, __ldg(Ab), __ldg(Ab + 4));
+          }
+        }
       }
+      float* red = sRed + (warp * RMS_ROWS + g) * 16 + 2 * t;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        red[nt * 8] = acc[nt][0];
+        red[nt * 8 + 1] = acc[nt][1];
+      }
+      __syncthreads();
+      // thread -> (adapter, row, r): the 4 K quarters added in a fixed order
+      const int ad2 = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
+      const int orow = tile * RMS_ROWS + rr;
+      if (orow < a.n && (ad2 == 0 ? lora_q : lora_v)) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sum += sRed[((ad2 * 4 + q) * RMS_ROWS + rr) * 16 + r];
+        reinterpret_cast<T*>(ad2 == 0 ? a.xq : a.xv)[(int64_t)orow * LORA_R + r] = from_f<T>(sum);
+      }
+      __syncthreads();  // sY and sRed are refilled by the next tile
     }
   }
 }
@@ -204,86 +235,103 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
 template <typename T, int G>
 __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
   extern __shared__ __align__(16) uint8_t rms_smem[];
-  T* sAq = reinterpret_cast<T*>(rms_smem);
-  T* sAv = sAq + LORA_R * a.H;
-  const int H = a.H, ngroups = H / 4;
+  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
+  T* sT = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] tq, tv of the tile (formed in-kernel)
   const bool fq = a.drop.drop_q && a.tq == nullptr, fv = a.drop.drop_v && a.tv == nullptr;
-  if (fq || fv) {
-    if (fq) stage_to_smem(sAq, a.Aq, LORA_R * H * (int)sizeof(T));
-    if (fv) stage_to_smem(sAv, a.Av, LORA_R * H * (int)sizeof(T));
-    stage_wait();
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int row = blockIdx.x * 8 + warp; row < a.n; row += gridDim.x * 8) {
-    const int64_t base = (int64_t)row * H;
-    const float rstd = a.rstd[row];
-    // this row's LoRA input gradients dx_lo (q: lanes 0..15, v: lanes 16..31), broadcast below
-    float lo_mine = 0.f;
-    if (lane < LORA_R) { if (a.dxlo_q != nullptr) lo_mine = a.dxlo_q[(int64_t)row * LORA_R + lane]; }
-    else if (a.dxlo_v != nullptr) lo_mine = a.dxlo_v[(int64_t)row * LORA_R + lane - LORA_R];
-    float lo[2 * LORA_R];
+  const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    if (fq || fv) {
+      // t[8 rows][H] = round16(dx_lo)[8][16] . A[16][H] on the tensor cores, 8-column tiles
+      // strided over the warps; rows 0-7 of the A fragment are the tile's rows.
+      const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int r = 0; r < 2 * LORA_R; ++r) lo[r] = __shfl_sync(0xffffffffu, lo_mine, r);
-    const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
-    float4 gv[G], xh[G];
-    float dot = 0.f;
+      for (int ad = 0; ad < 2; ++ad) {
+        if (!(ad == 0 ? fq : fv)) continue;
+        const float* lo = ad == 0 ? a.dxlo_q : a.dxlo_v;
+        const int r0 = tile * RMS_ROWS + g;
+        uint32_t af[4] = {0u, 0u, 0u, 0u};
+        if (r0 < a.n) {
+          const float2 p0 = *reinterpret_cast<const float2*>(lo + (int64_t)r0 * LORA_R + 2 * t);
+          const float2 p1 = *reinterpret_cast<const float2*>(lo + (int64_t)r0 * LORA_R + 8 + 2 * t);
+          af[0] = pack_t2<T>(p0.x, p0.y);
+          af[2] = pack_t2<T>(p1.x, p1.y);
+        }
+        const unsigned short* Ab =
+            reinterpret_cast<const unsigned short*>(ad == 0 ? a.Aq : a.Av) + g;
+        T* dst = sT + (ad * RMS_ROWS + g) * ld + 2 * t;
+        for (int n0 = warp * 8; n0 < H; n0 += 8 * RMS_ROWS) {
+          const unsigned short* col = Ab + n0;
+          const uint32_t b0 = (uint32_t)__ldg(col + (2 * t) * H) |
+                              ((uint32_t)__ldg(col + (2 * t + 1) * H) << 16);
+          const uint32_t b1 = (uint32_t)__ldg(col + (2 * t + 8) * H) |
+                              ((uint32_t)__ldg(col + (2 * t + 9) * H) << 16);
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816<T>(c, af, b0, b1);
+          *reinterpret_cast<uint32_t*>(dst + n0) = pack_t2<T>(c[0], c[1]);
+        }
+      }
+      __syncthreads();
+    }
+    const int row = tile * RMS_ROWS + warp;
+    if (row < a.n) {
+      const int64_t base = (int64_t)row * H;
+      const float rstd = a.rstd[row];
+      const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
+      const int64_t wrow = (int64_t)row * (H / 32);
+      float4 gv[G], xh[G];
+      float dot = 0.f;
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const int gi = lane + 32 * k;
-      if (gi < ngroups) {
-        const int c = 4 * gi;
-        float4 dy = load4<T>(reinterpret_cast<const T*>(a.dy) + (int64_t)row * a.ld_dy + c);
+      for (int k = 0; k < G; ++k) {
+        const int gi = lane + 32 * k;
+        if (gi < ngroups) {
+          const int c = 4 * gi;
+          float4 dy = load4<T>(reinterpret_cast<const T*>(a.dy) + (int64_t)row * a.ld_dy + c);
 #pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          const bool on = which == 0 ? a.drop.drop_q : a.drop.drop_v;
-          if (!on) continue;
-          const void* tex = which == 0 ? a.tq : a.tv;
-          float4 t;
-          if (tex != nullptr) {
-            t = load4<T>(reinterpret_cast<const T*>(tex) + base + c);
-          } else {
-            const T* At = which == 0 ? sAq : sAv;
-            t = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int r = 0; r < LORA_R; ++r) {
-              const float l = lo[which * LORA_R + r];
-              const float4 av = load4<T>(At + r * H + c);
-              t.x += l * av.x; t.y += l * av.y; t.z += l * av.z; t.w += l * av.w;
-            }
-            t = round4<T>(t);
+          for (int which = 0; which < 2; ++which) {
+            const bool on = which == 0 ? a.drop.drop_q : a.drop.drop_v;
+            if (!on) continue;
+            const void* tex = which == 0 ? a.tq : a.tv;
+            const float4 t = tex != nullptr
+                                 ? load4<T>(reinterpret_cast<const T*>(tex) + base + c)
+                                 : load4<T>(sT + (which * RMS_ROWS + warp) * ld + c);
+            const uint32_t* bits = which == 0 ? a.keep_q : a.keep_v;
+            const uint32_t keep = bits != nullptr
+                                      ? (bits[wrow + c / 32] >> (c & 31)) & 15u
+                                      : keep4(e_row + c, which == 0 ? a.drop.ctr_q : a.drop.ctr_v, a.drop);
+            const float4 m = masked4(t, keep, a.drop.keep_scale);
+            dy = make_float4(dy.x + m.x, dy.y + m.y, dy.z + m.z, dy.w + m.w);
           }
-          const uint32_t keep = keep4(e_row + c, which == 0 ? a.drop.ctr_q : a.drop.ctr_v, a.drop);
-          const float4 m = masked4(t, keep, a.drop.keep_scale);
-          dy = make_float4(dy.x + m.x, dy.y + m.y, dy.z + m.z, dy.w + m.w);
+          const float4 w = *reinterpret_cast<const float4*>(a.w + c);
+          const float4 x = *reinterpret_cast<const float4*>(a.x + base + c);
+          const float4 g = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
+          const float4 h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
+          gv[k] = g;
+          xh[k] = h;
+          dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
         }
-        const float4 w = *reinterpret_cast<const float4*>(a.w + c);
-        const float4 x = *reinterpret_cast<const float4*>(a.x + base + c);
-        const float4 g = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
-        const float4 h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
-        gv[k] = g;
-        xh[k] = h;
-        dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
       }
-    }
-    const float mean = warp_sum(dot) / (float)H;
+      const float mean = warp_sum(dot) / (float)H;
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const int gi = lane + 32 * k;
-      if (gi < ngroups) {
-        const int c = 4 * gi;
-        const float4 g = gv[k], h = xh[k];
-        float4 d = make_float4(rstd * (g.x - h.x * mean) * a.grad_scale,
-                               rstd * (g.y - h.y * mean) * a.grad_scale,
-                               rstd * (g.z - h.z * mean) * a.grad_scale,
-                               rstd * (g.w - h.w * mean) * a.grad_scale);
-        if (a.dres != nullptr) {
-          const float4 r = *reinterpret_cast<const float4*>(a.dres + base + c);
-          d = make_float4(d.x + r.x, d.y + r.y, d.z + r.z, d.w + r.w);
+      for (int k = 0; k < G; ++k) {
+        const int gi = lane + 32 * k;
+        if (gi < ngroups) {
+          const int c = 4 * gi;
+          const float4 g = gv[k], h = xh[k];
+          float4 d = make_float4(rstd * (g.x - h.x * mean) * a.grad_scale,
+                                 rstd * (g.y - h.y * mean) * a.grad_scale,
+                                 rstd * (g.z - h.z * mean) * a.grad_scale,
+                                 rstd * (g.w - h.w * mean) * a.grad_scale);
+          if (a.dres != nullptr) {
+            const float4 r = *reinterpret_cast<const float4*>(a.dres + base + c);
+            d = make_float4(d.x + r.x, d.y + r.y, d.z + r.z, d.w + r.w);
+          }
+          *reinterpret_cast<float4*>(a.dx + base + c) = d;
+          if (a.dx16 != nullptr) store4<T>(reinterpret_cast<T*>(a.dx16) + base + c, d);
         }
-        *reinterpret_cast<float4*>(a.dx + base + c) = d;
-        if (a.dx16 != nullptr) store4<T>(reinterpret_cast<T*>(a.dx16) + base + c, d);
       }
     }
+    if (fq || fv) __syncthreads();  // sT is refilled by the next tile
   }
 }
 
@@ -314,11 +362,14 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   RmsFwdArgs a{c.x, c.delta, c.w, c.xsum, c.y, c.yq, c.yv, c.rstd, c.Aq, c.Av, c.xq, c.xv, c.n,
                c.H, c.eps,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
-                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}}};
+                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}},
+               c.drop_q ? c.keep_q : nullptr, c.drop_v ? c.keep_v : nullptr};
   if (c.vec != 4 && c.vec != 8) return QL_STATUS_BAD_ARG;
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.Aq != nullptr) || (c.drop_v && c.Av != nullptr);
-  const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
+  if (lora && c.H % 64 != 0) return QL_STATUS_UNSUPPORTED;  // 4 K quarters of 16-wide steps
+  if ((a.keep_q != nullptr || a.keep_v != nullptr) && c.H % 32 != 0) return QL_STATUS_BAD_ARG;
+  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 + RMS_ROWS * RMS_ROWS * LORA_R * 4 : 0;
   const int grid = rms_grid(c.n);
 #define QL_RMSF(TT, GG)                                              \
   do {                                                               \
@@ -352,10 +403,13 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   RmsBwdArgs a{c.dy, c.ld_dy, c.x, c.rstd, c.w, c.dres, c.dx, c.dx16, c.tq, c.tv, c.dxlo_q,
                c.dxlo_v, c.Aq, c.Av, c.n, c.H, c.grad_scale,
                DropoutArgs{c.tok, c.seed, c.ctr_q, c.ctr_v, c.threads > 0 ? c.threads : 1,
-                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}}};
+                           c.p_keep, c.keep_scale, c.vec, c.drop_q, c.drop_v, FastDiv{}},
+               c.keep_q, c.keep_v};
+  if ((c.keep_q != nullptr || c.keep_v != nullptr) && c.H % 32 != 0) return QL_STATUS_BAD_ARG;
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.tq == nullptr) || (c.drop_v && c.tv == nullptr);
-  const int smem = lora ? 2 * LORA_R * c.H * 2 : 0;
+  if (lora && c.H % 8 != 0) return QL_STATUS_UNSUPPORTED;  // 8-column tensor-core tiles
+  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 : 0;
   const int grid = rms_grid(c.n);
 #define QL_RMSB(TT, GG)                                              \
   do {                                                               \

@@ -623,7 +623,8 @@ class _SavedArena:
         sizes = [("rstd1", n * 4), ("yq", n * H * e), ("yv", n * H * e), ("xq", n * 16 * e),
                  ("xv", n * 16 * e), ("q", n * HQ * D * e), ("k", n * HKV * D * e),
                  ("v", n * HKV * D * e), ("out", n * HQ * D * e), ("lse", HQ * n * 4),
-                 ("h2", n * H * 4), ("rstd2", n * 4), ("gu", n * 2 * I * e)]
+                 ("h2", n * H * 4), ("rstd2", n * 4), ("gu", n * 2 * I * e),
+                 ("keep_q", n * (H // 32) * 4), ("keep_v", n * (H // 32) * 4)]
         self.fields, off = {}, 0
         for name, b in sizes:
             self.fields[name] = off

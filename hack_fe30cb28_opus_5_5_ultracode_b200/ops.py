@@ -160,9 +160,10 @@ def dropout_keep(nelem, seed, ctr, threads, p, vec=4, device="cuda"):
 
 
 def rms_fwd(x, w, eps, dtype=torch.float16, delta=None, write_y=True, drop=None, Aq=None,
-            Av=None, want_yq=False, out_y=None, out_xsum=None):
+            Av=None, want_yq=False, out_y=None, out_xsum=None, keep_bits=None):
     """(xsum, y, yq, yv, rstd, xq, xv) of reference _rms_fwd (engine.py:947-966), with the
-    LoRA-A products xq / xv when Aq / Av are given."""
+    LoRA-A products xq / xv when Aq / Av are given. keep_bits: (keep_q, keep_v) int32
+    [n, H / 32] tensors (or None) that receive the dropout masks as bits."""
     n, H = x.shape
     dev = x.device
     xsum = (out_xsum if out_xsum is not None else torch.empty_like(x)) if delta is not None else x
@@ -180,6 +181,8 @@ def rms_fwd(x, w, eps, dtype=torch.float16, delta=None, write_y=True, drop=None,
                   Aq=_ptr(Aq) if dq else None, Av=_ptr(Av) if dv else None, xq=_ptr(xq),
                   xv=_ptr(xv), n=n, H=H, rank=16, dtype=dtype_code(dtype), eps=float(eps),
                   vec=4)
+    if keep_bits is not None:
+        fields.update(keep_q=_ptr(keep_bits[0]), keep_v=_ptr(keep_bits[1]))
     if drop is not None:
         fields.update(drop.fields())
     args = _lib.struct("ql_rms_fwd_args", **fields)
@@ -188,14 +191,18 @@ def rms_fwd(x, w, eps, dtype=torch.float16, delta=None, write_y=True, drop=None,
 
 
 def rms_bwd(dy, x, rstd, w, dtype=torch.float16, dres=None, tq=None, tv=None, dxlo_q=None,
-            dxlo_v=None, Aq=None, Av=None, drop=None, grad_scale=1.0, out=None, out16=None):
-    """Reference _rms_bwd (engine.py:969-981); dx fp32 (and its 16-bit copy into out16)."""
+            dxlo_v=None, Aq=None, Av=None, drop=None, grad_scale=1.0, out=None, out16=None,
+            keep_bits=None):
+    """Reference _rms_bwd (engine.py:969-981); dx fp32 (and its 16-bit copy into out16).
+    keep_bits: the forward's (keep_q, keep_v) mask bits, read instead of redrawing the masks."""
     n, H = x.shape
     dx = out if out is not None else torch.empty_like(x)
     fields = dict(dy=_ptr(dy), ld_dy=dy.stride(0), x=_ptr(x), rstd=_ptr(rstd), w=_ptr(w),
                   dres=_ptr(dres), dx=_ptr(dx), dx16=_ptr(out16), tq=_ptr(tq), tv=_ptr(tv),
                   dxlo_q=_ptr(dxlo_q), dxlo_v=_ptr(dxlo_v), Aq=_ptr(Aq), Av=_ptr(Av), n=n, H=H,
                   rank=16, dtype=dtype_code(dtype), grad_scale=float(grad_scale), vec=4)
+    if keep_bits is not None:
+        fields.update(keep_q=_ptr(keep_bits[0]), keep_v=_ptr(keep_bits[1]))
     if drop is not None:
         fields.update(drop.fields())
     args = _lib.struct("ql_rms_bwd_args", **fields)

@@ -112,6 +112,8 @@ typedef struct {
   int32_t vec, drop_q, drop_v;
   const int64_t* tok;   /* [n] */
   int64_t seed, ctr_q, ctr_v, threads;
+  uint32_t* keep_q;     /* [n, H / 32] or NULL: the q / v dropout masks as bits (column c: bit */
+  uint32_t* keep_v;     /* c % 32 of word c / 32), kept for the backward; H % 32 == 0 */
 } ql_rms_fwd_args;
 
 typedef struct {
@@ -135,13 +137,16 @@ typedef struct {
   int32_t vec, drop_q, drop_v;
   const int64_t* tok;
   int64_t seed, ctr_q, ctr_v, threads;
+  const uint32_t* keep_q;  /* [n, H / 32] or NULL: masks written by the forward (else the */
+  const uint32_t* keep_v;  /* Philox draws are regenerated) */
 } ql_rms_bwd_args;
 
 /* Replaces _rms_fwd + rms_fwd_kernel (solution/engine.py:947-966, solution/kernels.py:145-175)
- * and the LoRA-A GEMMs xq = aq @ A^T (solution/engine.py:1088-1093). */
+ * and the LoRA-A GEMMs xq = aq @ A^T (solution/engine.py:1088-1093). With Aq / Av, H % 64 == 0. */
 int ql_rms_fwd(const ql_rms_fwd_args* args, cudaStream_t stream);
 /* Replaces _rms_bwd + rms_bwd_kernel (solution/engine.py:969-981, solution/kernels.py:178-205)
- * and the tq = dx_lo @ A GEMMs (solution/engine.py:1326-1330). */
+ * and the tq = dx_lo @ A GEMMs (solution/engine.py:1326-1330): dx_lo is rounded to the 16-bit
+ * type (the reference's fp16 dx_lo) and tq to the 16-bit type. */
 int ql_rms_bwd(const ql_rms_bwd_args* args, cudaStream_t stream);
 /* The keep mask (int8 0/1) of elements 0 .. nelem-1 of one dropout call; replaces
  * torch_dropout_keep_kernel (solution/kernels.py:129-135). */
@@ -379,6 +384,8 @@ typedef struct {              /* what the forward keeps for the backward (all [n
   float* h2;                  /* [n, H] residual after attention */
   float* rstd2;               /* [n] */
   void* gu;                   /* [n, 2 I] [gate | up] (overwritten by its gradient in backward) */
+  uint32_t* keep_q;           /* [n, H / 32] dropout masks of the q / v LoRA inputs as bits */
+  uint32_t* keep_v;
 } ql_layer_saved;
 
 /* Workspace bytes of the forward (backward = 0) or backward (backward = 1) of a layer. Its first

@@ -118,8 +118,9 @@ def test_rms_fused_lora_matches_torch(n, H, dtype):
     dres = torch.randn(n, H, device=DEV)
     dxlo_q = torch.randn(n, 16, device=DEV)
     dxlo_v = torch.randn(n, 16, device=DEV)
-    tq = (dxlo_q @ Aq.float()).to(dtype)
-    tv = (dxlo_v @ Av.float()).to(dtype)
+    # dx_lo in the 16-bit type, as the reference's fp16 LoRA GEMMs hold it
+    tq = (dxlo_q.to(dtype).float() @ Aq.float()).to(dtype)
+    tv = (dxlo_v.to(dtype).float() @ Av.float()).to(dtype)
     d16 = torch.empty(n, H, device=DEV, dtype=dtype)
     dx_a = o.rms_bwd(dy, xsum, rstd, w, dtype=dtype, dres=dres, dxlo_q=dxlo_q, dxlo_v=dxlo_v,
                      Aq=Aq, Av=Av, drop=drop, grad_scale=0.5, out16=d16)
@@ -130,6 +131,35 @@ def test_rms_fused_lora_matches_torch(n, H, dtype):
     (gx,) = torch.autograd.grad(yr, xr, g_total)
     close(dx_b, dres + 0.5 * gx, 2e-3)
     close(d16, dx_a, tol)
+
+
+@pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584)])
+def test_rms_mask_bits_match_redrawn_masks(n, H):
+    """The forward's mask bits are the Philox masks; a backward that reads them equals one that
+    draws the masks again, bit for bit."""
+    o = ops()
+    torch.manual_seed(1)
+    x = torch.randn(n, H, device=DEV)
+    w = torch.rand(H, device=DEV) + 0.5
+    Aq = (torch.randn(16, H, device=DEV) * 0.05).half()
+    Av = (torch.randn(16, H, device=DEV) * 0.05).half()
+    tok = (torch.arange(n, device=DEV) * 5 + 2).long()
+    drop = o.Drop(tok, 91, 21, 22, 1184 * 256, 0.3)
+    bits = (torch.full((n, H // 32), -1, device=DEV, dtype=torch.int32),
+            torch.full((n, H // 32), -1, device=DEV, dtype=torch.int32))
+    _, _, yq, yv, rstd, xq, xv = o.rms_fwd(x, w, 1e-6, drop=drop, Aq=Aq, Av=Av, want_yq=True,
+                                           keep_bits=bits)
+    cols = torch.arange(H, device=DEV)
+    for b, y in zip(bits, (yq, yv)):
+        kept = ((b[:, cols // 32] >> (cols % 32)) & 1).bool()
+        assert torch.equal(kept, y != 0)
+    dy = torch.randn(n, H, device=DEV).half()
+    dxlo_q = torch.randn(n, 16, device=DEV)
+    dxlo_v = torch.randn(n, 16, device=DEV)
+    kw = dict(dxlo_q=dxlo_q, dxlo_v=dxlo_v, Aq=Aq, Av=Av, drop=drop)
+    a = o.rms_bwd(dy, x, rstd, w, **kw)
+    b = o.rms_bwd(dy, x, rstd, w, keep_bits=bits, **kw)
+    assert torch.equal(a, b)
 
 
 # ---------------------------------------------------------------------------------------------
