@@ -118,27 +118,32 @@ __device__ __forceinline__ uint32_t gather_bits(uint32_t nib) {
   return w;
 }
 
-// Tiles of 8 rows (one warp per row, tiles strided over the grid); the row's groups of 4
-// columns g = lane + 32 k stay in registers between the two passes (G = groups per lane).
-template <typename T, int G>
-__global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
+// Tiles of 8 rows, tiles strided over the grid. WPR warps share a row (8 x WPR warps per CTA):
+// warp w works on row w / WPR, and its lanes hold the row's groups of 4 columns
+// gi = 32 (w % WPR) + lane + 32 WPR k (k < G) in registers between the two passes.
+template <typename T, int G, int WPR>
+__global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
+  constexpr int NW = RMS_ROWS * WPR, SL = NW / 2;  // warps; K slices per adapter
   extern __shared__ __align__(16) uint8_t rms_smem[];
+  __shared__ float sSS[NW];
   const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
   T* sY = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] dropped rows (q, v) of the tile
-  float* sRed = reinterpret_cast<float*>(sY + 2 * RMS_ROWS * ld);  // [8 warps][8 rows][16]
+  float* sRed = reinterpret_cast<float*>(sY + 2 * RMS_ROWS * ld);  // [NW][8 rows][16]
   const bool lora_q = a.drop.drop_q && a.Aq != nullptr, lora_v = a.drop.drop_v && a.Av != nullptr;
   const bool lora = lora_q || lora_v;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rrow = warp / WPR, part = warp % WPR;
   const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int row = tile * RMS_ROWS + warp;
-    if (row < a.n) {
-      const int64_t base = (int64_t)row * H;
-      float4 xv[G];
-      float ss = 0.f;
+    const int row = tile * RMS_ROWS + rrow;
+    const bool live = row < a.n;
+    const int64_t base = (int64_t)row * H;
+    float4 xv[G];
+    float ss = 0.f;
+    if (live) {
 #pragma unroll
       for (int k = 0; k < G; ++k) {
-        const int gi = lane + 32 * k;
+        const int gi = 32 * part + lane + 32 * WPR * k;
         if (gi < ngroups) {
           float4 x = *reinterpret_cast<const float4*>(a.x + base + 4 * gi);
           if (a.delta != nullptr) {
@@ -150,14 +155,23 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
           ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
         }
       }
-      ss = warp_sum(ss);
+    }
+    ss = warp_sum(ss);
+    if constexpr (WPR > 1) {  // the row's warps add their sums in a fixed order
+      if (lane == 0) sSS[warp] = ss;
+      __syncthreads();
+      ss = 0.f;
+#pragma unroll
+      for (int p = 0; p < WPR; ++p) ss += sSS[rrow * WPR + p];
+    }
+    if (live) {
       const float rstd = 1.0f / sqrtf(ss / (float)H + a.eps);
-      if (lane == 0) a.rstd[row] = rstd;
+      if (lane == 0 && part == 0) a.rstd[row] = rstd;
       const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
       const int64_t wrow = (int64_t)row * (H / 32);
 #pragma unroll
       for (int k = 0; k < G; ++k) {
-        const int gi = lane + 32 * k;
+        const int gi = 32 * part + lane + 32 * WPR * k;
         uint32_t nq = 0, nv = 0;
         if (gi < ngroups) {
           const int c = 4 * gi;
@@ -170,13 +184,13 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
             nq = keep4(e_row + c, a.drop.ctr_q, a.drop);
             const float4 yq = masked4(y, nq, a.drop.keep_scale);
             if (a.yq != nullptr) store4<T>(reinterpret_cast<T*>(a.yq) + base + c, yq);
-            if (lora_q) store4<T>(sY + warp * ld + c, yq);
+            if (lora_q) store4<T>(sY + rrow * ld + c, yq);
           }
           if (a.drop.drop_v) {
             nv = keep4(e_row + c, a.drop.ctr_v, a.drop);
             const float4 yv = masked4(y, nv, a.drop.keep_scale);
             if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
-            if (lora_v) store4<T>(sY + (RMS_ROWS + warp) * ld + c, yv);
+            if (lora_v) store4<T>(sY + (RMS_ROWS + rrow) * ld + c, yv);
           }
         }
         if (a.keep_q != nullptr) {
@@ -190,17 +204,17 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
       }
     }
     if (lora) {
-      // x_lo[8 rows][16] = drop(y)[8][H] . A^T on the tensor cores: warp = (adapter, K quarter);
+      // x_lo[8 rows][16] = drop(y)[8][H] . A^T on the tensor cores: warp = (adapter, K slice);
       // the tile's 8 rows are rows 0-7 of the 16-row A fragment (rows 8-15 zero).
       __syncthreads();
-      const int ad = warp >> 2, kq = warp & 3, g = lane >> 2, t = lane & 3;
+      const int ad = warp / SL, ks = warp % SL, g = lane >> 2, t = lane & 3;
       float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       if (ad == 0 ? lora_q : lora_v) {
         const T* A = reinterpret_cast<const T*>(ad == 0 ? a.Aq : a.Av);
         const T* Y = sY + (ad * RMS_ROWS + g) * ld + 2 * t;
-        const int kper = H / 4;
+        const int kper = H / SL;
 #pragma unroll 4
-        for (int k0 = kq * kper; k0 < (kq + 1) * kper; k0 += 16) {
+        for (int k0 = ks * kper; k0 < (ks + 1) * kper; k0 += 16) {
           const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(Y + k0), 0u,
                                   *reinterpret_cast<const uint32_t*>(Y + k0 + 8), 0u};
 #pragma unroll
@@ -218,27 +232,32 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(RmsFwdArgs a) {
         red[nt * 8 + 1] = acc[nt][1];
       }
       __syncthreads();
-      // thread -> (adapter, row, r): the 4 K quarters added in a fixed order
-      const int ad2 = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
-      const int orow = tile * RMS_ROWS + rr;
-      if (orow < a.n && (ad2 == 0 ? lora_q : lora_v)) {
-        float sum = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sum += sRed[((ad2 * 4 + q) * RMS_ROWS + rr) * 16 + r];
-        reinterpret_cast<T*>(ad2 == 0 ? a.xq : a.xv)[(int64_t)orow * LORA_R + r] = from_f<T>(sum);
+      // thread -> (adapter, row, r): the K slices added in a fixed order
+      if (threadIdx.x < 2 * RMS_ROWS * LORA_R) {
+        const int ad2 = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
+        const int orow = tile * RMS_ROWS + rr;
+        if (orow < a.n && (ad2 == 0 ? lora_q : lora_v)) {
+          float sum = 0.f;
+#pragma unroll 4
+          for (int q = 0; q < SL; ++q) sum += sRed[((ad2 * SL + q) * RMS_ROWS + rr) * 16 + r];
+          reinterpret_cast<T*>(ad2 == 0 ? a.xq : a.xv)[(int64_t)orow * LORA_R + r] = from_f<T>(sum);
+        }
       }
-      __syncthreads();  // sY and sRed are refilled by the next tile
     }
+    __syncthreads();  // shared buffers are refilled by the next tile
   }
 }
 
-template <typename T, int G>
-__global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
+template <typename T, int G, int WPR>
+__global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
+  constexpr int NW = RMS_ROWS * WPR;
   extern __shared__ __align__(16) uint8_t rms_smem[];
+  __shared__ float sDot[NW];
   const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
   T* sT = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] tq, tv of the tile (formed in-kernel)
   const bool fq = a.drop.drop_q && a.tq == nullptr, fv = a.drop.drop_v && a.tv == nullptr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rrow = warp / WPR, part = warp % WPR;
   const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     if (fq || fv) {
@@ -260,7 +279,7 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
         const unsigned short* Ab =
             reinterpret_cast<const unsigned short*>(ad == 0 ? a.Aq : a.Av) + g;
         T* dst = sT + (ad * RMS_ROWS + g) * ld + 2 * t;
-        for (int n0 = warp * 8; n0 < H; n0 += 8 * RMS_ROWS) {
+        for (int n0 = warp * 8; n0 < H; n0 += 8 * NW) {
           const unsigned short* col = Ab + n0;
           const uint32_t b0 = (uint32_t)__ldg(col + (2 * t) * H) |
                               ((uint32_t)__ldg(col + (2 * t + 1) * H) << 16);
@@ -273,17 +292,19 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
       }
       __syncthreads();
     }
-    const int row = tile * RMS_ROWS + warp;
-    if (row < a.n) {
-      const int64_t base = (int64_t)row * H;
-      const float rstd = a.rstd[row];
+    const int row = tile * RMS_ROWS + rrow;
+    const bool live = row < a.n;
+    const int64_t base = (int64_t)row * H;
+    float rstd = 0.f;
+    float4 gv[G], xh[G];
+    float dot = 0.f;
+    if (live) {
+      rstd = a.rstd[row];
       const int64_t e_row = (a.drop.drop_q || a.drop.drop_v) ? a.drop.tok[row] * (int64_t)H : 0;
       const int64_t wrow = (int64_t)row * (H / 32);
-      float4 gv[G], xh[G];
-      float dot = 0.f;
 #pragma unroll
       for (int k = 0; k < G; ++k) {
-        const int gi = lane + 32 * k;
+        const int gi = 32 * part + lane + 32 * WPR * k;
         if (gi < ngroups) {
           const int c = 4 * gi;
           float4 dy = load4<T>(reinterpret_cast<const T*>(a.dy) + (int64_t)row * a.ld_dy + c);
@@ -294,7 +315,7 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
             const void* tex = which == 0 ? a.tq : a.tv;
             const float4 t = tex != nullptr
                                  ? load4<T>(reinterpret_cast<const T*>(tex) + base + c)
-                                 : load4<T>(sT + (which * RMS_ROWS + warp) * ld + c);
+                                 : load4<T>(sT + (which * RMS_ROWS + rrow) * ld + c);
             const uint32_t* bits = which == 0 ? a.keep_q : a.keep_v;
             const uint32_t keep = bits != nullptr
                                       ? (bits[wrow + c / 32] >> (c & 31)) & 15u
@@ -311,10 +332,20 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
           dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
         }
       }
-      const float mean = warp_sum(dot) / (float)H;
+    }
+    dot = warp_sum(dot);
+    if constexpr (WPR > 1) {
+      if (lane == 0) sDot[warp] = dot;
+      __syncthreads();
+      dot = 0.f;
+#pragma unroll
+      for (int p = 0; p < WPR; ++p) dot += sDot[rrow * WPR + p];
+    }
+    if (live) {
+      const float mean = dot / (float)H;
 #pragma unroll
       for (int k = 0; k < G; ++k) {
-        const int gi = lane + 32 * k;
+        const int gi = 32 * part + lane + 32 * WPR * k;
         if (gi < ngroups) {
           const int c = 4 * gi;
           const float4 g = gv[k], h = xh[k];
@@ -331,7 +362,7 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(RmsBwdArgs a) {
         }
       }
     }
-    if (fq || fv) __syncthreads();  // sT is refilled by the next tile
+    __syncthreads();  // shared buffers are refilled by the next tile
   }
 }
 
@@ -343,6 +374,10 @@ static int rms_grid(int64_t n) {
   const int64_t cap = (int64_t)sms * 4;
   return (int)(want < cap ? want : cap);
 }
+
+// Warps per row: 4 for rows of 1024..2048 columns (more warps in flight over the few rows of a
+// step, 4 groups per lane), else 1.
+static int rms_wpr(int H) { return (H >= 1024 && H <= 2048 && H % 256 == 0) ? 4 : 1; }
 
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
 template <typename K>
@@ -367,21 +402,25 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   if (c.vec != 4 && c.vec != 8) return QL_STATUS_BAD_ARG;
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.Aq != nullptr) || (c.drop_v && c.Av != nullptr);
-  if (lora && c.H % 64 != 0) return QL_STATUS_UNSUPPORTED;  // 4 K quarters of 16-wide steps
   if ((a.keep_q != nullptr || a.keep_v != nullptr) && c.H % 32 != 0) return QL_STATUS_BAD_ARG;
-  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 + RMS_ROWS * RMS_ROWS * LORA_R * 4 : 0;
+  const int wpr = rms_wpr(c.H);
+  if (lora && c.H % (64 * wpr) != 0) return QL_STATUS_UNSUPPORTED;
+  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 + RMS_ROWS * wpr * RMS_ROWS * LORA_R * 4 : 0;
   const int grid = rms_grid(c.n);
-#define QL_RMSF(TT, GG)                                              \
-  do {                                                               \
-    set_smem(rms_fwd_kernel<TT, GG>, smem);                          \
-    rms_fwd_kernel<TT, GG><<<grid, 256, smem, s>>>(a);               \
+#define QL_RMSF(TT, GG, WW)                                           \
+  do {                                                                \
+    set_smem(rms_fwd_kernel<TT, GG, WW>, smem);                       \
+    rms_fwd_kernel<TT, GG, WW><<<grid, 256 * WW, smem, s>>>(a);       \
   } while (0)
-  const int G = (int)cdiv(c.H / 4, 32);
+  const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
-    if (G <= 4) QL_RMSF(__half, 4); else if (G <= 12) QL_RMSF(__half, 12); else QL_RMSF(__half, 32);
+    if (wpr == 4) QL_RMSF(__half, 4, 4);
+    else if (G <= 4) QL_RMSF(__half, 4, 1); else if (G <= 12) QL_RMSF(__half, 12, 1);
+    else QL_RMSF(__half, 32, 1);
   } else if (c.dtype == QL_BF16) {
-    if (G <= 4) QL_RMSF(__nv_bfloat16, 4); else if (G <= 12) QL_RMSF(__nv_bfloat16, 12);
-    else QL_RMSF(__nv_bfloat16, 32);
+    if (wpr == 4) QL_RMSF(__nv_bfloat16, 4, 4);
+    else if (G <= 4) QL_RMSF(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSF(__nv_bfloat16, 12, 1);
+    else QL_RMSF(__nv_bfloat16, 32, 1);
   } else {
     return QL_STATUS_BAD_ARG;
   }
@@ -409,19 +448,23 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.tq == nullptr) || (c.drop_v && c.tv == nullptr);
   if (lora && c.H % 8 != 0) return QL_STATUS_UNSUPPORTED;  // 8-column tensor-core tiles
+  const int wpr = rms_wpr(c.H);
   const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 : 0;
   const int grid = rms_grid(c.n);
-#define QL_RMSB(TT, GG)                                              \
-  do {                                                               \
-    set_smem(rms_bwd_kernel<TT, GG>, smem);                          \
-    rms_bwd_kernel<TT, GG><<<grid, 256, smem, s>>>(a);               \
+#define QL_RMSB(TT, GG, WW)                                           \
+  do {                                                                \
+    set_smem(rms_bwd_kernel<TT, GG, WW>, smem);                       \
+    rms_bwd_kernel<TT, GG, WW><<<grid, 256 * WW, smem, s>>>(a);       \
   } while (0)
-  const int G = (int)cdiv(c.H / 4, 32);
+  const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
-    if (G <= 4) QL_RMSB(__half, 4); else if (G <= 12) QL_RMSB(__half, 12); else QL_RMSB(__half, 32);
+    if (wpr == 4) QL_RMSB(__half, 4, 4);
+    else if (G <= 4) QL_RMSB(__half, 4, 1); else if (G <= 12) QL_RMSB(__half, 12, 1);
+    else QL_RMSB(__half, 32, 1);
   } else if (c.dtype == QL_BF16) {
-    if (G <= 4) QL_RMSB(__nv_bfloat16, 4); else if (G <= 12) QL_RMSB(__nv_bfloat16, 12);
-    else QL_RMSB(__nv_bfloat16, 32);
+    if (wpr == 4) QL_RMSB(__nv_bfloat16, 4, 4);
+    else if (G <= 4) QL_RMSB(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSB(__nv_bfloat16, 12, 1);
+    else QL_RMSB(__nv_bfloat16, 32, 1);
   } else {
     return QL_STATUS_BAD_ARG;
   }
