@@ -1,4 +1,4 @@
-// qkv + LoRA + rotary embedding, forward and backward, one CTA per token.
+// qkv + LoRA + rotary embedding, forward and backward, CTA tiles of 8 tokens.
 //
 // Forward (reference qkv_rope_fwd_kernel, solution/kernels.py:212-264): splits the biased qkv
 // GEMM output into q, k, v, adds lora_scale * (the LoRA-B output) to q and v in fp32, and rotates
@@ -42,230 +42,244 @@ __device__ __forceinline__ void st8(T* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(h);
 }
 
-// lo[j] = sum_r x[r] B[idx + j][r] for 8 consecutive rows of a [rows, 16] factor in smem,
-// rounded to the 16-bit type (the reference's fp16 GEMM output).
-template <typename T>
-__device__ __forceinline__ void lora_rows8(const T* B, int idx, const float* x, float* lo) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)(idx + j) * RANK);
-    const uint4 u0 = b4[0], u1 = b4[1];
-    const T* b0 = reinterpret_cast<const T*>(&u0);
-    const T* b1 = reinterpret_cast<const T*>(&u1);
-    float acc = 0.f;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc += x[r] * to_f<T>(b0[r]);
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc += x[8 + r] * to_f<T>(b1[r]);
-    lo[j] = to_f<T>(from_f<T>(acc));
-  }
-}
+constexpr int ROPE_ROWS = 8;  // tokens per CTA tile
+constexpr int ROPE_WPR = 2;   // warps per token
 
-// One warp per token (8 per CTA, tokens strided over the grid). A lane takes chunks of 8
-// consecutive positions d .. d+7 of the first half of a head together with their partners
-// d + D/2 (16-byte loads and stores); the LoRA-B factors sit in shared memory.
+// Tiles of 8 tokens (tiles strided over the grid), 2 warps per token. With LoRA, the tile's
+// LoRA-B outputs lq / lv = x_lo . B^T are formed first on the tensor cores (mma.sync m16n8k16,
+// fp32 accumulation; the 8 tokens are rows 0-7 of the A fragment), rounded to the 16-bit type
+// into shared memory. Then the warps of a token take chunks of 8 consecutive positions d .. d+7
+// of the first half of a head together with their partners d + D/2 (16-byte loads and stores).
 template <typename T>
-__global__ void __launch_bounds__(256) rope_fwd_kernel(RopeFwdC a) {
+__global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
+  constexpr int NW = ROPE_ROWS * ROPE_WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
-  const int C = (HQ + 2 * HKV) * D;
-  T* sBq = reinterpret_cast<T*>(rope_smem);
-  T* sBv = sBq + (int64_t)HQ * D * RANK;
+  const int C = (HQ + 2 * HKV) * D, QD = HQ * D, VD = HKV * D, ld = QD + VD + 8;
+  T* sL = reinterpret_cast<T*>(rope_smem);  // [8][ld]: [lq | lv] of the tile's tokens
   const bool fq = a.lq == nullptr && a.xq != nullptr, fv = a.lv == nullptr && a.xv != nullptr;
-  if (fq || fv) {
-    if (fq) stage_to_smem(sBq, a.Bq, HQ * D * RANK * (int)sizeof(T));
-    if (fv) stage_to_smem(sBv, a.Bv, HKV * D * RANK * (int)sizeof(T));
-    stage_wait();
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rrow = warp / ROPE_WPR, part = warp % ROPE_WPR;
   const float s = a.lora_scale;
   const int cph = HALF / 8;                 // chunks per head
   const int rot_chunks = (HQ + HKV) * cph;  // q and k heads
-  const int v_chunks = HKV * D / 8;
-  for (int64_t tok = blockIdx.x * 8 + warp; tok < a.n; tok += (int64_t)gridDim.x * 8) {
-    const T* row = reinterpret_cast<const T*>(a.qkv) + tok * C;
-    float mine = 0.f;
-    if (lane < RANK) { if (fq) mine = to_f<T>(reinterpret_cast<const T*>(a.xq)[tok * RANK + lane]); }
-    else if (fv) mine = to_f<T>(reinterpret_cast<const T*>(a.xv)[tok * RANK + lane - RANK]);
-    float xl[2 * RANK];
-#pragma unroll
-    for (int r = 0; r < 2 * RANK; ++r) xl[r] = __shfl_sync(0xffffffffu, mine, r);
-    const int pos = a.pos[tok];
-    const float* cs = a.cos + (int64_t)pos * HALF;
-    const float* sn = a.sin + (int64_t)pos * HALF;
-#pragma unroll 2
-    for (int ch = lane; ch < rot_chunks; ch += 32) {
-      const int hh = ch / cph, d = (ch % cph) * 8;
-      const bool is_q = hh < HQ;
-      const int src = hh * D + d;
-      float x1[8], x2[8], c[8], sv[8];
-      ld8<T>(row + src, x1);
-      ld8<T>(row + src + HALF, x2);
-      ld8<float>(cs + d, c);
-      ld8<float>(sn + d, sv);
-      if (is_q && (a.lq != nullptr || fq)) {
-        float l1[8], l2[8];
-        if (a.lq != nullptr) {
-          const T* lq = reinterpret_cast<const T*>(a.lq) + tok * HQ * D;
-          ld8<T>(lq + src, l1);
-          ld8<T>(lq + src + HALF, l2);
-        } else {
-          lora_rows8<T>(sBq, src, xl, l1);
-          lora_rows8<T>(sBq, src + HALF, xl, l2);
+  const int v_chunks = VD / 8;
+  const int ntiles = (a.n + ROPE_ROWS - 1) / ROPE_ROWS;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    if (fq || fv) {
+      const int g = lane >> 2, t = lane & 3;
+      const int tg = tile * ROPE_ROWS + g;
+      uint32_t aq[4] = {0u, 0u, 0u, 0u}, av[4] = {0u, 0u, 0u, 0u};
+      if (tg < a.n) {
+        if (fq) {
+          const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xq) + (int64_t)tg * RANK);
+          aq[0] = x[t];
+          aq[2] = x[4 + t];
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { x1[j] += l1[j] * s; x2[j] += l2[j] * s; }
+        if (fv) {
+          const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xv) + (int64_t)tg * RANK);
+          av[0] = x[t];
+          av[2] = x[4 + t];
+        }
       }
-      float o1[8], o2[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o1[j] = x1[j] * c[j] - x2[j] * sv[j];
-        o2[j] = x2[j] * c[j] + x1[j] * sv[j];
+      for (int n0 = warp * 8; n0 < QD + VD; n0 += 8 * NW) {
+        const bool isq = n0 < QD;
+        if (isq ? !fq : !fv) continue;
+        const unsigned int* Bw = reinterpret_cast<const unsigned int*>(
+            isq ? reinterpret_cast<const T*>(a.Bq) + (int64_t)(n0 + g) * RANK
+                : reinterpret_cast<const T*>(a.Bv) + (int64_t)(n0 - QD + g) * RANK);
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816<T>(c, isq ? aq : av, __ldg(Bw + t), __ldg(Bw + 4 + t));
+        *reinterpret_cast<uint32_t*>(sL + g * ld + n0 + 2 * t) = pack_t2<T>(c[0], c[1]);
       }
-      T* out = is_q ? reinterpret_cast<T*>(a.q) + tok * HQ * D + hh * D
-                    : reinterpret_cast<T*>(a.k) + tok * HKV * D + (hh - HQ) * D;
-      st8<T>(out + d, o1);
-      st8<T>(out + d + HALF, o2);
+      __syncthreads();
     }
-    for (int ch = lane; ch < v_chunks; ch += 32) {
-      const int idx = ch * 8;
-      float v[8];
-      ld8<T>(row + (HQ + HKV) * D + idx, v);
-      if (a.lv != nullptr || fv) {
-        float l[8];
-        if (a.lv != nullptr) ld8<T>(reinterpret_cast<const T*>(a.lv) + tok * HKV * D + idx, l);
-        else lora_rows8<T>(sBv, idx, xl + RANK, l);
+    const int64_t tok = (int64_t)tile * ROPE_ROWS + rrow;
+    if (tok < a.n) {
+      const T* row = reinterpret_cast<const T*>(a.qkv) + tok * C;
+      const T* lrow = sL + rrow * ld;
+      const int pos = a.pos[tok];
+      const float* cs = a.cos + (int64_t)pos * HALF;
+      const float* sn = a.sin + (int64_t)pos * HALF;
+      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * ROPE_WPR) {
+        const int hh = ch / cph, d = (ch % cph) * 8;
+        const bool is_q = hh < HQ;
+        const int src = hh * D + d;
+        float x1[8], x2[8], c[8], sv[8];
+        ld8<T>(row + src, x1);
+        ld8<T>(row + src + HALF, x2);
+        ld8<float>(cs + d, c);
+        ld8<float>(sn + d, sv);
+        if (is_q && (a.lq != nullptr || fq)) {
+          float l1[8], l2[8];
+          if (a.lq != nullptr) {
+            const T* lq = reinterpret_cast<const T*>(a.lq) + tok * QD;
+            ld8<T>(lq + src, l1);
+            ld8<T>(lq + src + HALF, l2);
+          } else {
+            ld8<T>(lrow + src, l1);
+            ld8<T>(lrow + src + HALF, l2);
+          }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] += l[j] * s;
+          for (int j = 0; j < 8; ++j) { x1[j] += l1[j] * s; x2[j] += l2[j] * s; }
+        }
+        float o1[8], o2[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o1[j] = x1[j] * c[j] - x2[j] * sv[j];
+          o2[j] = x2[j] * c[j] + x1[j] * sv[j];
+        }
+        T* out = is_q ? reinterpret_cast<T*>(a.q) + tok * QD + hh * D
+                      : reinterpret_cast<T*>(a.k) + tok * VD + (hh - HQ) * D;
+        st8<T>(out + d, o1);
+        st8<T>(out + d + HALF, o2);
       }
-      st8<T>(reinterpret_cast<T*>(a.v) + tok * HKV * D + idx, v);
+      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * ROPE_WPR) {
+        const int idx = ch * 8;
+        float v[8];
+        ld8<T>(row + (HQ + HKV) * D + idx, v);
+        if (a.lv != nullptr || fv) {
+          float l[8];
+          if (a.lv != nullptr) ld8<T>(reinterpret_cast<const T*>(a.lv) + tok * VD + idx, l);
+          else ld8<T>(lrow + QD + idx, l);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += l[j] * s;
+        }
+        st8<T>(reinterpret_cast<T*>(a.v) + tok * VD + idx, v);
+      }
     }
+    __syncthreads();  // sL is refilled by the next tile
   }
 }
 
-// Sum over the warp of 32 per-lane values; afterwards lane l holds the total of value l.
-__device__ __forceinline__ float rs32(float* v) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < off; ++i) {
-      const float send = upper ? v[i] : v[i + off];
-      const float keep = upper ? v[i + off] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  return v[0];
-}
-
-// acc[off + r] += sum_j g[j] B[idx + j][r] (8 consecutive rows of a [rows, 16] factor in smem)
-template <typename T>
-__device__ __forceinline__ void lora_acc8(const T* B, int idx, const float* g, float* acc, int off) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint4* b4 = reinterpret_cast<const uint4*>(B + (int64_t)(idx + j) * RANK);
-    const uint4 u0 = b4[0], u1 = b4[1];
-    const T* b0 = reinterpret_cast<const T*>(&u0);
-    const T* b1 = reinterpret_cast<const T*>(&u1);
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc[off + r] += g[j] * to_f<T>(b0[r]);
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc[off + 8 + r] += g[j] * to_f<T>(b1[r]);
-  }
-}
-
+// Backward, tiles of 8 tokens, 2 warps per token: the rotation pass writes the pre-rotary
+// gradient row and keeps its q and v parts (16-bit) in shared memory; then
+// dx_lo[8][16] = g[8][K] . B[K][16] on the tensor cores over K slices of 64 columns of [q | v]
+// strided over the warps, the slices' partials added in a fixed order.
 template <typename T, typename TIn>
-__global__ void __launch_bounds__(256) rope_bwd_kernel(RopeBwdC a) {
+__global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
+  constexpr int NW = ROPE_ROWS * ROPE_WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
-  const int C = (HQ + 2 * HKV) * D;
+  const int C = (HQ + 2 * HKV) * D, QD = HQ * D, VD = HKV * D, ld = QD + VD + 8;
   const int KVIN = a.kv_heads_in;  // HKV, or HQ (per query head: summed over the group)
   const int group = KVIN / HKV;
-  T* sBq = reinterpret_cast<T*>(rope_smem);
-  T* sBv = sBq + (int64_t)HQ * D * RANK;
+  T* sG = reinterpret_cast<T*>(rope_smem);                   // [8][ld] [g_q | g_v]
+  float* sRed = reinterpret_cast<float*>(sG + ROPE_ROWS * ld);  // [NW][2][8][16]
   const bool lq = a.dxlo_q != nullptr, lv = a.dxlo_v != nullptr;
-  if (lq || lv) {
-    if (lq) stage_to_smem(sBq, a.Bq, HQ * D * RANK * (int)sizeof(T));
-    if (lv) stage_to_smem(sBv, a.Bv, HKV * D * RANK * (int)sizeof(T));
-    stage_wait();
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rrow = warp / ROPE_WPR, part = warp % ROPE_WPR;
   const int cph = HALF / 8;
   const int rot_chunks = (HQ + HKV) * cph;
-  const int v_chunks = HKV * D / 8;
-  for (int64_t tok = blockIdx.x * 8 + warp; tok < a.n; tok += (int64_t)gridDim.x * 8) {
-    const int pos = a.pos[tok];
-    const float* cs = a.cos + (int64_t)pos * HALF;
-    const float* sn = a.sin + (int64_t)pos * HALF;
-    const TIn* dq = reinterpret_cast<const TIn*>(a.dq) + tok * HQ * D;
-    const TIn* dk = reinterpret_cast<const TIn*>(a.dk) + tok * KVIN * D;
-    const TIn* dv = reinterpret_cast<const TIn*>(a.dv) + tok * KVIN * D;
-    T* out = reinterpret_cast<T*>(a.dqkv) + tok * C;
-    float acc[2 * RANK];
+  const int v_chunks = VD / 8;
+  const int ntiles = (a.n + ROPE_ROWS - 1) / ROPE_ROWS;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t tok = (int64_t)tile * ROPE_ROWS + rrow;
+    T* grow = sG + rrow * ld;
+    if (tok < a.n) {
+      const int pos = a.pos[tok];
+      const float* cs = a.cos + (int64_t)pos * HALF;
+      const float* sn = a.sin + (int64_t)pos * HALF;
+      const TIn* dq = reinterpret_cast<const TIn*>(a.dq) + tok * QD;
+      const TIn* dk = reinterpret_cast<const TIn*>(a.dk) + tok * KVIN * D;
+      const TIn* dv = reinterpret_cast<const TIn*>(a.dv) + tok * KVIN * D;
+      T* out = reinterpret_cast<T*>(a.dqkv) + tok * C;
+      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * ROPE_WPR) {
+        const int hh = ch / cph, d = (ch % cph) * 8;
+        float g1[8], g2[8], c[8], sv[8];
+        if (hh < HQ) {
+          ld8<TIn>(dq + hh * D + d, g1);
+          ld8<TIn>(dq + hh * D + d + HALF, g2);
+        } else {
+          const int j = hh - HQ;
 #pragma unroll
-    for (int r = 0; r < 2 * RANK; ++r) acc[r] = 0.f;
-#pragma unroll 2
-    for (int ch = lane; ch < rot_chunks; ch += 32) {
-      const int hh = ch / cph, d = (ch % cph) * 8;
-      float g1[8], g2[8], c[8], sv[8];
-      if (hh < HQ) {
-        ld8<TIn>(dq + hh * D + d, g1);
-        ld8<TIn>(dq + hh * D + d + HALF, g2);
-      } else {
-        const int j = hh - HQ;
+          for (int t = 0; t < 8; ++t) g1[t] = g2[t] = 0.f;
+          for (int r = 0; r < group; ++r) {
+            float t1[8], t2[8];
+            ld8<TIn>(dk + (j * group + r) * D + d, t1);
+            ld8<TIn>(dk + (j * group + r) * D + d + HALF, t2);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) g1[t] = g2[t] = 0.f;
-        for (int r = 0; r < group; ++r) {
-          float t1[8], t2[8];
-          ld8<TIn>(dk + (j * group + r) * D + d, t1);
-          ld8<TIn>(dk + (j * group + r) * D + d + HALF, t2);
+            for (int t = 0; t < 8; ++t) { g1[t] += t1[t]; g2[t] += t2[t]; }
+          }
+        }
+        ld8<float>(cs + d, c);
+        ld8<float>(sn + d, sv);
+        float o1[8], o2[8];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) { g1[t] += t1[t]; g2[t] += t2[t]; }
+        for (int t = 0; t < 8; ++t) {
+          o1[t] = g1[t] * c[t] + g2[t] * sv[t];
+          o2[t] = g2[t] * c[t] - g1[t] * sv[t];
+        }
+        const int col = hh * D + d;
+        st8<T>(out + col, o1);
+        st8<T>(out + col + HALF, o2);
+        if (hh < HQ && lq) {
+          st8<T>(grow + col, o1);
+          st8<T>(grow + col + HALF, o2);
         }
       }
-      ld8<float>(cs + d, c);
-      ld8<float>(sn + d, sv);
-      float o1[8], o2[8];
+      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * ROPE_WPR) {
+        const int idx = ch * 8, j = idx / D, d = idx % D;
+        float g[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        o1[t] = to_f<T>(from_f<T>(g1[t] * c[t] + g2[t] * sv[t]));
-        o2[t] = to_f<T>(from_f<T>(g2[t] * c[t] - g1[t] * sv[t]));
+        for (int t = 0; t < 8; ++t) g[t] = 0.f;
+        for (int r = 0; r < group; ++r) {
+          float t1[8];
+          ld8<TIn>(dv + (j * group + r) * D + d, t1);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) g[t] += t1[t];
+        }
+        st8<T>(out + (HQ + HKV) * D + idx, g);
+        if (lv) st8<T>(grow + QD + idx, g);
       }
-      const int col = hh * D + d;
-      st8<T>(out + col, o1);
-      st8<T>(out + col + HALF, o2);
-      if (hh < HQ && lq) {
-        lora_acc8<T>(sBq, col, o1, acc, 0);
-        lora_acc8<T>(sBq, col + HALF, o2, acc, 0);
-      }
-    }
-    for (int ch = lane; ch < v_chunks; ch += 32) {
-      const int idx = ch * 8, j = idx / D, d = idx % D;
-      float g[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) g[t] = 0.f;
-      for (int r = 0; r < group; ++r) {
-        float t1[8];
-        ld8<TIn>(dv + (j * group + r) * D + d, t1);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) g[t] += t1[t];
-      }
-#pragma unroll
-      for (int t = 0; t < 8; ++t) g[t] = to_f<T>(from_f<T>(g[t]));
-      st8<T>(out + (HQ + HKV) * D + idx, g);
-      if (lv) lora_acc8<T>(sBv, idx, g, acc, RANK);
     }
     if (lq || lv) {
-      const float sum = rs32(acc);  // lane l: value l (q: 0..15, v: 16..31)
-      // (g @ B) rounded to the 16-bit type, then * s rounded again (fp16 tensor times a scalar)
-      const float v = to_f<T>(from_f<T>(to_f<T>(from_f<T>(sum)) * a.lora_scale));
-      if (lane < RANK) {
-        if (lq) a.dxlo_q[tok * RANK + lane] = v;
-      } else if (lv) {
-        a.dxlo_v[tok * RANK + lane - RANK] = v;
+      __syncthreads();
+      const int g = lane >> 2, t = lane & 3;
+      float accq[2][4] = {}, accv[2][4] = {};  // [n tile][fragment] per adapter
+      for (int k0 = warp * 64; k0 < QD + VD; k0 += 64 * NW) {
+        const bool isq = k0 < QD;
+        if (isq ? !lq : !lv) continue;
+        const unsigned short* B = reinterpret_cast<const unsigned short*>(isq ? a.Bq : a.Bv) +
+                                  (int64_t)(isq ? k0 : k0 - QD) * RANK;
+#pragma unroll
+        for (int kk = 0; kk < 64; kk += 16) {
+          const T* Y = sG + g * ld + k0 + kk + 2 * t;
+          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(Y), 0u,
+                                  *reinterpret_cast<const uint32_t*>(Y + 8), 0u};
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const unsigned short* bp = B + (kk + 2 * t) * RANK + nt * 8 + g;
+            const uint32_t b0 = (uint32_t)__ldg(bp) | ((uint32_t)__ldg(bp + RANK) << 16);
+            const uint32_t b1 = (uint32_t)__ldg(bp + 8 * RANK) | ((uint32_t)__ldg(bp + 9 * RANK) << 16);
+            if (isq) mma16816<T>(accq[nt], af, b0, b1);
+            else mma16816<T>(accv[nt], af, b0, b1);
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        float* rq = sRed + ((warp * 2 + 0) * ROPE_ROWS + g) * RANK + nt * 8 + 2 * t;
+        float* rv = sRed + ((warp * 2 + 1) * ROPE_ROWS + g) * RANK + nt * 8 + 2 * t;
+        rq[0] = accq[nt][0];
+        rq[1] = accq[nt][1];
+        rv[0] = accv[nt][0];
+        rv[1] = accv[nt][1];
+      }
+      __syncthreads();
+      if (threadIdx.x < 2 * ROPE_ROWS * RANK) {
+        const int ad = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
+        const int64_t orow = (int64_t)tile * ROPE_ROWS + rr;
+        if (orow < a.n && (ad == 0 ? lq : lv)) {
+          float sum = 0.f;
+          for (int w = 0; w < NW; ++w) sum += sRed[((w * 2 + ad) * ROPE_ROWS + rr) * RANK + r];
+          // (g @ B) rounded to the 16-bit type, then * s rounded again (fp16 tensor times a scalar)
+          const float v = to_f<T>(from_f<T>(to_f<T>(from_f<T>(sum)) * a.lora_scale));
+          (ad == 0 ? a.dxlo_q : a.dxlo_v)[orow * RANK + r] = v;
+        }
       }
     }
+    __syncthreads();  // sG and sRed are refilled by the next tile
   }
 }
 
@@ -289,14 +303,14 @@ int rope_fwd(const RopeFwdC& a, cudaStream_t s) {
   if ((a.xq != nullptr || a.xv != nullptr) && a.rank != RANK) return QL_STATUS_UNSUPPORTED;
   ProfScope prof(PK_ROPE_FWD, 0, (double)a.n * (a.HQ + 2 * a.HKV) * a.D * 2 * 2, s);
   const bool lora = (a.lq == nullptr && a.xq != nullptr) || (a.lv == nullptr && a.xv != nullptr);
-  const int smem = lora ? (a.HQ + a.HKV) * a.D * RANK * 2 : 0;
+  const int smem = lora ? ROPE_ROWS * ((a.HQ + a.HKV) * a.D + 8) * 2 : 0;
   const int grid = rope_grid(a.n);
   if (a.dtype == QL_F16) {
     rope_smem_attr(rope_fwd_kernel<__half>, smem);
-    rope_fwd_kernel<__half><<<grid, 256, smem, s>>>(a);
+    rope_fwd_kernel<__half><<<grid, 256 * ROPE_WPR, smem, s>>>(a);
   } else if (a.dtype == QL_BF16) {
     rope_smem_attr(rope_fwd_kernel<__nv_bfloat16>, smem);
-    rope_fwd_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(a);
+    rope_fwd_kernel<__nv_bfloat16><<<grid, 256 * ROPE_WPR, smem, s>>>(a);
   } else {
     return QL_STATUS_BAD_ARG;
   }
@@ -313,12 +327,15 @@ int rope_bwd(const RopeBwdC& a, cudaStream_t s) {
   if (a.grad_dtype != QL_F32 && a.grad_dtype != a.dtype) return QL_STATUS_BAD_ARG;
   ProfScope prof(PK_ROPE_BWD, 0, (double)a.n * (a.HQ + 2 * a.HKV) * a.D * (4 + 2), s);
   const bool lora = a.dxlo_q != nullptr || a.dxlo_v != nullptr;
-  const int smem = lora ? (a.HQ + a.HKV) * a.D * RANK * 2 : 0;
+  if (lora && a.D % 64 != 0) return QL_STATUS_UNSUPPORTED;  // 64-column K slices of [q | v]
+  const int smem = lora ? ROPE_ROWS * ((a.HQ + a.HKV) * a.D + 8) * 2 +
+                              ROPE_ROWS * ROPE_WPR * 2 * ROPE_ROWS * RANK * 4
+                        : 0;
   const int grid = rope_grid(a.n);
-#define QL_ROPEB(TT, TI)                                          \
-  do {                                                            \
-    rope_smem_attr(rope_bwd_kernel<TT, TI>, smem);                \
-    rope_bwd_kernel<TT, TI><<<grid, 256, smem, s>>>(a);           \
+#define QL_ROPEB(TT, TI)                                             \
+  do {                                                               \
+    rope_smem_attr(rope_bwd_kernel<TT, TI>, smem);                   \
+    rope_bwd_kernel<TT, TI><<<grid, 256 * ROPE_WPR, smem, s>>>(a);   \
   } while (0)
   if (a.dtype == QL_F16) {
     if (f32in) QL_ROPEB(__half, float); else QL_ROPEB(__half, __half);
