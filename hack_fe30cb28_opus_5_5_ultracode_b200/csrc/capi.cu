@@ -104,6 +104,15 @@ int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
               "ql_gemm_tn");
 }
 
+int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+               const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+               const float* residual, void* workspace, int64_t workspace_bytes,
+               cudaStream_t stream) {
+  return done(ql::gemm_nn(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
+                          residual, ql::status_word(), stream, workspace, workspace_bytes),
+              "ql_gemm_nn");
+}
+
 int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
 }  // extern "C"
@@ -267,6 +276,10 @@ int ql_scatter_rows(const float* src, const int64_t* idx, const float* scale, fl
 }  // extern "C"
 
 extern "C" {
+
+int64_t ql_layer_weight_elems(const ql_layer_desc* layer) {
+  return layer == nullptr ? -1 : ql::layer_weight_elems(*layer);
+}
 
 int64_t ql_layer_workspace_bytes(const ql_layer_desc* layer, int backward) {
   return layer == nullptr ? -1 : ql::layer_workspace_bytes(*layer, backward);

@@ -143,12 +143,27 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Descriptor of an MN-major operand tile with the 128-byte swizzle: chunks of 64 consecutive
+// M/N elements (128 B) per K row, 8-row K groups sbo bytes apart, 64-element M/N chunks lbo
+// bytes apart. A K-step of 16 rows advances the start address by 2 groups.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo,
+                                                       uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor of tcgen05.mma.kind::f16: fp32 accumulator, A and B of the same 16-bit
-// type (is_bf16), both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(bool is_bf16, int M, int N) {
+// type (is_bf16), A K-major, B K-major or MN-major (b_mn), M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool is_bf16, int M, int N, bool b_mn = false) {
   return (1u << 4)                                  // D format: f32
          | ((is_bf16 ? 1u : 0u) << 7)               // A format
          | ((is_bf16 ? 1u : 0u) << 10)              // B format
+         | ((b_mn ? 1u : 0u) << 16)                 // B major-ness
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 

@@ -80,7 +80,7 @@ __device__ __forceinline__ void store_row32(OutT* dst, const float* v, int ncols
   }
 }
 
-template <int BN, bool IS_BF16, typename OutT>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    GemmArgs p) {
@@ -135,14 +135,20 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           tma_load_2d(sa, &tma_a, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
-          tma_load_2d(sb, &tma_b, &full[stage], kb * Cfg::BK, nb * BN);
+          if constexpr (B_MN) {  // B stored [K, N]: boxes of 64 N-columns x 64 K-rows, 8 KB each
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 8192, &tma_b, &full[stage], nb * BN + j * 64, kb * Cfg::BK);
+          } else {
+            tma_load_2d(sb, &tma_b, &full[stage], kb * Cfg::BK, nb * BN);
+          }
           if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(IS_BF16, 128, BN);
+      constexpr uint32_t idesc = umma_idesc_f16(IS_BF16, 128, BN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -162,7 +168,9 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
-            umma_f16(tmem_d, umma_desc_k_sw128(sa + k * 32), umma_desc_k_sw128(sb + k * 32), idesc,
+            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, 8192, 1024)
+                                     : umma_desc_k_sw128(sb + k * 32);
+            umma_f16(tmem_d, umma_desc_k_sw128(sa + k * 32), db, idesc,
                      (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -324,11 +332,11 @@ static int num_sms() {
   return sms;
 }
 
-template <int BN, bool IS_BF16, typename OutT>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
                        cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tn_kernel<BN, IS_BF16, OutT>;
+  auto kern = gemm_tn_kernel<BN, IS_BF16, OutT, B_MN>;
   static bool configured = false;  // one static per instantiation
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) !=
@@ -342,21 +350,22 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   return launched(1);
 }
 
-template <int BN, bool IS_BF16>
+template <int BN, bool IS_BF16, bool B_MN>
 static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
                         cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_gemm<BN, IS_BF16, __half>(ma, mb, a, s);
-    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16>(ma, mb, a, s);
-    case QL_F32: return launch_gemm<BN, IS_BF16, float>(ma, mb, a, s);
+    case QL_F16: return launch_gemm<BN, IS_BF16, __half, B_MN>(ma, mb, a, s);
+    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, a, s);
+    case QL_F32: return launch_gemm<BN, IS_BF16, float, B_MN>(ma, mb, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
 
-template <int BN>
+template <int BN, bool B_MN>
 static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, bool bf16,
                        cudaStream_t s) {
-  return bf16 ? dispatch_out<BN, true>(ma, mb, a, s) : dispatch_out<BN, false>(ma, mb, a, s);
+  return bf16 ? dispatch_out<BN, true, B_MN>(ma, mb, a, s)
+              : dispatch_out<BN, false, B_MN>(ma, mb, a, s);
 }
 
 // Split-K workspace: tile counters first (a fixed region, left all-zero by every launch, so
@@ -375,11 +384,12 @@ struct GemmPlan {
 // split keeps at least 32 K-blocks (shorter splits cost more in partial traffic than they gain):
 // the best last-wave efficiency over 2..8 splits, the fewest splits within 2% of it, used only if
 // it beats the unsplit launch by 5 points.
-static GemmPlan plan_gemm(int M, int N, int K, int sms) {
+static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   static const int widths[] = {256, 224, 192, 128, 96};
   GemmPlan g{256, 0, 1, 0};
   int64_t best = -1;
   for (int bn : widths) {
+    if (b_mn && bn % 64 != 0) continue;  // an MN-major B tile is whole 64-column boxes
     const int64_t tiles = cdiv(M, 128) * cdiv(N, bn);
     const int64_t cost = cdiv(tiles, sms) * (bn + 64);
     if (best < 0 || cost < best) {
@@ -409,15 +419,19 @@ static GemmPlan plan_gemm(int M, int N, int K, int sms) {
 
 int64_t gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const GemmPlan g = plan_gemm(M, N, K, num_sms());
+  GemmPlan g = plan_gemm(M, N, K, num_sms());
+  const GemmPlan g2 = plan_gemm(M, N, K, num_sms(), true);  // the larger of the two layouts
+  if (g2.splits > 1 && g2.tiles * g2.splits * g2.bn > g.tiles * g.splits * g.bn) g = g2;
   if (g.splits == 1) return 0;
   return kCounterBytes + g.tiles * g.splits * 128 * g.bn * 4;
 }
 
-int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
-            const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
-            const float* residual, int* err, cudaStream_t stream, void* workspace,
-            int64_t workspace_bytes) {
+// C = A . op(B): b_mn = false, B is [N, K] (K contiguous, C = A B^T); b_mn = true, B is [K, N]
+// (N contiguous, C = A B), read by the tensor cores as an MN-major operand.
+static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                     const void* bias, int M, int N, int K, int in_dtype, int out_dtype,
+                     int accumulate, const float* residual, int* err, cudaStream_t stream,
+                     void* workspace, int64_t workspace_bytes, bool b_mn) {
   if (M < 0 || N < 0 || K < 0) return QL_STATUS_BAD_ARG;
   if (M == 0 || N == 0) return QL_STATUS_OK;
   if (in_dtype != QL_F16 && in_dtype != QL_BF16) return QL_STATUS_BAD_ARG;
@@ -426,12 +440,13 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) % 16 != 0)
     return QL_STATUS_BAD_ARG;
   if ((lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 || K % 8 != 0) return QL_STATUS_BAD_ARG;
+  if (b_mn && N % 8 != 0) return QL_STATUS_BAD_ARG;
   if (K == 0) return QL_STATUS_UNSUPPORTED;
   const bool bf16 = in_dtype == QL_BF16;
   ProfScope prof(PK_GEMM, 2.0 * M * N * K,
                  2.0 * ((double)M * K + (double)N * K) + (double)M * N * (out_dtype == QL_F32 ? 4 : 2),
                  stream);
-  GemmPlan g = plan_gemm(M, N, K, num_sms());
+  GemmPlan g = plan_gemm(M, N, K, num_sms(), b_mn);
   const int64_t need = kCounterBytes + g.tiles * g.splits * 128 * g.bn * 4;
   if (g.splits > 1 && (workspace == nullptr || workspace_bytes < need ||
                        reinterpret_cast<uintptr_t>(workspace) % 256 != 0 ||
@@ -441,7 +456,11 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
   }
   CUtensorMap ma, mb;
   if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  if (make_kmajor_map(&mb, B, N, K, ldb, g.bn, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+  if (b_mn) {
+    if (make_kmajor_map(&mb, B, K, N, ldb, 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+  } else {
+    if (make_kmajor_map(&mb, B, N, K, ldb, g.bn, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+  }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
              g.kb_per_split, nullptr, nullptr};
   if (g.splits > 1) {
@@ -449,13 +468,36 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
     a.counters = reinterpret_cast<int*>(w);
     a.ws = reinterpret_cast<float*>(w + kCounterBytes);
   }
-  switch (g.bn) {
-    case 96: return dispatch_in<96>(ma, mb, a, bf16, stream);
-    case 128: return dispatch_in<128>(ma, mb, a, bf16, stream);
-    case 192: return dispatch_in<192>(ma, mb, a, bf16, stream);
-    case 224: return dispatch_in<224>(ma, mb, a, bf16, stream);
-    default: return dispatch_in<256>(ma, mb, a, bf16, stream);
+  if (b_mn) {
+    switch (g.bn) {
+      case 128: return dispatch_in<128, true>(ma, mb, a, bf16, stream);
+      case 192: return dispatch_in<192, true>(ma, mb, a, bf16, stream);
+      default: return dispatch_in<256, true>(ma, mb, a, bf16, stream);
+    }
   }
+  switch (g.bn) {
+    case 96: return dispatch_in<96, false>(ma, mb, a, bf16, stream);
+    case 128: return dispatch_in<128, false>(ma, mb, a, bf16, stream);
+    case 192: return dispatch_in<192, false>(ma, mb, a, bf16, stream);
+    case 224: return dispatch_in<224, false>(ma, mb, a, bf16, stream);
+    default: return dispatch_in<256, false>(ma, mb, a, bf16, stream);
+  }
+}
+
+int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+            const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+            const float* residual, int* err, cudaStream_t stream, void* workspace,
+            int64_t workspace_bytes) {
+  return gemm_core(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
+                   residual, err, stream, workspace, workspace_bytes, false);
+}
+
+int gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+            const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+            const float* residual, int* err, cudaStream_t stream, void* workspace,
+            int64_t workspace_bytes) {
+  return gemm_core(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
+                   residual, err, stream, workspace, workspace_bytes, true);
 }
 
 }  // namespace ql

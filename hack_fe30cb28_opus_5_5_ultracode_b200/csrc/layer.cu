@@ -30,6 +30,22 @@ int64_t max_weight_elems(const ql_layer_desc& L) {
   return m;
 }
 
+// Offsets (elements) of the four dequantised groups [qkv | o | gate_up | down] in the forward's
+// kept weights (ql_layer_saved.w16).
+struct WeightSlots {
+  int64_t qkv, o, gu, down, total;
+};
+WeightSlots weight_slots(const ql_layer_desc& L) {
+  const int64_t C = (int64_t)(L.HQ + 2 * L.HKV) * L.D, QD = (int64_t)L.HQ * L.D;
+  WeightSlots w;
+  w.qkv = 0;
+  w.o = w.qkv + C * L.H;
+  w.gu = w.o + (int64_t)L.H * QD;
+  w.down = w.gu + 2LL * L.I * L.H;
+  w.total = w.down + (int64_t)L.H * L.I;
+  return w;
+}
+
 int dequant(const ql_nf4_weight& w, void* out, int dtype, int transpose, cudaStream_t s) {
   return nf4_dequant(w.packed, w.absmax, w.code2, w.absmax2, w.offsets, w.code, out, w.rows,
                      w.cols, w.nested, w.bs2, w.seg1, w.seg2, dtype, transpose, s);
@@ -142,6 +158,8 @@ int check(const ql_layer_desc& L) {
 
 }  // namespace
 
+int64_t layer_weight_elems(const ql_layer_desc& L) { return weight_slots(L).total; }
+
 int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward) {
   Bump b{nullptr, 0, 0};
   if (backward) carve_bwd(L, b); else carve_fwd(L, b);
@@ -157,6 +175,16 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   if (!bump.ok()) return QL_STATUS_BAD_ARG;
   const int64_t n = L.n, C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
   const int dt = L.dtype;
+  // each weight group dequantised once per step: into the kept copy when the caller gives one
+  // (the backward then reads it), else into the workspace
+  const WeightSlots slots = weight_slots(L);
+  auto wbuf = [&](int64_t off) -> void* {
+    return S.w16 != nullptr ? static_cast<uint8_t*>(S.w16) + off * esz(dt) : w.w;
+  };
+  void* const wqkv = wbuf(slots.qkv);
+  void* const wo = wbuf(slots.o);
+  void* const wgu = wbuf(slots.gu);
+  void* const wdown = wbuf(slots.down);
 
   // input RMSNorm + the dropped LoRA inputs + LoRA-A products
   RmsFwdC r1{};
@@ -168,8 +196,8 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
             r1.drop_q, r1.drop_v);
   QL_TRY(rms_fwd(r1, s));
   // q, k, v in one GEMM (bias in the epilogue), then LoRA-B + RoPE
-  QL_TRY(dequant(L.qkv, w.w, dt, 0, s));
-  QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, w.qkv, C, L.bias_qkv, L.n, (int)C, L.H, dt, dt, 0, nullptr,
+  QL_TRY(dequant(L.qkv, wqkv, dt, 0, s));
+  QL_TRY(gemm_tn(w.a, L.H, wqkv, L.H, w.qkv, C, L.bias_qkv, L.n, (int)C, L.H, dt, dt, 0, nullptr,
                  err, s, w.gws, w.gws_bytes));
   RopeFwdC rf{};
   rf.qkv = w.qkv; rf.xq = S.xq; rf.xv = S.xv; rf.Bq = L.Bq; rf.Bv = L.Bv; rf.cos = L.cos;
@@ -183,8 +211,8 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   af.HKV = L.HKV; af.D = L.D; af.dtype = dt;
   QL_TRY(attn_fwd(af, s));
   // o projection, residual add in the epilogue: h2 = h + o
-  QL_TRY(dequant(L.o, w.w, dt, 0, s));
-  QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, w.w, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
+  QL_TRY(dequant(L.o, wo, dt, 0, s));
+  QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, wo, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
                  L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s, w.gws, w.gws_bytes));
   // post-attention RMSNorm
   RmsFwdC r2{};
@@ -193,12 +221,12 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   r2.keep_scale = 1.f;
   QL_TRY(rms_fwd(r2, s));
   // [gate | up], SwiGLU, down with the residual add: h3 = h2 + d
-  QL_TRY(dequant(L.gu, w.w, dt, 0, s));
-  QL_TRY(gemm_tn(w.a, L.H, w.w, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
+  QL_TRY(dequant(L.gu, wgu, dt, 0, s));
+  QL_TRY(gemm_tn(w.a, L.H, wgu, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
                  nullptr, err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
-  QL_TRY(dequant(L.down, w.w, dt, 0, s));
-  QL_TRY(gemm_tn(w.m, L.I, w.w, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
+  QL_TRY(dequant(L.down, wdown, dt, 0, s));
+  QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
                  err, s, w.gws, w.gws_bytes));
   return QL_STATUS_OK;
 }
@@ -217,14 +245,26 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   float* gBq = gAq + (int64_t)L.rank * L.H;
   float* gAv = gBq + (int64_t)L.HQ * L.D * L.rank;
   float* gBv = gAv + (int64_t)L.rank * L.H;
+  // the data-gradient products read each weight in its forward layout (MN-major operand): the
+  // forward's kept copy, or a fresh dequantisation into the workspace
+  const WeightSlots slots = weight_slots(L);
+  auto weight = [&](const ql_nf4_weight& q, int64_t off, void** out) -> int {
+    if (S.w16 != nullptr) {
+      *out = static_cast<uint8_t*>(S.w16) + off * esz(dt);
+      return QL_STATUS_OK;
+    }
+    *out = w.w;
+    return dequant(q, w.w, dt, 0, s);
+  };
+  void* W = nullptr;
 
   // MLP: dm = dh3 . Wd ; [dg | du] in place ; db = [dg | du] . Wgu
-  QL_TRY(dequant(L.down, w.w, dt, 1, s));
-  QL_TRY(gemm_tn(dh3_16, L.H, w.w, L.H, w.dm, L.I, nullptr, L.n, L.I, L.H, dt, dt, 0, nullptr,
+  QL_TRY(weight(L.down, slots.down, &W));  // [H, I]
+  QL_TRY(gemm_nn(dh3_16, L.H, W, L.I, w.dm, L.I, nullptr, L.n, L.I, L.H, dt, dt, 0, nullptr,
                  err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_bwd(w.dm, S.gu, n, L.I, dt, s));
-  QL_TRY(dequant(L.gu, w.w, dt, 1, s));
-  QL_TRY(gemm_tn(S.gu, 2LL * L.I, w.w, 2LL * L.I, w.db, L.H, nullptr, L.n, L.H, 2 * L.I, dt, dt,
+  QL_TRY(weight(L.gu, slots.gu, &W));  // [2 I, H]
+  QL_TRY(gemm_nn(S.gu, 2LL * L.I, W, L.H, w.db, L.H, nullptr, L.n, L.H, 2 * L.I, dt, dt,
                  0, nullptr, err, s, w.gws, w.gws_bytes));
   RmsBwdC r2{};
   r2.dy = w.db; r2.ld_dy = L.H; r2.x = S.h2; r2.rstd = S.rstd2; r2.w = L.ln2; r2.dres = dh3;
@@ -232,9 +272,9 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   r2.grad_scale = 1.f; r2.vec = 4; r2.threads = 1; r2.p_keep = 1.f; r2.keep_scale = 1.f;
   QL_TRY(rms_bwd(r2, s));
   // attention
-  QL_TRY(dequant(L.o, w.w, dt, 1, s));
-  QL_TRY(gemm_tn(w.dh2_16, L.H, w.w, L.H, w.dout, (int64_t)L.HQ * L.D, nullptr, L.n, L.HQ * L.D,
-                 L.H, dt, dt, 0, nullptr, err, s, w.gws, w.gws_bytes));
+  QL_TRY(weight(L.o, slots.o, &W));  // [H, HQ D]
+  QL_TRY(gemm_nn(w.dh2_16, L.H, W, (int64_t)L.HQ * L.D, w.dout, (int64_t)L.HQ * L.D, nullptr, L.n,
+                 L.HQ * L.D, L.H, dt, dt, 0, nullptr, err, s, w.gws, w.gws_bytes));
   AttnBwdC ab{};
   ab.q = S.q; ab.k = S.k; ab.v = S.v; ab.out = S.out; ab.dout = w.dout; ab.lse = S.lse;
   ab.cu_seqlens = L.cu_seqlens; ab.dvec = w.dvec; ab.dq = w.dq; ab.dk = w.dk; ab.dv = w.dv;
@@ -259,8 +299,8 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   QL_TRY(lora_colsum(S.yv, L.H, dt, w.dxv, QL_F32, n, L.H, L.rank, 1.f, 1, gAv, w.cs,
                      w.cs_floats, s));
   if (dh_out == nullptr) return QL_STATUS_OK;  // the first layer's input is the frozen embedding
-  QL_TRY(dequant(L.qkv, w.w, dt, 1, s));
-  QL_TRY(gemm_tn(w.dqkv, C, w.w, C, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,
+  QL_TRY(weight(L.qkv, slots.qkv, &W));  // [C, H]
+  QL_TRY(gemm_nn(w.dqkv, C, W, L.H, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,
                  err, s, w.gws, w.gws_bytes));
   RmsBwdC r1{};
   r1.dy = w.da; r1.ld_dy = L.H; r1.x = S.h; r1.rstd = S.rstd1; r1.w = L.ln1; r1.dres = w.dh2;

@@ -18,6 +18,10 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
             const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
             const float* residual, int* err, cudaStream_t stream, void* workspace = nullptr,
             int64_t workspace_bytes = 0);
+int gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+            const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+            const float* residual, int* err, cudaStream_t stream, void* workspace = nullptr,
+            int64_t workspace_bytes = 0);
 int64_t gemm_workspace_bytes(int M, int N, int K);
 
 typedef ql_rms_fwd_args RmsFwdC;
@@ -65,6 +69,7 @@ int scatter_rows(const float* src, const int64_t* idx, const float* scale, float
 
 namespace ql {
 int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward);
+int64_t layer_weight_elems(const ql_layer_desc& L);
 int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,
                   int64_t ws_bytes, int* err, cudaStream_t s);
 int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float* dh3,

@@ -6,9 +6,10 @@ autograd, same use of the CUDA generator for the LoRA dropout masks.
 B200-first differences from the reference (which was built for a 16 GB T4):
   * HBM is plentiful (180 GB), so the default plan keeps every intermediate a layer's backward
     reads instead of recomputing it; NF4 weights stay resident (0.74 GB for 1.5B).
-  * every matrix product runs on the tcgen05 GEMM of this library (fp32 accumulation in TMEM),
-    the NF4 weights dequantised by this library's kernel once per pass (forward: W, backward: W^T
-    for the data-gradient GEMMs);
+  * every matrix product runs on the tcgen05 GEMM of this library (fp32 accumulation in TMEM);
+    each NF4 weight is dequantised once per step, in the forward, into a kept 16-bit copy that
+    the backward's data-gradient GEMMs read as an MN-major operand (no second dequantisation,
+    no transposed copy; 2.6 GB for 1.5B);
   * LoRA-A products ride in the RMSNorm kernel, LoRA-B products and the LoRA input gradients in
     the RoPE kernels, the residual adds in the GEMM epilogues;
   * attention is this library's varlen causal GQA kernel: k / v are never expanded;
@@ -374,7 +375,7 @@ class LayerSpec:
 class FusedQwen2:
     """Holds what the step needs from a PEFT-wrapped, 4-bit Qwen2ForCausalLM."""
 
-    def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK):
+    def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True):
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -396,8 +397,6 @@ class FusedQwen2:
         lm = causal.lm_head.weight.detach()
         self.lm_w = self.embed if lm.data_ptr() == inner.embed_tokens.weight.data_ptr() \
             and lm.dtype == dtype else lm.to(dtype).contiguous()
-        # the head's data-gradient GEMM reads the lm_head weight K-major along the vocabulary
-        self.lm_wT = self.lm_w.t().contiguous()
         self.V = self.lm_w.shape[0]
         self.rope = RopeTable(inner.rotary_emb, spec.D, self.device)
         self.head_chunk = head_chunk
@@ -422,6 +421,10 @@ class FusedQwen2:
                     raise ValueError("double-quantised weights whose absmax2 blocks straddle "
                                      "two members of a group are not supported")
         self.descs = [self._layer_desc(spec) for spec in self.layers]
+        # the forward's dequantised weights, per layer, read again by the backward
+        self.weight_elems = int(_lib.lib().ql_layer_weight_elems(ctypes.byref(self.descs[0])))
+        self.w16 = torch.empty(len(self.layers) * self.weight_elems, device=self.device,
+                               dtype=dtype) if keep_weights else None
         self._workspace = None
         self._arena_buf = None     # grow-only device memory of the saved activations
         self._arena_busy = False   # a forward's activations await their backward
@@ -509,6 +512,8 @@ class FusedQwen2:
             drop = self._drop(packed, spec.H)
             self._set_step(desc, packed, drop, cos, sin)
             sv = arena.saved(spec.index)
+            if self.w16 is not None:
+                sv.w16 = self.w16[spec.index * self.weight_elems:].data_ptr()
             if n:
                 ws = self._workspace_for(desc)
                 _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
@@ -558,7 +563,7 @@ class FusedQwen2:
             ops.ce_rows(logits, targets[c0:c1], write_grad=sup > 0, loss=tok_loss[c0:c1],
                         entropy=entropy[c0:c1], correct=correct[c0:c1])
             if sup:
-                dhn = ops.gemm(logits[:sup], self.lm_wT)
+                dhn = ops.gemm(logits[:sup], self.lm_w, b_kn=True)
                 ops.rms_bwd(dhn, hp[c0:c0 + sup], rstd[c0:c0 + sup], self.norm_w, dtype=dt,
                             grad_scale=inv, out=dhp[c0:c0 + sup])
         stats.order, stats.tok_loss, stats.entropy, stats.correct = order, tok_loss, entropy, correct

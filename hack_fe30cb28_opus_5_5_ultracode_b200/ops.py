@@ -55,13 +55,15 @@ def nf4_dequant(w, out=None, transpose=False, dtype=torch.float16):
 # ---------------------------------------------------------------------------------------------
 # GEMM
 # ---------------------------------------------------------------------------------------------
-def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=None):
-    """out[M, N] (+)= a[M, K] @ b[N, K]^T (+ bias) on tcgen05. a and b: fp16 or bf16 with unit
-    column stride; out: fp16 / bf16 / fp32 with unit column stride."""
+def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=None,
+         b_kn=False):
+    """out[M, N] (+)= a[M, K] @ b[N, K]^T (+ bias) on tcgen05; with b_kn, b is [K, N] and
+    out = a @ b (ql_gemm_nn). a and b: fp16 or bf16 with unit column stride; out: fp16 / bf16 /
+    fp32 with unit column stride."""
     M, K = a.shape
-    N, K2 = b.shape
+    N, K2 = (b.shape[1], b.shape[0]) if b_kn else b.shape
     if K != K2:
-        raise ValueError(f"inner dimensions differ: {a.shape} x {b.shape}^T")
+        raise ValueError(f"inner dimensions differ: {a.shape} x {b.shape}")
     if a.dtype != b.dtype:
         raise ValueError("a and b must have the same dtype")
     if out is None:
@@ -74,9 +76,10 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
     if residual is not None and (residual.stride(0) != out.stride(0) or residual.stride(1) != 1):
         raise ValueError("residual must share the output's row stride")
     ws = gemm_workspace(a.device, int(_lib.lib().ql_gemm_workspace_bytes(M, N, K)))
-    call("ql_gemm_tn", _ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out), out.stride(0),
-         _ptr(bias), M, N, K, dtype_code(a.dtype), dtype_code(out.dtype), int(accumulate),
-         _ptr(residual), _ptr(ws), 0 if ws is None else ws.numel(), stream_ptr())
+    call("ql_gemm_nn" if b_kn else "ql_gemm_tn", _ptr(a), a.stride(0), _ptr(b), b.stride(0),
+         _ptr(out), out.stride(0), _ptr(bias), M, N, K, dtype_code(a.dtype),
+         dtype_code(out.dtype), int(accumulate), _ptr(residual), _ptr(ws),
+         0 if ws is None else ws.numel(), stream_ptr())
     return out
 
 

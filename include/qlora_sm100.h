@@ -84,6 +84,14 @@ int ql_gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
                const float* residual, void* workspace, int64_t workspace_bytes,
                cudaStream_t stream);
+/* C[M, N] (+)= A[M, K] . B[K, N] (+ bias[N]) with B row-major, N contiguous (ldb >= N, N % 8 ==
+ * 0), read by the tensor cores as an MN-major operand: the data-gradient products dX = dY . W of
+ * the reference's backward (solution/engine.py:1239, 1293, 1301, 1316) straight from the
+ * forward-layout weight, with no transposed copy. Other arguments as ql_gemm_tn. */
+int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+               const void* bias, int M, int N, int K, int in_dtype, int out_dtype, int accumulate,
+               const float* residual, void* workspace, int64_t workspace_bytes,
+               cudaStream_t stream);
 int64_t ql_gemm_workspace_bytes(int M, int N, int K);
 
 /* ---- RMSNorm with the LoRA dropout inputs --------------------------------------------------
@@ -386,7 +394,13 @@ typedef struct {              /* what the forward keeps for the backward (all [n
   void* gu;                   /* [n, 2 I] [gate | up] (overwritten by its gradient in backward) */
   uint32_t* keep_q;           /* [n, H / 32] dropout masks of the q / v LoRA inputs as bits */
   uint32_t* keep_v;
+  void* w16;                  /* NULL, or ql_layer_weight_elems() 16-bit elements: the forward's
+                                 dequantised weights [qkv | o | gate_up | down], read again by
+                                 the backward instead of a second dequantisation */
 } ql_layer_saved;
+
+/* Elements of ql_layer_saved.w16 for a layer: (HQ + 2 HKV) D H + H HQ D + 3 I H. */
+int64_t ql_layer_weight_elems(const ql_layer_desc* layer);
 
 /* Workspace bytes of the forward (backward = 0) or backward (backward = 1) of a layer. Its first
  * 2048 bytes must be zero before the first call (GEMM tile counters); calls leave them zero. */

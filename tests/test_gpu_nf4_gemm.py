@@ -125,6 +125,29 @@ def test_gemm_matches_torch(M, N, K, dt):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(1090, 8960, 1536), (1090, 1536, 17920), (1090, 1536, 1536),
+                                   (1090, 1536, 2048), (37, 192, 64), (129, 200, 136),
+                                   (300, 96, 512), (1, 8, 8)])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_nn_matches_torch(M, N, K, dt):
+    """C = A . B with B stored [K, N] (the forward-layout weight in the data-gradient products),
+    read as an MN-major tensor-core operand."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + N * 3 + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(dt)
+    b = (torch.randn(K, N, device=DEV, generator=g) * 0.05).to(dt)
+    ref = a.float() @ b.float()
+    out = ops.gemm(a, b, b_kn=True)
+    tol = 2e-2 if dt == torch.bfloat16 else 4e-3
+    scale = ref.abs().max().item() + 1e-6
+    assert (out.float() - ref).abs().max().item() / scale < tol
+    res = torch.randn(M, N, device=DEV, generator=g)
+    out32 = ops.gemm(a, b, b_kn=True, out_dtype=torch.float32, residual=res)
+    assert (out32 - (res + out.float())).abs().max().item() / scale < 2e-3
+    assert ops.device_status() == 0
+
+
 def test_gemm_strided_output():
     """C written into columns of a wider buffer (the [gate | up] halves, the LoRA slices)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops

@@ -27,7 +27,7 @@ def _rel(a, b):
     return ((a.float().cpu() - b.float().cpu()).norm() / b.float().cpu().norm().clamp(min=1e-12)).item()
 
 
-def _run(cfg, lengths, dropout, nested, dtype=torch.float16, seed=1):
+def _run(cfg, lengths, dropout, nested, dtype=torch.float16, seed=1, keep_weights=True):
     from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
     from hack_fe30cb28_opus_5_5_ultracode_b200.model import build_qwen2_qlora, lora_parameters
 
@@ -37,7 +37,7 @@ def _run(cfg, lengths, dropout, nested, dtype=torch.float16, seed=1):
     n_items = float((labels[:, 1:] != -100).sum())
     dname = "f16" if dtype == torch.float16 else "bf16"
     W = oracle_step.weights_from_model(model, dname)  # before the engine re-points the bytes
-    engine = FusedQwen2(model, dtype=dtype)
+    engine = FusedQwen2(model, dtype=dtype, keep_weights=keep_weights)
     params = lora_parameters(model)
     gen = torch.cuda.default_generators[torch.cuda.current_device()]
     torch.cuda.manual_seed(5)
@@ -87,11 +87,15 @@ def test_fused_step_full_width_layer_bf16():
         assert _rel(g, r_) < 5e-2
 
 
-def test_fused_step_full_width_two_layers_fp16():
+@pytest.mark.parametrize("keep_weights", [True, False])
+def test_fused_step_full_width_two_layers_fp16(keep_weights):
+    """keep_weights=False: the backward dequantises each weight again instead of reading the
+    forward's copy."""
     from hack_fe30cb28_opus_5_5_ultracode_b200.model import Qwen2Config
 
     cfg = Qwen2Config(vocab_size=4096, num_hidden_layers=2)
-    engine, loss, packed, stats, grads, ref, gen = _run(cfg, [150, 64, 256, 97], 0.05, True)
+    engine, loss, packed, stats, grads, ref, gen = _run(cfg, [150, 64, 256, 97], 0.05, True,
+                                                        keep_weights=keep_weights)
     assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 2e-3
     for g, r_ in zip(grads, ref["grads"]):
         assert _rel(g, r_) < 2e-2
