@@ -224,6 +224,16 @@ int ql_lora_colsum_noalloc(const void* X, int64_t ldx, int x_dtype, const void* 
               "ql_lora_colsum_noalloc");
 }
 
+int64_t ql_lora_grads_workspace(int64_t n, const int32_t* ncols, int njobs) {
+  return ql::lora_grads_workspace(n, ncols, njobs);
+}
+
+int ql_lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, void* workspace,
+                  int64_t workspace_bytes, cudaStream_t stream) {
+  return done(ql::lora_grads(jobs, njobs, n, x_dtype, workspace, workspace_bytes, stream),
+              "ql_lora_grads");
+}
+
 int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
              int dtype, cudaStream_t stream) {
   return done(ql::embed(ids, W, h, n, H, vocab, dtype, ql::status_word(), stream), "ql_embed");

@@ -282,4 +282,16 @@ __device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
   return (uint32_t)(*reinterpret_cast<uint16_t*>(&l)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&h)) << 16);
 }
 
+// ldmatrix: four 8 x 8 16-bit matrices from shared memory (rows addressed by lanes 8i..8i+7).
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+
 }  // namespace ql

@@ -210,6 +210,217 @@ int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dt
 }
 
 // ---------------------------------------------------------------------------------------------
+// the LoRA weight gradients of a layer, all four products in one launch
+// ---------------------------------------------------------------------------------------------
+constexpr int LG_COLS = 64, LG_THREADS = 256, LG_MAXJOBS = 4, LG_MAXSPLITS = 16;
+constexpr int LG_MAXTOK = 256;  // tokens staged in shared memory at once
+constexpr int64_t LG_COUNTER_BYTES = 2048;
+
+struct LgJob {
+  const void* X;
+  int64_t ldx;
+  const void* Y;
+  float* out;
+  float* part;  // [S][nblk * 64][16]
+  int ncols, y_f32, transpose, blk0;
+  float scale;
+};
+struct LgArgs {
+  LgJob job[LG_MAXJOBS];
+  int njobs, splits;
+  int64_t n, tok_per_split;
+  int* counters;  // one per 64-column block of all jobs
+};
+
+// CTA (column block b, split sp): out^T-partial[64 cols][16] = X[toks][64]^T . Y[toks][16] on
+// the tensor cores (mma.sync m16n8k16, fp32 accumulation). Rounds of up to 256 tokens of X
+// (16-byte chunks XOR-swizzled by token: conflict-free ldmatrix) and Y (fp32 rounded to the
+// 16-bit type on the way in: the reference's fp16 dx_lo) are staged in shared memory; warp w
+// takes column tile w % 4 (16 columns) and the 16-token steps of parity w / 4, both operands
+// read with ldmatrix.trans. The two parities meet in shared memory (fixed order), the split's
+// partial goes to the workspace, and the last split of the block (counter) adds all splits in
+// split order.
+template <typename TX>
+__global__ void __launch_bounds__(LG_THREADS) lora_grads_kernel(LgArgs a) {
+  extern __shared__ __align__(16) uint8_t lg_smem[];
+  __shared__ float sp2[2][LG_COLS * 16];
+  __shared__ int last;
+  int j = 0;
+#pragma unroll
+  for (int q = 1; q < LG_MAXJOBS; ++q)
+    if (q < a.njobs && (int)blockIdx.x >= a.job[q].blk0) j = q;
+  const LgJob& J = a.job[j];
+  const int blk = blockIdx.x - J.blk0, c0 = blk * LG_COLS;
+  const int64_t t0 = blockIdx.y * a.tok_per_split;
+  const int64_t t1 = min(a.n, t0 + a.tok_per_split);
+  const int stage_tok = (int)min(a.tok_per_split, (int64_t)LG_MAXTOK);  // a multiple of 16
+  TX* sX = reinterpret_cast<TX*>(lg_smem);   // [stage_tok][64], chunk c of token t at c ^ (t & 7)
+  TX* sY = sX + stage_tok * LG_COLS;          // [stage_tok][16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = warp & 3, par = warp >> 2;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int64_t tb = t0; tb < t1; tb += stage_tok) {  // rounds of up to 256 tokens
+    const int nt = (int)min((int64_t)stage_tok, t1 - tb);
+    const int nt16 = (nt + 15) & ~15;  // rows past nt are zero
+    const TX* X = reinterpret_cast<const TX*>(J.X) + c0;
+    for (int i = threadIdx.x; i < nt16 * 8; i += LG_THREADS) {  // 8 chunks of 16 B per row
+      const int tt = i >> 3, ch = i & 7;
+      const bool ok = tt < nt && c0 + ch * 8 < J.ncols;
+      cs_cp16(sX + tt * LG_COLS + ((ch ^ (tt & 7)) << 3), ok ? X + (tb + tt) * J.ldx + ch * 8 : J.X, ok);
+    }
+    if (J.y_f32) {
+      const float* Y = reinterpret_cast<const float*>(J.Y) + tb * 16;
+      for (int i = threadIdx.x; i < nt16 * 4; i += LG_THREADS) {  // 4 values per thread
+        const int tt = i >> 2;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tt < nt) v = __ldg(reinterpret_cast<const float4*>(Y) + i);
+        TX h[4] = {from_f<TX>(v.x), from_f<TX>(v.y), from_f<TX>(v.z), from_f<TX>(v.w)};
+        *reinterpret_cast<uint2*>(sY + i * 4) = *reinterpret_cast<const uint2*>(h);
+      }
+    } else {
+      const TX* Y = reinterpret_cast<const TX*>(J.Y) + tb * 16;
+      for (int i = threadIdx.x; i < nt16 * 2; i += LG_THREADS)
+        cs_cp16(sY + i * 8, (i >> 1) < nt ? Y + i * 8 : J.Y, (i >> 1) < nt);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const int mi = lane >> 3, ri = lane & 7;  // ldmatrix: matrix, row of this lane's address
+    for (int k0 = par * 16; k0 < nt16; k0 += 32) {
+      // A = X^T (16 columns x 16 tokens): matrices (cols +0/+8) x (tokens +0/+8)
+      const int ta = k0 + ((mi >> 1) << 3) + ri;
+      const int cha = mt * 2 + (mi & 1);
+      uint32_t af[4];
+      ldsm_x4_t(sX + ta * LG_COLS + ((cha ^ (ta & 7)) << 3), af[0], af[1], af[2], af[3]);
+      // B = Y (16 tokens x 16 ranks): matrices (tokens +0/+8) x (ranks +0/+8)
+      const int tb2 = k0 + ((mi & 1) << 3) + ri;
+      uint32_t b00, b01, b10, b11;
+      ldsm_x4_t(sY + tb2 * 16 + ((mi >> 1) << 3), b00, b01, b10, b11);
+      mma16816<TX>(acc[0], af, b00, b01);
+      mma16816<TX>(acc[1], af, b10, b11);
+    }
+    __syncthreads();  // the staging buffers are refilled by the next round
+  }
+  // C fragments: column mt*16 + g (+8), ranks nt*8 + 2t (+1)
+  {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int n8 = 0; n8 < 2; ++n8) {
+      float* d0 = &sp2[par][(mt * 16 + g) * 16 + n8 * 8 + 2 * t];
+      float* d1 = &sp2[par][(mt * 16 + g + 8) * 16 + n8 * 8 + 2 * t];
+      d0[0] = acc[n8][0];
+      d0[1] = acc[n8][1];
+      d1[0] = acc[n8][2];
+      d1[1] = acc[n8][3];
+    }
+  }
+  __syncthreads();
+  const int64_t padc = (int64_t)((J.ncols + LG_COLS - 1) / LG_COLS) * LG_COLS;  // columns per split
+  float* part = J.part + ((int64_t)blockIdx.y * padc + c0) * 16;
+#pragma unroll
+  for (int e = threadIdx.x; e < LG_COLS * 16; e += LG_THREADS) __stcg(part + e, sp2[0][e] + sp2[1][e]);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(a.counters + blockIdx.x, 1);
+    last = old == a.splits - 1;
+    if (last) a.counters[blockIdx.x] = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int64_t stride = padc * 16;
+  const float* base = J.part + (int64_t)c0 * 16;
+#pragma unroll
+  for (int e = threadIdx.x; e < LG_COLS * 16; e += LG_THREADS) {
+    const int c = c0 + e / 16, r = e % 16;
+    float v[LG_MAXSPLITS];
+#pragma unroll
+    for (int q = 0; q < LG_MAXSPLITS; ++q) v[q] = q < a.splits ? __ldcg(base + q * stride + e) : 0.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < LG_MAXSPLITS; ++q)
+      if (q < a.splits) sum += v[q];  // split order
+    if (c < J.ncols) {
+      if (J.transpose) J.out[(int64_t)r * J.ncols + c] = sum * J.scale;
+      else J.out[(int64_t)c * 16 + r] = sum * J.scale;
+    }
+  }
+}
+
+static int lora_grads_splits(int64_t n, int64_t blocks) {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t s = cdiv(4LL * sms, blocks > 0 ? blocks : 1);  // about 4 CTAs per SM
+  const int64_t by_tokens = cdiv(n, 32);                  // at least 32 tokens per split
+  if (s > by_tokens) s = by_tokens;
+  if (s > LG_MAXSPLITS) s = LG_MAXSPLITS;
+  return (int)(s < 1 ? 1 : s);
+}
+
+int64_t lora_grads_workspace(int64_t n, const int32_t* ncols, int njobs) {
+  if (njobs < 0 || njobs > LG_MAXJOBS || (njobs > 0 && ncols == nullptr)) return -1;
+  int64_t blocks = 0, cols = 0;
+  for (int q = 0; q < njobs; ++q) {
+    blocks += cdiv(ncols[q], LG_COLS);
+    cols += cdiv(ncols[q], LG_COLS) * LG_COLS;
+  }
+  const int s = lora_grads_splits(n, blocks);
+  return LG_COUNTER_BYTES + ((s * cols * 16 * 4 + 255) / 256) * 256 + 256 * LG_MAXJOBS;
+}
+
+int lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, void* workspace,
+               int64_t workspace_bytes, cudaStream_t s) {
+  if (njobs <= 0 || njobs > LG_MAXJOBS || jobs == nullptr || n < 0) return QL_STATUS_BAD_ARG;
+  if (x_dtype != QL_F16 && x_dtype != QL_BF16) return QL_STATUS_BAD_ARG;
+  if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return QL_STATUS_BAD_ARG;
+  LgArgs a{};
+  a.njobs = njobs;
+  a.n = n;
+  int32_t nc[LG_MAXJOBS];
+  int64_t blocks = 0;
+  for (int q = 0; q < njobs; ++q) {
+    const ql_lora_grad_job& J = jobs[q];
+    if (J.ncols <= 0 || J.ncols % 8 != 0 || J.ldx % 8 != 0 || J.X == nullptr || J.Y == nullptr ||
+        J.out == nullptr || reinterpret_cast<uintptr_t>(J.X) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(J.Y) % 16 != 0)
+      return QL_STATUS_BAD_ARG;
+    if (J.y_dtype != QL_F32 && J.y_dtype != x_dtype) return QL_STATUS_BAD_ARG;
+    nc[q] = J.ncols;
+    a.job[q] = LgJob{J.X, J.ldx, J.Y, J.out, nullptr, J.ncols, J.y_dtype == QL_F32 ? 1 : 0,
+                     J.transpose, (int)blocks, J.scale};
+    blocks += cdiv(J.ncols, LG_COLS);
+  }
+  if (blocks * 4 > LG_COUNTER_BYTES) return QL_STATUS_UNSUPPORTED;
+  if (workspace_bytes < lora_grads_workspace(n, nc, njobs)) return QL_STATUS_BAD_ARG;
+  a.splits = lora_grads_splits(n, blocks);
+  a.tok_per_split = cdiv(cdiv(n > 0 ? n : 1, a.splits), 16) * 16;  // whole 16-token steps
+  a.splits = (int)cdiv(n > 0 ? n : 1, a.tok_per_split);
+  a.counters = static_cast<int*>(workspace);
+  float* p = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + LG_COUNTER_BYTES);
+  for (int q = 0; q < njobs; ++q) {
+    a.job[q].part = p;
+    p += (int64_t)a.splits * cdiv(nc[q], LG_COLS) * LG_COLS * 16;
+  }
+  double flops = 0, bytes = 0;
+  for (int q = 0; q < njobs; ++q) {
+    flops += 2.0 * n * nc[q] * 16;
+    bytes += (double)n * nc[q] * 2;
+  }
+  ProfScope prof(PK_COLSUM, flops, bytes, s);
+  dim3 grid((unsigned)blocks, (unsigned)a.splits);
+  const int smem = (int)(min(a.tok_per_split, (int64_t)LG_MAXTOK) * (LG_COLS + 16) * 2);
+  if (x_dtype == QL_F16) {
+    smem_optin(reinterpret_cast<const void*>(lora_grads_kernel<__half>), smem);
+    lora_grads_kernel<__half><<<grid, LG_THREADS, smem, s>>>(a);
+  } else {
+    smem_optin(reinterpret_cast<const void*>(lora_grads_kernel<__nv_bfloat16>), smem);
+    lora_grads_kernel<__nv_bfloat16><<<grid, LG_THREADS, smem, s>>>(a);
+  }
+  return launched(1);
+}
+
+// ---------------------------------------------------------------------------------------------
 // embedding gather: h[t, :] = float(W[ids[t], :])
 // ---------------------------------------------------------------------------------------------
 template <typename T>

@@ -72,9 +72,18 @@ int64_t layer_gemm_ws(const ql_layer_desc& L) {
   return m;
 }
 
+// The LoRA-gradient kernel's workspace follows at the same offset in both carves (its counters,
+// zero between launches, must not be overwritten by the forward's temporaries).
+int64_t layer_lora_ws(const ql_layer_desc& L) {
+  const int32_t nc[4] = {L.HQ * L.D, L.HKV * L.D, L.H, L.H};
+  return lora_grads_workspace(L.n, nc, 4);
+}
+
 struct FwdWs {
   void* gws;  // split-K GEMM workspace
   int64_t gws_bytes;
+  void* lgw;  // LoRA-gradient workspace (unused by the forward, reserved)
+  int64_t lgw_bytes;
   void* w;    // dequantised weight (largest of the four)
   void* a;    // [n, H] norm output (a, then b)
   void* qkv;  // [n, C]
@@ -86,6 +95,8 @@ FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
   FwdWs w;
   w.gws_bytes = layer_gemm_ws(L);
   w.gws = b.take(w.gws_bytes);
+  w.lgw_bytes = layer_lora_ws(L);
+  w.lgw = b.take(w.lgw_bytes);
   w.w = b.take(max_weight_elems(L) * e);
   w.a = b.take(n * L.H * e);
   w.qkv = b.take(n * C * e);
@@ -96,6 +107,8 @@ FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
 struct BwdWs {
   void* gws;
   int64_t gws_bytes;
+  void* lgw;
+  int64_t lgw_bytes;
   void* w;
   void* dm;      // [n, I]
   void* db;      // [n, H]
@@ -109,8 +122,6 @@ struct BwdWs {
   void* dqkv;    // [n, C]
   float* dxq;    // [n, rank]
   float* dxv;
-  float* cs;     // colsum partials
-  int64_t cs_floats;
   void* da;      // [n, H]
 };
 
@@ -119,6 +130,8 @@ BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
   BwdWs w;
   w.gws_bytes = layer_gemm_ws(L);
   w.gws = b.take(w.gws_bytes);
+  w.lgw_bytes = layer_lora_ws(L);
+  w.lgw = b.take(w.lgw_bytes);
   w.w = b.take(max_weight_elems(L) * e);
   w.dm = b.take(n * L.I * e);
   w.db = b.take(n * L.H * e);
@@ -132,13 +145,6 @@ BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
   w.dqkv = b.take(n * C * e);
   w.dxq = (float*)b.take(n * L.rank * 4);
   w.dxv = (float*)b.take(n * L.rank * 4);
-  int64_t csf = 0;
-  for (int64_t cols : {(int64_t)L.H, (int64_t)L.HQ * L.D, (int64_t)L.HKV * L.D}) {
-    const int64_t f = (int64_t)lora_colsum_splits(n, (int)cols) * cols * L.rank;
-    csf = f > csf ? f : csf;
-  }
-  w.cs_floats = csf;
-  w.cs = (float*)b.take(w.cs_floats * 4);
   w.da = b.take(n * L.H * e);
   return w;
 }
@@ -287,17 +293,15 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   rb.lora_scale = L.lora_scale; rb.n = L.n; rb.HQ = L.HQ; rb.HKV = L.HKV; rb.D = L.D;
   rb.kv_heads_in = L.HKV; rb.rank = L.rank; rb.dtype = dt; rb.grad_dtype = QL_F32;
   QL_TRY(rope_bwd(rb, s));
-  // LoRA weight gradients: dB = s g^T x_lo, dA = dx_lo^T drop(a)
+  // LoRA weight gradients in one launch: dB = s g^T x_lo, dA = dx_lo^T drop(a)
   const int64_t qcols = (int64_t)L.HQ * L.D, vcols = (int64_t)L.HKV * L.D;
   const uint8_t* dqkv = (const uint8_t*)w.dqkv;
-  QL_TRY(lora_colsum(dqkv, C, dt, S.xq, dt, n, (int)qcols, L.rank, L.lora_scale, 0, gBq, w.cs,
-                     w.cs_floats, s));
-  QL_TRY(lora_colsum(dqkv + (qcols + vcols) * esz(dt), C, dt, S.xv, dt, n, (int)vcols, L.rank,
-                     L.lora_scale, 0, gBv, w.cs, w.cs_floats, s));
-  QL_TRY(lora_colsum(S.yq, L.H, dt, w.dxq, QL_F32, n, L.H, L.rank, 1.f, 1, gAq, w.cs,
-                     w.cs_floats, s));
-  QL_TRY(lora_colsum(S.yv, L.H, dt, w.dxv, QL_F32, n, L.H, L.rank, 1.f, 1, gAv, w.cs,
-                     w.cs_floats, s));
+  const ql_lora_grad_job jobs[4] = {
+      {dqkv, C, S.xq, gBq, (int)qcols, dt, 0, L.lora_scale},
+      {dqkv + (qcols + vcols) * esz(dt), C, S.xv, gBv, (int)vcols, dt, 0, L.lora_scale},
+      {S.yq, L.H, w.dxq, gAq, L.H, QL_F32, 1, 1.f},
+      {S.yv, L.H, w.dxv, gAv, L.H, QL_F32, 1, 1.f}};
+  QL_TRY(lora_grads(jobs, 4, n, dt, w.lgw, w.lgw_bytes, s));
   if (dh_out == nullptr) return QL_STATUS_OK;  // the first layer's input is the frozen embedding
   QL_TRY(weight(L.qkv, slots.qkv, &W));  // [C, H]
   QL_TRY(gemm_nn(w.dqkv, C, W, L.H, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,

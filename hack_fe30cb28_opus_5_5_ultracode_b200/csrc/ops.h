@@ -44,6 +44,9 @@ int rope_bwd(const RopeBwdC& a, cudaStream_t s);
 int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s);
 int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t s);
 int lora_colsum_splits(int64_t n, int ncols);
+int64_t lora_grads_workspace(int64_t n, const int32_t* ncols, int njobs);
+int lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, void* workspace,
+               int64_t workspace_bytes, cudaStream_t s);
 int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
                 int ncols, int rank, float scale, int transpose, float* out, float* workspace,
                 int64_t workspace_floats, cudaStream_t s);

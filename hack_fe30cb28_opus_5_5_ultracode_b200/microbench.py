@@ -124,6 +124,10 @@ def main():
                 sec = _time(lambda i: ops.gemm(at[i % copies], bt[i % 2], out=ct[i % copies]),
                             args.iters)
                 _report("gemm_tn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
+                # the same product straight from the forward-layout weight (MN-major B)
+                sec = _time(lambda i: ops.gemm(at[i % copies], b[i % 2], out=ct[i % copies],
+                                               b_kn=True), args.iters)
+                _report("gemm_nn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
     if want("gemm") and want_shape("lm_head"):
         hn = torch.randn(n, H, device=dev, generator=g).to(dt)
         W = torch.randn(V, H, device=dev, generator=g).to(dt) * 0.02
@@ -133,6 +137,8 @@ def main():
         WT = W.t().contiguous()
         sec = _time(lambda i: ops.gemm(logits, WT), args.iters)
         _report("gemm_tn lm_head dgrad", [n, H, V], sec, flops=2.0 * n * V * H)
+        sec = _time(lambda i: ops.gemm(logits, W, b_kn=True), args.iters)
+        _report("gemm_nn lm_head dgrad", [n, H, V], sec, flops=2.0 * n * V * H)
     if want("attn"):
         lengths = [300, 257, 400, 133]
         m = sum(lengths)
@@ -205,6 +211,15 @@ def main():
         sec = _time(lambda i: ops.lora_colsum(X, Y, transpose=True, out=out, workspace=ws),
                     args.iters)
         _report("lora_colsum", [n, H], sec, nbytes=n * H * 2)
+        # the four products of a layer in one launch (what the layer backward runs)
+        C = (HQ + 2 * HKV) * D
+        gq = torch.randn(n, C, device=dev, generator=g).to(dt)
+        x16 = Y.to(dt)
+        jobs = [(gq[:, :HQ * D], x16, 2.0, False), (gq[:, (HQ + HKV) * D:], x16, 2.0, False),
+                (X, Y, 1.0, True), (X, Y, 1.0, True)]
+        sec = _time(lambda i: ops.lora_grads(jobs), args.iters)
+        _report("lora_grads (4 products)", [n, (HQ + HKV) * D + 2 * H], sec,
+                nbytes=n * ((HQ + HKV) * D + 2 * H) * 2)
     if want("ce"):
         logits = [torch.randn(n, V, device=dev, generator=g).to(dt) for _ in range(2)]
         tgt = torch.randint(0, V, (n,), device=dev, generator=g)

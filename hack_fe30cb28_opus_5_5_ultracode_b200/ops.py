@@ -292,6 +292,39 @@ def lora_colsum(X, Y, scale=1.0, transpose=False, out=None, workspace=None):
     return out
 
 
+_LG_WS = {}
+
+
+def lora_grads(jobs):
+    """The LoRA weight gradients of a layer in one launch (ql_lora_grads). jobs: up to 4 tuples
+    (X [n, ncols] 16-bit with unit column stride, Y [n, 16] 16-bit or fp32, scale, transpose);
+    returns the fp32 outputs ([ncols, 16], or [16, ncols] when transposed)."""
+    import ctypes
+
+    n = jobs[0][0].shape[0]
+    x_dtype = jobs[0][0].dtype
+    outs, structs = [], []
+    for X, Y, scale, transpose in jobs:
+        ncols = X.shape[1]
+        out = torch.empty((16, ncols) if transpose else (ncols, 16), device=X.device,
+                          dtype=torch.float32)
+        outs.append(out)
+        structs.append(dict(X=_ptr(X), ldx=X.stride(0), Y=_ptr(Y), out=_ptr(out), ncols=ncols,
+                            y_dtype=dtype_code(Y.dtype), transpose=int(transpose),
+                            scale=float(scale)))
+    arr = (_lib.STRUCTS["ql_lora_grad_job"] * len(jobs))(
+        *[_lib.struct("ql_lora_grad_job", **f) for f in structs])
+    nc = (ctypes.c_int32 * len(jobs))(*[X.shape[1] for X, _, _, _ in jobs])
+    need = int(_lib.lib().ql_lora_grads_workspace(n, ctypes.addressof(nc), len(jobs)))
+    ws = _LG_WS.get(jobs[0][0].device)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, device=jobs[0][0].device, dtype=torch.uint8)  # counters start at 0
+        _LG_WS[jobs[0][0].device] = ws
+    call("ql_lora_grads", ctypes.addressof(arr), len(jobs), n, dtype_code(x_dtype), _ptr(ws),
+         ws.numel(), stream_ptr())
+    return outs
+
+
 def embed(ids, W, out=None):
     n = ids.numel()
     h = out if out is not None else torch.empty((n, W.shape[1]), device=W.device,

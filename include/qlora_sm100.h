@@ -223,6 +223,27 @@ int ql_lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y
                    int ncols, int rank, float scale, int transpose, float* out, float* workspace,
                    int64_t workspace_floats, cudaStream_t stream);
 
+/* ---- the LoRA weight gradients of a layer in one launch -----------------------------------
+ * Replaces the four LoRA weight-gradient GEMMs of _Layer.backward (solution/engine.py:1322-1328):
+ * up to 4 products out_j = scale_j * X_j^T Y_j over the same n tokens. X_j: [n, ncols_j] 16-bit
+ * (x_dtype) with row stride ldx_j (a column slice is fine; ncols_j, ldx_j multiples of 4, X_j
+ * 8-byte aligned); Y_j: [n, rank = 16] of y_dtype_j (16-bit or QL_F32); out_j fp32 [ncols_j, 16],
+ * or [16, ncols_j] with transpose_j. The tokens are split over CTAs; each 64-column block's last
+ * split adds the splits' partials in split order (deterministic) and writes out_j. workspace:
+ * ql_lora_grads_workspace(...) bytes, 256-byte aligned, its first 2048 bytes zero before the first
+ * call (block counters; calls leave them zero). */
+typedef struct {
+  const void* X;
+  int64_t ldx;
+  const void* Y;
+  float* out;
+  int32_t ncols, y_dtype, transpose;
+  float scale;
+} ql_lora_grad_job;
+int64_t ql_lora_grads_workspace(int64_t n, const int32_t* ncols, int njobs);
+int ql_lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, void* workspace,
+                  int64_t workspace_bytes, cudaStream_t stream);
+
 /* ---- LoRA column sums with the scratch built in (no counterpart in the reference) ---------
  * The same operation and results as ql_lora_colsum, but the per-split partial sums go to a
  * scratch array compiled into this library (static device memory, QL_COLSUM_STATIC_FLOATS floats

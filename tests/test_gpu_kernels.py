@@ -252,6 +252,33 @@ def test_lora_colsum(n, ncols):
     assert torch.equal(out, o.lora_colsum(X, Y, scale=2.0))
 
 
+@pytest.mark.parametrize("n", [1, 37, 1090, 4000])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_lora_grads_one_launch(n, dt):
+    """The four LoRA weight-gradient products of a layer in one launch against torch fp32, twice
+    (deterministic, counters left at zero)."""
+    o = ops()
+    torch.manual_seed(n)
+    g = torch.randn(n, 2048, device=DEV).to(dt)  # [q | k | v] gradient row
+    xq = torch.randn(n, 16, device=DEV).to(dt)
+    xv = torch.randn(n, 16, device=DEV).to(dt)
+    yq = torch.randn(n, 1536, device=DEV).to(dt)
+    yv = torch.randn(n, 1536, device=DEV).to(dt)
+    dxq = torch.randn(n, 16, device=DEV).to(dt).float()
+    dxv = torch.randn(n, 16, device=DEV).to(dt).float()
+    jobs = [(g[:, :1536], xq, 2.0, False), (g[:, 1792:], xv, 2.0, False), (yq, dxq, 1.0, True),
+            (yv, dxv, 1.0, True)]
+    outs = o.lora_grads(jobs)
+    refs = [2.0 * g[:, :1536].float().t() @ xq.float(), 2.0 * g[:, 1792:].float().t() @ xv.float(),
+            (yq.float().t() @ dxq).t(), (yv.float().t() @ dxv).t()]
+    for out, ref in zip(outs, refs):
+        close(out, ref, 1e-3 * max(1.0, math.sqrt(n)))
+    again = o.lora_grads(jobs)
+    for a, b in zip(outs, again):
+        assert torch.equal(a, b)
+    assert o.device_status() == 0
+
+
 def test_embed():
     o = ops()
     W = torch.randn(3000, 256, device=DEV).half()
