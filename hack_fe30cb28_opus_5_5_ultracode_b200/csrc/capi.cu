@@ -115,6 +115,12 @@ int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
 
 int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
+int ql_gemm_set_mode(int mode) {
+  if (mode < 0 || mode > 2) return done(QL_STATUS_BAD_ARG, "ql_gemm_set_mode");
+  ql::gemm_set_mode(mode);
+  return QL_STATUS_OK;
+}
+
 }  // extern "C"
 
 extern "C" {

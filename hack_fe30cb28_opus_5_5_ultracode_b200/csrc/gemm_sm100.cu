@@ -16,6 +16,8 @@
 //               the end of a tile, signals the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld of their 32 TMEM lanes, bias add, conversion, stores.
 // The accumulator of tile t+1 is written while the epilogue drains tile t.
+#include <atomic>
+
 #include "common.cuh"
 #include "profile.h"
 
@@ -285,6 +287,190 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// 2-SM variant: clusters of two CTAs compute 256 x BN pair tiles with tcgen05.mma.cta_group::2.
+// CTA r of the pair loads rows [128 r, 128 r + 128) of the A tile and half r of the B tile (BN/2
+// rows, or BN/2 columns of an MN-major B); the even CTA issues the MMAs, which read both halves
+// and leave rows 0-127 of the accumulator in its TMEM and rows 128-255 in the odd CTA's. Per CTA
+// and K step the operands are 16 KB + BN x 64 B for 128 x BN outputs: a third fewer bytes per
+// FLOP than the single-CTA tile at BN = 256, the limit of that kernel.
+//   full[s]   even CTA's: its producer expects both CTAs' bytes; the odd CTA's loads count there
+//   empty[s]  each CTA's: the even CTA's MMA commit arrives in both (CTA mask 0b11)
+//   tfull[a]  each CTA's: the accumulator is complete (commit to both)
+//   tempty[a] even CTA's: 8 arrivals, the 4 epilogue warps of each CTA
+// ---------------------------------------------------------------------------------------------
+template <int BN>
+struct PairCfg {
+  static constexpr int BM = 128, BK = 64, HB = BN / 2;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = HB * BK * 2;  // this CTA's half of B
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_FIT = (225 * 1024 - 1280) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "UMMA N (M = 256) and 32-column epilogue");
+  static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
+};
+
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, GemmArgs p) {
+  using Cfg = PairCfg<BN>;
+  using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + Cfg::STAGES;
+  uint64_t* tfull = empty + Cfg::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_pairs = (int)cdiv(p.M, 2 * Cfg::BM), n_tiles = (int)cdiv(p.N, BN);
+  const int num_units = m_pairs * n_tiles;
+  const int k_blocks = (int)cdiv(p.K, Cfg::BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair; u < num_units && ok; u += npairs) {
+        const int mp = u % m_pairs, nb = u / m_pairs;
+        const int arow = mp * 2 * Cfg::BM + (int)rank * Cfg::BM;
+        const int brow = nb * BN + (int)rank * Cfg::HB;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          tma_load_2d_pair(sa, &tma_a, &full[stage], kb * Cfg::BK, arow);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < Cfg::HB / 64; ++j)
+              tma_load_2d_pair(sb + j * 8192, &tma_b, &full[stage], brow + j * 64, kb * Cfg::BK);
+          } else {
+            tma_load_2d_pair(sb, &tma_b, &full[stage], kb * Cfg::BK, brow);
+          }
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_f16(IS_BF16, 2 * Cfg::BM, BN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int u = pair; u < num_units && ok; u += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, 8192, 1024)
+                                     : umma_desc_k_sw128(sb + k * 32);
+            umma_f16_pair(tmem_d, umma_desc_k_sw128(sa + k * 32), db, idesc,
+                          (kb != 0 || k != 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) umma_commit_pair(&tfull[acc], 0x3);
+      }
+    }
+  } else {
+    // epilogue warps 2..5 of each CTA: TMEM lane quadrant = warp % 4, this CTA's 128 rows
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    OutT* C = reinterpret_cast<OutT*>(p.C);
+    const InT* bias = reinterpret_cast<const InT*>(p.bias);
+    for (int u = pair; u < num_units; u += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
+      tc_fence_after();
+      const int mp = u % m_pairs, nb = u / m_pairs;
+      const int row = mp * 2 * Cfg::BM + (int)rank * Cfg::BM + row_in_tile;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(taddr + c, v);
+        const int col0 = nb * BN + c;
+        if (row < p.M && col0 < p.N) {
+          const int ncols = min(32, p.N - col0);
+          if (bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < ncols) v[i] += to_f<InT>(bias[col0 + i]);
+          }
+          OutT* dst = C + (int64_t)row * p.ldc + col0;
+          if constexpr (sizeof(OutT) == 4) {
+            if (p.residual != nullptr) {
+              const float* res = p.residual + (int64_t)row * p.ldc + col0;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < ncols) v[i] = to_f<InT>(from_f<InT>(v[i])) + res[i];
+            } else if (p.accumulate) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < ncols) v[i] += to_f<OutT>(dst[i]);
+            }
+          }
+          store_row32<OutT>(dst, v, ncols);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_cluster(&tempty[acc], 0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the pair's MMAs and both epilogues are done before the collective dealloc
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -350,6 +536,76 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   return launched(1);
 }
 
+// Clusters of two CTAs that can be resident at once (a GPC's SM count can be odd), per kernel.
+template <typename K>
+static int pair_slots(K kern, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (num_sms() / 2));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();
+    clusters = num_sms() / 2;
+  }
+  return clusters;
+}
+
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                       cudaStream_t stream) {
+  using Cfg = PairCfg<BN>;
+  auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN>;
+  static int slots = 0;  // one per instantiation
+  if (slots == 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) !=
+        cudaSuccess)
+      return QL_STATUS_CUDA;
+    slots = pair_slots(kern, Cfg::SMEM_BYTES);
+  }
+  const int units = (int)(cdiv(a.M, 2 * Cfg::BM) * cdiv(a.N, BN));
+  const int pairs = units < slots ? units : slots;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, a) != cudaSuccess) return QL_STATUS_CUDA;
+  return launched(1);
+}
+
+template <int BN, bool IS_BF16, bool B_MN>
+static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                             cudaStream_t s) {
+  switch (a.out_dtype) {
+    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, a, s);
+    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, a, s);
+    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, a, s);
+  }
+  return QL_STATUS_BAD_ARG;
+}
+
+template <int BN, bool B_MN>
+static int dispatch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+                         bool bf16, cudaStream_t s) {
+  return bf16 ? dispatch_pair_out<BN, true, B_MN>(ma, mb, a, s)
+              : dispatch_pair_out<BN, false, B_MN>(ma, mb, a, s);
+}
+
 template <int BN, bool IS_BF16, bool B_MN>
 static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
                         cudaStream_t s) {
@@ -376,7 +632,21 @@ struct GemmPlan {
   int bn;
   int64_t tiles;
   int splits, kb_per_split;
+  bool pair;  // 2-SM pair tiles (256 x bn)
 };
+
+// Tile-kind selection: 0 = cost model, 1 = single-CTA tiles only, 2 = pair tiles where possible.
+static std::atomic<int> g_gemm_mode{0};
+void gemm_set_mode(int mode) { g_gemm_mode.store(mode); }
+
+// Clocks of one 64-deep K step of a CTA holding a 128-row tile of width w: the larger of its
+// operand fill (rows of A and B x 128 B at about 64 B per clock into shared memory) and its MMA
+// time (about 7,700 dense FLOP per clock per SM).
+static double kstep_clocks(int a_rows, int b_rows, int w) {
+  const double fill = (double)(a_rows + b_rows) * 128.0 / 64.0;
+  const double mma = 2.0 * 128.0 * w * 64.0 / 7700.0;
+  return fill > mma ? fill : mma;
+}
 
 // Tile width and K splits of a shape. BN: the fewest waves of output tiles over the SMs, each
 // wave costed as BN + 64 (a tile streams 128 + BN rows of A and B per K step and does BN columns
@@ -386,7 +656,7 @@ struct GemmPlan {
 // it beats the unsplit launch by 5 points.
 static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   static const int widths[] = {256, 224, 192, 128, 96};
-  GemmPlan g{256, 0, 1, 0};
+  GemmPlan g{256, 0, 1, 0, false};
   int64_t best = -1;
   for (int bn : widths) {
     if (b_mn && bn % 64 != 0) continue;  // an MN-major B tile is whole 64-column boxes
@@ -400,6 +670,29 @@ static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   }
   const int k_blocks = (int)cdiv(K, 64);
   g.kb_per_split = k_blocks;
+  // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
+  // K <= 4096: the gate/up and lm_head forwards), the shapes where they measured faster than the
+  // single-CTA tiles at 1-4K rows. Elsewhere the 256-row pairs waste rows of M and were slower.
+  const int mode = g_gemm_mode.load();
+  if (mode == 2 || (mode == 0 && !b_mn && N >= 16384 && K <= 4096 && M >= 512)) {
+    int pbn = 0;
+    int64_t punits = 0;
+    double pbest = 0.0;
+    for (int bn : {256, 192, 128}) {
+      if (b_mn && (bn / 2) % 64 != 0) continue;  // each CTA's half of an MN-major B: whole boxes
+      const int64_t units = cdiv(M, 256) * cdiv(N, bn);
+      const double cost = (double)cdiv(units, sms / 2) * kstep_clocks(128, bn / 2, bn);
+      if (pbn == 0 || cost < pbest) {
+        pbest = cost;
+        pbn = bn;
+        punits = units;
+      }
+    }
+    g.pair = true;
+    g.bn = pbn;
+    g.tiles = punits;
+    return g;
+  }
   if (g.tiles >= 2 * (int64_t)sms || g.tiles * 4 > kCounterBytes) return g;
   auto eff = [&](int s) {
     const int64_t u = g.tiles * s;
@@ -459,7 +752,8 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
   if (b_mn) {
     if (make_kmajor_map(&mb, B, K, N, ldb, 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
   } else {
-    if (make_kmajor_map(&mb, B, N, K, ldb, g.bn, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+    if (make_kmajor_map(&mb, B, N, K, ldb, g.pair ? g.bn / 2 : g.bn, bf16) != QL_STATUS_OK)
+      return QL_STATUS_CUDA;
   }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
              g.kb_per_split, nullptr, nullptr};
@@ -467,6 +761,17 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
     uint8_t* w = static_cast<uint8_t*>(workspace);
     a.counters = reinterpret_cast<int*>(w);
     a.ws = reinterpret_cast<float*>(w + kCounterBytes);
+  }
+  if (g.pair) {
+    if (b_mn) {
+      if (g.bn == 128) return dispatch_pair<128, true>(ma, mb, a, bf16, stream);
+      return dispatch_pair<256, true>(ma, mb, a, bf16, stream);
+    }
+    switch (g.bn) {
+      case 128: return dispatch_pair<128, false>(ma, mb, a, bf16, stream);
+      case 192: return dispatch_pair<192, false>(ma, mb, a, bf16, stream);
+      default: return dispatch_pair<256, false>(ma, mb, a, bf16, stream);
+    }
   }
   if (b_mn) {
     switch (g.bn) {

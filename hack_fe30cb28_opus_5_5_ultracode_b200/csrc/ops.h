@@ -23,6 +23,7 @@ int gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
             const float* residual, int* err, cudaStream_t stream, void* workspace = nullptr,
             int64_t workspace_bytes = 0);
 int64_t gemm_workspace_bytes(int M, int N, int K);
+void gemm_set_mode(int mode);
 
 typedef ql_rms_fwd_args RmsFwdC;
 typedef ql_rms_bwd_args RmsBwdC;

@@ -79,10 +79,13 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=1090)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--gemm-mode", type=int, default=0,
+                    help="GEMM tile kind: 0 cost model, 1 single-CTA, 2 2-SM pair tiles")
     ap.add_argument("--only", default=None,
                     help="gemm | gemm:<qkv|o|gate_up|down|lm_head> | dequant | attn | glu | rms | ce")
     args = ap.parse_args()
     dev = torch.device("cuda")
+    ops.gemm_set_mode(args.gemm_mode)
     cfg = QWEN25_1P5B
     n, H, I, V = args.tokens, cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
     HQ, HKV, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim

@@ -83,6 +83,11 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
     return out
 
 
+def gemm_set_mode(mode):
+    """Tile kind of the GEMMs: 0 per-shape cost model, 1 single-CTA tiles, 2 2-SM pair tiles."""
+    call("ql_gemm_set_mode", int(mode))
+
+
 _GEMM_WS = {}
 
 

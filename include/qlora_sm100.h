@@ -93,6 +93,10 @@ int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                const float* residual, void* workspace, int64_t workspace_bytes,
                cudaStream_t stream);
 int64_t ql_gemm_workspace_bytes(int M, int N, int K);
+/* Tile kind of ql_gemm_tn / ql_gemm_nn for this process (a tuning and test switch, no counterpart
+ * in the reference): 0 = chosen per shape by the cost model (default), 1 = single-CTA 128-row
+ * tiles only, 2 = 2-SM 256-row pair tiles (tcgen05 cta_group::2) for every shape they support. */
+int ql_gemm_set_mode(int mode);
 
 /* ---- RMSNorm with the LoRA dropout inputs --------------------------------------------------
  * Dropout fields (shared by both structs): the mask is PyTorch's CUDA dropout mask of the padded

@@ -148,6 +148,37 @@ def test_gemm_nn_matches_torch(M, N, K, dt):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K,b_kn", [(256, 256, 128, False), (1090, 1536, 1536, False),
+                                        (1090, 17920, 1536, False), (1090, 8960, 1536, False),
+                                        (37, 200, 64, False), (1000, 151936 // 8, 1536, False),
+                                        (1090, 1536, 8960, True), (1090, 1536, 17920, True),
+                                        (129, 128, 136, True), (300, 8960, 1536, True)])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_pair_tiles(M, N, K, b_kn, dt):
+    """The 2-SM path (256-row pair tiles over a CTA pair, tcgen05 cta_group::2) forced on for
+    every shape: against torch, with the residual epilogue, and bit-equal on a second call."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(M * 5 + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).to(dt)
+    b = (torch.randn(*((K, N) if b_kn else (N, K)), device=DEV, generator=g) * 0.05).to(dt)
+    ref = a.float() @ (b.float() if b_kn else b.float().t())
+    res = torch.randn(M, N, device=DEV, generator=g)
+    ops.gemm_set_mode(2)
+    try:
+        out = ops.gemm(a, b, b_kn=b_kn)
+        again = ops.gemm(a, b, b_kn=b_kn)
+        out32 = ops.gemm(a, b, b_kn=b_kn, out_dtype=torch.float32, residual=res)
+    finally:
+        ops.gemm_set_mode(0)
+    tol = 2e-2 if dt == torch.bfloat16 else 4e-3
+    scale = ref.abs().max().item() + 1e-6
+    assert (out.float() - ref).abs().max().item() / scale < tol
+    assert torch.equal(out, again)
+    assert (out32 - (res + out.float())).abs().max().item() / scale < 2e-3
+    assert ops.device_status() == 0
+
+
 def test_gemm_strided_output():
     """C written into columns of a wider buffer (the [gate | up] halves, the LoRA slices)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
@@ -175,7 +206,17 @@ def test_bf16_helpers():
 def test_gemm_split_k(M, N, K, dt):
     """Shapes with too few output tiles to fill the GPU split K; the partial sums are added in a
     fixed order, so two calls agree bit for bit, and the result matches the unsplit GEMM (no
-    workspace) to rounding."""
+    workspace) to rounding. Split-K belongs to the single-CTA tiles: those are forced here."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    ops.gemm_set_mode(1)
+    try:
+        _split_k_case(M, N, K, dt)
+    finally:
+        ops.gemm_set_mode(0)
+
+
+def _split_k_case(M, N, K, dt):
     from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
 
     assert _lib.lib().ql_gemm_workspace_bytes(M, N, K) > 0
