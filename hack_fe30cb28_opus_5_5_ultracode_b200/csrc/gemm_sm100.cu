@@ -17,6 +17,7 @@
 //   warps 2-5   epilogue: tcgen05.ld of their 32 TMEM lanes, bias add, conversion, stores.
 // The accumulator of tile t+1 is written while the epilogue drains tile t.
 #include <atomic>
+#include <cstring>
 
 #include "common.cuh"
 #include "profile.h"
@@ -38,20 +39,25 @@ struct GemmArgs {
   int splits, kb_per_split;
   float* ws;
   int* counters;
+  int tma_c;  // 16-bit C written by TMA tensor stores from per-warp shared-memory staging
 };
 
-template <int BN>
+// Epilogue staging for TMA stores of a 16-bit C: per epilogue warp two 32 x 32 buffers of 2 KB.
+constexpr int EPI_BYTES = 4 * 2 * 2048;
+
+template <int BN, bool kEpi = false>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI = kEpi ? EPI_BYTES : 0;  // TMA-store staging (16-bit outputs)
   // as many ring slots as fit in 225 KB (at most 8)
-  static constexpr int STAGES_FIT = (225 * 1024 - 1280) / STAGE_BYTES;
+  static constexpr int STAGES_FIT = (225 * 1024 - 1280 - EPI) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   // two accumulators of BN fp32 columns; the allocation is a power of two >= 32 columns
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (M = 128) and 32-column epilogue");
   static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
 };
@@ -82,15 +88,43 @@ __device__ __forceinline__ void store_row32(OutT* dst, const float* v, int ncols
   }
 }
 
+// One 32-row x 32-column chunk of a 16-bit C from this warp, through shared memory and a TMA
+// tensor store: rows staged as 64-byte segments with the 64-byte swizzle (16-byte unit u of row
+// r at u ^ ((r >> 1) & 3): conflict-free), two buffers per warp, lane 0 issuing the store. The
+// tensor map clips rows and columns past C's edge.
+template <typename OutT>
+__device__ __forceinline__ void epi_tma_chunk(const CUtensorMap* map, uint8_t* stage, int& buf,
+                                              const float* v, int x, int y) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* stg = stage + buf * 2048;
+  if (lane == 0) bulk_wait_read<1>();  // the store issued from this buffer two chunks ago
+  __syncwarp();
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint4 w = make_uint4(pack_t2<OutT>(v[8 * u], v[8 * u + 1]), pack_t2<OutT>(v[8 * u + 2], v[8 * u + 3]),
+                               pack_t2<OutT>(v[8 * u + 4], v[8 * u + 5]), pack_t2<OutT>(v[8 * u + 6], v[8 * u + 7]));
+    *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, stg, x, y);
+    bulk_commit();
+  }
+  buf ^= 1;
+}
+
 template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   GemmArgs p) {
-  using Cfg = GemmCfg<BN>;
+                   const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
+  constexpr bool kTmaC = sizeof(OutT) == 2;
+  using Cfg = GemmCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint8_t* epi_stage = smem + Cfg::STAGES * Cfg::STAGE_BYTES;  // EPI bytes (16-bit C only)
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::EPI);
   uint64_t* empty = full + Cfg::STAGES;
   uint64_t* tfull = empty + Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -189,6 +223,7 @@ __global__ void __launch_bounds__(192, 1)
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const InT* bias = reinterpret_cast<const InT*>(p.bias);
     __shared__ int last_flag;
+    int ebuf = 0;  // TMA-store staging buffer of this warp
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       const int tile = u / S, sp = u % S;
       const int acc = local & 1;
@@ -250,6 +285,20 @@ __global__ void __launch_bounds__(192, 1)
             tmem_ld32(taddr + c, v);
           }
           const int col0 = nb * BN + c;
+          if constexpr (kTmaC) {
+            if (p.tma_c) {
+              const int wrow0 = mb * Cfg::BM + quad * 32;  // this warp's 32 rows
+              if (col0 < p.N && wrow0 < p.M) {
+                if (bias != nullptr) {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i)
+                    if (col0 + i < p.N) v[i] += to_f<InT>(bias[col0 + i]);
+                }
+                epi_tma_chunk<OutT>(&tma_c, epi_stage + quad * 4096, ebuf, v, col0, wrow0);
+              }
+              continue;
+            }
+          }
           if (row < p.M && col0 < p.N) {
             const int ncols = min(32, p.N - col0);
             if (bias != nullptr) {
@@ -277,6 +326,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    if (kTmaC && p.tma_c && lane == 0) bulk_wait<0>();  // this warp's stores are complete
   }
   tc_fence_before();
   __syncthreads();
@@ -298,16 +348,17 @@ __global__ void __launch_bounds__(192, 1)
 //   tfull[a]  each CTA's: the accumulator is complete (commit to both)
 //   tempty[a] even CTA's: 8 arrivals, the 4 epilogue warps of each CTA
 // ---------------------------------------------------------------------------------------------
-template <int BN>
+template <int BN, bool kEpi = false>
 struct PairCfg {
   static constexpr int BM = 128, BK = 64, HB = BN / 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = HB * BK * 2;  // this CTA's half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES_FIT = (225 * 1024 - 1280) / STAGE_BYTES;
+  static constexpr int EPI = kEpi ? EPI_BYTES : 0;
+  static constexpr int STAGES_FIT = (225 * 1024 - 1280 - EPI) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI + 1024 + 256;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "UMMA N (M = 256) and 32-column epilogue");
   static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
 };
@@ -315,12 +366,15 @@ struct PairCfg {
 template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, GemmArgs p) {
-  using Cfg = PairCfg<BN>;
+                     const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
+  constexpr bool kTmaC = sizeof(OutT) == 2;
+  using Cfg = PairCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint8_t* epi_stage = smem + Cfg::STAGES * Cfg::STAGE_BYTES;  // EPI bytes (16-bit C only)
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::EPI);
   uint64_t* empty = full + Cfg::STAGES;
   uint64_t* tfull = empty + Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -417,6 +471,7 @@ __global__ void __launch_bounds__(192, 1)
     int local = 0;
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const InT* bias = reinterpret_cast<const InT*>(p.bias);
+    int ebuf = 0;
     for (int u = pair; u < num_units; u += npairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -430,6 +485,20 @@ __global__ void __launch_bounds__(192, 1)
         float v[32];
         tmem_ld32(taddr + c, v);
         const int col0 = nb * BN + c;
+        if constexpr (kTmaC) {
+          if (p.tma_c) {
+            const int wrow0 = mp * 2 * Cfg::BM + (int)rank * Cfg::BM + quad * 32;
+            if (col0 < p.N && wrow0 < p.M) {
+              if (bias != nullptr) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (col0 + i < p.N) v[i] += to_f<InT>(bias[col0 + i]);
+              }
+              epi_tma_chunk<OutT>(&tma_c, epi_stage + quad * 4096, ebuf, v, col0, wrow0);
+            }
+            continue;
+          }
+        }
         if (row < p.M && col0 < p.N) {
           const int ncols = min(32, p.N - col0);
           if (bias != nullptr) {
@@ -460,6 +529,7 @@ __global__ void __launch_bounds__(192, 1)
         else mbar_arrive_cluster(&tempty[acc], 0);
       }
     }
+    if (kTmaC && p.tma_c && lane == 0) bulk_wait<0>();
   }
   tc_fence_before();
   __syncthreads();
@@ -507,6 +577,23 @@ static int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int6
   return r == CUDA_SUCCESS ? QL_STATUS_OK : QL_STATUS_CUDA;
 }
 
+// A row-major [rows, cols] 16-bit C with row stride ld (elements), boxes of 32 x 32 staged with
+// the 64-byte swizzle (rows of 64 bytes).
+static int make_store_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                          bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return QL_STATUS_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
 static int num_sms() {
   static int sms = 0;
   if (sms == 0) {
@@ -519,9 +606,9 @@ static int num_sms() {
 }
 
 template <int BN, bool IS_BF16, typename OutT, bool B_MN>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                        cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, sizeof(OutT) == 2>;
   auto kern = gemm_tn_kernel<BN, IS_BF16, OutT, B_MN>;
   static bool configured = false;  // one static per instantiation
   if (!configured) {
@@ -532,7 +619,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   }
   const int units = (int)(cdiv(a.M, 128) * cdiv(a.N, BN)) * a.splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, a);
+  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, mc, a);
   return launched(1);
 }
 
@@ -559,9 +646,9 @@ static int pair_slots(K kern, int smem) {
 }
 
 template <int BN, bool IS_BF16, typename OutT, bool B_MN>
-static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                        cudaStream_t stream) {
-  using Cfg = PairCfg<BN>;
+  using Cfg = PairCfg<BN, sizeof(OutT) == 2>;
   auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN>;
   static int slots = 0;  // one per instantiation
   if (slots == 0) {
@@ -584,44 +671,44 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, a) != cudaSuccess) return QL_STATUS_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a) != cudaSuccess) return QL_STATUS_CUDA;
   return launched(1);
 }
 
 template <int BN, bool IS_BF16, bool B_MN>
-static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                              cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, a, s);
-    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, a, s);
-    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, a, s);
+    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, mc, a, s);
+    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, a, s);
+    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, mc, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
 
 template <int BN, bool B_MN>
-static int dispatch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+static int dispatch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                          bool bf16, cudaStream_t s) {
-  return bf16 ? dispatch_pair_out<BN, true, B_MN>(ma, mb, a, s)
-              : dispatch_pair_out<BN, false, B_MN>(ma, mb, a, s);
+  return bf16 ? dispatch_pair_out<BN, true, B_MN>(ma, mb, mc, a, s)
+              : dispatch_pair_out<BN, false, B_MN>(ma, mb, mc, a, s);
 }
 
 template <int BN, bool IS_BF16, bool B_MN>
-static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
+static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                         cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_gemm<BN, IS_BF16, __half, B_MN>(ma, mb, a, s);
-    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, a, s);
-    case QL_F32: return launch_gemm<BN, IS_BF16, float, B_MN>(ma, mb, a, s);
+    case QL_F16: return launch_gemm<BN, IS_BF16, __half, B_MN>(ma, mb, mc, a, s);
+    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, a, s);
+    case QL_F32: return launch_gemm<BN, IS_BF16, float, B_MN>(ma, mb, mc, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
 
 template <int BN, bool B_MN>
-static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, bool bf16,
+static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a, bool bf16,
                        cudaStream_t s) {
-  return bf16 ? dispatch_out<BN, true, B_MN>(ma, mb, a, s)
-              : dispatch_out<BN, false, B_MN>(ma, mb, a, s);
+  return bf16 ? dispatch_out<BN, true, B_MN>(ma, mb, mc, a, s)
+              : dispatch_out<BN, false, B_MN>(ma, mb, mc, a, s);
 }
 
 // Split-K workspace: tile counters first (a fixed region, left all-zero by every launch, so
@@ -756,7 +843,15 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
       return QL_STATUS_CUDA;
   }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
-             g.kb_per_split, nullptr, nullptr};
+             g.kb_per_split, nullptr, nullptr, 0};
+  // 16-bit C with no read-modify epilogue: TMA tensor stores (needs a 16-byte aligned C and row
+  // stride); otherwise per-thread row stores and an unused map
+  CUtensorMap mc;
+  std::memset(&mc, 0, sizeof(mc));
+  if (out_dtype != QL_F32 && residual == nullptr && !accumulate &&
+      reinterpret_cast<uintptr_t>(C) % 16 == 0 && (ldc * 2) % 16 == 0 &&
+      make_store_map(&mc, C, M, N, ldc, out_dtype == QL_BF16) == QL_STATUS_OK)
+    a.tma_c = 1;
   if (g.splits > 1) {
     uint8_t* w = static_cast<uint8_t*>(workspace);
     a.counters = reinterpret_cast<int*>(w);
@@ -764,28 +859,28 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
   }
   if (g.pair) {
     if (b_mn) {
-      if (g.bn == 128) return dispatch_pair<128, true>(ma, mb, a, bf16, stream);
-      return dispatch_pair<256, true>(ma, mb, a, bf16, stream);
+      if (g.bn == 128) return dispatch_pair<128, true>(ma, mb, mc, a, bf16, stream);
+      return dispatch_pair<256, true>(ma, mb, mc, a, bf16, stream);
     }
     switch (g.bn) {
-      case 128: return dispatch_pair<128, false>(ma, mb, a, bf16, stream);
-      case 192: return dispatch_pair<192, false>(ma, mb, a, bf16, stream);
-      default: return dispatch_pair<256, false>(ma, mb, a, bf16, stream);
+      case 128: return dispatch_pair<128, false>(ma, mb, mc, a, bf16, stream);
+      case 192: return dispatch_pair<192, false>(ma, mb, mc, a, bf16, stream);
+      default: return dispatch_pair<256, false>(ma, mb, mc, a, bf16, stream);
     }
   }
   if (b_mn) {
     switch (g.bn) {
-      case 128: return dispatch_in<128, true>(ma, mb, a, bf16, stream);
-      case 192: return dispatch_in<192, true>(ma, mb, a, bf16, stream);
-      default: return dispatch_in<256, true>(ma, mb, a, bf16, stream);
+      case 128: return dispatch_in<128, true>(ma, mb, mc, a, bf16, stream);
+      case 192: return dispatch_in<192, true>(ma, mb, mc, a, bf16, stream);
+      default: return dispatch_in<256, true>(ma, mb, mc, a, bf16, stream);
     }
   }
   switch (g.bn) {
-    case 96: return dispatch_in<96, false>(ma, mb, a, bf16, stream);
-    case 128: return dispatch_in<128, false>(ma, mb, a, bf16, stream);
-    case 192: return dispatch_in<192, false>(ma, mb, a, bf16, stream);
-    case 224: return dispatch_in<224, false>(ma, mb, a, bf16, stream);
-    default: return dispatch_in<256, false>(ma, mb, a, bf16, stream);
+    case 96: return dispatch_in<96, false>(ma, mb, mc, a, bf16, stream);
+    case 128: return dispatch_in<128, false>(ma, mb, mc, a, bf16, stream);
+    case 192: return dispatch_in<192, false>(ma, mb, mc, a, bf16, stream);
+    case 224: return dispatch_in<224, false>(ma, mb, mc, a, bf16, stream);
+    default: return dispatch_in<256, false>(ma, mb, mc, a, bf16, stream);
   }
 }
 
