@@ -115,6 +115,15 @@ int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
 
 int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
+int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, void* C,
+                int64_t ldc, const void* bias, int M, int in_dtype, int out_dtype, int accumulate,
+                const float* residual, cudaStream_t stream) {
+  if (W == nullptr) return done(QL_STATUS_BAD_ARG, "ql_gemm_nf4");
+  return done(ql::gemm_nf4(A, lda, *W, layout, C, ldc, bias, M, in_dtype, out_dtype, accumulate,
+                           residual, ql::status_word(), stream),
+              "ql_gemm_nf4");
+}
+
 int ql_gemm_set_mode(int mode) {
   if (mode < 0 || mode > 2) return done(QL_STATUS_BAD_ARG, "ql_gemm_set_mode");
   ql::gemm_set_mode(mode);

@@ -72,6 +72,9 @@ int scatter_rows(const float* src, const int64_t* idx, const float* scale, float
 }  // namespace ql
 
 namespace ql {
+int gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight& W, int layout, void* C, int64_t ldc,
+             const void* bias, int M, int in_dtype, int out_dtype, int accumulate,
+             const float* residual, int* err, cudaStream_t stream);
 int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward);
 int64_t layer_weight_elems(const ql_layer_desc& L);
 int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,

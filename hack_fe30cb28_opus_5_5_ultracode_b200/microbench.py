@@ -127,6 +127,14 @@ def main():
                 sec = _time(lambda i: ops.gemm(at[i % copies], bt[i % 2], out=ct[i % copies]),
                             args.iters)
                 _report("gemm_tn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
+                # NF4 dequantised inside the GEMM (no 16-bit weight in HBM), both layouts
+                sec = _time(lambda i: ops.gemm_nf4(a[i % copies], ws[i % 2], layout=0,
+                                                   out=c[i % copies]), args.iters)
+                _report("gemm_nf4 " + name, [n, N, K], sec, flops=2.0 * n * N * K)
+                if K % 64 == 0 and N % 64 == 0:
+                    sec = _time(lambda i: ops.gemm_nf4(at[i % copies], ws[i % 2], layout=1,
+                                                       out=ct[i % copies]), args.iters)
+                    _report("gemm_nf4 dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
                 # the same product straight from the forward-layout weight (MN-major B)
                 sec = _time(lambda i: ops.gemm(at[i % copies], b[i % 2], out=ct[i % copies],
                                                b_kn=True), args.iters)

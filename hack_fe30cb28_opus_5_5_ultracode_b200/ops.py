@@ -52,6 +52,34 @@ def nf4_dequant(w, out=None, transpose=False, dtype=torch.float16):
     return out
 
 
+def nf4_weight_struct(w):
+    """The ql_nf4_weight view of an NF4 weight object (as ops.nf4_dequant reads it)."""
+    rows, cols = w.shape
+    return _lib.struct("ql_nf4_weight", packed=_ptr(w.packed), absmax=_ptr(w.absmax),
+                       code=_ptr(w.code), code2=_ptr(w.code2), absmax2=_ptr(w.absmax2),
+                       offsets=_ptr(w.offsets), rows=rows, cols=cols,
+                       seg1=int(getattr(w, "seg1", INT_MAX)), seg2=int(getattr(w, "seg2", INT_MAX)),
+                       nested=int(w.nested), bs2=int(w.bs2))
+
+
+def gemm_nf4(a, w, layout=0, out=None, bias=None, accumulate=False, out_dtype=None,
+             residual=None):
+    """out = a @ W^T (layout 0, W [N, K]) or a @ W (layout 1, W [K, N]) with the NF4 weight w
+    dequantised inside the kernel (ql_gemm_nf4)."""
+    M, K = a.shape
+    rows, cols = w.shape
+    N = rows if layout == 0 else cols
+    if (cols if layout == 0 else rows) != K:
+        raise ValueError(f"inner dimensions differ: {a.shape} x NF4 {w.shape} (layout {layout})")
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=out_dtype or a.dtype)
+    ws = nf4_weight_struct(w)
+    call("ql_gemm_nf4", _ptr(a), a.stride(0), ctypes_ref(ws), int(layout), _ptr(out),
+         out.stride(0), _ptr(bias), M, dtype_code(a.dtype), dtype_code(out.dtype),
+         int(accumulate), _ptr(residual), stream_ptr())
+    return out
+
+
 # ---------------------------------------------------------------------------------------------
 # GEMM
 # ---------------------------------------------------------------------------------------------

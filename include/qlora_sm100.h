@@ -382,6 +382,18 @@ typedef struct {
   int32_t nested, bs2;
 } ql_nf4_weight;
 
+/* GEMM with the NF4 weight dequantised inside the kernel (shared memory only, the 16-bit weight
+ * never reaches HBM): replaces the reference's dequant_into + cuBLAS pairs (solution/engine.py:
+ * 103-109 with 1081-1093, 1111-1112, 1132-1139, 1163-1165, 1178-1179, and 1239, 1293, 1301,
+ * 1316 in the backward). layout 0: C[M, N] (+)= A[M, K] . W^T with W [N, K] (W.cols % 64 == 0);
+ * layout 1: C[M, N] (+)= A[M, K] . W with W [K, N] (N % 64 == 0). Dequantisation is the
+ * reference's (level x scale in fp32, rounded once to in_dtype; nested scales as ql_nf4_dequant),
+ * so the result equals ql_nf4_dequant followed by ql_gemm_tn / ql_gemm_nn. Other arguments as
+ * ql_gemm_tn (no workspace: no split-K). */
+int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, void* C,
+                int64_t ldc, const void* bias, int M, int in_dtype, int out_dtype, int accumulate,
+                const float* residual, cudaStream_t stream);
+
 typedef struct {
   ql_nf4_weight qkv, o, gu, down;   /* [C, H], [H, HQ D], [2 I, H] (gate rows, then up), [H, I] */
   const void* bias_qkv;             /* [C] */

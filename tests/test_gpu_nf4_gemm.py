@@ -179,6 +179,43 @@ def test_gemm_pair_tiles(M, N, K, b_kn, dt):
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("N,K,M", [(2048, 1536, 1090), (1536, 1536, 300), (17920, 1536, 1090),
+                                   (1536, 8960, 1090), (200, 128, 37), (256, 64, 1)])
+@pytest.mark.parametrize("nested", [False, True])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_gemm_nf4_fused_equals_dequant_then_gemm(N, K, M, nested, dt):
+    """The NF4-fused GEMM in both layouts against ql_nf4_dequant + the dense GEMM on the same
+    bytes (the same 16-bit weight, the same fp32 accumulation order), and against torch."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = torch.Generator().manual_seed(N + K + M + int(nested))
+    st = quantize_nf4(np.asarray(torch.randn(N, K, generator=g) * 0.05), nested=nested)
+    w = _W(st)
+    W = ops.nf4_dequant(w, dtype=dt)  # [N, K]
+    a = torch.randn(M, K, device=DEV, generator=torch.Generator(device=DEV).manual_seed(M)).to(dt)
+    bias = torch.randn(N, device=DEV).to(dt)
+    fused = ops.gemm_nf4(a, w, layout=0, bias=bias)
+    dense = ops.gemm(a, W, bias=bias)
+    ref = a.float() @ W.float().t() + bias.float()
+    scale = ref.abs().max().item() + 1e-6
+    tol = 2e-2 if dt == torch.bfloat16 else 4e-3
+    assert (fused.float() - ref).abs().max().item() / scale < tol
+    ulp = 2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10  # one rounding step of the output
+    assert (fused.float() - dense.float()).abs().max().item() / scale <= ulp
+    res = torch.randn(M, N, device=DEV)
+    f32 = ops.gemm_nf4(a, w, layout=0, out_dtype=torch.float32, residual=res)
+    plain = ops.gemm_nf4(a, w, layout=0)  # residual epilogue: res + round16(A W^T)
+    assert (f32 - (res + plain.float())).abs().max().item() / scale < 1e-5
+    if N % 64 == 0:  # layout 1: dX[M, K] = dY[M, N] . W[N, K]
+        dy = torch.randn(M, N, device=DEV).to(dt)
+        dx = ops.gemm_nf4(dy, w, layout=1)
+        ref1 = dy.float() @ W.float()
+        s1 = ref1.abs().max().item() + 1e-6
+        assert (dx.float() - ref1).abs().max().item() / s1 < tol
+        assert (dx.float() - ops.gemm(dy, W, b_kn=True).float()).abs().max().item() / s1 <= ulp
+    assert ops.device_status() == 0
+
+
 def test_gemm_strided_output():
     """C written into columns of a wider buffer (the [gate | up] halves, the LoRA slices)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
