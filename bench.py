@@ -53,12 +53,20 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--spill", choices=["recompute", "offload"], default=None,
+                    help="activation-memory plan: spill all but --keep-layers layers this way "
+                         "(default: every layer keeps its activations in HBM)")
+    ap.add_argument("--keep-layers", type=int, default=0)
+    ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per rank and step")
+    ap.add_argument("--median", type=int, default=MEDIAN, help="median sequence length")
+    ap.add_argument("--lo", type=int, default=LO)
+    ap.add_argument("--hi", type=int, default=HI)
     return ap.parse_args()
 
 
-def make_batch(rng, vocab, seqs=SEQS):
+def make_batch(rng, vocab, seqs=SEQS, median=MEDIAN, lo=LO, hi=HI):
     """Right-padded [B, T] input_ids / attention_mask / labels (HF-style, unshifted)."""
-    lengths = np.clip(np.round(np.exp(rng.normal(math.log(MEDIAN), 0.6, seqs))), LO, HI).astype(int)
+    lengths = np.clip(np.round(np.exp(rng.normal(math.log(median), 0.6, seqs))), lo, hi).astype(int)
     T = int(lengths.max())
     ids = rng.integers(0, vocab, (seqs, T), dtype=np.int64)
     mask = (np.arange(T)[None, :] < lengths[:, None]).astype(np.int64)
@@ -203,13 +211,15 @@ def run_ours(args, rank, world, local):
     cfg = QWEN25_1P5B
     model = build_qwen2_qlora(cfg, dropout=0.05, device=dev, seed=0, embed_dtype=torch.float16)
     model.train()
-    engine = FusedQwen2(model, dtype=torch.float16)
+    plan_kw = {} if args.spill is None else dict(spill=args.spill, keep_layers=args.keep_layers)
+    engine = FusedQwen2(model, dtype=torch.float16, **plan_kw)
     if world > 1:
         engine.set_data_parallel(None)
     params = lora_parameters(model)
     opt = torch.optim.AdamW(params, lr=2e-4, fused=True)
     rng = np.random.default_rng(1000 + rank)
-    host = [make_batch(rng, cfg.vocab_size) for _ in range(args.warmup + args.steps)]
+    host = [make_batch(rng, cfg.vocab_size, args.seqs, args.median, args.lo, args.hi)
+            for _ in range(args.warmup + args.steps)]
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
 
@@ -271,9 +281,27 @@ def run_ours(args, rank, world, local):
     ops.profile_stop()
     prof = ops.profile_read()
     ms = max_over_ranks(e0.elapsed_time(e1))
+    peak_mib = torch.cuda.max_memory_allocated(dev) / 2**20  # of the timed plan
     tokens = sum_over_ranks(sum(b[3] for b in host[args.warmup:]))
+    mem_line = {"plan": engine.last_plan.summary() if engine.last_plan else None}
+    if args.spill is not None:
+        # the same steps with every layer kept: the cost of the spill (exposed copy or
+        # recompute time) and the host-link traffic it moves
+        spill_bytes = engine.last_offload_bytes  # of the last timed step
+        keep_layers, engine.keep_layers, engine.spill = engine.keep_layers, None, "recompute"
+        barrier_sync()
+        e0.record()
+        for i in range(args.warmup, args.warmup + args.steps):
+            train_step(i)
+        e1.record()
+        barrier_sync()
+        keep_ms = max_over_ranks(e0.elapsed_time(e1))
+        engine.keep_layers, engine.spill = keep_layers, args.spill
+        mem_line.update(offload_bytes_per_step=spill_bytes,
+                        keep_all_ms_per_step=keep_ms / args.steps,
+                        spill_ms_per_step=ms / args.steps,
+                        exposed_fraction=max(0.0, (ms - keep_ms) / ms))
     value = tokens / (ms / 1000.0)
-    peak_mib = torch.cuda.max_memory_allocated(dev) / 2**20
     gemm_ms = prof.get("gemm", {}).get("ms", 0.0)
     gemm_flops = prof.get("gemm", {}).get("flops", 0.0)
     kernel_ms = {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()}
@@ -330,12 +358,16 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (seeded lognormal lengths, uniform token ids, random-init weights)",
-        "config": {"workload": WORKLOAD, "global_batch": SEQS * world, "seq_len": "varlen",
+        "config": {"workload": WORKLOAD if (args.seqs, args.median, args.lo, args.hi) ==
+                   (SEQS, MEDIAN, LO, HI) else
+                   f"Qwen2.5-1.5B as configs[1], {args.seqs} seqs/rank, lognormal lengths "
+                   f"(median {args.median}, clip [{args.lo},{args.hi}])",
+                   "global_batch": args.seqs * world, "seq_len": "varlen",
                    "parallelism": f"dp{world}",
                    "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of "
                          "activations) is larger than the 126 MB L2",
                    "tokens_per_step_per_rank": tokens / world / args.steps},
-        "peak_hbm_mib": peak_mib,
+        "peak_hbm_mib": peak_mib, "memory": mem_line,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d_total / args.steps,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": launches,

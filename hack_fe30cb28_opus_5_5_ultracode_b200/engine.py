@@ -23,7 +23,7 @@ import ctypes
 
 import torch
 
-from . import _lib, ops
+from . import _lib, memory, ops
 
 HEAD_CHUNK = 4096  # rows of logits alive at a time: 4096 x 151936 x 2 B = 1.2 GB of HBM
 
@@ -375,7 +375,12 @@ class LayerSpec:
 class FusedQwen2:
     """Holds what the step needs from a PEFT-wrapped, 4-bit Qwen2ForCausalLM."""
 
-    def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True):
+    def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True,
+                 spill="recompute", keep_layers=None, activation_budget_mib=None):
+        """spill / keep_layers / activation_budget_mib: the activation-memory plan of each step
+        (memory.plan_memory): by default every layer keeps its saved activations in HBM; with a
+        budget (MiB for the saved sets) or a forced keep_layers the first layers spill by
+        recompute or by offload to pinned host memory."""
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -425,6 +430,14 @@ class FusedQwen2:
         self.weight_elems = int(_lib.lib().ql_layer_weight_elems(ctypes.byref(self.descs[0])))
         self.w16 = torch.empty(len(self.layers) * self.weight_elems, device=self.device,
                                dtype=dtype) if keep_weights else None
+        self.spill, self.keep_layers = spill, keep_layers
+        self.activation_budget = None if activation_budget_mib is None \
+            else int(activation_budget_mib) << 20
+        self._host_ring = None     # pinned host memory of offloaded layers (grow-only)
+        self._copy_stream = None
+        self._scratch_h = None
+        self.last_plan = None
+        self.last_offload_bytes = 0  # host-link bytes of the last backward's offload plan
         self._workspace = None
         self._arena_buf = None     # grow-only device memory of the saved activations
         self._arena_busy = False   # a forward's activations await their backward
@@ -498,8 +511,14 @@ class FusedQwen2:
         n = packed.n
         spec0 = self.layers[0]
         cos, sin = self.rope.table(max(packed.max_len, 1))
+        layer_bytes, _ = memory.saved_set_bytes(n, spec0.H, spec0.HQ, spec0.HKV, spec0.D,
+                                                spec0.I, self._esize())
+        plan = memory.plan_memory(len(self.layers), layer_bytes, self.activation_budget,
+                                  self.spill, self.keep_layers)
+        self.last_plan = plan
         arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device,
-                            None if self._arena_busy else self._arena_buf)
+                            None if self._arena_busy else self._arena_buf, plan)
+        offload = _Offload(self, arena, plan) if memory.OFFLOAD in plan.modes and n else None
         if not self._arena_busy:
             self._arena_buf = arena.buf
             self._arena_busy = True
@@ -515,16 +534,32 @@ class FusedQwen2:
             if self.w16 is not None:
                 sv.w16 = self.w16[spec.index * self.weight_elems:].data_ptr()
             if n:
+                if offload is not None:
+                    offload.before_forward(spec.index)
                 ws = self._workspace_for(desc)
                 _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
                           arena.h(spec.index + 1).data_ptr(), ws.data_ptr(), ws.numel(),
                           ops.stream_ptr())
+                if offload is not None:
+                    offload.after_forward(spec.index)
             saved.append((sv, drop))
         h = arena.h(len(self.layers))
         dhp, loss = self._head(h, packed, denom, stats) if n else (None, None)
         if loss is None:
             loss = torch.zeros((), device=self.device)
-        return loss, (arena, saved), dhp
+        return loss, (arena, saved, offload), dhp
+
+    def _esize(self):
+        return torch.empty((), dtype=self.dtype).element_size()
+
+    def _recompute(self, i, desc, sv, arena):
+        """Reruns layer i's forward from its kept input into its (ring) saved set."""
+        n, H = arena.n, arena.H
+        if self._scratch_h is None or self._scratch_h.numel() < n * H:
+            self._scratch_h = torch.empty(n * H, device=self.device, dtype=torch.float32)
+        ws = self._workspace_for(desc)
+        _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
+                  self._scratch_h.data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
 
     def _set_step(self, desc, packed, drop, cos, sin):
         """The step-dependent fields of a layer's descriptor."""
@@ -575,7 +610,8 @@ class FusedQwen2:
     def _backward(self, packed, saved, dhp, grad):
         n = packed.n
         H = self.layers[0].H
-        arena, per_layer = saved
+        arena, per_layer, offload = saved
+        plan = arena.plan
         if arena.owned:  # the next forward may reuse the arena (queued after this backward)
             self._arena_busy = False
         grads = torch.zeros(self.lora_total, device=self.device, dtype=torch.float32)
@@ -593,11 +629,17 @@ class FusedQwen2:
             g = grad.detach().float().reshape(1).contiguous()
             ops.scatter_rows(dhp, packed.head_order, dh[0], scale=g, out16=dh16[0])
             cur = 0
+            if offload is not None:
+                offload.start_backward()
             for spec in reversed(self.layers):
                 i = spec.index
                 desc = self.descs[i]
                 sv, drop = per_layer[i]
                 self._set_step(desc, packed, drop, cos, sin)
+                if plan.modes[i] == memory.RECOMPUTE:
+                    self._recompute(i, desc, sv, arena)
+                elif plan.modes[i] == memory.OFFLOAD:
+                    offload.before_backward(i)
                 ws = self._workspace_for(desc)
                 lo = self.offsets[4 * i]
                 nxt = 1 - cur
@@ -607,6 +649,8 @@ class FusedQwen2:
                           dh[nxt].data_ptr() if need else None,
                           dh16[nxt].data_ptr() if need else None, ws.data_ptr(), ws.numel(),
                           ops.stream_ptr())
+                if offload is not None and plan.modes[i] == memory.OFFLOAD:
+                    offload.after_backward(i)
                 if reducer is not None:
                     reducer.launch(grads[lo:self.offsets[4 * i + 4]])
                 cur = nxt
@@ -614,6 +658,7 @@ class FusedQwen2:
             reducer.launch(grads)
         if reducer is not None:
             reducer.finish(grads)
+        self.last_offload_bytes = offload.bytes_moved if offload is not None else 0
         return views
 
 
@@ -621,23 +666,17 @@ class _SavedArena:
     """One device allocation per step for every layer's saved activations (ql_layer_saved) and
     the residual stream between layers (L + 1 fp32 [n, H] slots)."""
 
-    def __init__(self, n, spec, layers, dtype, device, reuse=None):
+    def __init__(self, n, spec, layers, dtype, device, reuse=None, plan=None):
         self.owned = False
         e = torch.empty((), dtype=dtype).element_size()
-        H, HQ, HKV, D, I = spec.H, spec.HQ, spec.HKV, spec.D, spec.I
-        sizes = [("rstd1", n * 4), ("yq", n * H * e), ("yv", n * H * e), ("xq", n * 16 * e),
-                 ("xv", n * 16 * e), ("q", n * HQ * D * e), ("k", n * HKV * D * e),
-                 ("v", n * HKV * D * e), ("out", n * HQ * D * e), ("lse", HQ * n * 4),
-                 ("h2", n * H * 4), ("rstd2", n * 4), ("gu", n * 2 * I * e),
-                 ("keep_q", n * (H // 32) * 4), ("keep_v", n * (H // 32) * 4)]
-        self.fields, off = {}, 0
-        for name, b in sizes:
-            self.fields[name] = off
-            off = (off + b + 255) // 256 * 256
-        self.layer_bytes = off
+        self.layer_bytes, self.fields = memory.saved_set_bytes(n, spec.H, spec.HQ, spec.HKV,
+                                                               spec.D, spec.I, e)
+        H = spec.H
+        self.plan = plan if plan is not None else memory.MemoryPlan([memory.KEEP] * layers)
+        self.slots = self.plan.slots  # saved sets in HBM: kept layers + the spill ring
         self.h_bytes = (n * H * 4 + 255) // 256 * 256
         self.layers, self.n, self.H = layers, n, H
-        total = max(layers * self.layer_bytes + (layers + 1) * self.h_bytes, 256)
+        total = max(self.slots * self.layer_bytes + (layers + 1) * self.h_bytes, 256)
         if reuse is not None and reuse.numel() >= total:
             self.buf = reuse
         else:  # grow by a quarter beyond the need, so slightly longer steps still fit
@@ -647,14 +686,101 @@ class _SavedArena:
 
     def h(self, i):
         """Residual stream slot i: the input of layer i (slot L: the head's input)."""
-        start = self.layers * self.layer_bytes + i * self.h_bytes
+        start = self.slots * self.layer_bytes + i * self.h_bytes
         return self.buf[start:start + self.n * self.H * 4].view(torch.float32).view(self.n, self.H)
 
+    def slot_base(self, i):
+        """Device address of layer i's saved set (its own slot, or its ring slot)."""
+        return self.base + self.plan.slot(i) * self.layer_bytes
+
     def saved(self, i):
-        b = self.base + i * self.layer_bytes
+        b = self.slot_base(i)
         fields = {k: b + off for k, off in self.fields.items()}
         fields["h"] = self.h(i).data_ptr()
         return _lib.struct("ql_layer_saved", **fields)
+
+
+class _Offload:
+    """Offload of spilled layers' saved sets to pinned host memory: the forward's set of layer
+    i leaves its ring slot on a copy stream right after the layer (the slot is reused two
+    spilled layers later, after that copy), and the backward brings each set back into a ring
+    slot one spilled layer ahead of its use (the slot is free once the layer that used it is
+    done). One cudaMemcpyAsync per layer and direction; events order the two streams."""
+
+    def __init__(self, engine, arena, plan):
+        self.arena, self.plan = arena, plan
+        self.spilled = [i for i in plan.spilled() if plan.modes[i] == memory.OFFLOAD]
+        nbytes = len(self.spilled) * arena.layer_bytes
+        if engine._host_ring is None or engine._host_ring.numel() < nbytes:
+            engine._host_ring = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        if engine._copy_stream is None:
+            engine._copy_stream = torch.cuda.Stream(device=engine.device)
+        self.host, self.stream = engine._host_ring, engine._copy_stream
+        self.index = {i: k for k, i in enumerate(self.spilled)}
+        self.slot_free = {}   # ring slot -> event after which it may be overwritten
+        self.arrived = {}     # layer -> event: its set is back in HBM
+        self.bytes_moved = 0
+
+    def _dev(self, i):
+        lb = self.arena.layer_bytes
+        off = self.arena.plan.slot(i) * lb
+        return self.arena.buf[off:off + lb]
+
+    def _host(self, i):
+        lb = self.arena.layer_bytes
+        k = self.index[i]
+        return self.host[k * lb:(k + 1) * lb]
+
+    def before_forward(self, i):
+        if i in self.index:
+            ev = self.slot_free.get(self.plan.slot(i))
+            if ev is not None:
+                torch.cuda.current_stream().wait_event(ev)
+
+    def after_forward(self, i):
+        if i not in self.index:
+            return
+        done = torch.cuda.Event()
+        done.record()
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_event(done)
+            self._host(i).copy_(self._dev(i), non_blocking=True)
+            out = torch.cuda.Event()
+            out.record(self.stream)
+        self.slot_free[self.plan.slot(i)] = out
+        self.bytes_moved += self.arena.layer_bytes
+
+    def _fetch(self, i):
+        ev = self.slot_free.get(self.plan.slot(i))
+        with torch.cuda.stream(self.stream):
+            if ev is not None:
+                self.stream.wait_event(ev)
+            self._dev(i).copy_(self._host(i), non_blocking=True)
+            got = torch.cuda.Event()
+            got.record(self.stream)
+        self.arrived[i] = got
+        self.bytes_moved += self.arena.layer_bytes
+
+    def start_backward(self):
+        # the ring slots' last forward copies must finish before the backward refills them
+        for ev in self.slot_free.values():
+            self.stream.wait_event(ev)
+        self.slot_free = {}
+        order = sorted(self.spilled, reverse=True)
+        self.order = order
+        if order:
+            self._fetch(order[0])
+
+    def before_backward(self, i):
+        torch.cuda.current_stream().wait_event(self.arrived.pop(i))
+        k = self.order.index(i)
+        if k + 1 < len(self.order):  # the next spilled layer, into the other ring slot
+            self._fetch(self.order[k + 1])
+
+    def after_backward(self, i):
+        done = torch.cuda.Event()
+        done.record()
+        self.slot_free[self.plan.slot(i)] = done
 
 
 class _FusedStep(torch.autograd.Function):

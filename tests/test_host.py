@@ -233,3 +233,24 @@ def test_prepare_inputs_keeps_the_host_facts():
     moved = patch.prepare_inputs(t, dict(b), torch.device("cpu"))
     assert t._qlora_host_batch[0] is moved["input_ids"]
     assert t._qlora_host_batch[1].lengths == [5, 3, 7]
+
+
+def test_memory_plan_keeps_the_last_layers_and_fits_the_budget():
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+
+    lb, fields = memory.saved_set_bytes(1090, 1536, 12, 2, 128, 8960, 2)
+    assert all(off % 256 == 0 for off in fields.values()) and lb >= 1090 * 55_000
+    everything = memory.plan_memory(28, lb)
+    assert everything.modes == ["keep"] * 28 and everything.ring == 0 and everything.slots == 28
+    # a budget for 10 sets: one ring slot for recompute, 9 kept (the last 9 layers)
+    p = memory.plan_memory(28, lb, budget_bytes=10 * lb, spill="recompute")
+    assert p.modes == ["recompute"] * 19 + ["keep"] * 9 and p.ring == 1 and p.slots == 10
+    assert {p.slot(i) for i in range(19)} == {9} and [p.slot(i) for i in range(19, 28)] == list(range(9))
+    # offload: two ring slots, alternating between consecutive spilled layers
+    q = memory.plan_memory(28, lb, budget_bytes=10 * lb, spill="offload")
+    assert q.modes.count("keep") == 8 and q.ring == 2 and q.slots == 10
+    assert [q.slot(i) for i in range(4)] == [8, 9, 8, 9]
+    assert memory.plan_memory(4, lb, keep_layers=1).modes == ["recompute"] * 3 + ["keep"]
+    assert memory.plan_memory(4, lb, budget_bytes=0).modes == ["recompute"] * 4
+    with pytest.raises(ValueError):
+        memory.plan_memory(4, lb, spill="disk")
