@@ -19,6 +19,7 @@ namespace ql {
 constexpr int AT_BM = 64;   // queries per forward CTA
 constexpr int AT_BN = 64;   // keys per step / per backward CTA
 constexpr int AT_BQ = 32;   // queries per backward step
+constexpr int AT_QCH = 128; // queries per backward CTA (a chunk of a key block's rows)
 
 // element offset of (row, col) in a [rows][D] 16-bit tile (D = 64 or 128) with its 16-byte
 // chunks XOR-swizzled by the row (conflict-free ldmatrix)
@@ -271,9 +272,12 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
   float* sD = sL + 2 * AT_BQ;                              // [2][32] Dvec
   constexpr int SROW = 40;
 
-  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // blockIdx.x = (query chunk) x (key block): the key block's query rows are cut into chunks of
+  // AT_QCH so that no CTA walks a long sequence alone (dK / dV are added atomically anyway)
+  const int nkb = (int)cdiv(a.max_len, AT_BN);
+  const int kb = blockIdx.x % nkb, chunk = blockIdx.x / nkb, h = blockIdx.y, b = blockIdx.z;
   const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
-  if (kb * AT_BN >= len) return;
+  if (kb * AT_BN >= len || kb * AT_BN + chunk * AT_QCH >= len) return;
   const int group = a.HQ / a.HKV, kvh = h / group;
   const int64_t ldq = (int64_t)a.HQ * AT_D, ldk = (int64_t)a.HKV * AT_D;
   const T* Q = reinterpret_cast<const T*>(a.q) + (int64_t)start * ldq + h * AT_D;
@@ -288,8 +292,9 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
 
   load_tile<T, AT_D, AT_BN, 128>(sK, K, ldk, kb * AT_BN, len);
   load_tile<T, AT_D, AT_BN, 128>(sV, V, ldk, kb * AT_BN, len);
-  const int q_first = kb * AT_BN;
-  const int nsteps = (int)cdiv(len - q_first, AT_BQ);
+  const int q_first = kb * AT_BN + chunk * AT_QCH;
+  const int q_end = min(len, q_first + AT_QCH);
+  const int nsteps = (int)cdiv(q_end - q_first, AT_BQ);
   auto load_q = [&](int step, int buf) {
     const int r0 = q_first + step * AT_BQ;
     load_tile<T, AT_D, AT_BQ, 128>(sQ + buf * AT_BQ * AT_D, Q, ldq, r0, len);
@@ -474,7 +479,8 @@ static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
     cudaFuncSetAttribute(attn_bwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cfg = true;
   }
-  dim3 grid((unsigned)cdiv(a.max_len, AT_BN), (unsigned)a.HQ, (unsigned)a.B);
+  dim3 grid((unsigned)(cdiv(a.max_len, AT_BN) * cdiv(a.max_len, AT_QCH)), (unsigned)a.HQ,
+            (unsigned)a.B);
   attn_bwd_kernel<T, D><<<grid, 128, smem, s>>>(a);
 }
 
