@@ -56,6 +56,7 @@ __device__ __forceinline__ void load_tile(T* tile, const T* base, int64_t ld, in
 // ---------------------------------------------------------------------------------------------
 template <typename T, int AT_D>
 __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t at_smem[];
   T* sQ = reinterpret_cast<T*>(at_smem);
   T* sK = sQ + AT_BM * AT_D;          // [2][64][D]
@@ -209,7 +210,7 @@ static void launch_attn_fwd(const AttnFwdC& a, cudaStream_t s) {
     cfg = true;
   }
   dim3 grid((unsigned)cdiv(a.max_len, AT_BM), (unsigned)a.HQ, (unsigned)a.B);
-  attn_fwd_kernel<T, D><<<grid, 128, smem, s>>>(a);
+  launch_k(attn_fwd_kernel<T, D>, grid, dim3(128), smem, s, a);
 }
 
 int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
@@ -238,6 +239,7 @@ namespace ql {
 template <typename T, int AT_D>
 __global__ void attn_bwd_pre_kernel(const T* __restrict__ dout, const T* __restrict__ out,
                                     float* __restrict__ dvec, int64_t n, int HQ) {
+  pdl_enter();
   const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + (threadIdx.x >> 5);  // (t, h)
   const int lane = threadIdx.x & 31;
   if (row >= n * HQ) return;
@@ -262,6 +264,7 @@ __global__ void attn_bwd_pre_kernel(const T* __restrict__ dout, const T* __restr
 // into the KV head's fp32 rows at the end (the group's query heads all contribute).
 template <typename T, int AT_D>
 __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t at_smem[];
   T* sK = reinterpret_cast<T*>(at_smem);   // [64][D]
   T* sV = sK + AT_BN * AT_D;                // [64][D]
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
 template <typename T, int D>
 static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   const int64_t rows = (int64_t)a.n * a.HQ;
-  attn_bwd_pre_kernel<T, D><<<(unsigned)cdiv(rows, 8), 256, 0, s>>>(
+  launch_k(attn_bwd_pre_kernel<T, D>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s, 
       (const T*)a.dout, (const T*)a.out, a.dvec, a.n, a.HQ);
   const int smem = (2 * AT_BN + 4 * AT_BQ) * D * 2 + AT_BN * 40 * 2 + 4 * AT_BQ * 4;
   static bool cfg = false;
@@ -481,7 +484,7 @@ static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   }
   dim3 grid((unsigned)(cdiv(a.max_len, AT_BN) * cdiv(a.max_len, AT_QCH)), (unsigned)a.HQ,
             (unsigned)a.B);
-  attn_bwd_kernel<T, D><<<grid, 128, smem, s>>>(a);
+  launch_k(attn_bwd_kernel<T, D>, grid, dim3(128), smem, s, a);
 }
 
 int attn_bwd(const AttnBwdC& a, cudaStream_t s) {

@@ -98,6 +98,7 @@ __device__ __forceinline__ OnlineStat row_stats(const T* src, int64_t width, int
 
 template <typename T>
 __global__ void __launch_bounds__(CE_THREADS) ce_rows_kernel(CeRowsC a) {
+  pdl_enter();
   __shared__ OnlineStat sh[CE_THREADS / 32];
   __shared__ float xt_sh;
   const int64_t row = blockIdx.x;
@@ -125,6 +126,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_rows_kernel(CeRowsC a) {
 
 template <typename T>
 __global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
+  pdl_enter();
   __shared__ OnlineStat sh[CE_THREADS / 32];
   __shared__ float xt_sh;
   const int64_t row = blockIdx.x;
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
 
 template <typename T>
 __global__ void ce_finish_kernel(CeFinishC a) {
+  pdl_enter();
   const int64_t row = blockIdx.x;
   const float m = a.state[row * 4], s = a.state[row * 4 + 1], t = a.state[row * 4 + 2];
   const float lse = m + logf(s);

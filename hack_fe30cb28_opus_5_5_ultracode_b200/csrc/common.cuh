@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include <type_traits>
+#include <utility>
 
 #include "../../include/qlora_sm100.h"
 
@@ -386,6 +387,34 @@ __device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t&
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(smem_u32(p)));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of this library starts with pdl_enter(): it lets the
+// next kernel on the stream be scheduled as soon as all of this one's CTAs are running (that one
+// waits in its own pdl_enter), then waits until the previous kernel has completed and its memory
+// is visible, before any global access. Launched without the attribute (or after a non-kernel
+// operation), the wait returns at once.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace ql

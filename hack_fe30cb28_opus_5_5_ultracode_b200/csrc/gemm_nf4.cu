@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(448, 1)
     gemm_nf4_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_p,
                     const __grid_constant__ CUtensorMap tma_c, GemmArgs p, Nf4Src w) {
+  pdl_enter();
   using Cfg = Nf4Cfg<BN>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
   constexpr bool kTmaC = sizeof(OutT) == 2;

@@ -29,6 +29,7 @@ template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
+  pdl_enter();
   constexpr bool kTmaC = sizeof(OutT) == 2;
   using Cfg = GemmCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
@@ -279,6 +280,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
+  pdl_enter();
   constexpr bool kTmaC = sizeof(OutT) == 2;
   using Cfg = PairCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
@@ -468,7 +470,8 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   }
   const int units = (int)(cdiv(a.M, 128) * cdiv(a.N, BN)) * a.splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ma, mb, mc, a);
+  if (launch_k(kern, dim3(grid), dim3(192), Cfg::SMEM_BYTES, stream, ma, mb, mc, a) != cudaSuccess)
+    return QL_STATUS_CUDA;
   return launched(1);
 }
 
@@ -513,13 +516,15 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a) != cudaSuccess) return QL_STATUS_CUDA;
   return launched(1);
 }

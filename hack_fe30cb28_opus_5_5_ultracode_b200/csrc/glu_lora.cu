@@ -19,6 +19,7 @@ namespace ql {
 
 template <typename T>
 __global__ void glu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ m, int64_t n, int I) {
+  pdl_enter();
   const int64_t per_row = I / 8;
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= n * per_row) return;
@@ -38,6 +39,7 @@ __global__ void glu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ m, int6
 
 template <typename T>
 __global__ void glu_bwd_kernel(const T* __restrict__ dm, T* __restrict__ gu, int64_t n, int I) {
+  pdl_enter();
   const int64_t per_row = I / 8;
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= n * per_row) return;
@@ -69,9 +71,9 @@ int glu_fwd(const void* gu, void* m, int64_t n, int I, int dtype, cudaStream_t s
   const int64_t work = n * (I / 8);
   const unsigned grid = (unsigned)cdiv(work, 256);
   if (dtype == QL_F16)
-    glu_fwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)gu, (__half*)m, n, I);
+    launch_k(glu_fwd_kernel<__half>, dim3(grid), dim3(256), 0, s, (const __half*)gu, (__half*)m, n, I);
   else if (dtype == QL_BF16)
-    glu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)gu, (__nv_bfloat16*)m, n, I);
+    launch_k(glu_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, (const __nv_bfloat16*)gu, (__nv_bfloat16*)m, n, I);
   else return QL_STATUS_BAD_ARG;
   return launched(1);
 }
@@ -83,9 +85,9 @@ int glu_bwd(const void* dm, void* gu, int64_t n, int I, int dtype, cudaStream_t 
   const int64_t work = n * (I / 8);
   const unsigned grid = (unsigned)cdiv(work, 256);
   if (dtype == QL_F16)
-    glu_bwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)dm, (__half*)gu, n, I);
+    launch_k(glu_bwd_kernel<__half>, dim3(grid), dim3(256), 0, s, (const __half*)dm, (__half*)gu, n, I);
   else if (dtype == QL_BF16)
-    glu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)dm, (__nv_bfloat16*)gu, n, I);
+    launch_k(glu_bwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, (const __nv_bfloat16*)dm, (__nv_bfloat16*)gu, n, I);
   else return QL_STATUS_BAD_ARG;
   return launched(1);
 }
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(CS_THREADS) colsum_kernel(const TX* __restrict
                                                              const TY* __restrict__ Y, int64_t n,
                                                              int ncols, int64_t tok_per_split,
                                                              float* __restrict__ partial) {
+  pdl_enter();
   __shared__ __align__(16) TX xs[2][CS_TOK][CS_COLS];
   __shared__ __align__(16) TY ys[2][CS_TOK][CS_R];
   const int c0 = blockIdx.x * CS_COLS;
@@ -162,6 +165,7 @@ __global__ void __launch_bounds__(CS_THREADS) colsum_kernel(const TX* __restrict
 // Stage 2: out = scale * sum over splits (fixed order), as [ncols, R] or transposed [R, ncols].
 __global__ void colsum_reduce_kernel(const float* __restrict__ partial, int splits, int ncols,
                                      float scale, int transpose, float* __restrict__ out) {
+  pdl_enter();
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= (int64_t)ncols * CS_R) return;
   float s = 0.f;
@@ -242,6 +246,7 @@ struct LgArgs {
 // split order.
 template <typename TX>
 __global__ void __launch_bounds__(LG_THREADS) lora_grads_kernel(LgArgs a) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t lg_smem[];
   __shared__ float sp2[2][LG_COLS * 16];
   __shared__ int last;
@@ -412,10 +417,10 @@ int lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, 
   const int smem = (int)(min(a.tok_per_split, (int64_t)LG_MAXTOK) * (LG_COLS + 16) * 2);
   if (x_dtype == QL_F16) {
     smem_optin(reinterpret_cast<const void*>(lora_grads_kernel<__half>), smem);
-    lora_grads_kernel<__half><<<grid, LG_THREADS, smem, s>>>(a);
+    launch_k(lora_grads_kernel<__half>, grid, dim3(LG_THREADS), smem, s, a);
   } else {
     smem_optin(reinterpret_cast<const void*>(lora_grads_kernel<__nv_bfloat16>), smem);
-    lora_grads_kernel<__nv_bfloat16><<<grid, LG_THREADS, smem, s>>>(a);
+    launch_k(lora_grads_kernel<__nv_bfloat16>, grid, dim3(LG_THREADS), smem, s, a);
   }
   return launched(1);
 }
@@ -426,6 +431,7 @@ int lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, 
 template <typename T>
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const T* __restrict__ W,
                              float* __restrict__ h, int64_t n, int H, int64_t vocab, int* err) {
+  pdl_enter();
   const int64_t t = blockIdx.x;
   const int64_t id = ids[t];
   if (id < 0 || id >= vocab) {
@@ -456,6 +462,7 @@ namespace ql {
 // ---------------------------------------------------------------------------------------------
 __global__ void gather_rows_kernel(const float* __restrict__ src, const int64_t* __restrict__ idx,
                                    float* __restrict__ dst, int H) {
+  pdl_enter();
   const int64_t r = blockIdx.x;
   const float4* s = reinterpret_cast<const float4*>(src + idx[r] * H);
   float4* d = reinterpret_cast<float4*>(dst + r * H);
@@ -466,6 +473,7 @@ template <typename T>
 __global__ void scatter_rows_kernel(const float* __restrict__ src, const int64_t* __restrict__ idx,
                                     const float* __restrict__ scale, float* __restrict__ dst,
                                     T* __restrict__ dst16, int H) {
+  pdl_enter();
   const int64_t r = blockIdx.x;
   const float s = scale != nullptr ? *scale : 1.f;
   const int64_t o = idx[r] * H;

@@ -46,6 +46,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // One thread: 16 packed bytes = 32 values = half of a 64-value block.
 template <typename OutT, bool NESTED>
 __global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args a, OutT* __restrict__ out) {
+  pdl_enter();
   __shared__ float lv[16];
   if (threadIdx.x < 16) lv[threadIdx.x] = a.code[threadIdx.x];
   __syncthreads();
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args a, OutT* __res
 template <typename OutT, bool NESTED>
 __global__ void __launch_bounds__(128) nf4_dequant_t_kernel(Nf4Args a, OutT* __restrict__ out,
                                                             int64_t rows, int64_t cols) {
+  pdl_enter();
   __shared__ float lv[16];
   __shared__ uint16_t tile[64][64 + 2];
   if (threadIdx.x < 16) lv[threadIdx.x] = a.code[threadIdx.x];
@@ -120,13 +122,13 @@ static int launch_nf4(const Nf4Args& a, void* out, int64_t rows, int64_t cols, b
   OutT* o = reinterpret_cast<OutT*>(out);
   if (transpose) {
     dim3 grid((unsigned)(cols / 64), (unsigned)(rows / 64));
-    if (nested) nf4_dequant_t_kernel<OutT, true><<<grid, 128, 0, s>>>(a, o, rows, cols);
-    else nf4_dequant_t_kernel<OutT, false><<<grid, 128, 0, s>>>(a, o, rows, cols);
+    if (nested) launch_k(nf4_dequant_t_kernel<OutT, true>, grid, dim3(128), 0, s, a, o, rows, cols);
+    else launch_k(nf4_dequant_t_kernel<OutT, false>, grid, dim3(128), 0, s, a, o, rows, cols);
   } else {
     const int64_t threads = a.n_blocks * 2;
     const unsigned grid = (unsigned)cdiv(threads, 256);
-    if (nested) nf4_dequant_kernel<OutT, true><<<grid, 256, 0, s>>>(a, o);
-    else nf4_dequant_kernel<OutT, false><<<grid, 256, 0, s>>>(a, o);
+    if (nested) launch_k(nf4_dequant_kernel<OutT, true>, dim3(grid), dim3(256), 0, s, a, o);
+    else launch_k(nf4_dequant_kernel<OutT, false>, dim3(grid), dim3(256), 0, s, a, o);
   }
   return launched(1);
 }

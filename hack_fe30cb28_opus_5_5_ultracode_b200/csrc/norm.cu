@@ -123,6 +123,7 @@ __device__ __forceinline__ uint32_t gather_bits(uint32_t nib) {
 // gi = 32 (w % WPR) + lane + 32 WPR k (k < G) in registers between the two passes.
 template <typename T, int G, int WPR>
 __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
+  pdl_enter();
   constexpr int NW = RMS_ROWS * WPR, SL = NW / 2;  // warps; K slices per adapter
   extern __shared__ __align__(16) uint8_t rms_smem[];
   __shared__ float sSS[NW];
@@ -250,6 +251,7 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
 
 template <typename T, int G, int WPR>
 __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
+  pdl_enter();
   constexpr int NW = RMS_ROWS * WPR;
   extern __shared__ __align__(16) uint8_t rms_smem[];
   __shared__ float sDot[NW];
@@ -410,7 +412,7 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
 #define QL_RMSF(TT, GG, WW)                                           \
   do {                                                                \
     set_smem(rms_fwd_kernel<TT, GG, WW>, smem);                       \
-    rms_fwd_kernel<TT, GG, WW><<<grid, 256 * WW, smem, s>>>(a);       \
+    launch_k(rms_fwd_kernel<TT, GG, WW>, dim3(grid), dim3(256 * WW), smem, s, a);       \
   } while (0)
   const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
@@ -454,7 +456,7 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
 #define QL_RMSB(TT, GG, WW)                                           \
   do {                                                                \
     set_smem(rms_bwd_kernel<TT, GG, WW>, smem);                       \
-    rms_bwd_kernel<TT, GG, WW><<<grid, 256 * WW, smem, s>>>(a);       \
+    launch_k(rms_bwd_kernel<TT, GG, WW>, dim3(grid), dim3(256 * WW), smem, s, a);       \
   } while (0)
   const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
@@ -477,6 +479,7 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
 namespace ql {
 
 __global__ void dropout_keep_kernel(int8_t* out, int64_t nelem, DropoutArgs d) {
+  pdl_enter();
   const int64_t e0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4;
   if (e0 >= nelem) return;
   const uint32_t k = keep4(e0, d.ctr_q, d);

@@ -52,6 +52,7 @@ constexpr int ROPE_WPR = 2;   // warps per token
 // of the first half of a head together with their partners d + D/2 (16-byte loads and stores).
 template <typename T>
 __global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
+  pdl_enter();
   constexpr int NW = ROPE_ROWS * ROPE_WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
@@ -158,6 +159,7 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
 // strided over the warps, the slices' partials added in a fixed order.
 template <typename T, typename TIn>
 __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
+  pdl_enter();
   constexpr int NW = ROPE_ROWS * ROPE_WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
@@ -307,10 +309,10 @@ int rope_fwd(const RopeFwdC& a, cudaStream_t s) {
   const int grid = rope_grid(a.n);
   if (a.dtype == QL_F16) {
     rope_smem_attr(rope_fwd_kernel<__half>, smem);
-    rope_fwd_kernel<__half><<<grid, 256 * ROPE_WPR, smem, s>>>(a);
+    launch_k(rope_fwd_kernel<__half>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);
   } else if (a.dtype == QL_BF16) {
     rope_smem_attr(rope_fwd_kernel<__nv_bfloat16>, smem);
-    rope_fwd_kernel<__nv_bfloat16><<<grid, 256 * ROPE_WPR, smem, s>>>(a);
+    launch_k(rope_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);
   } else {
     return QL_STATUS_BAD_ARG;
   }
@@ -335,7 +337,7 @@ int rope_bwd(const RopeBwdC& a, cudaStream_t s) {
 #define QL_ROPEB(TT, TI)                                             \
   do {                                                               \
     rope_smem_attr(rope_bwd_kernel<TT, TI>, smem);                   \
-    rope_bwd_kernel<TT, TI><<<grid, 256 * ROPE_WPR, smem, s>>>(a);   \
+    launch_k(rope_bwd_kernel<TT, TI>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);   \
   } while (0)
   if (a.dtype == QL_F16) {
     if (f32in) QL_ROPEB(__half, float); else QL_ROPEB(__half, __half);
