@@ -113,6 +113,11 @@ int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
               "ql_gemm_nn");
 }
 
+int ql_nf4_dequant_batch(const ql_nf4_weight* weights, void* const* outs, int count, int out_dtype,
+                         cudaStream_t stream) {
+  return done(ql::nf4_dequant_batch(weights, outs, count, out_dtype, stream), "ql_nf4_dequant_batch");
+}
+
 int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
 int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, void* C,

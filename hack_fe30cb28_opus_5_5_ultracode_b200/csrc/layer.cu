@@ -202,7 +202,8 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
             r1.drop_q, r1.drop_v);
   QL_TRY(rms_fwd(r1, s));
   // q, k, v in one GEMM (bias in the epilogue), then LoRA-B + RoPE
-  QL_TRY(dequant(L.qkv, wqkv, dt, 0, s));
+  const bool ready = S.w16 != nullptr && S.w16_ready;  // dequantised by the caller this step
+  if (!ready) QL_TRY(dequant(L.qkv, wqkv, dt, 0, s));
   QL_TRY(gemm_tn(w.a, L.H, wqkv, L.H, w.qkv, C, L.bias_qkv, L.n, (int)C, L.H, dt, dt, 0, nullptr,
                  err, s, w.gws, w.gws_bytes));
   RopeFwdC rf{};
@@ -217,7 +218,7 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   af.HKV = L.HKV; af.D = L.D; af.dtype = dt;
   QL_TRY(attn_fwd(af, s));
   // o projection, residual add in the epilogue: h2 = h + o
-  QL_TRY(dequant(L.o, wo, dt, 0, s));
+  if (!ready) QL_TRY(dequant(L.o, wo, dt, 0, s));
   QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, wo, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
                  L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s, w.gws, w.gws_bytes));
   // post-attention RMSNorm
@@ -227,11 +228,11 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   r2.keep_scale = 1.f;
   QL_TRY(rms_fwd(r2, s));
   // [gate | up], SwiGLU, down with the residual add: h3 = h2 + d
-  QL_TRY(dequant(L.gu, wgu, dt, 0, s));
+  if (!ready) QL_TRY(dequant(L.gu, wgu, dt, 0, s));
   QL_TRY(gemm_tn(w.a, L.H, wgu, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
                  nullptr, err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
-  QL_TRY(dequant(L.down, wdown, dt, 0, s));
+  if (!ready) QL_TRY(dequant(L.down, wdown, dt, 0, s));
   QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
                  err, s, w.gws, w.gws_bytes));
   return QL_STATUS_OK;

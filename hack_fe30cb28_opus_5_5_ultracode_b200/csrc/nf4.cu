@@ -155,4 +155,107 @@ int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
   return QL_STATUS_BAD_ARG;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Many weights in one launch (every group of every layer at the start of a step): one thread per
+// half block as above; the item of a thread is found by binary search over the items' first
+// threads (kernel parameters, up to NF4_BATCH items per launch).
+// ---------------------------------------------------------------------------------------------
+constexpr int NF4_BATCH = 28;
+
+struct Nf4Item {
+  const uint8_t* packed;
+  const void* absmax;
+  const float* code2;
+  const float* absmax2;
+  const float* offsets;
+  const float* code;
+  void* out;
+  int64_t first;     // first thread (half block) of this item in the launch
+  int64_t seg1, seg2;
+  int32_t bs2, nested;
+};
+struct Nf4Batch {
+  Nf4Item item[NF4_BATCH];
+  int count;
+  int64_t total;     // threads of the launch
+};
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) nf4_dequant_batch_kernel(const __grid_constant__ Nf4Batch b) {
+  pdl_enter();
+  const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (t >= b.total) return;
+  int lo = 0, hi = b.count - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (t >= b.item[mid].first) lo = mid; else hi = mid - 1;
+  }
+  const Nf4Item& it = b.item[lo];
+  const int64_t lt = t - it.first, blk = lt >> 1;
+  float scale;
+  if (it.nested) {
+    const uint8_t q = reinterpret_cast<const uint8_t*>(it.absmax)[blk];
+    const float s = __fmul_rn(__ldg(it.code2 + q), __ldg(it.absmax2 + blk / it.bs2));
+    const int seg = (blk >= it.seg1) + (blk >= it.seg2);
+    scale = __fadd_rn(s, __ldg(it.offsets + seg));
+  } else {
+    scale = __ldg(reinterpret_cast<const float*>(it.absmax) + blk);
+  }
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(it.packed) + lt);
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t byte = (words[k] >> (8 * j)) & 0xFFu;
+      o[k * 4 + j] = pack2<OutT>(__fmul_rn(__ldg(it.code + (byte >> 4)), scale),
+                                 __fmul_rn(__ldg(it.code + (byte & 15u)), scale));
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(it.out) + lt * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+}
+
+int nf4_dequant_batch(const ql_nf4_weight* w, void* const* outs, int count, int out_dtype,
+                      cudaStream_t s) {
+  if (count < 0 || (count > 0 && (w == nullptr || outs == nullptr))) return QL_STATUS_BAD_ARG;
+  if (out_dtype != QL_F16 && out_dtype != QL_BF16) return QL_STATUS_BAD_ARG;
+  double bytes = 0;
+  for (int i = 0; i < count; ++i) {
+    const ql_nf4_weight& g = w[i];
+    const int64_t numel = g.rows * g.cols;
+    if (g.rows < 0 || g.cols < 0 || numel % 64 != 0 || g.packed == nullptr || g.absmax == nullptr ||
+        g.code == nullptr || outs[i] == nullptr ||
+        reinterpret_cast<uintptr_t>(g.packed) % 16 != 0 || reinterpret_cast<uintptr_t>(outs[i]) % 16 != 0)
+      return QL_STATUS_BAD_ARG;
+    if (g.nested && (g.bs2 <= 0 || g.code2 == nullptr || g.absmax2 == nullptr || g.offsets == nullptr))
+      return QL_STATUS_BAD_ARG;
+    bytes += numel * (0.5 + (g.nested ? 1.0 : 4.0) / 64 + 2.0);
+  }
+  ProfScope prof(PK_DEQUANT, 0, bytes, s);
+  int launches = 0;
+  for (int i0 = 0; i0 < count; i0 += NF4_BATCH) {
+    Nf4Batch b{};
+    b.count = count - i0 < NF4_BATCH ? count - i0 : NF4_BATCH;
+    int64_t first = 0;
+    for (int k = 0; k < b.count; ++k) {
+      const ql_nf4_weight& g = w[i0 + k];
+      b.item[k] = Nf4Item{g.packed, g.absmax, g.code2, g.absmax2, g.offsets, g.code, outs[i0 + k],
+                          first, g.seg1, g.seg2, g.bs2 > 0 ? g.bs2 : 1, g.nested};
+      first += g.rows * g.cols / 32;  // half blocks
+    }
+    b.total = first;
+    if (first == 0) continue;
+    const dim3 grid((unsigned)cdiv(first, 256));
+    cudaError_t e = out_dtype == QL_F16
+                        ? launch_k(nf4_dequant_batch_kernel<__half>, grid, dim3(256), 0, s, b)
+                        : launch_k(nf4_dequant_batch_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, b);
+    if (e != cudaSuccess) return QL_STATUS_CUDA;
+    ++launches;
+  }
+  return launches ? launched(launches) : QL_STATUS_OK;
+}
+
 }  // namespace ql

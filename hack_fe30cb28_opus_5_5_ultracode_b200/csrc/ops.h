@@ -9,6 +9,8 @@ namespace ql {
 
 int* status_word();
 
+int nf4_dequant_batch(const ql_nf4_weight* w, void* const* outs, int count, int out_dtype,
+                      cudaStream_t s);
 int nf4_dequant(const uint8_t* packed, const void* absmax, const float* code2,
                 const float* absmax2, const float* offsets, const float* code, void* out,
                 int64_t rows, int64_t cols, int nested, int bs2, int64_t seg1, int64_t seg2,

@@ -526,6 +526,8 @@ class FusedQwen2:
         h = arena.h(0)
         if n:
             ops.embed(packed.ids, self.embed, out=h)
+            if self.w16 is not None:  # this step's 16-bit weights, every layer, few launches
+                self._dequant_all()
         saved = []
         for spec, desc in zip(self.layers, self.descs):
             drop = self._drop(packed, spec.H)
@@ -533,6 +535,7 @@ class FusedQwen2:
             sv = arena.saved(spec.index)
             if self.w16 is not None:
                 sv.w16 = self.w16[spec.index * self.weight_elems:].data_ptr()
+                sv.w16_ready = 1
             if n:
                 if offload is not None:
                     offload.before_forward(spec.index)
@@ -548,6 +551,28 @@ class FusedQwen2:
         if loss is None:
             loss = torch.zeros((), device=self.device)
         return loss, (arena, saved, offload), dhp
+
+    def _dequant_all(self):
+        """Every layer's four NF4 groups into the kept 16-bit weights ([qkv | o | gate_up |
+        down] per layer, as the layer kernels lay them out) with ql_nf4_dequant_batch."""
+        if getattr(self, "_dq_args", None) is None:
+            spec = self.layers[0]
+            C = (spec.HQ + 2 * spec.HKV) * spec.D
+            offs = [0, C * spec.H, C * spec.H + spec.H * spec.HQ * spec.D,
+                    C * spec.H + spec.H * spec.HQ * spec.D + 2 * spec.I * spec.H]
+            e = self._esize()
+            groups, outs = [], []
+            for i, desc in enumerate(self.descs):
+                base = self.w16.data_ptr() + i * self.weight_elems * e
+                for g, off in zip((desc.qkv, desc.o, desc.gu, desc.down), offs):
+                    groups.append(g)
+                    outs.append(base + off * e)
+            arr = (_lib.STRUCTS["ql_nf4_weight"] * len(groups))(*groups)
+            ptrs = (ctypes.c_void_p * len(outs))(*outs)
+            self._dq_args = (arr, ptrs, len(groups))
+        arr, ptrs, count = self._dq_args
+        _lib.call("ql_nf4_dequant_batch", ctypes.addressof(arr), ctypes.addressof(ptrs), count,
+                  ops.dtype_code(self.dtype), ops.stream_ptr())
 
     def _esize(self):
         return torch.empty((), dtype=self.dtype).element_size()

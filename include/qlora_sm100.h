@@ -382,6 +382,13 @@ typedef struct {
   int32_t nested, bs2;
 } ql_nf4_weight;
 
+/* Many NF4 weights dequantised in as few launches as possible (one per 28 weights): out[i] gets
+ * weights[i] [rows, cols] as ql_nf4_dequant with transpose = 0. Replaces the reference's
+ * per-group dequant_into calls (solution/engine.py:103-109, 148-157) at the start of a step: all
+ * layers' groups at once instead of four small launches per layer. */
+int ql_nf4_dequant_batch(const ql_nf4_weight* weights, void* const* outs, int count, int out_dtype,
+                         cudaStream_t stream);
+
 /* GEMM with the NF4 weight dequantised inside the kernel (shared memory only, the 16-bit weight
  * never reaches HBM): replaces the reference's dequant_into + cuBLAS pairs (solution/engine.py:
  * 103-109 with 1081-1093, 1111-1112, 1132-1139, 1163-1165, 1178-1179, and 1239, 1293, 1301,
@@ -434,6 +441,8 @@ typedef struct {              /* what the forward keeps for the backward (all [n
   void* w16;                  /* NULL, or ql_layer_weight_elems() 16-bit elements: the forward's
                                  dequantised weights [qkv | o | gate_up | down], read again by
                                  the backward instead of a second dequantisation */
+  int32_t w16_ready;          /* 1: w16 already holds this step's dequantised weights (e.g. from
+                                 one ql_nf4_dequant_batch over all layers): no dequant here */
 } ql_layer_saved;
 
 /* Elements of ql_layer_saved.w16 for a layer: (HQ + 2 HKV) D H + H HQ D + 3 I H. */

@@ -216,6 +216,28 @@ def test_gemm_nf4_fused_equals_dequant_then_gemm(N, K, M, nested, dt):
     assert ops.device_status() == 0
 
 
+def test_nf4_dequant_batch_equals_per_weight_dequant():
+    """ql_nf4_dequant_batch over 31 weights (two launches, plain and nested scales) equals
+    ql_nf4_dequant of each, bit for bit."""
+    import ctypes
+
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
+
+    g = torch.Generator().manual_seed(3)
+    shapes = [(64 * (1 + i % 5), 64 * (1 + i % 3)) for i in range(31)]
+    ws = [_W(quantize_nf4(np.asarray(torch.randn(r, c, generator=g) * 0.1), nested=bool(i % 2)))
+          for i, (r, c) in enumerate(shapes)]
+    for dt in (torch.float16, torch.bfloat16):
+        outs = [torch.full(w.shape, float("nan"), device=DEV, dtype=dt) for w in ws]
+        arr = (_lib.STRUCTS["ql_nf4_weight"] * len(ws))(*[ops.nf4_weight_struct(w) for w in ws])
+        ptrs = (ctypes.c_void_p * len(ws))(*[o.data_ptr() for o in outs])
+        _lib.call("ql_nf4_dequant_batch", ctypes.addressof(arr), ctypes.addressof(ptrs), len(ws),
+                  ops.dtype_code(dt), torch.cuda.current_stream().cuda_stream)
+        for w, o in zip(ws, outs):
+            assert torch.equal(o, ops.nf4_dequant(w, dtype=dt))
+    assert ops.device_status() == 0
+
+
 def test_gemm_strided_output():
     """C written into columns of a wider buffer (the [gate | up] halves, the LoRA slices)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
