@@ -61,12 +61,20 @@ def parse():
     ap.add_argument("--median", type=int, default=MEDIAN, help="median sequence length")
     ap.add_argument("--lo", type=int, default=LO)
     ap.add_argument("--hi", type=int, default=HI)
+    ap.add_argument("--uniform", default=None, metavar="LO,HI",
+                    help="sequence lengths uniform in [LO, HI] instead of lognormal")
+    ap.add_argument("--model", choices=["1.5b", "7b"], default="1.5b")
+    ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
     return ap.parse_args()
 
 
-def make_batch(rng, vocab, seqs=SEQS, median=MEDIAN, lo=LO, hi=HI):
+def make_batch(rng, vocab, seqs=SEQS, median=MEDIAN, lo=LO, hi=HI, uniform=None):
     """Right-padded [B, T] input_ids / attention_mask / labels (HF-style, unshifted)."""
-    lengths = np.clip(np.round(np.exp(rng.normal(math.log(median), 0.6, seqs))), lo, hi).astype(int)
+    if uniform is not None:
+        lengths = rng.integers(uniform[0], uniform[1] + 1, seqs)
+    else:
+        lengths = np.clip(np.round(np.exp(rng.normal(math.log(median), 0.6, seqs))), lo,
+                          hi).astype(int)
     T = int(lengths.max())
     ids = rng.integers(0, vocab, (seqs, T), dtype=np.int64)
     mask = (np.arange(T)[None, :] < lengths[:, None]).astype(np.int64)
@@ -208,17 +216,21 @@ def run_ours(args, rank, world, local):
     torch.cuda.set_device(dev)
     if world > 1:
         dist.barrier(device_ids=[local])
-    cfg = QWEN25_1P5B
-    model = build_qwen2_qlora(cfg, dropout=0.05, device=dev, seed=0, embed_dtype=torch.float16)
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_7B
+
+    cfg = QWEN25_1P5B if args.model == "1.5b" else QWEN25_7B
+    cdt = torch.float16 if args.dtype == "fp16" else torch.bfloat16
+    model = build_qwen2_qlora(cfg, dropout=0.05, device=dev, seed=0, embed_dtype=cdt)
     model.train()
     plan_kw = {} if args.spill is None else dict(spill=args.spill, keep_layers=args.keep_layers)
-    engine = FusedQwen2(model, dtype=torch.float16, **plan_kw)
+    engine = FusedQwen2(model, dtype=cdt, **plan_kw)
     if world > 1:
         engine.set_data_parallel(None)
     params = lora_parameters(model)
     opt = torch.optim.AdamW(params, lr=2e-4, fused=True)
     rng = np.random.default_rng(1000 + rank)
-    host = [make_batch(rng, cfg.vocab_size, args.seqs, args.median, args.lo, args.hi)
+    uniform = tuple(int(x) for x in args.uniform.split(",")) if args.uniform else None
+    host = [make_batch(rng, cfg.vocab_size, args.seqs, args.median, args.lo, args.hi, uniform)
             for _ in range(args.warmup + args.steps)]
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
@@ -356,12 +368,14 @@ def run_ours(args, rank, world, local):
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic (seeded lognormal lengths, uniform token ids, random-init weights)",
-        "config": {"workload": WORKLOAD if (args.seqs, args.median, args.lo, args.hi) ==
-                   (SEQS, MEDIAN, LO, HI) else
-                   f"Qwen2.5-1.5B as configs[1], {args.seqs} seqs/rank, lognormal lengths "
-                   f"(median {args.median}, clip [{args.lo},{args.hi}])",
+        "config": {"workload": WORKLOAD if (args.seqs, args.median, args.lo, args.hi,
+                                            args.uniform, args.model, args.dtype) ==
+                   (SEQS, MEDIAN, LO, HI, None, "1.5b", "fp16") else
+                   f"Qwen2.5-{args.model.upper()} {args.dtype}, {args.seqs} seqs/rank, lengths "
+                   + (f"uniform [{args.uniform}]" if args.uniform else
+                      f"lognormal (median {args.median}, clip [{args.lo},{args.hi}])"),
                    "global_batch": args.seqs * world, "seq_len": "varlen",
                    "parallelism": f"dp{world}",
                    "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of "

@@ -2,6 +2,8 @@
 // of the reference's _layer_forward / _Layer.backward (solution/engine.py:1054-1340) over this
 // library's kernels, on one stream, temporaries carved out of a caller-owned workspace. One call
 // per layer pass replaces ~20 Python-level launches.
+#include <mutex>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -162,6 +164,43 @@ int check(const ql_layer_desc& L) {
   return QL_STATUS_OK;
 }
 
+// One side stream (and its fork / join events) per device for work of a layer pass that can run
+// next to the main stream; created on first use.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+SideStream& side_stream() {
+  static std::mutex mu;
+  static SideStream per_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    static SideStream none;
+    return none;
+  }
+  SideStream& ss = per_dev[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  if (ss.s == nullptr) {
+    cudaStream_t st = nullptr;
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+        cudaEventCreateWithFlags(&a, cudaEventDisableTiming) == cudaSuccess &&
+        cudaEventCreateWithFlags(&b, cudaEventDisableTiming) == cudaSuccess) {
+      ss.fork = a;
+      ss.join = b;
+      ss.s = st;
+    } else {
+      cudaGetLastError();  // no side stream: the work runs on the main stream
+    }
+  }
+  return ss;
+}
+
+int layer_backward_input(const ql_layer_desc& L, const ql_layer_saved& S, const BwdWs& w,
+                         int64_t C, int dt, float* dh_out, void* dh16_out, int* err,
+                         cudaStream_t s);
+
 }  // namespace
 
 int64_t layer_weight_elems(const ql_layer_desc& L) { return weight_slots(L).total; }
@@ -302,11 +341,39 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
       {dqkv + (qcols + vcols) * esz(dt), C, S.xv, gBv, (int)vcols, dt, 0, L.lora_scale},
       {S.yq, L.H, w.dxq, gAq, L.H, QL_F32, 1, 1.f},
       {S.yv, L.H, w.dxv, gAv, L.H, QL_F32, 1, 1.f}};
-  QL_TRY(lora_grads(jobs, 4, n, dt, w.lgw, w.lgw_bytes, s));
-  if (dh_out == nullptr) return QL_STATUS_OK;  // the first layer's input is the frozen embedding
-  QL_TRY(weight(L.qkv, slots.qkv, &W));  // [C, H]
+  // the LoRA weight gradients need nothing of the data-gradient path below: a side stream runs
+  // them next to the qkv data-gradient GEMM and RMSNorm backward, joined before returning
+  SideStream& side = side_stream();
+  if (side.s != nullptr) {
+    if (cudaEventRecord(side.fork, s) != cudaSuccess || cudaStreamWaitEvent(side.s, side.fork, 0) != cudaSuccess)
+      return QL_STATUS_CUDA;
+    QL_TRY(lora_grads(jobs, 4, n, dt, w.lgw, w.lgw_bytes, side.s));
+    if (cudaEventRecord(side.join, side.s) != cudaSuccess) return QL_STATUS_CUDA;
+  } else {
+    QL_TRY(lora_grads(jobs, 4, n, dt, w.lgw, w.lgw_bytes, s));
+  }
+  const int rc = layer_backward_input(L, S, w, C, dt, dh_out, dh16_out, err, s);
+  if (side.s != nullptr && cudaStreamWaitEvent(s, side.join, 0) != cudaSuccess) return QL_STATUS_CUDA;
+  return rc;
+}
+
+namespace {
+// The gradient of the layer's input (none for the first layer: its input is the frozen
+// embedding): da = dqkv . Wqkv, then the input RMSNorm's backward.
+int layer_backward_input(const ql_layer_desc& L, const ql_layer_saved& S, const BwdWs& w,
+                         int64_t C, int dt, float* dh_out, void* dh16_out, int* err,
+                         cudaStream_t s) {
+  if (dh_out == nullptr) return QL_STATUS_OK;
+  const WeightSlots slots = weight_slots(L);
+  void* W = nullptr;
+  if (S.w16 != nullptr) {
+    W = static_cast<uint8_t*>(S.w16) + slots.qkv * esz(dt);
+  } else {
+    W = w.w;
+    QL_TRY(dequant(L.qkv, w.w, dt, 0, s));
+  }
   QL_TRY(gemm_nn(w.dqkv, C, W, L.H, w.da, L.H, nullptr, L.n, L.H, (int)C, dt, dt, 0, nullptr,
-                 err, s, w.gws, w.gws_bytes));
+                 err, s, w.gws, w.gws_bytes));  // [C, H] weight
   RmsBwdC r1{};
   r1.dy = w.da; r1.ld_dy = L.H; r1.x = S.h; r1.rstd = S.rstd1; r1.w = L.ln1; r1.dres = w.dh2;
   r1.dx = dh_out; r1.dx16 = dh16_out; r1.dxlo_q = w.dxq; r1.dxlo_v = w.dxv; r1.Aq = L.Aq;
@@ -317,5 +384,6 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   QL_TRY(rms_bwd(r1, s));
   return QL_STATUS_OK;
 }
+}  // namespace
 
 }  // namespace ql

@@ -102,6 +102,21 @@ def test_fused_step_full_width_two_layers_fp16(keep_weights):
     assert gen.get_offset() == ref["offset"]
 
 
+def test_fused_step_qwen25_7b_width_layer_bf16():
+    """One decoder layer at the Qwen2.5-7B shapes (H 3584, 28 / 4 heads, D 128, I 18944), bf16:
+    the wide-row RMSNorm path, 7-way GQA groups and the 7B GEMM shapes against the oracle."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import Qwen2Config
+
+    cfg = Qwen2Config(vocab_size=2048, hidden_size=3584, intermediate_size=18944,
+                      num_hidden_layers=1, num_attention_heads=28, num_key_value_heads=4,
+                      head_dim=128)
+    engine, loss, packed, stats, grads, ref, gen = _run(cfg, [300, 120, 513], 0.05, False,
+                                                        dtype=torch.bfloat16)
+    assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 1e-2
+    for g, r_ in zip(grads, ref["grads"]):
+        assert _rel(g, r_) < 5e-2
+
+
 def test_two_steps_are_deterministic():
     """Same generator state, same batch: bit-identical loss and gradients (no atomics in the
     LoRA reductions; attention atomics only touch dq / dk / dv, whose order cannot change the
