@@ -7,18 +7,21 @@
 // backward recomputes the probabilities from it (FlashAttention-2 scheme, Dao 2023) and writes
 // dq [n, HQ, D], dk and dv [n, HKV, D] in fp32 (accumulated over the GQA group and query blocks).
 //
-// This first version runs on the warp-level tensor-core path (mma.sync m16n8k16, fp32
-// accumulation); the tiles are 64 queries x 64 keys, head dim D = 128 (Qwen2.5) or 64, staged by
-// cp.async into XOR-swizzled shared memory read with ldmatrix.
+// Runs on the warp-level tensor-core path (mma.sync m16n8k16, fp32 accumulation); the tiles are
+// 64 queries x 64 keys, head dim D = 128 (Qwen2.5) or 64, staged by cp.async into XOR-swizzled
+// shared memory read with ldmatrix. The forward's online softmax raises its running row max
+// lazily (output rescaled only on a rise of more than 2^8); the backward's fp32 gradient tiles are
+// added to dq / dk / dv by bulk reductions from shared memory (cp.reduce.async.bulk).
 #include "common.cuh"
 #include "profile.h"
 #include "ops.h"
 
 namespace ql {
 
-constexpr int AT_BM = 64;   // queries per forward CTA
+constexpr int AT_BM = 64;   // queries per forward CTA (= AT_BN: the Q tile borrows a K buffer)
 constexpr int AT_BN = 64;   // keys per step / per backward CTA
 constexpr int AT_BQ = 32;   // queries per backward step
+constexpr int AT_LONG = 1024; // max_len from which the forward takes its long-sequence shape
 constexpr int AT_QCH = 128; // queries per backward CTA (a chunk of a key block's rows)
 
 // element offset of (row, col) in a [rows][D] 16-bit tile (D = 64 or 128) with its 16-byte
@@ -54,14 +57,20 @@ __device__ __forceinline__ void load_tile(T* tile, const T* base, int64_t ld, in
 // ---------------------------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------------------------
-template <typename T, int AT_D>
-__global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
+// Two shapes of the same kernel. kShare (long sequences, many key blocks per CTA): the Q tile is
+// staged in the second K buffer and its fragments move to registers before the first prefetch
+// overwrites it, so a CTA holds 64 KB (D = 128) and three CTAs share an SM. Otherwise (short
+// sequences, one wave of CTAs whose latency is the kernel's time): Q has its own buffer, the
+// second key block is prefetched at once, and the register budget is that of two CTAs per SM.
+template <typename T, int AT_D, bool kShare>
+__global__ void __launch_bounds__(128, kShare ? 3 : 2) attn_fwd_kernel(AttnFwdC a) {
   pdl_enter();
   extern __shared__ __align__(16) uint8_t at_smem[];
-  T* sQ = reinterpret_cast<T*>(at_smem);
-  T* sK = sQ + AT_BM * AT_D;          // [2][64][D]
-  T* sV = sK + 2 * AT_BN * AT_D;      // [2][64][D]
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  T* sK = reinterpret_cast<T*>(at_smem);  // [2][64][D]
+  T* sV = sK + 2 * AT_BN * AT_D;          // [2][64][D]
+  T* sQ = kShare ? sK + AT_BN * AT_D : sV + 2 * AT_BN * AT_D;
+  // the longest causal rows first: the last query blocks of a sequence run the most key blocks
+  const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
   if (qb * AT_BM >= len) return;
   const int group = a.HQ / a.HKV, kvh = h / group;
@@ -88,6 +97,21 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
   uint32_t qf[KS][4];
   const int qrow0 = qb * AT_BM + warp * 16;  // first query row of this warp (in the sequence)
 
+  auto load_q_fragments = [&]() {
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int c = kk * 16 + (lane >> 4) * 8;
+      ldsm_x4(sQ + sw<AT_D>(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+  };
+  if (kShare) {
+    cp_async_wait<0>();
+    __syncthreads();
+    load_q_fragments();
+    __syncthreads();  // every warp holds its Q fragments: K buffer 1 is free
+  }
+
   for (int kb = 0; kb < nkb; ++kb) {
     const int buf = kb & 1;
     if (kb + 1 < nkb) {
@@ -95,18 +119,12 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
       load_tile<T, AT_D, AT_BN, 128>(sV + (buf ^ 1) * AT_BN * AT_D, V, ldk, (kb + 1) * AT_BN, len);
       cp_async_commit();
       cp_async_wait<1>();
-    } else {
+      __syncthreads();
+    } else if (!kShare || kb > 0) {
       cp_async_wait<0>();
+      __syncthreads();
     }
-    __syncthreads();
-    if (kb == 0) {
-#pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = kk * 16 + (lane >> 4) * 8;
-        ldsm_x4(sQ + sw<AT_D>(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-      }
-    }
+    if (!kShare && kb == 0) load_q_fragments();
     const T* tK = sK + buf * AT_BN * AT_D;
     const T* tV = sV + buf * AT_BN * AT_D;
     float s[8][4];
@@ -124,43 +142,53 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
         mma16816<T>(s[2 * jp + 1], qf[kk], b2, b3);
       }
     }
-    // scale, causal / length mask, online softmax (rows g and g + 8 of this warp)
+    // causal / length mask and online softmax (rows g and g + 8 of this warp). The running max
+    // mrow is in the scaled log2 domain and is raised lazily: only when a row's new max exceeds
+    // it by more than 8 (probabilities up to 2^8 stay exact in the 16-bit P and fp32 sums) are O
+    // and l rescaled, and never unless some row of the warp needs it.
     const bool diag = kb == qb;
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
       const int qi = qrow0 + g + hr * 8;
-      float mx = mrow[hr];
+      float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int kj = kb * AT_BN + j * 8 + 2 * t4 + e;
-          float v = s[j][hr * 2 + e] * sl2;
-          if (diag && (kj > qi || kj >= len)) v = -INFINITY;
-          s[j][hr * 2 + e] = v;
-          mx = fmaxf(mx, v);
+          if (diag) {
+            const int kj = kb * AT_BN + j * 8 + 2 * t4 + e;
+            if (kj > qi || kj >= len) s[j][hr * 2 + e] = -INFINITY;
+          }
+          mx = fmaxf(mx, s[j][hr * 2 + e]);
         }
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float corr = mrow[hr] == -INFINITY ? 0.f : exp2f(mrow[hr] - mx);
-      mrow[hr] = mx;
+      const float ms = mx * sl2;  // this block's row max, scaled
+      const bool raise = ms > mrow[hr] + 8.f;
+      if (__any_sync(0xffffffffu, raise)) {
+        const float m_new = raise ? ms : mrow[hr];
+        const float corr = mrow[hr] == -INFINITY ? 0.f : exp2f(mrow[hr] - m_new);
+        mrow[hr] = m_new;
+        lrow[hr] *= corr;
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+          o[i][hr * 2] *= corr;
+          o[i][hr * 2 + 1] *= corr;
+        }
+      }
+      const float mneg = mrow[hr] == -INFINITY ? 0.f : -mrow[hr];
       float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float p = mx == -INFINITY ? 0.f : exp2f(s[j][hr * 2 + e] - mx);
+          const float p = exp2f(fmaf(s[j][hr * 2 + e], sl2, mneg));  // exp2(-inf) = 0
           s[j][hr * 2 + e] = p;
           sum += p;
         }
       }
-      lrow[hr] = lrow[hr] * corr + sum;
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        o[i][hr * 2] *= corr;
-        o[i][hr * 2 + 1] *= corr;
-      }
+      lrow[hr] += sum;
     }
     // O += P V
 #pragma unroll
@@ -201,16 +229,21 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(AttnFwdC a) {
   }
 }
 
-template <typename T, int D>
-static void launch_attn_fwd(const AttnFwdC& a, cudaStream_t s) {
-  const int smem = (AT_BM + 4 * AT_BN) * D * 2;
+template <typename T, int D, bool kShare>
+static void launch_attn_fwd_shape(const AttnFwdC& a, cudaStream_t s) {
+  const int smem = (kShare ? 4 * AT_BN : 4 * AT_BN + AT_BM) * D * 2;
   static bool cfg = false;
   if (!cfg) {
-    cudaFuncSetAttribute(attn_fwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(attn_fwd_kernel<T, D, kShare>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cfg = true;
   }
   dim3 grid((unsigned)cdiv(a.max_len, AT_BM), (unsigned)a.HQ, (unsigned)a.B);
-  launch_k(attn_fwd_kernel<T, D>, grid, dim3(128), smem, s, a);
+  launch_k(attn_fwd_kernel<T, D, kShare>, grid, dim3(128), smem, s, a);
+}
+template <typename T, int D>
+static void launch_attn_fwd(const AttnFwdC& a, cudaStream_t s) {
+  if (a.max_len >= AT_LONG) launch_attn_fwd_shape<T, D, true>(a, s);
+  else launch_attn_fwd_shape<T, D, false>(a, s);
 }
 
 int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
@@ -260,8 +293,10 @@ __global__ void attn_bwd_pre_kernel(const T* __restrict__ dout, const T* __restr
 // One CTA per (64-key block, query head, sequence); 4 warps, warp w owns keys 16w .. 16w + 15.
 // Steps over the query rows from the key block's start in blocks of 32: recomputes P^T, then
 // dV += P^T dO, dP^T = V dO^T, dS^T = P^T (dP^T - Dvec), dK += dS^T Q, and dQ += dS K through a
-// shared-memory copy of dS^T (atomically added to the fp32 dq). dK, dV are added atomically
-// into the KV head's fp32 rows at the end (the group's query heads all contribute).
+// shared-memory copy of dS^T. The step's dQ tile is staged in shared memory and added to the
+// fp32 dq rows by bulk reductions (one 4D-byte row per query, issued by warp 0's lanes); dK and dV
+// are staged the same way at the end and bulk-added into the KV head's fp32 rows (the query
+// chunks and the group's query heads all contribute).
 template <typename T, int AT_D>
 __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
   pdl_enter();
@@ -271,9 +306,11 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
   T* sQ = sV + AT_BN * AT_D;                // [2][32][D]
   T* sO = sQ + 2 * AT_BQ * AT_D;            // [2][32][D] (dO)
   T* sS = sO + 2 * AT_BQ * AT_D;            // [64][40] dS^T (padded rows)
-  float* sL = reinterpret_cast<float*>(sS + AT_BN * 40);  // [2][32] lse
+  float* sL = reinterpret_cast<float*>(sS + AT_BN * 40);  // [2][32] lse * log2(e)
   float* sD = sL + 2 * AT_BQ;                              // [2][32] Dvec
+  float* sDQ = sD + 2 * AT_BQ;                             // [32][D + 8] dQ tile (fp32)
   constexpr int SROW = 40;
+  constexpr int FROW = AT_D + 8;  // fp32 staging pitch: 16-byte rows, conflict-free float2 stores
 
   // blockIdx.x = (query chunk) x (key block): the key block's query rows are cut into chunks of
   // AT_QCH so that no CTA walks a long sequence alone (dK / dV are added atomically anyway)
@@ -304,7 +341,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
     load_tile<T, AT_D, AT_BQ, 128>(sO + buf * AT_BQ * AT_D, dO, ldq, r0, len);
     if (threadIdx.x < AT_BQ) {
       const int qi = r0 + threadIdx.x;
-      sL[buf * AT_BQ + threadIdx.x] = qi < len ? lse[qi] : INFINITY;  // masked: p = 0
+      sL[buf * AT_BQ + threadIdx.x] = qi < len ? lse[qi] * 1.4426950408889634f : INFINITY;  // masked: p = 0
       sD[buf * AT_BQ + threadIdx.x] = qi < len ? dvec[qi] : 0.f;
     }
   };
@@ -329,6 +366,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
     } else {
       cp_async_wait<0>();
     }
+    if (warp == 0) bulk_wait_read<0>();  // the previous step's dQ tile has been read out
     __syncthreads();
     const T* tQ = sQ + buf * AT_BQ * AT_D;
     const T* tO = sO + buf * AT_BQ * AT_D;
@@ -371,7 +409,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
         const int key = key0 + g + (e >> 1) * 8;
         const int ql = j * 8 + 2 * t4 + (e & 1);  // query within the step
         const int qi = qbase + ql;
-        float p = exp2f(s[j][e] * sl2 - tL[ql] * 1.4426950408889634f);
+        float p = exp2f(fmaf(s[j][e], sl2, -tL[ql]));
         if (key > qi || qi >= len || key >= len) p = 0.f;
         s[j][e] = p;
         dp[j][e] = p * (dp[j][e] - tD[ql]);
@@ -440,43 +478,56 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(AttnBwdC a) {
       }
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
-        const int qi = qbase + qm + g + hr * 8;
-        if (qi < len) {
-          float* dst = a.dq + ((int64_t)(start + qi) * a.HQ + h) * AT_D + dn;
+        float* row = sDQ + (qm + g + hr * 8) * FROW + dn + 2 * t4;
 #pragma unroll
-          for (int i = 0; i < HT; ++i) {
-            atomicAdd(dst + i * 8 + 2 * t4, dq[i][hr * 2] * a.scale);
-            atomicAdd(dst + i * 8 + 2 * t4 + 1, dq[i][hr * 2 + 1] * a.scale);
-          }
-        }
+        for (int i = 0; i < HT; ++i)
+          *reinterpret_cast<float2*>(row + i * 8) = make_float2(dq[i][hr * 2] * a.scale, dq[i][hr * 2 + 1] * a.scale);
       }
+      fence_proxy_async_smem();
     }
-    __syncthreads();  // sS, and the Q / dO buffer reloaded next step
+    __syncthreads();  // sS and the dQ tile written; the Q / dO buffer is reloaded next step
+    if (warp == 0) {
+      const int qi = qbase + lane;
+      if (qi < len)
+        bulk_reduce_add_f32(a.dq + ((int64_t)(start + qi) * a.HQ + h) * AT_D, sDQ + lane * FROW, AT_D * 4);
+      bulk_commit();
+    }
   }
-  // dK (scaled), dV into the KV head's fp32 rows
+  // dK (scaled) and dV staged over the K / V / Q / dO / dS^T tiles (all dead after the last
+  // step's closing barrier), then bulk-added into the KV head's fp32 rows
+  float* sDK = reinterpret_cast<float*>(at_smem);  // [64][D + 8]
+  float* sDV = sDK + AT_BN * FROW;                  // [64][D + 8]
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
-    const int key = key0 + g + hr * 8;
-    if (key < len) {
-      float* dkp = a.dk + ((int64_t)(start + key) * a.HKV + kvh) * AT_D;
-      float* dvp = a.dv + ((int64_t)(start + key) * a.HKV + kvh) * AT_D;
+    const int kr = warp * 16 + g + hr * 8;
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        atomicAdd(dkp + i * 8 + 2 * t4, dk[i][hr * 2] * a.scale);
-        atomicAdd(dkp + i * 8 + 2 * t4 + 1, dk[i][hr * 2 + 1] * a.scale);
-        atomicAdd(dvp + i * 8 + 2 * t4, dv[i][hr * 2]);
-        atomicAdd(dvp + i * 8 + 2 * t4 + 1, dv[i][hr * 2 + 1]);
-      }
+    for (int i = 0; i < NT; ++i) {
+      *reinterpret_cast<float2*>(sDK + kr * FROW + i * 8 + 2 * t4) = make_float2(dk[i][hr * 2] * a.scale, dk[i][hr * 2 + 1] * a.scale);
+      *reinterpret_cast<float2*>(sDV + kr * FROW + i * 8 + 2 * t4) = make_float2(dv[i][hr * 2], dv[i][hr * 2 + 1]);
     }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  {
+    const int r = threadIdx.x & (AT_BN - 1);  // threads 0-63: dK rows, 64-127: dV rows
+    const int key = kb * AT_BN + r;
+    if (key < len) {
+      float* dst = (threadIdx.x < AT_BN ? a.dk : a.dv) + ((int64_t)(start + key) * a.HKV + kvh) * AT_D;
+      bulk_reduce_add_f32(dst, (threadIdx.x < AT_BN ? sDK : sDV) + r * FROW, AT_D * 4);
+    }
+    bulk_commit();
+    bulk_wait<0>();  // dQ, dK and dV reductions of this thread complete before the CTA exits
   }
 }
 
 template <typename T, int D>
 static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   const int64_t rows = (int64_t)a.n * a.HQ;
-  launch_k(attn_bwd_pre_kernel<T, D>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s, 
+  launch_k(attn_bwd_pre_kernel<T, D>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
       (const T*)a.dout, (const T*)a.out, a.dvec, a.n, a.HQ);
-  const int smem = (2 * AT_BN + 4 * AT_BQ) * D * 2 + AT_BN * 40 * 2 + 4 * AT_BQ * 4;
+  const int smem = (2 * AT_BN + 4 * AT_BQ) * D * 2 + AT_BN * 40 * 2 + 4 * AT_BQ * 4 +
+                   AT_BQ * (D + 8) * 4;
+  static_assert(AT_BQ == 32 && 2 * AT_BN == 128, "one dQ row per lane of warp 0; one dK / dV row per thread");
   static bool cfg = false;
   if (!cfg) {
     cudaFuncSetAttribute(attn_bwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -492,6 +543,10 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
   if (a.n == 0 || a.B == 0) return QL_STATUS_OK;
   if (a.dvec == nullptr) return QL_STATUS_BAD_ARG;
+  // dq, dk and dv rows are bulk-reduced: 16-byte aligned bases
+  if ((reinterpret_cast<uintptr_t>(a.dq) | reinterpret_cast<uintptr_t>(a.dk) |
+       reinterpret_cast<uintptr_t>(a.dv)) & 15)
+    return QL_STATUS_BAD_ARG;
   ProfScope prof(PK_ATTN_BWD, 0, 0, s);
   // gradients accumulate atomically: start from zero
   if (cudaMemsetAsync(a.dq, 0, sizeof(float) * a.n * a.HQ * a.D, s) != cudaSuccess ||

@@ -151,7 +151,8 @@ def main():
         sec = _time(lambda i: ops.gemm(logits, W, b_kn=True), args.iters)
         _report("gemm_nn lm_head dgrad", [n, H, V], sec, flops=2.0 * n * V * H)
     if want("attn"):
-        lengths = [300, 257, 400, 133]
+        # the bench's short packed sequences, or (attn:long) configs[2]-like long ones
+        lengths = [3072, 2560, 4096, 2048] if shape_only == "long" else [300, 257, 400, 133]
         m = sum(lengths)
         cu = torch.tensor([0] + torch.tensor(lengths).cumsum(0).tolist(), device=dev,
                           dtype=torch.int32)

@@ -357,7 +357,7 @@ def test_ce_rows_and_pieces_match_torch(V):
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("lengths", [[7, 130, 1, 64], [300, 257, 1024, 33], [65]])
+@pytest.mark.parametrize("lengths", [[7, 130, 1, 64], [300, 257, 1024, 33], [65], [2100, 700, 5]])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("heads", [(12, 2, 128), (4, 2, 64), (28, 4, 128)])
 def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads):
@@ -394,5 +394,40 @@ def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads):
         close(dq[sl], g[0].transpose(0, 1), 5 * tol)
         close(dk[sl], g[1].transpose(0, 1), 5 * tol)
         close(dv[sl], g[2].transpose(0, 1), 5 * tol)
+        start += length
+    assert o.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_attention_rising_scores(dtype):
+    """Scores that climb along the keys (a shared direction in q and a ramp in k), so the running
+    row max of the forward's online softmax keeps rising by small and large steps: the lazily
+    rescaled output and logsumexp still match fp32 SDPA."""
+    o = ops()
+    torch.manual_seed(1)
+    HQ, HKV, D = 12, 2, 128
+    lengths = [1500, 190]
+    cu = torch.tensor([0, *np.cumsum(lengths).tolist()], device=DEV, dtype=torch.int32)
+    n = sum(lengths)
+    u = torch.randn(D, device=DEV)
+    u = u / u.norm()
+    ramp = torch.cat([torch.linspace(0, 1, L, device=DEV) ** 2 for L in lengths])
+    q = (torch.randn(n, HQ, D, device=DEV) + 4 * u).to(dtype)
+    k = (torch.randn(n, HKV, D, device=DEV) + 40 * ramp[:, None, None] * u).to(dtype)
+    v = torch.randn(n, HKV, D, device=DEV).to(dtype)
+    scale = D ** -0.5
+    out, lse = o.attn_fwd(q, k, v, cu, max(lengths), scale)
+    tol = 2e-3 if dtype == torch.float16 else 1.5e-2
+    start = 0
+    for length in lengths:
+        sl = slice(start, start + length)
+        qr = q[sl].float().transpose(0, 1)
+        ke = k[sl].float().transpose(0, 1).repeat_interleave(HQ // HKV, 0)
+        ve = v[sl].float().transpose(0, 1).repeat_interleave(HQ // HKV, 0)
+        ref = torch.nn.functional.scaled_dot_product_attention(qr, ke, ve, is_causal=True)
+        close(out[sl], ref.transpose(0, 1), tol)
+        s = (qr @ ke.transpose(-1, -2)) * scale
+        s = s.masked_fill(torch.ones(length, length, device=DEV).triu(1).bool(), float("-inf"))
+        close(lse[:, sl], torch.logsumexp(s, -1), 1e-3)
         start += length
     assert o.device_status() == 0
