@@ -12,6 +12,8 @@
 // shared memory read with ldmatrix. The forward's online softmax raises its running row max
 // lazily (output rescaled only on a rise of more than 2^8); the backward's fp32 gradient tiles are
 // added to dq / dk / dv by bulk reductions from shared memory (cp.reduce.async.bulk).
+#include <atomic>
+
 #include "common.cuh"
 #include "profile.h"
 #include "ops.h"
@@ -246,11 +248,18 @@ static void launch_attn_fwd(const AttnFwdC& a, cudaStream_t s) {
   else launch_attn_fwd_shape<T, D, false>(a, s);
 }
 
+static std::atomic<int> g_attn_impl{0};
+void attn_set_impl(int impl) { g_attn_impl.store(impl); }
+
 int attn_fwd(const AttnFwdC& a, cudaStream_t s) {
   if (a.D != 128 && a.D != 64) return QL_STATUS_UNSUPPORTED;
   if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
   if (a.n == 0 || a.B == 0 || a.max_len == 0) return QL_STATUS_OK;
   ProfScope prof(PK_ATTN_FWD, 0, 0, s);
+  if (a.D == 128 && (a.dtype == QL_F16 || a.dtype == QL_BF16) && g_attn_impl.load() != 1) {
+    const int st = attn_fwd_tc(a, s);
+    return st == QL_STATUS_OK ? launched(1) : st;
+  }
   if (a.dtype == QL_F16) {
     if (a.D == 128) launch_attn_fwd<__half, 128>(a, s); else launch_attn_fwd<__half, 64>(a, s);
   } else if (a.dtype == QL_BF16) {

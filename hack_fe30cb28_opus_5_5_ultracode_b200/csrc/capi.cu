@@ -288,6 +288,12 @@ int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream) {
   return done(ql::attn_bwd(*args, stream), "ql_attn_bwd");
 }
 
+int ql_attn_set_impl(int impl) {
+  if (impl < 0 || impl > 2) return done(QL_STATUS_BAD_ARG, "ql_attn_set_impl");
+  ql::attn_set_impl(impl);
+  return QL_STATUS_OK;
+}
+
 }  // extern "C"
 
 extern "C" {

@@ -161,9 +161,11 @@ def main():
         v = torch.randn(m, HKV, D, device=dev, generator=g).to(dt)
         flops = sum(4.0 * L * (L + 1) / 2 * HQ * D for L in lengths)
         out, lse = ops.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5)
-        sec = _time(lambda i: ops.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5, out=out, lse=lse),
-                    args.iters)
-        _report("attn_fwd", lengths, sec, flops=flops)
+        for impl, name in ((1, "attn_fwd mma.sync"), (0, "attn_fwd")):
+            ops.attn_set_impl(impl)
+            sec = _time(lambda i: ops.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5, out=out,
+                                               lse=lse), args.iters)
+            _report(name, lengths, sec, flops=flops)
         dout = torch.randn_like(q)
         sec = _time(lambda i: ops.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths), D ** -0.5),
                     args.iters)

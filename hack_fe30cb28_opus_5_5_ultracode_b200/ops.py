@@ -116,6 +116,11 @@ def gemm_set_mode(mode):
     call("ql_gemm_set_mode", int(mode))
 
 
+def attn_set_impl(impl):
+    """Attention forward kernel for D = 128: 0 default (tcgen05), 1 warp-level mma.sync, 2 tcgen05."""
+    call("ql_attn_set_impl", int(impl))
+
+
 _GEMM_WS = {}
 
 

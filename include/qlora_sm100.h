@@ -354,6 +354,11 @@ typedef struct {
 
 int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream);
 int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream);
+/* Which forward kernel serves D = 128: 0 (default) the tcgen05 kernel (TMEM accumulators, TMA
+ * tiles), 1 the warp-level mma.sync kernel (always used for D = 64), 2 the tcgen05 kernel.
+ * No counterpart in the reference (one attention implementation there); tests and the
+ * microbenchmark compare the two. */
+int ql_attn_set_impl(int impl);
 
 /* ---- head row order ----------------------------------------------------------------------
  * The head takes rows with a target first (solution/engine.py:731, 1364-1398):

@@ -357,15 +357,27 @@ def test_ce_rows_and_pieces_match_torch(V):
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
+@pytest.fixture
+def attn_impl(request):
+    """The attention forward kernel for D = 128 (1 mma.sync, 2 tcgen05); reset afterwards."""
+    o = ops()
+    o.attn_set_impl(request.param)
+    yield request.param
+    o.attn_set_impl(0)
+
+
+@pytest.mark.parametrize("attn_impl", [1, 2], indirect=True)
 @pytest.mark.parametrize("lengths", [[7, 130, 1, 64], [300, 257, 1024, 33], [65], [2100, 700, 5]])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("heads", [(12, 2, 128), (4, 2, 64), (28, 4, 128)])
-def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads):
+def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads, attn_impl):
     """Against per-sequence SDPA in fp32 (reference test_varlen_attention_matches_sdpa,
-    solution/test_kernels.py:245-281), with k / v per KV head."""
+    solution/test_kernels.py:245-281), with k / v per KV head; both forward kernels."""
     o = ops()
     torch.manual_seed(0)
     HQ, HKV, D = heads
+    if D == 64 and attn_impl == 2:
+        pytest.skip("the tcgen05 forward serves D = 128 only")
     group = HQ // HKV
     cu = torch.tensor([0, *np.cumsum(lengths).tolist()], device=DEV, dtype=torch.int32)
     n = sum(lengths)
@@ -398,8 +410,9 @@ def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads):
     assert o.device_status() == 0
 
 
+@pytest.mark.parametrize("attn_impl", [1, 2], indirect=True)
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_attention_rising_scores(dtype):
+def test_attention_rising_scores(dtype, attn_impl):
     """Scores that climb along the keys (a shared direction in q and a ramp in k), so the running
     row max of the forward's online softmax keeps rising by small and large steps: the lazily
     rescaled output and logsumexp still match fp32 SDPA."""
