@@ -563,6 +563,17 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
       cudaMemsetAsync(a.dv, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess)
     return QL_STATUS_CUDA;
   if (a.max_len == 0) return QL_STATUS_OK;
+  if (a.D == 128 && (a.dtype == QL_F16 || a.dtype == QL_BF16) && g_attn_impl.load() != 1) {
+    const int64_t rows = (int64_t)a.n * a.HQ;
+    if (a.dtype == QL_F16)
+      launch_k(attn_bwd_pre_kernel<__half, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
+               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ);
+    else
+      launch_k(attn_bwd_pre_kernel<__nv_bfloat16, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
+               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ);
+    const int st = attn_bwd_tc(a, s);
+    return st == QL_STATUS_OK ? launched(2) : st;
+  }
   if (a.dtype == QL_F16) {
     if (a.D == 128) launch_attn_bwd<__half, 128>(a, s); else launch_attn_bwd<__half, 64>(a, s);
   } else if (a.dtype == QL_BF16) {

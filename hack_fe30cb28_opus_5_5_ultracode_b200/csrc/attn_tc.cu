@@ -245,6 +245,307 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------------
+// One CTA per (128-key block, query chunk of up to TB_QCH queries, query head, sequence). The
+// key block's K and V stay in shared memory; the chunk's query blocks of 64 stream through a
+// two-stage ring (Q, dO, lse * log2(e), Dvec). Per query block j, all on tcgen05 with fp32
+// accumulators in TMEM (lane = the M row):
+//   S^T  = K Q_j^T          [128 keys x 64 q]   K-major A and B
+//   dP^T = V dO_j^T         [128 keys x 64 q]
+//   (softmax warps, one key row per thread) P^T = exp2(S^T sl2 - lse2), masked causally;
+//   dS^T = P^T (dP^T - Dvec); both to shared memory as 16-bit [key][q] tiles (128-byte swizzle)
+//   dV  += P^T dO_j         [128 keys x 128 d]  A K-major, B (dO) MN-major
+//   dK  += dS^T Q_j         [128 keys x 128 d]
+//   dQ^T = K^T dS^T         [128 d x 64 q]      A (K) MN-major, B (dS^T) MN-major
+// dQ^T is read by four more warps (one d row per thread), scaled, staged as [64 q][128 d] fp32
+// and added to dq by bulk reductions; at the end dK (scaled) and dV are staged the same way and
+// bulk-added to the KV head's fp32 rows (the chunks and the group's query heads all add there).
+// Warps: 0 loads (all lanes: lse / Dvec; lane 0: TMA), 1 MMA, 2-5 softmax + final dK / dV,
+// 6-9 dQ. TMEM: S^T [0, 64), dP^T [64, 128), dQ^T [128, 192), dV [192, 320), dK [320, 448).
+constexpr int TB_BK = 128;           // keys per CTA
+constexpr int TB_BQ = 64;            // queries per block
+constexpr int TB_QCH = 512;          // queries per CTA (a chunk from the key block's diagonal)
+constexpr int TB_KT = TB_BK * 256;   // K or V tile: 128 rows x 128 d (two 64-column boxes)
+constexpr int TB_KBOX = TB_KT / 2;
+constexpr int TB_QT = TB_BQ * 256;   // Q or dO tile: 64 rows x 128 d
+constexpr int TB_QBOX = TB_QT / 2;
+constexpr int TB_PT = TB_BK * 128;   // P^T or dS^T tile: 128 keys x 64 q (one box)
+constexpr int TB_OFF_K = 0, TB_OFF_V = TB_KT, TB_OFF_STAGE = 2 * TB_KT;  // stage s at + 2 s TB_QT
+constexpr int TB_OFF_P = TB_OFF_STAGE + 4 * TB_QT, TB_OFF_DS = TB_OFF_P + TB_PT;
+constexpr int TB_OFF_DQ = TB_OFF_DS + TB_PT;              // [64 q][128 d] fp32
+constexpr int TB_OFF_L = TB_OFF_DQ + TB_BQ * 128 * 4;     // [2][64] lse2, [2][64] Dvec
+constexpr int TB_OFF_BAR = TB_OFF_L + 4 * TB_BQ * 4;
+constexpr int TB_SMEM = TB_OFF_BAR + 256 + 1024;
+constexpr int TB_KV_PITCH = 128 * 4 + 16;  // final dK / dV staging rows (conflict-free float4)
+static_assert(2 * TB_BK * TB_KV_PITCH <= TB_OFF_DQ, "dK / dV staging over the dead tiles");
+
+template <bool IS_BF16>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                       const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                       AttnBwdC a, int* err) {
+  pdl_enter();
+  using T = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* sL = reinterpret_cast<float*>(smem + TB_OFF_L);  // [2][64]
+  float* sDv = sL + 2 * TB_BQ;                              // [2][64]
+  float* sDQ = reinterpret_cast<float*>(smem + TB_OFF_DQ);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TB_OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;   // [2] Q, dO landed and lse2 / Dvec stored
+  uint64_t* qd_empty = bars + 3;  // [2] the MMAs reading the stage completed
+  uint64_t* st_full = bars + 5;   // S^T, dP^T written
+  uint64_t* st_free = bars + 6;   // S^T, dP^T read by the 128 softmax threads
+  uint64_t* p_full = bars + 7;    // P^T, dS^T tiles written by the 128 softmax threads
+  uint64_t* p_free = bars + 8;    // the MMAs reading P^T / dS^T completed
+  uint64_t* dq_full = bars + 9;   // dQ^T written
+  uint64_t* dq_free = bars + 10;  // dQ^T read by the 128 dQ threads
+  uint64_t* dkv_full = bars + 11; // the last dV / dK MMAs completed
+  uint64_t* dqs_free = bars + 12; // dQ staging read out by the previous block's reductions
+  uint64_t* dqs_full = bars + 13; // dQ staging written by the 128 dQ threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+
+  const int nkb = (int)cdiv(a.max_len, TB_BK);
+  const int kb = blockIdx.x % nkb, chunk = blockIdx.x / nkb, h = blockIdx.y, b = blockIdx.z;
+  const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
+  const int key0 = kb * TB_BK, q_first = key0 + chunk * TB_QCH;
+  if (key0 >= len || q_first >= len) return;  // the whole CTA, before any setup
+  const int q_end = min(len, q_first + TB_QCH);
+  const int nq = (int)cdiv(q_end - q_first, TB_BQ);
+  const int kvh = h / (a.HQ / a.HKV);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qd_full[s], 33);  // lane 0's expect_tx arrival + all 32 lanes after their stores
+      mbar_init(&qd_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(st_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(dkv_full, 1);
+    mbar_init(dqs_free, 32);
+    mbar_init(dqs_full, 128);
+    fence_barrier_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdo);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t C_ST = 0, C_DPT = 64, C_DQT = 128, C_DV = 192, C_DK = 320;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * TB_KT);
+      tma_load_2d(smem + TB_OFF_K, &tk, kv_full, kvh * 128, start + key0);
+      tma_load_2d(smem + TB_OFF_K + TB_KBOX, &tk, kv_full, kvh * 128 + 64, start + key0);
+      tma_load_2d(smem + TB_OFF_V, &tv, kv_full, kvh * 128, start + key0);
+      tma_load_2d(smem + TB_OFF_V + TB_KBOX, &tv, kv_full, kvh * 128 + 64, start + key0);
+    }
+    const float* lse = a.lse + (int64_t)h * a.n + start;
+    const float* dvec = a.dvec + (int64_t)h * a.n + start;
+    for (int j = 0; j < nq; ++j) {
+      const int s = j & 1, q0 = q_first + j * TB_BQ;
+      if (j >= 2 && !mbar_wait(&qd_empty[s], ((j >> 1) - 1) & 1, err)) break;
+      if (lane == 0) {
+        uint8_t* st = smem + TB_OFF_STAGE + s * 2 * TB_QT;
+        mbar_arrive_expect_tx(&qd_full[s], 2 * TB_QT);
+        tma_load_2d(st, &tq, &qd_full[s], h * 128, start + q0);
+        tma_load_2d(st + TB_QBOX, &tq, &qd_full[s], h * 128 + 64, start + q0);
+        tma_load_2d(st + TB_QT, &tdo, &qd_full[s], h * 128, start + q0);
+        tma_load_2d(st + TB_QT + TB_QBOX, &tdo, &qd_full[s], h * 128 + 64, start + q0);
+      }
+#pragma unroll
+      for (int t = lane; t < TB_BQ; t += 32) {
+        const int q = q0 + t;
+        sL[s * TB_BQ + t] = q < len ? lse[q] * 1.4426950408889634f : INFINITY;  // p = 0 past len
+        sDv[s * TB_BQ + t] = q < len ? dvec[q] : 0.f;
+      }
+      mbar_arrive(&qd_full[s]);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_st = umma_idesc_f16(IS_BF16, 128, TB_BQ);              // S^T, dP^T
+      constexpr uint32_t id_kv = umma_idesc_f16(IS_BF16, 128, 128, true);           // dV, dK
+      constexpr uint32_t id_dq = umma_idesc_f16(IS_BF16, 128, TB_BQ, true, true);   // dQ^T
+      const uint32_t sk = smem_u32(smem + TB_OFF_K), sv = smem_u32(smem + TB_OFF_V);
+      const uint32_t sp = smem_u32(smem + TB_OFF_P), sds = smem_u32(smem + TB_OFF_DS);
+      bool ok = mbar_wait(kv_full, 0, err);
+      for (int j = 0; ok && j <= nq; ++j) {
+        if (j < nq) {
+          const int s = j & 1;
+          if (!mbar_wait(&qd_full[s], (j >> 1) & 1, err)) break;
+          if (j >= 1 && !mbar_wait(st_free, (j - 1) & 1, err)) break;
+          tc_fence_after();
+          const uint32_t sq = smem_u32(smem + TB_OFF_STAGE + s * 2 * TB_QT), sdo = sq + TB_QT;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t ok_ = (kk >> 2) * TB_KBOX + (kk & 3) * 32, oq = (kk >> 2) * TB_QBOX + (kk & 3) * 32;
+            umma_f16(tmem + C_ST, umma_desc_k_sw128(sk + ok_), umma_desc_k_sw128(sq + oq), id_st, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t ok_ = (kk >> 2) * TB_KBOX + (kk & 3) * 32, oq = (kk >> 2) * TB_QBOX + (kk & 3) * 32;
+            umma_f16(tmem + C_DPT, umma_desc_k_sw128(sv + ok_), umma_desc_k_sw128(sdo + oq), id_st, kk > 0);
+          }
+          umma_commit(st_full);
+        }
+        if (j >= 1) {
+          const int i = j - 1, s = i & 1;
+          if (!mbar_wait(p_full, i & 1, err)) break;
+          tc_fence_after();
+          const uint32_t sq = smem_u32(smem + TB_OFF_STAGE + s * 2 * TB_QT), sdo = sq + TB_QT;
+#pragma unroll
+          for (int kk = 0; kk < TB_BQ / 16; ++kk) {  // dV += P^T dO ; dK += dS^T Q  (k = queries)
+            umma_f16(tmem + C_DV, umma_desc_k_sw128(sp + kk * 32),
+                     umma_desc_mn_sw128(sdo + kk * 2048, TB_QBOX, 1024), id_kv, (i > 0 || kk > 0));
+            umma_f16(tmem + C_DK, umma_desc_k_sw128(sds + kk * 32),
+                     umma_desc_mn_sw128(sq + kk * 2048, TB_QBOX, 1024), id_kv, (i > 0 || kk > 0));
+          }
+          if (i >= 1 && !mbar_wait(dq_free, (i - 1) & 1, err)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < TB_BK / 16; ++kk)  // dQ^T = K^T dS^T  (k = keys)
+            umma_f16(tmem + C_DQT, umma_desc_mn_sw128(sk + kk * 2048, TB_KBOX, 1024),
+                     umma_desc_mn_sw128(sds + kk * 2048, TB_PT, 1024), id_dq, kk > 0);
+          umma_commit(&qd_empty[s]);
+          umma_commit(p_free);
+          umma_commit(dq_full);
+        }
+      }
+      umma_commit(dkv_full);
+    }
+  } else if (warp < 6) {
+    // softmax: thread = key row r of the block
+    const int quad = warp & 3, r = quad * 32 + lane, key = key0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const float sl2 = a.scale * 1.4426950408889634f;
+    uint8_t* pP = smem + TB_OFF_P + r * 128;
+    uint8_t* pS = smem + TB_OFF_DS + r * 128;
+    bool ok = true;
+    for (int j = 0; j < nq; ++j) {
+      const int s = j & 1, q0 = q_first + j * TB_BQ;
+      if (!mbar_wait(st_full, j & 1, err)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t su[TB_BQ], du[TB_BQ];
+      tmem_ld32_nw(lane_base + C_ST, su);
+      tmem_ld32_nw(lane_base + C_ST + 32, su + 32);
+      tmem_ld32_nw(lane_base + C_DPT, du);
+      tmem_ld32_nw(lane_base + C_DPT + 32, du + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(st_free);
+      if (!mbar_wait(&qd_full[s], (j >> 1) & 1, err)) { ok = false; break; }
+      if (j >= 1 && !mbar_wait(p_free, (j - 1) & 1, err)) { ok = false; break; }
+      const float* l2 = sL + s * TB_BQ;
+      const float* dv = sDv + s * TB_BQ;
+      const bool diag = q0 < key0 + TB_BK;  // some query of the block precedes some key
+#pragma unroll
+      for (int ch = 0; ch < TB_BQ / 8; ++ch) {
+        float p[8], ds[8];
+        const float4 la = *reinterpret_cast<const float4*>(l2 + ch * 8);
+        const float4 lb = *reinterpret_cast<const float4*>(l2 + ch * 8 + 4);
+        const float4 da = *reinterpret_cast<const float4*>(dv + ch * 8);
+        const float4 db = *reinterpret_cast<const float4*>(dv + ch * 8 + 4);
+        const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+        const float dd[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = ch * 8 + e;
+          float pv = exp2f(fmaf(__uint_as_float(su[c]), sl2, -lv[e]));
+          if (diag && q0 + c < key) pv = 0.f;
+          p[e] = pv;
+          ds[e] = pv * (__uint_as_float(du[c]) - dd[e]);
+        }
+        const uint32_t off = (uint32_t)(((ch ^ (r & 7))) << 4);
+        *reinterpret_cast<uint4*>(pP + off) =
+            make_uint4(pack_t2<T>(p[0], p[1]), pack_t2<T>(p[2], p[3]), pack_t2<T>(p[4], p[5]), pack_t2<T>(p[6], p[7]));
+        *reinterpret_cast<uint4*>(pS + off) =
+            make_uint4(pack_t2<T>(ds[0], ds[1]), pack_t2<T>(ds[2], ds[3]), pack_t2<T>(ds[4], ds[5]), pack_t2<T>(ds[6], ds[7]));
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // dK (scaled) and dV: TMEM -> staging over the dead tiles -> bulk reductions
+    if (ok && mbar_wait(dkv_full, 0, err)) {
+      tc_fence_after();
+      uint8_t* stk = smem + r * TB_KV_PITCH;
+      uint8_t* stv = smem + TB_BK * TB_KV_PITCH + r * TB_KV_PITCH;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        float vk[32], vv[32];
+        tmem_ld32(lane_base + C_DK + c, vk);
+        tmem_ld32(lane_base + C_DV + c, vv);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          reinterpret_cast<float4*>(stk + c * 4)[u] =
+              make_float4(vk[4 * u] * a.scale, vk[4 * u + 1] * a.scale, vk[4 * u + 2] * a.scale, vk[4 * u + 3] * a.scale);
+          reinterpret_cast<float4*>(stv + c * 4)[u] = make_float4(vv[4 * u], vv[4 * u + 1], vv[4 * u + 2], vv[4 * u + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      if (key < len) {
+        const int64_t row = ((int64_t)(start + key) * a.HKV + kvh) * 128;
+        bulk_reduce_add_f32(a.dk + row, reinterpret_cast<const float*>(stk), 512);
+        bulk_reduce_add_f32(a.dv + row, reinterpret_cast<const float*>(stv), 512);
+      }
+      bulk_commit();
+      bulk_wait<0>();
+    }
+  } else {
+    // dQ: thread = d row of dQ^T
+    const int quad = warp & 3, d = quad * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    for (int i = 0; i < nq; ++i) {
+      const int q0 = q_first + i * TB_BQ;
+      if (!mbar_wait(dq_full, i & 1, err)) break;
+      tc_fence_after();
+      float v[TB_BQ];
+      tmem_ld32(lane_base + C_DQT, v);
+      tmem_ld32(lane_base + C_DQT + 32, v + 32);
+      tc_fence_before();
+      mbar_arrive(dq_free);
+      if (warp == 6) {  // the previous block's reductions have read the staging
+        bulk_wait_read<0>();
+        mbar_arrive(dqs_free);
+      }
+      if (!mbar_wait(dqs_free, i & 1, err)) break;
+#pragma unroll
+      for (int q = 0; q < TB_BQ; ++q) sDQ[q * 128 + d] = v[q] * a.scale;
+      fence_proxy_async_smem();
+      mbar_arrive(dqs_full);
+      if (warp == 6) {
+        if (!mbar_wait(dqs_full, i & 1, err)) break;
+#pragma unroll
+        for (int t = lane; t < TB_BQ; t += 32)
+          if (q0 + t < len)
+            bulk_reduce_add_f32(a.dq + ((int64_t)(start + q0 + t) * a.HQ + h) * 128, sDQ + t * 128, 512);
+        bulk_commit();
+      }
+    }
+    if (warp == 6) bulk_wait<0>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
 }  // namespace
 
 // Host side: tensor maps over q [n, HQ * 128] and k / v [n, HKV * 128] (boxes of 64 columns x
@@ -266,6 +567,28 @@ int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s) {
   } else {
     smem_optin(reinterpret_cast<const void*>(attn_fwd_tc_kernel<false>), TA_SMEM);
     launch_k(attn_fwd_tc_kernel<false>, grid, dim3(192), TA_SMEM, s, mq, mk, mv, a, err);
+  }
+  return QL_STATUS_OK;
+}
+
+int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s) {
+  if (a.D != 128) return QL_STATUS_UNSUPPORTED;
+  const bool bf = a.dtype == QL_BF16;
+  CUtensorMap mq, mdo, mk, mv;
+  const int64_t wq = (int64_t)a.HQ * 128, wk = (int64_t)a.HKV * 128;
+  if (make_kmajor_map(&mq, a.q, a.n, wq, wq, TB_BQ, bf) != QL_STATUS_OK ||
+      make_kmajor_map(&mdo, a.dout, a.n, wq, wq, TB_BQ, bf) != QL_STATUS_OK ||
+      make_kmajor_map(&mk, a.k, a.n, wk, wk, TB_BK, bf) != QL_STATUS_OK ||
+      make_kmajor_map(&mv, a.v, a.n, wk, wk, TB_BK, bf) != QL_STATUS_OK)
+    return QL_STATUS_CUDA;
+  dim3 grid((unsigned)(cdiv(a.max_len, TB_BK) * cdiv(a.max_len, TB_QCH)), (unsigned)a.HQ, (unsigned)a.B);
+  int* err = status_word();
+  if (bf) {
+    smem_optin(reinterpret_cast<const void*>(attn_bwd_tc_kernel<true>), TB_SMEM);
+    launch_k(attn_bwd_tc_kernel<true>, grid, dim3(320), TB_SMEM, s, mq, mdo, mk, mv, a, err);
+  } else {
+    smem_optin(reinterpret_cast<const void*>(attn_bwd_tc_kernel<false>), TB_SMEM);
+    launch_k(attn_bwd_tc_kernel<false>, grid, dim3(320), TB_SMEM, s, mq, mdo, mk, mv, a, err);
   }
   return QL_STATUS_OK;
 }

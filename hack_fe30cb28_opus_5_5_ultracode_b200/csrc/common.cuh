@@ -227,11 +227,13 @@ __device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint3
 }
 
 // Instruction descriptor of tcgen05.mma.kind::f16: fp32 accumulator, A and B of the same 16-bit
-// type (is_bf16), A K-major, B K-major or MN-major (b_mn), M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(bool is_bf16, int M, int N, bool b_mn = false) {
+// type (is_bf16), A and B each K-major or MN-major (a_mn, b_mn), M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool is_bf16, int M, int N, bool b_mn = false,
+                                                      bool a_mn = false) {
   return (1u << 4)                                  // D format: f32
          | ((is_bf16 ? 1u : 0u) << 7)               // A format
          | ((is_bf16 ? 1u : 0u) << 10)              // B format
+         | ((a_mn ? 1u : 0u) << 15)                 // A major-ness
          | ((b_mn ? 1u : 0u) << 16)                 // B major-ness
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }

@@ -65,6 +65,7 @@ typedef ql_attn_fwd_args AttnFwdC;
 typedef ql_attn_bwd_args AttnBwdC;
 int attn_fwd(const AttnFwdC& a, cudaStream_t s);
 int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (launch only)
+int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (main kernel only)
 void attn_set_impl(int impl);
 int attn_bwd(const AttnBwdC& a, cudaStream_t s);
 }  // namespace ql

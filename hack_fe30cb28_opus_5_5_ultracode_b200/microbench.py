@@ -167,9 +167,11 @@ def main():
                                                lse=lse), args.iters)
             _report(name, lengths, sec, flops=flops)
         dout = torch.randn_like(q)
-        sec = _time(lambda i: ops.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths), D ** -0.5),
-                    args.iters)
-        _report("attn_bwd", lengths, sec, flops=2.5 * flops)
+        for impl, name in ((1, "attn_bwd mma.sync"), (0, "attn_bwd")):
+            ops.attn_set_impl(impl)
+            sec = _time(lambda i: ops.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths),
+                                               D ** -0.5), args.iters)
+            _report(name, lengths, sec, flops=2.5 * flops)
     if want("glu"):
         gu = [torch.randn(n, 2 * I, device=dev, generator=g).to(dt) for _ in range(copies)]
         m_ = [torch.empty(n, I, device=dev, dtype=dt) for _ in range(copies)]

@@ -117,7 +117,7 @@ def gemm_set_mode(mode):
 
 
 def attn_set_impl(impl):
-    """Attention forward kernel for D = 128: 0 default (tcgen05), 1 warp-level mma.sync, 2 tcgen05."""
+    """Attention kernels for D = 128: 0 default (tcgen05), 1 warp-level mma.sync, 2 tcgen05."""
     call("ql_attn_set_impl", int(impl))
 
 

@@ -354,8 +354,9 @@ typedef struct {
 
 int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream);
 int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream);
-/* Which forward kernel serves D = 128: 0 (default) the tcgen05 kernel (TMEM accumulators, TMA
- * tiles), 1 the warp-level mma.sync kernel (always used for D = 64), 2 the tcgen05 kernel.
+/* Which kernels serve D = 128 (forward and backward): 0 (default) the tcgen05 kernels (TMEM
+ * accumulators, TMA tiles), 1 the warp-level mma.sync kernels (always used for D = 64), 2 the
+ * tcgen05 kernels.
  * No counterpart in the reference (one attention implementation there); tests and the
  * microbenchmark compare the two. */
 int ql_attn_set_impl(int impl);

@@ -359,7 +359,7 @@ def test_ce_rows_and_pieces_match_torch(V):
 # ---------------------------------------------------------------------------------------------
 @pytest.fixture
 def attn_impl(request):
-    """The attention forward kernel for D = 128 (1 mma.sync, 2 tcgen05); reset afterwards."""
+    """The attention kernels for D = 128 (1 mma.sync, 2 tcgen05); reset afterwards."""
     o = ops()
     o.attn_set_impl(request.param)
     yield request.param
@@ -372,7 +372,7 @@ def attn_impl(request):
 @pytest.mark.parametrize("heads", [(12, 2, 128), (4, 2, 64), (28, 4, 128)])
 def test_varlen_gqa_attention_matches_sdpa(lengths, dtype, heads, attn_impl):
     """Against per-sequence SDPA in fp32 (reference test_varlen_attention_matches_sdpa,
-    solution/test_kernels.py:245-281), with k / v per KV head; both forward kernels."""
+    solution/test_kernels.py:245-281), with k / v per KV head; both kernel families."""
     o = ops()
     torch.manual_seed(0)
     HQ, HKV, D = heads
