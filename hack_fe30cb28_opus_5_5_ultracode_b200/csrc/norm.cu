@@ -139,7 +139,10 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
     const int row = tile * RMS_ROWS + rrow;
     const bool live = row < a.n;
     const int64_t base = (int64_t)row * H;
-    float4 xv[G];
+    // the row is kept in registers between the passes for up to 16 columns per lane; wider rows
+    // (G = 8 with 4 warps per row: 1,024 threads and 64 registers each) read it again
+    constexpr bool kKeepX = G <= 4 || WPR == 1;
+    float4 xv[kKeepX ? G : 1];
     float ss = 0.f;
     if (live) {
 #pragma unroll
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
             x = make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
             *reinterpret_cast<float4*>(a.xsum + base + 4 * gi) = x;
           }
-          xv[k] = x;
+          if constexpr (kKeepX) xv[k] = x;
           ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
         }
       }
@@ -177,7 +180,9 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
         if (gi < ngroups) {
           const int c = 4 * gi;
           const float4 w = *reinterpret_cast<const float4*>(a.w + c);
-          const float4 x = xv[k];
+          float4 x;
+          if constexpr (kKeepX) x = xv[k];
+          else x = *reinterpret_cast<const float4*>((a.delta != nullptr ? a.xsum : a.x) + base + c);
           const float4 y = make_float4(w.x * (x.x * rstd), w.y * (x.y * rstd),
                                        w.z * (x.z * rstd), w.w * (x.w * rstd));
           if (a.y != nullptr) store4<T>(reinterpret_cast<T*>(a.y) + base + c, y);
@@ -298,7 +303,10 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
     const bool live = row < a.n;
     const int64_t base = (int64_t)row * H;
     float rstd = 0.f;
-    float4 gv[G], xh[G];
+    // x * rstd is kept in registers between the passes for up to 16 columns per lane; wider
+    // rows (G = 8 with 4 warps per row: 1,024 threads and 64 registers each) read x again
+    constexpr bool kKeepX = G <= 4 || WPR == 1;
+    float4 gv[G], xh[kKeepX ? G : 1];
     float dot = 0.f;
     if (live) {
       rstd = a.rstd[row];
@@ -330,7 +338,7 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
           const float4 g = make_float4(dy.x * w.x, dy.y * w.y, dy.z * w.z, dy.w * w.w);
           const float4 h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
           gv[k] = g;
-          xh[k] = h;
+          if constexpr (kKeepX) xh[k] = h;
           dot += g.x * h.x + g.y * h.y + g.z * h.z + g.w * h.w;
         }
       }
@@ -350,7 +358,14 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
         const int gi = 32 * part + lane + 32 * WPR * k;
         if (gi < ngroups) {
           const int c = 4 * gi;
-          const float4 g = gv[k], h = xh[k];
+          float4 h;
+          if constexpr (kKeepX) {
+            h = xh[k];
+          } else {
+            const float4 x = *reinterpret_cast<const float4*>(a.x + base + c);
+            h = make_float4(x.x * rstd, x.y * rstd, x.z * rstd, x.w * rstd);
+          }
+          const float4 g = gv[k];
           float4 d = make_float4(rstd * (g.x - h.x * mean) * a.grad_scale,
                                  rstd * (g.y - h.y * mean) * a.grad_scale,
                                  rstd * (g.z - h.z * mean) * a.grad_scale,
@@ -377,9 +392,9 @@ static int rms_grid(int64_t n) {
   return (int)(want < cap ? want : cap);
 }
 
-// Warps per row: 4 for rows of 1024..2048 columns (more warps in flight over the few rows of a
-// step, 4 groups per lane), else 1.
-static int rms_wpr(int H) { return (H >= 1024 && H <= 2048 && H % 256 == 0) ? 4 : 1; }
+// Warps per row: 4 for rows of 1024..4096 columns (more warps in flight over the few rows of a
+// step, 4 or 8 groups of 4 columns per lane), else 1.
+static int rms_wpr(int H) { return (H >= 1024 && H <= 4096 && H % 256 == 0) ? 4 : 1; }
 
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
 template <typename K>
@@ -416,11 +431,13 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   } while (0)
   const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
-    if (wpr == 4) QL_RMSF(__half, 4, 4);
+    if (wpr == 4 && G <= 4) QL_RMSF(__half, 4, 4);
+    else if (wpr == 4) QL_RMSF(__half, 8, 4);
     else if (G <= 4) QL_RMSF(__half, 4, 1); else if (G <= 12) QL_RMSF(__half, 12, 1);
     else QL_RMSF(__half, 32, 1);
   } else if (c.dtype == QL_BF16) {
-    if (wpr == 4) QL_RMSF(__nv_bfloat16, 4, 4);
+    if (wpr == 4 && G <= 4) QL_RMSF(__nv_bfloat16, 4, 4);
+    else if (wpr == 4) QL_RMSF(__nv_bfloat16, 8, 4);
     else if (G <= 4) QL_RMSF(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSF(__nv_bfloat16, 12, 1);
     else QL_RMSF(__nv_bfloat16, 32, 1);
   } else {
@@ -460,11 +477,13 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   } while (0)
   const int G = (int)cdiv(c.H / 4, 32 * wpr);
   if (c.dtype == QL_F16) {
-    if (wpr == 4) QL_RMSB(__half, 4, 4);
+    if (wpr == 4 && G <= 4) QL_RMSB(__half, 4, 4);
+    else if (wpr == 4) QL_RMSB(__half, 8, 4);
     else if (G <= 4) QL_RMSB(__half, 4, 1); else if (G <= 12) QL_RMSB(__half, 12, 1);
     else QL_RMSB(__half, 32, 1);
   } else if (c.dtype == QL_BF16) {
-    if (wpr == 4) QL_RMSB(__nv_bfloat16, 4, 4);
+    if (wpr == 4 && G <= 4) QL_RMSB(__nv_bfloat16, 4, 4);
+    else if (wpr == 4) QL_RMSB(__nv_bfloat16, 8, 4);
     else if (G <= 4) QL_RMSB(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSB(__nv_bfloat16, 12, 1);
     else QL_RMSB(__nv_bfloat16, 32, 1);
   } else {

@@ -90,7 +90,7 @@ def test_rms_matches_reference_golden(golden):
     close(dx, torch.from_numpy(g["dx"]), 1e-4)
 
 
-@pytest.mark.parametrize("n,H", [(37, 1536), (5, 256), (300, 3584)])
+@pytest.mark.parametrize("n,H", [(37, 1536), (5, 256), (300, 3584), (64, 4096), (40, 2304)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_rms_fused_lora_matches_torch(n, H, dtype):
     o = ops()
@@ -133,7 +133,7 @@ def test_rms_fused_lora_matches_torch(n, H, dtype):
     close(d16, dx_a, tol)
 
 
-@pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584)])
+@pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584), (64, 4096)])
 def test_rms_mask_bits_match_redrawn_masks(n, H):
     """The forward's mask bits are the Philox masks; a backward that reads them equals one that
     draws the masks again, bit for bit."""
