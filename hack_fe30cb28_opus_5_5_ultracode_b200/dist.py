@@ -1,8 +1,13 @@
 """Data parallelism of the fused step: each rank packs and runs its own batch on its own GPU
 with replicated frozen weights; the only exchange is the LoRA gradients, averaged over the ranks
-with NCCL over NVLink (torch.distributed), one bucket per decoder layer launched as soon as that
-layer's backward has written it, so the all-reduce of layer i overlaps the backward of layers
-below it. The reference runs on one GPU only; this is the B200 build's data-parallel layer.
+with NCCL over NVLink (torch.distributed). The reference runs on one GPU only; this is the B200
+build's data-parallel layer.
+
+The gradients of the whole model are one flat fp32 buffer (8.7 MB at Qwen2.5-1.5B r16), summed in
+one all-reduce after the backward: tens of microseconds over NVLink. Per-layer buckets launched
+during the backward (to overlap the exchange with the layers below) measured 12 ms per step
+slower on B200 at ~1 k tokens per rank: NCCL's kernels then wait for the slower rank on SMs that
+the persistent GEMM grids (one CTA per SM) need.
 """
 
 import torch

@@ -420,6 +420,7 @@ class FusedQwen2:
             self.offsets.append(self.offsets[-1] + n)
         self.process_group = None
         self.data_parallel = False  # LoRA gradients averaged over the ranks (dist.GradReducer)
+        self._comm = None           # the all-reduce buffer of the data-parallel gradients
         for spec in self.layers:
             for g in (spec.qkv, spec.o, spec.gu, spec.down):
                 if g.split:
@@ -469,8 +470,8 @@ class FusedQwen2:
         return self._workspace
 
     def set_data_parallel(self, group=None):
-        """Average the LoRA gradients over `group` (None: the default process group) inside the
-        backward, one bucket per layer as it finishes, overlapped with the layers below it."""
+        """Average the LoRA gradients over `group` (None: the default process group) at the end
+        of the backward, in one all-reduce of the flat gradient buffer."""
         self.process_group = group
         self.data_parallel = True
 
@@ -676,13 +677,16 @@ class FusedQwen2:
                           ops.stream_ptr())
                 if offload is not None and plan.modes[i] == memory.OFFLOAD:
                     offload.after_backward(i)
-                if reducer is not None:
-                    reducer.launch(grads[lo:self.offsets[4 * i + 4]])
                 cur = nxt
-        elif reducer is not None:
-            reducer.launch(grads)
-        if reducer is not None:
-            reducer.finish(grads)
+        if reducer is not None:  # one all-reduce of every LoRA gradient, after the backward
+            # through a buffer that keeps its address from step to step (NCCL registers it once);
+            # the gradients handed to autograd stay this step's own tensors
+            if self._comm is None:
+                self._comm = torch.empty_like(grads)
+            self._comm.copy_(grads)
+            reducer.launch(self._comm)
+            reducer.finish(self._comm)
+            grads.copy_(self._comm)
         self.last_offload_bytes = offload.bytes_moved if offload is not None else 0
         return views
 

@@ -1,5 +1,6 @@
-"""CPU, two gloo ranks: the data-parallel gradient reduction of the fused step (one bucket per
-layer launched as its backward finishes, averaged at the end) gives every rank the mean of the
+"""CPU, two gloo ranks: the data-parallel gradient reduction of the fused step (GradReducer: any
+number of contiguous buckets of the flat gradient buffer, summed and averaged at the end; the
+engine uses one bucket, the whole buffer, after the backward) gives every rank the mean of the
 ranks' LoRA gradients, and the bench's timing reduction takes the max over ranks."""
 
 import os
