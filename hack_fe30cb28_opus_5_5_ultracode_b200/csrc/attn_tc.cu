@@ -461,8 +461,6 @@ __global__ void __launch_bounds__(320, 1)
       const float* l2 = sL + s * TB_BQ;
       const float* dv = sDv + s * TB_BQ;
       const bool diag = q0 < key0 + TB_BK;  // some query of the block precedes some key
-      // off the diagonal every other group of 8 exponentials runs on the FMA pipe (exp2_fma)
-      auto emit = [&](auto mix) {
 #pragma unroll
       for (int ch = 0; ch < TB_BQ / 8; ++ch) {
         float p[8], ds[8];
@@ -475,9 +473,8 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = ch * 8 + e;
-          const float x = fmaf(__uint_as_float(su[c]), sl2, -lv[e]);
-          float pv = (decltype(mix)::value && (ch & 1)) ? exp2_fma(x) : exp2f(x);
-          if (!decltype(mix)::value && q0 + c < key) pv = 0.f;
+          float pv = exp2f(fmaf(__uint_as_float(su[c]), sl2, -lv[e]));
+          if (diag && q0 + c < key) pv = 0.f;
           p[e] = pv;
           ds[e] = pv * (__uint_as_float(du[c]) - dd[e]);
         }
@@ -487,9 +484,6 @@ __global__ void __launch_bounds__(320, 1)
         *reinterpret_cast<uint4*>(pS + off) =
             make_uint4(pack_t2<T>(ds[0], ds[1]), pack_t2<T>(ds[2], ds[3]), pack_t2<T>(ds[4], ds[5]), pack_t2<T>(ds[6], ds[7]));
       }
-      };
-      if (diag) emit(std::false_type{});
-      else emit(std::true_type{});
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
