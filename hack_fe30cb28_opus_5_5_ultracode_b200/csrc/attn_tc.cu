@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(192, 1)
 // 6-9 dQ. TMEM: S^T [0, 64), dP^T [64, 128), dQ^T [128, 192), dV [192, 320), dK [320, 448).
 constexpr int TB_BK = 128;           // keys per CTA
 constexpr int TB_BQ = 64;            // queries per block
-constexpr int TB_QCH = 512;          // queries per CTA (a chunk from the key block's diagonal)
+constexpr int TB_QCH = 1024;         // queries per CTA (a chunk from the key block's diagonal)
 constexpr int TB_KT = TB_BK * 256;   // K or V tile: 128 rows x 128 d (two 64-column boxes)
 constexpr int TB_KBOX = TB_KT / 2;
 constexpr int TB_QT = TB_BQ * 256;   // Q or dO tile: 64 rows x 128 d
