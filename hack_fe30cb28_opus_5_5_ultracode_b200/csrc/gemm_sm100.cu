@@ -29,7 +29,7 @@ template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
-  pdl_enter();
+  pdl_trigger();  // setup below reads no global memory; pdl_wait() follows it
   constexpr bool kTmaC = sizeof(OutT) == 2;
   using Cfg = GemmCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's results (A, counters, C) are visible from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -280,7 +281,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
-  pdl_enter();
+  pdl_trigger();  // setup below reads no global memory; pdl_wait() follows it
   constexpr bool kTmaC = sizeof(OutT) == 2;
   using Cfg = PairCfg<BN, kTmaC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
@@ -319,6 +320,7 @@ __global__ void __launch_bounds__(192, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's results are visible from here on
 
   if (warp == 0) {
     if (lane == 0) {
