@@ -360,8 +360,8 @@ int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream);
  * No counterpart in the reference (one attention implementation there); tests and the
  * microbenchmark compare the two. */
 int ql_attn_set_impl(int impl);
-/* y[i] = 2^x[i] by the FMA-pipe polynomial the tcgen05 attention softmax uses for half of its
- * off-diagonal exponentials (a check of its error bound against the GPU's exp2; no counterpart in
+/* y[i] = 2^x[i] by the FMA-pipe polynomial the tcgen05 attention forward's softmax uses for half
+ * of its off-diagonal exponentials (a check of its error bound against the GPU's exp2; no counterpart in
  * the reference). */
 int ql_exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t stream);
 
