@@ -333,7 +333,7 @@ def run_ours(args, rank, world, local):
         model_accepts_loss_kwargs=True, state=types.SimpleNamespace(global_step=0),
         _metrics={"train": {"entropy": [], "mean_token_accuracy": [], "num_tokens": []}},
         _total_train_tokens=0, _soup_rewind_state=None)
-    trainer._soup_original_compute_loss = trainer.compute_loss
+    setattr(trainer, patch._ORIGINAL_ATTR, trainer.compute_loss)
     setattr(trainer, patch._INSTALLED_ATTR, engine)
     pinned = [tuple(torch.from_numpy(a).pin_memory() for a in b[:3]) for b in host]
 
@@ -344,7 +344,7 @@ def run_ours(args, rank, world, local):
         loss = patch.fused_compute_loss(trainer, model, inputs,
                                         num_items_in_batch=denoms[i])
         loss.backward()
-        patch._flush_metrics(trainer)
+        patch.flush_metrics(trainer)
         opt.step()
         opt.zero_grad(set_to_none=True)
         return loss.detach().float().item()

@@ -21,6 +21,7 @@ B200-first differences from the reference (which was built for a 16 GB T4):
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import _lib, memory, ops
@@ -32,11 +33,13 @@ HEAD_CHUNK = 4096  # rows of logits alive at a time: 4096 x 151936 x 2 B = 1.2 G
 # NF4 weights (solution/engine.py:74-157)
 # ---------------------------------------------------------------------------------------------
 class NF4Group:
-    """One or more bitsandbytes NF4 weights with the same column count stored back to back in
-    device memory (q, k, v; gate, up; or a single weight): one dequantisation launch for all of
-    them. Only the double-quantisation offset differs between members (per segment); their
-    absmax2 are concatenated, which needs every member but the last to end on a whole absmax2
-    block (else each member is dequantised on its own)."""
+    """The NF4 weights one launch dequantises, read as a single weight of `rows` rows: q, k and
+    v; gate and up; or one weight alone. The members share their column count and quantisation
+    layout and sit contiguously in device memory in member order (all packed bytes, then all
+    first-level scales). With double quantisation each member keeps its own offset, switched at
+    the block indices seg1 / seg2, while the second-level scales are concatenated; that is only
+    right if every member but the last fills whole second-level blocks, and `split` marks the
+    groups where one does not."""
 
     def __init__(self, params, device):
         states = [p.quant_state for p in params]
@@ -117,65 +120,83 @@ class NF4Group:
 
 
 # ---------------------------------------------------------------------------------------------
-# LoRA dropout masks: PyTorch's own (solution/engine.py:767-828)
+# LoRA dropout: the slice of the CUDA generator's Philox stream PEFT's dropout calls consume
 # ---------------------------------------------------------------------------------------------
-def dropout_call(nelem, max_blocks, block=256, unroll=4):
-    """(threads, generator offset increment) of aten's CUDA dropout on nelem elements with at
-    most max_blocks resident blocks (solution/engine.py:787-797)."""
-    blocks = min(max_blocks, (nelem + block - 1) // block)
-    increment = ((nelem - 1) // (block * blocks * unroll) + 1) * unroll
-    return blocks * block, increment
+DROPOUT_BLOCK, DROPOUT_UNROLL = 256, 4  # launch constants of aten/src/ATen/native/cuda/Dropout.cu
+SELF_CHECK_SEED = 2_718_281_828         # seed of the mask self-check's private RNG fork
+SELF_CHECK_SHAPE = (3, 40)              # rows x tokens of the self-check's dropout inputs
 
 
-class TorchDropout:
-    """The LoRA dropout masks PEFT's nn.Dropout draws, bit for bit: each call takes the CUDA
-    generator's (seed, offset) and advances the offset as aten's dropout kernel does
-    (block 256, UNROLL 4, grid min(SMs * maxThreadsPerSM / 256, ceil(nelem / 256))); the
-    kernels of this library compute the mask from (seed, offset / 4, grid * 256) and the element
-    index, in backward again instead of storing it."""
+def dropout_call(nelem, max_blocks, block=DROPOUT_BLOCK, unroll=DROPOUT_UNROLL):
+    """What one aten CUDA dropout call on `nelem` elements takes from the generator, as
+    (threads of its grid, Philox offset consumed): the grid is the element count in 256-thread
+    blocks, capped at the device's resident blocks; each thread loops over the tensor drawing
+    `unroll` values per Philox call (solution/engine.py:787-797 computes the same)."""
+    blocks = min(max_blocks, -(-nelem // block))
+    passes = -(-nelem // (block * blocks * unroll)) if blocks else 0
+    return blocks * block, passes * unroll
 
-    BLOCK, UNROLL = 256, 4
-    CHECK_SEED = 20261031
-    CHECK_TOKENS = 64
+
+class LoraDropoutStream:
+    """The Philox draws of PEFT's LoRA dropout calls, reserved from the CUDA generator so this
+    library's kernels can regenerate every mask from (seed, counter, threads) and the element's
+    index instead of storing it.
+
+    PEFT applies one nn.Dropout per LoRA module in forward order (layer 0 q_proj, layer 0
+    v_proj, layer 1 q_proj, ...), each on a contiguous [rows, T, H] input, so every call of a step
+    consumes the same offset: `reserve` takes all of a step's calls at once (one read and one
+    write of the generator's offset) and hands call k the counter (offset + k * increment) / 4.
+    The generator ends exactly where PEFT's own forward leaves it."""
 
     def __init__(self, device, dtype):
         self.device, self.dtype = device, dtype
-        self.ok = None
         props = torch.cuda.get_device_properties(device)
         self.max_blocks = props.multi_processor_count * (
-            props.max_threads_per_multi_processor // self.BLOCK)
-        idx = device.index if device.index is not None else torch.cuda.current_device()
-        self.gen = torch.cuda.default_generators[idx]
+            props.max_threads_per_multi_processor // DROPOUT_BLOCK)
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        self.generator = torch.cuda.default_generators[index]
+        # aten takes its vectorised path (16-byte loads) on these contiguous inputs
         self.vec = 16 // torch.empty((), dtype=dtype).element_size()
-        assert self.vec in (4, 8), dtype
+        if self.vec not in (4, 8):
+            raise ValueError(f"unsupported LoRA input dtype {dtype}")
+        self.verified = None  # outcome of verify(), run once before the first step
 
-    def draw(self, nelem):
-        """(seed, counter, threads) of a dropout call on nelem elements; advances the generator."""
-        assert nelem % self.vec == 0, nelem
-        threads, increment = dropout_call(nelem, self.max_blocks, self.BLOCK, self.UNROLL)
-        seed, offset = self.gen.initial_seed(), self.gen.get_offset()
-        self.gen.set_offset(offset + increment)
-        if seed >= 2**63:
-            seed -= 2**64
-        return seed, offset // 4, threads
+    def reserve(self, nelem, calls):
+        """(seed as a signed int64, the Philox counter of each of `calls` consecutive dropout calls
+        on `nelem` elements, threads of their grid); advances the generator past all of them."""
+        if nelem % self.vec:
+            raise ValueError(f"{nelem} elements is not a multiple of {self.vec}")
+        threads, increment = dropout_call(nelem, self.max_blocks)
+        offset = self.generator.get_offset()
+        self.generator.set_offset(offset + calls * increment)
+        seed = self.generator.initial_seed()
+        if seed >> 63:  # the kernels take the 64 seed bits as an int64
+            seed -= 1 << 64
+        return seed, [(offset + k * increment) // 4 for k in range(calls)], threads
 
-    def check(self, B, T, H, p):
-        """Whether this library's mask is PyTorch's on this GPU: the RMSNorm kernel's dropout of
-        ones over [B, T, H] against torch._fused_dropout on a private generator (the default
-        generator is not touched)."""
-        gen = torch.Generator(device=self.device)
-        gen.manual_seed(self.CHECK_SEED)
-        ones = torch.ones((B, T, H), device=self.device, dtype=self.dtype)
-        _, ref = torch._fused_dropout(ones, 1.0 - p, gen)
-        nelem = B * T * H
-        blocks = min(self.max_blocks, (nelem + self.BLOCK - 1) // self.BLOCK)
-        tok = torch.arange(B * T, device=self.device)
-        drop = ops.Drop(tok, self.CHECK_SEED, 0, 0, blocks * self.BLOCK, p, self.vec,
-                        drop_q=True, drop_v=False)
-        x = torch.ones((B * T, H), device=self.device)
-        _, _, yq, _, _, _, _ = ops.rms_fwd(x, torch.ones(H, device=self.device), 1e-6,
-                                           write_y=False, drop=drop, want_yq=True)
-        return bool(torch.equal((yq != 0).view(B, T, H), ref.bool()))
+    def verify(self, H, p):
+        """Whether this library's masks are the ones torch.nn.functional.dropout draws on this GPU
+        and build: two consecutive dropout calls (a layer's q then v input) on a fork of the RNG
+        against the RMSNorm kernel's q and v masks from a reservation of the same two calls. The
+        training generator is left as it was (torch.random.fork_rng restores it)."""
+        rows, tokens = SELF_CHECK_SHAPE
+        ones = torch.ones((rows, tokens, H), device=self.device, dtype=self.dtype)
+        with torch.random.fork_rng(devices=[self.generator.device]):
+            self.generator.manual_seed(SELF_CHECK_SEED)
+            seed, (ctr_q, ctr_v), threads = self.reserve(ones.numel(), 2)
+            end = self.generator.get_offset()
+            self.generator.manual_seed(SELF_CHECK_SEED)
+            want_q = torch.nn.functional.dropout(ones, p, training=True) != 0
+            want_v = torch.nn.functional.dropout(ones, p, training=True) != 0
+            same_end = self.generator.get_offset() == end
+        drop = ops.Drop(torch.arange(rows * tokens, device=self.device), seed, ctr_q, ctr_v,
+                        threads, p, self.vec)
+        out = ops.rms_fwd(torch.ones((rows * tokens, H), device=self.device),
+                          torch.ones(H, device=self.device), 1e-6, write_y=False, drop=drop,
+                          want_yq=True)
+        got_q, got_v = out[2] != 0, out[3] != 0
+        return bool(same_end and torch.equal(got_q, want_q.view(rows * tokens, H))
+                    and torch.equal(got_v, want_v.view(rows * tokens, H)))
 
 
 class UnsupportedBatch(ValueError):
@@ -186,6 +207,14 @@ class UnsupportedBatch(ValueError):
 # ---------------------------------------------------------------------------------------------
 # per-step packing (solution/engine.py:705-764)
 # ---------------------------------------------------------------------------------------------
+def _right_padded_lengths(mask):
+    """Row lengths of a [rows, T] 0/1 attention mask, or None if some row is not a run of ones
+    followed by zeros."""
+    m = mask.to(torch.int64)
+    valid = bool(((m == 0) | (m == 1)).all()) and bool((m[:, 1:] <= m[:, :-1]).all())
+    return m.sum(dim=1).tolist() if valid else None
+
+
 class HostBatch:
     """What the step needs to know about a batch on the host: each row's length and the number
     of tokens with a target. Computed from the batch while it is still in host memory
@@ -200,20 +229,47 @@ class HostBatch:
     @classmethod
     def of(cls, attention_mask, labels):
         """From host (CPU) tensors of a right-padded batch; None if it is not right-padded."""
-        mask = attention_mask.to("cpu").bool()
-        T = mask.shape[1]
-        lengths = mask.sum(dim=1)
-        if not torch.equal(mask, torch.arange(T)[None, :] < lengths[:, None]):
+        lengths = _right_padded_lengths(attention_mask.to("cpu"))
+        if lengths is None:
             return None
         lab = labels.to("cpu")
-        cols = torch.arange(T - 1)[None, :]
-        sup = (lab[:, 1:] != -100) & (cols < (lengths[:, None] - 1))
-        return cls(lengths.tolist(), int(sup.sum()))
+        T = lab.shape[1]
+        # a token at column t < length - 1 has target labels[row, t + 1]
+        has_next = torch.arange(T - 1)[None, :] < (torch.tensor(lengths)[:, None] - 1)
+        return cls(lengths, int(((lab[:, 1:] != -100) & has_next).sum()))
+
+
+def _index_plan(lengths, T):
+    """Host-side int64 indices of the packed tokens, one buffer: [tok | pos | row | cu_seqlens],
+    tok = row * T + pos being a token's index in the padded batch."""
+    lens = np.asarray(lengths, dtype=np.int64)
+    n = int(lens.sum())
+    cu = np.zeros(len(lens) + 1, dtype=np.int64)
+    np.cumsum(lens, out=cu[1:])
+    row = np.repeat(np.arange(len(lens), dtype=np.int64), lens)
+    pos = np.arange(n, dtype=np.int64) - cu[:-1][row]
+    return np.concatenate([row * T + pos, pos, row, cu]), n
+
+
+def _supervised_first(targets):
+    """A stable permutation putting the tokens with a target (>= 0) first, without a device
+    read: each token's destination is its rank among its own kind, offset by the supervised
+    count for the others."""
+    n = targets.numel()
+    sup = targets >= 0
+    seen = torch.cumsum(sup.to(torch.int64), 0)  # supervised tokens up to and including j
+    idx = torch.arange(n, device=targets.device)
+    dest = torch.where(sup, seen - 1, seen[-1:] + idx - seen) if n else idx
+    order = torch.empty_like(idx)
+    order.scatter_(0, dest, idx)
+    return order, seen
 
 
 class Packed:
-    """One micro-batch without its padding: the real tokens of every row back to back
-    (solution/engine.py:705-764)."""
+    """One right-padded [rows, T] micro-batch as a single sequence of its real tokens, rows back to
+    back (solution/engine.py:705-764 is the reference's): the index tensors the kernels read, the
+    next-token targets, and the order the head visits the tokens in (those with a target first,
+    so the rows without one can skip the head's backward)."""
 
     def __init__(self, input_ids, attention_mask, labels, host=None):
         """host: a HostBatch of this batch (then nothing is read back from the device); without
@@ -223,42 +279,35 @@ class Packed:
                 or labels.shape != input_ids.shape:
             raise UnsupportedBatch("inputs are not [rows, tokens]")
         B, T = input_ids.shape
-        dev = input_ids.device
         if host is None:
-            lengths = attention_mask.sum(dim=1)
-            expected = torch.arange(T, device=dev)[None, :] < lengths[:, None]
-            if not bool(torch.equal(attention_mask.bool(), expected)):
+            lengths = _right_padded_lengths(attention_mask)
+            if lengths is None:
                 raise UnsupportedBatch("attention_mask is not right-padded")
-            lengths_cpu = [int(x) for x in lengths.tolist()]
         else:
-            lengths_cpu = list(host.lengths)
-            if len(lengths_cpu) != B or any(not 0 <= x <= T for x in lengths_cpu):
+            lengths = list(host.lengths)
+            if len(lengths) != B or not all(0 <= x <= T for x in lengths):
                 raise UnsupportedBatch("host lengths do not match the batch")
-        self.T, self.rows = T, B
-        self.lengths = lengths_cpu
-        self.n = sum(lengths_cpu)
-        self.max_len = max(lengths_cpu) if lengths_cpu else 0
-        # index tensors built on the host from the lengths, copied once
-        flat = torch.cat([torch.arange(r * T, r * T + ln) for r, ln in enumerate(lengths_cpu)]) \
-            if B else torch.zeros(0, dtype=torch.int64)
-        cu = torch.zeros(B + 1, dtype=torch.int32)
-        cu[1:] = torch.tensor(lengths_cpu, dtype=torch.int32).cumsum(0) if B else cu[1:]
-        rows = torch.repeat_interleave(torch.arange(B), torch.tensor(lengths_cpu, dtype=torch.int64))
-        staged = torch.cat([flat, (flat % T), rows, cu.to(torch.int64)])
+        self.rows, self.T = B, T
+        self.lengths = [int(x) for x in lengths]
+        self.max_len = max(self.lengths, default=0)
+        plan, self.n = _index_plan(self.lengths, T)
+        staged = torch.from_numpy(plan)
+        dev = input_ids.device
         if dev.type == "cuda":
             staged = staged.pin_memory().to(dev, non_blocking=True)
         n = self.n
-        self.tok = staged[:n]                       # padded-batch index of each token (int64)
-        self.pos = staged[n:2 * n].to(torch.int32)
+        self.tok = staged[:n]                        # index in the padded batch (int64)
+        self.pos = staged[n:2 * n].to(torch.int32)   # position within its row
         self.row_of_token = staged[2 * n:3 * n]
         self.cu_seqlens = staged[3 * n:].to(torch.int32)
-        self.ids = input_ids.reshape(-1).index_select(0, self.tok)
-        shifted = torch.full_like(labels, -100)
-        shifted[:, :-1] = labels[:, 1:]
-        self.targets = shifted.reshape(-1).index_select(0, self.tok)
-        supervised = self.targets >= 0
-        self.head_order = torch.argsort((~supervised).to(torch.int8), stable=True)
-        self.n_supervised = host.n_supervised if host is not None else int(supervised.sum())
+        self.ids = input_ids.reshape(-1).take(self.tok)
+        # HF labels are unshifted: a token's target is the label of the next column of its row
+        # (-100 past the last column)
+        nxt = labels.reshape(-1).take(torch.clamp(self.tok + 1, max=max(B * T - 1, 0)))
+        self.targets = torch.where(staged[n:2 * n] < T - 1, nxt, torch.full_like(nxt, -100))
+        self.head_order, seen = _supervised_first(self.targets)
+        self.n_supervised = host.n_supervised if host is not None \
+            else (int(seen[-1]) if n else 0)
 
 
 class RopeTable:
@@ -285,8 +334,12 @@ class RopeTable:
 
 
 class HeadStats:
-    """What the head hands back for the logged metrics: row order, per-token loss, entropy,
-    correct (solution/engine.py:1343-1349)."""
+    """Per-token results of the head, in the head's token order (`order`, supervised first):
+    `tok_loss` (cross-entropy, 0 without a target), `entropy` of the predicted distribution and
+    `correct` (argmax equals the target), the inputs of the logged metrics
+    (solution/engine.py:1343-1349 hands back the same four)."""
+
+    __slots__ = ("order", "tok_loss", "entropy", "correct")
 
 
 # ---------------------------------------------------------------------------------------------
@@ -393,7 +446,8 @@ class FusedQwen2:
                        for i, layer in enumerate(inner.layers)]
         spec = self.layers[0]
         self.dropout_p = _lora_dropout(inner.layers[0], lora_names)
-        self.dropout = TorchDropout(self.device, _lora_input_dtype(inner.layers[0], lora_names)) \
+        self.dropout = LoraDropoutStream(self.device,
+                                         _lora_input_dtype(inner.layers[0], lora_names)) \
             if self.dropout_p > 0 else None
         self.drop_vec = self.dropout.vec if self.dropout is not None else 4
         self.norm_w = inner.norm.weight.detach().float().contiguous()
@@ -485,11 +539,11 @@ class FusedQwen2:
         host: an optional HostBatch of this batch (see HostBatch)."""
         packed = Packed(input_ids, attention_mask, labels, host)
         spec = self.layers[0]
-        if self.dropout is not None and self.dropout.ok is None:
-            self.dropout.ok = self.dropout.check(
-                packed.rows, min(packed.T, TorchDropout.CHECK_TOKENS), spec.H, self.dropout_p)
-        if self.dropout is not None and not self.dropout.ok:
-            raise UnsupportedBatch("LoRA dropout masks differ from PyTorch's (TorchDropout.check)")
+        if self.dropout is not None and self.dropout.verified is None:
+            self.dropout.verified = self.dropout.verify(spec.H, self.dropout_p)
+        if self.dropout is not None and not self.dropout.verified:
+            raise UnsupportedBatch("LoRA dropout masks differ from PyTorch's on this GPU "
+                                   "(LoraDropoutStream.verify)")
         with torch.no_grad():
             torch._foreach_copy_(self.lora_views, self.lora_fp32)
         stats = HeadStats()
@@ -499,14 +553,16 @@ class FusedQwen2:
     # -----------------------------------------------------------------------------------------
     # forward
     # -----------------------------------------------------------------------------------------
-    def _drop(self, packed, H):
+    def _drops(self, packed):
+        """Each layer's q and v dropout state: PEFT's 2 L dropout calls of this step, reserved
+        from the CUDA generator at once (layer i: calls 2 i and 2 i + 1)."""
+        L = len(self.layers)
         if self.dropout is None:
-            return ops.Drop(packed.tok, 0, 0, 0, 1, 0.0, 4)
-        nelem = packed.rows * packed.T * H
-        seed, ctr_q, threads = self.dropout.draw(nelem)
-        seed_v, ctr_v, threads_v = self.dropout.draw(nelem)
-        assert seed_v == seed and threads_v == threads
-        return ops.Drop(packed.tok, seed, ctr_q, ctr_v, threads, self.dropout_p, self.drop_vec)
+            return [ops.Drop(packed.tok, 0, 0, 0, 1, 0.0, 4)] * L
+        nelem = packed.rows * packed.T * self.layers[0].H
+        seed, ctrs, threads = self.dropout.reserve(nelem, 2 * L)
+        return [ops.Drop(packed.tok, seed, ctrs[2 * i], ctrs[2 * i + 1], threads, self.dropout_p,
+                         self.drop_vec) for i in range(L)]
 
     def _forward(self, packed, denom, stats):
         n = packed.n
@@ -530,8 +586,9 @@ class FusedQwen2:
             if self.w16 is not None:  # this step's 16-bit weights, every layer, few launches
                 self._dequant_all()
         saved = []
+        drops = self._drops(packed)
         for spec, desc in zip(self.layers, self.descs):
-            drop = self._drop(packed, spec.H)
+            drop = drops[spec.index]
             self._set_step(desc, packed, drop, cos, sin)
             sv = arena.saved(spec.index)
             if self.w16 is not None:

@@ -16,7 +16,8 @@ import types
 
 import torch
 
-_INSTALLED_ATTR = "_soup_kernels_engine"
+_INSTALLED_ATTR = "_qlora_b200_step"      # the FusedQwen2 an installed trainer runs
+_ORIGINAL_ATTR = "_qlora_b200_original"   # the trainer's own compute_loss
 
 
 def _log(message):
@@ -73,127 +74,194 @@ def is_supported(model):
     return True
 
 
-def fused_compute_loss(self, model, inputs, return_outputs=False, num_items_in_batch=None):
-    """Trainer.compute_loss with the fused step (solution/patch.py:268-346)."""
-    engine = getattr(self, _INSTALLED_ATTR, None)
-    original = getattr(self, "_soup_original_compute_loss")
-    usable = (
-        engine is not None
-        and getattr(model, "training", False)
-        and isinstance(inputs, dict)
-        and set(inputs) <= {"input_ids", "attention_mask", "labels", "_prediction_loss_only"}
-        and all(key in inputs for key in ("input_ids", "attention_mask", "labels"))
-        and getattr(self, "compute_loss_func", None) is None
-        and getattr(self, "label_smoother", None) is None
-    )
-    if not usable:
-        return original(model, inputs, return_outputs=return_outputs,
-                        num_items_in_batch=num_items_in_batch)
-    popped = {key: inputs.pop(key) for key in ("_prediction_loss_only",) if key in inputs}
-    input_ids, attention_mask, labels = (inputs["input_ids"], inputs["attention_mask"],
-                                         inputs["labels"])
-    # HF Trainer: sum over the batch / num_items_in_batch when the model takes loss kwargs,
-    # otherwise the model's mean over supervised tokens.
-    if getattr(self, "model_accepts_loss_kwargs", False) and num_items_in_batch is not None:
-        denom = num_items_in_batch
+_ACCEPTED_KEYS = frozenset({"input_ids", "attention_mask", "labels", "_prediction_loss_only"})
+_REQUIRED_KEYS = ("input_ids", "attention_mask", "labels")
+
+
+def _why_not_fused(trainer, model, inputs):
+    """None when the fused step can take this compute_loss call, else the reason it cannot (the
+    original code then runs). The fused step covers plain causal-LM training on a right-padded
+    batch: no eval pass, no extra model inputs, no custom loss or label smoothing
+    (solution/patch.py:268-285 draws the same line)."""
+    if getattr(trainer, _INSTALLED_ATTR, None) is None:
+        return "not installed"
+    if not getattr(model, "training", False):
+        return "evaluation"
+    if not isinstance(inputs, dict) or not set(inputs) <= _ACCEPTED_KEYS \
+            or any(key not in inputs for key in _REQUIRED_KEYS):
+        return "inputs other than input_ids / attention_mask / labels"
+    if getattr(trainer, "compute_loss_func", None) is not None:
+        return "a custom loss function"
+    if getattr(trainer, "label_smoother", None) is not None:
+        return "label smoothing"
+    return None
+
+
+def _loss_denominator(trainer, labels, num_items_in_batch):
+    """What HF Trainer divides the summed token losses by: the trainer's own token count when
+    the model takes loss kwargs, else the number of shifted labels with a target (the model's
+    mean loss)."""
+    if num_items_in_batch is not None and getattr(trainer, "model_accepts_loss_kwargs", False):
+        count = num_items_in_batch
     else:
-        denom = (labels[:, 1:] != -100).sum()
-    denom = float(denom.item() if torch.is_tensor(denom) else denom)
+        count = (labels[..., 1:] != -100).sum()
+    return float(count.item()) if torch.is_tensor(count) else float(count)
+
+
+def _cross_device_factor(trainer, num_items_in_batch):
+    """HF Trainer's multiplier of the loss under average_tokens_across_devices: its token count
+    covers every process, and the gradient all-reduce averages, so the loss is scaled by the
+    number of data-parallel replicas (processes over the tensor-parallel size, or n_gpu under
+    DataParallel)."""
+    args = getattr(trainer, "args", None)
+    if num_items_in_batch is None or not getattr(args, "average_tokens_across_devices", False) \
+            or not getattr(trainer, "model_accepts_loss_kwargs", False):
+        return 1
+    n_gpu = getattr(args, "n_gpu", 1)
+    if n_gpu > 1:
+        return n_gpu
+    accelerator = getattr(trainer, "accelerator", None)
+    replicas = getattr(accelerator, "num_processes", 1)
+    parallelism = getattr(accelerator, "parallelism_config", None)
+    return replicas // parallelism.tp_size if parallelism is not None else replicas
+
+
+class MetricLedger:
+    """The logged side effects of fused steps, kept until the trainer's next optimizer step:
+    TRL's `entropy` (mean over a micro-batch's real tokens) and `mean_token_accuracy` (over the
+    tokens with a target), and Soup's rewind row (each row's mean cross-entropy over its
+    targets). `record` queues one small device tensor per micro-batch, reduced on the GPU right
+    after the step (no host sync between forward and backward); `flush` reads every pending one
+    back in a single transfer and appends the values in micro-batch order, before the optimizer
+    step and the log read them (solution/patch.py:334-389 keeps the same values)."""
+
+    def __init__(self):
+        self.pending = []  # (device summary, rows, real tokens, training step)
+
+    def record(self, packed, stats, labels, step):
+        rows = packed.rows
+        with torch.no_grad():
+            row_of = packed.row_of_token.index_select(0, stats.order)
+            per_row = torch.zeros(rows, device=stats.tok_loss.device, dtype=torch.float64)
+            per_row.index_add_(0, row_of, stats.tok_loss.double())
+            row_targets = (labels[:, 1:] != -100).sum(dim=1).double().to(per_row.device)
+            head = torch.stack([stats.entropy.double().sum(), stats.correct.double().sum(),
+                                (packed.targets >= 0).double().sum()])
+            summary = torch.cat([head, per_row, row_targets])
+        self.pending.append((summary, rows, packed.n, step))
+
+    def flush(self, trainer):
+        if not self.pending:
+            return
+        pending, self.pending = self.pending, []
+        values = torch.cat([s for s, _, _, _ in pending]).tolist()
+        metrics = trainer._metrics["train"]
+        recorder = getattr(trainer, "_soup_rewind_state", None)
+        at = 0
+        for _, rows, real, step in pending:
+            ent, correct, supervised = values[at:at + 3]
+            per_row = values[at + 3:at + 3 + rows]
+            targets = values[at + 3 + rows:at + 3 + 2 * rows]
+            at += 3 + 2 * rows
+            metrics["entropy"].append(ent / max(real, 1.0))
+            metrics["mean_token_accuracy"].append(correct / supervised if supervised else 0.0)
+            if recorder is None or recorder.failed:
+                continue
+            try:  # the rewind recorder must never stop training
+                recorder.on_micro_batch(step=step,
+                                        row_loss=[s / max(c, 1.0) for s, c in zip(per_row, targets)],
+                                        row_tokens=[int(c) for c in targets])
+            except Exception as exc:  # noqa: BLE001
+                recorder.fail(exc)
+
+
+def ledger(trainer):
+    """The trainer's MetricLedger (made on first use)."""
+    book = getattr(trainer, "_qlora_ledger", None)
+    if book is None:
+        book = trainer._qlora_ledger = MetricLedger()
+    return book
+
+
+def flush_metrics(trainer):
+    """Appends every queued micro-batch's TRL metrics and Soup rewind rows (see MetricLedger)."""
+    ledger(trainer).flush(trainer)
+
+
+def _run_original(trainer, model, inputs, return_outputs, num_items_in_batch):
+    return getattr(trainer, _ORIGINAL_ATTR)(model, inputs, return_outputs=return_outputs,
+                                            num_items_in_batch=num_items_in_batch)
+
+
+def fused_compute_loss(self, model, inputs, return_outputs=False, num_items_in_batch=None):
+    """HF Trainer.compute_loss through the fused step (the hook the reference installs,
+    solution/patch.py:268-346): the loss is the summed token cross-entropy over HF's
+    denominator, scaled for cross-device averaging; the step's LoRA gradients reach PEFT's
+    parameters through autograd; TRL's metrics and Soup's rewind rows are queued for the next
+    optimizer step. Anything the step does not take runs the trainer's original compute_loss."""
+    if _why_not_fused(self, model, inputs) is not None:
+        return _run_original(self, model, inputs, return_outputs, num_items_in_batch)
+    labels = inputs["labels"]
+    denom = _loss_denominator(self, labels, num_items_in_batch)
+    staged = getattr(self, "_qlora_host_batch", None)
+    self._qlora_host_batch = None
+    host = staged[1] if staged is not None and staged[0] is inputs["input_ids"] else None
     from .engine import UnsupportedBatch
 
-    host = getattr(self, "_qlora_host_batch", None)
-    self._qlora_host_batch = None
-    if host is not None and (host[0] is not input_ids):
-        host = None  # stale: prepared for other inputs
+    step = getattr(self, _INSTALLED_ATTR)
     try:
-        loss, packed, stats = engine.step(input_ids, attention_mask, labels, denom,
-                                          host[1] if host is not None else None)
-    except UnsupportedBatch:  # raised before the step changed anything
-        inputs.update(popped)
-        return original(model, inputs, return_outputs=return_outputs,
-                        num_items_in_batch=num_items_in_batch)
-    args = getattr(self, "args", None)
-    if getattr(args, "average_tokens_across_devices", False) \
-            and getattr(self, "model_accepts_loss_kwargs", False) and num_items_in_batch is not None:
-        accel = getattr(self, "accelerator", None)
-        scale = getattr(accel, "num_processes", 1)
-        pc = getattr(accel, "parallelism_config", None)
-        if pc is not None:
-            scale //= pc.tp_size
-        loss = loss * (scale if getattr(args, "n_gpu", 1) <= 1 else args.n_gpu)
-
-    # TRL metrics and Soup's rewind rows, recorded once backward is queued (no host sync between
-    # forward and backward): same values, same order as TRL's / Soup's own compute_loss.
-    _flush_metrics(self)
+        loss, packed, stats = step.step(inputs["input_ids"], inputs["attention_mask"], labels,
+                                        denom, host)
+    except UnsupportedBatch:  # raised before the step changed any state
+        return _run_original(self, model, inputs, return_outputs, num_items_in_batch)
+    factor = _cross_device_factor(self, num_items_in_batch)
+    if factor != 1:
+        loss = loss * factor
     metrics = self._metrics["train"]
-    metrics["entropy"], metrics["mean_token_accuracy"]  # noqa: B018 - keys in TRL's order
+    for key in ("entropy", "mean_token_accuracy"):  # TRL creates these two before num_tokens
+        metrics.setdefault(key, [])
     self._total_train_tokens += int(packed.n)
     metrics["num_tokens"] = [self._total_train_tokens]
-    self._soup_pending_metrics = (packed, stats, labels, int(self.state.global_step) + 1)
-    if return_outputs:
-        try:
-            from transformers.modeling_outputs import CausalLMOutputWithPast
+    ledger(self).record(packed, stats, labels, int(self.state.global_step) + 1)
+    if not return_outputs:
+        return loss
+    try:
+        from transformers.modeling_outputs import CausalLMOutputWithPast
 
-            return loss, CausalLMOutputWithPast(loss=loss, logits=None)
-        except ImportError:
-            return loss, types.SimpleNamespace(loss=loss, logits=None)
-    return loss
+        return loss, CausalLMOutputWithPast(loss=loss, logits=None)
+    except ImportError:
+        return loss, types.SimpleNamespace(loss=loss, logits=None)
+
+
+def _host_facts(inputs):
+    """The HostBatch of a batch still in host memory (None for anything else)."""
+    from .engine import HostBatch
+
+    if not isinstance(inputs, dict):
+        return None
+    mask, labels = inputs.get("attention_mask"), inputs.get("labels")
+    if not (torch.is_tensor(mask) and torch.is_tensor(labels)) or mask.is_cuda or labels.is_cuda:
+        return None
+    return HostBatch.of(mask, labels)
 
 
 def prepare_inputs(trainer, inputs, device):
-    """Move a host batch to the GPU as HF Trainer._prepare_inputs does (pinned, non-blocking)
-    and keep its HostBatch (lengths, supervised count) for the next fused_compute_loss, which
-    then reads nothing back from the device. install() routes the trainer's own
-    _prepare_inputs through this."""
-    from .engine import HostBatch
-
-    host = None
-    if isinstance(inputs, dict) and "attention_mask" in inputs and "labels" in inputs \
-            and not inputs["attention_mask"].is_cuda and not inputs["labels"].is_cuda:
-        host = HostBatch.of(inputs["attention_mask"], inputs["labels"])
+    """Moves a host batch to the GPU as HF Trainer._prepare_inputs does (pinned, non-blocking)
+    and keeps its HostBatch for the next fused_compute_loss, which then reads nothing back from
+    the device."""
+    host = _host_facts(inputs)
     device = torch.device(device)
 
     def move(v):
         if not torch.is_tensor(v) or v.device == device:
             return v
-        if device.type == "cuda":
-            return v.pin_memory().to(device, non_blocking=True)
-        return v.to(device)
+        return v.pin_memory().to(device, non_blocking=True) if device.type == "cuda" \
+            else v.to(device)
 
     moved = {k: move(v) for k, v in inputs.items()}
     if host is not None and "input_ids" in moved:
         trainer._qlora_host_batch = (moved["input_ids"], host)
     return moved
-
-
-def _flush_metrics(trainer):
-    """Record the queued micro-batch's TRL metrics and Soup rewind row
-    (solution/patch.py:349-389)."""
-    pending = getattr(trainer, "_soup_pending_metrics", None)
-    if pending is None:
-        return
-    trainer._soup_pending_metrics = None
-    packed, stats, labels, step = pending
-    with torch.no_grad():
-        valid = packed.targets >= 0
-        summary = torch.stack([stats.entropy.sum(), stats.correct.sum().float(),
-                               valid.sum().float()]).tolist()
-    trainer._metrics["train"]["entropy"].append(summary[0] / max(packed.n, 1))
-    trainer._metrics["train"]["mean_token_accuracy"].append(
-        summary[1] / summary[2] if summary[2] > 0 else 0.0)
-    state = getattr(trainer, "_soup_rewind_state", None)
-    if state is not None and not state.failed:
-        try:
-            with torch.no_grad():
-                totals = torch.zeros(packed.rows, device=labels.device, dtype=torch.float32)
-                totals.index_add_(0, packed.row_of_token.index_select(0, stats.order),
-                                  stats.tok_loss)
-                counts = (labels[:, 1:] != -100).sum(dim=1)
-                means = totals / counts.clamp(min=1).to(totals.dtype)
-            state.on_micro_batch(step=step, row_loss=[float(x) for x in means.tolist()],
-                                 row_tokens=[int(x) for x in counts.tolist()])
-        except Exception as exc:  # noqa: BLE001 - the recorder never raises into training
-            state.fail(exc)
 
 
 def _callback_base():
@@ -205,15 +273,18 @@ def _callback_base():
         return object
 
 
-class _FlushMetrics(_callback_base()):
+class _LedgerFlush(_callback_base()):
+    """Writes the queued metrics before each optimizer step (and at a step's end, for a step
+    that ran no optimizer step)."""
+
     def __init__(self, trainer):
         self.trainer = trainer
 
     def on_pre_optimizer_step(self, args, state, control, **kwargs):
-        _flush_metrics(self.trainer)
+        flush_metrics(self.trainer)
 
     def on_step_end(self, args, state, control, **kwargs):
-        _flush_metrics(self.trainer)
+        flush_metrics(self.trainer)
 
 
 def install(trainer, dtype=None):
@@ -232,20 +303,14 @@ def install(trainer, dtype=None):
         args = getattr(trainer, "args", None)
         dtype = torch.bfloat16 if getattr(args, "bf16", False) else torch.float16
     engine = FusedQwen2(model, dtype=dtype)
-    trainer._soup_original_compute_loss = trainer.compute_loss
+    setattr(trainer, _ORIGINAL_ATTR, trainer.compute_loss)
     setattr(trainer, _INSTALLED_ATTR, engine)
     trainer.compute_loss = types.MethodType(fused_compute_loss, trainer)
     original_prepare = getattr(trainer, "_prepare_inputs", None)
     if original_prepare is not None:
         def _prepare_inputs(inputs):
-            # keep the batch's host-side facts before HF moves it (no device read-backs later)
-            from .engine import HostBatch
-
-            host = None
-            if isinstance(inputs, dict) and "attention_mask" in inputs and "labels" in inputs \
-                    and torch.is_tensor(inputs["attention_mask"]) \
-                    and not inputs["attention_mask"].is_cuda and not inputs["labels"].is_cuda:
-                host = HostBatch.of(inputs["attention_mask"], inputs["labels"])
+            # the batch's host-side facts, taken before HF moves it (no device reads later)
+            host = _host_facts(inputs)
             moved = original_prepare(inputs)
             if host is not None and isinstance(moved, dict) and "input_ids" in moved:
                 trainer._qlora_host_batch = (moved["input_ids"], host)
@@ -253,7 +318,7 @@ def install(trainer, dtype=None):
 
         trainer._prepare_inputs = _prepare_inputs
     if hasattr(trainer, "add_callback"):
-        trainer.add_callback(_FlushMetrics(trainer))
+        trainer.add_callback(_LedgerFlush(trainer))
     _log(f"fused Qwen2 step installed ({len(engine.layers)} layers, {dtype}, LoRA dropout "
          f"{engine.dropout_p})")
     return True

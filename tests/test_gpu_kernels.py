@@ -50,21 +50,35 @@ def test_dropout_masks_are_torchs(shape, dtype, p):
     """Bit-exact against torch.nn.functional.dropout on this GPU (reference
     test_dropout_masks_are_torchs, solution/test_kernels.py:67-90): the draw takes the CUDA
     generator's state as nn.Dropout would and advances it identically."""
-    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import TorchDropout
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import LoraDropoutStream
 
     torch.cuda.manual_seed(1234)
-    drop = TorchDropout(torch.device(DEV), dtype)
+    drop = LoraDropoutStream(torch.device(DEV), dtype)
     nelem = math.prod(shape)
-    for _ in range(3):
-        state = drop.gen.get_state()
-        seed, ctr, threads = drop.draw(nelem)
-        after = drop.gen.get_offset()
-        drop.gen.set_state(state)
+    state = drop.generator.get_state()
+    seed, ctrs, threads = drop.reserve(nelem, 3)  # three consecutive calls at once
+    after = drop.generator.get_offset()
+    drop.generator.set_state(state)
+    for ctr in ctrs:
         ref = torch.nn.functional.dropout(torch.ones(shape, device=DEV, dtype=dtype), p,
                                           training=True) != 0
-        assert drop.gen.get_offset() == after
         keep = ops().dropout_keep(nelem, seed, ctr, threads, p, drop.vec).bool()
         assert torch.equal(keep, ref.reshape(-1))
+    assert drop.generator.get_offset() == after
+
+
+@pytest.mark.parametrize("dtype,p", [(torch.float32, 0.05), (torch.float16, 0.1)])
+def test_dropout_self_check_passes_and_leaves_the_generator(dtype, p):
+    """The step's one-time self-check (LoraDropoutStream.verify) passes on this GPU and leaves the
+    training generator's seed and offset as they were."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import LoraDropoutStream
+
+    torch.cuda.manual_seed(77)
+    drop = LoraDropoutStream(torch.device(DEV), dtype)
+    drop.generator.set_offset(40)
+    before = (drop.generator.initial_seed(), drop.generator.get_offset())
+    assert drop.verify(1536, p)
+    assert (drop.generator.initial_seed(), drop.generator.get_offset()) == before
 
 
 # ---------------------------------------------------------------------------------------------

@@ -143,8 +143,8 @@ def _trainer(engine, **kw):
                               _metrics={"train": {"entropy": [], "mean_token_accuracy": [],
                                                   "num_tokens": []}},
                               _total_train_tokens=0, _soup_rewind_state=_Rewind())
-    t._soup_original_compute_loss = original
-    t._soup_kernels_engine = engine
+    setattr(t, patch._ORIGINAL_ATTR, original)
+    setattr(t, patch._INSTALLED_ATTR, engine)
     for k, v in kw.items():
         setattr(t, k, v)
     return t, calls
@@ -164,7 +164,7 @@ def test_fused_compute_loss_bookkeeping():
     assert not calls and engine.calls == [float(n_items)]
     assert loss.item() == pytest.approx(2.0)  # every supervised token costs 2
     assert t._total_train_tokens == 15 and t._metrics["train"]["num_tokens"] == [15]
-    patch._flush_metrics(t)
+    patch.flush_metrics(t)
     assert t._metrics["train"]["entropy"] == [pytest.approx(3.0)]
     sup = n_items
     assert t._metrics["train"]["mean_token_accuracy"][0] == pytest.approx(
@@ -174,7 +174,7 @@ def test_fused_compute_loss_bookkeeping():
     # without loss kwargs the denominator is the supervised count
     t2, _ = _trainer(_FakeEngine(), model_accepts_loss_kwargs=False)
     patch.fused_compute_loss(t2, model, dict(b), num_items_in_batch=99)
-    assert t2._soup_kernels_engine.calls == [float(n_items)]
+    assert getattr(t2, patch._INSTALLED_ATTR).calls == [float(n_items)]
 
 
 def test_fused_compute_loss_scales_under_average_tokens_across_devices():
@@ -272,3 +272,42 @@ def test_gemm_planner_splits_only_long_k_few_tile_products():
     for M, N, K in [(n, 2048, H), (n, H, H), (n, I, H), (n, 2 * I, H), (8900, 18944, 3584)]:
         assert lib.ql_gemm_workspace_bytes(M, N, K) == 0, (M, N, K)
     assert lib.ql_gemm_workspace_bytes(0, H, I) == 0
+
+
+def test_ledger_flushes_accumulated_micro_batches_in_order():
+    """Two micro-batches of one optimizer step (gradient accumulation): both are queued on the
+    device and written by one flush, in order, with their own training step in the rewind rows;
+    a rewind recorder that raises is marked failed and training goes on."""
+    t, _ = _trainer(_FakeEngine())
+    model = _Model().train()
+    first, second = _batch([5, 3, 7]), _batch([4, 6])
+    for b in (first, second):
+        n_items = int((b["labels"][:, 1:] != -100).sum())
+        patch.fused_compute_loss(t, model, dict(b), num_items_in_batch=n_items)
+    assert t._metrics["train"]["entropy"] == [] and t._total_train_tokens == 25
+    patch.flush_metrics(t)
+    assert t._metrics["train"]["entropy"] == [pytest.approx(3.0)] * 2
+    assert [r[0] for r in t._soup_rewind_state.rows] == [5, 5]
+    assert t._soup_rewind_state.rows[1][2] == [2, 4]
+    patch.flush_metrics(t)  # nothing pending: nothing appended
+    assert len(t._metrics["train"]["mean_token_accuracy"]) == 2
+
+    class _Broken(_Rewind):
+        def on_micro_batch(self, step, row_loss, row_tokens):
+            raise RuntimeError("disk full")
+
+    t._soup_rewind_state = _Broken()
+    patch.fused_compute_loss(t, model, dict(first), num_items_in_batch=3)
+    patch.flush_metrics(t)
+    assert t._soup_rewind_state.failed and len(t._metrics["train"]["entropy"]) == 3
+
+
+def test_packed_partition_without_device_reads_matches_a_stable_sort():
+    """The supervised-first order is the stable argsort of 'has no target', for ragged rows, a
+    row without any target and an all-prompt batch."""
+    for lengths, prompt in (([9, 1, 4, 12], 2), ([3, 3], 5), ([1], 0)):
+        b = _batch(lengths, prompt=prompt)
+        p = Packed(b["input_ids"], b["attention_mask"], b["labels"])
+        want = torch.argsort((p.targets < 0).to(torch.int8), stable=True)
+        assert torch.equal(p.head_order, want), lengths
+        assert p.n_supervised == int((p.targets >= 0).sum())
