@@ -17,10 +17,16 @@ events, max over ranks; value = real (unpadded) tokens of all ranks / that time.
 object) from pinned host batches: the host-to-device copy of input_ids / attention_mask / labels
 and the loss read back are inside its timed region.
 
---impl reference times the reference's PyTorch path on the host cores instead (the CPU oracle
-restating solution/engine.py in torch fp32): each step one bounded sample (one decoder layer
-forward + backward and the head over one sequence of the workload's median length),
-extrapolated to the 28-layer model's tokens/s.
+`ops` breaks one step down per operation kind, from the same K steps run again with the library's
+event profiler and programmatic dependent launch off (so the per-operation times add up): time
+per step, algorithmic bytes (HBM-bound kinds) or FLOPs (GEMMs, attention) and the fraction of the
+measured peak. `roofline` is the GEMM class (the largest share of the step).
+
+--impl reference times the reference's PyTorch path on the host cores instead: the CPU oracle
+(a torch fp32 restatement of solution/engine.py with its 16-bit rounding points) on the very
+batches this arm runs (rank 0's), each step one bounded sample - NF4 dequantisation of one decoder
+layer's weights, its forward + backward over the step's whole packed batch, and the head over 256
+of its tokens - extrapolated to the 28-layer model and all of the batch's tokens.
 """
 
 import argparse
@@ -45,6 +51,8 @@ WORKLOAD = ("configs[1]: Qwen2.5-1.5B (28 layers, H 1536, 12/2 heads, D 128, I 8
             "fp16 compute, LoRA r16/alpha32/p0.05 on q,v; 4 seqs/rank, lognormal lengths "
             "(median 300, clip [32,1024]), 30% prompt-masked; AdamW lr 2e-4")
 SEQS, MEDIAN, LO, HI, PROMPT = 4, 300, 32, 1024, 0.3
+CPU_SAMPLE_LAYERS = 1  # decoder layers the CPU baseline times per step (then extrapolated)
+CPU_HEAD_ROWS = 256    # head rows it times per step (the head's cost is linear in its rows)
 
 
 def parse():
@@ -86,7 +94,30 @@ def make_batch(rng, vocab, seqs=SEQS, median=MEDIAN, lo=LO, hi=HI, uniform=None)
     return ids, mask, labels, int(lengths.sum())
 
 
+def batches(args, rank, vocab):
+    """The warm-up + timed batches of a rank (both arms draw the same ones)."""
+    rng = np.random.default_rng(1000 + rank)
+    uniform = tuple(int(x) for x in args.uniform.split(",")) if args.uniform else None
+    return [make_batch(rng, vocab, args.seqs, args.median, args.lo, args.hi, uniform)
+            for _ in range(args.warmup + args.steps)]
+
+
+def workload_config(args, world):
+    """The `config` object of both arms' JSON lines."""
+    default = (args.seqs, args.median, args.lo, args.hi, args.uniform, args.model,
+               args.dtype) == (SEQS, MEDIAN, LO, HI, None, "1.5b", "fp16")
+    name = WORKLOAD if default else (
+        f"Qwen2.5-{args.model.upper()} {args.dtype}, {args.seqs} seqs/rank, lengths "
+        + (f"uniform [{args.uniform}]" if args.uniform else
+           f"lognormal (median {args.median}, clip [{args.lo},{args.hi}])"))
+    return {"workload": name, "global_batch": args.seqs * world, "seq_len": "varlen",
+            "parallelism": f"dp{world}",
+            "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of activations) is "
+                  "larger than the 126 MB L2"}
+
+
 def peaks():
+    """(HBM GB/s, bf16 TF/s burst, bf16 TF/s sustained, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as fh:
@@ -147,44 +178,73 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------------------------
-# CPU: the reference's PyTorch path (oracle), bounded sample
+# CPU: the reference's PyTorch path (oracle), bounded sample of a bench batch
 # ---------------------------------------------------------------------------------------------
-def cpu_sample(model, seq_len=MEDIAN, layer_index=0):
-    """(tokens/s extrapolated to the whole model, seconds, threads, description)."""
-    from oracle import step as oracle_step
-    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B
+class CpuSample:
+    """Times the CPU oracle on one bench batch: NF4 dequantisation of CPU_SAMPLE_LAYERS decoder
+    layers' weights (numpy, inside the timer), their forward + backward over the whole packed
+    batch, and the head (final norm, 151,936-way logits, cross-entropy, its backward) over
+    CPU_HEAD_ROWS of the batch's tokens, on every host thread; extrapolated to the model's 28
+    layers and to all of the batch's head rows."""
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    W = oracle_step.weights_from_model_layers(model, [layer_index], "f16")
-    L = W["layers"][0]
-    g = torch.Generator().manual_seed(7)
-    h = torch.randn(seq_len, W["H"], generator=g)
-    dh3 = torch.randn(seq_len, W["H"], generator=g)
-    pos = torch.arange(seq_len)
-    t0 = time.perf_counter()
-    oracle_step.layer_forward_backward(W, L, h, [seq_len], pos, dh3)
-    t_layer = time.perf_counter() - t0
-    ids = torch.randint(0, W["lm"].shape[0], (seq_len,), generator=g)
-    t0 = time.perf_counter()
-    oracle_step.head_forward_backward(W, h, ids)
-    t_head = time.perf_counter() - t0
-    layers = QWEN25_1P5B.num_hidden_layers
-    total = layers * t_layer + t_head
-    desc = (f"one decoder layer fwd+bwd ({t_layer:.2f} s) + head fwd+bwd ({t_head:.2f} s) over "
-            f"one {seq_len}-token sequence, fp32 torch on the host, extrapolated to "
-            f"{layers} layers")
-    return seq_len / total, t_layer + t_head, torch.get_num_threads(), desc
+    def __init__(self):
+        from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B, build_qwen2_qlora
+
+        self.cfg = QWEN25_1P5B
+        self.model = build_qwen2_qlora(self.cfg, device="cpu", seed=0,
+                                       layers_override=CPU_SAMPLE_LAYERS)
+        causal = self.model.get_base_model()
+        self.embed = causal.model.embed_tokens.weight.detach().float()
+        self.norm = causal.model.norm.weight.detach().float()
+
+    def run(self, batch):
+        """(tokens/s, seconds of the sample, threads, description)."""
+        from oracle import step as oracle_step
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        ids, mask, labels, n = batch
+        lengths = mask.sum(1).tolist()
+        flat = np.flatnonzero(mask.reshape(-1))
+        T = mask.shape[1]
+        pos = torch.from_numpy(flat % T)
+        g = torch.Generator().manual_seed(7)
+        h = torch.randn(n, self.cfg.hidden_size, generator=g)
+        dh3 = torch.randn(n, self.cfg.hidden_size, generator=g)
+        shifted = np.full_like(labels, -100)
+        shifted[:, :-1] = labels[:, 1:]
+        targets = torch.from_numpy(shifted.reshape(-1)[flat])
+        t0 = time.perf_counter()
+        W = oracle_step.weights_from_model_layers(self.model, list(range(CPU_SAMPLE_LAYERS)),
+                                                  "f16", embed=self.embed, norm=self.norm)
+        for L in W["layers"]:
+            oracle_step.layer_forward_backward(W, L, h, lengths, pos, dh3)
+        t_layers = time.perf_counter() - t0
+        rows = min(n, CPU_HEAD_ROWS)
+        t0 = time.perf_counter()
+        oracle_step.head_forward_backward(W, h[:rows], targets[:rows])
+        t_head_sample = time.perf_counter() - t0
+        t_head = t_head_sample * n / rows
+        layers = self.cfg.num_hidden_layers
+        per_layer = t_layers / CPU_SAMPLE_LAYERS
+        total = layers * per_layer + t_head
+        desc = (f"the bench batch itself ({n} tokens, {len(lengths)} sequences): NF4 dequant + "
+                f"fwd+bwd of {CPU_SAMPLE_LAYERS} decoder layer(s) over all tokens "
+                f"({per_layer:.2f} s per layer) and the head fwd+bwd over {rows} rows "
+                f"({t_head_sample:.2f} s), fp32 torch on the host, extrapolated to {layers} "
+                f"layers and {n} head rows")
+        return n / total, t_layers + t_head_sample, torch.get_num_threads(), desc
 
 
-def run_reference(args, rank):
+def run_reference(args, rank, world):
     if rank != 0:
         return
-    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B, build_qwen2_qlora
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B
 
-    model = build_qwen2_qlora(QWEN25_1P5B, device="cpu", seed=0, layers_override=1)
+    sample = CpuSample()
+    host = batches(args, 0, QWEN25_1P5B.vocab_size)
     vals, secs, threads, desc = [], [], 1, ""
     for i in range(args.warmup + args.steps):
-        v, s, threads, desc = cpu_sample(model)
+        v, s, threads, desc = sample.run(host[i])
         if i >= args.warmup:
             vals.append(v)
             secs.append(s)
@@ -193,8 +253,8 @@ def run_reference(args, rank):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": statistics.median(secs) * 1000, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 rounding points)",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": SEQS,
-                                             "seq_len": "varlen", "parallelism": "cpu"},
+            "data": "synthetic (seeded lognormal lengths, uniform token ids, random-init weights)",
+            "config": workload_config(args, world),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
                              "kind": "port", "sample": desc},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -205,20 +265,50 @@ def run_reference(args, rank):
 # ---------------------------------------------------------------------------------------------
 # GPU
 # ---------------------------------------------------------------------------------------------
+def attention_flops(lengths_per_step, cfg):
+    """Algorithmic attention FLOPs per step (forward, backward) over the steps' sequences:
+    4 l (l + 1) / 2 HQ D per causal sequence and layer forward, 2.5x that backward."""
+    fwd = np.mean([sum(4.0 * L * (L + 1) / 2 for L in lengths) for lengths in lengths_per_step])
+    fwd *= cfg.num_attention_heads * cfg.head_dim * cfg.num_hidden_layers
+    return fwd, 2.5 * fwd
+
+
+def op_table(prof, steps, attn, hbm, tf_peak):
+    """Per operation kind: ms per step, algorithmic work and the fraction of the peak that bounds
+    it (HBM GB/s for the memory-bound kinds, tensor TF/s for GEMMs and attention)."""
+    out = {}
+    for kind, rec in prof.items():
+        ms = rec["ms"] / steps
+        row = {"ms_per_step": round(ms, 4), "launches_per_step": rec["count"] / steps}
+        flops = rec["flops"] / steps
+        if kind == "attn_fwd":
+            flops = attn[0]
+        elif kind == "attn_bwd":
+            flops = attn[1]
+        if kind in ("gemm", "attn_fwd", "attn_bwd") and flops and ms:
+            tf = flops / (ms / 1e3) / 1e12
+            row.update(tflop_per_step=flops / 1e12, achieved_tflops=round(tf, 1),
+                       frac_of_bf16_peak=round(tf / tf_peak, 3))
+        elif rec["bytes"] and ms:
+            gbs = rec["bytes"] / steps / (ms / 1e3) / 1e9
+            row.update(gb_per_step=rec["bytes"] / steps / 1e9, achieved_gbs=round(gbs, 1),
+                       frac_of_hbm=round(gbs / hbm, 3))
+        out[kind] = row
+    return out
+
+
 def run_ours(args, rank, world, local):
     import torch.distributed as dist
 
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops, patch
-    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
-    from hack_fe30cb28_opus_5_5_ultracode_b200.model import (QWEN25_1P5B, build_qwen2_qlora,
-                                                             lora_parameters)
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2, HostBatch
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import (QWEN25_1P5B, QWEN25_7B,
+                                                             build_qwen2_qlora, lora_parameters)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
         dist.barrier(device_ids=[local])
-    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_7B
-
     cfg = QWEN25_1P5B if args.model == "1.5b" else QWEN25_7B
     cdt = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     model = build_qwen2_qlora(cfg, dropout=0.05, device=dev, seed=0, embed_dtype=cdt)
@@ -229,16 +319,11 @@ def run_ours(args, rank, world, local):
         engine.set_data_parallel(None)
     params = lora_parameters(model)
     opt = torch.optim.AdamW(params, lr=2e-4, fused=True)
-    rng = np.random.default_rng(1000 + rank)
-    uniform = tuple(int(x) for x in args.uniform.split(",")) if args.uniform else None
-    host = [make_batch(rng, cfg.vocab_size, args.seqs, args.median, args.lo, args.hi, uniform)
-            for _ in range(args.warmup + args.steps)]
+    host = batches(args, rank, cfg.vocab_size)
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
-
-    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import HostBatch
-
     hosts = [HostBatch.of(torch.from_numpy(b[1]), torch.from_numpy(b[2])) for b in host]
+    timed = range(args.warmup, args.warmup + args.steps)
 
     def train_step(i):
         ids, mask, labels, _ = dev_batches[i]
@@ -253,19 +338,24 @@ def run_ours(args, rank, world, local):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
-    def max_over_ranks(x):
+    def over_ranks(x, op):
+        """x combined over the ranks with `op` ("max" or "sum")."""
         if world == 1:
             return x
         t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
         return float(t.item())
 
-    def sum_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t)
-        return float(t.item())
+    def timed_steps(step_fn):
+        """Device milliseconds of the K timed steps (max over ranks)."""
+        barrier_sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in timed:
+            step_fn(i)
+        e1.record()
+        barrier_sync()
+        return over_ranks(e0.elapsed_time(e1), "max")
 
     # The model, the libraries and the batches are set up: move every object made so far out of
     # the cyclic collector's scans, so the steps' short-lived objects do not trigger full scans of
@@ -280,49 +370,35 @@ def run_ours(args, rank, world, local):
     clocks.start()
     time.sleep(0.3)
     launches0 = ops.launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("bench_timed")  # (lets ncu --nvtx-include capture these steps)
-    e0.record()
-    for i in range(args.warmup, args.warmup + args.steps):
-        train_step(i)
-    e1.record()
+    ms = timed_steps(train_step)
     torch.cuda.nvtx.range_pop()
-    barrier_sync()
     launches = ops.launch_count() - launches0
     clk = clocks.stop()
-    # Per-operation breakdown and the GEMM roofline: the same K steps again with the library's
-    # CUDA-event profiler on (kept out of the timed region: its event pairs cost host time).
-    ops.profile_start()
-    for i in range(args.warmup, args.warmup + args.steps):
-        train_step(i)
-    barrier_sync()
-    ops.profile_stop()
-    prof = ops.profile_read()
-    ms = max_over_ranks(e0.elapsed_time(e1))
     peak_mib = torch.cuda.max_memory_allocated(dev) / 2**20  # of the timed plan
-    tokens = sum_over_ranks(sum(b[3] for b in host[args.warmup:]))
+    tokens = over_ranks(sum(b[3] for b in host[args.warmup:]), "sum")
+    # Per-operation breakdown: the same K steps again with the library's event profiler on and
+    # programmatic dependent launch off (outside the timed region: event pairs cost host time,
+    # and with launches overlapping, per-operation intervals would overlap too).
+    ops.set_pdl(False)
+    ops.profile_start()
+    profiled_ms = timed_steps(train_step)
+    ops.profile_stop()
+    ops.set_pdl(True)
+    prof = ops.profile_read()
     mem_line = {"plan": engine.last_plan.summary() if engine.last_plan else None}
     if args.spill is not None:
         # the same steps with every layer kept: the cost of the spill (exposed copy or
         # recompute time) and the host-link traffic it moves
         spill_bytes = engine.last_offload_bytes  # of the last timed step
         keep_layers, engine.keep_layers, engine.spill = engine.keep_layers, None, "recompute"
-        barrier_sync()
-        e0.record()
-        for i in range(args.warmup, args.warmup + args.steps):
-            train_step(i)
-        e1.record()
-        barrier_sync()
-        keep_ms = max_over_ranks(e0.elapsed_time(e1))
+        keep_ms = timed_steps(train_step)
         engine.keep_layers, engine.spill = keep_layers, args.spill
         mem_line.update(offload_bytes_per_step=spill_bytes,
                         keep_all_ms_per_step=keep_ms / args.steps,
                         spill_ms_per_step=ms / args.steps,
                         exposed_fraction=max(0.0, (ms - keep_ms) / ms))
     value = tokens / (ms / 1000.0)
-    gemm_ms = prof.get("gemm", {}).get("ms", 0.0)
-    gemm_flops = prof.get("gemm", {}).get("flops", 0.0)
-    kernel_ms = {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()}
 
     # e2e: the drop-in boundary from pinned host batches
     import types
@@ -351,67 +427,60 @@ def run_ours(args, rank, world, local):
 
     for i in range(min(2, args.warmup)):
         e2e_step(i)
-    barrier_sync()
-    h2d_total = 0
-    e0.record()
-    for i in range(args.warmup, args.warmup + args.steps):
-        e2e_step(i)
-        h2d_total += sum(a.numel() * a.element_size() for a in pinned[i])
-    e1.record()
-    barrier_sync()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_ms = timed_steps(e2e_step)
     e2e_value = tokens / (e2e_ms / 1000.0)
+    h2d = sum(a.numel() * a.element_size() for i in timed for a in pinned[i]) / args.steps
 
     if rank != 0:
         return
     hbm, tf_burst, tf_sust, src = peaks()
-    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as fh:
-            traffic = json.load(fh).get("bytes_per_launch")
+    # The burst peak applies when the timed steps ran at the maximum SM clock (short steps, no
+    # power cap); the sustained one (measured under the power cap) otherwise.
+    at_max = clk is not None and clk["sm_max_mhz"] and clk["sm_mhz"] >= 0.95 * clk["sm_max_mhz"] \
+        and "sw_power_cap" not in clk["reasons"]
+    tf_peak = tf_burst if at_max else tf_sust
+    attn = attention_flops([np.asarray(b[1]).sum(1).tolist() for b in host[args.warmup:]], cfg)
+    table = op_table(prof, args.steps, attn, hbm, tf_peak)
+    gemm = table.get("gemm", {})
+    achieved = gemm.get("achieved_tflops")
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic (seeded lognormal lengths, uniform token ids, random-init weights)",
-        "config": {"workload": WORKLOAD if (args.seqs, args.median, args.lo, args.hi,
-                                            args.uniform, args.model, args.dtype) ==
-                   (SEQS, MEDIAN, LO, HI, None, "1.5b", "fp16") else
-                   f"Qwen2.5-{args.model.upper()} {args.dtype}, {args.seqs} seqs/rank, lengths "
-                   + (f"uniform [{args.uniform}]" if args.uniform else
-                      f"lognormal (median {args.median}, clip [{args.lo},{args.hi}])"),
-                   "global_batch": args.seqs * world, "seq_len": "varlen",
-                   "parallelism": f"dp{world}",
-                   "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of "
-                         "activations) is larger than the 126 MB L2",
-                   "tokens_per_step_per_rank": tokens / world / args.steps},
+        "config": workload_config(args, world),
+        "tokens_per_step": tokens / args.steps,
         "peak_hbm_mib": peak_mib, "memory": mem_line,
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d_total / args.steps,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
-        "roofline": {"kernel": "gemm_tn_kernel (tcgen05, all GEMM launches of the timed steps)",
-                     "bound": "tensor", "achieved": achieved, "peak": tf_sust,
-                     "unit": "TFLOP/s", "frac": (achieved / tf_sust) if achieved else None,
-                     "peak_source": f"{src} bf16 dense, sustained (kernel inside a long step)",
-                     "traffic": traffic, "gemm_ms_per_step": gemm_ms / args.steps,
+        "roofline": {"kernel": "gemm_tn_kernel + gemm_pair_kernel (tcgen05; every GEMM launch "
+                               "of the profiled steps)",
+                     "bound": "tensor", "achieved": achieved, "peak": tf_peak,
+                     "unit": "TFLOP/s", "frac": (achieved / tf_peak) if achieved else None,
+                     "peak_source": f"{src} bf16 dense, "
+                                    + ("burst (steps ran at the max SM clock)" if at_max else
+                                       "sustained (clocks below max or power-capped)"),
+                     "frac_of_burst": (achieved / tf_burst) if achieved else None,
+                     "frac_of_sustained": (achieved / tf_sust) if achieved else None,
+                     "traffic": None,
+                     "traffic_note": "not captured in this run; the ncu DRAM bytes of the "
+                                     "GEMMs are in profiles/",
+                     "gemm_ms_per_step": gemm.get("ms_per_step"),
                      "launches": int(prof.get("gemm", {}).get("count", 0))},
-        "op_ms_per_step": kernel_ms,
+        "ops": table,
+        "ops_note": (f"profiled pass without programmatic dependent launch: "
+                     f"{profiled_ms / args.steps:.3f} ms per step, per-op sum "
+                     f"{sum(r['ms_per_step'] for r in table.values()):.3f} ms"),
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:
-        v, secs, threads, desc = cpu_sample_from_gpu_model()
+        cpu = CpuSample()
+        cpu.run(host[0])  # warm-up: the first call pays for thread pools and allocations
+        v, secs, threads, desc = cpu.run(host[args.warmup])
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads,
                                 "kind": "port", "sample": desc}
     print(json.dumps(line), flush=True)
-
-
-def cpu_sample_from_gpu_model():
-    from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B, build_qwen2_qlora
-
-    model = build_qwen2_qlora(QWEN25_1P5B, device="cpu", seed=0, layers_override=1)
-    return cpu_sample(model)
 
 
 def main():
@@ -420,7 +489,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if world > 1:
         import datetime

@@ -52,6 +52,10 @@ void smem_optin(const void* kernel, int bytes) {
     have = bytes;
 }
 
+static std::atomic<bool> g_pdl{true};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+void set_pdl(bool on) { g_pdl.store(on, std::memory_order_relaxed); }
+
 int* status_word() {
   // one address per device; cudaGetSymbolAddress is cheap after the first call per device
   static int* cache[64] = {nullptr};
@@ -127,6 +131,12 @@ int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, 
   return done(ql::gemm_nf4(A, lda, *W, layout, C, ldc, bias, M, in_dtype, out_dtype, accumulate,
                            residual, ql::status_word(), stream),
               "ql_gemm_nf4");
+}
+
+int ql_set_pdl(int on) {
+  if (on != 0 && on != 1) return done(QL_STATUS_BAD_ARG, "ql_set_pdl");
+  ql::set_pdl(on != 0);
+  return QL_STATUS_OK;
 }
 
 int ql_gemm_set_mode(int mode) {

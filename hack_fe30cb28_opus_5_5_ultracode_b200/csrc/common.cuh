@@ -27,6 +27,8 @@ __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 
 int launched(int kernels);
 // Host: raises a kernel's dynamic shared-memory limit to `bytes` the first time it is needed.
 void smem_optin(const void* kernel, int bytes);
+// Host: whether launches carry the programmatic-dependent-launch attribute (ql_set_pdl).
+bool pdl_enabled();
 
 // ---------------------------------------------------------------------------------------------
 // element conversion
@@ -502,7 +504,7 @@ inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 

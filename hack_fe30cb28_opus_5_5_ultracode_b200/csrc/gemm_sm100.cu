@@ -526,7 +526,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a) != cudaSuccess) return QL_STATUS_CUDA;
   return launched(1);
 }

@@ -687,6 +687,44 @@ class FusedQwen2:
         stats.order, stats.tok_loss, stats.entropy, stats.correct = order, tok_loss, entropy, correct
         return dhp, tok_loss.sum() * inv
 
+    def run_layer(self, index, packed, drop, h, dh3):
+        """One decoder layer forward and backward through the layer ABI (ql_layer_forward,
+        ql_layer_backward), outside a training step: the layer-level parity tests and
+        microbenchmarks. packed: the batch's Packed; drop: its ops.Drop for this layer; h, dh3:
+        the layer's input and upstream gradient, [n, H] fp32 on the device. Returns (h3, dh,
+        [dAq, dBq, dAv, dBv]); the generator and the step's state are not touched."""
+        spec, desc = self.layers[index], self.descs[index]
+        n, H = h.shape
+        with torch.no_grad():
+            torch._foreach_copy_(self.lora_views, self.lora_fp32)
+        cos, sin = self.rope.table(max(packed.max_len, 1))
+        self._set_step(desc, packed, drop, cos, sin)
+        arena = _SavedArena(n, spec, 1, self.dtype, self.device)
+        arena.h(0).copy_(h)
+        sv = arena.saved(0)
+        if self.w16 is not None:
+            self._dequant_all()
+            sv.w16 = self.w16[index * self.weight_elems:].data_ptr()
+            sv.w16_ready = 1
+        ws = self._workspace_for(desc)
+        _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
+                  arena.h(1).data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
+        h3 = arena.h(1).clone()
+        grads = torch.zeros(self.offsets[4 * index + 4] - self.offsets[4 * index],
+                            device=self.device, dtype=torch.float32)
+        dh3 = dh3.contiguous().float()
+        dh3_16 = dh3.to(self.dtype)
+        dh = torch.empty_like(dh3)
+        dh16 = torch.empty((n, H), device=self.device, dtype=self.dtype)
+        _lib.call("ql_layer_backward", ctypes.addressof(desc), ctypes.addressof(sv),
+                  dh3.data_ptr(), dh3_16.data_ptr(), grads.data_ptr(),
+                  dh.data_ptr(), dh16.data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
+        views, at = [], 0
+        for t in self.lora_fp32[4 * index:4 * index + 4]:
+            views.append(grads[at:at + t.numel()].view(t.shape))
+            at += t.numel()
+        return h3, dh, views
+
     # -----------------------------------------------------------------------------------------
     # backward
     # -----------------------------------------------------------------------------------------

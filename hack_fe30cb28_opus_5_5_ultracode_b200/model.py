@@ -253,6 +253,32 @@ def build_qwen2_qlora(config=QWEN25_1P5B, r=16, alpha=32, dropout=0.05, device="
     return model
 
 
+def move_to(model, device):
+    """Moves a stand-in model built by build_qwen2_qlora (on the CPU, say, where every machine
+    draws the same random numbers) to `device`: the NF4 bytes and quantisation state, biases,
+    norms, embeddings, rotary frequencies and the LoRA weights (kept as the same Parameters, so
+    their identity and requires_grad survive)."""
+    causal = model.get_base_model()
+    inner = causal.model
+    with torch.no_grad():
+        for p in model.parameters():
+            p.data = p.data.to(device)
+        for layer in inner.layers:
+            for mod in (layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj,
+                        layer.self_attn.o_proj, layer.mlp.gate_proj, layer.mlp.up_proj,
+                        layer.mlp.down_proj):
+                base = getattr(mod, "base_layer", mod)
+                w, qs = base.weight, base.weight.quant_state
+                w.data = w.data.to(device)
+                qs.absmax, qs.code = qs.absmax.to(device), qs.code.to(device)
+                if qs.nested:
+                    qs.state2.code = qs.state2.code.to(device)
+                    qs.state2.absmax = qs.state2.absmax.to(device)
+                    qs.offset = qs.offset.to(device)
+        inner.rotary_emb.inv_freq = inner.rotary_emb.inv_freq.to(device)
+    return model
+
+
 def lora_parameters(model):
     """The trainable LoRA weights in the order the fused step returns their gradients."""
     return [p for p in model.parameters() if p.requires_grad]

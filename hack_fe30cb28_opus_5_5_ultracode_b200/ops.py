@@ -160,6 +160,12 @@ def profile_read():
             for i, k in enumerate(PROFILE_KINDS) if arrs[0][i]}
 
 
+def set_pdl(on):
+    """Programmatic dependent launch on (default) or off for this library's launches
+    (ql_set_pdl)."""
+    call("ql_set_pdl", 1 if on else 0)
+
+
 def launch_count():
     """Kernels launched through the library so far (its own counter)."""
     return int(_lib.lib().ql_launch_count())

@@ -49,6 +49,11 @@ long long ql_launch_count(void);
 int ql_profile_start(int capacity);
 int ql_profile_stop(void);
 int ql_profile_read(double* count, double* ms, double* flops, double* bytes);
+/* Whether this library's launches carry the programmatic-dependent-launch attribute (1, the
+ * default: each kernel's CTAs are scheduled while the previous kernel drains and wait for its
+ * results in their first instruction) or not (0: plain stream order). A measurement switch with
+ * no counterpart in the reference: per-operation event timings add up only with it off. */
+int ql_set_pdl(int on);
 
 /* ---- NF4 dequantisation ------------------------------------------------------------------
  * Replaces NF4Weight.dequant_into / NF4Group.dequant_into (solution/engine.py:103-109,

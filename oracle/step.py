@@ -55,8 +55,10 @@ def weights_from_model(model, dtype="f16"):
     return weights_from_model_layers(model, None, dtype)
 
 
-def weights_from_model_layers(model, which, dtype="f16"):
-    """weights_from_model restricted to the decoder layers listed in `which` (None: all)."""
+def weights_from_model_layers(model, which, dtype="f16", embed=None, norm=None):
+    """weights_from_model restricted to the decoder layers listed in `which` (None: all).
+    embed / norm: fp32 CPU copies of the (tied) embedding and the final norm weight already at
+    hand, used instead of copying them again."""
     causal = model.get_base_model()
     inner = causal.model
     cfg = causal.config
@@ -84,11 +86,16 @@ def weights_from_model_layers(model, which, dtype="f16"):
             d["p"] = float(mod.lora_dropout[name].p)
         d["eps"] = float(layer.input_layernorm.variance_epsilon)
         layers.append(d)
+    if embed is None:
+        embed = inner.embed_tokens.weight.detach().to(tdt).float().cpu()
+        lm = causal.lm_head.weight.detach().to(tdt).float().cpu()
+    else:
+        lm = embed
     return {
         "layers": layers,
-        "embed": inner.embed_tokens.weight.detach().to(tdt).float().cpu(),
-        "lm": causal.lm_head.weight.detach().to(tdt).float().cpu(),
-        "norm": inner.norm.weight.detach().float().cpu(),
+        "embed": embed,
+        "lm": lm,
+        "norm": norm if norm is not None else inner.norm.weight.detach().float().cpu(),
         "eps": float(inner.norm.variance_epsilon),
         "H": cfg.hidden_size, "HQ": cfg.num_attention_heads, "HKV": cfg.num_key_value_heads,
         "D": cfg.head_dim, "I": cfg.intermediate_size, "theta": cfg.rope_theta,
@@ -135,6 +142,66 @@ class DropState:
         self.seed, self.offset, self.max_blocks, self.vec = seed, offset, max_blocks, vec
 
 
+def decoder_layer(W, L, h, lora, masks, lengths, cos, sin):
+    """One decoder layer forward (solution/engine.py:1054-1181): residual h [n, H] fp32 -> h3,
+    with the LoRA weights `lora` = [Aq, Bq, Av, Bv] (fp32 tensors, may require grad) and the
+    q / v dropout keep masks [n, H] (bool). The 16-bit roundings sit where the reference's
+    kernels and fp16 GEMMs put them; differentiable end to end."""
+    r = _rounder(W["dtype"])
+    H, HQ, HKV, D = W["H"], W["HQ"], W["HKV"], W["D"]
+    n = h.shape[0]
+    Aq, Bq, Av, Bv = lora
+    p, s = L["p"], L["s"]
+    keep = 1.0 / (1.0 - p) if p > 0 else 1.0
+    rstd = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + L["eps"])
+    y = L["ln1"] * (h * rstd)
+    a = r(y)
+    aq = r(torch.where(masks[0], y * keep, torch.zeros_like(y)))
+    av = r(torch.where(masks[1], y * keep, torch.zeros_like(y)))
+    Wqkv = torch.cat([L["Wq"], L["Wk"], L["Wv"]])
+    qkv = r(a @ Wqkv.t() + L["bias"])
+    lq = r(r(aq @ r(Aq).t()) @ r(Bq).t())
+    lv = r(r(av @ r(Av).t()) @ r(Bv).t())
+    q = qkv[:, :HQ * D] + s * lq
+    k = qkv[:, HQ * D:(HQ + HKV) * D]
+    v = qkv[:, (HQ + HKV) * D:] + s * lv
+    q = r(rope(q.view(n, HQ, D), cos, sin))
+    k = r(rope(k.view(n, HKV, D), cos, sin))
+    v = r(v.view(n, HKV, D))
+    out = r(causal_attention(q, k, v, lengths, D ** -0.5))
+    o = r(out.reshape(n, HQ * D) @ L["Wo"].t())
+    h2 = h + o
+    rstd2 = torch.rsqrt(h2.pow(2).mean(-1, keepdim=True) + L["eps"])
+    b = r(L["ln2"] * (h2 * rstd2))
+    g = r(b @ L["Wgate"].t())
+    u = r(b @ L["Wup"].t())
+    m = r(torch.nn.functional.silu(g) * u)
+    d = r(m @ L["Wdown"].t())
+    return h2 + d
+
+
+def layer_with_dropout(W, L, h, dh3, lengths, T, drop):
+    """One decoder layer forward and backward on a right-padded batch of `lengths` (padded width
+    T) with LoRA dropout: drop = (seed, counter of the q call, counter of the v call, threads,
+    vec). Returns (h3, dh, [dAq, dBq, dAv, dBv]) — what the reference's _Layer computes
+    (solution/engine.py:1184-1340) for upstream gradient dh3."""
+    H = W["H"]
+    n = h.shape[0]
+    pos = torch.cat([torch.arange(x) for x in lengths])
+    rows = torch.repeat_interleave(torch.arange(len(lengths)), torch.tensor(lengths))
+    tok = rows * T + pos
+    cos, sin = rope_tables(pos, W["D"], W["theta"])
+    elems = (tok[:, None] * H + torch.arange(H)[None, :]).numpy()
+    seed, ctr_q, ctr_v, threads, vec = drop
+    masks = [torch.from_numpy(dropout_keep(elems, seed, c, threads, L["p"], vec)).view(n, H)
+             for c in (ctr_q, ctr_v)]
+    h = h.clone().requires_grad_()
+    lora = [L[k].clone().requires_grad_() for k in ("Aq", "Bq", "Av", "Bv")]
+    h3 = decoder_layer(W, L, h, lora, masks, lengths, cos, sin)
+    grads = torch.autograd.grad(h3, [h] + lora, dh3)
+    return h3.detach(), grads[0], list(grads[1:])
+
+
 def step(W, input_ids, attention_mask, labels, denom, drop_state=None, lora_params=None):
     """One forward + backward. Returns dict(loss, tok_loss, entropy, correct, grads=[dAq, dBq,
     dAv, dBv per layer], offset=the generator offset after the step). Rows in packed order."""
@@ -157,47 +224,18 @@ def step(W, input_ids, attention_mask, labels, denom, drop_state=None, lora_para
     h = W["embed"][ids.reshape(-1)[flat]]
     offset = drop_state.offset if drop_state is not None else 0
     for L in W["layers"]:
-        Aq = L["Aq"].clone().requires_grad_()
-        Bq = L["Bq"].clone().requires_grad_()
-        Av = L["Av"].clone().requires_grad_()
-        Bv = L["Bv"].clone().requires_grad_()
-        params += [Aq, Bq, Av, Bv]
-        p, s = L["p"], L["s"]
+        lora = [L[k].clone().requires_grad_() for k in ("Aq", "Bq", "Av", "Bv")]
+        params += lora
         masks = []
         for _ in range(2):
-            if drop_state is not None and p > 0:
+            if drop_state is not None and L["p"] > 0:
                 seed, ctr, thr, offset = draw(B * T * H, offset, drop_state.seed,
                                               drop_state.max_blocks, drop_state.vec)
-                masks.append(torch.from_numpy(dropout_keep(elems, seed, ctr, thr, p,
+                masks.append(torch.from_numpy(dropout_keep(elems, seed, ctr, thr, L["p"],
                                                            drop_state.vec)))
             else:
                 masks.append(torch.ones(n, H, dtype=torch.bool))
-        keep = 1.0 / (1.0 - p) if p > 0 else 1.0
-        rstd = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + L["eps"])
-        y = L["ln1"] * (h * rstd)
-        a = r(y)
-        aq = r(torch.where(masks[0], y * keep, torch.zeros_like(y)))
-        av = r(torch.where(masks[1], y * keep, torch.zeros_like(y)))
-        Wqkv = torch.cat([L["Wq"], L["Wk"], L["Wv"]])
-        qkv = r(a @ Wqkv.t() + L["bias"])
-        lq = r(r(aq @ r(Aq).t()) @ r(Bq).t())
-        lv = r(r(av @ r(Av).t()) @ r(Bv).t())
-        q = qkv[:, :HQ * D] + s * lq
-        k = qkv[:, HQ * D:(HQ + HKV) * D]
-        v = qkv[:, (HQ + HKV) * D:] + s * lv
-        q = r(rope(q.view(n, HQ, D), cos, sin))
-        k = r(rope(k.view(n, HKV, D), cos, sin))
-        v = r(v.view(n, HKV, D))
-        out = r(causal_attention(q, k, v, lengths, D ** -0.5))
-        o = r(out.reshape(n, HQ * D) @ L["Wo"].t())
-        h2 = h + o
-        rstd2 = torch.rsqrt(h2.pow(2).mean(-1, keepdim=True) + L["eps"])
-        b = r(L["ln2"] * (h2 * rstd2))
-        g = r(b @ L["Wgate"].t())
-        u = r(b @ L["Wup"].t())
-        m = r(torch.nn.functional.silu(g) * u)
-        d = r(m @ L["Wdown"].t())
-        h = h2 + d
+        h = decoder_layer(W, L, h, lora, masks, lengths, cos, sin)
     rstd = torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + W["eps"])
     hn = r(W["norm"] * (h * rstd))
     logits = r(hn @ W["lm"].t())

@@ -1,8 +1,16 @@
 """The whole fused step (embedding, every layer, head; forward + backward) against the CPU oracle
-of the reference's step, on small random QLoRA Qwen2 models — the reference's own whole-step
-criteria (solution/test_kernels.py:314-400): loss and entropy rel < 2e-3, LoRA gradients rel-L2
-< 2e-2, and the CUDA generator left where PEFT's forward leaves it."""
+of the reference's step: small random QLoRA Qwen2 models, layers at the 1.5B and 7B widths, and
+the benchmarked configs[1] model itself (28 layers, tied V = 151,936, the bench's seeded batch).
 
+Tolerances, fp16: |loss - oracle| <= 1e-3 absolute, every LoRA gradient
+within rel-L2 1e-2, the CUDA generator left where PEFT's forward leaves it. bf16 (no reference
+step exists in bf16; the oracle rounds to bf16 at the same points): |loss - oracle| <= 5e-3,
+LoRA gradients within rel-L2 3e-2 (bf16 keeps 8 significant bits against fp16's 11)."""
+
+import json
+import os
+
+import numpy as np
 import pytest
 import torch
 
@@ -10,6 +18,25 @@ from oracle import step as oracle_step
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
+LOSS_ABS = {torch.float16: 1e-3, torch.bfloat16: 5e-3}
+GRAD_REL = {torch.float16: 1e-2, torch.bfloat16: 3e-2}
+
+
+def _record(name, **values):
+    """Appends a test's measured errors to gpurun_out/parity_errors.jsonl (when that folder
+    exists), so the margins below the bounds are on record."""
+    out = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "gpurun_out")
+    if os.path.isdir(out):
+        with open(os.path.join(out, "parity_errors.jsonl"), "a") as fh:
+            fh.write(json.dumps({"test": name, **values}) + "\n")
+
+
+def _check_step(name, loss, grads, ref, dtype):
+    dloss = abs(loss.item() - ref["loss"].item())
+    rels = [_rel(g, r_) for g, r_ in zip(grads, ref["grads"])]
+    _record(name, dloss=dloss, worst_grad_rel=max(rels), loss=loss.item())
+    assert dloss <= LOSS_ABS[dtype], dloss
+    assert max(rels) <= GRAD_REL[dtype], (int(np.argmax(rels)), max(rels))
 
 
 def _batch(lengths, vocab, seed=1, prompt=3):
@@ -63,14 +90,13 @@ def test_fused_step_matches_oracle(lengths, dropout, nested):
     from hack_fe30cb28_opus_5_5_ultracode_b200.model import TINY
 
     engine, loss, packed, stats, grads, ref, gen = _run(TINY, lengths, dropout, nested)
-    assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 2e-3
+    _check_step(f"tiny {lengths} p={dropout} nested={nested}", loss, grads, ref, torch.float16)
     order = stats.order.cpu()
     ent = stats.entropy.cpu()
     ref_ent = ref["entropy"][order]
-    assert abs(ent.sum().item() - ref_ent.sum().item()) / ref_ent.sum().item() < 2e-3
-    assert _rel(stats.tok_loss.cpu(), ref["tok_loss"][order]) < 2e-3
-    for g, r_ in zip(grads, ref["grads"]):
-        assert _rel(g, r_) < 2e-2
+    assert abs(ent.sum().item() - ref_ent.sum().item()) / ref_ent.sum().item() < 1e-3
+    assert _rel(stats.tok_loss.cpu(), ref["tok_loss"][order]) < 1e-3
+    assert torch.equal(stats.correct.cpu(), ref["correct"][order])
     if dropout > 0:
         assert gen.get_offset() == ref["offset"]
 
@@ -82,9 +108,7 @@ def test_fused_step_full_width_layer_bf16():
     cfg = Qwen2Config(vocab_size=2048, num_hidden_layers=1)
     engine, loss, packed, stats, grads, ref, gen = _run(cfg, [150, 64, 256, 97], 0.05, False,
                                                         dtype=torch.bfloat16)
-    assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 1e-2
-    for g, r_ in zip(grads, ref["grads"]):
-        assert _rel(g, r_) < 5e-2
+    _check_step("1.5b-width layer bf16", loss, grads, ref, torch.bfloat16)
 
 
 @pytest.mark.parametrize("keep_weights", [True, False])
@@ -96,9 +120,8 @@ def test_fused_step_full_width_two_layers_fp16(keep_weights):
     cfg = Qwen2Config(vocab_size=4096, num_hidden_layers=2)
     engine, loss, packed, stats, grads, ref, gen = _run(cfg, [150, 64, 256, 97], 0.05, True,
                                                         keep_weights=keep_weights)
-    assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 2e-3
-    for g, r_ in zip(grads, ref["grads"]):
-        assert _rel(g, r_) < 2e-2
+    _check_step(f"1.5b-width 2 layers fp16 keep_weights={keep_weights}", loss, grads, ref,
+                torch.float16)
     assert gen.get_offset() == ref["offset"]
 
 
@@ -112,9 +135,43 @@ def test_fused_step_qwen25_7b_width_layer_bf16():
                       head_dim=128)
     engine, loss, packed, stats, grads, ref, gen = _run(cfg, [300, 120, 513], 0.05, False,
                                                         dtype=torch.bfloat16)
-    assert abs(loss.item() - ref["loss"].item()) / ref["loss"].item() < 1e-2
-    for g, r_ in zip(grads, ref["grads"]):
-        assert _rel(g, r_) < 5e-2
+    _check_step("7b-width layer bf16", loss, grads, ref, torch.bfloat16)
+
+
+def test_configs1_model_matches_oracle():
+    """The benchmarked model itself: Qwen2.5-1.5B (28 layers, tied V = 151,936), NF4 on all
+    seven projections, LoRA r16 / alpha 32 / dropout 0.05, fp16, on the first batch bench.py
+    times (4 sequences, lognormal lengths, 30 % prompt-masked), against the CPU oracle."""
+    import bench
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import (QWEN25_1P5B, build_qwen2_qlora,
+                                                             lora_parameters)
+
+    cfg = QWEN25_1P5B
+    model = build_qwen2_qlora(cfg, dropout=0.05, device=DEV, seed=0, embed_dtype=torch.float16)
+    ids, mask, labels, _ = bench.make_batch(np.random.default_rng(1000), cfg.vocab_size)
+    ids, mask, labels = (torch.from_numpy(a) for a in (ids, mask, labels))
+    n_items = float((labels[:, 1:] != -100).sum())
+    W = oracle_step.weights_from_model(model, "f16")
+    engine = FusedQwen2(model, dtype=torch.float16)
+    params = lora_parameters(model)
+    gen = torch.cuda.default_generators[torch.cuda.current_device()]
+    torch.cuda.manual_seed(2024)
+    seed0, off0 = gen.initial_seed(), gen.get_offset()
+    loss, packed, stats = engine.step(ids.to(DEV), mask.to(DEV), labels.to(DEV), n_items)
+    grads = torch.autograd.grad(loss, params)
+    torch.cuda.synchronize()
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    assert ops.device_status() == 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref = oracle_step.step(W, ids, mask, labels, n_items,
+                           oracle_step.DropState(seed0, off0, engine.dropout.max_blocks,
+                                                 engine.drop_vec))
+    _check_step("configs[1] 28 layers V=151936 fp16", loss, grads, ref, torch.float16)
+    assert gen.get_offset() == ref["offset"]
+    order = stats.order.cpu()
+    assert _rel(stats.entropy.cpu(), ref["entropy"][order]) < 1e-3
 
 
 def test_two_steps_are_deterministic():
