@@ -8,7 +8,9 @@ Workload (per rank): full Qwen2.5-1.5B architecture, random
 (N(0, 0.02), every projection NF4-quantised, tied fp16 embedding / lm_head, V = 151936), LoRA
 r16 / alpha 32 / dropout 0.05 on q_proj and v_proj; 4 sequences per step with lognormal lengths
 (median 300, clipped to [32, 1024]), token ids uniform in [0, V), labels -100 on the first 30% of
-each sequence; one step = fused forward + backward + AdamW (lr 2e-4) on the LoRA weights.
+each sequence; one step = fused forward + backward + AdamW (lr 2e-4) on the LoRA weights, with
+fp16's GradScaler (loss scaled before the backward, gradients unscaled before AdamW) as HF
+Trainer runs fp16.
 Synthetic data stands in for Soup's Kazakh alpaca set (absent here); each rank draws its own
 seeded batches. Timed: exactly K steps between a barrier + synchronize on both sides, CUDA
 events, max over ranks; value = real (unpadded) tokens of all ranks / that time.
@@ -319,6 +321,9 @@ def run_ours(args, rank, world, local):
         engine.set_data_parallel(None)
     params = lora_parameters(model)
     opt = torch.optim.AdamW(params, lr=2e-4, fused=True)
+    # fp16 mixed precision as HF Trainer runs it: a GradScaler scales the loss before the backward
+    # and unscales (and checks) the gradients before the optimizer step; bf16 needs none
+    scaler = torch.amp.GradScaler("cuda", enabled=cdt == torch.float16)
     host = batches(args, rank, cfg.vocab_size)
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
@@ -328,8 +333,9 @@ def run_ours(args, rank, world, local):
     def train_step(i):
         ids, mask, labels, _ = dev_batches[i]
         loss, _, _ = engine.step(ids, mask, labels, denoms[i], hosts[i])
-        loss.backward()
-        opt.step()
+        scaler.scale(loss).backward()
+        scaler.step(opt)
+        scaler.update()
         opt.zero_grad(set_to_none=True)
 
     def barrier_sync():
@@ -419,9 +425,10 @@ def run_ours(args, rank, world, local):
                                                 "labels": labels}, dev)
         loss = patch.fused_compute_loss(trainer, model, inputs,
                                         num_items_in_batch=denoms[i])
-        loss.backward()
+        scaler.scale(loss).backward()
         patch.flush_metrics(trainer)
-        opt.step()
+        scaler.step(opt)
+        scaler.update()
         opt.zero_grad(set_to_none=True)
         return loss.detach().float().item()
 

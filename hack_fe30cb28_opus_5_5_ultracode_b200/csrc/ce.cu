@@ -11,7 +11,10 @@
 // [rows, 4] state (max, sum exp, sum exp * x, best) plus the argmax; rows with a target get
 // exp(x - running max) written over their logits for the gradient GEMM and the rescale factor
 // alpha = exp(old max - new max); the target's weight row is copied out when it falls in the
-// piece; finish forms loss, entropy, accuracy and dh = acc / s - W_target.
+// piece; optionally the fp32 gradient accumulator is moved to the new max in the same pass,
+// acc = alpha (acc + part), folding in the previous piece's product `part` (so the product GEMM
+// never reads its output and keeps its split-K); finish forms loss, entropy, accuracy and
+// dh = (acc + part) / s - W_target.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -161,6 +164,17 @@ __global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
     const float m = st.m;
     for (int64_t c = threadIdx.x; c < a.width; c += blockDim.x)
       src[c] = from_f<T>(__expf(to_f<T>(src[c]) - m));
+    if (a.acc != nullptr) {
+      // the gradient accumulator, moved to this piece's running max: acc = alpha (acc + part),
+      // part being the previous piece's product (when part_valid); zero before the first piece
+      float* acc = a.acc + row * a.H;
+      const float* part = a.part_valid ? a.part + row * a.H : nullptr;
+      const float alpha = m_old == -CUDART_INF_F ? 0.f : __expf(m_old - m);
+      for (int c = threadIdx.x; c < a.H; c += blockDim.x) {
+        if (m_old == -CUDART_INF_F) acc[c] = 0.f;
+        else acc[c] = alpha * (acc[c] + (part != nullptr ? part[c] : 0.f));
+      }
+    }
   }
 }
 
@@ -179,9 +193,11 @@ __global__ void ce_finish_kernel(CeFinishC a) {
   }
   if (row < a.n_sup) {
     const float* acc = a.acc + row * a.H;
+    const float* part = a.part != nullptr ? a.part + row * a.H : nullptr;
     const T* wt = reinterpret_cast<const T*>(a.wt) + row * a.H;
     T* dh = reinterpret_cast<T*>(a.dh) + row * a.H;
-    for (int c = threadIdx.x; c < a.H; c += blockDim.x) dh[c] = from_f<T>(acc[c] / s - to_f<T>(wt[c]));
+    for (int c = threadIdx.x; c < a.H; c += blockDim.x)
+      dh[c] = from_f<T>((acc[c] + (part != nullptr ? part[c] : 0.f)) / s - to_f<T>(wt[c]));
   }
 }
 
@@ -197,7 +213,11 @@ int ce_rows(const CeRowsC& a, cudaStream_t s) {
 
 int ce_piece(const CePieceC& a, cudaStream_t s) {
   if (a.rows < 0 || a.width <= 0 || a.ld < a.width || a.H <= 0) return QL_STATUS_BAD_ARG;
+  if (a.part_valid && (a.acc == nullptr || a.part == nullptr)) return QL_STATUS_BAD_ARG;
   if (a.rows == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_CE, 0, (double)a.rows * a.width * 2 + (double)a.n_sup * a.width * 2 +
+                               (a.acc != nullptr ? (double)a.n_sup * a.H * (a.part_valid ? 12 : 4) : 0),
+                 s);
   if (a.dtype == QL_F16) ce_piece_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
   else if (a.dtype == QL_BF16) ce_piece_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
   else return QL_STATUS_BAD_ARG;
@@ -207,6 +227,7 @@ int ce_piece(const CePieceC& a, cudaStream_t s) {
 int ce_finish(const CeFinishC& a, cudaStream_t s) {
   if (a.rows < 0 || a.H <= 0) return QL_STATUS_BAD_ARG;
   if (a.rows == 0) return QL_STATUS_OK;
+  ProfScope prof(PK_CE, 0, (double)a.n_sup * a.H * (4 + (a.part != nullptr ? 4 : 0) + 2 + 2), s);
   if (a.dtype == QL_F16) ce_finish_kernel<__half><<<a.rows, 256, 0, s>>>(a);
   else if (a.dtype == QL_BF16) ce_finish_kernel<__nv_bfloat16><<<a.rows, 256, 0, s>>>(a);
   else return QL_STATUS_BAD_ARG;

@@ -105,8 +105,8 @@ __device__ __forceinline__ float4 masked4(float4 v, uint32_t keep, float s) {
                      (keep & 4u) ? v.z * s : 0.f, (keep & 8u) ? v.w * s : 0.f);
 }
 
-constexpr int RMS_ROWS = 8;  // rows per CTA tile (one per warp)
-constexpr int RMS_PAD = 8;   // 16-bit elements of padding per shared row: conflict-free fragments
+constexpr int RMS_MAXR = 16;  // rows per CTA tile at most (the tensor-core fragments' 16 rows)
+constexpr int RMS_PAD = 8;    // 16-bit elements of padding per shared row: conflict-free fragments
 
 // OR of 4-bit masks over the 8 lanes that share a 32-column word; lane 8j returns word j.
 __device__ __forceinline__ uint32_t gather_bits(uint32_t nib) {
@@ -118,29 +118,42 @@ __device__ __forceinline__ uint32_t gather_bits(uint32_t nib) {
   return w;
 }
 
-// Tiles of 8 rows, tiles strided over the grid. WPR warps share a row (8 x WPR warps per CTA):
-// warp w works on row w / WPR, and its lanes hold the row's groups of 4 columns
-// gi = 32 (w % WPR) + lane + 32 WPR k (k < G) in registers between the two passes.
+// The A fragment of m16n8k16 for tile rows g and g + 8 from 16-bit rows in shared memory at
+// column k0 (rows at or past `rows` read as zero).
+template <typename T>
+__device__ __forceinline__ void frag_rows(uint32_t (&af)[4], const T* base, int ld, int g, int t,
+                                          int rows, int k0) {
+  const T* r0 = base + g * ld + k0 + 2 * t;
+  const T* r1 = base + (g + 8) * ld + k0 + 2 * t;
+  af[0] = g < rows ? *reinterpret_cast<const uint32_t*>(r0) : 0u;
+  af[1] = g + 8 < rows ? *reinterpret_cast<const uint32_t*>(r1) : 0u;
+  af[2] = g < rows ? *reinterpret_cast<const uint32_t*>(r0 + 8) : 0u;
+  af[3] = g + 8 < rows ? *reinterpret_cast<const uint32_t*>(r1 + 8) : 0u;
+}
+
+// Tiles of `rows` rows (at most 16; the launcher picks the count that spreads the rows over one
+// balanced wave of CTAs), tiles strided over the grid. WPR warps share a row (rows x WPR warps per
+// CTA): warp w works on row w / WPR, and its lanes hold the row's groups of 4 columns
+// gi = 32 (w % WPR) + lane + 32 WPR k (k < G).
 template <typename T, int G, int WPR>
-__global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
+__global__ void __launch_bounds__(WPR == 1 ? 32 * RMS_MAXR : 1024) rms_fwd_kernel(RmsFwdArgs a, int rows) {
   pdl_enter();
-  constexpr int NW = RMS_ROWS * WPR, SL = NW / 2;  // warps; K slices per adapter
   extern __shared__ __align__(16) uint8_t rms_smem[];
-  __shared__ float sSS[NW];
-  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
-  T* sY = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] dropped rows (q, v) of the tile
-  float* sRed = reinterpret_cast<float*>(sY + 2 * RMS_ROWS * ld);  // [NW][8 rows][16]
+  __shared__ float sSS[32];
+  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD, NW = rows * WPR;
+  T* sY = reinterpret_cast<T*>(rms_smem);  // [2][rows][ld] dropped rows (q, v) of the tile
+  float* sRed = reinterpret_cast<float*>(sY + 2 * rows * ld);  // [NW][16 rows][16]
   const bool lora_q = a.drop.drop_q && a.Aq != nullptr, lora_v = a.drop.drop_v && a.Av != nullptr;
-  const bool lora = lora_q || lora_v;
+  const int nad = (int)lora_q + (int)lora_v;  // adapters with a LoRA-A product
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rrow = warp / WPR, part = warp % WPR;
-  const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
+  const int ntiles = (a.n + rows - 1) / rows;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int row = tile * RMS_ROWS + rrow;
+    const int row = tile * rows + rrow;
     const bool live = row < a.n;
     const int64_t base = (int64_t)row * H;
-    // the row is kept in registers between the passes for up to 16 columns per lane; wider rows
-    // (G = 8 with 4 warps per row: 1,024 threads and 64 registers each) read it again
+    // the row stays in registers between the passes for up to 16 columns per lane; wider rows
+    // read it again (from L1)
     constexpr bool kKeepX = G <= 4 || WPR == 1;
     float4 xv[kKeepX ? G : 1];
     float ss = 0.f;
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
             nv = keep4(e_row + c, a.drop.ctr_v, a.drop);
             const float4 yv = masked4(y, nv, a.drop.keep_scale);
             if (a.yv != nullptr) store4<T>(reinterpret_cast<T*>(a.yv) + base + c, yv);
-            if (lora_v) store4<T>(sY + (RMS_ROWS + rrow) * ld + c, yv);
+            if (lora_v) store4<T>(sY + (rows + rrow) * ld + c, yv);
           }
         }
         if (a.keep_q != nullptr) {
@@ -209,20 +222,24 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
         }
       }
     }
-    if (lora) {
-      // x_lo[8 rows][16] = drop(y)[8][H] . A^T on the tensor cores: warp = (adapter, K slice);
-      // the tile's 8 rows are rows 0-7 of the 16-row A fragment (rows 8-15 zero).
+    if (nad > 0) {
+      // x_lo[rows][16] = drop(y)[rows][H] . A^T on the tensor cores, as nad x S work items
+      // (adapter, K slice), S = max(1, NW / nad) slices per adapter; item i = adapter i / S, slice
+      // i % S takes the 16-column K steps slice, slice + S, ... and goes to warp i % NW (a CTA of
+      // one warp does both adapters). The tile's rows are rows 0 .. rows-1 of the A fragment.
       __syncthreads();
-      const int ad = warp / SL, ks = warp % SL, g = lane >> 2, t = lane & 3;
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      if (ad == 0 ? lora_q : lora_v) {
+      const int S = NW / nad > 0 ? NW / nad : 1;
+      const int g = lane >> 2, t = lane & 3;
+      for (int item = warp; item < nad * S; item += NW) {
+        const int adi = item / S, slice = item % S;
+        const int ad = (nad == 2) ? adi : (lora_q ? 0 : 1);
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         const T* A = reinterpret_cast<const T*>(ad == 0 ? a.Aq : a.Av);
-        const T* Y = sY + (ad * RMS_ROWS + g) * ld + 2 * t;
-        const int kper = H / SL;
-#pragma unroll 4
-        for (int k0 = ks * kper; k0 < (ks + 1) * kper; k0 += 16) {
-          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(Y + k0), 0u,
-                                  *reinterpret_cast<const uint32_t*>(Y + k0 + 8), 0u};
+        const T* Y = sY + ad * rows * ld;
+#pragma unroll 2
+        for (int k0 = 16 * slice; k0 < H; k0 += 16 * S) {
+          uint32_t af[4];
+          frag_rows<T>(af, Y, ld, g, t, rows, k0);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             const unsigned int* Ab =
@@ -230,23 +247,26 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
             mma16816<T>(acc[nt], af, __ldg(Ab), __ldg(Ab + 4));
           }
         }
-      }
-      float* red = sRed + (warp * RMS_ROWS + g) * 16 + 2 * t;
+        // rows g and g + 8 of columns nt * 8 + 2t, 2t + 1
+        float* red = sRed + (item * RMS_MAXR + g) * 16 + 2 * t;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        red[nt * 8] = acc[nt][0];
-        red[nt * 8 + 1] = acc[nt][1];
+        for (int nt = 0; nt < 2; ++nt) {
+          red[nt * 8] = acc[nt][0];
+          red[nt * 8 + 1] = acc[nt][1];
+          red[8 * 16 + nt * 8] = acc[nt][2];
+          red[8 * 16 + nt * 8 + 1] = acc[nt][3];
+        }
       }
       __syncthreads();
-      // thread -> (adapter, row, r): the K slices added in a fixed order
-      if (threadIdx.x < 2 * RMS_ROWS * LORA_R) {
-        const int ad2 = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
-        const int orow = tile * RMS_ROWS + rr;
-        if (orow < a.n && (ad2 == 0 ? lora_q : lora_v)) {
+      // thread -> (adapter, row, r): the adapter's slices added in a fixed order
+      for (int idx = threadIdx.x; idx < nad * rows * LORA_R; idx += blockDim.x) {
+        const int oad = idx / (rows * LORA_R), rr = (idx / LORA_R) % rows, r = idx % LORA_R;
+        const int orow = tile * rows + rr;
+        if (orow < a.n) {
           float sum = 0.f;
-#pragma unroll 4
-          for (int q = 0; q < SL; ++q) sum += sRed[((ad2 * SL + q) * RMS_ROWS + rr) * 16 + r];
-          reinterpret_cast<T*>(ad2 == 0 ? a.xq : a.xv)[(int64_t)orow * LORA_R + r] = from_f<T>(sum);
+          for (int sl = 0; sl < S; ++sl) sum += sRed[((oad * S + sl) * RMS_MAXR + rr) * 16 + r];
+          const int dst = (nad == 2) ? oad : (lora_q ? 0 : 1);
+          reinterpret_cast<T*>(dst == 0 ? a.xq : a.xv)[(int64_t)orow * LORA_R + r] = from_f<T>(sum);
         }
       }
     }
@@ -255,37 +275,43 @@ __global__ void __launch_bounds__(256 * WPR) rms_fwd_kernel(RmsFwdArgs a) {
 }
 
 template <typename T, int G, int WPR>
-__global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
+__global__ void __launch_bounds__(WPR == 1 ? 32 * RMS_MAXR : 1024) rms_bwd_kernel(RmsBwdArgs a, int rows) {
   pdl_enter();
-  constexpr int NW = RMS_ROWS * WPR;
   extern __shared__ __align__(16) uint8_t rms_smem[];
-  __shared__ float sDot[NW];
-  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD;
-  T* sT = reinterpret_cast<T*>(rms_smem);  // [2][8][ld] tq, tv of the tile (formed in-kernel)
+  __shared__ float sDot[32];
+  const int H = a.H, ngroups = H / 4, ld = H + RMS_PAD, NW = rows * WPR;
+  T* sT = reinterpret_cast<T*>(rms_smem);  // [2][rows][ld] tq, tv of the tile (formed in-kernel)
   const bool fq = a.drop.drop_q && a.tq == nullptr, fv = a.drop.drop_v && a.tv == nullptr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rrow = warp / WPR, part = warp % WPR;
-  const int ntiles = (a.n + RMS_ROWS - 1) / RMS_ROWS;
+  const int ntiles = (a.n + rows - 1) / rows;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     if (fq || fv) {
-      // t[8 rows][H] = round16(dx_lo)[8][16] . A[16][H] on the tensor cores, 8-column tiles
-      // strided over the warps; rows 0-7 of the A fragment are the tile's rows.
+      // t[rows][H] = round16(dx_lo)[rows][16] . A[16][H] on the tensor cores, 8-column tiles
+      // strided over the warps; the tile's rows are rows 0 .. rows-1 of the A fragment.
       const int g = lane >> 2, t = lane & 3;
 #pragma unroll
       for (int ad = 0; ad < 2; ++ad) {
         if (!(ad == 0 ? fq : fv)) continue;
         const float* lo = ad == 0 ? a.dxlo_q : a.dxlo_v;
-        const int r0 = tile * RMS_ROWS + g;
+        const int r0 = tile * rows + g, r1 = r0 + 8;
         uint32_t af[4] = {0u, 0u, 0u, 0u};
-        if (r0 < a.n) {
+        if (g < rows && r0 < a.n) {
           const float2 p0 = *reinterpret_cast<const float2*>(lo + (int64_t)r0 * LORA_R + 2 * t);
           const float2 p1 = *reinterpret_cast<const float2*>(lo + (int64_t)r0 * LORA_R + 8 + 2 * t);
           af[0] = pack_t2<T>(p0.x, p0.y);
           af[2] = pack_t2<T>(p1.x, p1.y);
         }
+        if (g + 8 < rows && r1 < a.n) {
+          const float2 p0 = *reinterpret_cast<const float2*>(lo + (int64_t)r1 * LORA_R + 2 * t);
+          const float2 p1 = *reinterpret_cast<const float2*>(lo + (int64_t)r1 * LORA_R + 8 + 2 * t);
+          af[1] = pack_t2<T>(p0.x, p0.y);
+          af[3] = pack_t2<T>(p1.x, p1.y);
+        }
         const unsigned short* Ab =
             reinterpret_cast<const unsigned short*>(ad == 0 ? a.Aq : a.Av) + g;
-        T* dst = sT + (ad * RMS_ROWS + g) * ld + 2 * t;
+        T* dst0 = sT + (ad * rows + g) * ld + 2 * t;
+        T* dst1 = sT + (ad * rows + g + 8) * ld + 2 * t;
         for (int n0 = warp * 8; n0 < H; n0 += 8 * NW) {
           const unsigned short* col = Ab + n0;
           const uint32_t b0 = (uint32_t)__ldg(col + (2 * t) * H) |
@@ -294,17 +320,18 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
                               ((uint32_t)__ldg(col + (2 * t + 9) * H) << 16);
           float c[4] = {0.f, 0.f, 0.f, 0.f};
           mma16816<T>(c, af, b0, b1);
-          *reinterpret_cast<uint32_t*>(dst + n0) = pack_t2<T>(c[0], c[1]);
+          if (g < rows) *reinterpret_cast<uint32_t*>(dst0 + n0) = pack_t2<T>(c[0], c[1]);
+          if (g + 8 < rows) *reinterpret_cast<uint32_t*>(dst1 + n0) = pack_t2<T>(c[2], c[3]);
         }
       }
       __syncthreads();
     }
-    const int row = tile * RMS_ROWS + rrow;
+    const int row = tile * rows + rrow;
     const bool live = row < a.n;
     const int64_t base = (int64_t)row * H;
     float rstd = 0.f;
-    // x * rstd is kept in registers between the passes for up to 16 columns per lane; wider
-    // rows (G = 8 with 4 warps per row: 1,024 threads and 64 registers each) read x again
+    // x * rstd stays in registers between the passes for up to 16 columns per lane; wider rows
+    // read x again (from L1)
     constexpr bool kKeepX = G <= 4 || WPR == 1;
     float4 gv[G], xh[kKeepX ? G : 1];
     float dot = 0.f;
@@ -325,7 +352,7 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
             const void* tex = which == 0 ? a.tq : a.tv;
             const float4 t = tex != nullptr
                                  ? load4<T>(reinterpret_cast<const T*>(tex) + base + c)
-                                 : load4<T>(sT + (which * RMS_ROWS + rrow) * ld + c);
+                                 : load4<T>(sT + (which * rows + rrow) * ld + c);
             const uint32_t* bits = which == 0 ? a.keep_q : a.keep_v;
             const uint32_t keep = bits != nullptr
                                       ? (bits[wrow + c / 32] >> (c & 31)) & 15u
@@ -383,24 +410,62 @@ __global__ void __launch_bounds__(256 * WPR) rms_bwd_kernel(RmsBwdArgs a) {
   }
 }
 
-static int rms_grid(int64_t n) {
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = cdiv(n, 8);
-  const int64_t cap = (int64_t)sms * 4;
-  return (int)(want < cap ? want : cap);
-}
+// Launch shape of both kernels for n rows of H columns: warps per row (wpr), rows per tile and
+// grid. As many warps per row as still let the rows spread over one wave of CTAs of at most 32
+// warps (4 for up to 8 rows per SM, 3 or 2 for up to 10 or 16, with G <= 4 / 8 groups per lane);
+// past that, several waves of 8-row tiles with 4 warps per row. The row count per tile is then
+// balanced so the tiles fill whole waves: ceil(n / (SMs x waves)).
+struct RmsShape {
+  int wpr, rows, grid, G;
+};
 
-// Warps per row: 4 for rows of 1024..4096 columns (more warps in flight over the few rows of a
-// step, 4 or 8 groups of 4 columns per lane), else 1.
-static int rms_wpr(int H) { return (H >= 1024 && H <= 4096 && H % 256 == 0) ? 4 : 1; }
+static RmsShape rms_shape(int64_t n, int H) {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int groups = H / 4;
+  RmsShape r{1, RMS_MAXR, 0, 0};
+  if (H >= 1024 && H <= 4096 && H % 128 == 0) {
+    r.wpr = 4;
+    r.rows = 8;
+    if (n > (int64_t)sms * 8) {
+      if (cdiv(groups, 96) <= 4 && n <= (int64_t)sms * 10) {
+        r.wpr = 3;
+        r.rows = 10;
+      } else if (cdiv(groups, 64) <= 8 && n <= (int64_t)sms * 16) {
+        r.wpr = 2;
+        r.rows = 16;
+      }
+    }
+  }
+  const int64_t waves = cdiv(n, (int64_t)sms * r.rows);
+  r.rows = (int)cdiv(n, (int64_t)sms * waves);
+  r.grid = (int)cdiv(n, r.rows);
+  r.G = (int)cdiv(groups, 32 * r.wpr);
+  return r;
+}
 
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
 template <typename K>
 static void set_smem(K kern, int bytes) {
   if (bytes > 48 * 1024) smem_optin(reinterpret_cast<const void*>(kern), bytes);
 }
+
+// Instantiates kernel K<T, G, WPR> for the launch shape's (wpr, G) and launches it.
+#define QL_RMS_DISPATCH(K, TT)                                                         \
+  do {                                                                                 \
+    if (sh.wpr == 4 && sh.G <= 4) QL_RMS_LAUNCH(K, TT, 4, 4);                          \
+    else if (sh.wpr == 4) QL_RMS_LAUNCH(K, TT, 8, 4);                                  \
+    else if (sh.wpr == 3) QL_RMS_LAUNCH(K, TT, 4, 3);                                  \
+    else if (sh.wpr == 2) QL_RMS_LAUNCH(K, TT, 8, 2);                                  \
+    else if (sh.G <= 4) QL_RMS_LAUNCH(K, TT, 4, 1);                                    \
+    else if (sh.G <= 12) QL_RMS_LAUNCH(K, TT, 12, 1);                                  \
+    else QL_RMS_LAUNCH(K, TT, 32, 1);                                                  \
+  } while (0)
+#define QL_RMS_LAUNCH(K, TT, GG, WW)                                                   \
+  do {                                                                                 \
+    set_smem(K<TT, GG, WW>, smem);                                                     \
+    launch_k(K<TT, GG, WW>, dim3(sh.grid), dim3(32 * WW * sh.rows), smem, s, a, sh.rows); \
+  } while (0)
 
 int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   if (c.n < 0 || c.H <= 0 || c.H % 4 != 0 || c.H > 4 * RMS_THREADS * RMS_MAXG) return QL_STATUS_BAD_ARG;
@@ -420,30 +485,15 @@ int rms_fwd(const RmsFwdC& c, cudaStream_t s) {
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.Aq != nullptr) || (c.drop_v && c.Av != nullptr);
   if ((a.keep_q != nullptr || a.keep_v != nullptr) && c.H % 32 != 0) return QL_STATUS_BAD_ARG;
-  const int wpr = rms_wpr(c.H);
-  if (lora && c.H % (64 * wpr) != 0) return QL_STATUS_UNSUPPORTED;
-  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 + RMS_ROWS * wpr * RMS_ROWS * LORA_R * 4 : 0;
-  const int grid = rms_grid(c.n);
-#define QL_RMSF(TT, GG, WW)                                           \
-  do {                                                                \
-    set_smem(rms_fwd_kernel<TT, GG, WW>, smem);                       \
-    launch_k(rms_fwd_kernel<TT, GG, WW>, dim3(grid), dim3(256 * WW), smem, s, a);       \
-  } while (0)
-  const int G = (int)cdiv(c.H / 4, 32 * wpr);
-  if (c.dtype == QL_F16) {
-    if (wpr == 4 && G <= 4) QL_RMSF(__half, 4, 4);
-    else if (wpr == 4) QL_RMSF(__half, 8, 4);
-    else if (G <= 4) QL_RMSF(__half, 4, 1); else if (G <= 12) QL_RMSF(__half, 12, 1);
-    else QL_RMSF(__half, 32, 1);
-  } else if (c.dtype == QL_BF16) {
-    if (wpr == 4 && G <= 4) QL_RMSF(__nv_bfloat16, 4, 4);
-    else if (wpr == 4) QL_RMSF(__nv_bfloat16, 8, 4);
-    else if (G <= 4) QL_RMSF(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSF(__nv_bfloat16, 12, 1);
-    else QL_RMSF(__nv_bfloat16, 32, 1);
-  } else {
-    return QL_STATUS_BAD_ARG;
-  }
-#undef QL_RMSF
+  if (lora && c.H % 16 != 0) return QL_STATUS_UNSUPPORTED;  // 16-column tensor-core K steps
+  const RmsShape sh = rms_shape(c.n, c.H);
+  // the dropped rows, then one [16 rows][16] partial per (adapter, K slice) work item: at most
+  // max(warps, 2) items
+  const int items = sh.rows * sh.wpr > 2 ? sh.rows * sh.wpr : 2;
+  const int smem = lora ? 2 * sh.rows * (c.H + RMS_PAD) * 2 + items * RMS_MAXR * LORA_R * 4 : 0;
+  if (c.dtype == QL_F16) QL_RMS_DISPATCH(rms_fwd_kernel, __half);
+  else if (c.dtype == QL_BF16) QL_RMS_DISPATCH(rms_fwd_kernel, __nv_bfloat16);
+  else return QL_STATUS_BAD_ARG;
   return launched(1);
 }
 
@@ -467,31 +517,15 @@ int rms_bwd(const RmsBwdC& c, cudaStream_t s) {
   if (!prepare_dropout(a.drop)) return QL_STATUS_BAD_ARG;
   const bool lora = (c.drop_q && c.tq == nullptr) || (c.drop_v && c.tv == nullptr);
   if (lora && c.H % 8 != 0) return QL_STATUS_UNSUPPORTED;  // 8-column tensor-core tiles
-  const int wpr = rms_wpr(c.H);
-  const int smem = lora ? 2 * RMS_ROWS * (c.H + RMS_PAD) * 2 : 0;
-  const int grid = rms_grid(c.n);
-#define QL_RMSB(TT, GG, WW)                                           \
-  do {                                                                \
-    set_smem(rms_bwd_kernel<TT, GG, WW>, smem);                       \
-    launch_k(rms_bwd_kernel<TT, GG, WW>, dim3(grid), dim3(256 * WW), smem, s, a);       \
-  } while (0)
-  const int G = (int)cdiv(c.H / 4, 32 * wpr);
-  if (c.dtype == QL_F16) {
-    if (wpr == 4 && G <= 4) QL_RMSB(__half, 4, 4);
-    else if (wpr == 4) QL_RMSB(__half, 8, 4);
-    else if (G <= 4) QL_RMSB(__half, 4, 1); else if (G <= 12) QL_RMSB(__half, 12, 1);
-    else QL_RMSB(__half, 32, 1);
-  } else if (c.dtype == QL_BF16) {
-    if (wpr == 4 && G <= 4) QL_RMSB(__nv_bfloat16, 4, 4);
-    else if (wpr == 4) QL_RMSB(__nv_bfloat16, 8, 4);
-    else if (G <= 4) QL_RMSB(__nv_bfloat16, 4, 1); else if (G <= 12) QL_RMSB(__nv_bfloat16, 12, 1);
-    else QL_RMSB(__nv_bfloat16, 32, 1);
-  } else {
-    return QL_STATUS_BAD_ARG;
-  }
-#undef QL_RMSB
+  const RmsShape sh = rms_shape(c.n, c.H);
+  const int smem = lora ? 2 * sh.rows * (c.H + RMS_PAD) * 2 : 0;
+  if (c.dtype == QL_F16) QL_RMS_DISPATCH(rms_bwd_kernel, __half);
+  else if (c.dtype == QL_BF16) QL_RMS_DISPATCH(rms_bwd_kernel, __nv_bfloat16);
+  else return QL_STATUS_BAD_ARG;
   return launched(1);
 }
+#undef QL_RMS_LAUNCH
+#undef QL_RMS_DISPATCH
 
 }  // namespace ql
 

@@ -1,4 +1,4 @@
-// qkv + LoRA + rotary embedding, forward and backward, CTA tiles of 8 tokens.
+// qkv + LoRA + rotary embedding, forward and backward, CTA tiles of up to 16 tokens.
 //
 // Forward (reference qkv_rope_fwd_kernel, solution/kernels.py:212-264): splits the biased qkv
 // GEMM output into q, k, v, adds lora_scale * (the LoRA-B output) to q and v in fp32, and rotates
@@ -42,45 +42,50 @@ __device__ __forceinline__ void st8(T* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(h);
 }
 
-constexpr int ROPE_ROWS = 8;  // tokens per CTA tile
-constexpr int ROPE_WPR = 2;   // warps per token
+constexpr int ROPE_MAXR = 16;  // tokens per CTA tile at most (the tensor-core fragments' rows)
 
-// Tiles of 8 tokens (tiles strided over the grid), 2 warps per token. With LoRA, the tile's
-// LoRA-B outputs lq / lv = x_lo . B^T are formed first on the tensor cores (mma.sync m16n8k16,
-// fp32 accumulation; the 8 tokens are rows 0-7 of the A fragment), rounded to the 16-bit type
-// into shared memory. Then the warps of a token take chunks of 8 consecutive positions d .. d+7
-// of the first half of a head together with their partners d + D/2 (16-byte loads and stores).
-template <typename T>
-__global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
+// Tiles of `rows` tokens (at most 16, picked by the launcher so the tiles fill one balanced
+// wave; tiles strided over the grid), WPR warps per token (rows x WPR <= 16). With LoRA, the
+// tile's LoRA-B outputs lq / lv = x_lo . B^T are formed first on the tensor cores (mma.sync
+// m16n8k16, fp32 accumulation; the tokens are rows 0 .. rows-1 of the A fragment), rounded to
+// the 16-bit type into shared memory. Then the warps of a token take chunks of 8 consecutive
+// positions d .. d+7 of the first half of a head together with their partners d + D/2 (16-byte
+// loads and stores).
+template <typename T, int WPR>
+__global__ void __launch_bounds__(512) rope_fwd_kernel(RopeFwdC a, int rows) {
   pdl_enter();
-  constexpr int NW = ROPE_ROWS * ROPE_WPR;
+  const int NW = rows * WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
   const int C = (HQ + 2 * HKV) * D, QD = HQ * D, VD = HKV * D, ld = QD + VD + 8;
-  T* sL = reinterpret_cast<T*>(rope_smem);  // [8][ld]: [lq | lv] of the tile's tokens
+  T* sL = reinterpret_cast<T*>(rope_smem);  // [rows][ld]: [lq | lv] of the tile's tokens
   const bool fq = a.lq == nullptr && a.xq != nullptr, fv = a.lv == nullptr && a.xv != nullptr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rrow = warp / ROPE_WPR, part = warp % ROPE_WPR;
+  const int rrow = warp / WPR, part = warp % WPR;
   const float s = a.lora_scale;
   const int cph = HALF / 8;                 // chunks per head
   const int rot_chunks = (HQ + HKV) * cph;  // q and k heads
   const int v_chunks = VD / 8;
-  const int ntiles = (a.n + ROPE_ROWS - 1) / ROPE_ROWS;
+  const int ntiles = (a.n + rows - 1) / rows;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     if (fq || fv) {
       const int g = lane >> 2, t = lane & 3;
-      const int tg = tile * ROPE_ROWS + g;
       uint32_t aq[4] = {0u, 0u, 0u, 0u}, av[4] = {0u, 0u, 0u, 0u};
-      if (tg < a.n) {
-        if (fq) {
-          const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xq) + (int64_t)tg * RANK);
-          aq[0] = x[t];
-          aq[2] = x[4 + t];
-        }
-        if (fv) {
-          const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xv) + (int64_t)tg * RANK);
-          av[0] = x[t];
-          av[2] = x[4 + t];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // fragment rows g and g + 8
+        const int r = g + 8 * half;
+        const int64_t tg = (int64_t)tile * rows + r;
+        if (r < rows && tg < a.n) {
+          if (fq) {
+            const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xq) + tg * RANK);
+            aq[half] = x[t];
+            aq[2 + half] = x[4 + t];
+          }
+          if (fv) {
+            const uint32_t* x = reinterpret_cast<const uint32_t*>(reinterpret_cast<const T*>(a.xv) + tg * RANK);
+            av[half] = x[t];
+            av[2 + half] = x[4 + t];
+          }
         }
       }
       for (int n0 = warp * 8; n0 < QD + VD; n0 += 8 * NW) {
@@ -91,18 +96,20 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
                 : reinterpret_cast<const T*>(a.Bv) + (int64_t)(n0 - QD + g) * RANK);
         float c[4] = {0.f, 0.f, 0.f, 0.f};
         mma16816<T>(c, isq ? aq : av, __ldg(Bw + t), __ldg(Bw + 4 + t));
-        *reinterpret_cast<uint32_t*>(sL + g * ld + n0 + 2 * t) = pack_t2<T>(c[0], c[1]);
+        if (g < rows) *reinterpret_cast<uint32_t*>(sL + g * ld + n0 + 2 * t) = pack_t2<T>(c[0], c[1]);
+        if (g + 8 < rows)
+          *reinterpret_cast<uint32_t*>(sL + (g + 8) * ld + n0 + 2 * t) = pack_t2<T>(c[2], c[3]);
       }
       __syncthreads();
     }
-    const int64_t tok = (int64_t)tile * ROPE_ROWS + rrow;
+    const int64_t tok = (int64_t)tile * rows + rrow;
     if (tok < a.n) {
       const T* row = reinterpret_cast<const T*>(a.qkv) + tok * C;
       const T* lrow = sL + rrow * ld;
       const int pos = a.pos[tok];
       const float* cs = a.cos + (int64_t)pos * HALF;
       const float* sn = a.sin + (int64_t)pos * HALF;
-      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * ROPE_WPR) {
+      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * WPR) {
         const int hh = ch / cph, d = (ch % cph) * 8;
         const bool is_q = hh < HQ;
         const int src = hh * D + d;
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
         st8<T>(out + d, o1);
         st8<T>(out + d + HALF, o2);
       }
-      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * ROPE_WPR) {
+      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * WPR) {
         const int idx = ch * 8;
         float v[8];
         ld8<T>(row + (HQ + HKV) * D + idx, v);
@@ -153,30 +160,30 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_fwd_kernel(RopeFwdC a) {
   }
 }
 
-// Backward, tiles of 8 tokens, 2 warps per token: the rotation pass writes the pre-rotary
-// gradient row and keeps its q and v parts (16-bit) in shared memory; then
-// dx_lo[8][16] = g[8][K] . B[K][16] on the tensor cores over K slices of 64 columns of [q | v]
-// strided over the warps, the slices' partials added in a fixed order.
-template <typename T, typename TIn>
-__global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
+// Backward, tiles of `rows` tokens (as the forward), WPR warps per token: the rotation pass
+// writes the pre-rotary gradient row and keeps its q and v parts (16-bit) in shared memory; then
+// dx_lo[rows][16] = g[rows][K] . B[K][16] on the tensor cores over K slices of 64 columns of
+// [q | v] strided over the warps, the slices' partials added in a fixed order.
+template <typename T, typename TIn, int WPR>
+__global__ void __launch_bounds__(512) rope_bwd_kernel(RopeBwdC a, int rows) {
   pdl_enter();
-  constexpr int NW = ROPE_ROWS * ROPE_WPR;
+  const int NW = rows * WPR;
   extern __shared__ __align__(16) uint8_t rope_smem[];
   const int HQ = a.HQ, HKV = a.HKV, D = a.D, HALF = D / 2;
   const int C = (HQ + 2 * HKV) * D, QD = HQ * D, VD = HKV * D, ld = QD + VD + 8;
   const int KVIN = a.kv_heads_in;  // HKV, or HQ (per query head: summed over the group)
   const int group = KVIN / HKV;
-  T* sG = reinterpret_cast<T*>(rope_smem);                   // [8][ld] [g_q | g_v]
-  float* sRed = reinterpret_cast<float*>(sG + ROPE_ROWS * ld);  // [NW][2][8][16]
+  T* sG = reinterpret_cast<T*>(rope_smem);                   // [rows][ld] [g_q | g_v]
+  float* sRed = reinterpret_cast<float*>(sG + rows * ld);     // [NW][2][16][16]
   const bool lq = a.dxlo_q != nullptr, lv = a.dxlo_v != nullptr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rrow = warp / ROPE_WPR, part = warp % ROPE_WPR;
+  const int rrow = warp / WPR, part = warp % WPR;
   const int cph = HALF / 8;
   const int rot_chunks = (HQ + HKV) * cph;
   const int v_chunks = VD / 8;
-  const int ntiles = (a.n + ROPE_ROWS - 1) / ROPE_ROWS;
+  const int ntiles = (a.n + rows - 1) / rows;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t tok = (int64_t)tile * ROPE_ROWS + rrow;
+    const int64_t tok = (int64_t)tile * rows + rrow;
     T* grow = sG + rrow * ld;
     if (tok < a.n) {
       const int pos = a.pos[tok];
@@ -186,7 +193,7 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
       const TIn* dk = reinterpret_cast<const TIn*>(a.dk) + tok * KVIN * D;
       const TIn* dv = reinterpret_cast<const TIn*>(a.dv) + tok * KVIN * D;
       T* out = reinterpret_cast<T*>(a.dqkv) + tok * C;
-      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * ROPE_WPR) {
+      for (int ch = part * 32 + lane; ch < rot_chunks; ch += 32 * WPR) {
         const int hh = ch / cph, d = (ch % cph) * 8;
         float g1[8], g2[8], c[8], sv[8];
         if (hh < HQ) {
@@ -220,7 +227,7 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
           st8<T>(grow + col + HALF, o2);
         }
       }
-      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * ROPE_WPR) {
+      for (int ch = part * 32 + lane; ch < v_chunks; ch += 32 * WPR) {
         const int idx = ch * 8, j = idx / D, d = idx % D;
         float g[8];
 #pragma unroll
@@ -246,9 +253,12 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
                                   (int64_t)(isq ? k0 : k0 - QD) * RANK;
 #pragma unroll
         for (int kk = 0; kk < 64; kk += 16) {
-          const T* Y = sG + g * ld + k0 + kk + 2 * t;
-          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(Y), 0u,
-                                  *reinterpret_cast<const uint32_t*>(Y + 8), 0u};
+          const T* Y0 = sG + g * ld + k0 + kk + 2 * t;
+          const T* Y1 = Y0 + 8 * ld;
+          const uint32_t af[4] = {g < rows ? *reinterpret_cast<const uint32_t*>(Y0) : 0u,
+                                  g + 8 < rows ? *reinterpret_cast<const uint32_t*>(Y1) : 0u,
+                                  g < rows ? *reinterpret_cast<const uint32_t*>(Y0 + 8) : 0u,
+                                  g + 8 < rows ? *reinterpret_cast<const uint32_t*>(Y1 + 8) : 0u};
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             const unsigned short* bp = B + (kk + 2 * t) * RANK + nt * 8 + g;
@@ -261,20 +271,24 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
       }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        float* rq = sRed + ((warp * 2 + 0) * ROPE_ROWS + g) * RANK + nt * 8 + 2 * t;
-        float* rv = sRed + ((warp * 2 + 1) * ROPE_ROWS + g) * RANK + nt * 8 + 2 * t;
+        float* rq = sRed + ((warp * 2 + 0) * ROPE_MAXR + g) * RANK + nt * 8 + 2 * t;
+        float* rv = sRed + ((warp * 2 + 1) * ROPE_MAXR + g) * RANK + nt * 8 + 2 * t;
         rq[0] = accq[nt][0];
         rq[1] = accq[nt][1];
+        rq[8 * RANK] = accq[nt][2];
+        rq[8 * RANK + 1] = accq[nt][3];
         rv[0] = accv[nt][0];
         rv[1] = accv[nt][1];
+        rv[8 * RANK] = accv[nt][2];
+        rv[8 * RANK + 1] = accv[nt][3];
       }
       __syncthreads();
-      if (threadIdx.x < 2 * ROPE_ROWS * RANK) {
-        const int ad = threadIdx.x >> 7, rr = (threadIdx.x >> 4) & 7, r = threadIdx.x & 15;
-        const int64_t orow = (int64_t)tile * ROPE_ROWS + rr;
+      for (int idx = threadIdx.x; idx < 2 * rows * RANK; idx += blockDim.x) {
+        const int ad = idx / (rows * RANK), rr = (idx / RANK) % rows, r = idx % RANK;
+        const int64_t orow = (int64_t)tile * rows + rr;
         if (orow < a.n && (ad == 0 ? lq : lv)) {
           float sum = 0.f;
-          for (int w = 0; w < NW; ++w) sum += sRed[((w * 2 + ad) * ROPE_ROWS + rr) * RANK + r];
+          for (int w = 0; w < NW; ++w) sum += sRed[((w * 2 + ad) * ROPE_MAXR + rr) * RANK + r];
           // (g @ B) rounded to the 16-bit type, then * s rounded again (fp16 tensor times a scalar)
           const float v = to_f<T>(from_f<T>(to_f<T>(from_f<T>(sum)) * a.lora_scale));
           (ad == 0 ? a.dxlo_q : a.dxlo_v)[orow * RANK + r] = v;
@@ -285,11 +299,21 @@ __global__ void __launch_bounds__(256 * ROPE_WPR) rope_bwd_kernel(RopeBwdC a) {
   }
 }
 
-static int rope_grid(int64_t n) {
+// Launch shape: tokens per tile balanced so the tiles fill whole waves of one CTA per SM (up to
+// 16 tokens per tile), two warps per token for up to 8 tokens per tile, else one.
+struct RopeShape {
+  int wpr, rows, grid;
+};
+
+static RopeShape rope_shape(int64_t n) {
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = cdiv(n, 8), cap = (int64_t)sms * 4;
-  return (int)(want < cap ? want : cap);
+  const int64_t waves = cdiv(n, (int64_t)sms * ROPE_MAXR);
+  RopeShape r;
+  r.rows = (int)cdiv(n, (int64_t)sms * waves);
+  r.wpr = r.rows <= 8 ? 2 : 1;
+  r.grid = (int)cdiv(n, r.rows);
+  return r;
 }
 
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per kernel (and size).
@@ -305,17 +329,21 @@ int rope_fwd(const RopeFwdC& a, cudaStream_t s) {
   if ((a.xq != nullptr || a.xv != nullptr) && a.rank != RANK) return QL_STATUS_UNSUPPORTED;
   ProfScope prof(PK_ROPE_FWD, 0, (double)a.n * (a.HQ + 2 * a.HKV) * a.D * 2 * 2, s);
   const bool lora = (a.lq == nullptr && a.xq != nullptr) || (a.lv == nullptr && a.xv != nullptr);
-  const int smem = lora ? ROPE_ROWS * ((a.HQ + a.HKV) * a.D + 8) * 2 : 0;
-  const int grid = rope_grid(a.n);
+  const RopeShape sh = rope_shape(a.n);
+  const int smem = lora ? sh.rows * ((a.HQ + a.HKV) * a.D + 8) * 2 : 0;
+#define QL_ROPEF(TT, WW)                                                                  \
+  do {                                                                                    \
+    rope_smem_attr(rope_fwd_kernel<TT, WW>, smem);                                        \
+    launch_k(rope_fwd_kernel<TT, WW>, dim3(sh.grid), dim3(32 * WW * sh.rows), smem, s, a, sh.rows); \
+  } while (0)
   if (a.dtype == QL_F16) {
-    rope_smem_attr(rope_fwd_kernel<__half>, smem);
-    launch_k(rope_fwd_kernel<__half>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);
+    if (sh.wpr == 2) QL_ROPEF(__half, 2); else QL_ROPEF(__half, 1);
   } else if (a.dtype == QL_BF16) {
-    rope_smem_attr(rope_fwd_kernel<__nv_bfloat16>, smem);
-    launch_k(rope_fwd_kernel<__nv_bfloat16>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);
+    if (sh.wpr == 2) QL_ROPEF(__nv_bfloat16, 2); else QL_ROPEF(__nv_bfloat16, 1);
   } else {
     return QL_STATUS_BAD_ARG;
   }
+#undef QL_ROPEF
   return launched(1);
 }
 
@@ -330,14 +358,19 @@ int rope_bwd(const RopeBwdC& a, cudaStream_t s) {
   ProfScope prof(PK_ROPE_BWD, 0, (double)a.n * (a.HQ + 2 * a.HKV) * a.D * (4 + 2), s);
   const bool lora = a.dxlo_q != nullptr || a.dxlo_v != nullptr;
   if (lora && a.D % 64 != 0) return QL_STATUS_UNSUPPORTED;  // 64-column K slices of [q | v]
-  const int smem = lora ? ROPE_ROWS * ((a.HQ + a.HKV) * a.D + 8) * 2 +
-                              ROPE_ROWS * ROPE_WPR * 2 * ROPE_ROWS * RANK * 4
+  const RopeShape sh = rope_shape(a.n);
+  const int smem = lora ? sh.rows * ((a.HQ + a.HKV) * a.D + 8) * 2 +
+                              sh.rows * sh.wpr * 2 * ROPE_MAXR * RANK * 4
                         : 0;
-  const int grid = rope_grid(a.n);
-#define QL_ROPEB(TT, TI)                                             \
-  do {                                                               \
-    rope_smem_attr(rope_bwd_kernel<TT, TI>, smem);                   \
-    launch_k(rope_bwd_kernel<TT, TI>, dim3(grid), dim3(256 * ROPE_WPR), smem, s, a);   \
+#define QL_ROPEB(TT, TI)                                                                      \
+  do {                                                                                        \
+    if (sh.wpr == 2) {                                                                        \
+      rope_smem_attr(rope_bwd_kernel<TT, TI, 2>, smem);                                       \
+      launch_k(rope_bwd_kernel<TT, TI, 2>, dim3(sh.grid), dim3(64 * sh.rows), smem, s, a, sh.rows); \
+    } else {                                                                                  \
+      rope_smem_attr(rope_bwd_kernel<TT, TI, 1>, smem);                                       \
+      launch_k(rope_bwd_kernel<TT, TI, 1>, dim3(sh.grid), dim3(32 * sh.rows), smem, s, a, sh.rows); \
+    }                                                                                         \
   } while (0)
   if (a.dtype == QL_F16) {
     if (f32in) QL_ROPEB(__half, float); else QL_ROPEB(__half, __half);

@@ -26,7 +26,8 @@ import torch
 
 from . import _lib, memory, ops
 
-HEAD_CHUNK = 4096  # rows of logits alive at a time: 4096 x 151936 x 2 B = 1.2 GB of HBM
+HEAD_CHUNK = 4096          # head rows per block (their per-row statistics and accumulators)
+HEAD_L2_BYTES = 24 << 20   # 16-bit logits of one vocabulary chunk of a head block: L2-resident
 
 
 # ---------------------------------------------------------------------------------------------
@@ -459,7 +460,6 @@ class FusedQwen2:
         self.V = self.lm_w.shape[0]
         self.rope = RopeTable(inner.rotary_emb, spec.D, self.device)
         self.head_chunk = head_chunk
-        self._logits = None
         # fp32 LoRA weights (PEFT owns them) and one 16-bit shadow buffer refreshed per step
         self.lora_fp32 = [t for s in self.layers for t in s.lora_params()]
         sizes = [t.numel() for t in self.lora_fp32]
@@ -528,11 +528,6 @@ class FusedQwen2:
         of the backward, in one all-reduce of the flat gradient buffer."""
         self.process_group = group
         self.data_parallel = True
-
-    def logits_buffer(self, rows):
-        if self._logits is None or self._logits.shape[0] < rows:
-            self._logits = torch.empty((rows, self.V), device=self.device, dtype=self.dtype)
-        return self._logits[:rows]
 
     def step(self, input_ids, attention_mask, labels, denom, host=None):
         """One training step's forward: (loss, packed, stats); autograd runs the backward.
@@ -657,9 +652,12 @@ class FusedQwen2:
         desc.drop_q, desc.drop_v = f["drop_q"], f["drop_v"]
 
     def _head(self, h, packed, denom, stats):
-        """Final norm, lm_head, cross-entropy and the logged metrics over chunks of rows taken
-        supervised-first, with the gradient w.r.t. the final hidden state formed here
-        (solution/engine.py:1352-1400). Returns (dh in head order, loss)."""
+        """Final norm, lm_head, cross-entropy and the logged metrics, with the gradient w.r.t.
+        the final hidden state formed in the same pass (solution/engine.py:1352-1400, and the
+        vocabulary-piece form of solution/engine.py:1498-1547). Tokens are taken supervised
+        first, in blocks of up to head_chunk rows; within a block the vocabulary is walked in
+        chunks small enough that a chunk's logits stay in L2 between the kernels that use them
+        (_head_block): no [rows, V] logits buffer exists. Returns (dh in head order, loss)."""
         n, H = h.shape
         dev, dt = self.device, self.dtype
         order = packed.head_order
@@ -674,18 +672,78 @@ class FusedQwen2:
         if n_sup < n:
             dhp[n_sup:].zero_()
         inv = 1.0 / denom if denom else float("nan")  # 0 / 0, as in the base
-        for c0 in range(0, n, self.head_chunk):
-            c1 = min(n, c0 + self.head_chunk)
-            logits = ops.gemm(hn[c0:c1], self.lm_w, out=self.logits_buffer(c1 - c0))
-            sup = max(0, min(c1, n_sup) - c0)
-            ops.ce_rows(logits, targets[c0:c1], write_grad=sup > 0, loss=tok_loss[c0:c1],
-                        entropy=entropy[c0:c1], correct=correct[c0:c1])
+        for r0 in range(0, n, self.head_chunk):
+            r1 = min(n, r0 + self.head_chunk)
+            sup = max(0, min(r1, n_sup) - r0)
+            dhn = self._head_block(hn[r0:r1], targets[r0:r1], sup, tok_loss[r0:r1],
+                                   entropy[r0:r1], correct[r0:r1])
             if sup:
-                dhn = ops.gemm(logits[:sup], self.lm_w, b_kn=True)
-                ops.rms_bwd(dhn, hp[c0:c0 + sup], rstd[c0:c0 + sup], self.norm_w, dtype=dt,
-                            grad_scale=inv, out=dhp[c0:c0 + sup])
+                ops.rms_bwd(dhn, hp[r0:r0 + sup], rstd[r0:r0 + sup], self.norm_w, dtype=dt,
+                            grad_scale=inv, out=dhp[r0:r0 + sup])
         stats.order, stats.tok_loss, stats.entropy, stats.correct = order, tok_loss, entropy, correct
         return dhp, tok_loss.sum() * inv
+
+    def vocab_chunk(self, rows):
+        """Vocabulary entries per chunk of a head block of `rows` rows: as many as keep the
+        chunk's 16-bit logits within HEAD_L2_BYTES (they are written, rewritten and read again
+        by three kernels in a row), in multiples of 64, evened out over the chunks."""
+        def cdiv(a, b):
+            return -(-a // b)
+
+        width = max(1024, HEAD_L2_BYTES // (self._esize() * max(rows, 1)) // 64 * 64)
+        return cdiv(cdiv(self.V, cdiv(self.V, width)), 64) * 64
+
+    def _head_buffers(self, rows, width, sup):
+        """Grow-only buffers of a head block (reused from step to step)."""
+        H, dt, dev = self.layers[0].H, self.dtype, self.device
+        b = getattr(self, "_hb", None)
+        need = (rows, width, sup)
+        if b is None or any(x < y for x, y in zip(b["shape"], need)):
+            rows_, width_, sup_ = (max(x, y) for x, y in zip(b["shape"] if b else (0, 0, 0), need))
+            b = {"shape": (rows_, width_, sup_),
+                 "logits": torch.empty(rows_ * width_, device=dev, dtype=dt),
+                 "state": torch.empty((rows_, 4), device=dev, dtype=torch.float32),
+                 "best": torch.empty(rows_, device=dev, dtype=torch.int64),
+                 "xt": torch.empty(rows_, device=dev, dtype=torch.float32),
+                 "alpha": torch.empty(max(sup_, 1), device=dev, dtype=torch.float32),
+                 "acc": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
+                 "part": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
+                 "wt": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
+                 "dhn": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
+                 "init": torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")], device=dev)}
+            self._hb = b
+        return b
+
+    def _head_block(self, hn, targets, sup, tok_loss, entropy, correct):
+        """One block of head rows (the first `sup` have a target) over the whole vocabulary,
+        chunk by chunk: (1) the chunk's logits = hn . W_chunk^T on the tensor cores; (2) ce_piece
+        carries each row's online max / sum exp / sum exp * x / argmax across chunks, writes
+        exp(x - running max) over the supervised rows' logits, copies the target's weight row
+        and moves the fp32 gradient accumulator to the new max, folding in the previous chunk's
+        product (acc = alpha (acc + part)); (3) part = exp(x - max) . W_chunk on the tensor cores.
+        ce_finish then gives loss, entropy, accuracy and dhn = (acc + part) / sum - W_target
+        (16-bit) for the supervised rows, which it returns."""
+        rows, H = hn.shape
+        width = self.vocab_chunk(rows)
+        b = self._head_buffers(rows, width, sup)
+        state, best, xt = b["state"][:rows], b["best"][:rows], b["xt"][:rows]
+        state.copy_(b["init"].expand(rows, 4))
+        logits = b["logits"][:rows * width].view(rows, width)
+        acc = b["acc"][:sup] if sup else None
+        part = b["part"][:sup] if sup else None
+        wt, dhn = b["wt"][:sup], b["dhn"][:sup]
+        for v0 in range(0, self.V, width):
+            w = min(width, self.V - v0)
+            W = self.lm_w[v0:v0 + w]
+            chunk = logits[:, :w]
+            ops.gemm(hn, W, out=chunk)
+            ops.ce_piece(chunk, W, targets, state, best, xt, b["alpha"], wt, v0, sup, acc=acc,
+                         part=part, part_valid=v0 > 0 and sup > 0, H=H)
+            if sup:
+                ops.gemm(chunk[:sup], W, out=part, b_kn=True)
+        ops.ce_finish(state, best, xt, targets, tok_loss, entropy, correct, b["acc"], wt, dhn,
+                      sup, part=part)
+        return dhn
 
     def run_layer(self, index, packed, drop, h, dh3):
         """One decoder layer forward and backward through the layer ABI (ql_layer_forward,

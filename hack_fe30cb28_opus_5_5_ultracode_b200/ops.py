@@ -398,22 +398,29 @@ def ce_rows(logits, target, write_grad=True, zero_unsupervised=False, loss=None,
     return loss, entropy, correct
 
 
-def ce_piece(logits, w, target, state, best_idx, xt, alpha, wt, v0, n_sup):
+def ce_piece(logits, w, target, state, best_idx, xt, alpha, wt, v0, n_sup, acc=None,
+             part=None, part_valid=False, H=None):
+    """Reference _ce_piece (engine.py:1033-1038) on a vocabulary piece [v0, v0 + width) of the
+    logits. acc / part: the fp32 gradient accumulator moved to the new running max in place,
+    acc = alpha (acc + part) (part folded in when part_valid)."""
     rows, width = logits.shape
     args = _lib.struct("ql_ce_piece_args", logits=_ptr(logits), w=_ptr(w), target=_ptr(target),
                        state=_ptr(state), best_idx=_ptr(best_idx), xt=_ptr(xt),
                        alpha=_ptr(alpha), wt=_ptr(wt), rows=rows, v0=int(v0), width=width,
-                       ld=logits.stride(0), n_sup=int(n_sup), H=w.shape[1],
-                       dtype=dtype_code(logits.dtype))
+                       ld=logits.stride(0), n_sup=int(n_sup),
+                       H=int(H) if H is not None else w.shape[1],
+                       dtype=dtype_code(logits.dtype), acc=_ptr(acc), part=_ptr(part),
+                       part_valid=int(bool(part_valid)))
     call("ql_ce_piece", ctypes_ref(args), stream_ptr())
 
 
-def ce_finish(state, best_idx, xt, target, loss, entropy, correct, acc, wt, dh, n_sup):
+def ce_finish(state, best_idx, xt, target, loss, entropy, correct, acc, wt, dh, n_sup,
+              part=None):
     args = _lib.struct("ql_ce_finish_args", state=_ptr(state), best_idx=_ptr(best_idx),
                        xt=_ptr(xt), target=_ptr(target), loss=_ptr(loss),
                        entropy=_ptr(entropy), correct=_ptr(correct), acc=_ptr(acc),
                        wt=_ptr(wt), dh=_ptr(dh), rows=state.shape[0], n_sup=int(n_sup),
-                       H=acc.shape[1], dtype=dtype_code(dh.dtype))
+                       H=acc.shape[1], dtype=dtype_code(dh.dtype), part=_ptr(part))
     call("ql_ce_finish", ctypes_ref(args), stream_ptr())
 
 

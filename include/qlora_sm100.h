@@ -300,6 +300,11 @@ typedef struct {
   void* wt;             /* [n_sup, H] or NULL: the target's weight row */
   int64_t rows, v0, width, ld, n_sup;
   int32_t H, dtype;
+  float* acc;           /* [n_sup, H] or NULL: fp32 gradient accumulator, moved to this piece's
+                           running max in place: acc = alpha (acc + part); zeroed at the first
+                           piece (state max -inf) */
+  const float* part;    /* [n_sup, H]: the previous piece's product exp(x - max) . W_piece */
+  int32_t part_valid;   /* whether `part` holds a product yet (0 before the first one) */
 } ql_ce_piece_args;
 
 typedef struct {
@@ -312,9 +317,10 @@ typedef struct {
   int32_t* correct;
   const float* acc;     /* [n_sup, H] sum_v exp(x_v - max) W_v */
   const void* wt;       /* [n_sup, H] */
-  void* dh;             /* [n_sup, H] acc / s - W_target */
+  void* dh;             /* [n_sup, H] (acc + part) / s - W_target */
   int64_t rows, n_sup;
   int32_t H, dtype;
+  const float* part;    /* [n_sup, H] or NULL: the last piece's product, not yet in acc */
 } ql_ce_finish_args;
 
 /* Replaces _ce + lm_head_ce_kernel (solution/engine.py:1026-1030, solution/kernels.py:344-388). */

@@ -2,7 +2,7 @@
 CPU tensors under TRITON_INTERPRET=1 (only where the reference tree is mounted: the build
 container; nothing on the GPU box reads the reference).
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/the/reference/checkout
 
 Each fixture holds seeded inputs and the reference kernel's outputs:
   nf4.npz        nf4_dequant_kernel (non-nested; the interpreter lacks libdevice.mul_rn for
@@ -23,8 +23,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-sys.path.insert(0, REF)
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_golden.py /path/to/the/reference/checkout")
+sys.path.insert(0, sys.argv[1])
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from solution import kernels as K  # noqa: E402  (the reference's kernels)

@@ -104,7 +104,12 @@ def test_rms_matches_reference_golden(golden):
     close(dx, torch.from_numpy(g["dx"]), 1e-4)
 
 
-@pytest.mark.parametrize("n,H", [(37, 1536), (5, 256), (300, 3584), (64, 4096), (40, 2304)])
+# launch shapes covered: 4 warps per row and tiles of 1-8 rows in one wave (37, 300, 64, 40,
+# 1100 x 3584), 3 warps x 9 rows (1264), 2 warps x 11-14 rows (1500, 2000), several waves of
+# 7-row tiles (5000) and of 5-row tiles at the 7B width (1300 x 3584), one warp per row (256)
+@pytest.mark.parametrize("n,H", [(37, 1536), (5, 256), (300, 3584), (64, 4096), (40, 2304),
+                                 (1264, 1536), (1500, 1536), (2000, 1536), (5000, 1536),
+                                 (1100, 3584), (1300, 3584), (700, 256)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_rms_fused_lora_matches_torch(n, H, dtype):
     o = ops()
@@ -147,7 +152,8 @@ def test_rms_fused_lora_matches_torch(n, H, dtype):
     close(d16, dx_a, tol)
 
 
-@pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584), (64, 4096)])
+@pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584), (64, 4096), (1264, 1536),
+                                 (2000, 1536)])
 def test_rms_mask_bits_match_redrawn_masks(n, H):
     """The forward's mask bits are the Philox masks; a backward that reads them equals one that
     draws the masks again, bit for bit."""
@@ -164,9 +170,14 @@ def test_rms_mask_bits_match_redrawn_masks(n, H):
     _, _, yq, yv, rstd, xq, xv = o.rms_fwd(x, w, 1e-6, drop=drop, Aq=Aq, Av=Av, want_yq=True,
                                            keep_bits=bits)
     cols = torch.arange(H, device=DEV)
-    for b, y in zip(bits, (yq, yv)):
+    nelem = (int(tok.max()) + 1) * H
+    for b, y, ctr in zip(bits, (yq, yv), (21, 22)):
         kept = ((b[:, cols // 32] >> (cols % 32)) & 1).bool()
-        assert torch.equal(kept, y != 0)
+        # against an independent draw of the same Philox masks (comparing with y != 0 would trip
+        # on kept values below fp16's smallest subnormal, which round to zero)
+        redrawn = o.dropout_keep(nelem, 91, ctr, 1184 * 256, 0.3).bool()
+        assert torch.equal(kept, redrawn[tok[:, None] * H + cols[None, :]])
+        assert not bool((y != 0)[~kept].any())
     dy = torch.randn(n, H, device=DEV).half()
     dxlo_q = torch.randn(n, 16, device=DEV)
     dxlo_v = torch.randn(n, 16, device=DEV)
@@ -194,11 +205,12 @@ def test_rope_matches_reference_golden(golden):
     close(dqkv, torch.from_numpy(g["dqkv"]), 1e-2)
 
 
+@pytest.mark.parametrize("n", [23, 1264, 2500])  # tiles of 1 (2 warps / token), 9 and 9 tokens
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_rope_fused_lora(dtype):
+def test_rope_fused_lora(n, dtype):
     o = ops()
     torch.manual_seed(0)
-    n, HQ, HKV, D = 23, 12, 2, 128
+    HQ, HKV, D = 12, 2, 128
     C = (HQ + 2 * HKV) * D
     qkv = torch.randn(n, C, device=DEV).to(dtype)
     xq = torch.randn(n, 16, device=DEV).to(dtype)
@@ -366,6 +378,23 @@ def test_ce_rows_and_pieces_match_torch(V):
     exact = (torch.softmax(lg[:n_sup].double(), -1)
              - torch.nn.functional.one_hot(tg[:n_sup], V).double()) @ W.double()
     assert ((dh.double() - exact).norm() / exact.norm()).item() < 2e-3
+
+    # the same pieces with the accumulator moved by the kernel (acc = alpha (acc + part)) and the
+    # last product folded in by finish, as the step's chunked head runs them
+    state2 = torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")], device=DEV).repeat(n, 1)
+    acc2 = torch.full((n_sup, H), float("nan"), device=DEV)  # must be zeroed by the first piece
+    part = torch.full((n_sup, H), float("nan"), device=DEV)
+    for v0 in range(0, V, piece):
+        width = min(piece, V - v0)
+        pc = lg[:, v0:v0 + width].clone()
+        w = W[v0:v0 + width].contiguous()
+        o.ce_piece(pc, w, tg, state2, best, xt, alpha, wt, v0, n_sup, acc=acc2, part=part,
+                   part_valid=v0 > 0)
+        part = pc[:n_sup].float() @ w.float()
+    dh2 = torch.empty_like(dh)
+    o.ce_finish(state2, best, xt, tg, l2, e2, c2, acc2, wt, dh2, n_sup, part=part)
+    assert ((dh2.double() - exact).norm() / exact.norm()).item() < 2e-3
+    close(l2, loss[order], 1e-4)
 
 
 # ---------------------------------------------------------------------------------------------

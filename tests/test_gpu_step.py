@@ -20,6 +20,17 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 LOSS_ABS = {torch.float16: 1e-3, torch.bfloat16: 5e-3}
 GRAD_REL = {torch.float16: 1e-2, torch.bfloat16: 3e-2}
+# fp16 training backpropagates a scaled loss (HF Trainer's GradScaler starts at 2^16) so the
+# backward's 16-bit intermediates stay clear of fp16's subnormal range; the gradients are unscaled
+# before use. bf16 needs no scale.
+LOSS_SCALE = {torch.float16: 65536.0, torch.bfloat16: 1.0}
+
+
+def _grads(loss, params, dtype):
+    """LoRA gradients of the step's loss as fp16 / bf16 training computes them."""
+    scale = LOSS_SCALE[dtype]
+    grads = torch.autograd.grad(loss, params, grad_outputs=torch.full_like(loss, scale))
+    return [g / scale for g in grads]
 
 
 def _record(name, **values):
@@ -70,7 +81,7 @@ def _run(cfg, lengths, dropout, nested, dtype=torch.float16, seed=1, keep_weight
     torch.cuda.manual_seed(5)
     seed0, off0 = gen.initial_seed(), gen.get_offset()
     loss, packed, stats = engine.step(ids.to(DEV), mask.to(DEV), labels.to(DEV), n_items)
-    grads = torch.autograd.grad(loss, params)
+    grads = _grads(loss, params, dtype)
     torch.cuda.synchronize()
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
 
@@ -159,7 +170,7 @@ def test_configs1_model_matches_oracle():
     torch.cuda.manual_seed(2024)
     seed0, off0 = gen.initial_seed(), gen.get_offset()
     loss, packed, stats = engine.step(ids.to(DEV), mask.to(DEV), labels.to(DEV), n_items)
-    grads = torch.autograd.grad(loss, params)
+    grads = _grads(loss, params, torch.float16)
     torch.cuda.synchronize()
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
 
