@@ -64,10 +64,16 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--spill", choices=["recompute", "offload"], default=None,
+    ap.add_argument("--spill", choices=["recompute", "offload", "auto"], default=None,
                     help="activation-memory plan: spill all but --keep-layers layers this way "
-                         "(default: every layer keeps its activations in HBM)")
-    ap.add_argument("--keep-layers", type=int, default=0)
+                         "(auto: offload only the layers whose copies hide behind compute, "
+                         "recompute the rest; default: every layer keeps its activations)")
+    ap.add_argument("--keep-layers", type=int, default=None,
+                    help="with --spill: keep exactly the last k layers (default 0 without "
+                         "--budget-gib)")
+    ap.add_argument("--budget-gib", type=float, default=None,
+                    help="with --spill: keep as many last layers as fit this many GiB of saved "
+                         "activations")
     ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per rank and step")
     ap.add_argument("--median", type=int, default=MEDIAN, help="median sequence length")
     ap.add_argument("--lo", type=int, default=LO)
@@ -315,7 +321,11 @@ def run_ours(args, rank, world, local):
     cdt = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     model = build_qwen2_qlora(cfg, dropout=0.05, device=dev, seed=0, embed_dtype=cdt)
     model.train()
-    plan_kw = {} if args.spill is None else dict(spill=args.spill, keep_layers=args.keep_layers)
+    plan_kw = {}
+    if args.spill is not None:
+        budget = None if args.budget_gib is None else int(args.budget_gib * 1024)
+        keep = args.keep_layers if args.keep_layers is not None or budget is not None else 0
+        plan_kw = dict(spill=args.spill, keep_layers=keep, activation_budget_mib=budget)
     engine = FusedQwen2(model, dtype=cdt, **plan_kw)
     if world > 1:
         engine.set_data_parallel(None)
@@ -352,16 +362,25 @@ def run_ours(args, rank, world, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
         return float(t.item())
 
-    def timed_steps(step_fn):
-        """Device milliseconds of the K timed steps (max over ranks)."""
+    host_ms = {}
+
+    def timed_steps(step_fn, name=None):
+        """Device milliseconds of the K timed steps (max over ranks); with a name, also this rank's
+        host time to enqueue them (the steps run ahead of the GPU: a host time close to the device
+        time means the host, not the GPU, sets the pace)."""
         barrier_sync()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        t0 = time.perf_counter()
         for i in timed:
             step_fn(i)
+        t1 = time.perf_counter()
         e1.record()
         barrier_sync()
-        return over_ranks(e0.elapsed_time(e1), "max")
+        dev_ms = e0.elapsed_time(e1)
+        if name is not None:
+            host_ms[name] = ((t1 - t0) * 1e3, dev_ms)
+        return over_ranks(dev_ms, "max")
 
     # The model, the libraries and the batches are set up: move every object made so far out of
     # the cyclic collector's scans, so the steps' short-lived objects do not trigger full scans of
@@ -377,7 +396,7 @@ def run_ours(args, rank, world, local):
     time.sleep(0.3)
     launches0 = ops.launch_count()
     torch.cuda.nvtx.range_push("bench_timed")  # (lets ncu --nvtx-include capture these steps)
-    ms = timed_steps(train_step)
+    ms = timed_steps(train_step, "timed")
     torch.cuda.nvtx.range_pop()
     launches = ops.launch_count() - launches0
     clk = clocks.stop()
@@ -394,16 +413,42 @@ def run_ours(args, rank, world, local):
     prof = ops.profile_read()
     mem_line = {"plan": engine.last_plan.summary() if engine.last_plan else None}
     if args.spill is not None:
-        # the same steps with every layer kept: the cost of the spill (exposed copy or
-        # recompute time) and the host-link traffic it moves
+        from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+
+        # the spill's costs, each against a variant of the same steps: the copies' exposed time
+        # (the plan with its offloaded layers kept instead), the whole spill's cost (every layer
+        # kept), and the host-link traffic and its achieved bandwidth (copy-stream events)
+        off = engine.last_offload
+        torch.cuda.synchronize(dev)
+        copy_ms = off.copy_ms() if off is not None else 0.0
         spill_bytes = engine.last_offload_bytes  # of the last timed step
-        keep_layers, engine.keep_layers, engine.spill = engine.keep_layers, None, "recompute"
-        keep_ms = timed_steps(train_step)
-        engine.keep_layers, engine.spill = keep_layers, args.spill
-        mem_line.update(offload_bytes_per_step=spill_bytes,
-                        keep_all_ms_per_step=keep_ms / args.steps,
-                        spill_ms_per_step=ms / args.steps,
-                        exposed_fraction=max(0.0, (ms - keep_ms) / ms))
+        link_peak = memory.measure_link_gbs(dev)
+        variants = {}
+        for name, transform, keep in (("offload_kept", memory.MemoryPlan.with_offload_kept,
+                                       engine.keep_layers), ("keep_all", None, None)):
+            saved = engine.plan_transform, engine.keep_layers, engine.spill
+            engine.plan_transform = transform
+            if name == "keep_all":
+                engine.keep_layers, engine.spill = None, "recompute"
+            torch.cuda.reset_peak_memory_stats(dev)
+            t = timed_steps(train_step)
+            variants[name] = (t, torch.cuda.max_memory_allocated(dev) / 2**20,
+                              engine.last_plan.summary())
+            engine.plan_transform, engine.keep_layers, engine.spill = saved
+        t_kept = variants["offload_kept"][0]
+        mem_line.update(
+            spill_ms_per_step=ms / args.steps,
+            offload_kept_ms_per_step=t_kept / args.steps,
+            offload_kept_plan=variants["offload_kept"][2],
+            offload_kept_peak_hbm_mib=variants["offload_kept"][1],
+            keep_all_ms_per_step=variants["keep_all"][0] / args.steps,
+            keep_all_peak_hbm_mib=variants["keep_all"][1],
+            exposed_copy_fraction=max(0.0, (ms - t_kept) / ms) if spill_bytes else 0.0,
+            offload_bytes_per_step=spill_bytes,
+            copy_stream_ms_per_step=copy_ms,
+            host_link_gbs=(spill_bytes / (copy_ms / 1e3) / 1e9) if copy_ms else None,
+            host_link_peak_gbs=link_peak,
+            link_gbs_seen_by_planner=engine.link_gbs, layer_ms_seen_by_planner=engine.layer_ms)
     value = tokens / (ms / 1000.0)
 
     # e2e: the drop-in boundary from pinned host batches
@@ -434,10 +479,19 @@ def run_ours(args, rank, world, local):
 
     for i in range(min(2, args.warmup)):
         e2e_step(i)
-    e2e_ms = timed_steps(e2e_step)
+    e2e_ms = timed_steps(e2e_step, "e2e")
     e2e_value = tokens / (e2e_ms / 1000.0)
     h2d = sum(a.numel() * a.element_size() for i in timed for a in pinned[i]) / args.steps
 
+    # per rank: (host enqueue ms, device ms) per step of the timed and e2e loops
+    mine = [host_ms["timed"][0] / args.steps, host_ms["timed"][1] / args.steps,
+            host_ms["e2e"][0] / args.steps, host_ms["e2e"][1] / args.steps]
+    if world > 1:
+        allr = [torch.zeros(4, dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(allr, torch.tensor(mine, dtype=torch.float64, device=dev))
+        per_rank = [[round(float(x), 3) for x in t.tolist()] for t in allr]
+    else:
+        per_rank = [[round(x, 3) for x in mine]]
     if rank != 0:
         return
     hbm, tf_burst, tf_sust, src = peaks()
@@ -480,6 +534,8 @@ def run_ours(args, rank, world, local):
                      f"{profiled_ms / args.steps:.3f} ms per step, per-op sum "
                      f"{sum(r['ms_per_step'] for r in table.values()):.3f} ms"),
         "clocks": clk,
+        "per_rank_ms_per_step": {"fields": ["host_enqueue", "device", "e2e_host", "e2e_device"],
+                                 "ranks": per_rank},
     }
     if world == 1 and not args.no_cpu_baseline:
         cpu = CpuSample()

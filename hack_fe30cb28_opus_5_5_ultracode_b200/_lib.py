@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libqlora_sm100a.so")
 HEADER = os.path.join(os.path.dirname(_HERE), "include", "qlora_sm100.h")
 
 _SCALARS = {"int": ctypes.c_int, "int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64,
+            "uint32_t": ctypes.c_uint32,
             "long long": ctypes.c_longlong,
             "float": ctypes.c_float, "double": ctypes.c_double, "void": None}
 

@@ -547,6 +547,50 @@ static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   launch_k(attn_bwd_kernel<T, D>, grid, dim3(128), smem, s, a);
 }
 
+static std::atomic<bool> g_attn_det{false};
+void attn_set_deterministic(bool on) { g_attn_det.store(on); }
+bool attn_deterministic() { return g_attn_det.load(); }
+
+// The deterministic backward's sums: thread = (row, head, 4 columns). dq of query row p (position
+// in its sequence) adds the contributions of key blocks 0 .. p / 128; dk / dv of key row j add,
+// over the GQA group's query heads g and the 1024-query chunks c that exist for j's key block,
+// slot (g, c), in that order.
+__global__ void attn_bwd_det_reduce_kernel(const float* __restrict__ parts, AttnBwdC a) {
+  pdl_enter();  // the backward kernel's partials are complete and visible from here on
+  const int hh_all = a.HQ + 2 * a.HKV;
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)a.n * hh_all * 32) return;
+  const int c4 = (int)(idx % 32), hh = (int)((idx / 32) % hh_all);
+  const int64_t row = idx / (32 * (int64_t)hh_all);
+  int lo = 0, hi = a.B;  // the sequence holding row: cu[lo] <= row < cu[lo + 1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (a.cu_seqlens[mid] <= row) lo = mid; else hi = mid;
+  }
+  const int start = a.cu_seqlens[lo], len = a.cu_seqlens[lo + 1] - start;
+  const int p = (int)(row - start), kb = p / 128;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [&](const float* src) {
+    const float4 v = *reinterpret_cast<const float4*>(src + 4 * c4);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  };
+  if (hh < a.HQ) {
+    const float* q = parts + (row * a.HQ + hh) * 128;
+    for (int b = 0; b <= kb; ++b) add(q + (int64_t)b * a.n * a.HQ * 128);
+    *reinterpret_cast<float4*>(a.dq + (row * a.HQ + hh) * 128 + 4 * c4) = acc;
+  } else {
+    const int which = (hh - a.HQ) / a.HKV, j = (hh - a.HQ) % a.HKV;
+    const int group = a.HQ / a.HKV, nch = (a.max_len + 1023) / 1024;
+    const int chunks = (len - kb * 128 + 1023) / 1024;
+    const float* base = parts + attn_part_q_floats(a) + which * attn_part_kv_floats(a) +
+                        (row * a.HKV + j) * 128;
+    for (int g = 0; g < group; ++g)
+      for (int c = 0; c < chunks; ++c) add(base + ((int64_t)g * nch + c) * a.n * a.HKV * 128);
+    float* dst = which == 0 ? a.dk : a.dv;
+    *reinterpret_cast<float4*>(dst + (row * a.HKV + j) * 128 + 4 * c4) = acc;
+  }
+}
+
 int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   if (a.D != 128 && a.D != 64) return QL_STATUS_UNSUPPORTED;
   if (a.n < 0 || a.B < 0 || a.HKV <= 0 || a.HQ % a.HKV != 0 || a.max_len < 0) return QL_STATUS_BAD_ARG;
@@ -556,7 +600,26 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   if ((reinterpret_cast<uintptr_t>(a.dq) | reinterpret_cast<uintptr_t>(a.dk) |
        reinterpret_cast<uintptr_t>(a.dv)) & 15)
     return QL_STATUS_BAD_ARG;
+  const bool tc = a.D == 128 && (a.dtype == QL_F16 || a.dtype == QL_BF16) && g_attn_impl.load() != 1;
+  if (a.partials != nullptr && (!tc || (reinterpret_cast<uintptr_t>(a.partials) & 15)))
+    return QL_STATUS_UNSUPPORTED;  // the deterministic form: tcgen05 kernels, 16-byte aligned
   ProfScope prof(PK_ATTN_BWD, 0, 0, s);
+  if (a.partials != nullptr) {  // every contribution to its own slot, then one ordered sum
+    if (a.max_len == 0) return QL_STATUS_OK;
+    const int64_t rows = (int64_t)a.n * a.HQ;
+    if (a.dtype == QL_F16)
+      launch_k(attn_bwd_pre_kernel<__half, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
+               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ);
+    else
+      launch_k(attn_bwd_pre_kernel<__nv_bfloat16, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
+               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ);
+    const int st = attn_bwd_tc(a, s);
+    if (st != QL_STATUS_OK) return st;
+    const int64_t threads = (int64_t)a.n * (a.HQ + 2 * a.HKV) * 32;
+    launch_k(attn_bwd_det_reduce_kernel, dim3((unsigned)cdiv(threads, 256)), dim3(256), 0, s,
+             (const float*)a.partials, a);
+    return launched(3);
+  }
   // gradients accumulate atomically: start from zero
   if (cudaMemsetAsync(a.dq, 0, sizeof(float) * a.n * a.HQ * a.D, s) != cudaSuccess ||
       cudaMemsetAsync(a.dk, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess ||

@@ -508,8 +508,17 @@ __global__ void __launch_bounds__(320, 1)
       fence_proxy_async_smem();
       if (key < len) {
         const int64_t row = ((int64_t)(start + key) * a.HKV + kvh) * 128;
-        bulk_reduce_add_f32(a.dk + row, reinterpret_cast<const float*>(stk), 512);
-        bulk_reduce_add_f32(a.dv + row, reinterpret_cast<const float*>(stv), 512);
+        if (a.partials == nullptr) {
+          bulk_reduce_add_f32(a.dk + row, reinterpret_cast<const float*>(stk), 512);
+          bulk_reduce_add_f32(a.dv + row, reinterpret_cast<const float*>(stv), 512);
+        } else {  // this (query head of the group, chunk)'s own slot
+          const int group = a.HQ / a.HKV, nch = (int)cdiv(a.max_len, TB_QCH);
+          const int64_t slot = ((int64_t)(h - kvh * group) * nch + chunk) * a.n * a.HKV * 128;
+          float* pk = a.partials + attn_part_q_floats(a) + slot;
+          float* pv = pk + attn_part_kv_floats(a);
+          bulk_store(pk + row, reinterpret_cast<const float*>(stk), 512);
+          bulk_store(pv + row, reinterpret_cast<const float*>(stv), 512);
+        }
       }
       bulk_commit();
       bulk_wait<0>();
@@ -540,8 +549,11 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(dqs_full, i & 1, err)) break;
 #pragma unroll
         for (int t = lane; t < TB_BQ; t += 32)
-          if (q0 + t < len)
-            bulk_reduce_add_f32(a.dq + ((int64_t)(start + q0 + t) * a.HQ + h) * 128, sDQ + t * 128, 512);
+          if (q0 + t < len) {
+            const int64_t off = ((int64_t)(start + q0 + t) * a.HQ + h) * 128;
+            if (a.partials == nullptr) bulk_reduce_add_f32(a.dq + off, sDQ + t * 128, 512);
+            else bulk_store(a.partials + (int64_t)kb * a.n * a.HQ * 128 + off, sDQ + t * 128, 512);
+          }
         bulk_commit();
       }
     }

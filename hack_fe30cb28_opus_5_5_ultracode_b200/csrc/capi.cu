@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "ops.h"
+#include "philox.cuh"
 
 namespace {
 __device__ int g_status_word = 0;  // QL_STATUS_TIMEOUT etc., recorded by kernels
@@ -52,21 +53,57 @@ void smem_optin(const void* kernel, int bytes) {
     have = bytes;
 }
 
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 static std::atomic<bool> g_pdl{true};
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 void set_pdl(bool on) { g_pdl.store(on, std::memory_order_relaxed); }
 
 int* status_word() {
-  // one address per device; cudaGetSymbolAddress is cheap after the first call per device
-  static int* cache[64] = {nullptr};
+  // one address per device, looked up once (host threads may race to fill an entry: both store
+  // the same address)
+  static std::atomic<int*> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (cache[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
-    cache[dev] = static_cast<int*>(p);
+  int* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_status_word) != cudaSuccess) return nullptr;
+    p = static_cast<int*>(addr);
+    cache[dev].store(p, std::memory_order_release);
   }
-  return cache[dev];
+  return p;
+}
+
+// The bounded-wait probe (ql_wait_probe): one CTA, two roles. Warp 0 waits on an mbarrier that
+// nothing arrives on, under limit_ns, so its wait runs out and records QL_STATUS_TIMEOUT; warp 1
+// waits on another such barrier under the full limit and gives up as soon as it sees the status
+// recorded (what every other role of a kernel does when one role times out). Each role adds 1 to
+// *returned when it has left its wait.
+__global__ void wait_probe_kernel(int* err, unsigned long long limit_ns, int* returned) {
+  __shared__ __align__(8) uint64_t bars[2];
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0 && warp < 2) {
+    mbar_wait(&bars[warp], 0, err, warp == 0 ? limit_ns : QL_WAIT_NS);
+    atomicAdd(returned, 1);
+  }
 }
 }  // namespace ql
 
@@ -131,6 +168,23 @@ int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, 
   return done(ql::gemm_nf4(A, lda, *W, layout, C, ldc, bias, M, in_dtype, out_dtype, accumulate,
                            residual, ql::status_word(), stream),
               "ql_gemm_nf4");
+}
+
+int ql_wait_probe(int64_t limit_ns, int* returned, cudaStream_t stream) {
+  if (returned == nullptr || limit_ns < 1000000 || limit_ns > (int64_t)ql::QL_WAIT_NS)
+    return done(QL_STATUS_BAD_ARG, "ql_wait_probe");
+  int* err = ql::status_word();
+  if (err == nullptr) return fail(QL_STATUS_CUDA, "ql_wait_probe");
+  ql::wait_probe_kernel<<<1, 64, 0, stream>>>(err, (unsigned long long)limit_ns, returned);
+  return done(ql::launched(1), "ql_wait_probe");
+}
+
+uint32_t ql_dropout_keep_threshold(float p_keep) {
+  ql::DropoutArgs d{};
+  d.threads = 1;
+  d.p_keep = p_keep;
+  ql::prepare_dropout(d);
+  return d.keep_below;
 }
 
 int ql_set_pdl(int on) {
@@ -237,8 +291,13 @@ int colsum_scratch(float** out) {
 int ql_lora_colsum_noalloc(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype,
                            int64_t n, int ncols, int rank, float scale, int transpose, float* out,
                            cudaStream_t stream) {
+  if (rank != 16) {
+    g_last_error = "ql_lora_colsum_noalloc: rank " + std::to_string(rank) +
+                   " is not supported (rank 16 only)";
+    return QL_STATUS_UNSUPPORTED;
+  }
   if (n < 0 || ncols <= 0) return done(QL_STATUS_BAD_ARG, "ql_lora_colsum_noalloc");
-  const int64_t need = (int64_t)ql::lora_colsum_splits(n, ncols) * ncols * rank;
+  const int64_t need = (int64_t)ql::lora_colsum_splits(n, ncols) * (int64_t)ncols * 16;
   if (need > QL_COLSUM_STATIC_FLOATS) {
     g_last_error = "ql_lora_colsum_noalloc: this shape needs " + std::to_string(need) +
                    " floats of scratch, the static scratch holds " +
@@ -300,6 +359,19 @@ int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream) {
 
 int ql_exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t stream) {
   return done(ql::exp2_fma_eval(x, y, n, stream), "ql_exp2_fma_eval");
+}
+
+int64_t ql_attn_bwd_partials_floats(int32_t n, int32_t max_len, int32_t HQ, int32_t HKV) {
+  if (n <= 0 || max_len <= 0 || HKV <= 0 || HQ % HKV != 0) return 0;
+  ql_attn_bwd_args a{};
+  a.n = n; a.max_len = max_len; a.HQ = HQ; a.HKV = HKV;
+  return ql::attn_part_q_floats(a) + 2 * ql::attn_part_kv_floats(a);
+}
+
+int ql_attn_set_deterministic(int on) {
+  if (on != 0 && on != 1) return done(QL_STATUS_BAD_ARG, "ql_attn_set_deterministic");
+  ql::attn_set_deterministic(on != 0);
+  return QL_STATUS_OK;
 }
 
 int ql_attn_set_impl(int impl) {

@@ -127,42 +127,137 @@ __global__ void __launch_bounds__(CE_THREADS) ce_rows_kernel(CeRowsC a) {
   }
 }
 
+// Adds 8 consecutive logits (columns col0 .. col0+7, in increasing order) to a running state:
+// one rescale for the group's maximum, then the exponentials against it; the first maximum
+// keeps the argmax.
+__device__ __forceinline__ void stat_add8(OnlineStat& st, const float* v, int64_t col0) {
+  float m8 = v[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) m8 = fmaxf(m8, v[j]);
+  if (m8 > st.m) {
+    const float f = st.m == -CUDART_INF_F ? 0.f : __expf(st.m - m8);
+    st.s *= f;
+    st.t *= f;
+    st.m = m8;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (v[j] > st.best) {
+      st.best = v[j];
+      st.arg = col0 + j;
+    }
+    const float e = __expf(v[j] - st.m);
+    st.s += e;
+    st.t += e * v[j];
+  }
+}
+
+__device__ __forceinline__ OnlineStat warp_merge(OnlineStat st) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    OnlineStat b;
+    b.m = __shfl_xor_sync(0xffffffffu, st.m, o);
+    b.s = __shfl_xor_sync(0xffffffffu, st.s, o);
+    b.t = __shfl_xor_sync(0xffffffffu, st.t, o);
+    b.best = __shfl_xor_sync(0xffffffffu, st.best, o);
+    b.arg = __shfl_xor_sync(0xffffffffu, st.arg, o);
+    stat_merge(st, b);
+  }
+  return st;
+}
+
+constexpr int CE_PIECE_THREADS = 128;  // per row: a CTA of 4 warps (~8 CTAs, 32 warps per SM)
+constexpr int CE_PIECE_UNROLL = 4;     // 16-byte vectors each thread has in flight
+
+// One CTA of 4 warps per row of a vocabulary piece: each thread walks the row in 8-column vectors
+// (16-byte loads, four in flight) with its own running state; the states are merged across the
+// warp, the CTA and into the row's state from the earlier pieces. Then, for rows with a target,
+// exp(x - new max) over the row in place, and the fp32 gradient accumulator moved to the new max
+// (acc = alpha (acc + part)).
 template <typename T>
-__global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
+__global__ void __launch_bounds__(CE_PIECE_THREADS) ce_piece_kernel(CePieceC a) {
   pdl_enter();
-  __shared__ OnlineStat sh[CE_THREADS / 32];
-  __shared__ float xt_sh;
+  __shared__ OnlineStat sh[CE_PIECE_THREADS / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;
   T* src = reinterpret_cast<T*>(a.logits) + row * a.ld;
   const int64_t target = a.target[row];
   const int64_t local = target - a.v0;
   const bool here = target >= 0 && local >= 0 && local < a.width;
-  if (threadIdx.x == 0) xt_sh = here ? to_f<T>(src[local]) : 0.f;
+  const float xt = here ? to_f<T>(src[local]) : 0.f;  // read before the row is overwritten
+  OnlineStat st{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0};
+  const bool vec = (reinterpret_cast<uintptr_t>(src) % 16 == 0);
+  const int64_t nvec = vec ? a.width / 8 : 0;
+  constexpr int STEP = CE_PIECE_THREADS * CE_PIECE_UNROLL;
+  for (int64_t i0 = threadIdx.x; i0 < nvec; i0 += STEP) {
+    uint4 u[CE_PIECE_UNROLL];
+#pragma unroll
+    for (int k = 0; k < CE_PIECE_UNROLL; ++k) {
+      const int64_t i = i0 + (int64_t)k * CE_PIECE_THREADS;
+      if (i < nvec) u[k] = *reinterpret_cast<const uint4*>(src + i * 8);
+    }
+#pragma unroll
+    for (int k = 0; k < CE_PIECE_UNROLL; ++k) {
+      const int64_t i = i0 + (int64_t)k * CE_PIECE_THREADS;
+      if (i < nvec) {
+        const T* h = reinterpret_cast<const T*>(&u[k]);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = to_f<T>(h[j]);
+        stat_add8(st, v, a.v0 + i * 8);
+      }
+    }
+  }
+  for (int64_t c = nvec * 8 + threadIdx.x; c < a.width; c += CE_PIECE_THREADS)
+    stat_add(st, to_f<T>(src[c]), a.v0 + c);
+  st = warp_merge(st);
+  if (lane == 0) sh[warp] = st;
+  __syncthreads();
+  st = sh[0];
+#pragma unroll
+  for (int w = 1; w < CE_PIECE_THREADS / 32; ++w) stat_merge(st, sh[w]);
   OnlineStat prev{a.state[row * 4], a.state[row * 4 + 1], a.state[row * 4 + 2],
                   a.state[row * 4 + 3], a.best_idx[row]};
-  OnlineStat st = row_stats<T>(src, a.width, a.v0);
-  st = block_merge(st, sh);
   const float m_old = prev.m;
   // earlier pieces hold smaller columns, so on a tie the earlier maximum stays (stat_merge)
   stat_merge(prev, st);
   st = prev;
+  __syncthreads();  // every thread has read the row state before thread 0 rewrites it
   if (threadIdx.x == 0) {
     a.state[row * 4] = st.m;
     a.state[row * 4 + 1] = st.s;
     a.state[row * 4 + 2] = st.t;
     a.state[row * 4 + 3] = st.best;
     a.best_idx[row] = st.arg;
-    if (here) a.xt[row] = xt_sh;
+    if (here) a.xt[row] = xt;
     if (row < a.n_sup) a.alpha[row] = m_old == -CUDART_INF_F ? 0.f : __expf(m_old - st.m);
   }
   if (here && a.wt != nullptr) {
     const T* w = reinterpret_cast<const T*>(a.w) + local * a.H;
     T* dst = reinterpret_cast<T*>(a.wt) + row * a.H;
-    for (int c = threadIdx.x; c < a.H; c += blockDim.x) dst[c] = w[c];
+    for (int c = threadIdx.x; c < a.H; c += CE_PIECE_THREADS) dst[c] = w[c];
   }
   if (row < a.n_sup) {
     const float m = st.m;
-    for (int64_t c = threadIdx.x; c < a.width; c += blockDim.x)
+    for (int64_t i0 = threadIdx.x; i0 < nvec; i0 += STEP) {
+      uint4 u[CE_PIECE_UNROLL];
+#pragma unroll
+      for (int k = 0; k < CE_PIECE_UNROLL; ++k) {
+        const int64_t i = i0 + (int64_t)k * CE_PIECE_THREADS;
+        if (i < nvec) u[k] = *reinterpret_cast<const uint4*>(src + i * 8);
+      }
+#pragma unroll
+      for (int k = 0; k < CE_PIECE_UNROLL; ++k) {
+        const int64_t i = i0 + (int64_t)k * CE_PIECE_THREADS;
+        if (i < nvec) {
+          T* h = reinterpret_cast<T*>(&u[k]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[j] = from_f<T>(__expf(to_f<T>(h[j]) - m));
+          *reinterpret_cast<uint4*>(src + i * 8) = u[k];
+        }
+      }
+    }
+    for (int64_t c = nvec * 8 + threadIdx.x; c < a.width; c += CE_PIECE_THREADS)
       src[c] = from_f<T>(__expf(to_f<T>(src[c]) - m));
     if (a.acc != nullptr) {
       // the gradient accumulator, moved to this piece's running max: acc = alpha (acc + part),
@@ -170,7 +265,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_piece_kernel(CePieceC a) {
       float* acc = a.acc + row * a.H;
       const float* part = a.part_valid ? a.part + row * a.H : nullptr;
       const float alpha = m_old == -CUDART_INF_F ? 0.f : __expf(m_old - m);
-      for (int c = threadIdx.x; c < a.H; c += blockDim.x) {
+      for (int c = threadIdx.x; c < a.H; c += CE_PIECE_THREADS) {
         if (m_old == -CUDART_INF_F) acc[c] = 0.f;
         else acc[c] = alpha * (acc[c] + (part != nullptr ? part[c] : 0.f));
       }
@@ -218,8 +313,9 @@ int ce_piece(const CePieceC& a, cudaStream_t s) {
   ProfScope prof(PK_CE, 0, (double)a.rows * a.width * 2 + (double)a.n_sup * a.width * 2 +
                                (a.acc != nullptr ? (double)a.n_sup * a.H * (a.part_valid ? 12 : 4) : 0),
                  s);
-  if (a.dtype == QL_F16) ce_piece_kernel<__half><<<a.rows, CE_THREADS, 0, s>>>(a);
-  else if (a.dtype == QL_BF16) ce_piece_kernel<__nv_bfloat16><<<a.rows, CE_THREADS, 0, s>>>(a);
+  const unsigned grid = (unsigned)a.rows;
+  if (a.dtype == QL_F16) launch_k(ce_piece_kernel<__half>, dim3(grid), dim3(CE_PIECE_THREADS), 0, s, a);
+  else if (a.dtype == QL_BF16) launch_k(ce_piece_kernel<__nv_bfloat16>, dim3(grid), dim3(CE_PIECE_THREADS), 0, s, a);
   else return QL_STATUS_BAD_ARG;
   return launched(1);
 }

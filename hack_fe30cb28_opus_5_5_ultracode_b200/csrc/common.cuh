@@ -29,6 +29,8 @@ int launched(int kernels);
 void smem_optin(const void* kernel, int bytes);
 // Host: whether launches carry the programmatic-dependent-launch attribute (ql_set_pdl).
 bool pdl_enabled();
+// Host: the current device's SM count (looked up once per device).
+int sm_count();
 
 // ---------------------------------------------------------------------------------------------
 // element conversion
@@ -97,14 +99,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of the given parity to complete. Returns false (and records a timeout in
-// *err) if it has not after QL_WAIT_NS; the caller then stops issuing work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// *err) if it has not after limit_ns (QL_WAIT_NS unless a caller passes less); the caller then
+// stops issuing work. A wait also gives up as soon as another role has recorded a status.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          unsigned long long limit_ns = QL_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++spins & 255u) == 0) {
-      if (global_ns() - t0 > QL_WAIT_NS) {
+      if (global_ns() - t0 > limit_ns) {
         raise_status(err, QL_STATUS_TIMEOUT);
         return false;
       }
@@ -173,6 +177,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 // a multiple of 16.
 __device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const float* ssrc, uint32_t bytes) {
   asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(gdst)),
+               "r"(smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
+// Bulk copy: global[dst .. dst + bytes) = shared[src .. src + bytes) (bulk async-group of the
+// issuing thread; same alignment rules as the reduction).
+__device__ __forceinline__ void bulk_store(float* gdst, const float* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
                    reinterpret_cast<uint64_t>(gdst)),
                "r"(smem_u32(ssrc)), "r"(bytes)
                : "memory");

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstring>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -116,9 +117,37 @@ static inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Tensor maps already encoded, per host thread: a map is a pure function of its encode
+// arguments, and the step asks for the same ones again and again (the static weights every step,
+// the layer workspaces' buffers in every layer), while an encode costs a driver call. Keyed by
+// every argument; cleared when it grows past a few thousand entries.
+struct MapKey {
+  uintptr_t ptr;
+  int64_t rows, cols, ld;
+  int box_rows, kind;  // kind: 0 K-major 128B-swizzle fp16, 1 the same bf16, 2 / 3 store maps
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld &&
+           box_rows == o.box_rows && kind == o.kind;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.ptr * 0x9E3779B97F4A7C15ull;
+    for (uint64_t v : {(uint64_t)k.rows, (uint64_t)k.cols, (uint64_t)k.ld,
+                       (uint64_t)(k.box_rows * 8 + k.kind)})
+      h = (h ^ v) * 0x100000001B3ull;
+    return (size_t)h;
+  }
+};
+static inline std::unordered_map<MapKey, CUtensorMap, MapKeyHash>& map_cache() {
+  thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  if (cache.size() > 4096) cache.clear();
+  return cache;
+}
+
 // A row-major [rows, cols] 16-bit matrix with row stride ld (elements), boxes of box_rows x 64.
-static inline int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
-                           int64_t ld, int box_rows, bool bf16) {
+static inline int encode_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
+                                    int64_t ld, int box_rows, bool bf16) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return QL_STATUS_CUDA;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -132,10 +161,24 @@ static inline int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t row
   return r == CUDA_SUCCESS ? QL_STATUS_OK : QL_STATUS_CUDA;
 }
 
+static inline int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
+                                  int64_t ld, int box_rows, bool bf16) {
+  const MapKey key{reinterpret_cast<uintptr_t>(ptr), rows, cols, ld, box_rows, bf16 ? 1 : 0};
+  auto& cache = map_cache();
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *map = it->second;
+    return QL_STATUS_OK;
+  }
+  const int rc = encode_kmajor_map(map, ptr, rows, cols, ld, box_rows, bf16);
+  if (rc == QL_STATUS_OK) cache.emplace(key, *map);
+  return rc;
+}
+
 // A row-major [rows, cols] 16-bit C with row stride ld (elements), boxes of 32 x 32 staged with
 // the 64-byte swizzle (rows of 64 bytes).
-static inline int make_store_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols, int64_t ld,
-                          bool bf16) {
+static inline int encode_store_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols,
+                                   int64_t ld, bool bf16) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return QL_STATUS_CUDA;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -147,6 +190,20 @@ static inline int make_store_map(CUtensorMap* map, void* ptr, int64_t rows, int6
                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+static inline int make_store_map(CUtensorMap* map, void* ptr, int64_t rows, int64_t cols,
+                                 int64_t ld, bool bf16) {
+  const MapKey key{reinterpret_cast<uintptr_t>(ptr), rows, cols, ld, 32, bf16 ? 3 : 2};
+  auto& cache = map_cache();
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *map = it->second;
+    return QL_STATUS_OK;
+  }
+  const int rc = encode_store_map(map, ptr, rows, cols, ld, bf16);
+  if (rc == QL_STATUS_OK) cache.emplace(key, *map);
+  return rc;
 }
 
 static inline int num_sms() {

@@ -125,6 +125,7 @@ struct BwdWs {
   float* dxq;    // [n, rank]
   float* dxv;
   void* da;      // [n, H]
+  float* attn_part;  // the deterministic attention backward's partials, or null
 };
 
 BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
@@ -148,6 +149,11 @@ BwdWs carve_bwd(const ql_layer_desc& L, Bump& b) {
   w.dxq = (float*)b.take(n * L.rank * 4);
   w.dxv = (float*)b.take(n * L.rank * 4);
   w.da = b.take(n * L.H * e);
+  w.attn_part = nullptr;
+  if (attn_deterministic() && L.D == 128) {
+    const int64_t floats = ql_attn_bwd_partials_floats(L.n, L.max_len, L.HQ, L.HKV);
+    if (floats > 0) w.attn_part = (float*)b.take(floats * 4);
+  }
   return w;
 }
 
@@ -325,7 +331,7 @@ int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float*
   ab.q = S.q; ab.k = S.k; ab.v = S.v; ab.out = S.out; ab.dout = w.dout; ab.lse = S.lse;
   ab.cu_seqlens = L.cu_seqlens; ab.dvec = w.dvec; ab.dq = w.dq; ab.dk = w.dk; ab.dv = w.dv;
   ab.scale = L.scale; ab.n = L.n; ab.B = L.B; ab.max_len = L.max_len; ab.HQ = L.HQ;
-  ab.HKV = L.HKV; ab.D = L.D; ab.dtype = dt;
+  ab.HKV = L.HKV; ab.D = L.D; ab.dtype = dt; ab.partials = w.attn_part;
   QL_TRY(attn_bwd(ab, s));
   RopeBwdC rb{};
   rb.dq = w.dq; rb.dk = w.dk; rb.dv = w.dv; rb.cos = L.cos; rb.sin = L.sin; rb.pos = L.pos;

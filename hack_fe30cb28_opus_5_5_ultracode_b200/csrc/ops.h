@@ -63,6 +63,18 @@ int ce_finish(const CeFinishC& a, cudaStream_t s);
 namespace ql {
 typedef ql_attn_fwd_args AttnFwdC;
 typedef ql_attn_bwd_args AttnBwdC;
+// The deterministic attention backward's partials (D = 128): the dq contributions of each
+// 128-key block, [ceil(max_len / 128)][n][HQ][128]; then the dk, and the dv, contributions of
+// each (query head of the GQA group, 1024-query chunk), [HQ / HKV][ceil(max_len / 1024)][n][HKV]
+// [128] each.
+__host__ __device__ inline int64_t attn_part_q_floats(const AttnBwdC& a) {
+  return (int64_t)((a.max_len + 127) / 128) * a.n * a.HQ * 128;
+}
+__host__ __device__ inline int64_t attn_part_kv_floats(const AttnBwdC& a) {
+  return (int64_t)(a.HQ / a.HKV) * ((a.max_len + 1023) / 1024) * a.n * a.HKV * 128;
+}
+void attn_set_deterministic(bool on);
+bool attn_deterministic();
 int attn_fwd(const AttnFwdC& a, cudaStream_t s);
 int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (launch only)
 int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s);  // D = 128 on tcgen05 (main kernel only)

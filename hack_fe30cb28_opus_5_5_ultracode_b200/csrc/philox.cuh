@@ -40,13 +40,36 @@ struct DropoutArgs {
   int vec;             // 16 / sizeof(LoRA input element): 4 for fp32
   int drop_q, drop_v;  // which masks exist
   FastDiv div_threads; // division by `threads`, set by the launcher (prepare_dropout)
+  uint32_t keep_below; // a draw u is kept iff u < keep_below (set by prepare_dropout)
 };
+
+// Host: the keep test u * 2^-32 + 2^-33 < p_keep, evaluated in fp32 as the dropout kernel does
+// (u rounded to fp32, an exact power-of-two product, one rounded add), is non-decreasing in u, so
+// the kept draws are exactly u < U* for the least u whose value reaches p_keep; found by
+// bisection over [0, 2^32) with the same fp32 operations (p_keep < 1: the largest u reaches 1).
+inline float keep_value(uint32_t u) {
+  volatile float f = static_cast<float>(u);  // round to nearest, as __uint2float_rn
+  volatile float g = f * 2.3283064365386963e-10f;
+  volatile float h = g + 1.1641532182693481e-10f;
+  return h;
+}
+
+inline uint32_t keep_threshold(float p_keep) {
+  uint64_t lo = 0, hi = 0xFFFFFFFFull;  // keep_value(hi) = 1 >= p_keep
+  while (lo < hi) {
+    const uint64_t mid = (lo + hi) >> 1;
+    if (keep_value((uint32_t)mid) >= p_keep) hi = mid;
+    else lo = mid + 1;
+  }
+  return (uint32_t)lo;
+}
 
 // Host: completes a DropoutArgs before launch. The element indices of a mask stay below 2^32
 // (B T H < 4.3e9), so the per-element index math runs in 32 bits.
 inline bool prepare_dropout(DropoutArgs& d) {
   if (d.threads <= 0 || d.threads > 0xFFFFFFFFll) return false;
   d.div_threads = make_fastdiv((uint32_t)d.threads);
+  d.keep_below = d.p_keep < 1.0f ? keep_threshold(d.p_keep) : 0xFFFFFFFFu;
   return true;
 }
 
@@ -84,8 +107,8 @@ __device__ __forceinline__ uint32_t keep4(int64_t e0, int64_t ctr, const Dropout
                      (((e & (uint32_t)(d.vec - 1))) >> 2);    // + (e % VEC) / 4
   const uint4 r = philox4x32_10(make_uint4((uint32_t)c, (uint32_t)(c >> 32), thread, 0u),
                                 (uint32_t)(uint64_t)d.seed, (uint32_t)((uint64_t)d.seed >> 32));
-  return (keep_from_u(r.x, d.p_keep) ? 1u : 0u) | (keep_from_u(r.y, d.p_keep) ? 2u : 0u) |
-         (keep_from_u(r.z, d.p_keep) ? 4u : 0u) | (keep_from_u(r.w, d.p_keep) ? 8u : 0u);
+  const uint32_t t = d.keep_below;  // == keep_from_u(u, p_keep) for every u (prepare_dropout)
+  return (r.x < t ? 1u : 0u) | (r.y < t ? 2u : 0u) | (r.z < t ? 4u : 0u) | (r.w < t ? 8u : 0u);
 }
 
 }  // namespace ql

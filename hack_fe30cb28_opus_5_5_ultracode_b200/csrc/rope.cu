@@ -306,8 +306,7 @@ struct RopeShape {
 };
 
 static RopeShape rope_shape(int64_t n) {
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sm_count();
   const int64_t waves = cdiv(n, (int64_t)sms * ROPE_MAXR);
   RopeShape r;
   r.rows = (int)cdiv(n, (int64_t)sms * waves);

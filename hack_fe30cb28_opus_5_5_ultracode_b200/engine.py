@@ -27,7 +27,7 @@ import torch
 from . import _lib, memory, ops
 
 HEAD_CHUNK = 4096          # head rows per block (their per-row statistics and accumulators)
-HEAD_L2_BYTES = 24 << 20   # 16-bit logits of one vocabulary chunk of a head block: L2-resident
+HEAD_L2_BYTES = 40 << 20   # 16-bit logits of one vocabulary chunk of a head block (L2-resident)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -434,7 +434,9 @@ class FusedQwen2:
         """spill / keep_layers / activation_budget_mib: the activation-memory plan of each step
         (memory.plan_memory): by default every layer keeps its saved activations in HBM; with a
         budget (MiB for the saved sets) or a forced keep_layers the first layers spill by
-        recompute or by offload to pinned host memory."""
+        recompute, by offload to pinned host memory, or "auto": offload only the layers whose
+        copies hide behind compute (from the host link's measured bandwidth and the previous
+        step's time per layer) and recompute the others."""
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -458,6 +460,7 @@ class FusedQwen2:
         self.lm_w = self.embed if lm.data_ptr() == inner.embed_tokens.weight.data_ptr() \
             and lm.dtype == dtype else lm.to(dtype).contiguous()
         self.V = self.lm_w.shape[0]
+        self.head = VocabHead(self.lm_w, dtype)
         self.rope = RopeTable(inner.rotary_emb, spec.D, self.device)
         self.head_chunk = head_chunk
         # fp32 LoRA weights (PEFT owns them) and one 16-bit shadow buffer refreshed per step
@@ -490,6 +493,11 @@ class FusedQwen2:
             else int(activation_budget_mib) << 20
         self._host_ring = None     # pinned host memory of offloaded layers (grow-only)
         self._copy_stream = None
+        self.link_gbs = None       # host link bandwidth, measured at the first "auto" plan
+        self._step_events = None   # (start, end) of the last step, for the time per layer
+        self.layer_ms = None       # the last completed step's time per layer
+        self.last_offload = None   # the last step's _Offload (copy bytes and timing), if any
+        self.plan_transform = None  # optional plan -> plan hook (the bench times variants)
         self._scratch_h = None
         self.last_plan = None
         self.last_offload_bytes = 0  # host-link bytes of the last backward's offload plan
@@ -565,9 +573,21 @@ class FusedQwen2:
         cos, sin = self.rope.table(max(packed.max_len, 1))
         layer_bytes, _ = memory.saved_set_bytes(n, spec0.H, spec0.HQ, spec0.HKV, spec0.D,
                                                 spec0.I, self._esize())
+        if self.spill == memory.AUTO:
+            if self.link_gbs is None:
+                self.link_gbs = memory.measure_link_gbs(self.device)
+            ev = self._step_events
+            if ev is not None and ev[1].query():  # the previous step has finished: no wait
+                self.layer_ms = ev[0].elapsed_time(ev[1]) / len(self.layers)
         plan = memory.plan_memory(len(self.layers), layer_bytes, self.activation_budget,
-                                  self.spill, self.keep_layers)
+                                  self.spill, self.keep_layers, self.link_gbs, self.layer_ms)
+        if self.plan_transform is not None:
+            plan = self.plan_transform(plan)
         self.last_plan = plan
+        if self.spill == memory.AUTO:
+            self._step_events = (torch.cuda.Event(enable_timing=True),
+                                 torch.cuda.Event(enable_timing=True))
+            self._step_events[0].record()
         arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device,
                             None if self._arena_busy else self._arena_buf, plan)
         offload = _Offload(self, arena, plan) if memory.OFFLOAD in plan.modes and n else None
@@ -657,7 +677,7 @@ class FusedQwen2:
         vocabulary-piece form of solution/engine.py:1498-1547). Tokens are taken supervised
         first, in blocks of up to head_chunk rows; within a block the vocabulary is walked in
         chunks small enough that a chunk's logits stay in L2 between the kernels that use them
-        (_head_block): no [rows, V] logits buffer exists. Returns (dh in head order, loss)."""
+        (VocabHead): no [rows, V] logits buffer exists. Returns (dh in head order, loss)."""
         n, H = h.shape
         dev, dt = self.device, self.dtype
         order = packed.head_order
@@ -675,75 +695,13 @@ class FusedQwen2:
         for r0 in range(0, n, self.head_chunk):
             r1 = min(n, r0 + self.head_chunk)
             sup = max(0, min(r1, n_sup) - r0)
-            dhn = self._head_block(hn[r0:r1], targets[r0:r1], sup, tok_loss[r0:r1],
-                                   entropy[r0:r1], correct[r0:r1])
+            dhn = self.head.block(hn[r0:r1], targets[r0:r1], sup, tok_loss[r0:r1],
+                                  entropy[r0:r1], correct[r0:r1])
             if sup:
                 ops.rms_bwd(dhn, hp[r0:r0 + sup], rstd[r0:r0 + sup], self.norm_w, dtype=dt,
                             grad_scale=inv, out=dhp[r0:r0 + sup])
         stats.order, stats.tok_loss, stats.entropy, stats.correct = order, tok_loss, entropy, correct
         return dhp, tok_loss.sum() * inv
-
-    def vocab_chunk(self, rows):
-        """Vocabulary entries per chunk of a head block of `rows` rows: as many as keep the
-        chunk's 16-bit logits within HEAD_L2_BYTES (they are written, rewritten and read again
-        by three kernels in a row), in multiples of 64, evened out over the chunks."""
-        def cdiv(a, b):
-            return -(-a // b)
-
-        width = max(1024, HEAD_L2_BYTES // (self._esize() * max(rows, 1)) // 64 * 64)
-        return cdiv(cdiv(self.V, cdiv(self.V, width)), 64) * 64
-
-    def _head_buffers(self, rows, width, sup):
-        """Grow-only buffers of a head block (reused from step to step)."""
-        H, dt, dev = self.layers[0].H, self.dtype, self.device
-        b = getattr(self, "_hb", None)
-        need = (rows, width, sup)
-        if b is None or any(x < y for x, y in zip(b["shape"], need)):
-            rows_, width_, sup_ = (max(x, y) for x, y in zip(b["shape"] if b else (0, 0, 0), need))
-            b = {"shape": (rows_, width_, sup_),
-                 "logits": torch.empty(rows_ * width_, device=dev, dtype=dt),
-                 "state": torch.empty((rows_, 4), device=dev, dtype=torch.float32),
-                 "best": torch.empty(rows_, device=dev, dtype=torch.int64),
-                 "xt": torch.empty(rows_, device=dev, dtype=torch.float32),
-                 "alpha": torch.empty(max(sup_, 1), device=dev, dtype=torch.float32),
-                 "acc": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
-                 "part": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
-                 "wt": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
-                 "dhn": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
-                 "init": torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")], device=dev)}
-            self._hb = b
-        return b
-
-    def _head_block(self, hn, targets, sup, tok_loss, entropy, correct):
-        """One block of head rows (the first `sup` have a target) over the whole vocabulary,
-        chunk by chunk: (1) the chunk's logits = hn . W_chunk^T on the tensor cores; (2) ce_piece
-        carries each row's online max / sum exp / sum exp * x / argmax across chunks, writes
-        exp(x - running max) over the supervised rows' logits, copies the target's weight row
-        and moves the fp32 gradient accumulator to the new max, folding in the previous chunk's
-        product (acc = alpha (acc + part)); (3) part = exp(x - max) . W_chunk on the tensor cores.
-        ce_finish then gives loss, entropy, accuracy and dhn = (acc + part) / sum - W_target
-        (16-bit) for the supervised rows, which it returns."""
-        rows, H = hn.shape
-        width = self.vocab_chunk(rows)
-        b = self._head_buffers(rows, width, sup)
-        state, best, xt = b["state"][:rows], b["best"][:rows], b["xt"][:rows]
-        state.copy_(b["init"].expand(rows, 4))
-        logits = b["logits"][:rows * width].view(rows, width)
-        acc = b["acc"][:sup] if sup else None
-        part = b["part"][:sup] if sup else None
-        wt, dhn = b["wt"][:sup], b["dhn"][:sup]
-        for v0 in range(0, self.V, width):
-            w = min(width, self.V - v0)
-            W = self.lm_w[v0:v0 + w]
-            chunk = logits[:, :w]
-            ops.gemm(hn, W, out=chunk)
-            ops.ce_piece(chunk, W, targets, state, best, xt, b["alpha"], wt, v0, sup, acc=acc,
-                         part=part, part_valid=v0 > 0 and sup > 0, H=H)
-            if sup:
-                ops.gemm(chunk[:sup], W, out=part, b_kn=True)
-        ops.ce_finish(state, best, xt, targets, tok_loss, entropy, correct, b["acc"], wt, dhn,
-                      sup, part=part)
-        return dhn
 
     def run_layer(self, index, packed, drop, h, dh3):
         """One decoder layer forward and backward through the layer ABI (ql_layer_forward,
@@ -841,7 +799,89 @@ class FusedQwen2:
             reducer.finish(self._comm)
             grads.copy_(self._comm)
         self.last_offload_bytes = offload.bytes_moved if offload is not None else 0
+        self.last_offload = offload
+        if self._step_events is not None:
+            self._step_events[1].record()
         return views
+
+
+class VocabHead:
+    """The lm_head + cross-entropy over the vocabulary in chunks, for a block of head rows (the
+    vocabulary-piece form of the reference's head, solution/engine.py:1498-1547 and
+    solution/kernels.py:401-479, with pieces sized for L2 instead of streamed from the host):
+      (1) logits of the chunk = hn . W_chunk^T on the tensor cores (16-bit, into a chunk buffer
+          that stays in L2 until (3) has read it);
+      (2) ce_piece: each row's online max / sum exp / sum exp * x / argmax carried across the
+          chunks; exp(x - running max) written over the supervised rows' logits; the target's
+          weight row copied; the fp32 gradient accumulator moved to the new max with the previous
+          chunk's product folded in, acc = alpha (acc + part);
+      (3) part = exp(x - max) . W_chunk on the tensor cores (fp32, split-K allowed: the GEMM never
+          reads its output).
+    ce_finish then gives loss, entropy, accuracy and dhn = (acc + part) / sum - W_target.
+    W is read from HBM once per chunk (the second GEMM finds it in L2); no [rows, V] logits
+    buffer exists. Buffers grow to the largest block seen and are reused from step to step."""
+
+    def __init__(self, lm_w, dtype, l2_bytes=HEAD_L2_BYTES):
+        self.lm_w, self.dtype, self.l2_bytes = lm_w, dtype, l2_bytes
+        self.V, self.H = lm_w.shape
+        self.device = lm_w.device
+        self._buf = None
+
+    def chunk_width(self, rows):
+        """Vocabulary entries per chunk: as many as keep the chunk's 16-bit logits within
+        l2_bytes, in multiples of 64, evened out over the chunks."""
+        def cdiv(a, b):
+            return -(-a // b)
+
+        esize = torch.empty((), dtype=self.dtype).element_size()
+        width = max(1024, self.l2_bytes // (esize * max(rows, 1)) // 64 * 64)
+        return cdiv(cdiv(self.V, cdiv(self.V, width)), 64) * 64
+
+    def _buffers(self, rows, width, sup):
+        H, dt, dev = self.H, self.dtype, self.device
+        b = self._buf
+        need = (rows, width, sup)
+        if b is None or any(x < y for x, y in zip(b["shape"], need)):
+            rows_, width_, sup_ = (max(x, y) for x, y in zip(b["shape"] if b else (0, 0, 0), need))
+            b = {"shape": (rows_, width_, sup_),
+                 "logits": torch.empty(rows_ * width_, device=dev, dtype=dt),
+                 "state": torch.empty((rows_, 4), device=dev, dtype=torch.float32),
+                 "best": torch.empty(rows_, device=dev, dtype=torch.int64),
+                 "xt": torch.empty(rows_, device=dev, dtype=torch.float32),
+                 "alpha": torch.empty(max(sup_, 1), device=dev, dtype=torch.float32),
+                 "acc": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
+                 "part": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
+                 "wt": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
+                 "dhn": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
+                 "init": torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")], device=dev)}
+            self._buf = b
+        return b
+
+    def block(self, hn, targets, sup, tok_loss, entropy, correct):
+        """One block of head rows hn [rows, H] (16-bit, the first `sup` rows have a target):
+        writes tok_loss / entropy / correct [rows] and returns dhn [sup, H] (16-bit), the
+        gradient of the summed token losses w.r.t. hn."""
+        rows, H = hn.shape
+        width = self.chunk_width(rows)
+        b = self._buffers(rows, width, sup)
+        state, best, xt = b["state"][:rows], b["best"][:rows], b["xt"][:rows]
+        state.copy_(b["init"].expand(rows, 4))
+        logits = b["logits"][:rows * width].view(rows, width)
+        acc = b["acc"][:sup] if sup else None
+        part = b["part"][:sup] if sup else None
+        wt, dhn = b["wt"][:sup], b["dhn"][:sup]
+        for v0 in range(0, self.V, width):
+            w = min(width, self.V - v0)
+            W = self.lm_w[v0:v0 + w]
+            chunk = logits[:, :w]
+            ops.gemm(hn, W, out=chunk)
+            ops.ce_piece(chunk, W, targets, state, best, xt, b["alpha"], wt, v0, sup, acc=acc,
+                         part=part, part_valid=v0 > 0 and sup > 0, H=H)
+            if sup:
+                ops.gemm(chunk[:sup], W, out=part, b_kn=True)
+        ops.ce_finish(state, best, xt, targets, tok_loss, entropy, correct, b["acc"], wt, dhn,
+                      sup, part=part)
+        return dhn
 
 
 class _SavedArena:
@@ -902,6 +942,7 @@ class _Offload:
         self.slot_free = {}   # ring slot -> event after which it may be overwritten
         self.arrived = {}     # layer -> event: its set is back in HBM
         self.bytes_moved = 0
+        self.copy_events = []  # (start, end) timing events of every copy, on the copy stream
 
     def _dev(self, i):
         lb = self.arena.layer_bytes
@@ -926,9 +967,12 @@ class _Offload:
         done.record()
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(done)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(self.stream)
             self._host(i).copy_(self._dev(i), non_blocking=True)
-            out = torch.cuda.Event()
+            out = torch.cuda.Event(enable_timing=True)
             out.record(self.stream)
+            self.copy_events.append((t0, out))
         self.slot_free[self.plan.slot(i)] = out
         self.bytes_moved += self.arena.layer_bytes
 
@@ -937,11 +981,18 @@ class _Offload:
         with torch.cuda.stream(self.stream):
             if ev is not None:
                 self.stream.wait_event(ev)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(self.stream)
             self._dev(i).copy_(self._host(i), non_blocking=True)
-            got = torch.cuda.Event()
+            got = torch.cuda.Event(enable_timing=True)
             got.record(self.stream)
+            self.copy_events.append((t0, got))
         self.arrived[i] = got
         self.bytes_moved += self.arena.layer_bytes
+
+    def copy_ms(self):
+        """Milliseconds the copy stream spent copying this step (after the copies finished)."""
+        return sum(a.elapsed_time(b) for a, b in self.copy_events)
 
     def start_backward(self):
         # the ring slots' last forward copies must finish before the backward refills them

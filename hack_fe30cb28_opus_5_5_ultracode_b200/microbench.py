@@ -2,7 +2,7 @@
 on the launching stream (warm-up, then `--iters` launches, each input set larger than L2):
 
     python -m hack_fe30cb28_opus_5_5_ultracode_b200.microbench [--tokens 1090] [--iters 20]
-        [--only gemm|dequant|attn|rms|glu|rope|ce]
+        [--only gemm|dequant|attn|rms|glu|rope|ce|head]
 
 Prints one JSON line per kernel and shape: average launch time, algorithmic FLOPs or bytes per
 launch, achieved TFLOP/s or GB/s and the fraction of the measured peak (MEASURED_PEAKS.json).
@@ -236,6 +236,33 @@ def main():
         sec = _time(lambda i: ops.lora_grads(jobs), args.iters)
         _report("lora_grads (4 products)", [n, (HQ + HKV) * D + 2 * H], sec,
                 nbytes=n * ((HQ + HKV) * D + 2 * H) * 2)
+    if want("head"):
+        # the head over a block of rows (70 % with a target): the chunked, L2-resident form the
+        # step runs (VocabHead) against materialised [rows, V] logits (logits GEMM, ce_rows,
+        # data-gradient GEMM), same inputs
+        from .engine import VocabHead
+
+        W = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(dt)
+        hn = torch.randn(n, H, device=dev, generator=g).to(dt)
+        sup = int(0.7 * n)
+        tgt = torch.randint(0, V, (n,), device=dev, generator=g)
+        tgt[sup:] = -100
+        stats = [torch.empty(n, device=dev), torch.empty(n, device=dev),
+                 torch.empty(n, device=dev, dtype=torch.int32)]
+        head = VocabHead(W, dt)
+        flops = 2.0 * V * H * (n + sup)
+        sec = _time(lambda i: head.block(hn, tgt, sup, *stats), args.iters)
+        _report(f"head chunked ({head.chunk_width(n)}-entry chunks)", [n, V, H], sec, flops=flops)
+        logits = torch.empty(n, V, device=dev, dtype=dt)
+
+        def materialised(i):
+            ops.gemm(hn, W, out=logits)
+            ops.ce_rows(logits, tgt, write_grad=True, loss=stats[0], entropy=stats[1],
+                        correct=stats[2])
+            ops.gemm(logits[:sup], W, b_kn=True)
+
+        sec = _time(materialised, args.iters)
+        _report("head materialised logits", [n, V, H], sec, flops=flops)
     if want("ce"):
         logits = [torch.randn(n, V, device=dev, generator=g).to(dt) for _ in range(2)]
         tgt = torch.randint(0, V, (n,), device=dev, generator=g)

@@ -10,6 +10,7 @@ from ._lib import call
 
 _DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 INT_MAX = 2147483647
+STATUS_TIMEOUT = 4  # QL_STATUS_TIMEOUT of include/qlora_sm100.h: a kernel gave up a bounded wait
 
 
 def dtype_code(dtype):
@@ -20,7 +21,12 @@ def dtype_code(dtype):
 
 
 def stream_ptr():
-    return torch.cuda.current_stream().cuda_stream
+    """The current CUDA stream of the current device, as a raw pointer (called for every
+    launch: the raw lookup skips torch.cuda.current_stream()'s Python-level device resolution)."""
+    try:
+        return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())
+    except AttributeError:  # pragma: no cover - other torch builds
+        return torch.cuda.current_stream().cuda_stream
 
 
 def _ptr(t):
@@ -114,6 +120,12 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
 def gemm_set_mode(mode):
     """Tile kind of the GEMMs: 0 per-shape cost model, 1 single-CTA tiles, 2 2-SM pair tiles."""
     call("ql_gemm_set_mode", int(mode))
+
+
+def attn_set_deterministic(on):
+    """The layer backward's attention gradients summed in a fixed order (bit-reproducible run to
+    run) or by fp32 bulk reductions (default; ql_attn_set_deterministic)."""
+    call("ql_attn_set_deterministic", 1 if on else 0)
 
 
 def attn_set_impl(impl):
@@ -441,10 +453,17 @@ def attn_fwd(q, k, v, cu_seqlens, max_len, scale, out=None, lse=None):
 
 
 def attn_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len, scale, dq=None, dk=None, dv=None,
-             dvec=None):
+             dvec=None, deterministic=False):
+    """Reference _attn_bwd (engine.py:864-869): dq, dk, dv (fp32; dk / dv per KV head). With
+    deterministic, each contribution goes to its own slot of a partials workspace and one kernel
+    sums them in a fixed order (D = 128)."""
     n, HQ, D = q.shape
     HKV = k.shape[1]
     dev = q.device
+    parts = None
+    if deterministic:
+        floats = int(_lib.lib().ql_attn_bwd_partials_floats(n, int(max_len), HQ, HKV))
+        parts = torch.empty(max(floats, 4), device=dev, dtype=torch.float32)
     dq = dq if dq is not None else torch.empty((n, HQ, D), device=dev, dtype=torch.float32)
     dk = dk if dk is not None else torch.empty((n, HKV, D), device=dev, dtype=torch.float32)
     dv = dv if dv is not None else torch.empty((n, HKV, D), device=dev, dtype=torch.float32)
@@ -453,7 +472,7 @@ def attn_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len, scale, dq=None, dk=No
                        dout=_ptr(dout), lse=_ptr(lse), cu_seqlens=_ptr(cu_seqlens),
                        dvec=_ptr(dvec), dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv),
                        scale=float(scale), n=n, B=cu_seqlens.numel() - 1, max_len=int(max_len),
-                       HQ=HQ, HKV=HKV, D=D, dtype=dtype_code(q.dtype))
+                       HQ=HQ, HKV=HKV, D=D, dtype=dtype_code(q.dtype), partials=_ptr(parts))
     call("ql_attn_bwd", ctypes_ref(args), stream_ptr())
     return dq, dk, dv
 

@@ -32,7 +32,7 @@ def _is_nf4(module):
 
 def is_supported(model):
     """Qwen2 + silu + default RoPE, every projection NF4, LoRA (one active adapter, no DoRA) on
-    q_proj and v_proj only (solution/patch.py:154-203)."""
+    q_proj and v_proj only (solution/patch.py:154-203), heads of 64 or 128."""
     if not isinstance(model, torch.nn.Module) or not hasattr(model, "get_base_model"):
         return False
     causal = model.get_base_model()
@@ -49,8 +49,8 @@ def is_supported(model):
         return False
     if not torch.cuda.is_available() or inner.norm.weight.device.type != "cuda":
         return False
-    if getattr(config, "head_dim", None) not in (None, 128) and \
-            config.hidden_size // config.num_attention_heads != 128:
+    head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+    if head_dim not in (64, 128):  # the attention kernels of this library
         return False
     for layer in inner.layers:
         attn, mlp = layer.self_attn, layer.mlp

@@ -54,6 +54,12 @@ int ql_profile_read(double* count, double* ms, double* flops, double* bytes);
  * results in their first instruction) or not (0: plain stream order). A measurement switch with
  * no counterpart in the reference: per-operation event timings add up only with it off. */
 int ql_set_pdl(int on);
+/* Exercises the bounded waits' timeout path (a test entry point, no counterpart in the
+ * reference): a one-CTA kernel whose first role waits on an mbarrier nothing arrives on, under
+ * limit_ns (1 ms .. 2 s), and so records QL_STATUS_TIMEOUT in the device status word; its second
+ * role gives up its own wait when it sees that status. Each role adds 1 to the device int
+ * *returned when it has left its wait; ql_device_status then reports the timeout. */
+int ql_wait_probe(int64_t limit_ns, int* returned, cudaStream_t stream);
 
 /* ---- NF4 dequantisation ------------------------------------------------------------------
  * Replaces NF4Weight.dequant_into / NF4Group.dequant_into (solution/engine.py:103-109,
@@ -169,6 +175,11 @@ int ql_rms_bwd(const ql_rms_bwd_args* args, cudaStream_t stream);
  * torch_dropout_keep_kernel (solution/kernels.py:129-135). */
 int ql_dropout_keep(int8_t* out, int64_t nelem, int64_t seed, int64_t ctr, int64_t threads,
                     float p_keep, int vec, cudaStream_t stream);
+/* The integer form of the keep test the kernels use: a Philox draw u is kept iff
+ * u < ql_dropout_keep_threshold(p_keep), which equals the fp32 test u * 2^-32 + 2^-33 < p_keep of
+ * solution/kernels.py:108-126 for every u (p_keep < 1; 0xFFFFFFFF for p_keep >= 1, where the
+ * kernels keep everything without drawing). Host only. */
+uint32_t ql_dropout_keep_threshold(float p_keep);
 
 /* ---- qkv + LoRA + RoPE ---------------------------------------------------------------------
  * cos / sin: fp32 [positions, D/2] (the first half of the model's rotary table); pos: int32 [n].
@@ -361,6 +372,10 @@ typedef struct {
   float* dv;
   float scale;
   int32_t n, B, max_len, HQ, HKV, D, dtype;
+  float* partials;      /* NULL, or ql_attn_bwd_partials_floats(...) floats: the deterministic
+                           form (D = 128 tcgen05 kernels): each contribution to dq / dk / dv goes
+                           to its own slot and one kernel sums the slots in a fixed order, instead
+                           of fp32 reductions whose order varies from run to run */
 } ql_attn_bwd_args;
 
 int ql_attn_fwd(const ql_attn_fwd_args* args, cudaStream_t stream);
@@ -371,6 +386,14 @@ int ql_attn_bwd(const ql_attn_bwd_args* args, cudaStream_t stream);
  * No counterpart in the reference (one attention implementation there); tests and the
  * microbenchmark compare the two. */
 int ql_attn_set_impl(int impl);
+/* Size in floats of the deterministic attention backward's partials for a batch of n tokens
+ * whose longest sequence has max_len tokens (D = 128). */
+int64_t ql_attn_bwd_partials_floats(int32_t n, int32_t max_len, int32_t HQ, int32_t HKV);
+/* Whether ql_layer_backward runs the attention backward in its deterministic form (1) or with
+ * fp32 bulk reductions (0, the default: faster, not bit-reproducible run to run); the layer
+ * workspace grows by the partials when on. A process-wide switch with no counterpart in the
+ * reference, for reproducible gradients (the memory-plan and determinism tests). */
+int ql_attn_set_deterministic(int on);
 /* y[i] = 2^x[i] by the FMA-pipe polynomial the tcgen05 attention forward's softmax uses for half
  * of its off-diagonal exponentials (a check of its error bound against the GPU's exp2; no counterpart in
  * the reference). */

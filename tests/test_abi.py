@@ -58,3 +58,12 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "missing.so"))
     with pytest.raises(ImportError):
         _lib.lib()
+
+
+def test_status_constant_matches_the_header():
+    import re
+
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
+
+    text = open(_lib.HEADER, encoding="utf-8").read()
+    assert int(re.search(r"QL_STATUS_TIMEOUT\s*=\s*(\d+)", text).group(1)) == ops.STATUS_TIMEOUT

@@ -509,3 +509,53 @@ def test_exp2_fma_error_bound():
               torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert torch.all(yl > 0) and torch.all(yl < 3e-38)
+
+
+# ---------------------------------------------------------------------------------------------
+# bounded waits
+# ---------------------------------------------------------------------------------------------
+def test_a_wait_that_runs_out_reports_a_timeout_and_the_context_stays_usable():
+    """ql_wait_probe: one role's mbarrier wait is never satisfied and runs out after 50 ms; the
+    other role gives up its own wait on seeing the recorded status; both return, the host reads
+    QL_STATUS_TIMEOUT from the device status word, and the next launches run normally."""
+    import time
+
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib
+
+    o = ops()
+    assert o.device_status() == 0
+    returned = torch.zeros(1, device=DEV, dtype=torch.int32)
+    t0 = time.perf_counter()
+    _lib.call("ql_wait_probe", int(50e6), returned.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert int(returned.item()) == 2 and 0.04 < elapsed < 1.9
+    assert o.device_status() == o.STATUS_TIMEOUT
+    assert o.device_status() == 0  # (read with clear: the word was reset)
+    a = torch.randn(256, 128, device=DEV).half()
+    b = torch.randn(192, 128, device=DEV).half()
+    close(o.gemm(a, b), a.float() @ b.float().t(), 1e-2)
+    assert o.device_status() == 0
+
+
+@pytest.mark.parametrize("lengths", [[7, 130, 1, 64], [300, 257, 1024, 33], [2100, 700, 5]])
+def test_attention_backward_deterministic_form(lengths):
+    """The deterministic attention backward (contributions to their own slots, one ordered sum):
+    bit-identical from run to run, and equal to the bulk-reduction form to fp32 rounding (long
+    sequences: several 128-key blocks and 1024-query chunks per slot set)."""
+    o = ops()
+    torch.manual_seed(2)
+    HQ, HKV, D = 12, 2, 128
+    cu = torch.tensor([0, *np.cumsum(lengths).tolist()], device=DEV, dtype=torch.int32)
+    n = sum(lengths)
+    q, k, v = (torch.randn(n, h, D, device=DEV).half() for h in (HQ, HKV, HKV))
+    out, lse = o.attn_fwd(q, k, v, cu, max(lengths), D ** -0.5)
+    dout = torch.randn_like(q)
+    runs = [o.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths), D ** -0.5, deterministic=True)
+            for _ in range(2)]
+    fast = o.attn_bwd(dout, q, k, v, out, lse, cu, max(lengths), D ** -0.5)
+    for a, b, c in zip(runs[0], runs[1], fast):
+        assert torch.equal(a, b)
+        close(a, c, 1e-4)
+    assert o.device_status() == 0

@@ -311,3 +311,26 @@ def test_packed_partition_without_device_reads_matches_a_stable_sort():
         want = torch.argsort((p.targets < 0).to(torch.int8), stable=True)
         assert torch.equal(p.head_order, want), lengths
         assert p.n_supervised == int((p.targets >= 0).sum())
+
+
+def test_auto_plan_offloads_only_what_the_link_can_hide():
+    """'auto': with a measured host link and time per layer, every stride-th spilled layer is
+    offloaded (counted from the highest spilled one, needed first in the backward) and the others
+    recomputed; offloaded layers alternate over two ring slots, recomputed ones share one; with no
+    measurement yet everything spilled is recomputed."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+
+    lb, _ = memory.saved_set_bytes(25000, 1536, 12, 2, 128, 8960, 2)  # 1.4 GB per layer
+    # 1.4 GB at 55 GB/s = 25 ms against ~3 ms of forward per layer: every 9th spilled layer
+    assert memory.offload_stride(lb, 55.0, 9.25) == 9
+    assert memory.offload_stride(lb, None, 9.25) is None
+    p = memory.plan_memory(28, lb, budget_bytes=10 * lb, spill="auto", link_gbs=55.0,
+                           layer_ms=9.25)
+    assert p.modes.count("keep") == 7 and p.ring == 3 and p.slots == 10
+    off = [i for i, m in enumerate(p.modes) if m == "offload"]
+    assert off == [2, 11, 20] and all(p.modes[i] == "recompute" for i in range(21) if i not in off)
+    assert [p.slot(i) for i in off] == [8, 9, 8] and {p.slot(i) for i in (0, 1, 3)} == {7}
+    assert memory.plan_memory(28, lb, budget_bytes=10 * lb, spill="auto").summary() == \
+        {"keep": 7, "recompute": 21}
+    kept = p.with_offload_kept()
+    assert kept.summary() == {"keep": 10, "recompute": 18} and kept.slots == 11

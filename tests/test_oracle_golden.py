@@ -102,3 +102,26 @@ def test_ce_vs_reference(golden):
     np.testing.assert_allclose(ent, g["entropy"], rtol=1e-3, atol=1e-3)
     assert np.array_equal(cor, g["correct"])
     np.testing.assert_allclose(grad, g["grad"].astype(np.float32), rtol=1e-3, atol=1e-3)
+
+
+def test_integer_keep_threshold_equals_the_fp32_keep_test():
+    """The kernels keep a Philox draw u iff u < ql_dropout_keep_threshold(p): the same set as the
+    fp32 test u * 2^-32 + 2^-33 < p (solution/kernels.py:108-126), checked at the threshold and
+    around it, and on a random sample of draws, for the dropout rates in use."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib
+
+    lib = _lib.lib()
+
+    def keep(u, p):
+        f = u.astype(np.float32) * np.float32(2.3283064365386963e-10) + np.float32(1.1641532182693481e-10)
+        return f.astype(np.float32) < np.float32(p)
+
+    rng = np.random.default_rng(5)
+    for p_drop in (0.05, 0.1, 0.25, 0.3, 0.5, 0.9, 1e-7):
+        p = np.float32(1.0 - p_drop)
+        t = int(lib.ql_dropout_keep_threshold(float(p)))
+        near = np.arange(max(t - 300, 0), min(t + 300, 2**32), dtype=np.uint64).astype(np.uint32)
+        sample = rng.integers(0, 2**32, 100000, dtype=np.uint64).astype(np.uint32)
+        for u in (near, sample):
+            assert np.array_equal(keep(u, p), u < t), p_drop
+    assert lib.ql_dropout_keep_threshold(1.0) == 0xFFFFFFFF

@@ -60,3 +60,41 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     Y = torch.zeros(n, 16, device=DEV, dtype=torch.float16)
     with pytest.raises(_lib.QLError, match="floats of scratch"):
         _colsum("ql_lora_colsum_noalloc", X, Y, 1.0, False)
+
+
+def test_noalloc_accepts_a_shape_that_fills_its_scratch_exactly():
+    """One split of 65,536 columns x rank 16 needs exactly the 1,048,576 floats of the scratch:
+    accepted, and equal to the workspace entry point's result (twice in a row)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib
+
+    n, ncols = 1, 65536
+    assert _lib.lib().ql_lora_colsum_workspace(n, ncols, 16) == 1048576
+    g = torch.Generator(device=DEV).manual_seed(3)
+    X = torch.randn(n, ncols, device=DEV, generator=g).half()
+    Y = torch.randn(n, 16, device=DEV, generator=g).half()
+    ws = torch.empty(1048576, device=DEV, dtype=torch.float32)
+    ref = _colsum("ql_lora_colsum", X, Y, 1.0, False, ws)
+    for _ in range(2):
+        got = _colsum("ql_lora_colsum_noalloc", X, Y, 1.0, False)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_noalloc_rejects_bad_layouts_and_ranks():
+    """Column counts that are not whole 8-column groups, and ranks other than 16, are refused
+    with a status (BAD_ARG, UNSUPPORTED) before anything launches."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
+
+    lib = _lib.lib()
+    X = torch.zeros(4, 104, device=DEV, dtype=torch.float16)  # rows of 104, 100 of them used
+    Y = torch.zeros(4, 16, device=DEV, dtype=torch.float16)
+    out = torch.zeros(100, 16, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.ql_lora_colsum_noalloc(X.data_ptr(), 104, ops.dtype_code(X.dtype), Y.data_ptr(),
+                                    ops.dtype_code(Y.dtype), 4, 100, 16, 1.0, 0, out.data_ptr(),
+                                    stream)
+    assert rc == 1  # QL_STATUS_BAD_ARG: 100 columns are not whole 8-column groups
+    rc = lib.ql_lora_colsum_noalloc(X.data_ptr(), 104, ops.dtype_code(X.dtype), Y.data_ptr(),
+                                    ops.dtype_code(Y.dtype), 4, 96, 8, 1.0, 0, out.data_ptr(),
+                                    stream)
+    assert rc == 3 and b"rank 8" in lib.ql_last_error()  # QL_STATUS_UNSUPPORTED
