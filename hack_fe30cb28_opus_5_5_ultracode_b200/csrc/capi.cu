@@ -424,6 +424,58 @@ int ql_layer_backward(const ql_layer_desc* layer, const ql_layer_saved* saved, c
               "ql_layer_backward");
 }
 
+int ql_layers_set_step(ql_layer_desc* descs, int count, const ql_layer_desc* step,
+                       const int64_t* ctr_q, const int64_t* ctr_v) {
+  if (descs == nullptr || step == nullptr || count < 0) return fail(QL_STATUS_BAD_ARG, "ql_layers_set_step");
+  for (int i = 0; i < count; ++i) {
+    ql_layer_desc& d = descs[i];
+    d.cos = step->cos; d.sin = step->sin; d.pos = step->pos; d.cu_seqlens = step->cu_seqlens;
+    d.tok = step->tok; d.seed = step->seed; d.threads = step->threads;
+    d.ctr_q = ctr_q != nullptr ? ctr_q[i] : 0;
+    d.ctr_v = ctr_v != nullptr ? ctr_v[i] : 0;
+    d.p_keep = step->p_keep; d.keep_scale = step->keep_scale; d.vec = step->vec;
+    d.drop_q = step->drop_q; d.drop_v = step->drop_v;
+    d.n = step->n; d.B = step->B; d.max_len = step->max_len;
+  }
+  return QL_STATUS_OK;
+}
+
+int ql_layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                      float* const* h_out, void* workspace, int64_t workspace_bytes,
+                      cudaStream_t stream) {
+  if (descs == nullptr || saved == nullptr || h_out == nullptr || count < 0)
+    return fail(QL_STATUS_BAD_ARG, "ql_layers_forward");
+  int* err = ql::status_word();
+  for (int i = 0; i < count; ++i) {
+    const int rc = ql::layer_forward(descs[i], saved[i], h_out[i], workspace, workspace_bytes, err,
+                                     stream);
+    if (rc != QL_STATUS_OK) return done(rc, "ql_layers_forward");
+  }
+  return QL_STATUS_OK;
+}
+
+int ql_layers_backward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                       float* dh, void* dh16, float* dh_alt, void* dh16_alt, float* grads,
+                       const int64_t* grad_offsets, int skip_first_input_grad, void* workspace,
+                       int64_t workspace_bytes, cudaStream_t stream) {
+  if (descs == nullptr || saved == nullptr || grads == nullptr || grad_offsets == nullptr ||
+      count < 0)
+    return fail(QL_STATUS_BAD_ARG, "ql_layers_backward");
+  int* err = ql::status_word();
+  float* cur[2] = {dh, dh_alt};
+  void* cur16[2] = {dh16, dh16_alt};
+  int c = 0;
+  for (int i = count - 1; i >= 0; --i) {
+    const bool need = !(i == 0 && skip_first_input_grad);
+    const int rc = ql::layer_backward(descs[i], saved[i], cur[c], cur16[c], grads + grad_offsets[i],
+                                      need ? cur[1 - c] : nullptr, need ? cur16[1 - c] : nullptr,
+                                      workspace, workspace_bytes, err, stream);
+    if (rc != QL_STATUS_OK) return done(rc, "ql_layers_backward");
+    c = 1 - c;
+  }
+  return QL_STATUS_OK;
+}
+
 }  // extern "C"
 
 extern "C" {

@@ -483,7 +483,14 @@ class FusedQwen2:
                 if g.split:
                     raise ValueError("double-quantised weights whose absmax2 blocks straddle "
                                      "two members of a group are not supported")
-        self.descs = [self._layer_desc(spec) for spec in self.layers]
+        # the layers' descriptors in one contiguous array (views of it in self.descs), so that
+        # the all-layers ABI calls can take them at once
+        L = len(self.layers)
+        desc_t = _lib.STRUCTS["ql_layer_desc"]
+        self.desc_array = (desc_t * L)(*[self._layer_desc(spec) for spec in self.layers])
+        self.descs = [self.desc_array[i] for i in range(L)]
+        self._step_desc = desc_t()
+        self._grad_offsets = (ctypes.c_int64 * L)(*[self.offsets[4 * i] for i in range(L)])
         # the forward's dequantised weights, per layer, read again by the backward
         self.weight_elems = int(_lib.lib().ql_layer_weight_elems(ctypes.byref(self.descs[0])))
         self.w16 = torch.empty(len(self.layers) * self.weight_elems, device=self.device,
@@ -600,25 +607,34 @@ class FusedQwen2:
             ops.embed(packed.ids, self.embed, out=h)
             if self.w16 is not None:  # this step's 16-bit weights, every layer, few launches
                 self._dequant_all()
-        saved = []
+        L = len(self.layers)
         drops = self._drops(packed)
-        for spec, desc in zip(self.layers, self.descs):
-            drop = drops[spec.index]
-            self._set_step(desc, packed, drop, cos, sin)
-            sv = arena.saved(spec.index)
+        self._set_all_steps(packed, drops, cos, sin)
+        saved_arr = (_lib.STRUCTS["ql_layer_saved"] * L)()
+        for i in range(L):
+            saved_arr[i] = arena.saved(i)
             if self.w16 is not None:
-                sv.w16 = self.w16[spec.index * self.weight_elems:].data_ptr()
-                sv.w16_ready = 1
-            if n:
+                saved_arr[i].w16 = self.w16[i * self.weight_elems:].data_ptr()
+                saved_arr[i].w16_ready = 1
+        saved = [(saved_arr[i], drops[i]) for i in range(L)]
+        if n and all(m == memory.KEEP for m in plan.modes):
+            # every layer keeps its saved set: the whole forward in one call
+            ws = self._workspace_for(self.descs[0])
+            h_out = (ctypes.c_void_p * L)(*[arena.h(i + 1).data_ptr() for i in range(L)])
+            _lib.call("ql_layers_forward", ctypes.addressof(self.desc_array),
+                      ctypes.addressof(saved_arr), L, ctypes.addressof(h_out), ws.data_ptr(),
+                      ws.numel(), ops.stream_ptr())
+        elif n:
+            for i, desc in enumerate(self.descs):
                 if offload is not None:
-                    offload.before_forward(spec.index)
+                    offload.before_forward(i)
                 ws = self._workspace_for(desc)
-                _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
-                          arena.h(spec.index + 1).data_ptr(), ws.data_ptr(), ws.numel(),
-                          ops.stream_ptr())
+                _lib.call("ql_layer_forward", ctypes.addressof(desc),
+                          ctypes.addressof(saved_arr[i]), arena.h(i + 1).data_ptr(),
+                          ws.data_ptr(), ws.numel(), ops.stream_ptr())
                 if offload is not None:
-                    offload.after_forward(spec.index)
-            saved.append((sv, drop))
+                    offload.after_forward(i)
+        saved = (saved_arr, saved)
         h = arena.h(len(self.layers))
         dhp, loss = self._head(h, packed, denom, stats) if n else (None, None)
         if loss is None:
@@ -658,6 +674,17 @@ class FusedQwen2:
         ws = self._workspace_for(desc)
         _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
                   self._scratch_h.data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
+
+    def _set_all_steps(self, packed, drops, cos, sin):
+        """The step-dependent fields of every layer's descriptor (ql_layers_set_step): the
+        shared ones through one template descriptor, each layer's dropout counters."""
+        L = len(self.layers)
+        self._set_step(self._step_desc, packed, drops[0], cos, sin)
+        ctr_q = (ctypes.c_int64 * L)(*[d.ctr_q for d in drops])
+        ctr_v = (ctypes.c_int64 * L)(*[d.ctr_v for d in drops])
+        _lib.call("ql_layers_set_step", ctypes.addressof(self.desc_array), L,
+                  ctypes.addressof(self._step_desc), ctypes.addressof(ctr_q),
+                  ctypes.addressof(ctr_v))
 
     def _set_step(self, desc, packed, drop, cos, sin):
         """The step-dependent fields of a layer's descriptor."""
@@ -747,7 +774,7 @@ class FusedQwen2:
     def _backward(self, packed, saved, dhp, grad):
         n = packed.n
         H = self.layers[0].H
-        arena, per_layer, offload = saved
+        arena, (saved_arr, per_layer), offload = saved
         plan = arena.plan
         if arena.owned:  # the next forward may reuse the arena (queued after this backward)
             self._arena_busy = False
@@ -768,11 +795,21 @@ class FusedQwen2:
             cur = 0
             if offload is not None:
                 offload.start_backward()
-            for spec in reversed(self.layers):
+            L = len(self.layers)
+            self._set_all_steps(packed, [d for _, d in per_layer], cos, sin)
+            if all(m == memory.KEEP for m in plan.modes):
+                # every saved set is in HBM: the whole backward in one call
+                ws = self._workspace_for(self.descs[0])
+                _lib.call("ql_layers_backward", ctypes.addressof(self.desc_array),
+                          ctypes.addressof(saved_arr), L, dh[0].data_ptr(), dh16[0].data_ptr(),
+                          dh[1].data_ptr(), dh16[1].data_ptr(), grads.data_ptr(),
+                          ctypes.addressof(self._grad_offsets), 1, ws.data_ptr(), ws.numel(),
+                          ops.stream_ptr())
+            for spec in reversed(self.layers if not all(m == memory.KEEP for m in plan.modes)
+                                 else []):
                 i = spec.index
                 desc = self.descs[i]
                 sv, drop = per_layer[i]
-                self._set_step(desc, packed, drop, cos, sin)
                 if plan.modes[i] == memory.RECOMPUTE:
                     self._recompute(i, desc, sv, arena)
                 elif plan.modes[i] == memory.OFFLOAD:

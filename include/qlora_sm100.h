@@ -505,6 +505,30 @@ int ql_layer_backward(const ql_layer_desc* layer, const ql_layer_saved* saved, c
                       const void* dh3_16, float* grads, float* dh_out, void* dh16_out,
                       void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 
+/* ---- all layers of a step in one call -------------------------------------------------------
+ * The same work as the per-layer calls above, looped over the layers in the library, for a host
+ * that would otherwise pay its own per-call overhead 2 L times a step (no counterpart in the
+ * reference, whose layer loop is Python: solution/engine.py:1904-1913). */
+/* The step-dependent fields of every layer descriptor at once: cos .. max_len copied from `step`
+ * into descs[0 .. count-1], and layer i's dropout counters from ctr_q[i] / ctr_v[i] (NULL: 0).
+ * Host only, no launch. */
+int ql_layers_set_step(ql_layer_desc* descs, int count, const ql_layer_desc* step,
+                       const int64_t* ctr_q, const int64_t* ctr_v);
+/* ql_layer_forward for layers 0 .. count-1 in order: layer i reads saved[i].h and writes h_out[i]
+ * (normally saved[i + 1].h). */
+int ql_layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                      float* const* h_out, void* workspace, int64_t workspace_bytes,
+                      cudaStream_t stream);
+/* ql_layer_backward for layers count-1 .. 0. The top layer takes (dh, dh16), the gradient of its
+ * output; each layer's input gradient goes to the other buffer pair, (dh_alt, dh16_alt) then
+ * (dh, dh16) and so on, and feeds the layer below; layer 0's is not formed when
+ * skip_first_input_grad (its input is the frozen embedding). grads: the flat fp32 LoRA gradients,
+ * layer i's at grads + grad_offsets[i] floats. */
+int ql_layers_backward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                       float* dh, void* dh16, float* dh_alt, void* dh16_alt, float* grads,
+                       const int64_t* grad_offsets, int skip_first_input_grad, void* workspace,
+                       int64_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
