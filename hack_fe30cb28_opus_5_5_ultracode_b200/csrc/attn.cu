@@ -280,8 +280,19 @@ namespace ql {
 // Dvec[h][t] = sum_d dO[t, h, d] * O[t, h, d] (the softmax-gradient row term).
 template <typename T, int AT_D>
 __global__ void attn_bwd_pre_kernel(const T* __restrict__ dout, const T* __restrict__ out,
-                                    float* __restrict__ dvec, int64_t n, int HQ) {
+                                    float* __restrict__ dvec, int64_t n, int HQ,
+                                    float* __restrict__ dq, float* __restrict__ dk,
+                                    float* __restrict__ dv, int64_t kv_vec4) {
   pdl_enter();
+  // the gradients the backward kernel bulk-adds into start from zero: one float4 of dq per thread
+  // (n HQ rows of 32 float4), and of dk and dv for the first kv_vec4 threads (null: not needed)
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (dq != nullptr && gid < n * HQ * (AT_D / 4)) reinterpret_cast<float4*>(dq)[gid] = zero;
+  if (dk != nullptr && gid < kv_vec4) {
+    reinterpret_cast<float4*>(dk)[gid] = zero;
+    reinterpret_cast<float4*>(dv)[gid] = zero;
+  }
   const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + (threadIdx.x >> 5);  // (t, h)
   const int lane = threadIdx.x & 31;
   if (row >= n * HQ) return;
@@ -533,7 +544,9 @@ template <typename T, int D>
 static void launch_attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   const int64_t rows = (int64_t)a.n * a.HQ;
   launch_k(attn_bwd_pre_kernel<T, D>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
-      (const T*)a.dout, (const T*)a.out, a.dvec, a.n, a.HQ);
+      (const T*)a.dout, (const T*)a.out, a.dvec, a.n, a.HQ, a.dq, a.dk, a.dv,
+      (int64_t)a.n * a.HKV * (D / 4));
+  if (a.max_len == 0) return;  // every sequence empty: the zeroed gradients are the answer
   const int smem = (2 * AT_BN + 4 * AT_BQ) * D * 2 + AT_BN * 40 * 2 + 4 * AT_BQ * 4 +
                    AT_BQ * (D + 8) * 4;
   static_assert(AT_BQ == 32 && 2 * AT_BN == 128, "one dQ row per lane of warp 0; one dK / dV row per thread");
@@ -609,10 +622,12 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
     const int64_t rows = (int64_t)a.n * a.HQ;
     if (a.dtype == QL_F16)
       launch_k(attn_bwd_pre_kernel<__half, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
-               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ);
+               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ, (float*)nullptr,
+               (float*)nullptr, (float*)nullptr, (int64_t)0);
     else
       launch_k(attn_bwd_pre_kernel<__nv_bfloat16, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
-               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ);
+               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ,
+               (float*)nullptr, (float*)nullptr, (float*)nullptr, (int64_t)0);
     const int st = attn_bwd_tc(a, s);
     if (st != QL_STATUS_OK) return st;
     const int64_t threads = (int64_t)a.n * (a.HQ + 2 * a.HKV) * 32;
@@ -620,20 +635,20 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
              (const float*)a.partials, a);
     return launched(3);
   }
-  // gradients accumulate atomically: start from zero
-  if (cudaMemsetAsync(a.dq, 0, sizeof(float) * a.n * a.HQ * a.D, s) != cudaSuccess ||
-      cudaMemsetAsync(a.dk, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess ||
-      cudaMemsetAsync(a.dv, 0, sizeof(float) * a.n * a.HKV * a.D, s) != cudaSuccess)
-    return QL_STATUS_CUDA;
-  if (a.max_len == 0) return QL_STATUS_OK;
-  if (a.D == 128 && (a.dtype == QL_F16 || a.dtype == QL_BF16) && g_attn_impl.load() != 1) {
+  // the gradients accumulate by bulk reductions from zero: the pre-kernel (which every path runs
+  // first) zeroes them, so no separate memset breaks the launch chain
+  if (tc) {
     const int64_t rows = (int64_t)a.n * a.HQ;
+    const int64_t kv4 = (int64_t)a.n * a.HKV * 32;
     if (a.dtype == QL_F16)
       launch_k(attn_bwd_pre_kernel<__half, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
-               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ);
+               (const __half*)a.dout, (const __half*)a.out, a.dvec, a.n, a.HQ, a.dq, a.dk, a.dv,
+               kv4);
     else
       launch_k(attn_bwd_pre_kernel<__nv_bfloat16, 128>, dim3((unsigned)cdiv(rows, 8)), dim3(256), 0, s,
-               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ);
+               (const __nv_bfloat16*)a.dout, (const __nv_bfloat16*)a.out, a.dvec, a.n, a.HQ, a.dq,
+               a.dk, a.dv, kv4);
+    if (a.max_len == 0) return launched(1);
     const int st = attn_bwd_tc(a, s);
     return st == QL_STATUS_OK ? launched(2) : st;
   }
@@ -644,7 +659,7 @@ int attn_bwd(const AttnBwdC& a, cudaStream_t s) {
   } else {
     return QL_STATUS_BAD_ARG;
   }
-  return launched(2);
+  return launched(a.max_len == 0 ? 1 : 2);
 }
 
 }  // namespace ql
