@@ -23,6 +23,7 @@ import ctypes
 
 import numpy as np
 import torch
+from torch._utils import _unflatten_dense_tensors
 
 from . import _lib, memory, ops
 
@@ -510,6 +511,7 @@ class FusedQwen2:
         self.last_offload_bytes = 0  # host-link bytes of the last backward's offload plan
         self._workspace = None
         self._arena_buf = None     # grow-only device memory of the saved activations
+        self._saved_cache = None   # (key, ql_layer_saved array, residual-slot pointers)
         self._arena_busy = False   # a forward's activations await their backward
 
     def _layer_desc(self, spec):
@@ -610,17 +612,11 @@ class FusedQwen2:
         L = len(self.layers)
         drops = self._drops(packed)
         self._set_all_steps(packed, drops, cos, sin)
-        saved_arr = (_lib.STRUCTS["ql_layer_saved"] * L)()
-        for i in range(L):
-            saved_arr[i] = arena.saved(i)
-            if self.w16 is not None:
-                saved_arr[i].w16 = self.w16[i * self.weight_elems:].data_ptr()
-                saved_arr[i].w16_ready = 1
+        saved_arr, h_out = self._saved_structs(arena, plan)
         saved = [(saved_arr[i], drops[i]) for i in range(L)]
         if n and all(m == memory.KEEP for m in plan.modes):
             # every layer keeps its saved set: the whole forward in one call
             ws = self._workspace_for(self.descs[0])
-            h_out = (ctypes.c_void_p * L)(*[arena.h(i + 1).data_ptr() for i in range(L)])
             _lib.call("ql_layers_forward", ctypes.addressof(self.desc_array),
                       ctypes.addressof(saved_arr), L, ctypes.addressof(h_out), ws.data_ptr(),
                       ws.numel(), ops.stream_ptr())
@@ -640,6 +636,25 @@ class FusedQwen2:
         if loss is None:
             loss = torch.zeros((), device=self.device)
         return loss, (arena, saved, offload), dhp
+
+    def _saved_structs(self, arena, plan):
+        """Every layer's ql_layer_saved (device addresses in the arena) and the residual slots
+        the layers write. They depend only on the arena's address, the token count and the plan,
+        so the arrays are rebuilt only when one of those changes (a new array is made then: the
+        previous one may still be held by a step whose backward has not run)."""
+        L = len(self.layers)
+        w16 = self.w16.data_ptr() if self.w16 is not None else 0
+        key = (arena.base, arena.n, tuple(plan.modes), w16)
+        if self._saved_cache is None or self._saved_cache[0] != key:
+            saved_arr = (_lib.STRUCTS["ql_layer_saved"] * L)()
+            for i in range(L):
+                saved_arr[i] = arena.saved(i)
+                if self.w16 is not None:
+                    saved_arr[i].w16 = w16 + i * self.weight_elems * self._esize()
+                    saved_arr[i].w16_ready = 1
+            h_out = (ctypes.c_void_p * L)(*[arena.h(i + 1).data_ptr() for i in range(L)])
+            self._saved_cache = (key, saved_arr, h_out)
+        return self._saved_cache[1], self._saved_cache[2]
 
     def _dequant_all(self):
         """Every layer's four NF4 groups into the kept 16-bit weights ([qkv | o | gate_up |
@@ -779,8 +794,8 @@ class FusedQwen2:
         if arena.owned:  # the next forward may reuse the arena (queued after this backward)
             self._arena_busy = False
         grads = torch.zeros(self.lora_total, device=self.device, dtype=torch.float32)
-        views = [grads[self.offsets[i]:self.offsets[i + 1]].view(t.shape)
-                 for i, t in enumerate(self.lora_fp32)]
+        # one view per LoRA weight, made in one call (the buffer is laid out in lora_fp32 order)
+        views = list(_unflatten_dense_tensors(grads, self.lora_fp32))
         reducer = None
         if self.data_parallel:
             from .dist import GradReducer

@@ -10,6 +10,7 @@ from ._lib import call
 
 _DT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
 INT_MAX = 2147483647
+STATUS_UNSUPPORTED = 3  # QL_STATUS_UNSUPPORTED of include/qlora_sm100.h: no kernel for this request
 STATUS_TIMEOUT = 4  # QL_STATUS_TIMEOUT of include/qlora_sm100.h: a kernel gave up a bounded wait
 
 
@@ -324,6 +325,27 @@ def glu_fwd(gu, I, out=None):
     m = out if out is not None else torch.empty((n, I), device=gu.device, dtype=gu.dtype)
     call("ql_glu_fwd", _ptr(gu), _ptr(m), n, I, dtype_code(gu.dtype), stream_ptr())
     return m
+
+
+def gemm_glu(a, w, I, gu=None, m=None):
+    """(gu, m): gu = a . w^T with w = [gate rows; up rows] ([2 I, K]) and m = silu(g) * u, in one
+    kernel (ql_gemm_glu); None where that kernel does not take the shape (ql_gemm_glu returns
+    QL_STATUS_UNSUPPORTED: the caller runs gemm and glu_fwd)."""
+    M, K = a.shape
+    if w.shape != (2 * I, K) or a.dtype != w.dtype:
+        raise ValueError(f"gemm_glu: weight {tuple(w.shape)} for I {I}, K {K}")
+    gu = gu if gu is not None else torch.empty((M, 2 * I), device=a.device, dtype=a.dtype)
+    m = m if m is not None else torch.empty((M, I), device=a.device, dtype=a.dtype)
+    _need_cuda(a, w, gu, m)
+    status = _lib.lib().ql_gemm_glu(_ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(gu),
+                                    gu.stride(0), _ptr(m), m.stride(0), M, I, K,
+                                    dtype_code(a.dtype), stream_ptr())
+    if status == STATUS_UNSUPPORTED:
+        return None
+    if status != 0:
+        raise _lib.QLError("ql_gemm_glu", status,
+                           _lib.lib().ql_last_error().decode(errors="replace"))
+    return gu, m
 
 
 def glu_bwd(dm, gu, I):

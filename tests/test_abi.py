@@ -67,3 +67,5 @@ def test_status_constant_matches_the_header():
 
     text = open(_lib.HEADER, encoding="utf-8").read()
     assert int(re.search(r"QL_STATUS_TIMEOUT\s*=\s*(\d+)", text).group(1)) == ops.STATUS_TIMEOUT
+    assert int(re.search(r"QL_STATUS_UNSUPPORTED\s*=\s*(\d+)", text).group(1)) == \
+        ops.STATUS_UNSUPPORTED
