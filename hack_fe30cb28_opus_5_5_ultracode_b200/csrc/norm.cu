@@ -312,16 +312,30 @@ __global__ void __launch_bounds__(WPR == 1 ? 32 * RMS_MAXR : 1024) rms_bwd_kerne
             reinterpret_cast<const unsigned short*>(ad == 0 ? a.Aq : a.Av) + g;
         T* dst0 = sT + (ad * rows + g) * ld + 2 * t;
         T* dst1 = sT + (ad * rows + g + 8) * ld + 2 * t;
-        for (int n0 = warp * 8; n0 < H; n0 += 8 * NW) {
-          const unsigned short* col = Ab + n0;
-          const uint32_t b0 = (uint32_t)__ldg(col + (2 * t) * H) |
-                              ((uint32_t)__ldg(col + (2 * t + 1) * H) << 16);
-          const uint32_t b1 = (uint32_t)__ldg(col + (2 * t + 8) * H) |
-                              ((uint32_t)__ldg(col + (2 * t + 9) * H) << 16);
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-          mma16816<T>(c, af, b0, b1);
-          if (g < rows) *reinterpret_cast<uint32_t*>(dst0 + n0) = pack_t2<T>(c[0], c[1]);
-          if (g + 8 < rows) *reinterpret_cast<uint32_t*>(dst1 + n0) = pack_t2<T>(c[2], c[3]);
+        // 8-column groups n0 = 8 (warp + NW j), RB at a time: the groups' B fragments (strided
+        // 16-bit reads of A's rows, from L2) are all requested before the first multiply
+        constexpr int RB = 2;
+        for (int j0 = 0; warp * 8 + j0 * 8 * NW < H; j0 += RB) {
+          uint32_t b0[RB], b1[RB];
+#pragma unroll
+          for (int j = 0; j < RB; ++j) {
+            const int n0 = warp * 8 + (j0 + j) * 8 * NW;
+            b0[j] = b1[j] = 0u;
+            if (n0 < H) {
+              const unsigned short* col = Ab + n0;
+              b0[j] = (uint32_t)__ldg(col + (2 * t) * H) | ((uint32_t)__ldg(col + (2 * t + 1) * H) << 16);
+              b1[j] = (uint32_t)__ldg(col + (2 * t + 8) * H) | ((uint32_t)__ldg(col + (2 * t + 9) * H) << 16);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < RB; ++j) {
+            const int n0 = warp * 8 + (j0 + j) * 8 * NW;
+            if (n0 >= H) break;
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816<T>(c, af, b0[j], b1[j]);
+            if (g < rows) *reinterpret_cast<uint32_t*>(dst0 + n0) = pack_t2<T>(c[0], c[1]);
+            if (g + 8 < rows) *reinterpret_cast<uint32_t*>(dst1 + n0) = pack_t2<T>(c[2], c[3]);
+          }
         }
       }
       __syncthreads();

@@ -88,17 +88,35 @@ __global__ void __launch_bounds__(512) rope_fwd_kernel(RopeFwdC a, int rows) {
           }
         }
       }
-      for (int n0 = warp * 8; n0 < QD + VD; n0 += 8 * NW) {
-        const bool isq = n0 < QD;
-        if (isq ? !fq : !fv) continue;
-        const unsigned int* Bw = reinterpret_cast<const unsigned int*>(
-            isq ? reinterpret_cast<const T*>(a.Bq) + (int64_t)(n0 + g) * RANK
-                : reinterpret_cast<const T*>(a.Bv) + (int64_t)(n0 - QD + g) * RANK);
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816<T>(c, isq ? aq : av, __ldg(Bw + t), __ldg(Bw + 4 + t));
-        if (g < rows) *reinterpret_cast<uint32_t*>(sL + g * ld + n0 + 2 * t) = pack_t2<T>(c[0], c[1]);
-        if (g + 8 < rows)
-          *reinterpret_cast<uint32_t*>(sL + (g + 8) * ld + n0 + 2 * t) = pack_t2<T>(c[2], c[3]);
+      // 8-column groups n0 = 8 (warp + NW j) of [q | v], RB at a time: the RB groups' B fragments
+      // are loaded first (independent L2 reads in flight together), then multiplied
+      constexpr int RB = 8;
+      for (int j0 = 0; warp * 8 + j0 * 8 * NW < QD + VD; j0 += RB) {
+        uint32_t b0[RB], b1[RB];
+#pragma unroll
+        for (int j = 0; j < RB; ++j) {
+          const int n0 = warp * 8 + (j0 + j) * 8 * NW;
+          const bool isq = n0 < QD;
+          b0[j] = b1[j] = 0u;
+          if (n0 < QD + VD && (isq ? fq : fv)) {
+            const unsigned int* Bw = reinterpret_cast<const unsigned int*>(
+                isq ? reinterpret_cast<const T*>(a.Bq) + (int64_t)(n0 + g) * RANK
+                    : reinterpret_cast<const T*>(a.Bv) + (int64_t)(n0 - QD + g) * RANK);
+            b0[j] = __ldg(Bw + t);
+            b1[j] = __ldg(Bw + 4 + t);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < RB; ++j) {
+          const int n0 = warp * 8 + (j0 + j) * 8 * NW;
+          const bool isq = n0 < QD;
+          if (n0 >= QD + VD || (isq ? !fq : !fv)) continue;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          mma16816<T>(c, isq ? aq : av, b0[j], b1[j]);
+          if (g < rows) *reinterpret_cast<uint32_t*>(sL + g * ld + n0 + 2 * t) = pack_t2<T>(c[0], c[1]);
+          if (g + 8 < rows)
+            *reinterpret_cast<uint32_t*>(sL + (g + 8) * ld + n0 + 2 * t) = pack_t2<T>(c[2], c[3]);
+        }
       }
       __syncthreads();
     }
