@@ -454,6 +454,12 @@ static RmsShape rms_shape(int64_t n, int H) {
   }
   const int64_t waves = cdiv(n, (int64_t)sms * r.rows);
   r.rows = (int)cdiv(n, (int64_t)sms * waves);
+  if (r.wpr == 4 && n > (int64_t)sms * 16 && cdiv(groups, 64) <= 8) {
+    // several waves: 8-row tiles of two warps per row (512 threads), two CTAs resident per SM,
+    // so one tile's loads and stores overlap the other's arithmetic
+    r.wpr = 2;
+    r.rows = 8;
+  }
   r.grid = (int)cdiv(n, r.rows);
   r.G = (int)cdiv(groups, 32 * r.wpr);
   return r;

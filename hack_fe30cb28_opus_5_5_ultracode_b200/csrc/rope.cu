@@ -327,8 +327,15 @@ static RopeShape rope_shape(int64_t n) {
   const int sms = sm_count();
   const int64_t waves = cdiv(n, (int64_t)sms * ROPE_MAXR);
   RopeShape r;
-  r.rows = (int)cdiv(n, (int64_t)sms * waves);
-  r.wpr = r.rows <= 8 ? 2 : 1;
+  if (waves > 1) {
+    // more rows than one wave of 16-row tiles: 8-row tiles of one warp per token (256 threads),
+    // two CTAs resident per SM, so one CTA's loads overlap the other's arithmetic
+    r.rows = 8;
+    r.wpr = 1;
+  } else {
+    r.rows = (int)cdiv(n, (int64_t)sms * waves);
+    r.wpr = r.rows <= 8 ? 2 : 1;
+  }
   r.grid = (int)cdiv(n, r.rows);
   return r;
 }

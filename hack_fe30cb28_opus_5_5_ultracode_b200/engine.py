@@ -977,13 +977,19 @@ class _SavedArena:
 class _Offload:
     """Offload of spilled layers' saved sets to pinned host memory: the forward's set of layer
     i leaves its ring slot on a copy stream right after the layer (the slot is reused two
-    spilled layers later, after that copy), and the backward brings each set back into a ring
-    slot one spilled layer ahead of its use (the slot is free once the layer that used it is
-    done). One cudaMemcpyAsync per layer and direction; events order the two streams."""
+    offloaded layers later, after that copy), and the backward brings each set back into a ring
+    slot one offloaded layer ahead of its use (the slot is free once the layer that used it is
+    done). The last two offloaded layers of the forward stay in their ring slots (no later
+    layer reuses them, and the backward needs them first): they make no round trip, so no copy
+    sits between the end of the forward and the start of the backward. One cudaMemcpyAsync per
+    layer and direction; events order the two streams."""
 
     def __init__(self, engine, arena, plan):
         self.arena, self.plan = arena, plan
-        self.spilled = [i for i in plan.spilled() if plan.modes[i] == memory.OFFLOAD]
+        offloaded = [i for i in plan.spilled() if plan.modes[i] == memory.OFFLOAD]
+        self.resident = set(offloaded[-2:])  # ring slots 0 and 1 hold them into the backward
+        self.spilled = [i for i in offloaded if i not in self.resident]
+        self.order = sorted(offloaded, reverse=True)  # the backward's order
         nbytes = len(self.spilled) * arena.layer_bytes
         if engine._host_ring is None or engine._host_ring.numel() < nbytes:
             engine._host_ring = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
@@ -1007,7 +1013,7 @@ class _Offload:
         return self.host[k * lb:(k + 1) * lb]
 
     def before_forward(self, i):
-        if i in self.index:
+        if i in self.index or i in self.resident:
             ev = self.slot_free.get(self.plan.slot(i))
             if ev is not None:
                 torch.cuda.current_stream().wait_event(ev)
@@ -1051,15 +1057,18 @@ class _Offload:
         for ev in self.slot_free.values():
             self.stream.wait_event(ev)
         self.slot_free = {}
-        order = sorted(self.spilled, reverse=True)
-        self.order = order
-        if order:
-            self._fetch(order[0])
+        # the first offloaded layers of the backward are resident; a fetch is only needed first
+        # if a single ring slot holds a resident layer (then the next set goes into the other)
+        if self.order and self.order[0] not in self.resident:
+            self._fetch(self.order[0])
 
     def before_backward(self, i):
-        torch.cuda.current_stream().wait_event(self.arrived.pop(i))
+        if i in self.arrived:
+            torch.cuda.current_stream().wait_event(self.arrived.pop(i))
         k = self.order.index(i)
-        if k + 1 < len(self.order):  # the next spilled layer, into the other ring slot
+        # the next offloaded layer into the slot the previous one used (free once that layer's
+        # backward is done): resident layers need no fetch
+        if k + 1 < len(self.order) and self.order[k + 1] not in self.resident:
             self._fetch(self.order[k + 1])
 
     def after_backward(self, i):

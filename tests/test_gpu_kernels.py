@@ -106,7 +106,8 @@ def test_rms_matches_reference_golden(golden):
 
 # launch shapes covered: 4 warps per row and tiles of 1-8 rows in one wave (37, 300, 64, 40,
 # 1100 x 3584), 3 warps x 9 rows (1264), 2 warps x 11-14 rows (1500, 2000), several waves of
-# 7-row tiles (5000) and of 5-row tiles at the 7B width (1300 x 3584), one warp per row (256)
+# 8-row tiles of 2 warps per row (5000) and of 5-row tiles at the 7B width (1300 x 3584), one
+# warp per row (256)
 @pytest.mark.parametrize("n,H", [(37, 1536), (5, 256), (300, 3584), (64, 4096), (40, 2304),
                                  (1264, 1536), (1500, 1536), (2000, 1536), (5000, 1536),
                                  (1100, 3584), (1300, 3584), (700, 256)])
@@ -153,7 +154,7 @@ def test_rms_fused_lora_matches_torch(n, H, dtype):
 
 
 @pytest.mark.parametrize("n,H", [(37, 1536), (9, 64), (300, 3584), (64, 4096), (1264, 1536),
-                                 (2000, 1536)])
+                                 (2000, 1536), (5000, 1536)])
 def test_rms_mask_bits_match_redrawn_masks(n, H):
     """The forward's mask bits are the Philox masks; a backward that reads them equals one that
     draws the masks again, bit for bit."""
@@ -205,7 +206,8 @@ def test_rope_matches_reference_golden(golden):
     close(dqkv, torch.from_numpy(g["dqkv"]), 1e-2)
 
 
-@pytest.mark.parametrize("n", [23, 1264, 2500])  # tiles of 1 (2 warps / token), 9 and 9 tokens
+# tiles of 1 token (2 warps / token), 9 tokens, and several waves of 8-token tiles (one warp each)
+@pytest.mark.parametrize("n", [23, 1264, 2500, 6000])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_rope_fused_lora(n, dtype):
     o = ops()
