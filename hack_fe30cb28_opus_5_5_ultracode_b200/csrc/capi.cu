@@ -161,13 +161,6 @@ int ql_nf4_dequant_batch(const ql_nf4_weight* weights, void* const* outs, int co
 
 int64_t ql_gemm_workspace_bytes(int M, int N, int K) { return ql::gemm_workspace_bytes(M, N, K); }
 
-int ql_gemm_glu(const void* A, int64_t lda, const void* W, int64_t ldw, void* gu, int64_t ldgu,
-                void* m, int64_t ldm, int M, int I, int K, int dtype, cudaStream_t stream) {
-  return done(ql::gemm_glu(A, lda, W, ldw, gu, ldgu, m, ldm, M, I, K, dtype, ql::status_word(),
-                           stream),
-              "ql_gemm_glu");
-}
-
 int ql_gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight* W, int layout, void* C,
                 int64_t ldc, const void* bias, int M, int in_dtype, int out_dtype, int accumulate,
                 const float* residual, cudaStream_t stream) {

@@ -25,11 +25,6 @@ struct GemmArgs {
   float* ws;
   int* counters;
   int tma_c;  // 16-bit C written by TMA tensor stores from per-warp shared-memory staging
-  // SwiGLU epilogue (pair kernel only, glu_I > 0): B is the [2 I, K] [gate | up] weight and C
-  // the [M, 2 I] gate / up output; a pair tile of width BN covers gate columns j .. j + BN/2 - 1
-  // (the even CTA's half of B) and the same up columns (the odd CTA's half), and the epilogue
-  // also writes m = silu(g) u into the [M, I] map of the kernel's fourth tensor map.
-  int glu_I;
 };
 
 // Epilogue staging for TMA stores of a 16-bit C: per epilogue warp two 32 x 32 buffers of 2 KB.

@@ -276,20 +276,11 @@ struct PairCfg {
   static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
 };
 
-// SwiGLU of one 32-column chunk, as glu_fwd computes it from the 16-bit g and u: m = g / (1 +
-// e^-g) * u in fp32 (g and u already rounded to the output type).
-template <typename T>
-__device__ __forceinline__ void glu_chunk(const float* g, const float* u, float* m) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) m[i] = g[i] / (1.0f + __expf(-g[i])) * u[i];
-}
-
-template <int BN, bool IS_BF16, typename OutT, bool B_MN, bool kGlu = false>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
-                     const __grid_constant__ CUtensorMap tma_c,
-                     const __grid_constant__ CUtensorMap tma_m, GemmArgs p) {
+                     const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
   pdl_trigger();  // setup below reads no global memory; pdl_wait() follows it
   constexpr bool kTmaC = sizeof(OutT) == 2;
   using Cfg = PairCfg<BN, kTmaC>;
@@ -307,9 +298,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  static_assert(!kGlu || (kTmaC && !B_MN), "the SwiGLU epilogue: K-major B, 16-bit outputs");
-  const int m_pairs = (int)cdiv(p.M, 2 * Cfg::BM);
-  const int n_tiles = kGlu ? (int)cdiv(p.glu_I, Cfg::HB) : (int)cdiv(p.N, BN);
+  const int m_pairs = (int)cdiv(p.M, 2 * Cfg::BM), n_tiles = (int)cdiv(p.N, BN);
   const int num_units = m_pairs * n_tiles;
   const int k_blocks = (int)cdiv(p.K, Cfg::BK);
 
@@ -341,8 +330,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int u = pair; u < num_units && ok; u += npairs) {
         const int mp = u % m_pairs, nb = u / m_pairs;
         const int arow = mp * 2 * Cfg::BM + (int)rank * Cfg::BM;
-        // SwiGLU: the even CTA streams gate rows, the odd one the matching up rows
-        const int brow = kGlu ? (int)rank * p.glu_I + nb * Cfg::HB : nb * BN + (int)rank * Cfg::HB;
+        const int brow = nb * BN + (int)rank * Cfg::HB;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
@@ -407,36 +395,6 @@ __global__ void __launch_bounds__(192, 1)
       const int mp = u % m_pairs, nb = u / m_pairs;
       const int row = mp * 2 * Cfg::BM + (int)rank * Cfg::BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
-      if constexpr (kGlu) {
-        // accumulator columns [0, HB): gate, [HB, BN): up, of columns nb * HB + c of I
-        const int wrow0 = mp * 2 * Cfg::BM + (int)rank * Cfg::BM + quad * 32;
-#pragma unroll 1
-        for (int c = 0; c < Cfg::HB; c += 32) {
-          float g[32], v[32];
-          tmem_ld32(taddr + c, g);
-          tmem_ld32(taddr + Cfg::HB + c, v);
-          const int col = nb * Cfg::HB + c;
-          if (col < p.glu_I && wrow0 < p.M) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              g[i] = to_f<OutT>(from_f<OutT>(g[i]));
-              v[i] = to_f<OutT>(from_f<OutT>(v[i]));
-            }
-            epi_tma_chunk<OutT>(&tma_c, epi_stage + quad * 4096, ebuf, g, col, wrow0);
-            epi_tma_chunk<OutT>(&tma_c, epi_stage + quad * 4096, ebuf, v, p.glu_I + col, wrow0);
-            float m[32];
-            glu_chunk<OutT>(g, v, m);
-            epi_tma_chunk<OutT>(&tma_m, epi_stage + quad * 4096, ebuf, m, col, wrow0);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(&tempty[acc]);
-          else mbar_arrive_cluster(&tempty[acc], 0);
-        }
-        continue;
-      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
@@ -541,11 +499,11 @@ static int pair_slots(K kern, int smem) {
   return clusters;
 }
 
-template <int BN, bool IS_BF16, typename OutT, bool B_MN, bool kGlu = false>
-static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                       const CUtensorMap& mm, const GemmArgs& a, cudaStream_t stream) {
+template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
+                       cudaStream_t stream) {
   using Cfg = PairCfg<BN, sizeof(OutT) == 2>;
-  auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN, kGlu>;
+  auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN>;
   static int slots = 0;  // one per instantiation
   if (slots == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) !=
@@ -553,8 +511,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
       return QL_STATUS_CUDA;
     slots = pair_slots(kern, Cfg::SMEM_BYTES);
   }
-  const int units =
-      (int)(cdiv(a.M, 2 * Cfg::BM) * (kGlu ? cdiv(a.glu_I, Cfg::HB) : cdiv(a.N, BN)));
+  const int units = (int)(cdiv(a.M, 2 * Cfg::BM) * cdiv(a.N, BN));
   const int pairs = units < slots ? units : slots;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
@@ -570,7 +527,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mm, a) != cudaSuccess) return QL_STATUS_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, a) != cudaSuccess) return QL_STATUS_CUDA;
   return launched(1);
 }
 
@@ -578,9 +535,9 @@ template <int BN, bool IS_BF16, bool B_MN>
 static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                              cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, mc, mc, a, s);
-    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, mc, a, s);
-    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, mc, mc, a, s);
+    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, mc, a, s);
+    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, a, s);
+    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, mc, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
@@ -741,7 +698,7 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
       return QL_STATUS_CUDA;
   }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
-             g.kb_per_split, nullptr, nullptr, 0, 0};
+             g.kb_per_split, nullptr, nullptr, 0};
   // 16-bit C with no read-modify epilogue: TMA tensor stores (needs a 16-byte aligned C and row
   // stride); otherwise per-thread row stores and an unused map
   CUtensorMap mc;
@@ -788,50 +745,6 @@ int gemm_tn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
             int64_t workspace_bytes) {
   return gemm_core(A, lda, B, ldb, C, ldc, bias, M, N, K, in_dtype, out_dtype, accumulate,
                    residual, err, stream, workspace, workspace_bytes, false);
-}
-
-// [gate | up] = A . W^T with W = [gate rows; up rows] ([2 I, K]) and the SwiGLU m = silu(g) u
-// in the pair kernel's epilogue (see GemmArgs::glu_I): the gate/up output is written as by
-// gemm_tn and m as by glu_fwd on it, with no second pass over [M, 2 I]. Only where the cost model
-// picks 2-SM pair tiles whose half width divides I (and the 16-bit outputs are TMA-storable);
-// otherwise QL_STATUS_UNSUPPORTED before anything is launched, and the caller runs gemm_tn and
-// glu_fwd.
-int gemm_glu(const void* A, int64_t lda, const void* W, int64_t ldw, void* GU, int64_t ldgu,
-             void* Mout, int64_t ldm, int M, int I, int K, int dtype, int* err,
-             cudaStream_t stream) {
-  if (M < 0 || I <= 0 || K <= 0 || (dtype != QL_F16 && dtype != QL_BF16)) return QL_STATUS_BAD_ARG;
-  if (M == 0) return QL_STATUS_OK;
-  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) |
-       reinterpret_cast<uintptr_t>(GU) | reinterpret_cast<uintptr_t>(Mout)) % 16 != 0 ||
-      (lda * 2) % 16 != 0 || (ldw * 2) % 16 != 0 || (ldgu * 2) % 16 != 0 || (ldm * 2) % 16 != 0 ||
-      K % 8 != 0)
-    return QL_STATUS_BAD_ARG;
-  const GemmPlan g = plan_gemm(M, 2 * I, K, num_sms());
-  int bn = g.bn;
-  if (g.pair && bn == 192 && I % 96 != 0) bn = 256;  // a half width that divides I, if any
-  if (!g.pair || g.splits != 1 || I % (bn / 2) != 0) return QL_STATUS_UNSUPPORTED;
-  const bool bf16 = dtype == QL_BF16;
-  ProfScope prof(PK_GEMM, 2.0 * M * 2.0 * I * K,
-                 2.0 * ((double)M * K + 2.0 * I * K) + (double)M * I * 6, stream);
-  CUtensorMap ma, mb, mc, mm;
-  if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK ||
-      make_kmajor_map(&mb, W, 2LL * I, K, ldw, bn / 2, bf16) != QL_STATUS_OK ||
-      make_store_map(&mc, GU, M, 2LL * I, ldgu, bf16) != QL_STATUS_OK ||
-      make_store_map(&mm, Mout, M, I, ldm, bf16) != QL_STATUS_OK)
-    return QL_STATUS_CUDA;
-  GemmArgs a{M, 2 * I, K, GU, ldgu, nullptr, dtype, 0, nullptr, err, 1, (int)cdiv(K, 64),
-             nullptr, nullptr, 1, I};
-  switch (bn) {
-    case 128:
-      return bf16 ? launch_pair<128, true, __nv_bfloat16, false, true>(ma, mb, mc, mm, a, stream)
-                  : launch_pair<128, false, __half, false, true>(ma, mb, mc, mm, a, stream);
-    case 192:
-      return bf16 ? launch_pair<192, true, __nv_bfloat16, false, true>(ma, mb, mc, mm, a, stream)
-                  : launch_pair<192, false, __half, false, true>(ma, mb, mc, mm, a, stream);
-    default:
-      return bf16 ? launch_pair<256, true, __nv_bfloat16, false, true>(ma, mb, mc, mm, a, stream)
-                  : launch_pair<256, false, __half, false, true>(ma, mb, mc, mm, a, stream);
-  }
 }
 
 int gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,

@@ -274,14 +274,9 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   QL_TRY(rms_fwd(r2, s));
   // [gate | up], SwiGLU, down with the residual add: h3 = h2 + d
   if (!ready) QL_TRY(dequant(L.gu, wgu, dt, 0, s));
-  const int glu = gemm_glu(w.a, L.H, wgu, L.H, S.gu, 2LL * L.I, w.m, L.I, L.n, L.I, L.H, dt, err, s);
-  if (glu == QL_STATUS_UNSUPPORTED) {  // shapes the fused epilogue does not take: two passes
-    QL_TRY(gemm_tn(w.a, L.H, wgu, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
-                   nullptr, err, s, w.gws, w.gws_bytes));
-    QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
-  } else {
-    QL_TRY(glu);
-  }
+  QL_TRY(gemm_tn(w.a, L.H, wgu, L.H, S.gu, 2LL * L.I, nullptr, L.n, 2 * L.I, L.H, dt, dt, 0,
+                 nullptr, err, s, w.gws, w.gws_bytes));
+  QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
   if (!ready) QL_TRY(dequant(L.down, wdown, dt, 0, s));
   QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
                  err, s, w.gws, w.gws_bytes));

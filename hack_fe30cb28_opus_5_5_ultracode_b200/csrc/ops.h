@@ -25,9 +25,6 @@ int gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int
             const float* residual, int* err, cudaStream_t stream, void* workspace = nullptr,
             int64_t workspace_bytes = 0);
 int64_t gemm_workspace_bytes(int M, int N, int K);
-int gemm_glu(const void* A, int64_t lda, const void* W, int64_t ldw, void* GU, int64_t ldgu,
-             void* Mout, int64_t ldm, int M, int I, int K, int dtype, int* err,
-             cudaStream_t stream);
 void gemm_set_mode(int mode);
 
 typedef ql_rms_fwd_args RmsFwdC;

@@ -120,22 +120,6 @@ def main():
                 sec = _time(lambda i: ops.gemm(a[i % copies], b[i % 2], out=c[i % copies]),
                             args.iters)
                 _report("gemm_tn " + name, [n, N, K], sec, flops=2.0 * n * N * K)
-                if name == "gate_up":  # SwiGLU in the epilogue against GEMM + glu_fwd
-                    I_ = N // 2
-                    ms = [torch.empty(n, I_, device=dev, dtype=dt) for _ in range(copies)]
-                    if ops.gemm_glu(a[0], b[0], I_, gu=c[0], m=ms[0]) is not None:
-                        sec = _time(lambda i: ops.gemm_glu(a[i % copies], b[i % 2], I_,
-                                                           gu=c[i % copies], m=ms[i % copies]),
-                                    args.iters)
-                        _report("gemm_glu gate_up (+SwiGLU epilogue)", [n, N, K], sec,
-                                flops=2.0 * n * N * K)
-
-                        def two_pass(i):
-                            ops.gemm(a[i % copies], b[i % 2], out=c[i % copies])
-                            ops.glu_fwd(c[i % copies], I_, out=ms[i % copies])
-
-                        sec = _time(two_pass, args.iters)
-                        _report("gemm_tn gate_up + glu_fwd", [n, N, K], sec, flops=2.0 * n * N * K)
                 # the data-gradient GEMM of the same projection: [n, N] x [K, N]^T
                 at = [torch.randn(n, N, device=dev, generator=g).to(dt) for _ in range(copies)]
                 bt = [torch.randn(K, N, device=dev, generator=g).to(dt) * 0.02 for _ in range(2)]

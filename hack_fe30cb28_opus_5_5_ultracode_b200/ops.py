@@ -327,27 +327,6 @@ def glu_fwd(gu, I, out=None):
     return m
 
 
-def gemm_glu(a, w, I, gu=None, m=None):
-    """(gu, m): gu = a . w^T with w = [gate rows; up rows] ([2 I, K]) and m = silu(g) * u, in one
-    kernel (ql_gemm_glu); None where that kernel does not take the shape (ql_gemm_glu returns
-    QL_STATUS_UNSUPPORTED: the caller runs gemm and glu_fwd)."""
-    M, K = a.shape
-    if w.shape != (2 * I, K) or a.dtype != w.dtype:
-        raise ValueError(f"gemm_glu: weight {tuple(w.shape)} for I {I}, K {K}")
-    gu = gu if gu is not None else torch.empty((M, 2 * I), device=a.device, dtype=a.dtype)
-    m = m if m is not None else torch.empty((M, I), device=a.device, dtype=a.dtype)
-    _need_cuda(a, w, gu, m)
-    status = _lib.lib().ql_gemm_glu(_ptr(a), a.stride(0), _ptr(w), w.stride(0), _ptr(gu),
-                                    gu.stride(0), _ptr(m), m.stride(0), M, I, K,
-                                    dtype_code(a.dtype), stream_ptr())
-    if status == STATUS_UNSUPPORTED:
-        return None
-    if status != 0:
-        raise _lib.QLError("ql_gemm_glu", status,
-                           _lib.lib().ql_last_error().decode(errors="replace"))
-    return gu, m
-
-
 def glu_bwd(dm, gu, I):
     call("ql_glu_bwd", _ptr(dm), _ptr(gu), gu.shape[0], I, dtype_code(gu.dtype), stream_ptr())
     return gu

@@ -104,15 +104,6 @@ int ql_gemm_nn(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                const float* residual, void* workspace, int64_t workspace_bytes,
                cudaStream_t stream);
 int64_t ql_gemm_workspace_bytes(int M, int N, int K);
-/* The gate/up projection with SwiGLU in its epilogue: gu[M, 2 I] = A[M, K] . W^T, W = [gate
- * rows; up rows] ([2 I, K], K contiguous), and m[M, I] = silu(g) * u of the 16-bit g and u -
- * the same values as ql_gemm_tn then ql_glu_fwd (replaces the gate_up addmm + _glu_fwd pair,
- * solution/engine.py:1163-1166, solution/kernels.py:312-321) in one kernel. Runs where the
- * GEMM cost model picks 2-SM pair tiles (about 512 rows and more) whose half width divides I;
- * otherwise returns QL_STATUS_UNSUPPORTED with nothing launched. 16-byte aligned pointers and
- * row strides; dtype QL_F16 / QL_BF16 for every operand. */
-int ql_gemm_glu(const void* A, int64_t lda, const void* W, int64_t ldw, void* gu, int64_t ldgu,
-                void* m, int64_t ldm, int M, int I, int K, int dtype, cudaStream_t stream);
 /* Tile kind of ql_gemm_tn / ql_gemm_nn for this process (a tuning and test switch, no counterpart
  * in the reference): 0 = chosen per shape by the cost model (default), 1 = single-CTA 128-row
  * tiles only, 2 = 2-SM 256-row pair tiles (tcgen05 cta_group::2) for every shape they support. */
