@@ -130,13 +130,16 @@ class MetricLedger:
     """The logged side effects of fused steps, kept until the trainer's next optimizer step:
     TRL's `entropy` (mean over a micro-batch's real tokens) and `mean_token_accuracy` (over the
     tokens with a target), and Soup's rewind row (each row's mean cross-entropy over its
-    targets). `record` queues one small device tensor per micro-batch, reduced on the GPU right
-    after the step (no host sync between forward and backward); `flush` reads every pending one
-    back in a single transfer and appends the values in micro-batch order, before the optimizer
-    step and the log read them (solution/patch.py:334-389 keeps the same values)."""
+    targets). `record` reduces one small summary per micro-batch on the GPU right after the
+    step and starts its copy into pinned host memory on the same stream (no host sync between
+    forward and backward); `flush` waits for those copies - done long before, as the head of
+    each forward finished - and appends the values in micro-batch order, before the optimizer
+    step and the log read them (solution/patch.py:334-389 keeps the same values). The flush
+    therefore does not wait for the backward, and the optimizer's launches are not held back
+    behind it."""
 
     def __init__(self):
-        self.pending = []  # (device summary, rows, real tokens, training step)
+        self.pending = []  # (summary: host copy or tensor, copy event, rows, real tokens, step)
 
     def record(self, packed, stats, labels, step):
         rows = packed.rows
@@ -148,17 +151,27 @@ class MetricLedger:
             head = torch.stack([stats.entropy.double().sum(), stats.correct.double().sum(),
                                 (packed.targets >= 0).double().sum()])
             summary = torch.cat([head, per_row, row_targets])
-        self.pending.append((summary, rows, packed.n, step))
+            done = None
+            if summary.is_cuda:
+                host = torch.empty(summary.shape, dtype=summary.dtype, pin_memory=True)
+                host.copy_(summary, non_blocking=True)
+                done = torch.cuda.Event()
+                done.record()
+                summary = host
+        self.pending.append((summary, done, rows, packed.n, step))
 
     def flush(self, trainer):
         if not self.pending:
             return
         pending, self.pending = self.pending, []
-        values = torch.cat([s for s, _, _, _ in pending]).tolist()
+        for _, done, _, _, _ in pending:
+            if done is not None:
+                done.synchronize()
+        values = torch.cat([s for s, _, _, _, _ in pending]).tolist()
         metrics = trainer._metrics["train"]
         recorder = getattr(trainer, "_soup_rewind_state", None)
         at = 0
-        for _, rows, real, step in pending:
+        for _, _, rows, real, step in pending:
             ent, correct, supervised = values[at:at + 3]
             per_row = values[at + 3:at + 3 + rows]
             targets = values[at + 3 + rows:at + 3 + 2 * rows]
