@@ -5,18 +5,22 @@
 // writes out [n, HQ, 128] and the natural-log logsumexp [HQ, n].
 //
 // One CTA per (128-query tile, query head, sequence), the tiles with the most key blocks first.
-// Six warps with fixed roles:
+// Ten warps with fixed roles:
 //   warp 0     TMA: the Q tile once, then K and V tiles of 128 keys into a two-stage ring;
 //   warp 1     one thread issues tcgen05.mma: S_j = Q K_j^T into one of two TMEM score buffers,
 //              then O += P_{j-1} V_{j-1} into the TMEM output accumulator (S_j runs while the
 //              softmax warps work on S_{j-1});
-//   warps 2-5  softmax, one query row per thread (TMEM lane = row): the row's 128 scores come
-//              from TMEM with no cross-thread reduction, P is written as 16-bit values into a
-//              swizzled shared-memory tile (the A operand of the next MMA; two buffers), and
-//              the running row max is raised lazily: O (in TMEM) is rescaled only when a row's
-//              max grows by more than 2^8, after the MMA that last added to O has completed.
+//   warps 2-9  softmax, two threads per query row (TMEM lane = row; warps w and w + 4 share a
+//              lane quadrant): both read the row's 128 scores from TMEM and take the same row
+//              max with no exchange, and each exponentiates its own 64 of them, writing P as
+//              16-bit values into a swizzled shared-memory tile (the A operand of the next MMA;
+//              two buffers). The running row max is raised lazily: O (in TMEM) is rescaled,
+//              each thread its 64 columns, only when a row's max grows by more than 2^8, after
+//              the MMA that last added to O has completed. The two partial row sums are added
+//              once, at the end, through shared memory.
 // TMEM columns: O [0, 128), score buffers [128, 256) and [256, 384) (512 allocated).
-// Shared memory: Q 32 KB, two (K, V) stages of 64 KB, two P tiles of 32 KB (224 KB).
+// Shared memory: Q 32 KB, two (K, V) stages of 64 KB, two P tiles of 32 KB (224 KB), barriers,
+// the row sums' exchange (1 KB).
 // Every wait is bounded (QL_STATUS_TIMEOUT in the library's status word on expiry).
 #include "common.cuh"
 #include "gemm_common.cuh"
@@ -32,7 +36,8 @@ constexpr int TA_BN = 128;               // keys per block
 constexpr int TA_D = 128;                // head dim
 constexpr int TA_TILE = 128 * TA_D * 2;  // a 128 x 128 16-bit tile: two 64-column boxes
 constexpr int TA_BOX = TA_TILE / 2;      // one 128-row x 64-column box (128-byte rows)
-constexpr int TA_SMEM = 7 * TA_TILE + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int TA_SOFTMAX = 256;          // softmax threads: two per query row
+constexpr int TA_SMEM = 7 * TA_TILE + 1024 /*align*/ + 256 /*barriers*/ + 2 * TA_BM * 4 /*sums*/;
 constexpr uint32_t TA_TMEM_COLS = 512;
 
 // offset of the 16-byte chunk ch (0-15) of row r in a K-major 128-byte-swizzled two-box tile
@@ -41,7 +46,7 @@ __device__ __forceinline__ uint32_t ta_chunk(int r, int ch) {
 }
 
 template <bool IS_BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + TA_SOFTMAX, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, AttnFwdC a, int* err) {
   pdl_enter();
@@ -59,7 +64,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_free = bars + 7;    // [2] score buffer read by all 128 softmax threads
   uint64_t* p_full = bars + 9;    // [2] P tile written by all 128 softmax threads
   uint64_t* pv_done = bars + 11;  // [2] O += P V of the P tile completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* l_bar = bars + 13;    // both halves' row sums stored
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  float* sL = reinterpret_cast<float*>(smem + 7 * TA_TILE + 256);  // [2 halves][128 rows]
 
   const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
@@ -74,10 +81,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
-      mbar_init(&p_full[s], 128);
+      mbar_init(&s_free[s], TA_SOFTMAX);
+      mbar_init(&p_full[s], TA_SOFTMAX);
       mbar_init(&pv_done[s], 1);
     }
+    mbar_init(l_bar, TA_SOFTMAX);
     fence_barrier_init();
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
@@ -146,34 +154,36 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int quad = warp & 3, r = quad * 32 + lane;  // TMEM lane quadrant = warp % 4
+    const int half = (warp - 2) >> 2;                   // this thread's 64 score / O columns
     const int qi = qb * TA_BM + r;                      // query row in the sequence
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = a.scale * 1.4426950408889634f;
+    constexpr int HC = TA_BN / 2;  // columns per thread
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, err)) { ok = false; break; }
       tc_fence_after();
-      float sv[TA_BN];
+      // the whole row for its max (both threads of the row find the same one), this thread's
+      // half for the exponentials
+      float sv[HC];
+      float mx = -INFINITY;
       {
         uint32_t su[TA_BN];
 #pragma unroll
         for (int c = 0; c < TA_BN / 32; ++c) tmem_ld32_nw(lane_base + 128 + s * TA_BN + c * 32, su + c * 32);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < TA_BN; ++c) sv[c] = __uint_as_float(su[c]);
+        for (int c = 0; c < TA_BN; ++c) {
+          float x = __uint_as_float(su[c]);
+          if (j == qb && j * TA_BN + c > qi) x = -INFINITY;  // the diagonal block: causal mask
+          mx = fmaxf(mx, x);
+          if ((c >= HC) == (half == 1)) sv[c % HC] = x;
+        }
       }
       tc_fence_before();
       mbar_arrive(&s_free[s]);
-      if (j == qb) {  // the diagonal block: keys after the query are masked
-#pragma unroll
-        for (int c = 0; c < TA_BN; ++c)
-          if (j * TA_BN + c > qi) sv[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < TA_BN; ++c) mx = fmaxf(mx, sv[c]);
       const float ms = mx * sl2;
       float corr = 1.f;
       if (ms > m_run + 8.f) {
@@ -190,15 +200,15 @@ __global__ void __launch_bounds__(192, 1)
       // the masked keys)
       auto emit = [&](auto mix) {
 #pragma unroll
-        for (int ch = 0; ch < TA_BN / 8; ++ch) {
+        for (int cc = 0; cc < HC / 8; ++cc) {
           float p[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float x = fmaf(sv[ch * 8 + e], sl2, mneg);
-            p[e] = (decltype(mix)::value && (ch & 1)) ? exp2_fma(x) : exp2f(x);  // exp2f(-inf) = 0
+            const float x = fmaf(sv[cc * 8 + e], sl2, mneg);
+            p[e] = (decltype(mix)::value && (cc & 1)) ? exp2_fma(x) : exp2f(x);  // exp2f(-inf) = 0
             sum += p[e];
           }
-          *reinterpret_cast<uint4*>(pt + ta_chunk(r, ch)) =
+          *reinterpret_cast<uint4*>(pt + ta_chunk(r, half * (HC / 8) + cc)) =
               make_uint4(pack_t2<T>(p[0], p[1]), pack_t2<T>(p[2], p[3]), pack_t2<T>(p[4], p[5]),
                          pack_t2<T>(p[6], p[7]));
         }
@@ -207,16 +217,17 @@ __global__ void __launch_bounds__(192, 1)
       else emit(std::true_type{});
       l_run = l_run * corr + sum;
       if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-        // rescale this warp's O rows once the last MMA adding to O (P_{j-1} V_{j-1}) is done
+        // rescale this thread's O columns once the last MMA adding to O (P_{j-1} V_{j-1}) is done
         if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, err)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < TA_D / 32; ++c) {
+        for (int c = 0; c < TA_D / 64; ++c) {
           float ov[32];
-          tmem_ld32(lane_base + c * 32, ov);
+          const uint32_t col = lane_base + half * (TA_D / 2) + c * 32;
+          tmem_ld32(col, ov);
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] *= corr;
-          tmem_st32(lane_base + c * 32, ov);
+          tmem_st32(col, ov);
         }
         tmem_wait_st();
       }
@@ -224,14 +235,20 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&p_full[s]);
     }
+    // the row sum: both halves' partial sums, added in a fixed order
+    sL[half * TA_BM + r] = l_run;
+    mbar_arrive(l_bar);
+    if (ok) ok = mbar_wait(l_bar, 0, err);
     if (ok && mbar_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, err)) {
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* out = reinterpret_cast<T*>(a.out) + ((int64_t)(start + qi) * a.HQ + h) * TA_D;
+      const float l_row = sL[r] + sL[TA_BM + r];
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      T* out = reinterpret_cast<T*>(a.out) + ((int64_t)(start + qi) * a.HQ + h) * TA_D +
+               half * (TA_D / 2);
 #pragma unroll 1
-      for (int c = 0; c < TA_D / 32; ++c) {
+      for (int c = 0; c < TA_D / 64; ++c) {
         float ov[32];
-        tmem_ld32(lane_base + c * 32, ov);
+        tmem_ld32(lane_base + half * (TA_D / 2) + c * 32, ov);
         if (qi < len) {
 #pragma unroll
           for (int u = 0; u < 4; ++u)
@@ -242,7 +259,8 @@ __global__ void __launch_bounds__(192, 1)
                            pack_t2<T>(ov[8 * u + 6] * inv, ov[8 * u + 7] * inv));
         }
       }
-      if (qi < len) a.lse[(int64_t)h * a.n + start + qi] = (m_run + log2f(l_run)) * 0.6931471805599453f;
+      if (qi < len && half == 0)
+        a.lse[(int64_t)h * a.n + start + qi] = (m_run + log2f(l_row)) * 0.6931471805599453f;
     }
   }
   tc_fence_before();
@@ -595,10 +613,10 @@ int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s) {
   int* err = status_word();
   if (bf) {
     smem_optin(reinterpret_cast<const void*>(attn_fwd_tc_kernel<true>), TA_SMEM);
-    launch_k(attn_fwd_tc_kernel<true>, grid, dim3(192), TA_SMEM, s, mq, mk, mv, a, err);
+    launch_k(attn_fwd_tc_kernel<true>, grid, dim3(64 + TA_SOFTMAX), TA_SMEM, s, mq, mk, mv, a, err);
   } else {
     smem_optin(reinterpret_cast<const void*>(attn_fwd_tc_kernel<false>), TA_SMEM);
-    launch_k(attn_fwd_tc_kernel<false>, grid, dim3(192), TA_SMEM, s, mq, mk, mv, a, err);
+    launch_k(attn_fwd_tc_kernel<false>, grid, dim3(64 + TA_SOFTMAX), TA_SMEM, s, mq, mk, mv, a, err);
   }
   return QL_STATUS_OK;
 }
