@@ -102,12 +102,39 @@ def make_batch(rng, vocab, seqs=SEQS, median=MEDIAN, lo=LO, hi=HI, uniform=None)
     return ids, mask, labels, int(lengths.sum())
 
 
-def batches(args, rank, vocab):
-    """The warm-up + timed batches of a rank (both arms draw the same ones)."""
-    rng = np.random.default_rng(1000 + rank)
+def batches(args, rank, vocab, world=1):
+    """The warm-up + timed batches of a rank (both arms draw the same ones). Rank r's sequences
+    are drawn from seed 1000 + r; with several ranks, each step's sequences of all ranks are
+    dealt back to the ranks token-balanced, args.seqs each (dist.balanced_shards)."""
     uniform = tuple(int(x) for x in args.uniform.split(",")) if args.uniform else None
-    return [make_batch(rng, vocab, args.seqs, args.median, args.lo, args.hi, uniform)
-            for _ in range(args.warmup + args.steps)]
+
+    def draws(r):
+        rng = np.random.default_rng(1000 + r)
+        return [make_batch(rng, vocab, args.seqs, args.median, args.lo, args.hi, uniform)
+                for _ in range(args.warmup + args.steps)]
+
+    if world == 1:
+        return draws(rank)
+    from hack_fe30cb28_opus_5_5_ultracode_b200.dist import balanced_shards
+
+    every = [draws(r) for r in range(world)]
+    out = []
+    for step in range(args.warmup + args.steps):
+        rows = []  # (ids, mask, labels) of each sequence of the step, ranks in order
+        for r in range(world):
+            ids, mask, labels, _ = every[r][step]
+            rows += [(ids[i], mask[i], labels[i]) for i in range(ids.shape[0])]
+        lengths = [int(m.sum()) for _, m, _ in rows]
+        mine = balanced_shards(lengths, world, args.seqs)[rank]
+        T = max(lengths[i] for i in mine)
+        ids = np.zeros((len(mine), T), dtype=np.int64)
+        mask = np.zeros((len(mine), T), dtype=np.int64)
+        labels = np.full((len(mine), T), -100, dtype=np.int64)
+        for j, i in enumerate(mine):  # right-padded again to this rank's longest sequence
+            n = lengths[i]
+            ids[j, :n], mask[j, :n], labels[j, :n] = rows[i][0][:n], rows[i][1][:n], rows[i][2][:n]
+        out.append((ids, mask, labels, int(sum(lengths[i] for i in mine))))
+    return out
 
 
 def workload_config(args, world):
@@ -118,10 +145,15 @@ def workload_config(args, world):
         f"Qwen2.5-{args.model.upper()} {args.dtype}, {args.seqs} seqs/rank, lengths "
         + (f"uniform [{args.uniform}]" if args.uniform else
            f"lognormal (median {args.median}, clip [{args.lo},{args.hi}])"))
-    return {"workload": name, "global_batch": args.seqs * world, "seq_len": "varlen",
-            "parallelism": f"dp{world}",
-            "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of activations) is "
-                  "larger than the 126 MB L2"}
+    cfg = {"workload": name, "global_batch": args.seqs * world, "seq_len": "varlen",
+           "parallelism": f"dp{world}",
+           "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of activations) is "
+                 "larger than the 126 MB L2"}
+    if world > 1:
+        cfg["sharding"] = (f"each step's {args.seqs * world} sequences (rank r's drawn from seed "
+                           f"1000 + r) dealt back {args.seqs} per rank, token-balanced "
+                           "(longest first to the least-loaded rank)")
+    return cfg
 
 
 def peaks():
@@ -249,7 +281,7 @@ def run_reference(args, rank, world):
     from hack_fe30cb28_opus_5_5_ultracode_b200.model import QWEN25_1P5B
 
     sample = CpuSample()
-    host = batches(args, 0, QWEN25_1P5B.vocab_size)
+    host = batches(args, 0, QWEN25_1P5B.vocab_size, world)
     vals, secs, threads, desc = [], [], 1, ""
     for i in range(args.warmup + args.steps):
         v, s, threads, desc = sample.run(host[i])
@@ -334,7 +366,7 @@ def run_ours(args, rank, world, local):
     # fp16 mixed precision as HF Trainer runs it: a GradScaler scales the loss before the backward
     # and unscales (and checks) the gradients before the optimizer step; bf16 needs none
     scaler = torch.amp.GradScaler("cuda", enabled=cdt == torch.float16)
-    host = batches(args, rank, cfg.vocab_size)
+    host = batches(args, rank, cfg.vocab_size, world)
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
     hosts = [HostBatch.of(torch.from_numpy(b[1]), torch.from_numpy(b[2])) for b in host]

@@ -35,3 +35,22 @@ class GradReducer:
         if self.world > 1:
             flat.div_(self.world)
         return flat
+
+
+def balanced_shards(lengths, ranks, per_rank):
+    """Deals a data-parallel step's sequences to the ranks, `per_rank` each, so that the ranks'
+    token counts come out as even as a longest-first greedy gets them: each sequence, longest
+    first, goes to the least-loaded rank that still has room (ties: the lower rank, then the
+    earlier sequence). A rank's step time grows with its token count and every rank waits for
+    the slowest in the gradient all-reduce, so an even split is what lets N ranks run N times
+    the tokens. Returns one list of sequence indices per rank, each ascending."""
+    if len(lengths) != ranks * per_rank:
+        raise ValueError(f"{len(lengths)} sequences for {ranks} ranks x {per_rank}")
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    load, shards = [0] * ranks, [[] for _ in range(ranks)]
+    for i in order:
+        k = min((r for r in range(ranks) if len(shards[r]) < per_rank),
+                key=lambda r: (load[r], r))
+        shards[k].append(i)
+        load[k] += int(lengths[i])
+    return [sorted(s) for s in shards]

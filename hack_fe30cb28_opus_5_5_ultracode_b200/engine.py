@@ -230,15 +230,18 @@ class HostBatch:
 
     @classmethod
     def of(cls, attention_mask, labels):
-        """From host (CPU) tensors of a right-padded batch; None if it is not right-padded."""
-        lengths = _right_padded_lengths(attention_mask.to("cpu"))
-        if lengths is None:
+        """From host (CPU) tensors of a right-padded batch; None if it is not right-padded.
+        (numpy on the host arrays: this runs on the step's critical path, before its first
+        launch.)"""
+        m = attention_mask.to("cpu").numpy()
+        if m.ndim != 2 or not (((m == 0) | (m == 1)).all() and (m[:, 1:] <= m[:, :-1]).all()):
             return None
-        lab = labels.to("cpu")
+        lengths = m.sum(axis=1, dtype=np.int64)
+        lab = labels.to("cpu").numpy()
         T = lab.shape[1]
         # a token at column t < length - 1 has target labels[row, t + 1]
-        has_next = torch.arange(T - 1)[None, :] < (torch.tensor(lengths)[:, None] - 1)
-        return cls(lengths, int(((lab[:, 1:] != -100) & has_next).sum()))
+        has_next = np.arange(T - 1)[None, :] < (lengths[:, None] - 1)
+        return cls(lengths.tolist(), int(((lab[:, 1:] != -100) & has_next).sum()))
 
 
 def _index_plan(lengths, T):

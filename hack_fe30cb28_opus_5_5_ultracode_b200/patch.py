@@ -268,8 +268,9 @@ def prepare_inputs(trainer, inputs, device):
     def move(v):
         if not torch.is_tensor(v) or v.device == device:
             return v
-        return v.pin_memory().to(device, non_blocking=True) if device.type == "cuda" \
-            else v.to(device)
+        if device.type != "cuda":
+            return v.to(device)
+        return (v if v.is_pinned() else v.pin_memory()).to(device, non_blocking=True)
 
     moved = {k: move(v) for k, v in inputs.items()}
     if host is not None and "input_ids" in moved:

@@ -53,3 +53,56 @@ def test_grad_reducer_averages_over_two_gloo_ranks():
     for rank, flat, tmax in results:
         assert flat == pytest.approx(expect)
         assert tmax == 4.0
+
+
+def test_balanced_shards_deal_every_sequence_once_and_even_out_tokens():
+    """The bench's data-parallel batches: each step's sequences of all ranks dealt back per_rank
+    each, longest first to the least-loaded rank (every sequence exactly once, deterministic),
+    evening out the ranks' token counts."""
+    import random
+
+    from hack_fe30cb28_opus_5_5_ultracode_b200.dist import balanced_shards
+
+    rng = random.Random(7)
+    for ranks, per in ((2, 4), (4, 4), (8, 4), (8, 8), (3, 1)):
+        lengths = [int(min(1024, max(32, rng.lognormvariate(5.7, 0.6)))) for _ in range(ranks * per)]
+        shards = balanced_shards(lengths, ranks, per)
+        assert sorted(i for s in shards for i in s) == list(range(ranks * per))
+        assert all(len(s) == per and s == sorted(s) for s in shards)
+        assert shards == balanced_shards(lengths, ranks, per)
+        loads = [sum(lengths[i] for i in s) for s in shards]
+        # no worse than the ranks' own draws, and within one longest sequence of the mean
+        own = [sum(lengths[r * per:(r + 1) * per]) for r in range(ranks)]
+        assert max(loads) <= max(own)
+        assert max(loads) - sum(loads) / ranks <= max(lengths)
+    with pytest.raises(ValueError):
+        balanced_shards([1, 2, 3], 2, 2)
+
+
+def test_bench_batches_are_the_dealt_shards():
+    """bench.batches with several ranks: the ranks' batches of a step hold every drawn sequence
+    once, right-padded, with labels -100 past each length, and rank 0 alone equals its own draws."""
+    import sys
+
+    import numpy as np
+
+    sys.argv = ["bench.py", "--steps", "2", "--warmup", "1"]
+    import bench
+
+    args = bench.parse()
+    world, vocab = 4, 1000
+    own = [bench.batches(args, r, vocab) for r in range(world)]
+    dealt = [bench.batches(args, r, vocab, world) for r in range(world)]
+    for step in range(args.warmup + args.steps):
+        drawn = sorted(tuple(ids[i, :m[i].sum()]) for ids, m, _, _ in (o[step] for o in own)
+                       for i in range(ids.shape[0]))
+        got = []
+        for ids, mask, labels, n in (d[step] for d in dealt):
+            assert ids.shape == mask.shape == labels.shape and n == int(mask.sum())
+            for i in range(ids.shape[0]):
+                L = int(mask[i].sum())
+                assert mask[i, :L].all() and not mask[i, L:].any()
+                assert (labels[i, L:] == -100).all()
+                got.append(tuple(ids[i, :L]))
+        assert sorted(got) == drawn
+    assert all(np.array_equal(a[0], b[0]) for a, b in zip(bench.batches(args, 0, vocab), own[0]))
