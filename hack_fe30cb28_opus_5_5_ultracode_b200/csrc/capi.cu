@@ -194,7 +194,7 @@ int ql_set_pdl(int on) {
 }
 
 int ql_gemm_set_mode(int mode) {
-  if (mode < 0 || mode > 2) return done(QL_STATUS_BAD_ARG, "ql_gemm_set_mode");
+  if (mode < 0 || mode > 6 || (mode & 3) == 3) return done(QL_STATUS_BAD_ARG, "ql_gemm_set_mode");
   ql::gemm_set_mode(mode);
   return QL_STATUS_OK;
 }

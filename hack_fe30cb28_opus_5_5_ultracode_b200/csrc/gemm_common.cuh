@@ -30,9 +30,11 @@ struct GemmArgs {
 // Epilogue staging for TMA stores of a 16-bit C: per epilogue warp two 32 x 32 buffers of 2 KB.
 constexpr int EPI_BYTES = 4 * 2 * 2048;
 
-template <int BN, bool kEpi = false>
+// KC: 64-element K chunks per pipeline stage (1: one 2-D copy per 64-wide box; 2: one 3-D copy
+// of two chunks per operand, see tma_load_3d).
+template <int BN, bool kEpi = false, int KC = 1>
 struct GemmCfg {
-  static constexpr int BM = 128, BK = 64;
+  static constexpr int BM = 128, BK = 64 * KC;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -124,7 +126,7 @@ static inline EncodeTiledFn encode_fn() {
 struct MapKey {
   uintptr_t ptr;
   int64_t rows, cols, ld;
-  int box_rows, kind;  // kind: 0 K-major 128B-swizzle fp16, 1 the same bf16, 2 / 3 store maps
+  int box_rows, kind;  // kind: 0 / 1 K-major fp16 / bf16, 2 / 3 store maps, 4 + 2 chunks + bf16: 3-D
   bool operator==(const MapKey& o) const {
     return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld &&
            box_rows == o.box_rows && kind == o.kind;
@@ -171,6 +173,40 @@ static inline int make_kmajor_map(CUtensorMap* map, const void* ptr, int64_t row
     return QL_STATUS_OK;
   }
   const int rc = encode_kmajor_map(map, ptr, rows, cols, ld, box_rows, bf16);
+  if (rc == QL_STATUS_OK) cache.emplace(key, *map);
+  return rc;
+}
+
+// The 3-D view of a row-major [rows, cols] 16-bit matrix (row stride ld elements, cols a multiple
+// of 64): {64 columns, rows, cols / 64 chunks}, chunk stride 128 B, 128-byte swizzle, boxes of
+// {64, box_rows, box_chunks}. K-major operands take box_chunks 2 (two K chunks of box_rows rows);
+// an MN-major operand [K, N] takes box_rows K rows of box_chunks 64-column N chunks.
+static inline int encode_chunked_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
+                                     int64_t ld, int box_rows, int box_chunks, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr || cols % 64 != 0) return QL_STATUS_CUDA;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_chunks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QL_STATUS_OK : QL_STATUS_CUDA;
+}
+
+static inline int make_chunked_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
+                                   int64_t ld, int box_rows, int box_chunks, bool bf16) {
+  const MapKey key{reinterpret_cast<uintptr_t>(ptr), rows, cols, ld, box_rows,
+                   4 + 2 * box_chunks + (bf16 ? 1 : 0)};
+  auto& cache = map_cache();
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *map = it->second;
+    return QL_STATUS_OK;
+  }
+  const int rc = encode_chunked_map(map, ptr, rows, cols, ld, box_rows, box_chunks, bf16);
   if (rc == QL_STATUS_OK) cache.emplace(key, *map);
   return rc;
 }

@@ -25,13 +25,13 @@
 
 namespace ql {
 
-template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN, int KC>
 __global__ void __launch_bounds__(192, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
   pdl_trigger();  // setup below reads no global memory; pdl_wait() follows it
   constexpr bool kTmaC = sizeof(OutT) == 2;
-  using Cfg = GemmCfg<BN, kTmaC>;
+  using Cfg = GemmCfg<BN, kTmaC, KC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -83,13 +83,21 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(sa, &tma_a, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
-          if constexpr (B_MN) {  // B stored [K, N]: boxes of 64 N-columns x 64 K-rows, 8 KB each
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * 8192, &tma_b, &full[stage], nb * BN + j * 64, kb * Cfg::BK);
+          if constexpr (KC == 2) {  // one 3-D copy per operand: two 64-wide K chunks
+            tma_load_3d(sa, &tma_a, &full[stage], 0, mb * Cfg::BM, kb * 2);
+            if constexpr (B_MN)  // [BN / 64 N chunks][128 K rows][64]
+              tma_load_3d(sb, &tma_b, &full[stage], 0, kb * Cfg::BK, nb * (BN / 64));
+            else
+              tma_load_3d(sb, &tma_b, &full[stage], 0, nb * BN, kb * 2);
           } else {
-            tma_load_2d(sb, &tma_b, &full[stage], kb * Cfg::BK, nb * BN);
+            tma_load_2d(sa, &tma_a, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
+            if constexpr (B_MN) {  // B stored [K, N]: boxes of 64 N-columns x 64 K-rows, 8 KB each
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sb + j * 8192, &tma_b, &full[stage], nb * BN + j * 64, kb * Cfg::BK);
+            } else {
+              tma_load_2d(sb, &tma_b, &full[stage], kb * Cfg::BK, nb * BN);
+            }
           }
           if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
         }
@@ -116,10 +124,11 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 16; ++k) {
-            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, 8192, 1024)
-                                     : umma_desc_k_sw128(sb + k * 32);
-            umma_f16(tmem_d, umma_desc_k_sw128(sa + k * 32), db, idesc,
+          for (int k = 0; k < Cfg::BK / 16; ++k) {  // K chunk k / 4, 16-wide step k % 4 of it
+            const uint32_t ka = (k >> 2) * (Cfg::BM * 128) + (k & 3) * 32;
+            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, Cfg::BK * 128, 1024)
+                                     : umma_desc_k_sw128(sb + (k >> 2) * (BN * 128) + (k & 3) * 32);
+            umma_f16(tmem_d, umma_desc_k_sw128(sa + ka), db, idesc,
                      (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -261,9 +270,9 @@ __global__ void __launch_bounds__(192, 1)
 //   tfull[a]  each CTA's: the accumulator is complete (commit to both)
 //   tempty[a] even CTA's: 8 arrivals, the 4 epilogue warps of each CTA
 // ---------------------------------------------------------------------------------------------
-template <int BN, bool kEpi = false>
+template <int BN, bool kEpi = false, int KC = 1>
 struct PairCfg {
-  static constexpr int BM = 128, BK = 64, HB = BN / 2;
+  static constexpr int BM = 128, BK = 64 * KC, HB = BN / 2;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = HB * BK * 2;  // this CTA's half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -276,14 +285,14 @@ struct PairCfg {
   static_assert(B_BYTES % 1024 == 0, "128-byte swizzle atoms of 8 rows");
 };
 
-template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN, int KC>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
   pdl_trigger();  // setup below reads no global memory; pdl_wait() follows it
   constexpr bool kTmaC = sizeof(OutT) == 2;
-  using Cfg = PairCfg<BN, kTmaC>;
+  using Cfg = PairCfg<BN, kTmaC, KC>;
   using InT = typename std::conditional<IS_BF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -336,13 +345,21 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
-          tma_load_2d_pair(sa, &tma_a, &full[stage], kb * Cfg::BK, arow);
-          if constexpr (B_MN) {
-#pragma unroll
-            for (int j = 0; j < Cfg::HB / 64; ++j)
-              tma_load_2d_pair(sb + j * 8192, &tma_b, &full[stage], brow + j * 64, kb * Cfg::BK);
+          if constexpr (KC == 2) {  // one 3-D copy per operand: two 64-wide K chunks
+            tma_load_3d_pair(sa, &tma_a, &full[stage], 0, arow, kb * 2);
+            if constexpr (B_MN)
+              tma_load_3d_pair(sb, &tma_b, &full[stage], 0, kb * Cfg::BK, brow / 64);
+            else
+              tma_load_3d_pair(sb, &tma_b, &full[stage], 0, brow, kb * 2);
           } else {
-            tma_load_2d_pair(sb, &tma_b, &full[stage], kb * Cfg::BK, brow);
+            tma_load_2d_pair(sa, &tma_a, &full[stage], kb * Cfg::BK, arow);
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < Cfg::HB / 64; ++j)
+                tma_load_2d_pair(sb + j * 8192, &tma_b, &full[stage], brow + j * 64, kb * Cfg::BK);
+            } else {
+              tma_load_2d_pair(sb, &tma_b, &full[stage], kb * Cfg::BK, brow);
+            }
           }
           if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
         }
@@ -367,10 +384,11 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 16; ++k) {
-            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, 8192, 1024)
-                                     : umma_desc_k_sw128(sb + k * 32);
-            umma_f16_pair(tmem_d, umma_desc_k_sw128(sa + k * 32), db, idesc,
+          for (int k = 0; k < Cfg::BK / 16; ++k) {  // K chunk k / 4, 16-wide step k % 4 of it
+            const uint32_t ka = (k >> 2) * (Cfg::BM * 128) + (k & 3) * 32;
+            const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, Cfg::BK * 128, 1024)
+                                     : umma_desc_k_sw128(sb + (k >> 2) * (Cfg::HB * 128) + (k & 3) * 32);
+            umma_f16_pair(tmem_d, umma_desc_k_sw128(sa + ka), db, idesc,
                           (kb != 0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
@@ -458,11 +476,12 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN, int KC>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                        cudaStream_t stream) {
-  using Cfg = GemmCfg<BN, sizeof(OutT) == 2>;
-  auto kern = gemm_tn_kernel<BN, IS_BF16, OutT, B_MN>;
+  using Cfg = GemmCfg<BN, sizeof(OutT) == 2, KC>;
+  static_assert(Cfg::STAGES >= 2, "at least two pipeline stages");
+  auto kern = gemm_tn_kernel<BN, IS_BF16, OutT, B_MN, KC>;
   static bool configured = false;  // one static per instantiation
   if (!configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) !=
@@ -499,11 +518,12 @@ static int pair_slots(K kern, int smem) {
   return clusters;
 }
 
-template <int BN, bool IS_BF16, typename OutT, bool B_MN>
+template <int BN, bool IS_BF16, typename OutT, bool B_MN, int KC>
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                        cudaStream_t stream) {
-  using Cfg = PairCfg<BN, sizeof(OutT) == 2>;
-  auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN>;
+  using Cfg = PairCfg<BN, sizeof(OutT) == 2, KC>;
+  static_assert(Cfg::STAGES >= 2, "at least two pipeline stages");
+  auto kern = gemm_pair_kernel<BN, IS_BF16, OutT, B_MN, KC>;
   static int slots = 0;  // one per instantiation
   if (slots == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) !=
@@ -531,40 +551,46 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   return launched(1);
 }
 
-template <int BN, bool IS_BF16, bool B_MN>
+template <int BN, bool IS_BF16, bool B_MN, int KC>
 static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                              cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN>(ma, mb, mc, a, s);
-    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, a, s);
-    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN>(ma, mb, mc, a, s);
+    case QL_F16: return launch_pair<BN, IS_BF16, __half, B_MN, KC>(ma, mb, mc, a, s);
+    case QL_BF16: return launch_pair<BN, IS_BF16, __nv_bfloat16, B_MN, KC>(ma, mb, mc, a, s);
+    case QL_F32: return launch_pair<BN, IS_BF16, float, B_MN, KC>(ma, mb, mc, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
 
 template <int BN, bool B_MN>
 static int dispatch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
-                         bool bf16, cudaStream_t s) {
-  return bf16 ? dispatch_pair_out<BN, true, B_MN>(ma, mb, mc, a, s)
-              : dispatch_pair_out<BN, false, B_MN>(ma, mb, mc, a, s);
+                         bool bf16, int kc, cudaStream_t s) {
+  if (kc == 2)
+    return bf16 ? dispatch_pair_out<BN, true, B_MN, 2>(ma, mb, mc, a, s)
+                : dispatch_pair_out<BN, false, B_MN, 2>(ma, mb, mc, a, s);
+  return bf16 ? dispatch_pair_out<BN, true, B_MN, 1>(ma, mb, mc, a, s)
+              : dispatch_pair_out<BN, false, B_MN, 1>(ma, mb, mc, a, s);
 }
 
-template <int BN, bool IS_BF16, bool B_MN>
+template <int BN, bool IS_BF16, bool B_MN, int KC>
 static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                         cudaStream_t s) {
   switch (a.out_dtype) {
-    case QL_F16: return launch_gemm<BN, IS_BF16, __half, B_MN>(ma, mb, mc, a, s);
-    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16, B_MN>(ma, mb, mc, a, s);
-    case QL_F32: return launch_gemm<BN, IS_BF16, float, B_MN>(ma, mb, mc, a, s);
+    case QL_F16: return launch_gemm<BN, IS_BF16, __half, B_MN, KC>(ma, mb, mc, a, s);
+    case QL_BF16: return launch_gemm<BN, IS_BF16, __nv_bfloat16, B_MN, KC>(ma, mb, mc, a, s);
+    case QL_F32: return launch_gemm<BN, IS_BF16, float, B_MN, KC>(ma, mb, mc, a, s);
   }
   return QL_STATUS_BAD_ARG;
 }
 
 template <int BN, bool B_MN>
 static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a, bool bf16,
-                       cudaStream_t s) {
-  return bf16 ? dispatch_out<BN, true, B_MN>(ma, mb, mc, a, s)
-              : dispatch_out<BN, false, B_MN>(ma, mb, mc, a, s);
+                       int kc, cudaStream_t s) {
+  if (kc == 2)
+    return bf16 ? dispatch_out<BN, true, B_MN, 2>(ma, mb, mc, a, s)
+                : dispatch_out<BN, false, B_MN, 2>(ma, mb, mc, a, s);
+  return bf16 ? dispatch_out<BN, true, B_MN, 1>(ma, mb, mc, a, s)
+              : dispatch_out<BN, false, B_MN, 1>(ma, mb, mc, a, s);
 }
 
 // Split-K workspace: tile counters first (a fixed region, left all-zero by every launch, so
@@ -578,7 +604,8 @@ struct GemmPlan {
   bool pair;  // 2-SM pair tiles (256 x bn)
 };
 
-// Tile-kind selection: 0 = cost model, 1 = single-CTA tiles only, 2 = pair tiles where possible.
+// Tile-kind selection (mode & 3): 0 = cost model, 1 = single-CTA tiles only, 2 = pair tiles
+// where possible; mode & 4: single-chunk (2-D copy) stages only.
 static std::atomic<int> g_gemm_mode{0};
 void gemm_set_mode(int mode) { g_gemm_mode.store(mode); }
 
@@ -608,7 +635,7 @@ static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
   // K <= 4096: the gate/up and lm_head forwards), the shapes where they measured faster than the
   // single-CTA tiles at 1-4K rows. Elsewhere the 256-row pairs waste rows of M and were slower.
-  const int mode = g_gemm_mode.load();
+  const int mode = g_gemm_mode.load() & 3;
   if (mode == 2 || (mode == 0 && !b_mn && N >= 16384 && K <= 4096 && M >= 512)) {
     int pbn = 0;
     int64_t punits = 0;
@@ -689,13 +716,27 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
     g.splits = 1;
     g.kb_per_split = (int)cdiv(K, 64);
   }
+  // Two 64-wide K chunks per pipeline stage, each operand in one 3-D copy, where K is a multiple
+  // of 128 (and an MN-major B's N of 64); single-chunk stages (2-D copies) otherwise.
+  const int kc = (K % 128 == 0 && (!b_mn || N % 64 == 0) && !(g_gemm_mode.load() & 4)) ? 2 : 1;
+  const int brows = g.pair ? g.bn / 2 : g.bn;  // B rows (or MN-major columns) per CTA
   CUtensorMap ma, mb;
-  if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  if (b_mn) {
-    if (make_kmajor_map(&mb, B, K, N, ldb, 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-  } else {
-    if (make_kmajor_map(&mb, B, N, K, ldb, g.pair ? g.bn / 2 : g.bn, bf16) != QL_STATUS_OK)
+  if (kc == 2) {
+    if (make_chunked_map(&ma, A, M, K, lda, 128, 2, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+    if (b_mn ? make_chunked_map(&mb, B, K, N, ldb, 128, brows / 64, bf16) != QL_STATUS_OK
+             : make_chunked_map(&mb, B, N, K, ldb, brows, 2, bf16) != QL_STATUS_OK)
       return QL_STATUS_CUDA;
+    // the split-K plan is in 64-wide blocks: the same split points rounded up to whole stages
+    const int kper = (int)cdiv(g.kb_per_split, 2);
+    g.kb_per_split = kper;
+    g.splits = (int)cdiv(cdiv(K, 128), kper);
+  } else {
+    if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+    if (b_mn) {
+      if (make_kmajor_map(&mb, B, K, N, ldb, 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+    } else {
+      if (make_kmajor_map(&mb, B, N, K, ldb, brows, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+    }
   }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
              g.kb_per_split, nullptr, nullptr, 0};
@@ -714,28 +755,28 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
   }
   if (g.pair) {
     if (b_mn) {
-      if (g.bn == 128) return dispatch_pair<128, true>(ma, mb, mc, a, bf16, stream);
-      return dispatch_pair<256, true>(ma, mb, mc, a, bf16, stream);
+      if (g.bn == 128) return dispatch_pair<128, true>(ma, mb, mc, a, bf16, kc, stream);
+      return dispatch_pair<256, true>(ma, mb, mc, a, bf16, kc, stream);
     }
     switch (g.bn) {
-      case 128: return dispatch_pair<128, false>(ma, mb, mc, a, bf16, stream);
-      case 192: return dispatch_pair<192, false>(ma, mb, mc, a, bf16, stream);
-      default: return dispatch_pair<256, false>(ma, mb, mc, a, bf16, stream);
+      case 128: return dispatch_pair<128, false>(ma, mb, mc, a, bf16, kc, stream);
+      case 192: return dispatch_pair<192, false>(ma, mb, mc, a, bf16, kc, stream);
+      default: return dispatch_pair<256, false>(ma, mb, mc, a, bf16, kc, stream);
     }
   }
   if (b_mn) {
     switch (g.bn) {
-      case 128: return dispatch_in<128, true>(ma, mb, mc, a, bf16, stream);
-      case 192: return dispatch_in<192, true>(ma, mb, mc, a, bf16, stream);
-      default: return dispatch_in<256, true>(ma, mb, mc, a, bf16, stream);
+      case 128: return dispatch_in<128, true>(ma, mb, mc, a, bf16, kc, stream);
+      case 192: return dispatch_in<192, true>(ma, mb, mc, a, bf16, kc, stream);
+      default: return dispatch_in<256, true>(ma, mb, mc, a, bf16, kc, stream);
     }
   }
   switch (g.bn) {
-    case 96: return dispatch_in<96, false>(ma, mb, mc, a, bf16, stream);
-    case 128: return dispatch_in<128, false>(ma, mb, mc, a, bf16, stream);
-    case 192: return dispatch_in<192, false>(ma, mb, mc, a, bf16, stream);
-    case 224: return dispatch_in<224, false>(ma, mb, mc, a, bf16, stream);
-    default: return dispatch_in<256, false>(ma, mb, mc, a, bf16, stream);
+    case 96: return dispatch_in<96, false>(ma, mb, mc, a, bf16, kc, stream);
+    case 128: return dispatch_in<128, false>(ma, mb, mc, a, bf16, kc, stream);
+    case 192: return dispatch_in<192, false>(ma, mb, mc, a, bf16, kc, stream);
+    case 224: return dispatch_in<224, false>(ma, mb, mc, a, bf16, kc, stream);
+    default: return dispatch_in<256, false>(ma, mb, mc, a, bf16, kc, stream);
   }
 }
 

@@ -119,7 +119,8 @@ def gemm(a, b, out=None, bias=None, accumulate=False, out_dtype=None, residual=N
 
 
 def gemm_set_mode(mode):
-    """Tile kind of the GEMMs: 0 per-shape cost model, 1 single-CTA tiles, 2 2-SM pair tiles."""
+    """Tile kind of the GEMMs (mode & 3): 0 per-shape cost model, 1 single-CTA tiles, 2 2-SM
+    pair tiles; + 4: one 64-wide K chunk per pipeline stage (2-D copies) instead of two."""
     call("ql_gemm_set_mode", int(mode))
 
 

@@ -303,3 +303,31 @@ def _split_k_case(M, N, K, dt):
     assert int(ws[:2048].count_nonzero()) == 0  # the tile counters are left at zero
     assert ops.device_status() == 0
 
+
+
+@pytest.mark.parametrize("M,N,K,b_kn", [(1090, 2048, 1536, False), (1090, 17920, 1536, False),
+                                        (1090, 1536, 1536, True), (300, 8960, 1536, True),
+                                        (777, 256, 384, False), (2100, 1536, 2048, True)])
+@pytest.mark.parametrize("tiles", [0, 1, 2])
+def test_gemm_two_chunk_stages_equal_single_chunk(M, N, K, b_kn, tiles):
+    """Pipeline stages of two 64-wide K chunks (one 3-D copy per operand: the default where K is
+    a multiple of 128) and of one chunk (2-D copies, mode bit 4) issue the same MMAs in the same
+    K order, so without split-K (K <= 2048 here) the outputs are equal; every tile kind
+    (cost model, single-CTA, 2-SM pairs)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=DEV, generator=g).half()
+    b = (torch.randn(K, N, device=DEV, generator=g) * 0.05).half() if b_kn else \
+        (torch.randn(N, K, device=DEV, generator=g) * 0.05).half()
+    try:
+        ops.gemm_set_mode(tiles)
+        two = ops.gemm(a, b, b_kn=b_kn)
+        ops.gemm_set_mode(tiles + 4)
+        one = ops.gemm(a, b, b_kn=b_kn)
+    finally:
+        ops.gemm_set_mode(0)
+    assert torch.equal(two, one)
+    ref = a.float() @ (b.float() if b_kn else b.float().t())
+    assert (two.float() - ref).abs().max().item() / (ref.abs().max().item() + 1e-6) < 4e-3
+    assert ops.device_status() == 0
