@@ -100,8 +100,8 @@ __global__ void __launch_bounds__(64 + TA_SOFTMAX, 1)
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, TA_TILE);
-      tma_load_2d(sQ, &tq, q_full, h * TA_D, start + qb * TA_BM);
-      tma_load_2d(sQ + TA_BOX, &tq, q_full, h * TA_D + 64, start + qb * TA_BM);
+      // each tile in one 3-D copy of both 64-column halves of the head ([2][128 rows][64])
+      tma_load_3d(sQ, &tq, q_full, 0, start + qb * TA_BM, h * 2);
       for (int j = 0; j < nkb; ++j) {
         const int s = j & 1;
         if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, err)) break;
@@ -109,10 +109,8 @@ __global__ void __launch_bounds__(64 + TA_SOFTMAX, 1)
         uint8_t* v = k + TA_TILE;
         const int row = start + j * TA_BN;
         mbar_arrive_expect_tx(&kv_full[s], 2 * TA_TILE);
-        tma_load_2d(k, &tk, &kv_full[s], kvh * TA_D, row);
-        tma_load_2d(k + TA_BOX, &tk, &kv_full[s], kvh * TA_D + 64, row);
-        tma_load_2d(v, &tv, &kv_full[s], kvh * TA_D, row);
-        tma_load_2d(v + TA_BOX, &tv, &kv_full[s], kvh * TA_D + 64, row);
+        tma_load_3d(k, &tk, &kv_full[s], 0, row, kvh * 2);
+        tma_load_3d(v, &tv, &kv_full[s], 0, row, kvh * 2);
       }
     }
   } else if (warp == 1) {
@@ -376,10 +374,9 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * TB_KT);
-      tma_load_2d(smem + TB_OFF_K, &tk, kv_full, kvh * 128, start + key0);
-      tma_load_2d(smem + TB_OFF_K + TB_KBOX, &tk, kv_full, kvh * 128 + 64, start + key0);
-      tma_load_2d(smem + TB_OFF_V, &tv, kv_full, kvh * 128, start + key0);
-      tma_load_2d(smem + TB_OFF_V + TB_KBOX, &tv, kv_full, kvh * 128 + 64, start + key0);
+      // each tile in one 3-D copy of both 64-column halves of the head
+      tma_load_3d(smem + TB_OFF_K, &tk, kv_full, 0, start + key0, kvh * 2);
+      tma_load_3d(smem + TB_OFF_V, &tv, kv_full, 0, start + key0, kvh * 2);
     }
     const float* lse = a.lse + (int64_t)h * a.n + start;
     const float* dvec = a.dvec + (int64_t)h * a.n + start;
@@ -389,10 +386,8 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) {
         uint8_t* st = smem + TB_OFF_STAGE + s * 2 * TB_QT;
         mbar_arrive_expect_tx(&qd_full[s], 2 * TB_QT);
-        tma_load_2d(st, &tq, &qd_full[s], h * 128, start + q0);
-        tma_load_2d(st + TB_QBOX, &tq, &qd_full[s], h * 128 + 64, start + q0);
-        tma_load_2d(st + TB_QT, &tdo, &qd_full[s], h * 128, start + q0);
-        tma_load_2d(st + TB_QT + TB_QBOX, &tdo, &qd_full[s], h * 128 + 64, start + q0);
+        tma_load_3d(st, &tq, &qd_full[s], 0, start + q0, h * 2);
+        tma_load_3d(st + TB_QT, &tdo, &qd_full[s], 0, start + q0, h * 2);
       }
 #pragma unroll
       for (int t = lane; t < TB_BQ; t += 32) {
@@ -598,16 +593,17 @@ int exp2_fma_eval(const float* x, float* y, int64_t n, cudaStream_t s) {
   return launched(1);
 }
 
-// Host side: tensor maps over q [n, HQ * 128] and k / v [n, HKV * 128] (boxes of 64 columns x
-// 128 rows with the 128-byte swizzle; rows past n read as zeros).
+// Host side: tensor maps over q [n, HQ * 128] and k / v [n, HKV * 128] seen as {64 columns, n rows,
+// 2 H column chunks} (128-byte swizzle; a box of {64, 128, 2} is one head's tile of 128 rows, both
+// halves, in one copy; rows past n read as zeros).
 int attn_fwd_tc(const AttnFwdC& a, cudaStream_t s) {
   if (a.D != TA_D) return QL_STATUS_UNSUPPORTED;
   const bool bf = a.dtype == QL_BF16;
   CUtensorMap mq, mk, mv;
   const int64_t wq = (int64_t)a.HQ * TA_D, wk = (int64_t)a.HKV * TA_D;
-  if (make_kmajor_map(&mq, a.q, a.n, wq, wq, 128, bf) != QL_STATUS_OK ||
-      make_kmajor_map(&mk, a.k, a.n, wk, wk, 128, bf) != QL_STATUS_OK ||
-      make_kmajor_map(&mv, a.v, a.n, wk, wk, 128, bf) != QL_STATUS_OK)
+  if (make_chunked_map(&mq, a.q, a.n, wq, wq, 128, 2, bf) != QL_STATUS_OK ||
+      make_chunked_map(&mk, a.k, a.n, wk, wk, 128, 2, bf) != QL_STATUS_OK ||
+      make_chunked_map(&mv, a.v, a.n, wk, wk, 128, 2, bf) != QL_STATUS_OK)
     return QL_STATUS_CUDA;
   dim3 grid((unsigned)cdiv(a.max_len, TA_BM), (unsigned)a.HQ, (unsigned)a.B);
   int* err = status_word();
@@ -626,10 +622,10 @@ int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s) {
   const bool bf = a.dtype == QL_BF16;
   CUtensorMap mq, mdo, mk, mv;
   const int64_t wq = (int64_t)a.HQ * 128, wk = (int64_t)a.HKV * 128;
-  if (make_kmajor_map(&mq, a.q, a.n, wq, wq, TB_BQ, bf) != QL_STATUS_OK ||
-      make_kmajor_map(&mdo, a.dout, a.n, wq, wq, TB_BQ, bf) != QL_STATUS_OK ||
-      make_kmajor_map(&mk, a.k, a.n, wk, wk, TB_BK, bf) != QL_STATUS_OK ||
-      make_kmajor_map(&mv, a.v, a.n, wk, wk, TB_BK, bf) != QL_STATUS_OK)
+  if (make_chunked_map(&mq, a.q, a.n, wq, wq, TB_BQ, 2, bf) != QL_STATUS_OK ||
+      make_chunked_map(&mdo, a.dout, a.n, wq, wq, TB_BQ, 2, bf) != QL_STATUS_OK ||
+      make_chunked_map(&mk, a.k, a.n, wk, wk, TB_BK, 2, bf) != QL_STATUS_OK ||
+      make_chunked_map(&mv, a.v, a.n, wk, wk, TB_BK, 2, bf) != QL_STATUS_OK)
     return QL_STATUS_CUDA;
   dim3 grid((unsigned)(cdiv(a.max_len, TB_BK) * cdiv(a.max_len, TB_QCH)), (unsigned)a.HQ, (unsigned)a.B);
   int* err = status_word();
