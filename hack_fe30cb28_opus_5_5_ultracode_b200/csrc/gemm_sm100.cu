@@ -565,9 +565,7 @@ static int dispatch_pair_out(const CUtensorMap& ma, const CUtensorMap& mb, const
 template <int BN, bool B_MN>
 static int dispatch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a,
                          bool bf16, int kc, cudaStream_t s) {
-  if (kc == 2)
-    return bf16 ? dispatch_pair_out<BN, true, B_MN, 2>(ma, mb, mc, a, s)
-                : dispatch_pair_out<BN, false, B_MN, 2>(ma, mb, mc, a, s);
+  if (kc != 1) return QL_STATUS_UNSUPPORTED;  // pair tiles keep single-chunk stages (gemm_core)
   return bf16 ? dispatch_pair_out<BN, true, B_MN, 1>(ma, mb, mc, a, s)
               : dispatch_pair_out<BN, false, B_MN, 1>(ma, mb, mc, a, s);
 }
@@ -586,9 +584,12 @@ static int dispatch_out(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 template <int BN, bool B_MN>
 static int dispatch_in(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmArgs& a, bool bf16,
                        int kc, cudaStream_t s) {
-  if (kc == 2)
-    return bf16 ? dispatch_out<BN, true, B_MN, 2>(ma, mb, mc, a, s)
-                : dispatch_out<BN, false, B_MN, 2>(ma, mb, mc, a, s);
+  if constexpr (BN <= 128) {  // two-chunk stages: tiles of up to 128 columns only (gemm_core)
+    if (kc == 2)
+      return bf16 ? dispatch_out<BN, true, B_MN, 2>(ma, mb, mc, a, s)
+                  : dispatch_out<BN, false, B_MN, 2>(ma, mb, mc, a, s);
+  }
+  if (kc != 1) return QL_STATUS_UNSUPPORTED;
   return bf16 ? dispatch_out<BN, true, B_MN, 1>(ma, mb, mc, a, s)
               : dispatch_out<BN, false, B_MN, 1>(ma, mb, mc, a, s);
 }
@@ -716,9 +717,14 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
     g.splits = 1;
     g.kb_per_split = (int)cdiv(K, 64);
   }
-  // Two 64-wide K chunks per pipeline stage, each operand in one 3-D copy, where K is a multiple
-  // of 128 (and an MN-major B's N of 64); single-chunk stages (2-D copies) otherwise.
-  const int kc = (K % 128 == 0 && (!b_mn || N % 64 == 0) && !(g_gemm_mode.load() & 4)) ? 2 : 1;
+  // Two 64-wide K chunks per pipeline stage, each operand in one 3-D copy (32 KB boxes stream
+  // from L2 faster than 16 KB ones), for single-CTA tiles of up to 128 columns, where the larger
+  // stages still leave three of them in flight, and K is a multiple of 128 (an MN-major B's N of
+  // 64). Wider tiles would drop to two stages and measured slower (the down projection 34.7 ->
+  // 40.2 us, its data gradient 29.6 -> 33.7 us, the 2-SM gate/up tiles 50 -> 52 us); the qkv and
+  // o products (tiles of 96-128 columns) gained 20-25 %.
+  const int kc = (!g.pair && g.bn <= 128 && K % 128 == 0 && (!b_mn || N % 64 == 0) &&
+                  !(g_gemm_mode.load() & 4)) ? 2 : 1;
   const int brows = g.pair ? g.bn / 2 : g.bn;  // B rows (or MN-major columns) per CTA
   CUtensorMap ma, mb;
   if (kc == 2) {

@@ -108,7 +108,8 @@ int64_t ql_gemm_workspace_bytes(int M, int N, int K);
  * in the reference): mode & 3 = 0 chosen per shape by the cost model (default), 1 single-CTA
  * 128-row tiles only, 2 2-SM 256-row pair tiles (tcgen05 cta_group::2) for every shape they
  * support; mode & 4: pipeline stages of one 64-wide K chunk (one 2-D copy per 64-column box)
- * instead of the default two chunks in one 3-D copy per operand where K is a multiple of 128. */
+ * instead of two chunks in one 3-D copy per operand (the default for single-CTA tiles of up to
+ * 128 columns where K is a multiple of 128). */
 int ql_gemm_set_mode(int mode);
 
 /* ---- RMSNorm with the LoRA dropout inputs --------------------------------------------------

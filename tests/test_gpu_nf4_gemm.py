@@ -310,10 +310,11 @@ def _split_k_case(M, N, K, dt):
                                         (777, 256, 384, False), (2100, 1536, 2048, True)])
 @pytest.mark.parametrize("tiles", [0, 1, 2])
 def test_gemm_two_chunk_stages_equal_single_chunk(M, N, K, b_kn, tiles):
-    """Pipeline stages of two 64-wide K chunks (one 3-D copy per operand: the default where K is
-    a multiple of 128) and of one chunk (2-D copies, mode bit 4) issue the same MMAs in the same
-    K order, so without split-K (K <= 2048 here) the outputs are equal; every tile kind
-    (cost model, single-CTA, 2-SM pairs)."""
+    """Pipeline stages of two 64-wide K chunks (one 3-D copy per operand: the default for
+    single-CTA tiles of up to 128 columns where K is a multiple of 128) and of one chunk (2-D
+    copies, mode bit 4) issue the same MMAs in the same K order, so without split-K (K <= 2048
+    here) the outputs are equal; every tile-kind mode (cost model, single-CTA, 2-SM pairs, which
+    keep one-chunk stages)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
 
     g = torch.Generator(device=DEV).manual_seed(M + N + K)
