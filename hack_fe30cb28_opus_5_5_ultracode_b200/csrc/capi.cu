@@ -445,13 +445,9 @@ int ql_layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, i
                       cudaStream_t stream) {
   if (descs == nullptr || saved == nullptr || h_out == nullptr || count < 0)
     return fail(QL_STATUS_BAD_ARG, "ql_layers_forward");
-  int* err = ql::status_word();
-  for (int i = 0; i < count; ++i) {
-    const int rc = ql::layer_forward(descs[i], saved[i], h_out[i], workspace, workspace_bytes, err,
-                                     stream);
-    if (rc != QL_STATUS_OK) return done(rc, "ql_layers_forward");
-  }
-  return QL_STATUS_OK;
+  return done(ql::layers_forward(descs, saved, count, h_out, workspace, workspace_bytes,
+                                 ql::status_word(), stream),
+              "ql_layers_forward");
 }
 
 int ql_layers_backward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,

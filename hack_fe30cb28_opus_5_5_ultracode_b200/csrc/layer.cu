@@ -90,6 +90,8 @@ struct FwdWs {
   void* a;    // [n, H] norm output (a, then b)
   void* qkv;  // [n, C]
   void* m;    // [n, I]
+  void* o16;  // [n, H] the o projection, 16-bit (added to the residual by the second norm)
+  void* d16[2];  // [n, H] down projections handed from layer to layer (layers_forward)
 };
 
 FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
@@ -103,6 +105,9 @@ FwdWs carve_fwd(const ql_layer_desc& L, Bump& b) {
   w.a = b.take(n * L.H * e);
   w.qkv = b.take(n * C * e);
   w.m = b.take(n * L.I * e);
+  w.o16 = b.take(n * L.H * e);
+  w.d16[0] = b.take(n * L.H * e);
+  w.d16[1] = b.take(n * L.H * e);
   return w;
 }
 
@@ -217,8 +222,17 @@ int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward) {
   return b.off + 256;
 }
 
+// The residual stream goes through the norms: the o and down projections are written in the
+// 16-bit type, and the RMSNorm that follows each adds it to the fp32 residual (h2 = h + o in the
+// post-attention norm, the next layer's h = h2 + d in its input norm), writing the sum as its
+// xsum - the same fp32 additions of the rounded projections as an add in the GEMM epilogue,
+// done by a streaming kernel instead of a per-row epilogue behind the GEMM's last tile.
+// x_base / d_in: this layer's input is x_base + d_in (the previous layer's h2 and down output),
+// written to S.h by the input norm; both null: S.h is the input as it stands. d_out: the down
+// projection goes there (16-bit) for the next layer; null: h_out = h2 + d (fp32) here.
 int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,
-                  int64_t ws_bytes, int* err, cudaStream_t s) {
+                  int64_t ws_bytes, int* err, cudaStream_t s, const float* x_base,
+                  const void* d_in, void* d_out) {
   QL_TRY(check(L));
   if (L.n == 0) return QL_STATUS_OK;
   Bump bump{(uint8_t*)ws, ws_bytes, 0};
@@ -238,8 +252,14 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   void* const wdown = wbuf(slots.down);
 
   // input RMSNorm + the dropped LoRA inputs + LoRA-A products
+  if ((d_in != nullptr) != (x_base != nullptr)) return QL_STATUS_BAD_ARG;
   RmsFwdC r1{};
-  r1.x = S.h; r1.w = L.ln1; r1.y = w.a; r1.yq = S.yq; r1.yv = S.yv; r1.rstd = S.rstd1;
+  r1.x = d_in != nullptr ? x_base : S.h; r1.w = L.ln1; r1.y = w.a; r1.yq = S.yq; r1.yv = S.yv;
+  r1.rstd = S.rstd1;
+  if (d_in != nullptr) {  // the layer input h = h2 + d of the previous layer, kept as S.h
+    r1.delta = d_in;
+    r1.xsum = const_cast<float*>(S.h);
+  }
   r1.Aq = L.Aq; r1.Av = L.Av; r1.xq = S.xq; r1.xv = S.xv; r1.keep_q = S.keep_q;
   r1.keep_v = S.keep_v;
   r1.n = L.n; r1.H = L.H; r1.rank = L.rank; r1.dtype = dt; r1.eps = L.eps; r1.tok = L.tok;
@@ -262,13 +282,13 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
   af.scale = L.scale; af.n = L.n; af.B = L.B; af.max_len = L.max_len; af.HQ = L.HQ;
   af.HKV = L.HKV; af.D = L.D; af.dtype = dt;
   QL_TRY(attn_fwd(af, s));
-  // o projection, residual add in the epilogue: h2 = h + o
+  // o projection (16-bit), then the post-attention RMSNorm of h2 = h + o (kept as S.h2)
   if (!ready) QL_TRY(dequant(L.o, wo, dt, 0, s));
-  QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, wo, (int64_t)L.HQ * L.D, S.h2, L.H, nullptr, L.n,
-                 L.H, L.HQ * L.D, dt, QL_F32, 0, S.h, err, s, w.gws, w.gws_bytes));
-  // post-attention RMSNorm
+  QL_TRY(gemm_tn(S.out, (int64_t)L.HQ * L.D, wo, (int64_t)L.HQ * L.D, w.o16, L.H, nullptr, L.n,
+                 L.H, L.HQ * L.D, dt, dt, 0, nullptr, err, s, w.gws, w.gws_bytes));
   RmsFwdC r2{};
-  r2.x = S.h2; r2.w = L.ln2; r2.y = w.a; r2.rstd = S.rstd2; r2.n = L.n; r2.H = L.H;
+  r2.x = S.h; r2.delta = w.o16; r2.xsum = S.h2;
+  r2.w = L.ln2; r2.y = w.a; r2.rstd = S.rstd2; r2.n = L.n; r2.H = L.H;
   r2.rank = L.rank; r2.dtype = dt; r2.eps = L.eps; r2.vec = 4; r2.threads = 1; r2.p_keep = 1.f;
   r2.keep_scale = 1.f;
   QL_TRY(rms_fwd(r2, s));
@@ -278,8 +298,35 @@ int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out,
                  nullptr, err, s, w.gws, w.gws_bytes));
   QL_TRY(glu_fwd(S.gu, w.m, n, L.I, dt, s));
   if (!ready) QL_TRY(dequant(L.down, wdown, dt, 0, s));
-  QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0, S.h2,
-                 err, s, w.gws, w.gws_bytes));
+  if (d_out != nullptr)  // the next layer's input norm adds it to h2
+    QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, d_out, L.H, nullptr, L.n, L.H, L.I, dt, dt, 0, nullptr,
+                   err, s, w.gws, w.gws_bytes));
+  else
+    QL_TRY(gemm_tn(w.m, L.I, wdown, L.I, h_out, L.H, nullptr, L.n, L.H, L.I, dt, QL_F32, 0,
+                   S.h2, err, s, w.gws, w.gws_bytes));
+  return QL_STATUS_OK;
+}
+
+// Every layer's forward in order (the keep-everything plan): layer i's down projection reaches
+// layer i + 1 as a 16-bit delta through two alternating workspace buffers, and only the last
+// layer writes its output h_out[count - 1] = h2 + d in fp32 (h_out[i] of the others is where the
+// next layer's input norm writes that sum: saved[i + 1].h).
+int layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                   float* const* h_out, void* ws, int64_t ws_bytes, int* err, cudaStream_t s) {
+  for (int i = 0; i < count; ++i) {
+    QL_TRY(check(descs[i]));
+    if (i + 1 < count && h_out[i] != saved[i + 1].h) return QL_STATUS_BAD_ARG;
+  }
+  if (count == 0 || descs[0].n == 0) return QL_STATUS_OK;
+  Bump bump{(uint8_t*)ws, ws_bytes, 0};
+  const FwdWs w = carve_fwd(descs[0], bump);
+  if (!bump.ok()) return QL_STATUS_BAD_ARG;
+  for (int i = 0; i < count; ++i) {
+    const bool last = i + 1 == count;
+    QL_TRY(layer_forward(descs[i], saved[i], h_out[i], ws, ws_bytes, err, s,
+                         i > 0 ? saved[i - 1].h2 : nullptr, i > 0 ? w.d16[(i - 1) & 1] : nullptr,
+                         last ? nullptr : w.d16[i & 1]));
+  }
   return QL_STATUS_OK;
 }
 

@@ -96,7 +96,10 @@ int gemm_nf4(const void* A, int64_t lda, const ql_nf4_weight& W, int layout, voi
 int64_t layer_workspace_bytes(const ql_layer_desc& L, int backward);
 int64_t layer_weight_elems(const ql_layer_desc& L);
 int layer_forward(const ql_layer_desc& L, const ql_layer_saved& S, float* h_out, void* ws,
-                  int64_t ws_bytes, int* err, cudaStream_t s);
+                  int64_t ws_bytes, int* err, cudaStream_t s, const float* x_base = nullptr,
+                  const void* d_in = nullptr, void* d_out = nullptr);
+int layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
+                   float* const* h_out, void* ws, int64_t ws_bytes, int* err, cudaStream_t s);
 int layer_backward(const ql_layer_desc& L, const ql_layer_saved& S, const float* dh3,
                    const void* dh3_16, float* grads, float* dh_out, void* dh16_out, void* ws,
                    int64_t ws_bytes, int* err, cudaStream_t s);

@@ -517,8 +517,11 @@ int ql_layer_backward(const ql_layer_desc* layer, const ql_layer_saved* saved, c
  * Host only, no launch. */
 int ql_layers_set_step(ql_layer_desc* descs, int count, const ql_layer_desc* step,
                        const int64_t* ctr_q, const int64_t* ctr_v);
-/* ql_layer_forward for layers 0 .. count-1 in order: layer i reads saved[i].h and writes h_out[i]
- * (normally saved[i + 1].h). */
+/* ql_layer_forward for layers 0 .. count-1 in order, h_out[i] = saved[i + 1].h for i < count - 1
+ * (QL_STATUS_BAD_ARG otherwise). Between layers the residual stream goes through the norms: layer
+ * i's down projection is handed on in the 16-bit type and layer i + 1's input RMSNorm writes
+ * saved[i + 1].h = saved[i].h2 + d (the same fp32 addition of the rounded projection the
+ * per-layer call does in its down GEMM); the last layer writes h_out[count - 1] itself. */
 int ql_layers_forward(const ql_layer_desc* descs, const ql_layer_saved* saved, int count,
                       float* const* h_out, void* workspace, int64_t workspace_bytes,
                       cudaStream_t stream);
