@@ -610,7 +610,7 @@ class FusedQwen2:
         h = arena.h(0)
         if n:
             ops.embed(packed.ids, self.embed, out=h)
-            if self.w16 is not None:  # this step's 16-bit weights, every layer, few launches
+            if self.w16 is not None:  # the 16-bit weights of every layer, few launches
                 self._dequant_all()
         L = len(self.layers)
         drops = self._drops(packed)
@@ -659,9 +659,26 @@ class FusedQwen2:
             self._saved_cache = (key, saved_arr, h_out)
         return self._saved_cache[1], self._saved_cache[2]
 
+    def _nf4_version(self):
+        """Sum of the version counters of every NF4 tensor the kept weights come from (packed
+        bytes, scales): it grows whenever one of them is written in place."""
+        if getattr(self, "_nf4_tensors", None) is None:
+            ts = []
+            for spec in self.layers:
+                for g in (spec.qkv, spec.o, spec.gu, spec.down):
+                    ts += [g.packed, g.absmax] + ([g.absmax2, g.offsets] if g.nested else [])
+            self._nf4_tensors = ts
+        return sum(t._version for t in self._nf4_tensors)
+
     def _dequant_all(self):
         """Every layer's four NF4 groups into the kept 16-bit weights ([qkv | o | gate_up |
-        down] per layer, as the layer kernels lay them out) with ql_nf4_dequant_batch."""
+        down] per layer, as the layer kernels lay them out) with ql_nf4_dequant_batch. The base
+        weights are frozen, so the kept copy is refreshed only when the NF4 storage has changed
+        since the last dequantisation (its version counters) - once, for training as usual:
+        every later step reads the same 16-bit weights a fresh dequantisation would write."""
+        version = self._nf4_version()
+        if getattr(self, "_w16_version", None) == version:
+            return
         if getattr(self, "_dq_args", None) is None:
             spec = self.layers[0]
             C = (spec.HQ + 2 * spec.HKV) * spec.D
@@ -680,6 +697,7 @@ class FusedQwen2:
         arr, ptrs, count = self._dq_args
         _lib.call("ql_nf4_dequant_batch", ctypes.addressof(arr), ctypes.addressof(ptrs), count,
                   ops.dtype_code(self.dtype), ops.stream_ptr())
+        self._w16_version = version
 
     def _esize(self):
         return torch.empty((), dtype=self.dtype).element_size()

@@ -259,3 +259,34 @@ def test_spilled_layers_match_oracle(spill):
     assert engine.last_plan.modes == [spill, spill, "keep"]
     _check_step(f"3 layers, 2 by {spill}", loss, grads, ref, torch.float16)
     assert gen.get_offset() == ref["offset"]
+
+
+def test_kept_weights_follow_the_nf4_storage():
+    """The 16-bit weights are dequantised once and reused while the frozen NF4 storage is
+    unchanged; an in-place change to a layer's packed bytes (the storage the model's bitsandbytes
+    parameters view) refreshes them at the next step."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import ops
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import TINY
+
+    engine = _run(TINY, [23, 9], 0.0, False)[0]
+    spec = engine.layers[0]
+    first = engine.w16.clone()
+    # a second step with the same weights: nothing is dequantised again, the copy is unchanged
+    ids, mask, labels = _batch([23, 9], TINY.vocab_size)
+    n_items = float((labels[:, 1:] != -100).sum())
+    launches = ops.launch_count()
+    engine.step(ids.to(DEV), mask.to(DEV), labels.to(DEV), n_items)[0].backward()
+    torch.cuda.synchronize()
+    assert torch.equal(engine.w16, first)
+    version = engine._w16_version
+    # flip bits of layer 0's q projection in place
+    storage = spec.qkv.packed
+    storage[:64].bitwise_xor_(0x11)
+    engine.step(ids.to(DEV), mask.to(DEV), labels.to(DEV), n_items)[0].backward()
+    torch.cuda.synchronize()
+    assert engine._w16_version != version
+    fresh = torch.empty(spec.qkv.shape, device=DEV, dtype=torch.float16)
+    spec.qkv.dequant(fresh)
+    assert torch.equal(engine.w16[:fresh.numel()].view_as(fresh), fresh)
+    assert not torch.equal(engine.w16, first)
+    assert ops.launch_count() > launches
