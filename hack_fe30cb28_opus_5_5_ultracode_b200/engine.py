@@ -899,6 +899,9 @@ class VocabHead:
         self.V, self.H = lm_w.shape
         self.device = lm_w.device
         self._buf = None
+        # the per-row state's starting value (max, sum, sum x e^x, best): made once here, since
+        # a device tensor built from host values waits for the device
+        self._init = torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")]).to(self.device)
 
     def chunk_width(self, rows):
         """Vocabulary entries per chunk: as many as keep the chunk's 16-bit logits within
@@ -911,13 +914,17 @@ class VocabHead:
         return cdiv(cdiv(self.V, cdiv(self.V, width)), 64) * 64
 
     def _buffers(self, rows, width, sup):
+        """The block's buffers, grown (by a quarter more than asked, so that slightly larger
+        blocks later reuse them) only when a block needs more rows, logits or supervised rows
+        than any before."""
         H, dt, dev = self.H, self.dtype, self.device
         b = self._buf
-        need = (rows, width, sup)
+        need = (rows, rows * width, sup)
         if b is None or any(x < y for x, y in zip(b["shape"], need)):
-            rows_, width_, sup_ = (max(x, y) for x, y in zip(b["shape"] if b else (0, 0, 0), need))
-            b = {"shape": (rows_, width_, sup_),
-                 "logits": torch.empty(rows_ * width_, device=dev, dtype=dt),
+            rows_, logits_, sup_ = (max(x, y + y // 4) if x < y else x
+                                    for x, y in zip(b["shape"] if b else (0, 0, 0), need))
+            b = {"shape": (rows_, logits_, sup_),
+                 "logits": torch.empty(logits_, device=dev, dtype=dt),
                  "state": torch.empty((rows_, 4), device=dev, dtype=torch.float32),
                  "best": torch.empty(rows_, device=dev, dtype=torch.int64),
                  "xt": torch.empty(rows_, device=dev, dtype=torch.float32),
@@ -925,8 +932,7 @@ class VocabHead:
                  "acc": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
                  "part": torch.empty((max(sup_, 1), H), device=dev, dtype=torch.float32),
                  "wt": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
-                 "dhn": torch.empty((max(sup_, 1), H), device=dev, dtype=dt),
-                 "init": torch.tensor([float("-inf"), 0.0, 0.0, float("-inf")], device=dev)}
+                 "dhn": torch.empty((max(sup_, 1), H), device=dev, dtype=dt)}
             self._buf = b
         return b
 
@@ -938,7 +944,7 @@ class VocabHead:
         width = self.chunk_width(rows)
         b = self._buffers(rows, width, sup)
         state, best, xt = b["state"][:rows], b["best"][:rows], b["xt"][:rows]
-        state.copy_(b["init"].expand(rows, 4))
+        state.copy_(self._init.expand(rows, 4))
         logits = b["logits"][:rows * width].view(rows, width)
         acc = b["acc"][:sup] if sup else None
         part = b["part"][:sup] if sup else None
