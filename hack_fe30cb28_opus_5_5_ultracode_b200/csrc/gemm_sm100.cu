@@ -18,6 +18,7 @@
 // The accumulator of tile t+1 is written while the epilogue drains tile t.
 #include <atomic>
 #include <cstring>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "gemm_common.cuh"
@@ -628,7 +629,36 @@ static double kstep_clocks(int a_rows, int b_rows, int w) {
 // the fewer splits). Long-K products with few output tiles (the down projection, the data
 // gradients of gate/up and of the LM head at ~1 k tokens) thereby take wider tiles, split in two,
 // instead of narrow unsplit ones: less operand traffic per FLOP.
+static GemmPlan plan_gemm_uncached(int M, int N, int K, int sms, bool b_mn, int mode);
+
+// plan_gemm memoised per host thread: the same few shapes come back every layer of every step.
 static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
+  struct Key {
+    int M, N, K, sms, b_mn, mode;
+    bool operator==(const Key& o) const {
+      return M == o.M && N == o.N && K == o.K && sms == o.sms && b_mn == o.b_mn && mode == o.mode;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      uint64_t h = 0x9E3779B97F4A7C15ull;
+      for (uint64_t x : {(uint64_t)k.M, (uint64_t)k.N, (uint64_t)k.K,
+                         (uint64_t)(k.sms * 64 + k.b_mn * 8 + k.mode)})
+        h = (h ^ x) * 0x100000001B3ull;
+      return (size_t)h;
+    }
+  };
+  thread_local std::unordered_map<Key, GemmPlan, Hash> cache;
+  const Key key{M, N, K, sms, (int)b_mn, g_gemm_mode.load() & 3};
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 1024) cache.clear();
+  const GemmPlan g = plan_gemm_uncached(M, N, K, sms, b_mn, key.mode);
+  cache.emplace(key, g);
+  return g;
+}
+
+static GemmPlan plan_gemm_uncached(int M, int N, int K, int sms, bool b_mn, int mode) {
   static const int widths[] = {256, 224, 192, 128, 96};
   GemmPlan g{256, 0, 1, 0, false};
   const int k_blocks = (int)cdiv(K, 64);
@@ -636,7 +666,6 @@ static GemmPlan plan_gemm(int M, int N, int K, int sms, bool b_mn = false) {
   // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
   // K <= 4096: the gate/up and lm_head forwards), the shapes where they measured faster than the
   // single-CTA tiles at 1-4K rows. Elsewhere the 256-row pairs waste rows of M and were slower.
-  const int mode = g_gemm_mode.load() & 3;
   if (mode == 2 || (mode == 0 && !b_mn && N >= 16384 && K <= 4096 && M >= 512)) {
     int pbn = 0;
     int64_t punits = 0;

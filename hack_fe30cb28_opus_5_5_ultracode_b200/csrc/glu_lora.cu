@@ -354,8 +354,7 @@ __global__ void __launch_bounds__(LG_THREADS) lora_grads_kernel(LgArgs a) {
 }
 
 static int lora_grads_splits(int64_t n, int64_t blocks) {
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sm_count();
   int64_t s = cdiv(4LL * sms, blocks > 0 ? blocks : 1);  // about 4 CTAs per SM
   const int64_t by_tokens = cdiv(n, 32);                  // at least 32 tokens per split
   if (s > by_tokens) s = by_tokens;

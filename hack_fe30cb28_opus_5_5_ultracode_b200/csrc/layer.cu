@@ -3,6 +3,7 @@
 // library's kernels, on one stream, temporaries carved out of a caller-owned workspace. One call
 // per layer pass replaces ~20 Python-level launches.
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "ops.h"
@@ -59,9 +60,43 @@ int dequant(const ql_nf4_weight& w, void* out, int dtype, int transpose, cudaStr
     if (_rc != QL_STATUS_OK) return _rc; \
   } while (0)
 
+// Per-shape memo of a pure function of a few ints (the host-side planning below runs for every
+// layer of every pass; its result depends on the shapes only).
+struct ShapeKey {
+  int64_t v[6];
+  bool operator==(const ShapeKey& o) const {
+    for (int i = 0; i < 6; ++i)
+      if (v[i] != o.v[i]) return false;
+    return true;
+  }
+};
+struct ShapeKeyHash {
+  size_t operator()(const ShapeKey& k) const {
+    uint64_t h = 0x9E3779B97F4A7C15ull;
+    for (int64_t x : k.v) h = (h ^ (uint64_t)x) * 0x100000001B3ull;
+    return (size_t)h;
+  }
+};
+template <typename F>
+int64_t memo(const ShapeKey& key, F compute) {
+  thread_local std::unordered_map<ShapeKey, int64_t, ShapeKeyHash> cache;
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 1024) cache.clear();
+  const int64_t v = compute();
+  cache.emplace(key, v);
+  return v;
+}
+
+int64_t layer_gemm_ws_uncached(const ql_layer_desc& L);
+
 // The split-K GEMM workspace sits at the start of the layer workspace (its first bytes are
 // tile counters, zero between launches): the largest any GEMM of the layer asks for.
 int64_t layer_gemm_ws(const ql_layer_desc& L) {
+  return memo(ShapeKey{{L.n, L.H, L.HQ, L.HKV, L.D, L.I}}, [&] { return layer_gemm_ws_uncached(L); });
+}
+
+int64_t layer_gemm_ws_uncached(const ql_layer_desc& L) {
   const int64_t C = (int64_t)(L.HQ + 2 * L.HKV) * L.D;
   const int n = L.n, H = L.H, I = L.I, QD = L.HQ * L.D;
   const int64_t shapes[8][3] = {{n, C, H}, {n, H, QD}, {n, 2 * I, H}, {n, H, I},
@@ -77,8 +112,10 @@ int64_t layer_gemm_ws(const ql_layer_desc& L) {
 // The LoRA-gradient kernel's workspace follows at the same offset in both carves (its counters,
 // zero between launches, must not be overwritten by the forward's temporaries).
 int64_t layer_lora_ws(const ql_layer_desc& L) {
-  const int32_t nc[4] = {L.HQ * L.D, L.HKV * L.D, L.H, L.H};
-  return lora_grads_workspace(L.n, nc, 4);
+  return memo(ShapeKey{{L.n, L.H, L.HQ, L.HKV, L.D, -1}}, [&] {
+    const int32_t nc[4] = {L.HQ * L.D, L.HKV * L.D, L.H, L.H};
+    return lora_grads_workspace(L.n, nc, 4);
+  });
 }
 
 struct FwdWs {

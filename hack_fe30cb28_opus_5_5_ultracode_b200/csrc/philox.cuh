@@ -69,7 +69,18 @@ inline uint32_t keep_threshold(float p_keep) {
 inline bool prepare_dropout(DropoutArgs& d) {
   if (d.threads <= 0 || d.threads > 0xFFFFFFFFll) return false;
   d.div_threads = make_fastdiv((uint32_t)d.threads);
-  d.keep_below = d.p_keep < 1.0f ? keep_threshold(d.p_keep) : 0xFFFFFFFFu;
+  // the threshold of the last probability asked for (one per training run, normally)
+  thread_local float last_p = -1.f;
+  thread_local uint32_t last_t = 0;
+  if (d.p_keep >= 1.0f) {
+    d.keep_below = 0xFFFFFFFFu;
+  } else {
+    if (d.p_keep != last_p) {
+      last_t = keep_threshold(d.p_keep);
+      last_p = d.p_keep;
+    }
+    d.keep_below = last_t;
+  }
   return true;
 }
 
