@@ -566,8 +566,8 @@ bool attn_deterministic() { return g_attn_det.load(); }
 
 // The deterministic backward's sums: thread = (row, head, 4 columns). dq of query row p (position
 // in its sequence) adds the contributions of key blocks 0 .. p / 128; dk / dv of key row j add,
-// over the GQA group's query heads g and the 1024-query chunks c that exist for j's key block,
-// slot (g, c), in that order.
+// over the GQA group's query heads g and the query chunks c (attn_bwd_qch queries each) that
+// exist for j's key block, slot (g, c), in that order.
 __global__ void attn_bwd_det_reduce_kernel(const float* __restrict__ parts, AttnBwdC a) {
   pdl_enter();  // the backward kernel's partials are complete and visible from here on
   const int hh_all = a.HQ + 2 * a.HKV;
@@ -593,8 +593,9 @@ __global__ void attn_bwd_det_reduce_kernel(const float* __restrict__ parts, Attn
     *reinterpret_cast<float4*>(a.dq + (row * a.HQ + hh) * 128 + 4 * c4) = acc;
   } else {
     const int which = (hh - a.HQ) / a.HKV, j = (hh - a.HQ) % a.HKV;
-    const int group = a.HQ / a.HKV, nch = (a.max_len + 1023) / 1024;
-    const int chunks = (len - kb * 128 + 1023) / 1024;
+    const int qch = attn_bwd_qch(a.max_len);
+    const int group = a.HQ / a.HKV, nch = (a.max_len + qch - 1) / qch;
+    const int chunks = (len - kb * 128 + qch - 1) / qch;
     const float* base = parts + attn_part_q_floats(a) + which * attn_part_kv_floats(a) +
                         (row * a.HKV + j) * 128;
     for (int g = 0; g < group; ++g)

@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(64 + TA_SOFTMAX, 1)
 // ---------------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------------
-// One CTA per (128-key block, query chunk of up to TB_QCH queries, query head, sequence). The
+// One CTA per (128-key block, query chunk of attn_bwd_qch queries, query head, sequence). The
 // key block's K and V stay in shared memory; the chunk's query blocks of 64 stream through a
 // two-stage ring (Q, dO, lse * log2(e), Dvec). Per query block j, all on tcgen05 with fp32
 // accumulators in TMEM (lane = the M row):
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(64 + TA_SOFTMAX, 1)
 // 6-9 dQ. TMEM: S^T [0, 64), dP^T [64, 128), dQ^T [128, 192), dV [192, 320), dK [320, 448).
 constexpr int TB_BK = 128;           // keys per CTA
 constexpr int TB_BQ = 64;            // queries per block
-constexpr int TB_QCH = 1024;         // queries per CTA (a chunk from the key block's diagonal)
+
 constexpr int TB_KT = TB_BK * 256;   // K or V tile: 128 rows x 128 d (two 64-column boxes)
 constexpr int TB_KBOX = TB_KT / 2;
 constexpr int TB_QT = TB_BQ * 256;   // Q or dO tile: 64 rows x 128 d
@@ -336,9 +336,10 @@ __global__ void __launch_bounds__(320, 1)
   const int nkb = (int)cdiv(a.max_len, TB_BK);
   const int kb = blockIdx.x % nkb, chunk = blockIdx.x / nkb, h = blockIdx.y, b = blockIdx.z;
   const int start = a.cu_seqlens[b], len = a.cu_seqlens[b + 1] - start;
-  const int key0 = kb * TB_BK, q_first = key0 + chunk * TB_QCH;
+  const int qch = attn_bwd_qch(a.max_len);
+  const int key0 = kb * TB_BK, q_first = key0 + chunk * qch;
   if (key0 >= len || q_first >= len) return;  // the whole CTA, before any setup
-  const int q_end = min(len, q_first + TB_QCH);
+  const int q_end = min(len, q_first + qch);
   const int nq = (int)cdiv(q_end - q_first, TB_BQ);
   const int kvh = h / (a.HQ / a.HKV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -525,7 +526,7 @@ __global__ void __launch_bounds__(320, 1)
           bulk_reduce_add_f32(a.dk + row, reinterpret_cast<const float*>(stk), 512);
           bulk_reduce_add_f32(a.dv + row, reinterpret_cast<const float*>(stv), 512);
         } else {  // this (query head of the group, chunk)'s own slot
-          const int group = a.HQ / a.HKV, nch = (int)cdiv(a.max_len, TB_QCH);
+          const int group = a.HQ / a.HKV, nch = (int)cdiv(a.max_len, qch);
           const int64_t slot = ((int64_t)(h - kvh * group) * nch + chunk) * a.n * a.HKV * 128;
           float* pk = a.partials + attn_part_q_floats(a) + slot;
           float* pv = pk + attn_part_kv_floats(a);
@@ -627,7 +628,8 @@ int attn_bwd_tc(const AttnBwdC& a, cudaStream_t s) {
       make_chunked_map(&mk, a.k, a.n, wk, wk, TB_BK, 2, bf) != QL_STATUS_OK ||
       make_chunked_map(&mv, a.v, a.n, wk, wk, TB_BK, 2, bf) != QL_STATUS_OK)
     return QL_STATUS_CUDA;
-  dim3 grid((unsigned)(cdiv(a.max_len, TB_BK) * cdiv(a.max_len, TB_QCH)), (unsigned)a.HQ, (unsigned)a.B);
+  dim3 grid((unsigned)(cdiv(a.max_len, TB_BK) * cdiv(a.max_len, attn_bwd_qch(a.max_len))),
+            (unsigned)a.HQ, (unsigned)a.B);
   int* err = status_word();
   if (bf) {
     smem_optin(reinterpret_cast<const void*>(attn_bwd_tc_kernel<true>), TB_SMEM);

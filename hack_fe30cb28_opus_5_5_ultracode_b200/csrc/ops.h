@@ -63,15 +63,21 @@ int ce_finish(const CeFinishC& a, cudaStream_t s);
 namespace ql {
 typedef ql_attn_fwd_args AttnFwdC;
 typedef ql_attn_bwd_args AttnBwdC;
+// Queries per CTA of the tcgen05 attention backward (a chunk of a key block's queries, from its
+// diagonal on): 256 for sequences of up to 2,048 tokens, so the longest key block's walk is four
+// 64-query blocks and the work spreads over the SMs instead of waiting on one long chain; 1,024
+// for longer ones, where every chain is long enough to keep the tensor cores busy.
+__host__ __device__ inline int attn_bwd_qch(int max_len) { return max_len <= 2048 ? 256 : 1024; }
 // The deterministic attention backward's partials (D = 128): the dq contributions of each
 // 128-key block, [ceil(max_len / 128)][n][HQ][128]; then the dk, and the dv, contributions of
-// each (query head of the GQA group, 1024-query chunk), [HQ / HKV][ceil(max_len / 1024)][n][HKV]
-// [128] each.
+// each (query head of the GQA group, query chunk), [HQ / HKV][ceil(max_len / qch)][n][HKV][128]
+// each.
 __host__ __device__ inline int64_t attn_part_q_floats(const AttnBwdC& a) {
   return (int64_t)((a.max_len + 127) / 128) * a.n * a.HQ * 128;
 }
 __host__ __device__ inline int64_t attn_part_kv_floats(const AttnBwdC& a) {
-  return (int64_t)(a.HQ / a.HKV) * ((a.max_len + 1023) / 1024) * a.n * a.HKV * 128;
+  const int qch = attn_bwd_qch(a.max_len);
+  return (int64_t)(a.HQ / a.HKV) * ((a.max_len + qch - 1) / qch) * a.n * a.HKV * 128;
 }
 void attn_set_deterministic(bool on);
 bool attn_deterministic();
