@@ -25,6 +25,7 @@ struct GemmArgs {
   float* ws;
   int* counters;
   int tma_c;  // 16-bit C written by TMA tensor stores from per-warp shared-memory staging
+  int b3d;    // MN-major B with one-chunk stages: the stage's 64-column boxes in one 3-D copy
 };
 
 // Epilogue staging for TMA stores of a 16-bit C: per epilogue warp two 32 x 32 buffers of 2 KB.

@@ -93,9 +93,13 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             tma_load_2d(sa, &tma_a, &full[stage], kb * Cfg::BK, mb * Cfg::BM);
             if constexpr (B_MN) {  // B stored [K, N]: boxes of 64 N-columns x 64 K-rows, 8 KB each
+              if (p.b3d) {  // all of them in one 3-D copy ([BN / 64 chunks][64 K rows][64])
+                tma_load_3d(sb, &tma_b, &full[stage], 0, kb * Cfg::BK, nb * (BN / 64));
+              } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                tma_load_2d(sb + j * 8192, &tma_b, &full[stage], nb * BN + j * 64, kb * Cfg::BK);
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_2d(sb + j * 8192, &tma_b, &full[stage], nb * BN + j * 64, kb * Cfg::BK);
+              }
             } else {
               tma_load_2d(sb, &tma_b, &full[stage], kb * Cfg::BK, nb * BN);
             }
@@ -355,9 +359,13 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             tma_load_2d_pair(sa, &tma_a, &full[stage], kb * Cfg::BK, arow);
             if constexpr (B_MN) {
+              if (p.b3d) {
+                tma_load_3d_pair(sb, &tma_b, &full[stage], 0, kb * Cfg::BK, brow / 64);
+              } else {
 #pragma unroll
-              for (int j = 0; j < Cfg::HB / 64; ++j)
-                tma_load_2d_pair(sb + j * 8192, &tma_b, &full[stage], brow + j * 64, kb * Cfg::BK);
+                for (int j = 0; j < Cfg::HB / 64; ++j)
+                  tma_load_2d_pair(sb + j * 8192, &tma_b, &full[stage], brow + j * 64, kb * Cfg::BK);
+              }
             } else {
               tma_load_2d_pair(sb, &tma_b, &full[stage], kb * Cfg::BK, brow);
             }
@@ -756,6 +764,7 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
                   !(g_gemm_mode.load() & 4)) ? 2 : 1;
   const int brows = g.pair ? g.bn / 2 : g.bn;  // B rows (or MN-major columns) per CTA
   CUtensorMap ma, mb;
+  int b3d = 0;
   if (kc == 2) {
     if (make_chunked_map(&ma, A, M, K, lda, 128, 2, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
     if (b_mn ? make_chunked_map(&mb, B, K, N, ldb, 128, brows / 64, bf16) != QL_STATUS_OK
@@ -767,14 +776,19 @@ static int gemm_core(const void* A, int64_t lda, const void* B, int64_t ldb, voi
     g.splits = (int)cdiv(cdiv(K, 128), kper);
   } else {
     if (make_kmajor_map(&ma, A, M, K, lda, 128, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
-    if (b_mn) {
+    if (b_mn && N % 64 == 0 && !(g_gemm_mode.load() & 4)) {
+      // the stage's 64-column boxes of an MN-major B in one 3-D copy (8 KB boxes are the
+      // slowest to stream)
+      if (make_chunked_map(&mb, B, K, N, ldb, 64, brows / 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
+      b3d = 1;
+    } else if (b_mn) {
       if (make_kmajor_map(&mb, B, K, N, ldb, 64, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
     } else {
       if (make_kmajor_map(&mb, B, N, K, ldb, brows, bf16) != QL_STATUS_OK) return QL_STATUS_CUDA;
     }
   }
   GemmArgs a{M, N, K, C, ldc, bias, out_dtype, accumulate, residual, err, g.splits,
-             g.kb_per_split, nullptr, nullptr, 0};
+             g.kb_per_split, nullptr, nullptr, 0, b3d};
   // 16-bit C with no read-modify epilogue: TMA tensor stores (needs a 16-byte aligned C and row
   // stride); otherwise per-thread row stores and an unused map
   CUtensorMap mc;

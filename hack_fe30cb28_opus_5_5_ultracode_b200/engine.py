@@ -616,7 +616,6 @@ class FusedQwen2:
         drops = self._drops(packed)
         self._set_all_steps(packed, drops, cos, sin)
         saved_arr, h_out = self._saved_structs(arena, plan)
-        saved = [(saved_arr[i], drops[i]) for i in range(L)]
         if n and all(m == memory.KEEP for m in plan.modes):
             # every layer keeps its saved set: the whole forward in one call
             ws = self._workspace_for(self.descs[0])
@@ -633,7 +632,7 @@ class FusedQwen2:
                           ws.data_ptr(), ws.numel(), ops.stream_ptr())
                 if offload is not None:
                     offload.after_forward(i)
-        saved = (saved_arr, saved)
+        saved = (saved_arr, drops)
         h = arena.h(len(self.layers))
         dhp, loss = self._head(h, packed, denom, stats) if n else (None, None)
         if loss is None:
@@ -649,13 +648,27 @@ class FusedQwen2:
         w16 = self.w16.data_ptr() if self.w16 is not None else 0
         key = (arena.base, arena.n, tuple(plan.modes), w16)
         if self._saved_cache is None or self._saved_cache[0] != key:
-            saved_arr = (_lib.STRUCTS["ql_layer_saved"] * L)()
-            for i in range(L):
-                saved_arr[i] = arena.saved(i)
-                if self.w16 is not None:
-                    saved_arr[i].w16 = w16 + i * self.weight_elems * self._esize()
-                    saved_arr[i].w16_ready = 1
-            h_out = (ctypes.c_void_p * L)(*[arena.h(i + 1).data_ptr() for i in range(L)])
+            # every address is base + offsets: filled as one [L, 18] array of 8-byte words (the
+            # struct's 17 pointers, then w16_ready and its padding) and copied in at once, since
+            # the token count - and with it the layout - changes from step to step
+            st = _lib.STRUCTS["ql_layer_saved"]
+            names = [f for f, _ in st._fields_]
+            if ctypes.sizeof(st) != 18 * 8 or names[-1] != "w16_ready" or names[0] != "h":
+                raise RuntimeError("ql_layer_saved layout changed")
+            slots = np.array([plan.slot(i) for i in range(L)], dtype=np.uint64)
+            base = np.uint64(arena.base) + slots * np.uint64(arena.layer_bytes)
+            words = np.zeros((L, 18), dtype=np.uint64)
+            h0 = arena.base + arena.slots * arena.layer_bytes
+            words[:, 0] = h0 + np.arange(L, dtype=np.uint64) * np.uint64(arena.h_bytes)
+            for j, name in enumerate(names[1:16], start=1):
+                words[:, j] = base + np.uint64(arena.fields[name])
+            if w16:
+                words[:, 16] = np.uint64(w16) + np.arange(L, dtype=np.uint64) * np.uint64(
+                    self.weight_elems * self._esize())
+                words[:, 17] = 1  # w16_ready (little-endian int32 in the low half)
+            saved_arr = (st * L)()
+            ctypes.memmove(saved_arr, words.ctypes.data, words.nbytes)
+            h_out = (ctypes.c_void_p * L)(*(words[:, 0] + np.uint64(arena.h_bytes)).tolist())
             self._saved_cache = (key, saved_arr, h_out)
         return self._saved_cache[1], self._saved_cache[2]
 
@@ -810,7 +823,7 @@ class FusedQwen2:
     def _backward(self, packed, saved, dhp, grad):
         n = packed.n
         H = self.layers[0].H
-        arena, (saved_arr, per_layer), offload = saved
+        arena, (saved_arr, drops), offload = saved
         plan = arena.plan
         if arena.owned:  # the next forward may reuse the arena (queued after this backward)
             self._arena_busy = False
@@ -832,7 +845,7 @@ class FusedQwen2:
             if offload is not None:
                 offload.start_backward()
             L = len(self.layers)
-            self._set_all_steps(packed, [d for _, d in per_layer], cos, sin)
+            self._set_all_steps(packed, drops, cos, sin)
             if all(m == memory.KEEP for m in plan.modes):
                 # every saved set is in HBM: the whole backward in one call
                 ws = self._workspace_for(self.descs[0])
@@ -845,7 +858,7 @@ class FusedQwen2:
                                  else []):
                 i = spec.index
                 desc = self.descs[i]
-                sv, drop = per_layer[i]
+                sv, drop = saved_arr[i], drops[i]
                 if plan.modes[i] == memory.RECOMPUTE:
                     self._recompute(i, desc, sv, arena)
                 elif plan.modes[i] == memory.OFFLOAD:
