@@ -369,7 +369,8 @@ def run_ours(args, rank, world, local):
     host = batches(args, rank, cfg.vocab_size, world)
     dev_batches = [tuple(torch.from_numpy(a).to(dev) for a in b[:3]) + (b[3],) for b in host]
     denoms = [float((b[2][:, 1:] != -100).sum()) for b in host]
-    hosts = [HostBatch.of(torch.from_numpy(b[1]), torch.from_numpy(b[2])) for b in host]
+    hosts = [HostBatch.of(torch.from_numpy(b[1]), torch.from_numpy(b[2]), torch.from_numpy(b[0]))
+             for b in host]
     timed = range(args.warmup, args.warmup + args.steps)
 
     def train_step(i):

@@ -224,15 +224,18 @@ class HostBatch:
     host until the previous step's GPU work is done (the reference reads both back,
     solution/engine.py:714, 732)."""
 
-    def __init__(self, lengths, n_supervised):
+    def __init__(self, lengths, n_supervised, plan=None):
         self.lengths = [int(x) for x in lengths]
         self.n_supervised = int(n_supervised)
+        self.plan = plan  # the packed batch's index tensors in one pinned buffer (_host_plan)
 
     @classmethod
-    def of(cls, attention_mask, labels):
+    def of(cls, attention_mask, labels, input_ids=None):
         """From host (CPU) tensors of a right-padded batch; None if it is not right-padded.
-        (numpy on the host arrays: this runs on the step's critical path, before its first
-        launch.)"""
+        With the token ids as well, the whole packed batch (Packed's index tensors, packed ids,
+        targets, head order) is formed here too, so the step moves it to the device in one copy
+        instead of a dozen small device operations. (numpy on the host arrays: this runs on the
+        step's critical path, before its first launch.)"""
         m = attention_mask.to("cpu").numpy()
         if m.ndim != 2 or not (((m == 0) | (m == 1)).all() and (m[:, 1:] <= m[:, :-1]).all()):
             return None
@@ -241,7 +244,10 @@ class HostBatch:
         T = lab.shape[1]
         # a token at column t < length - 1 has target labels[row, t + 1]
         has_next = np.arange(T - 1)[None, :] < (lengths[:, None] - 1)
-        return cls(lengths.tolist(), int(((lab[:, 1:] != -100) & has_next).sum()))
+        plan = None
+        if input_ids is not None and input_ids.shape == attention_mask.shape:
+            plan = _host_plan(lengths, input_ids.to("cpu").numpy(), lab)
+        return cls(lengths.tolist(), int(((lab[:, 1:] != -100) & has_next).sum()), plan)
 
 
 def _index_plan(lengths, T):
@@ -254,6 +260,26 @@ def _index_plan(lengths, T):
     row = np.repeat(np.arange(len(lens), dtype=np.int64), lens)
     pos = np.arange(n, dtype=np.int64) - cu[:-1][row]
     return np.concatenate([row * T + pos, pos, row, cu]), n
+
+
+def _host_plan(lengths, ids, lab):
+    """Packed's device inputs computed on the host, in one pinned byte buffer: int64 [tok | row |
+    ids | targets | head_order] (n each), then int32 [pos (n) | cu_seqlens (B + 1)] - the values
+    the device path of Packed forms (the same next-label rule and stable supervised-first order)."""
+    B, T = lab.shape
+    idx, n = _index_plan(lengths, T)
+    tok, pos, row, cu = idx[:n], idx[n:2 * n], idx[2 * n:3 * n], idx[3 * n:]
+    nxt = lab.reshape(-1)[np.minimum(tok + 1, max(B * T - 1, 0))] if n else tok
+    targets = np.where(pos < T - 1, nxt, -100).astype(np.int64)
+    order = np.argsort(targets < 0, kind="stable").astype(np.int64)
+    i64 = np.concatenate([tok, row, ids.reshape(-1)[tok].astype(np.int64), targets, order])
+    i32 = np.concatenate([pos, cu]).astype(np.int32)
+    buf = torch.empty(i64.nbytes + i32.nbytes, dtype=torch.uint8,
+                      pin_memory=torch.cuda.is_available())
+    view = buf.numpy()
+    view[:i64.nbytes] = i64.view(np.uint8)
+    view[i64.nbytes:] = i32.view(np.uint8)
+    return buf
 
 
 def _supervised_first(targets):
@@ -295,6 +321,9 @@ class Packed:
         self.rows, self.T = B, T
         self.lengths = [int(x) for x in lengths]
         self.max_len = max(self.lengths, default=0)
+        if host is not None and host.plan is not None:
+            self._from_host_plan(host, input_ids.device)
+            return
         plan, self.n = _index_plan(self.lengths, T)
         staged = torch.from_numpy(plan)
         dev = input_ids.device
@@ -313,6 +342,17 @@ class Packed:
         self.head_order, seen = _supervised_first(self.targets)
         self.n_supervised = host.n_supervised if host is not None \
             else (int(seen[-1]) if n else 0)
+
+    def _from_host_plan(self, host, dev):
+        """The packed batch from the host's buffer (HostBatch.plan) in one copy."""
+        n = self.n = sum(self.lengths)
+        staged = host.plan.to(dev, non_blocking=True)
+        i64 = staged[:5 * n * 8].view(torch.int64)
+        i32 = staged[5 * n * 8:].view(torch.int32)
+        self.tok, self.row_of_token = i64[:n], i64[n:2 * n]
+        self.ids, self.targets, self.head_order = i64[2 * n:3 * n], i64[3 * n:4 * n], i64[4 * n:]
+        self.pos, self.cu_seqlens = i32[:n], i32[n:]
+        self.n_supervised = host.n_supervised
 
 
 class RopeTable:

@@ -252,10 +252,10 @@ def _host_facts(inputs):
 
     if not isinstance(inputs, dict):
         return None
-    mask, labels = inputs.get("attention_mask"), inputs.get("labels")
+    mask, labels, ids = inputs.get("attention_mask"), inputs.get("labels"), inputs.get("input_ids")
     if not (torch.is_tensor(mask) and torch.is_tensor(labels)) or mask.is_cuda or labels.is_cuda:
         return None
-    return HostBatch.of(mask, labels)
+    return HostBatch.of(mask, labels, ids if torch.is_tensor(ids) and not ids.is_cuda else None)
 
 
 def prepare_inputs(trainer, inputs, device):

@@ -225,6 +225,15 @@ def test_host_batch_matches_the_device_reads():
     for name in ("tok", "pos", "cu_seqlens", "ids", "targets", "head_order", "row_of_token"):
         assert torch.equal(getattr(a, name), getattr(p, name)), name
     assert HostBatch.of(_batch([5, 3], left=True)["attention_mask"], b["labels"][:2, :5]) is None
+    # with the ids too, the packed batch comes from the host in one buffer: the same tensors
+    for lengths in ([5, 3, 7], [1, 9], [4], [6, 6, 2, 1]):
+        b = _batch(lengths)
+        host = HostBatch.of(b["attention_mask"], b["labels"], b["input_ids"])
+        a = Packed(b["input_ids"], b["attention_mask"], b["labels"])
+        p = Packed(b["input_ids"], b["attention_mask"], b["labels"], host)
+        assert host.plan is not None and p.n == a.n and p.n_supervised == a.n_supervised
+        for name in ("tok", "pos", "cu_seqlens", "ids", "targets", "head_order", "row_of_token"):
+            assert torch.equal(getattr(a, name), getattr(p, name)), (lengths, name)
 
 
 def test_prepare_inputs_keeps_the_host_facts():
