@@ -313,7 +313,8 @@ __global__ void __launch_bounds__(192, 1)
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int m_pairs = (int)cdiv(p.M, 2 * Cfg::BM), n_tiles = (int)cdiv(p.N, BN);
-  const int num_units = m_pairs * n_tiles;
+  const int S = p.splits;  // unit u: pair tile u / S, K split u % S
+  const int num_units = m_pairs * n_tiles * S;
   const int k_blocks = (int)cdiv(p.K, Cfg::BK);
 
   if (threadIdx.x == 0) {
@@ -342,10 +343,12 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int u = pair; u < num_units && ok; u += npairs) {
-        const int mp = u % m_pairs, nb = u / m_pairs;
+        const int tile = u / S, sp = u % S;
+        const int mp = tile % m_pairs, nb = tile / m_pairs;
         const int arow = mp * 2 * Cfg::BM + (int)rank * Cfg::BM;
         const int brow = nb * BN + (int)rank * Cfg::HB;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb0 = sp * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err)) { ok = false; break; }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
@@ -382,12 +385,14 @@ __global__ void __launch_bounds__(192, 1)
       int local = 0;
       bool ok = true;
       for (int u = pair; u < num_units && ok; u += npairs, ++local) {
+        const int sp = u % S;
+        const int kb0 = sp * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.err)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
@@ -398,7 +403,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t db = B_MN ? umma_desc_mn_sw128(sb + k * 2048, Cfg::BK * 128, 1024)
                                      : umma_desc_k_sw128(sb + (k >> 2) * (Cfg::HB * 128) + (k & 3) * 32);
             umma_f16_pair(tmem_d, umma_desc_k_sw128(sa + ka), db, idesc,
-                          (kb != 0 || k != 0) ? 1u : 0u);
+                          (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
@@ -414,18 +419,57 @@ __global__ void __launch_bounds__(192, 1)
     OutT* C = reinterpret_cast<OutT*>(p.C);
     const InT* bias = reinterpret_cast<const InT*>(p.bias);
     int ebuf = 0;
+    __shared__ int last_flag;
     for (int u = pair; u < num_units; u += npairs, ++local) {
+      const int tile = u / S, sp = u % S;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, p.err)) break;
       tc_fence_after();
-      const int mp = u % m_pairs, nb = u / m_pairs;
+      const int mp = tile % m_pairs, nb = tile / m_pairs;
       const int row = mp * 2 * Cfg::BM + (int)rank * Cfg::BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      bool finish = true;  // this CTA writes its 128 rows of the output tile
+      float* part = nullptr;
+      if (S > 1) {
+        // this CTA's 128 x BN sub-tile of the split: its fp32 partial, column-major within the
+        // sub-tile so that a warp's 32 lanes (32 consecutive rows) write whole 128-byte lines;
+        // the last of the S units of a sub-tile (its counter) adds them in split order
+        const int64_t st = (int64_t)tile * 2 + rank;
+        part = p.ws + st * S * Cfg::BM * BN;
+        float* mine = part + (int64_t)sp * Cfg::BM * BN + row_in_tile;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(taddr + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) __stcg(mine + (c + i) * Cfg::BM, v[i]);
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(p.counters + st, 1);
+          last_flag = (old == S - 1);
+          if (old == S - 1) p.counters[st] = 0;  // ready for the next launch
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        finish = last_flag != 0;
+        if (finish) __threadfence();
+      }
+#pragma unroll 1
+      for (int c = 0; c < BN && finish; c += 32) {
         float v[32];
-        tmem_ld32(taddr + c, v);
+        if (S > 1) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          const float* src = part + row_in_tile + (int64_t)c * Cfg::BM;
+          for (int j = 0; j < S; ++j) {  // fixed order p0 + p1 + ...: reproducible sums
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += __ldcg(src + (int64_t)j * Cfg::BM * BN + i * Cfg::BM);
+          }
+        } else {
+          tmem_ld32(taddr + c, v);
+        }
         const int col0 = nb * BN + c;
         if constexpr (kTmaC) {
           if (p.tma_c) {
@@ -540,7 +584,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
       return QL_STATUS_CUDA;
     slots = pair_slots(kern, Cfg::SMEM_BYTES);
   }
-  const int units = (int)(cdiv(a.M, 2 * Cfg::BM) * cdiv(a.N, BN));
+  const int units = (int)(cdiv(a.M, 2 * Cfg::BM) * cdiv(a.N, BN)) * a.splits;
   const int pairs = units < slots ? units : slots;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
@@ -674,6 +718,22 @@ static GemmPlan plan_gemm_uncached(int M, int N, int K, int sms, bool b_mn, int 
   // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
   // K <= 4096: the gate/up and lm_head forwards), the shapes where they measured faster than the
   // single-CTA tiles at 1-4K rows. Elsewhere the 256-row pairs waste rows of M and were slower.
+  // Narrow long-K products at ~1 k tokens or more (the down projection, the data gradients of
+  // gate/up and of the head's vocabulary chunks): 256-row pair tiles cut the operand bytes each
+  // CTA streams by a fifth against the single-CTA tiles, and a K split fills the SMs.
+  if (mode == 0 && N <= 2048 && K >= 4096 && M >= 512) {
+    const int64_t ptiles = cdiv(M, 256) * cdiv(N, 256);
+    const int s = (int)((sms / 2) / ptiles);
+    if (s >= 2 && k_blocks / s >= 32 && 2 * ptiles * 4 <= kCounterBytes) {
+      g.pair = true;
+      g.bn = 256;
+      g.tiles = 2 * ptiles;  // 128-row sub-tiles: one split-K partial and counter each
+      g.splits = s;
+      g.kb_per_split = (int)cdiv(k_blocks, s);
+      g.splits = (int)cdiv(k_blocks, g.kb_per_split);
+      return g;
+    }
+  }
   if (mode == 2 || (mode == 0 && !b_mn && N >= 16384 && K <= 4096 && M >= 512)) {
     int pbn = 0;
     int64_t punits = 0;
