@@ -718,10 +718,11 @@ static GemmPlan plan_gemm_uncached(int M, int N, int K, int sms, bool b_mn, int 
   // 2-SM pair tiles: forced by mode 2; by default only for K-major wide products (N >= 16384,
   // K <= 4096: the gate/up and lm_head forwards), the shapes where they measured faster than the
   // single-CTA tiles at 1-4K rows. Elsewhere the 256-row pairs waste rows of M and were slower.
-  // Narrow long-K products at ~1 k tokens or more (the down projection, the data gradients of
-  // gate/up and of the head's vocabulary chunks): 256-row pair tiles cut the operand bytes each
-  // CTA streams by a fifth against the single-CTA tiles, and a K split fills the SMs.
-  if (mode == 0 && N <= 2048 && K >= 4096 && M >= 512) {
+  // Narrow long-K data gradients at ~1 k tokens or more (gate/up's and the head's vocabulary
+  // chunks', an MN-major B): 256-row pair tiles cut the operand bytes each CTA streams by a fifth
+  // against the single-CTA tiles, and a K split fills the SMs (gate/up 52.8 -> 50.8 µs in the
+  // step). The K-major down projection measured no better this way (35.6 -> 36.6 µs).
+  if (mode == 0 && b_mn && N <= 2048 && K >= 4096 && M >= 512) {
     const int64_t ptiles = cdiv(M, 256) * cdiv(N, 256);
     const int s = (int)((sms / 2) / ptiles);
     if (s >= 2 && k_blocks / s >= 32 && 2 * ptiles * 4 <= kCounterBytes) {

@@ -268,13 +268,15 @@ def test_memory_plan_keeps_the_last_layers_and_fits_the_budget():
 def test_gemm_planner_splits_only_long_k_few_tile_products():
     """The GEMM planner (host arithmetic, no GPU needed; 148 SMs assumed without a device) at
     the configs[1] shapes: the long-K products with few output tiles (down projection, gate/up
-    and LM-head data gradients at 1,090 tokens) take 128 x 192 tiles split in two, whose fp32
-    partials need counters + 72 tiles x 2 splits x 128 x 192 floats of workspace; short-K
-    products and large-M products are not split (no workspace)."""
+    and LM-head data gradients at 1,090 tokens) are split in two - the data gradients (MN-major
+    B) as 2-SM pair tiles of 256 x 256 (5 x 6 pair tiles, 60 pairs of 148 SMs), whose fp32
+    partials need counters + 60 sub-tiles of 128 rows x 2 splits x 128 x 256 floats, the most any
+    layout of these shapes asks for; short-K products and large-M products are not split (no
+    workspace)."""
     from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib
 
     lib = _lib.lib()
-    split_two = 2048 + 72 * 2 * 128 * 192 * 4
+    split_two = 2048 + 60 * 2 * 128 * 256 * 4
     n, H, I, V = 1090, 1536, 8960, 151936
     for M, N, K in [(n, H, I), (n, H, 2 * I), (n, H, V)]:
         assert lib.ql_gemm_workspace_bytes(M, N, K) == split_two, (M, N, K)
