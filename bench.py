@@ -16,8 +16,11 @@ seeded batches. Timed: exactly K steps between a barrier + synchronize on both s
 events, max over ranks; value = real (unpadded) tokens of all ranks / that time.
 
 `e2e` runs the same steps through the drop-in boundary (patch.fused_compute_loss on a trainer
-object) from pinned host batches: the host-to-device copy of input_ids / attention_mask / labels
-and the loss read back are inside its timed region.
+object) from pinned host batches: the host-to-device copy of input_ids / attention_mask / labels,
+the ledger's per-step metric read (entropy, accuracy, per-row losses) and the loss read back are
+inside its timed region. The loss of step i is read after step i + 1 is launched (as a trainer's
+logger reads it), so the host's packing of the next batch overlaps the GPU; the last one is read
+before the region closes.
 
 `ops` breaks one step down per operation kind, from the same K steps run again with the library's
 event profiler and programmatic dependent launch off (so the per-operation times add up): time
@@ -397,16 +400,19 @@ def run_ours(args, rank, world, local):
 
     host_ms = {}
 
-    def timed_steps(step_fn, name=None):
+    def timed_steps(step_fn, name=None, finish=None):
         """Device milliseconds of the K timed steps (max over ranks); with a name, also this rank's
         host time to enqueue them (the steps run ahead of the GPU: a host time close to the device
-        time means the host, not the GPU, sets the pace)."""
+        time means the host, not the GPU, sets the pace). finish: run after the last step, inside
+        the timed region (the e2e loop's last host read)."""
         barrier_sync()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         t0 = time.perf_counter()
         for i in timed:
             step_fn(i)
+        if finish is not None:
+            finish()
         t1 = time.perf_counter()
         e1.record()
         barrier_sync()
@@ -497,6 +503,20 @@ def run_ours(args, rank, world, local):
     setattr(trainer, patch._INSTALLED_ATTR, engine)
     pinned = [tuple(torch.from_numpy(a).pin_memory() for a in b[:3]) for b in host]
 
+    # Each step's loss is copied into pinned host memory on the step's stream and read on the host
+    # one step later (after the next step's launches), the way a trainer's logger reads it: the
+    # host prepares step i + 1 while the GPU still runs step i. The metrics (entropy, accuracy,
+    # the per-row losses) are read every step inside the step, by the ledger's flush.
+    in_flight = []  # (copy event, pinned loss) not yet read
+    losses = []
+    slots = [torch.empty((), dtype=torch.float32, pin_memory=True) for _ in range(4)]
+
+    def read_losses(keep):
+        while len(in_flight) > keep:
+            done, slot = in_flight.pop(0)
+            done.synchronize()
+            losses.append(float(slot))
+
     def e2e_step(i):
         ids, mask, labels = pinned[i]
         inputs = patch.prepare_inputs(trainer, {"input_ids": ids, "attention_mask": mask,
@@ -508,13 +528,24 @@ def run_ours(args, rank, world, local):
         scaler.step(opt)
         scaler.update()
         opt.zero_grad(set_to_none=True)
-        return loss.detach().float().item()
+        slot = slots[i % len(slots)]  # (read, two steps back at most, before it is reused)
+        slot.copy_(loss.detach().float(), non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        in_flight.append((done, slot))
+        read_losses(1)
 
-    for i in range(min(2, args.warmup)):
+    for i in range(args.warmup):
         e2e_step(i)
-    e2e_ms = timed_steps(e2e_step, "e2e")
+    read_losses(0)
+    e2e_ms = timed_steps(e2e_step, "e2e", finish=lambda: read_losses(0))
+    if not all(math.isfinite(x) for x in losses):
+        raise RuntimeError(f"non-finite e2e losses: {losses}")
     e2e_value = tokens / (e2e_ms / 1000.0)
     h2d = sum(a.numel() * a.element_size() for i in timed for a in pinned[i]) / args.steps
+    # the loss (fp32) and the ledger's float64 summary: entropy, correct, supervised, and per row
+    # its loss sum and target count
+    d2h = 4 + sum(8 * (3 + 2 * pinned[i][0].shape[0]) for i in timed) / args.steps
 
     # per rank: (host enqueue ms, device ms) per step of the timed and e2e loops
     mine = [host_ms["timed"][0] / args.steps, host_ms["timed"][1] / args.steps,
@@ -546,7 +577,7 @@ def run_ours(args, rank, world, local):
         "tokens_per_step": tokens / args.steps,
         "peak_hbm_mib": peak_mib, "memory": mem_line,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": 4},
+                "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "roofline": {"kernel": "gemm_tn_kernel + gemm_pair_kernel (tcgen05; every GEMM launch "
                                "of the profiled steps)",

@@ -227,7 +227,7 @@ class HostBatch:
     def __init__(self, lengths, n_supervised, plan=None):
         self.lengths = [int(x) for x in lengths]
         self.n_supervised = int(n_supervised)
-        self.plan = plan  # the packed batch's index tensors in one pinned buffer (_host_plan)
+        self.plan = plan  # the packed batch's index tensors in one byte array (_host_plan)
 
     @classmethod
     def of(cls, attention_mask, labels, input_ids=None):
@@ -263,9 +263,10 @@ def _index_plan(lengths, T):
 
 
 def _host_plan(lengths, ids, lab):
-    """Packed's device inputs computed on the host, in one pinned byte buffer: int64 [tok | row |
-    ids | targets | head_order] (n each), then int32 [pos (n) | cu_seqlens (B + 1)] - the values
-    the device path of Packed forms (the same next-label rule and stable supervised-first order)."""
+    """Packed's device inputs computed on the host, in one uint8 array: int64 [tok | row | ids |
+    targets | head_order] (n each), then int32 [pos (n) | cu_seqlens (B + 1)] - the values the
+    device path of Packed forms (the same next-label rule and stable supervised-first order).
+    Pageable: the step copies it through its pinned staging ring (PinnedStaging)."""
     B, T = lab.shape
     idx, n = _index_plan(lengths, T)
     tok, pos, row, cu = idx[:n], idx[n:2 * n], idx[2 * n:3 * n], idx[3 * n:]
@@ -274,12 +275,61 @@ def _host_plan(lengths, ids, lab):
     order = np.argsort(targets < 0, kind="stable").astype(np.int64)
     i64 = np.concatenate([tok, row, ids.reshape(-1)[tok].astype(np.int64), targets, order])
     i32 = np.concatenate([pos, cu]).astype(np.int32)
-    buf = torch.empty(i64.nbytes + i32.nbytes, dtype=torch.uint8,
-                      pin_memory=torch.cuda.is_available())
-    view = buf.numpy()
-    view[:i64.nbytes] = i64.view(np.uint8)
-    view[i64.nbytes:] = i32.view(np.uint8)
-    return buf
+    return np.concatenate([i64.view(np.uint8), i32.view(np.uint8)])
+
+
+class PinnedStaging:
+    """Reusable pinned host buffers for the step's host-to-device copies (its packed batch, and
+    the batch tensors a data loader did not pin).
+    Pinning host memory (cudaHostAlloc) is slow and may wait for the work already queued on the
+    device, so a step that pinned a fresh buffer while the previous step still ran on the GPU
+    would stall the host by up to a step; these buffers are pinned once (with headroom, grown
+    only for a larger batch), and a slot is refilled only after the copy that last read it has
+    finished (its event - long done, a few steps back)."""
+
+    SLOTS = 8
+
+    def __init__(self):
+        self.bufs = [None] * self.SLOTS
+        self.done = [None] * self.SLOTS
+        self.next = 0
+
+    def to_device(self, array, device):
+        """A device copy of the bytes of the numpy array `array`, on the current stream."""
+        data = np.ascontiguousarray(array).reshape(-1).view(np.uint8)
+        if device.type != "cuda":
+            return torch.from_numpy(data.copy()).to(device)
+        k = self.next
+        self.next = (k + 1) % self.SLOTS
+        if self.done[k] is not None:
+            self.done[k].synchronize()
+        buf = self.bufs[k]
+        if buf is None or buf.numel() < data.nbytes:
+            buf = self.bufs[k] = torch.empty(max(64 << 10, 2 * data.nbytes), dtype=torch.uint8,
+                                             pin_memory=True)
+        view = buf[:data.nbytes]
+        view.numpy()[:] = data
+        out = view.to(device, non_blocking=True)
+        if self.done[k] is None:
+            self.done[k] = torch.cuda.Event()
+        self.done[k].record(torch.cuda.current_stream(device))
+        return out
+
+    def tensor_to_device(self, t, device):
+        """A device copy of the CPU tensor `t` (same dtype and shape) staged through the ring."""
+        data = t.contiguous().reshape(-1).view(torch.uint8).numpy()
+        return self.to_device(data, device).view(t.dtype).reshape(t.shape)
+
+
+_STAGING = {}  # device -> PinnedStaging
+
+
+def staging(device):
+    """The process's PinnedStaging ring for copies to `device`."""
+    ring = _STAGING.get(device)
+    if ring is None:
+        ring = _STAGING[device] = PinnedStaging()
+    return ring
 
 
 def _supervised_first(targets):
@@ -325,10 +375,8 @@ class Packed:
             self._from_host_plan(host, input_ids.device)
             return
         plan, self.n = _index_plan(self.lengths, T)
-        staged = torch.from_numpy(plan)
         dev = input_ids.device
-        if dev.type == "cuda":
-            staged = staged.pin_memory().to(dev, non_blocking=True)
+        staged = staging(dev).to_device(plan, dev).view(torch.int64)
         n = self.n
         self.tok = staged[:n]                        # index in the padded batch (int64)
         self.pos = staged[n:2 * n].to(torch.int32)   # position within its row
@@ -346,7 +394,7 @@ class Packed:
     def _from_host_plan(self, host, dev):
         """The packed batch from the host's buffer (HostBatch.plan) in one copy."""
         n = self.n = sum(self.lengths)
-        staged = host.plan.to(dev, non_blocking=True)
+        staged = staging(dev).to_device(host.plan, dev)
         i64 = staged[:5 * n * 8].view(torch.int64)
         i32 = staged[5 * n * 8:].view(torch.int32)
         self.tok, self.row_of_token = i64[:n], i64[n:2 * n]

@@ -136,10 +136,23 @@ class MetricLedger:
     each forward finished - and appends the values in micro-batch order, before the optimizer
     step and the log read them (solution/patch.py:334-389 keeps the same values). The flush
     therefore does not wait for the backward, and the optimizer's launches are not held back
-    behind it."""
+    behind it. The pinned host buffers are reused from flush to flush (pinning memory on every
+    step could wait for the GPU's queued work)."""
 
     def __init__(self):
         self.pending = []  # (summary: host copy or tensor, copy event, rows, real tokens, step)
+        self.free = []     # pinned float64 buffers the last flush gave back
+        self.lent = []     # the buffers of the pending summaries
+
+    def _pinned(self, n):
+        for k, buf in enumerate(self.free):
+            if buf.numel() >= n:
+                del self.free[k]
+                break
+        else:
+            buf = torch.empty(max(64, 2 * n), dtype=torch.float64, pin_memory=True)
+        self.lent.append(buf)
+        return buf[:n]
 
     def record(self, packed, stats, labels, step):
         rows = packed.rows
@@ -153,7 +166,7 @@ class MetricLedger:
             summary = torch.cat([head, per_row, row_targets])
             done = None
             if summary.is_cuda:
-                host = torch.empty(summary.shape, dtype=summary.dtype, pin_memory=True)
+                host = self._pinned(summary.numel())
                 host.copy_(summary, non_blocking=True)
                 done = torch.cuda.Event()
                 done.record()
@@ -168,6 +181,8 @@ class MetricLedger:
             if done is not None:
                 done.synchronize()
         values = torch.cat([s for s, _, _, _, _ in pending]).tolist()
+        self.free.extend(self.lent)
+        self.lent = []
         metrics = trainer._metrics["train"]
         recorder = getattr(trainer, "_soup_rewind_state", None)
         at = 0
@@ -259,18 +274,22 @@ def _host_facts(inputs):
 
 
 def prepare_inputs(trainer, inputs, device):
-    """Moves a host batch to the GPU as HF Trainer._prepare_inputs does (pinned, non-blocking)
-    and keeps its HostBatch for the next fused_compute_loss, which then reads nothing back from
-    the device."""
+    """Moves a host batch to the GPU as HF Trainer._prepare_inputs does (non-blocking: pinned
+    tensors directly, others through the engine's reusable pinned staging buffers) and keeps its
+    HostBatch for the next fused_compute_loss, which then reads nothing back from the device."""
+    from .engine import staging
+
     host = _host_facts(inputs)
     device = torch.device(device)
 
     def move(v):
         if not torch.is_tensor(v) or v.device == device:
             return v
-        if device.type != "cuda":
+        if device.type != "cuda" or v.device.type != "cpu":
             return v.to(device)
-        return (v if v.is_pinned() else v.pin_memory()).to(device, non_blocking=True)
+        if v.is_pinned():
+            return v.to(device, non_blocking=True)
+        return staging(device).tensor_to_device(v, device)
 
     moved = {k: move(v) for k, v in inputs.items()}
     if host is not None and "input_ids" in moved:
