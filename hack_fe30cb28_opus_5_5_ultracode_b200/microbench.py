@@ -6,6 +6,7 @@ on the launching stream (warm-up, then `--iters` launches, each input set larger
 
 Prints one JSON line per kernel and shape: average launch time, algorithmic FLOPs or bytes per
 launch, achieved TFLOP/s or GB/s and the fraction of the measured peak (MEASURED_PEAKS.json).
+The layer GEMMs are also timed through cuBLAS (`torch.mm`, lines "cublas ...") for comparison.
 Also the small, self-contained case the ncu captures run on.
 """
 
@@ -120,6 +121,10 @@ def main():
                 sec = _time(lambda i: ops.gemm(a[i % copies], b[i % 2], out=c[i % copies]),
                             args.iters)
                 _report("gemm_tn " + name, [n, N, K], sec, flops=2.0 * n * N * K)
+                # cuBLAS on the same operands, for comparison (torch.mm)
+                sec = _time(lambda i: torch.mm(a[i % copies], b[i % 2].t(), out=c[i % copies]),
+                            args.iters)
+                _report("cublas " + name, [n, N, K], sec, flops=2.0 * n * N * K)
                 # the data-gradient GEMM of the same projection: [n, N] x [K, N]^T
                 at = [torch.randn(n, N, device=dev, generator=g).to(dt) for _ in range(copies)]
                 bt = [torch.randn(K, N, device=dev, generator=g).to(dt) * 0.02 for _ in range(2)]
@@ -127,6 +132,9 @@ def main():
                 sec = _time(lambda i: ops.gemm(at[i % copies], bt[i % 2], out=ct[i % copies]),
                             args.iters)
                 _report("gemm_tn dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
+                sec = _time(lambda i: torch.mm(at[i % copies], bt[i % 2].t(), out=ct[i % copies]),
+                            args.iters)
+                _report("cublas dgrad " + name, [n, K, N], sec, flops=2.0 * n * N * K)
                 # NF4 dequantised inside the GEMM (no 16-bit weight in HBM), both layouts
                 sec = _time(lambda i: ops.gemm_nf4(a[i % copies], ws[i % 2], layout=0,
                                                    out=c[i % copies]), args.iters)
