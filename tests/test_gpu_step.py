@@ -290,3 +290,24 @@ def test_kept_weights_follow_the_nf4_storage():
     assert torch.equal(engine.w16[:fresh.numel()].view_as(fresh), fresh)
     assert not torch.equal(engine.w16, first)
     assert ops.launch_count() > launches
+
+
+def test_pinned_staging_ring_keeps_every_copy():
+    """Many more copies than the ring has slots, of growing and shrinking sizes, queued behind
+    device work: each device copy holds its own source bytes (a slot is refilled only after the
+    copy that last read it)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import PinnedStaging
+
+    dev = torch.device("cuda", 0)
+    ring = PinnedStaging()
+    busy = torch.randn(4096, 4096, device=dev)
+    outs, srcs = [], []
+    for i in range(5 * PinnedStaging.SLOTS):
+        busy = busy @ busy.t() * 1e-4  # keep the stream busy so copies queue behind it
+        src = np.random.default_rng(i).integers(0, 1 << 62, size=1000 + 3000 * (i % 7),
+                                                dtype=np.int64)
+        srcs.append(src)
+        outs.append(ring.to_device(src, dev).view(torch.int64))
+    torch.cuda.synchronize()
+    for src, out in zip(srcs, outs):
+        assert np.array_equal(out.cpu().numpy(), src)

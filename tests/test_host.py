@@ -236,6 +236,18 @@ def test_host_batch_matches_the_device_reads():
             assert torch.equal(getattr(a, name), getattr(p, name)), (lengths, name)
 
 
+def test_staging_copies_keep_bytes_dtype_and_shape():
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import staging
+
+    ring = staging(torch.device("cpu"))
+    for t in (torch.arange(35, dtype=torch.int64).reshape(5, 7), torch.rand(3, 4) > 0.5,
+              torch.randn(6), torch.tensor(3.5)):
+        out = ring.tensor_to_device(t, torch.device("cpu"))
+        assert out.dtype == t.dtype and out.shape == t.shape and torch.equal(out, t)
+    plan = np.arange(10, dtype=np.int64).view(np.uint8)
+    assert torch.equal(ring.to_device(plan, torch.device("cpu")), torch.from_numpy(plan))
+
+
 def test_prepare_inputs_keeps_the_host_facts():
     t, _ = _trainer(_FakeEngine())
     b = _batch([5, 3, 7])
