@@ -83,6 +83,11 @@ def parse():
     ap.add_argument("--hi", type=int, default=HI)
     ap.add_argument("--uniform", default=None, metavar="LO,HI",
                     help="sequence lengths uniform in [LO, HI] instead of lognormal")
+    ap.add_argument("--stream-weights", action="store_true",
+                    help="NF4 base weights in pinned host memory, streamed into two device "
+                         "slots one layer ahead (FusedQwen2(stream_weights=True)); the line adds "
+                         "the copies' bytes, link rate and exposed time against the same steps "
+                         "with the NF4 bytes resident")
     ap.add_argument("--model", choices=["1.5b", "7b"], default="1.5b")
     ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
     return ap.parse_args()
@@ -152,6 +157,9 @@ def workload_config(args, world):
            "parallelism": f"dp{world}",
            "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of activations) is "
                  "larger than the 126 MB L2"}
+    if getattr(args, "stream_weights", False):
+        cfg["weights"] = ("NF4 base weights in pinned host memory, streamed into two device "
+                          "slots one layer ahead, dequantised per layer pass")
     if world > 1:
         cfg["sharding"] = (f"each step's {args.seqs * world} sequences (rank r's drawn from seed "
                            f"1000 + r) dealt back {args.seqs} per rank, token-balanced "
@@ -361,7 +369,7 @@ def run_ours(args, rank, world, local):
         budget = None if args.budget_gib is None else int(args.budget_gib * 1024)
         keep = args.keep_layers if args.keep_layers is not None or budget is not None else 0
         plan_kw = dict(spill=args.spill, keep_layers=keep, activation_budget_mib=budget)
-    engine = FusedQwen2(model, dtype=cdt, **plan_kw)
+    engine = FusedQwen2(model, dtype=cdt, stream_weights=args.stream_weights, **plan_kw)
     if world > 1:
         engine.set_data_parallel(None)
     params = lora_parameters(model)
@@ -488,6 +496,34 @@ def run_ours(args, rank, world, local):
             host_link_gbs=(spill_bytes / (copy_ms / 1e3) / 1e9) if copy_ms else None,
             host_link_peak_gbs=link_peak,
             link_gbs_seen_by_planner=engine.link_gbs, layer_ms_seen_by_planner=engine.layer_ms)
+    if args.stream_weights:
+        from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+
+        # the stream's copies (copy-stream events of the last timed step), and the same steps
+        # with the NF4 bytes resident and dequantised per layer pass as well (a second engine
+        # over the same model: its groups take device copies of the pinned bytes), whose time
+        # difference is the copies' exposed time
+        wst = engine.wstream
+        torch.cuda.synchronize(dev)
+        copy_ms, moved = wst.copy_ms(), wst.bytes_moved
+        streamed = engine
+        engine = FusedQwen2(model, dtype=cdt, keep_weights=False, **plan_kw)
+        if world > 1:
+            engine.set_data_parallel(None)
+        for i in range(args.warmup):
+            train_step(i)
+        torch.cuda.reset_peak_memory_stats(dev)
+        t_res = timed_steps(train_step)
+        res_peak = torch.cuda.max_memory_allocated(dev) / 2**20
+        engine = streamed
+        mem_line["weight_stream"] = dict(
+            layer_mib=wst.layer_bytes / 2**20, host_arena_mib=wst.host.numel() / 2**20,
+            device_slots_mib=wst.slots.numel() / 2**20, bytes_per_step=moved,
+            copy_stream_ms_per_step=copy_ms,
+            host_link_gbs=(moved / (copy_ms / 1e3) / 1e9) if copy_ms else None,
+            host_link_peak_gbs=memory.measure_link_gbs(dev),
+            resident_ms_per_step=t_res / args.steps, resident_peak_hbm_mib=res_peak,
+            exposed_copy_fraction=max(0.0, (ms - t_res) / ms))
     value = tokens / (ms / 1000.0)
 
     # e2e: the drop-in boundary from pinned host batches

@@ -79,11 +79,18 @@ class NF4Group:
         self.seg1, self.seg2 = (bounds + [ops.INT_MAX, ops.INT_MAX])[:2]
         self.blocks = blocks
         self.shape = (self.rows, self.cols)
-        # the bitsandbytes parameters now point at the group's bytes (no second copy)
+        self.params = list(params)
+        self.bind(self.packed, self.absmax)
+
+    def bind(self, packed, absmax):
+        """Makes `packed` / `absmax` (same sizes and dtypes, on the device or in pinned host
+        memory) the group's storage, and points the bitsandbytes parameters at them: the model's
+        4-bit weights are one copy, wherever the group keeps it."""
+        self.packed, self.absmax = packed, absmax
         off_p = off_a = 0
-        for p, s, b in zip(params, states, blocks):
-            p.data = self.packed[off_p:off_p + b * 32].view(-1, 1)
-            s.absmax = self.absmax[off_a:off_a + b]
+        for p, b in zip(self.params, self.blocks):
+            p.data = packed[off_p:off_p + b * 32].view(-1, 1)
+            p.quant_state.absmax = absmax[off_a:off_a + b]
             off_p += b * 32
             off_a += b
 
@@ -522,13 +529,18 @@ class FusedQwen2:
     """Holds what the step needs from a PEFT-wrapped, 4-bit Qwen2ForCausalLM."""
 
     def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True,
-                 spill="recompute", keep_layers=None, activation_budget_mib=None):
+                 spill="recompute", keep_layers=None, activation_budget_mib=None,
+                 stream_weights=False):
         """spill / keep_layers / activation_budget_mib: the activation-memory plan of each step
         (memory.plan_memory): by default every layer keeps its saved activations in HBM; with a
         budget (MiB for the saved sets) or a forced keep_layers the first layers spill by
         recompute, by offload to pinned host memory, or "auto": offload only the layers whose
         copies hide behind compute (from the host link's measured bandwidth and the previous
-        step's time per layer) and recompute the others."""
+        step's time per layer) and recompute the others.
+        stream_weights: move the NF4 base weights into pinned host memory and stream each layer's
+        bytes into one of two device slots ahead of its pass (weight_stream.WeightStream); the
+        layers then dequantise per pass (no kept 16-bit copy), so HBM holds two layers' NF4
+        bytes instead of every layer's NF4 bytes and their 16-bit copy."""
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -585,6 +597,12 @@ class FusedQwen2:
         self._grad_offsets = (ctypes.c_int64 * L)(*[self.offsets[4 * i] for i in range(L)])
         # the forward's dequantised weights, per layer, read again by the backward
         self.weight_elems = int(_lib.lib().ql_layer_weight_elems(ctypes.byref(self.descs[0])))
+        self.wstream = None
+        if stream_weights:
+            from .weight_stream import WeightStream
+
+            keep_weights = False
+            self.wstream = WeightStream(self.layers, self.descs, self.device)
         self.w16 = torch.empty(len(self.layers) * self.weight_elems, device=self.device,
                                dtype=dtype) if keep_weights else None
         self.spill, self.keep_layers = spill, keep_layers
@@ -704,7 +722,10 @@ class FusedQwen2:
         drops = self._drops(packed)
         self._set_all_steps(packed, drops, cos, sin)
         saved_arr, h_out = self._saved_structs(arena, plan)
-        if n and all(m == memory.KEEP for m in plan.modes):
+        wst = self.wstream
+        if wst is not None:
+            wst.reset()
+        if n and all(m == memory.KEEP for m in plan.modes) and wst is None:
             # every layer keeps its saved set: the whole forward in one call
             ws = self._workspace_for(self.descs[0])
             _lib.call("ql_layers_forward", ctypes.addressof(self.desc_array),
@@ -714,10 +735,14 @@ class FusedQwen2:
             for i, desc in enumerate(self.descs):
                 if offload is not None:
                     offload.before_forward(i)
+                if wst is not None:  # layer i's NF4 bytes in its slot, layer i + 1's on the way
+                    wst.use(i, i + 1 if i + 1 < L else None)
                 ws = self._workspace_for(desc)
                 _lib.call("ql_layer_forward", ctypes.addressof(desc),
                           ctypes.addressof(saved_arr[i]), arena.h(i + 1).data_ptr(),
                           ws.data_ptr(), ws.numel(), ops.stream_ptr())
+                if wst is not None:
+                    wst.done(i)
                 if offload is not None:
                     offload.after_forward(i)
         saved = (saved_arr, drops)
@@ -887,6 +912,8 @@ class FusedQwen2:
             sv.w16 = self.w16[index * self.weight_elems:].data_ptr()
             sv.w16_ready = 1
         ws = self._workspace_for(desc)
+        if self.wstream is not None:
+            self.wstream.use(index)
         _lib.call("ql_layer_forward", ctypes.addressof(desc), ctypes.addressof(sv),
                   arena.h(1).data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
         h3 = arena.h(1).clone()
@@ -899,6 +926,8 @@ class FusedQwen2:
         _lib.call("ql_layer_backward", ctypes.addressof(desc), ctypes.addressof(sv),
                   dh3.data_ptr(), dh3_16.data_ptr(), grads.data_ptr(),
                   dh.data_ptr(), dh16.data_ptr(), ws.data_ptr(), ws.numel(), ops.stream_ptr())
+        if self.wstream is not None:
+            self.wstream.done(index)
         views, at = [], 0
         for t in self.lora_fp32[4 * index:4 * index + 4]:
             views.append(grads[at:at + t.numel()].view(t.shape))
@@ -934,19 +963,22 @@ class FusedQwen2:
                 offload.start_backward()
             L = len(self.layers)
             self._set_all_steps(packed, drops, cos, sin)
-            if all(m == memory.KEEP for m in plan.modes):
-                # every saved set is in HBM: the whole backward in one call
+            wst = self.wstream
+            one_call = all(m == memory.KEEP for m in plan.modes) and wst is None
+            if one_call:
+                # every saved set and weight is in HBM: the whole backward in one call
                 ws = self._workspace_for(self.descs[0])
                 _lib.call("ql_layers_backward", ctypes.addressof(self.desc_array),
                           ctypes.addressof(saved_arr), L, dh[0].data_ptr(), dh16[0].data_ptr(),
                           dh[1].data_ptr(), dh16[1].data_ptr(), grads.data_ptr(),
                           ctypes.addressof(self._grad_offsets), 1, ws.data_ptr(), ws.numel(),
                           ops.stream_ptr())
-            for spec in reversed(self.layers if not all(m == memory.KEEP for m in plan.modes)
-                                 else []):
+            for spec in reversed(self.layers if not one_call else []):
                 i = spec.index
                 desc = self.descs[i]
                 sv, drop = saved_arr[i], drops[i]
+                if wst is not None:  # layer i's NF4 bytes in its slot, layer i - 1's on the way
+                    wst.use(i, i - 1 if i > 0 else None)
                 if plan.modes[i] == memory.RECOMPUTE:
                     self._recompute(i, desc, sv, arena)
                 elif plan.modes[i] == memory.OFFLOAD:
@@ -960,6 +992,8 @@ class FusedQwen2:
                           dh[nxt].data_ptr() if need else None,
                           dh16[nxt].data_ptr() if need else None, ws.data_ptr(), ws.numel(),
                           ops.stream_ptr())
+                if wst is not None:
+                    wst.done(i)
                 if offload is not None and plan.modes[i] == memory.OFFLOAD:
                     offload.after_backward(i)
                 cur = nxt

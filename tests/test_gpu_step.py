@@ -261,6 +261,64 @@ def test_spilled_layers_match_oracle(spill):
     assert gen.get_offset() == ref["offset"]
 
 
+@pytest.mark.parametrize("keep_layers", [None, 1])
+def test_streamed_weights_match_resident(keep_layers, deterministic_attention):
+    """NF4 base weights in pinned host memory, streamed into two device slots one layer ahead of
+    their pass (WeightStream, the reference's solution/engine.py:160-287), give the step with
+    resident NF4 bytes its loss and LoRA gradients bit for bit, over two steps, with every layer
+    kept or with the first three recomputed in the backward (from the slot their backward uses).
+    The layers at each turn of the layer order stay in their slots: the first step copies 2 L - 2
+    layers, every later one 2 (L - 2). The bitsandbytes parameters then view the pinned arena."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import Qwen2Config, build_qwen2_qlora, lora_parameters
+
+    L = 4
+    cfg = Qwen2Config(vocab_size=4096, num_hidden_layers=L)
+    ids, mask, labels = _batch([150, 64, 256, 97], cfg.vocab_size, seed=8)
+    ids, mask, labels = ids.to(DEV), mask.to(DEV), labels.to(DEV)
+    kw = {} if keep_layers is None else dict(keep_layers=keep_layers, spill="recompute")
+    runs = []
+    for stream in (False, True):
+        model = build_qwen2_qlora(cfg, dropout=0.1, device=DEV, seed=7)  # the same weights
+        params = lora_parameters(model)
+        engine = FusedQwen2(model, keep_weights=False, stream_weights=stream, **kw)
+        out, copies = [], []
+        for k in range(2):
+            torch.cuda.manual_seed(11 + k)
+            loss, _, _ = engine.step(ids, mask, labels, 300.0)
+            out.append((loss.detach(), _grads(loss, params, torch.float16)))
+            if stream:
+                copies.append(engine.wstream.copies)
+        runs.append((out, engine, copies))
+    (resident, _, _), (streamed, engine, copies) = runs
+    for (la, ga), (lb, gb) in zip(resident, streamed):
+        assert torch.equal(la, lb)
+        for a, b in zip(ga, gb):
+            assert torch.equal(a, b)
+    assert copies == [2 * L - 2, 2 * (L - 2)]
+    torch.cuda.synchronize()
+    assert engine.wstream.copy_ms() > 0
+    for spec in engine.layers:
+        for g in (spec.qkv, spec.o, spec.gu, spec.down):
+            assert g.packed.device.type == "cpu" and g.packed.is_pinned()
+            for p in g.params:
+                assert p.data.device.type == "cpu"
+                assert p.quant_state.absmax.device.type == "cpu"
+
+
+def test_streamed_weights_match_oracle():
+    """Three full-width layers with streamed NF4 weights (double quantisation: the second-level
+    scales stay resident) against the oracle at the keep-everything step's bounds."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import Qwen2Config
+
+    cfg = Qwen2Config(vocab_size=4096, num_hidden_layers=3)
+    engine, loss, packed, stats, grads, ref, gen = _run(cfg, [150, 64, 256, 97], 0.05, True,
+                                                        keep_weights=False, stream_weights=True)
+    assert engine.wstream is not None and engine.w16 is None
+    _check_step("3 layers, streamed NF4 weights", loss, grads, ref, torch.float16)
+    assert gen.get_offset() == ref["offset"]
+
+
 def test_kept_weights_follow_the_nf4_storage():
     """The 16-bit weights are dequantised once and reused while the frozen NF4 storage is
     unchanged; an in-place change to a layer's packed bytes (the storage the model's bitsandbytes
