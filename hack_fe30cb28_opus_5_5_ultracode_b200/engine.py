@@ -611,8 +611,9 @@ class FusedQwen2:
         self._host_ring = None     # pinned host memory of offloaded layers (grow-only)
         self._copy_stream = None
         self.link_gbs = None       # host link bandwidth, measured at the first "auto" plan
-        self._step_events = None   # (start, end) of the last step, for the time per layer
-        self.layer_ms = None       # the last completed step's time per layer
+        self._step_events = None   # (start, end, tokens) of the last step, for the time per layer
+        self.layer_ms = None       # the expected time per layer of this step's tokens
+        self._layer_ms_per_token = None  # per layer and token, the fastest step seen
         self.last_offload = None   # the last step's _Offload (copy bytes and timing), if any
         self.plan_transform = None  # optional plan -> plan hook (the bench times variants)
         self._scratch_h = None
@@ -695,8 +696,15 @@ class FusedQwen2:
             if self.link_gbs is None:
                 self.link_gbs = memory.measure_link_gbs(self.device)
             ev = self._step_events
-            if ev is not None and ev[1].query():  # the previous step has finished: no wait
-                self.layer_ms = ev[0].elapsed_time(ev[1]) / len(self.layers)
+            if ev is not None and ev[2] and ev[1].query():  # the previous step has finished
+                per_token = ev[0].elapsed_time(ev[1]) / len(self.layers) / ev[2]
+                # the fastest step so far sets the estimate: a step the host stalled (the first
+                # step's set-up, a host-memory allocation) must not make the next plan offload
+                # more layers than the link can hide
+                if self._layer_ms_per_token is None or per_token < self._layer_ms_per_token:
+                    self._layer_ms_per_token = per_token
+            if self._layer_ms_per_token is not None:
+                self.layer_ms = self._layer_ms_per_token * n
         plan = memory.plan_memory(len(self.layers), layer_bytes, self.activation_budget,
                                   self.spill, self.keep_layers, self.link_gbs, self.layer_ms)
         if self.plan_transform is not None:
@@ -704,7 +712,7 @@ class FusedQwen2:
         self.last_plan = plan
         if self.spill == memory.AUTO:
             self._step_events = (torch.cuda.Event(enable_timing=True),
-                                 torch.cuda.Event(enable_timing=True))
+                                 torch.cuda.Event(enable_timing=True), n)
             self._step_events[0].record()
         arena = _SavedArena(n, spec0, len(self.layers), self.dtype, self.device,
                             None if self._arena_busy else self._arena_buf, plan)
@@ -1154,7 +1162,12 @@ class _Offload:
         self.order = sorted(offloaded, reverse=True)  # the backward's order
         nbytes = len(self.spilled) * arena.layer_bytes
         if engine._host_ring is None or engine._host_ring.numel() < nbytes:
-            engine._host_ring = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+            # grown with half again as much headroom: pinning gigabytes of host memory takes
+            # seconds (and can wait for the GPU), so only a step well above every earlier one
+            # may pay it, never each step that is slightly longer than the last
+            engine._host_ring = None
+            engine._host_ring = torch.empty(nbytes + nbytes // 2, dtype=torch.uint8,
+                                            pin_memory=True)
         if engine._copy_stream is None:
             engine._copy_stream = torch.cuda.Stream(device=engine.device)
         self.host, self.stream = engine._host_ring, engine._copy_stream
