@@ -530,7 +530,7 @@ class FusedQwen2:
 
     def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True,
                  spill="recompute", keep_layers=None, activation_budget_mib=None,
-                 stream_weights=False):
+                 stream_weights=False, step_budget_mib=None):
         """spill / keep_layers / activation_budget_mib: the activation-memory plan of each step
         (memory.plan_memory): by default every layer keeps its saved activations in HBM; with a
         budget (MiB for the saved sets) or a forced keep_layers the first layers spill by
@@ -540,7 +540,13 @@ class FusedQwen2:
         stream_weights: move the NF4 base weights into pinned host memory and stream each layer's
         bytes into one of two device slots ahead of its pass (weight_stream.WeightStream); the
         layers then dequantise per pass (no kept 16-bit copy), so HBM holds two layers' NF4
-        bytes instead of every layer's NF4 bytes and their 16-bit copy."""
+        bytes instead of every layer's NF4 bytes and their 16-bit copy.
+        step_budget_mib: a budget for the step's whole working memory instead (the device memory
+        a step allocates beyond the model, its optimizer state and the kept weights: saved sets,
+        residual slots, backward buffers, head buffers, layer workspace), predicted for each
+        step's token count by predict_step_bytes; whatever is left after everything but the
+        saved sets goes to the saved sets (the reference's predicted-peak planner,
+        solution/engine.py:1630-1707, with a caller's budget in place of its T4 cap)."""
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -608,6 +614,7 @@ class FusedQwen2:
         self.spill, self.keep_layers = spill, keep_layers
         self.activation_budget = None if activation_budget_mib is None \
             else int(activation_budget_mib) << 20
+        self.step_budget = None if step_budget_mib is None else int(step_budget_mib) << 20
         self._host_ring = None     # pinned host memory of offloaded layers (grow-only)
         self._copy_stream = None
         self.link_gbs = None       # host link bandwidth, measured at the first "auto" plan
@@ -705,7 +712,14 @@ class FusedQwen2:
                     self._layer_ms_per_token = per_token
             if self._layer_ms_per_token is not None:
                 self.layer_ms = self._layer_ms_per_token * n
-        plan = memory.plan_memory(len(self.layers), layer_bytes, self.activation_budget,
+        budget = self.activation_budget
+        if self.step_budget is not None:  # what the rest of the step leaves for the saved sets
+            rest = self.predict_step_bytes(n, memory.MemoryPlan([]), packed.rows,
+                                           packed.max_len)
+            if self.spill != memory.OFFLOAD:
+                rest += n * spec0.H * 4  # a recomputed layer's scratch output
+            budget = max(0, self.step_budget - rest)
+        plan = memory.plan_memory(len(self.layers), layer_bytes, budget,
                                   self.spill, self.keep_layers, self.link_gbs, self.layer_ms)
         if self.plan_transform is not None:
             plan = self.plan_transform(plan)
@@ -759,6 +773,30 @@ class FusedQwen2:
         if loss is None:
             loss = torch.zeros((), device=self.device)
         return loss, (arena, saved, offload), dhp
+
+    def predict_step_bytes(self, n, plan, seqs=None, max_len=None):
+        """Predicted device memory a step of n tokens (seqs sequences, the longest max_len
+        tokens; by default one sequence of n) allocates under `plan` beyond what the model
+        already holds (memory.predict_peak_bytes with this engine's shapes, head block and layer
+        workspace)."""
+        spec = self.layers[0]
+        e = self._esize()
+        layer_bytes, _ = memory.saved_set_bytes(n, spec.H, spec.HQ, spec.HKV, spec.D, spec.I, e)
+        rows = min(n, self.head_chunk)
+        width = self.head.chunk_width(rows) if rows else 0
+        # the layer workspace for this step's sizes, from a copy of a layer's descriptor
+        desc = _lib.STRUCTS["ql_layer_desc"].from_buffer_copy(self.descs[0])
+        desc.n, desc.B = n, seqs if seqs is not None else 1
+        desc.max_len = max_len if max_len is not None else n
+        ws = max(int(_lib.lib().ql_layer_workspace_bytes(ctypes.addressof(desc), b))
+                 for b in (0, 1))
+        # the head's block buffers and the workspace are allocated with a quarter of headroom;
+        # fixed: the flat LoRA gradients and one more set (a caller's unscaled or accumulated
+        # copies), and an allowance for the packed batch's index tensors, the RoPE tables and
+        # other small temporaries
+        fixed = 2 * self.lora_total * 4 + n * 64 + (8 << 20)
+        return memory.predict_peak_bytes(len(self.layers), layer_bytes, plan, n, spec.H, self.V,
+                                         e, fixed, rows + rows // 4, width, ws + ws // 4)
 
     def _saved_structs(self, arena, plan):
         """Every layer's ql_layer_saved (device addresses in the arena) and the residual slots

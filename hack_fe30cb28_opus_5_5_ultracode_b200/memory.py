@@ -145,13 +145,21 @@ def plan_memory(layers, layer_bytes, budget_bytes=None, spill=RECOMPUTE, keep_la
 
 def predict_peak_bytes(layers, layer_bytes, plan, n, H, V, elem, fixed_bytes, head_rows,
                        head_width, workspace_bytes):
-    """The step's device-memory peak beyond what the model already holds: the saved-set arena
-    (the plan's slots) and the L + 1 fp32 residual slots, the backward's two [n, H] gradient
-    buffers (fp32 and 16-bit each), the head's chunk buffer and accumulators, the layer workspace,
-    and fixed_bytes (the kept 16-bit weights and other per-engine buffers)."""
+    """The step's device-memory peak beyond what the model already holds. Held through the
+    whole step: the saved-set arena (the plan's slots and the L + 1 fp32 residual slots), the
+    head's block buffers (a logits chunk, per row the online state, per supervised row the fp32
+    accumulator and chunk product and the 16-bit target row and gradient), the layer workspace,
+    the head's input gradient [n, H] fp32 and per-row statistics (rstd, loss, entropy, correct,
+    target), the recompute ring's fp32 scratch output, and fixed_bytes (the flat LoRA gradients,
+    other per-engine buffers). On top of that, the larger of the head's gathered and normed rows
+    (fp32 and 16-bit [n, H], forward only) and the backward's two gradient buffers of each type."""
     h_bytes = (n * H * 4 + 255) // 256 * 256
     arena = plan.slots * layer_bytes + (layers + 1) * h_bytes
+    block = head_rows * head_width * elem + head_rows * (4 * 4 + 8 + 4) \
+        + head_rows * H * (2 * 4 + 2 * elem)
+    held = arena + block + workspace_bytes + n * H * 4 + n * (4 * 4 + 8) + fixed_bytes
+    if RECOMPUTE in plan.modes:
+        held += n * H * 4
+    head_rows_fwd = n * H * (4 + elem)
     backward = 2 * n * H * (4 + elem)
-    head = head_rows * head_width * elem + head_rows * (4 * 4 + 8 + 4) + 2 * n * H * 4 \
-        + 2 * n * H * elem + 2 * n * H * 4
-    return fixed_bytes + arena + backward + head + workspace_bytes
+    return held + max(head_rows_fwd, backward)

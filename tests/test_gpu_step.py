@@ -319,6 +319,44 @@ def test_streamed_weights_match_oracle():
     assert gen.get_offset() == ref["offset"]
 
 
+def test_step_budget_bounds_the_step_memory():
+    """step_budget_mib (the reference's predicted-peak planner, solution/engine.py:1630-1707):
+    with a budget halfway between the predicted memory of a step that recomputes every layer and
+    one that keeps every layer, the plan keeps some layers but not all, and the step's measured
+    working memory (the allocator's peak during the step and its backward, above what was
+    allocated before it) stays within the prediction for that plan, and so within the budget;
+    the prediction is close (within 10 % above the measured peak)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import Qwen2Config, build_qwen2_qlora, lora_parameters
+
+    L = 6
+    cfg = Qwen2Config(vocab_size=4096, num_hidden_layers=L)
+    ids, mask, labels = _batch([150, 64, 256, 97], cfg.vocab_size, seed=8)
+    ids, mask, labels = ids.to(DEV), mask.to(DEV), labels.to(DEV)
+    model = build_qwen2_qlora(cfg, dropout=0.1, device=DEV, seed=7)
+    params = lora_parameters(model)
+    engine = FusedQwen2(model)
+    n, B, T = int(mask.sum()), mask.shape[0], int(mask.sum(1).max())
+    keep_all = engine.predict_step_bytes(n, memory.MemoryPlan([memory.KEEP] * L), B, T)
+    none = engine.predict_step_bytes(n, memory.MemoryPlan([memory.RECOMPUTE] * L), B, T)
+    budget = (keep_all + none) // 2
+    engine.step_budget = budget
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    loss, _, _ = engine.step(ids, mask, labels, 300.0)
+    _grads(loss, params, torch.float16)
+    torch.cuda.synchronize()
+    used = torch.cuda.max_memory_allocated() - base
+    plan = engine.last_plan
+    predicted = engine.predict_step_bytes(n, plan, B, T)
+    _record("step budget", used=used, predicted=predicted, budget=budget, plan=plan.summary())
+    assert 0 < plan.modes.count(memory.KEEP) < L, plan.summary()
+    assert used <= predicted <= budget, (used, predicted, budget)
+    assert predicted <= 1.10 * used, (used, predicted)
+
+
 def test_kept_weights_follow_the_nf4_storage():
     """The 16-bit weights are dequantised once and reused while the frozen NF4 storage is
     unchanged; an in-place change to a layer's packed bytes (the storage the model's bitsandbytes

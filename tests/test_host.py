@@ -277,6 +277,28 @@ def test_memory_plan_keeps_the_last_layers_and_fits_the_budget():
         memory.plan_memory(4, lb, spill="disk")
 
 
+def test_step_budget_prediction_and_plan():
+    """The predicted step memory (memory.predict_peak_bytes) at the configs[1] shapes: the plans
+    differ by their saved-set slots alone (a recompute plan adds its ring slot and the recompute
+    scratch), and the budget left for the saved sets after the rest of the step gives a plan
+    whose predicted total meets the step budget exactly."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import memory
+
+    n, H, HQ, HKV, D, I, L, V = 1090, 1536, 12, 2, 128, 8960, 28, 151936
+    lb, _ = memory.saved_set_bytes(n, H, HQ, HKV, D, I, 2)
+
+    def pred(plan):
+        return memory.predict_peak_bytes(L, lb, plan, n, H, V, 2, 0, 1362, 16896, 1 << 24)
+
+    none = pred(memory.MemoryPlan([]))
+    assert pred(memory.MemoryPlan(["keep"] * L)) - none == L * lb
+    assert pred(memory.MemoryPlan(["recompute"] * L)) - none == lb + n * H * 4
+    assert pred(memory.MemoryPlan(["offload"] * L)) - none == 2 * lb
+    budget = none + n * H * 4 + 10 * lb
+    plan = memory.plan_memory(L, lb, budget - none - n * H * 4, "recompute")
+    assert plan.modes.count("keep") == 9 and pred(plan) == budget
+
+
 def test_gemm_planner_splits_only_long_k_few_tile_products():
     """The GEMM planner (host arithmetic, no GPU needed; 148 SMs assumed without a device) at
     the configs[1] shapes: the long-K products with few output tiles (down projection, gate/up
