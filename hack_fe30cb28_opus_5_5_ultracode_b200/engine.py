@@ -657,6 +657,13 @@ class FusedQwen2:
             self._workspace = torch.zeros(need + need // 4, device=self.device, dtype=torch.uint8)
         return self._workspace
 
+    def restore_weights(self):
+        """For code outside the fused step that runs the model's own 4-bit layers: with streamed
+        weights, the NF4 bytes back on the GPU (the next step streams them again); otherwise
+        nothing to do (the model's parameters view the engine's device storage)."""
+        if self.wstream is not None:
+            self.wstream.restore()
+
     def set_data_parallel(self, group=None):
         """Average the LoRA gradients over `group` (None: the default process group) at the end
         of the backward, in one all-reduce of the flat gradient buffer."""
@@ -675,6 +682,8 @@ class FusedQwen2:
                                    "(LoraDropoutStream.verify)")
         with torch.no_grad():
             torch._foreach_copy_(self.lora_views, self.lora_fp32)
+        if self.wstream is not None:  # (after code outside the step brought the weights back)
+            self.wstream.offload()
         stats = HeadStats()
         loss = _FusedStep.apply(self, packed, float(denom), stats, *self.lora_fp32)
         return loss, packed, stats

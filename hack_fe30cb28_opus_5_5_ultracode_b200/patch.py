@@ -217,6 +217,9 @@ def flush_metrics(trainer):
 
 
 def _run_original(trainer, model, inputs, return_outputs, num_items_in_batch):
+    engine = getattr(trainer, _INSTALLED_ATTR, None)
+    if engine is not None and hasattr(engine, "restore_weights"):
+        engine.restore_weights()  # the original code runs the 4-bit layers: weights on the GPU
     return getattr(trainer, _ORIGINAL_ATTR)(model, inputs, return_outputs=return_outputs,
                                             num_items_in_batch=num_items_in_batch)
 
@@ -320,10 +323,11 @@ class _LedgerFlush(_callback_base()):
         flush_metrics(self.trainer)
 
 
-def install(trainer, dtype=None):
+def install(trainer, dtype=None, **engine_options):
     """Installs the fused step as trainer.compute_loss if the model is supported; returns
     whether it did (solution/patch.py:452-503). dtype: the compute type, from the trainer's
-    args (bf16 / fp16) unless given."""
+    args (bf16 / fp16) unless given; engine_options: FusedQwen2's memory options
+    (stream_weights, spill, activation_budget_mib, step_budget_mib, keep_weights, ...)."""
     model = getattr(trainer, "model", None)
     if getattr(trainer, _INSTALLED_ATTR, None) is not None:
         return True
@@ -335,7 +339,7 @@ def install(trainer, dtype=None):
     if dtype is None:
         args = getattr(trainer, "args", None)
         dtype = torch.bfloat16 if getattr(args, "bf16", False) else torch.float16
-    engine = FusedQwen2(model, dtype=dtype)
+    engine = FusedQwen2(model, dtype=dtype, **engine_options)
     setattr(trainer, _ORIGINAL_ATTR, trainer.compute_loss)
     setattr(trainer, _INSTALLED_ATTR, engine)
     trainer.compute_loss = types.MethodType(fused_compute_loss, trainer)

@@ -24,6 +24,12 @@ double quantisation are a few kilobytes per layer and stay resident.
 The dequantisation kernels read the slots like any device memory, so a streamed step gives the
 resident step's results bit for bit; with the kept 16-bit copy off (keep_weights=False), each
 layer pass dequantises its weights from the slot into the layer workspace.
+
+Code outside the fused step (an evaluation, a batch the step does not take) runs the model's own
+4-bit layers, which need their bytes on the GPU: restore() copies the arena back into one device
+buffer and points the bitsandbytes parameters there; offload(), at the next fused step, points
+them at the host arena again and frees that buffer (the reference's restore_weights /
+offload_weights, solution/engine.py:1800-1813 and solution/patch.py:280-298).
 """
 
 import torch
@@ -61,17 +67,17 @@ class WeightStream:
                     raise ValueError(f"layer {spec.index}: {name} differs in size from layer 0")
         # the host arena: each group's bytes moved in, then the group (and the bitsandbytes
         # parameters) re-pointed at them; the device copies are released as each layer is done
+        self.layers = layers
+        self.absmax_dtype = {name: getattr(layers[0], name).absmax.dtype for name in GROUPS}
         self.host = torch.empty(self.L * self.layer_bytes, dtype=torch.uint8, pin_memory=True)
         for i, spec in enumerate(layers):
-            base = i * self.layer_bytes
             for name in GROUPS:
                 g = getattr(spec, name)
-                po, pb, ao, ab = self.fields[name]
-                packed = self.host[base + po:base + po + pb]
-                absmax = self.host[base + ao:base + ao + ab].view(g.absmax.dtype)
+                packed, absmax = self._views(self.host, i, name)
                 packed.copy_(g.packed.reshape(-1).view(torch.uint8))
                 absmax.copy_(g.absmax.reshape(-1))
                 g.bind(packed, absmax)
+        self.device_copy = None  # the arena's bytes on the GPU while restore()d
         self.slots = torch.empty(2 * self.layer_bytes, device=device, dtype=torch.uint8)
         for i, desc in enumerate(descs):
             base = self.slots.data_ptr() + (i % 2) * self.layer_bytes
@@ -85,6 +91,32 @@ class WeightStream:
         self.free = [None, None]    # event: the slot's last pass has finished reading it
         self.copies = 0             # layer copies queued since the last reset()
         self.copy_events = []       # (start, end) timing events of those copies
+
+    def _views(self, buf, i, name):
+        """Group `name` of layer i in an arena-layout buffer: (packed bytes, absmax)."""
+        po, pb, ao, ab = self.fields[name]
+        base = i * self.layer_bytes
+        return (buf[base + po:base + po + pb],
+                buf[base + ao:base + ao + ab].view(self.absmax_dtype[name]))
+
+    def _bind_all(self, buf):
+        for i, spec in enumerate(self.layers):
+            for name in GROUPS:
+                getattr(spec, name).bind(*self._views(buf, i, name))
+
+    def restore(self):
+        """The model's 4-bit weights on the GPU again (one copy of the arena), for code that
+        runs the model's own layers; the slots and the stream are unchanged."""
+        if self.device_copy is None:
+            self.device_copy = torch.empty_like(self.host, device=self.device)
+            self.device_copy.copy_(self.host)
+            self._bind_all(self.device_copy)
+
+    def offload(self):
+        """Back to streaming: the weights viewed in the host arena, the device copy freed."""
+        if self.device_copy is not None:
+            self._bind_all(self.host)
+            self.device_copy = None
 
     def reset(self):
         """Starts a new step's accounting of copies (the slots keep what they hold)."""

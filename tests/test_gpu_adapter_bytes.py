@@ -70,3 +70,59 @@ def test_adapter_and_base_bytes_survive_install_step_and_fallback(tmp_path):
     for (packed, absmax), (packed2, absmax2) in zip(base, _base_state(model)):
         assert torch.equal(packed.reshape(-1), packed2.reshape(-1))
         assert torch.equal(absmax, absmax2)
+
+
+def test_streamed_weights_train_fallback_train():
+    """Streamed weights through the drop-in (patch.install(trainer, stream_weights=True)): after
+    a fused step the model's 4-bit parameters view pinned host memory; a fallback call to the
+    original compute_loss finds them on the GPU with their original bytes (the model's own layers
+    can run); the next fused step streams again (the device copy freed) and gives the first
+    step's loss bit for bit (the reference's train-eval-train test,
+    solution/test_fallback.py:100-117, and its restore_weights, solution/patch.py:280-283)."""
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import patch
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import TINY, build_qwen2_qlora
+
+    model = build_qwen2_qlora(TINY, dropout=0.0, device=DEV, seed=5, nested=True)
+    model.train()
+    base = _base_state(model)
+    seen = []
+
+    def original(model_, inputs, return_outputs=False, num_items_in_batch=None):
+        state = _base_state(model_)
+        seen.append(all(p.is_cuda and a.is_cuda for p, a in state))
+        seen.append(all(torch.equal(p.reshape(-1).cpu(), q.reshape(-1).cpu())
+                        and torch.equal(a.cpu(), b.cpu()) for (p, a), (q, b) in zip(state, base)))
+        return torch.zeros((), device=DEV)
+
+    trainer = types.SimpleNamespace(
+        model=model, compute_loss=original, compute_loss_func=None, label_smoother=None,
+        model_accepts_loss_kwargs=True, state=types.SimpleNamespace(global_step=0),
+        args=types.SimpleNamespace(average_tokens_across_devices=False, n_gpu=1, bf16=False),
+        _metrics={"train": {}}, _total_train_tokens=0, _soup_rewind_state=None)
+    assert patch.install(trainer, stream_weights=True)
+    engine = getattr(trainer, patch._INSTALLED_ATTR)
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, TINY.vocab_size, (3, 40), generator=g)
+    mask = (torch.arange(40)[None] < torch.tensor([40, 23, 9])[:, None]).long()
+    labels = torch.where(mask.bool(), ids, -100)
+    inputs = {"input_ids": ids.to(DEV), "attention_mask": mask.to(DEV), "labels": labels.to(DEV)}
+    losses = []
+
+    def fused():
+        loss = trainer.compute_loss(model, dict(inputs), num_items_in_batch=60)
+        loss.backward()
+        patch.flush_metrics(trainer)
+        losses.append(loss.detach())
+
+    fused()
+    assert all(not p.is_cuda and not a.is_cuda for p, a in _base_state(model))
+    model.eval()  # evaluation: the original compute_loss runs the model's own layers
+    trainer.compute_loss(model, dict(inputs))
+    model.train()
+    assert seen == [True, True]
+    assert engine.wstream.device_copy is not None
+    fused()
+    assert engine.wstream.device_copy is None
+    assert all(not p.is_cuda and not a.is_cuda for p, a in _base_state(model))
+    torch.cuda.synchronize()
+    assert torch.isfinite(losses[0]) and torch.equal(losses[0], losses[1])

@@ -100,6 +100,10 @@ class _FakeEngine:
 
     def __init__(self, fail=False):
         self.calls, self.fail = [], fail
+        self.restored = 0  # restore_weights calls (before each run of the original code)
+
+    def restore_weights(self):
+        self.restored += 1
 
     def step(self, input_ids, attention_mask, labels, denom, host=None):
         self.calls.append(denom)
@@ -204,6 +208,7 @@ def test_fused_compute_loss_falls_back(case):
         t.label_smoother = object()
     loss = patch.fused_compute_loss(t, model, b, num_items_in_batch=3)
     assert loss.item() == 123.0 and len(calls) == 1
+    assert engine.restored == 1  # the original code runs the model's own layers
     assert "_prediction_loss_only" in calls[0]  # the inputs reach the original unchanged
     assert t._total_train_tokens == 0
 
