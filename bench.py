@@ -79,8 +79,11 @@ def parse():
                          "activations")
     ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per rank and step")
     ap.add_argument("--median", type=int, default=MEDIAN, help="median sequence length")
-    ap.add_argument("--lo", type=int, default=LO)
-    ap.add_argument("--hi", type=int, default=HI)
+    # (--min-len / --max-len under torchrun: its own parser takes --lo for a prefix of --log-dir)
+    ap.add_argument("--lo", "--min-len", dest="lo", type=int, default=LO,
+                    help="shortest sequence length")
+    ap.add_argument("--hi", "--max-len", dest="hi", type=int, default=HI,
+                    help="longest sequence length")
     ap.add_argument("--uniform", default=None, metavar="LO,HI",
                     help="sequence lengths uniform in [LO, HI] instead of lognormal")
     ap.add_argument("--stream-weights", action="store_true",
