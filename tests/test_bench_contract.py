@@ -27,3 +27,17 @@ def test_reference_arm_prints_the_contract_line():
     assert base["value"] == line["value"] and base["unit"] == line["unit"]
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+
+
+def test_workload_options_survive_torchrun_parsing():
+    """Every workload option reaches bench.py intact through torchrun's own argument parser
+    (which takes any prefix of its options, e.g. --lo for --log-dir, as its own)."""
+    from torch.distributed.run import get_args_parser
+
+    opts = ["--gpus", "8", "--steps", "10", "--warmup", "3", "--dtype", "bf16", "--seqs", "8",
+            "--median", "512", "--min-len", "64", "--max-len", "2048", "--no-cpu-baseline",
+            "--stream-weights", "--spill", "auto", "--budget-gib", "40", "--model", "7b",
+            "--uniform", "1024,4096", "--impl", "reference"]
+    args = get_args_parser().parse_args(["--nnodes=1", "--nproc-per-node", "8", "--master-addr",
+                                         "127.0.0.1", "bench.py"] + opts)
+    assert args.training_script == "bench.py" and args.training_script_args == opts
