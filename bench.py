@@ -183,11 +183,13 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons (and the device memory in use) sampled every 200 ms
+    during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "memory.used")
 
     def __init__(self, index):
         self.index = index
@@ -211,7 +213,7 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, used = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
             parts = [p.strip() for p in line.split(",")]
@@ -225,10 +227,14 @@ class Clocks:
             for name, val in zip(names, parts[5:9]):
                 if val.lower() == "active":
                     reasons.add(name)
+            try:
+                used.append(float(parts[9]))
+            except (IndexError, ValueError):
+                pass
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "memory_used_mib": max(used) if used else None}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -623,6 +629,9 @@ def run_ours(args, rank, world, local):
         "config": workload_config(args, world),
         "tokens_per_step": tokens / args.steps,
         "peak_hbm_mib": peak_mib, "memory": mem_line,
+        # NVML's view: the device memory in use while the timed steps ran (this process's
+        # allocator reservations and CUDA context, on a GPU no other process uses)
+        "peak_hbm_nvml_mib": clk.get("memory_used_mib") if clk else None,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
