@@ -34,8 +34,8 @@ def _grads(loss, params, dtype):
 
 
 def _record(name, **values):
-    """Appends a test's measured errors to gpurun_out/parity_errors.jsonl (when that folder
-    exists), so the margins below the bounds are on record."""
+    """Appends a test's measured errors to parity_errors.jsonl in the repository's run-output
+    folder, when the run created one, so the margins below the bounds are on record."""
     out = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "gpurun_out")
     if os.path.isdir(out):
         with open(os.path.join(out, "parity_errors.jsonl"), "a") as fh:
