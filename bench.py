@@ -91,6 +91,9 @@ def parse():
                          "slots one layer ahead (FusedQwen2(stream_weights=True)); the line adds "
                          "the copies' bytes, link rate and exposed time against the same steps "
                          "with the NF4 bytes resident")
+    ap.add_argument("--host-embedding", action="store_true",
+                    help="the input embedding table in pinned host memory, rows gathered over "
+                         "the host link (untied models: --model 7b)")
     ap.add_argument("--model", choices=["1.5b", "7b"], default="1.5b")
     ap.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16")
     return ap.parse_args()
@@ -160,6 +163,8 @@ def workload_config(args, world):
            "parallelism": f"dp{world}",
            "l2": "no flush: per-step working set (0.74 GB NF4 weights + GBs of activations) is "
                  "larger than the 126 MB L2"}
+    if getattr(args, "host_embedding", False):
+        cfg["embedding"] = "input embedding table in pinned host memory, gathered over the link"
     if getattr(args, "stream_weights", False):
         cfg["weights"] = ("NF4 base weights in pinned host memory, streamed into two device "
                           "slots one layer ahead, dequantised per layer pass")
@@ -378,7 +383,8 @@ def run_ours(args, rank, world, local):
         budget = None if args.budget_gib is None else int(args.budget_gib * 1024)
         keep = args.keep_layers if args.keep_layers is not None or budget is not None else 0
         plan_kw = dict(spill=args.spill, keep_layers=keep, activation_budget_mib=budget)
-    engine = FusedQwen2(model, dtype=cdt, stream_weights=args.stream_weights, **plan_kw)
+    engine = FusedQwen2(model, dtype=cdt, stream_weights=args.stream_weights,
+                        host_embedding=args.host_embedding, **plan_kw)
     if world > 1:
         engine.set_data_parallel(None)
     params = lora_parameters(model)

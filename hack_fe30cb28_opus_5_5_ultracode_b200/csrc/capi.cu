@@ -328,6 +328,31 @@ int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int6
   return done(ql::embed(ids, W, h, n, H, vocab, dtype, ql::status_word(), stream), "ql_embed");
 }
 
+int ql_embed_host(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
+                  int dtype, cudaStream_t stream) {
+  if (W == nullptr || n < 0 || H <= 0 || vocab <= 0 || (dtype != QL_F16 && dtype != QL_BF16))
+    return fail(QL_STATUS_BAD_ARG, "ql_embed_host");
+  // The table must be page-locked host memory mapped for this device, over its whole extent:
+  // its device address (the same pointer under unified addressing) from the runtime, for the
+  // first and the last byte; anything else is refused before a kernel could touch it.
+  const char* first = static_cast<const char*>(W);
+  const char* last = first + vocab * (int64_t)H * 2 - 1;
+  cudaPointerAttributes a0{}, a1{};
+  const bool ok0 = cudaPointerGetAttributes(&a0, first) == cudaSuccess;
+  const bool ok1 = ok0 && cudaPointerGetAttributes(&a1, last) == cudaSuccess;
+  cudaGetLastError();
+  if (!ok1 || a0.type != cudaMemoryTypeHost || a1.type != cudaMemoryTypeHost ||
+      a0.devicePointer == nullptr ||
+      static_cast<const char*>(a1.devicePointer) !=
+          static_cast<const char*>(a0.devicePointer) + (last - first)) {
+    g_last_error = "ql_embed_host: the table is not page-locked host memory this device can read";
+    return QL_STATUS_BAD_ARG;
+  }
+  return done(ql::embed_host(ids, a0.devicePointer, h, n, H, vocab, dtype, ql::status_word(),
+                             stream),
+              "ql_embed_host");
+}
+
 int ql_ce_rows(const ql_ce_rows_args* args, cudaStream_t stream) {
   if (args == nullptr) return fail(QL_STATUS_BAD_ARG, "ql_ce_rows");
   return done(ql::ce_rows(*args, stream), "ql_ce_rows");

@@ -501,4 +501,62 @@ int scatter_rows(const float* src, const int64_t* idx, const float* scale, float
   return launched(1);
 }
 
+// embedding gather from a table in page-locked host memory, read by the kernel over the host
+// link (zero-copy): one CTA per token, 16-byte loads when the row allows. The loads are plain
+// ld.global (the read-only data path is not used on host memory).
+__device__ __forceinline__ uint4 ld_plain_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ unsigned short ld_plain_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+template <typename T>
+__global__ void embed_host_kernel(const int64_t* __restrict__ ids, const T* W, float* __restrict__ h,
+                                  int64_t n, int H, int64_t vocab, int vec, int* err) {
+  pdl_enter();
+  const int64_t t = blockIdx.x;
+  const int64_t id = ids[t];
+  float* out = h + t * H;
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) raise_status(err, QL_STATUS_BAD_ARG);
+    for (int c = threadIdx.x; c < H; c += blockDim.x) out[c] = 0.f;
+    return;
+  }
+  const T* row = W + id * H;
+  if (vec) {
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+      const uint4 v = ld_plain_v4(row + c * 8);
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[c * 8 + j] = to_f<T>(e[j]);
+    }
+  } else {
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+      const unsigned short b = ld_plain_u16(row + c);
+      out[c] = to_f<T>(*reinterpret_cast<const T*>(&b));
+    }
+  }
+}
+
+int embed_host(const int64_t* ids, const void* W_dev, float* h, int64_t n, int H, int64_t vocab,
+               int dtype, int* err, cudaStream_t s) {
+  if (n < 0 || H <= 0) return QL_STATUS_BAD_ARG;
+  if (n == 0) return QL_STATUS_OK;
+  const int vec = ((uintptr_t)W_dev % 16 == 0 && (H * 2) % 16 == 0) ? 1 : 0;
+  if (dtype == QL_F16)
+    embed_host_kernel<__half><<<n, 128, 0, s>>>(ids, (const __half*)W_dev, h, n, H, vocab, vec, err);
+  else if (dtype == QL_BF16)
+    embed_host_kernel<__nv_bfloat16><<<n, 128, 0, s>>>(ids, (const __nv_bfloat16*)W_dev, h, n, H,
+                                                       vocab, vec, err);
+  else return QL_STATUS_BAD_ARG;
+  return launched(1);
+}
+
 }  // namespace ql

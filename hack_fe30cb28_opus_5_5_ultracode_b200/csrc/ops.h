@@ -53,6 +53,8 @@ int lora_grads(const ql_lora_grad_job* jobs, int njobs, int64_t n, int x_dtype, 
 int lora_colsum(const void* X, int64_t ldx, int x_dtype, const void* Y, int y_dtype, int64_t n,
                 int ncols, int rank, float scale, int transpose, float* out, float* workspace,
                 int64_t workspace_floats, cudaStream_t s);
+int embed_host(const int64_t* ids, const void* W_dev, float* h, int64_t n, int H, int64_t vocab,
+               int dtype, int* err, cudaStream_t s);
 int embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
           int dtype, int* err, cudaStream_t s);
 int ce_rows(const CeRowsC& a, cudaStream_t s);

@@ -530,7 +530,7 @@ class FusedQwen2:
 
     def __init__(self, peft_model, dtype=torch.float16, head_chunk=HEAD_CHUNK, keep_weights=True,
                  spill="recompute", keep_layers=None, activation_budget_mib=None,
-                 stream_weights=False, step_budget_mib=None):
+                 stream_weights=False, step_budget_mib=None, host_embedding=False):
         """spill / keep_layers / activation_budget_mib: the activation-memory plan of each step
         (memory.plan_memory): by default every layer keeps its saved activations in HBM; with a
         budget (MiB for the saved sets) or a forced keep_layers the first layers spill by
@@ -546,7 +546,12 @@ class FusedQwen2:
         residual slots, backward buffers, head buffers, layer workspace), predicted for each
         step's token count by predict_step_bytes; whatever is left after everything but the
         saved sets goes to the saved sets (the reference's predicted-peak planner,
-        solution/engine.py:1630-1707, with a caller's budget in place of its T4 cap)."""
+        solution/engine.py:1630-1707, with a caller's budget in place of its T4 cap).
+        host_embedding: keep the input embedding table in page-locked host memory (the model's
+        embedding parameter views it) and gather each step's rows from there over the host link
+        (the reference's host-resident embedding, solution/offload.py:55-111); only for an untied
+        lm_head (a tied head's GEMMs read the table on the device every step); saves the table's
+        HBM (1.09 GB for Qwen2.5-7B) for n H 2 bytes of host reads per step."""
         causal = peft_model.get_base_model()
         inner = causal.model
         config = causal.config
@@ -570,6 +575,17 @@ class FusedQwen2:
         self.lm_w = self.embed if lm.data_ptr() == inner.embed_tokens.weight.data_ptr() \
             and lm.dtype == dtype else lm.to(dtype).contiguous()
         self.V = self.lm_w.shape[0]
+        self._embed_param = inner.embed_tokens.weight
+        self.host_embed = None
+        if host_embedding:
+            if self.lm_w.data_ptr() == self.embed.data_ptr():
+                raise ValueError("host_embedding needs an untied lm_head: a tied head's GEMMs "
+                                 "read the embedding table on the device every step")
+            self.host_embed = torch.empty(self.embed.shape, dtype=self.embed.dtype,
+                                          pin_memory=True)
+            self.host_embed.copy_(self.embed)
+            self.embed = self.host_embed
+            self._embed_to_host()
         self.head = VocabHead(self.lm_w, dtype)
         self.rope = RopeTable(inner.rotary_emb, spec.D, self.device)
         self.head_chunk = head_chunk
@@ -658,11 +674,22 @@ class FusedQwen2:
         return self._workspace
 
     def restore_weights(self):
-        """For code outside the fused step that runs the model's own 4-bit layers: with streamed
-        weights, the NF4 bytes back on the GPU (the next step streams them again); otherwise
-        nothing to do (the model's parameters view the engine's device storage)."""
+        """For code outside the fused step that runs the model's own layers: with streamed
+        weights, the NF4 bytes back on the GPU (the next step streams them again), and a
+        host-resident embedding table likewise; otherwise nothing to do (the model's parameters
+        view the engine's device storage)."""
         if self.wstream is not None:
             self.wstream.restore()
+        p = self._embed_param
+        if self.host_embed is not None and p.device.type == "cpu":
+            p.data = p.data.to(self.device)
+
+    def _embed_to_host(self):
+        """The model's embedding parameter views the pinned table (its device copy is freed),
+        when the table is kept in the parameter's own dtype."""
+        p = self._embed_param
+        if p.dtype == self.host_embed.dtype and p.device.type != "cpu":
+            p.data = self.host_embed
 
     def set_data_parallel(self, group=None):
         """Average the LoRA gradients over `group` (None: the default process group) at the end
@@ -684,6 +711,8 @@ class FusedQwen2:
             torch._foreach_copy_(self.lora_views, self.lora_fp32)
         if self.wstream is not None:  # (after code outside the step brought the weights back)
             self.wstream.offload()
+        if self.host_embed is not None:
+            self._embed_to_host()
         stats = HeadStats()
         loss = _FusedStep.apply(self, packed, float(denom), stats, *self.lora_fp32)
         return loss, packed, stats

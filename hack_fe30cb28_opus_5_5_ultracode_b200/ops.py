@@ -384,11 +384,13 @@ def lora_grads(jobs):
 
 
 def embed(ids, W, out=None):
+    """Rows W[ids] as fp32 [n, H]; W on the GPU, or in page-locked host memory (read over the
+    host link by ql_embed_host)."""
     n = ids.numel()
-    h = out if out is not None else torch.empty((n, W.shape[1]), device=W.device,
+    h = out if out is not None else torch.empty((n, W.shape[1]), device=ids.device,
                                                 dtype=torch.float32)
-    call("ql_embed", _ptr(ids), _ptr(W), _ptr(h), n, W.shape[1], W.shape[0],
-         dtype_code(W.dtype), stream_ptr())
+    call("ql_embed" if W.is_cuda else "ql_embed_host", _ptr(ids), _ptr(W), _ptr(h), n,
+         W.shape[1], W.shape[0], dtype_code(W.dtype), stream_ptr())
     return h
 
 

@@ -292,6 +292,14 @@ int ql_lora_colsum_noalloc(const void* X, int64_t ldx, int x_dtype, const void* 
 int ql_embed(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
              int dtype, cudaStream_t stream);
 
+/* The same lookup from a table in page-locked host memory, read by the kernel over the host link
+ * (the reference keeps the embedding in host memory, solution/offload.py:55-111 and
+ * solution/engine.py:1763-1771): W must be pinned and mapped for the current device over all of
+ * its vocab * H 16-bit entries (checked with cudaPointerGetAttributes; otherwise
+ * QL_STATUS_BAD_ARG and nothing is launched). */
+int ql_embed_host(const int64_t* ids, const void* W, float* h, int64_t n, int H, int64_t vocab,
+                  int dtype, cudaStream_t stream);
+
 /* ---- cross-entropy head ------------------------------------------------------------------ */
 typedef struct {
   void* logits;         /* [rows, ld] 16-bit, overwritten by the gradient */

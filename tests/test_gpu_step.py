@@ -357,6 +357,50 @@ def test_step_budget_bounds_the_step_memory():
     assert predicted <= 1.10 * used, (used, predicted)
 
 
+def test_host_embedding_matches_device_embedding(deterministic_attention):
+    """An untied model's input embedding kept in page-locked host memory (host_embedding=True:
+    each step's rows gathered over the host link by ql_embed_host) gives the step with the table
+    on the device its loss and LoRA gradients bit for bit, and the model's embedding parameter
+    then views the pinned table. ql_embed_host gathers exactly the table's rows (the last row
+    included) and refuses a table in pageable host memory before launching anything; a tied
+    lm_head is refused."""
+    import dataclasses
+
+    from hack_fe30cb28_opus_5_5_ultracode_b200 import _lib, ops
+    from hack_fe30cb28_opus_5_5_ultracode_b200.engine import FusedQwen2
+    from hack_fe30cb28_opus_5_5_ultracode_b200.model import TINY, build_qwen2_qlora, lora_parameters
+
+    cfg = dataclasses.replace(TINY, tie_word_embeddings=False)
+    ids, mask, labels = _batch([37, 12, 64], cfg.vocab_size, seed=6)
+    ids, mask, labels = ids.to(DEV), mask.to(DEV), labels.to(DEV)
+    runs = []
+    for host in (False, True):
+        model = build_qwen2_qlora(cfg, dropout=0.1, device=DEV, seed=3)  # the same weights
+        params = lora_parameters(model)
+        engine = FusedQwen2(model, host_embedding=host)
+        torch.cuda.manual_seed(4)
+        loss, _, _ = engine.step(ids, mask, labels, 90.0)
+        runs.append((loss.detach(), _grads(loss, params, torch.float16), engine, model))
+    (la, ga, _, _), (lb, gb, engine, model) = runs
+    assert torch.equal(la, lb)
+    for a, b in zip(ga, gb):
+        assert torch.equal(a, b)
+    weight = model.get_base_model().model.embed_tokens.weight
+    assert weight.device.type == "cpu" and weight.is_pinned()
+    table = engine.host_embed
+    rows = torch.tensor([0, 5, cfg.vocab_size - 1, 77], device=DEV)
+    got = ops.embed(rows, table)
+    assert torch.equal(got, table.to(DEV)[rows].float())
+    pageable = torch.empty(table.shape, dtype=table.dtype).copy_(table)
+    assert not pageable.is_pinned()
+    with pytest.raises(_lib.QLError):
+        ops.embed(rows, pageable)  # refused before anything is launched
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    with pytest.raises(ValueError):
+        FusedQwen2(build_qwen2_qlora(TINY, dropout=0.1, device=DEV, seed=3), host_embedding=True)
+
+
 def test_kept_weights_follow_the_nf4_storage():
     """The 16-bit weights are dequantised once and reused while the frozen NF4 storage is
     unchanged; an in-place change to a layer's packed bytes (the storage the model's bitsandbytes
