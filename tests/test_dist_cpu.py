@@ -106,3 +106,54 @@ def test_bench_batches_are_the_dealt_shards():
                 got.append(tuple(ids[i, :L]))
         assert sorted(got) == drawn
     assert all(np.array_equal(a[0], b[0]) for a, b in zip(bench.batches(args, 0, vocab), own[0]))
+
+
+def _dying_worker(rank, world, port, q):
+    """Rank 1 leaves between steps (it exits after the first exchange, as a crashed rank does);
+    rank 0 goes on to the next step's gradient exchange, which must end with an error within
+    the process group's timeout instead of waiting for good."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    from hack_fe30cb28_opus_5_5_ultracode_b200.dist import GradReducer
+
+    flat = torch.ones(16)
+    red = GradReducer()
+    red.launch(flat)
+    red.finish(flat)  # step 1: both ranks
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the message is written before the process ends
+        os._exit(0)  # no destroy_process_group: the peer learns of it from the transport
+    t0 = time.monotonic()
+    try:
+        red.launch(flat)
+        red.finish(flat)
+        q.put((rank, "no error"))
+    except Exception as exc:  # noqa: BLE001 - whatever the backend raises
+        q.put((rank, f"error after {time.monotonic() - t0:.1f} s: {type(exc).__name__}"))
+
+
+@pytest.mark.timeout(120)
+def test_a_rank_that_leaves_turns_the_next_exchange_into_an_error():
+    """A rank that leaves between steps does not hang the others: their next gradient
+    all-reduce raises within the process group's timeout (host-side failure, gloo on CPU)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("error after"), results[0]
+    assert float(results[0].split()[2]) < 30.0
